@@ -1,0 +1,204 @@
+"""ctypes binding of ``libaethermoe.so`` (declared in ``include/aem.h``).
+
+Loading fails loudly: there is no CPU fallback for any entry point.  Status
+codes become exceptions the way the reference reports errors
+(``ValueError`` for bad arguments, ``fused_gating_metal.py:380-388``,
+``quantized_gemm.py:204-205``; ``RuntimeError`` otherwise).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libaethermoe.so")
+
+AEM_OK, AEM_EINVAL, AEM_ECUDA, AEM_ENCCL, AEM_ETIMEOUT, AEM_ENOMEM, AEM_EUNSUPPORTED, AEM_EDEVICE = range(8)
+F32, BF16 = 0, 1
+GATING_EXACT, GATING_FAST = 0, 1
+CAPACITY_UNLIMITED = (1 << 64) - 1
+MAX_EXPERTS = 256
+MAX_TOPK = 64
+
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_u64 = ctypes.c_uint64
+
+
+class AemError(RuntimeError):
+    """A failed library call (CUDA, NCCL, timeout, in-kernel check)."""
+
+    def __init__(self, status, message):
+        super().__init__(f"[aem status {status}] {message}")
+        self.status = status
+
+
+class AemTimeout(AemError):
+    pass
+
+
+class MoeConfig(ctypes.Structure):
+    _fields_ = [("d_model", _i64), ("d_ffn", _i64), ("num_experts", _int), ("top_k", _int),
+                ("capacity", _u64), ("gating_mode", _int)]
+
+
+_SIGS = {
+    "aem_last_error": (ctypes.c_char_p, []),
+    "aem_version": (ctypes.c_char_p, []),
+    "aem_device_count": (_int, []),
+    "aem_device_status": (_int, [_vp]),
+    "aem_context_create": (_int, [_int, ctypes.POINTER(_vp)]),
+    "aem_context_destroy": (_int, [_vp]),
+    "aem_context_stream": (_vp, [_vp]),
+    "aem_gate_pack": (_int, [_vp, _vp, _i64, _i64, _int, ctypes.POINTER(_vp)]),
+    "aem_gate_free": (_int, [_vp]),
+    "aem_gating": (_int, [_vp, _vp, _int, _i64, _int, _int, _int, _vp, _vp, _vp]),
+    "aem_gating_host": (_int, [_vp, _vp, _vp, _int, _i64, _int, _int, _int, _vp, _vp]),
+    "aem_quantize_int8": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
+    "aem_quantize_int8_host": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
+    "aem_qweight_pack": (_int, [_vp, _vp, _i64, _i64, _i64, _int, ctypes.POINTER(_vp)]),
+    "aem_qweight_pack_device": (_int, [_vp, _vp, _i64, _i64, _i64, _vp, ctypes.POINTER(_vp)]),
+    "aem_qweight_free": (_int, [_vp]),
+    "aem_qweight_shape": (_int, [_vp, ctypes.POINTER(_i64), ctypes.POINTER(_i64),
+                                 ctypes.POINTER(_i64)]),
+    "aem_qgemm": (_int, [_vp, _i64, _vp, _int, _i64, _vp, _vp]),
+    "aem_qgemm_host": (_int, [_vp, _vp, _i64, _vp, _int, _i64, _vp]),
+    "aem_capacity_route_workspace": (ctypes.c_size_t, [_i64, _int]),
+    "aem_capacity_route": (_int, [_vp, _vp, _vp, _i64, _int, _u64, _vp, _vp, ctypes.c_size_t,
+                                  _vp]),
+    "aem_moe_create": (_int, [ctypes.POINTER(MoeConfig), _vp, _vp, _vp, ctypes.POINTER(_vp)]),
+    "aem_moe_free": (_int, [_vp]),
+    "aem_moe_forward": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp]),
+    "aem_moe_forward_host": (_int, [_vp, _vp, _vp, _int, _i64, _vp, _int]),
+    "aem_moe_last_routing": (_int, [_vp, _vp, _vp, _vp, _vp]),
+    "aem_ep_plan_bases": (_int, [_vp, _int, _int, _int, _int, _vp]),
+    "aem_ep_unique_id": (_int, [_vp]),
+    "aem_ep_create": (_int, [ctypes.POINTER(MoeConfig), _int, _int, _vp, _vp, _vp, _vp,
+                             ctypes.POINTER(_vp)]),
+    "aem_ep_free": (_int, [_vp]),
+    "aem_ep_forward": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp]),
+    "aem_ep_last_routing": (_int, [_vp, _vp, _vp, _vp, _vp]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib():
+    """The loaded library (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise ImportError(
+                        f"{LIB_PATH} is missing: build it with `python -m aethermoe_b200.build` "
+                        "(there is no CPU fallback)")
+                L = ctypes.CDLL(LIB_PATH)
+                for name, (res, args) in _SIGS.items():
+                    fn = getattr(L, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = L
+    return _lib
+
+
+def exported_symbols():
+    return list(_SIGS)
+
+
+def last_error():
+    return lib().aem_last_error().decode(errors="replace")
+
+
+def check(status, what=""):
+    """Raises the exception matching an aem_status."""
+    if status == AEM_OK:
+        return
+    msg = last_error()
+    if what:
+        msg = f"{what}: {msg}"
+    if status == AEM_EINVAL:
+        raise ValueError(msg)
+    if status == AEM_ETIMEOUT:
+        raise AemTimeout(status, msg)
+    raise AemError(status, msg)
+
+
+def device_count():
+    return lib().aem_device_count()
+
+
+# ------------------------------------------------------------------ contexts
+_contexts = {}
+
+
+def context(device=0):
+    """Per-device staging context for the *_host calls (created lazily)."""
+    c = _contexts.get(device)
+    if c is None:
+        h = _vp()
+        check(lib().aem_context_create(device, ctypes.byref(h)), "aem_context_create")
+        c = h.value
+        _contexts[device] = c
+    return c
+
+
+class Gate:
+    """Packed gating layer (device-resident [D/4][Epad][4] copy of W [D, E])."""
+
+    def __init__(self, gate_weight, gate_bias, device=0):
+        import numpy as np
+        w = np.ascontiguousarray(gate_weight, dtype=np.float32)
+        if w.ndim != 2:
+            raise ValueError("gate_weight must be [D, E]")
+        d, e = w.shape
+        b = None if gate_bias is None else np.ascontiguousarray(gate_bias, dtype=np.float32).reshape(-1)
+        if b is not None and b.shape[0] != e:
+            raise ValueError(f"gate_bias has {b.shape[0]} entries, expected {e}")
+        h = _vp()
+        check(lib().aem_gate_pack(w.ctypes.data, None if b is None else b.ctypes.data, d, e,
+                                  device, ctypes.byref(h)), "aem_gate_pack")
+        self.handle = h.value
+        self.D, self.E, self.device = d, e, device
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().aem_gate_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class QWeight:
+    """Packed INT8 weight groups: q [G][K][N] int8 + scale [G][N] -> device [G][N][K]."""
+
+    def __init__(self, q, scale, device=0):
+        import numpy as np
+        q = np.ascontiguousarray(q, dtype=np.int8)
+        if q.ndim == 2:
+            q = q[None]
+        g, k, n = q.shape
+        s = np.ascontiguousarray(scale, dtype=np.float32).reshape(g, n)
+        h = _vp()
+        check(lib().aem_qweight_pack(q.ctypes.data, s.ctypes.data, g, k, n, device,
+                                     ctypes.byref(h)), "aem_qweight_pack")
+        self.handle = h.value
+        self.G, self.K, self.N, self.device = g, k, n, device
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().aem_qweight_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,428 @@
+// Fused MoE gating on sm_100a: logits = hidden @ W + b, top-k by repeated
+// strict-greater max extraction (ties -> lowest expert id), softmax over the
+// k selected logits -- the semantics of fused_gating
+// (src/kernels/fused_gating_metal.py:236-307, :361-435) and of its NumPy
+// specification fused_kernel_simulation (prototype/math_proto.py:19-50).
+//
+// Design (B200): lanes own experts, not slices of d.  A warp is split into
+// lane groups of GROUP lanes (8, 16 or 32); a group owns TPG tokens and lane
+// `le` of the group owns experts le, le+GROUP, ...  Every (token, expert)
+// logit is therefore one sequential dot product inside one thread -- no
+// cross-lane reduction -- which makes the EXACT mode possible: float32
+// products summed in float32 in increasing d order (bit-identical to the
+// reference loop), computed two tokens at a time with the sm_100 packed
+// fp32x2 multiply/add so the exact arithmetic runs at FMA rate.
+// The CTA stages a 64-wide (or narrower for large E) chunk of d of the
+// packed weight ([d/4][Epad][4], contiguous per chunk) and of its tokens'
+// activations in shared memory; every weight chunk is reused by all tokens
+// of the CTA.  The top-k is a register/shuffle argmax inside the lane group.
+#include <cuda_bf16.h>
+
+#include <cfloat>
+
+#include "common.cuh"
+#include "runtime.h"
+
+namespace aem {
+
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kTPG = 4;  // tokens per lane group
+
+template <typename XT>
+__device__ __forceinline__ float load_x(const XT* p);
+template <>
+__device__ __forceinline__ float load_x<float>(const float* p) {
+    return *p;
+}
+template <>
+__device__ __forceinline__ float load_x<__nv_bfloat16>(const __nv_bfloat16* p) {
+    return __bfloat162float(*p);
+}
+
+template <typename XT>
+__device__ __forceinline__ float4 load_x4(const XT* p);
+template <>
+__device__ __forceinline__ float4 load_x4<float>(const float* p) {
+    return *reinterpret_cast<const float4*>(p);
+}
+template <>
+__device__ __forceinline__ float4 load_x4<__nv_bfloat16>(const __nv_bfloat16* p) {
+    uint2 u = *reinterpret_cast<const uint2*>(p);
+    float4 f;
+    f.x = __uint_as_float(u.x << 16);
+    f.y = __uint_as_float(u.x & 0xFFFF0000u);
+    f.z = __uint_as_float(u.y << 16);
+    f.w = __uint_as_float(u.y & 0xFFFF0000u);
+    return f;
+}
+
+template <int GROUP, int NSLOT, typename XT, bool EXACT>
+__global__ void __launch_bounds__(kThreads)
+    gating_kernel(const XT* __restrict__ x, const float4* __restrict__ wpk,
+                  const float* __restrict__ bias, int64_t N, int D, int E, int k, int ksel,
+                  int32_t* __restrict__ idx_out, float* __restrict__ val_out) {
+    constexpr int GPW = 32 / GROUP;
+    constexpr int TOK = kWarps * GPW * kTPG;  // tokens per CTA
+    constexpr int EPAD = GROUP * NSLOT;
+    constexpr int DK = EPAD <= 64 ? 64 : (EPAD <= 128 ? 32 : 16);
+    constexpr int DK4 = DK / 4;
+    constexpr int XS = DK + 4;                // padded row of the activation chunk
+    constexpr int KS = EPAD < 65 ? EPAD : 65;  // stored selections per token
+
+    __shared__ float4 ws[DK4 * EPAD];
+    __shared__ __align__(16) float xs[TOK * XS];
+    __shared__ float tv[TOK * KS];
+    __shared__ int te[TOK * KS];
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int grp = lane / GROUP;
+    const int le = lane % GROUP;
+    const int64_t tok0 = static_cast<int64_t>(blockIdx.x) * TOK;
+    const int tbase = (warp * GPW + grp) * kTPG;  // first local token of this lane group
+
+    float acc[kTPG][NSLOT];
+#pragma unroll
+    for (int i = 0; i < kTPG; ++i)
+#pragma unroll
+        for (int s = 0; s < NSLOT; ++s) acc[i][s] = 0.0f;
+
+    const bool vec_ok = (D & 3) == 0;
+    const int nchunks = (D + DK - 1) / DK;
+    for (int c = 0; c < nchunks; ++c) {
+        const int d0 = c * DK;
+        // weight chunk: contiguous DK4*EPAD float4 in the packed layout
+        const float4* wsrc = wpk + static_cast<int64_t>(c) * DK4 * EPAD;
+        for (int i = tid; i < DK4 * EPAD; i += kThreads) ws[i] = __ldg(wsrc + i);
+        // activation chunk (zero beyond D and beyond N)
+        for (int i = tid; i < TOK * DK4; i += kThreads) {
+            const int t = i / DK4;
+            const int q = i % DK4;
+            const int64_t tg = tok0 + t;
+            const int d = d0 + 4 * q;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (tg < N) {
+                const XT* row = x + tg * static_cast<int64_t>(D);
+                if (vec_ok) {
+                    if (d < D) v = load_x4<XT>(row + d);
+                } else {
+                    if (d + 0 < D) v.x = load_x<XT>(row + d + 0);
+                    if (d + 1 < D) v.y = load_x<XT>(row + d + 1);
+                    if (d + 2 < D) v.z = load_x<XT>(row + d + 2);
+                    if (d + 3 < D) v.w = load_x<XT>(row + d + 3);
+                }
+            }
+            *reinterpret_cast<float4*>(&xs[t * XS + 4 * q]) = v;
+        }
+        __syncthreads();
+
+#pragma unroll 4
+        for (int q = 0; q < DK4; ++q) {
+            float4 xv[kTPG];
+#pragma unroll
+            for (int i = 0; i < kTPG; ++i)
+                xv[i] = *reinterpret_cast<const float4*>(&xs[(tbase + i) * XS + 4 * q]);
+#pragma unroll
+            for (int s = 0; s < NSLOT; ++s) {
+                const float4 wv = ws[q * EPAD + le + GROUP * s];
+                if constexpr (EXACT) {
+                    // float32 product, then float32 add, d in increasing order;
+                    // two tokens per packed fp32x2 op.
+#pragma unroll
+                    for (int i = 0; i < kTPG; i += 2) {
+                        float2 a = make_float2(acc[i][s], acc[i + 1][s]);
+                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xv[i].x, xv[i + 1].x),
+                                                     make_float2(wv.x, wv.x)));
+                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xv[i].y, xv[i + 1].y),
+                                                     make_float2(wv.y, wv.y)));
+                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xv[i].z, xv[i + 1].z),
+                                                     make_float2(wv.z, wv.z)));
+                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xv[i].w, xv[i + 1].w),
+                                                     make_float2(wv.w, wv.w)));
+                        acc[i][s] = a.x;
+                        acc[i + 1][s] = a.y;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < kTPG; ++i) {
+                        acc[i][s] = fmaf(xv[i].x, wv.x, acc[i][s]);
+                        acc[i][s] = fmaf(xv[i].y, wv.y, acc[i][s]);
+                        acc[i][s] = fmaf(xv[i].z, wv.z, acc[i][s]);
+                        acc[i][s] = fmaf(xv[i].w, wv.w, acc[i][s]);
+                    }
+                }
+            }
+        }
+        __syncthreads();
+    }
+
+    // ---- bias, top-k selection, softmax (per lane group, per token)
+    float bv[NSLOT];
+#pragma unroll
+    for (int s = 0; s < NSLOT; ++s) {
+        const int e = le + GROUP * s;
+        bv[s] = e < E ? __ldg(bias + e) : 0.0f;
+    }
+    const unsigned gmask =
+        GROUP == 32 ? 0xFFFFFFFFu : (((1u << GROUP) - 1u) << (grp * GROUP));
+#pragma unroll
+    for (int i = 0; i < kTPG; ++i) {
+        const int tl = tbase + i;
+        const int64_t tg = tok0 + tl;
+        float v[NSLOT];
+#pragma unroll
+        for (int s = 0; s < NSLOT; ++s) {
+            const int e = le + GROUP * s;
+            v[s] = e < E ? __fadd_rn(acc[i][s], bv[s]) : -FLT_MAX;
+        }
+        for (int kk = 0; kk < ksel; ++kk) {
+            float best = -INFINITY;
+            int beste = 0x7FFFFFFF;
+#pragma unroll
+            for (int s = 0; s < NSLOT; ++s) {
+                const int e = le + GROUP * s;
+                if (e < E && v[s] > best) {  // strict: lowest id wins ties within the lane
+                    best = v[s];
+                    beste = e;
+                }
+            }
+#pragma unroll
+            for (int off = GROUP / 2; off >= 1; off >>= 1) {
+                const float ob = __shfl_xor_sync(gmask, best, off, GROUP);
+                const int oe = __shfl_xor_sync(gmask, beste, off, GROUP);
+                if (ob > best || (ob == best && oe < beste)) {
+                    best = ob;
+                    beste = oe;
+                }
+            }
+            // remove the winner from its owner lane
+#pragma unroll
+            for (int s = 0; s < NSLOT; ++s)
+                if (le + GROUP * s == beste) v[s] = -INFINITY;
+            if (le == 0 && kk < KS) {
+                tv[tl * KS + kk] = best;
+                te[tl * KS + kk] = beste;
+            }
+        }
+        __syncwarp(gmask);
+        if (tg < N) {
+            const float m = tv[tl * KS];
+            float sum = 0.0f;
+            for (int kk = 0; kk < k; ++kk) sum = __fadd_rn(sum, expf(tv[tl * KS + kk] - m));
+            for (int kk = le; kk < ksel; kk += GROUP) {
+                idx_out[tg * ksel + kk] = te[tl * KS + kk];
+                if (kk < k) val_out[tg * k + kk] = __fdiv_rn(expf(tv[tl * KS + kk] - m), sum);
+            }
+        }
+        __syncwarp(gmask);
+    }
+}
+
+template <int GROUP, int NSLOT, typename XT, bool EXACT>
+cudaError_t launch_one(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
+                       float* val, cudaStream_t s) {
+    constexpr int TOK = kWarps * (32 / GROUP) * kTPG;
+    const int64_t blocks = (N + TOK - 1) / TOK;
+    gating_kernel<GROUP, NSLOT, XT, EXACT><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(
+        static_cast<const XT*>(x), reinterpret_cast<const float4*>(g.wt), g.bias, N,
+        static_cast<int>(g.D), static_cast<int>(g.E), k, ksel, idx, val);
+    return cudaGetLastError();
+}
+
+template <typename XT, bool EXACT>
+cudaError_t dispatch_e(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
+                       float* val, cudaStream_t s) {
+    switch (g.Epad) {
+        case 8: return launch_one<8, 1, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+        case 16: return launch_one<16, 1, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+        case 32: return launch_one<32, 1, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+        case 64: return launch_one<32, 2, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+        case 128: return launch_one<32, 4, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+        default: return launch_one<32, 8, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+    }
+}
+
+// Packs W [D, E] (device, row-major) into [Dpad/4][Epad][4].
+__global__ void pack_gate_kernel(const float* __restrict__ w, const float* __restrict__ b, int64_t D,
+                                 int64_t E, int64_t Dpad, int64_t Epad, float* __restrict__ out,
+                                 float* __restrict__ bout) {
+    const int64_t total = Dpad * Epad;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t c = i & 3;
+        const int64_t e = (i >> 2) % Epad;
+        const int64_t d4 = (i >> 2) / Epad;
+        const int64_t d = d4 * 4 + c;
+        out[i] = (d < D && e < E) ? w[d * E + e] : 0.0f;
+    }
+    for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < Epad;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        bout[e] = (e < E && b) ? b[e] : 0.0f;
+}
+
+}  // namespace
+
+int gate_epad(int64_t E) {
+    if (E <= 8) return 8;
+    if (E <= 16) return 16;
+    if (E <= 32) return 32;
+    if (E <= 64) return 64;
+    if (E <= 128) return 128;
+    return 256;
+}
+
+aem_status launch_gating(const Gate& g, const void* x, aem_dtype xd, int64_t N, int k, int ksel,
+                         aem_gating_mode mode, int32_t* idx, float* val, cudaStream_t s) {
+    if (N == 0) return AEM_OK;
+    cudaError_t e;
+    const bool exact = mode == AEM_GATING_EXACT;
+    if (xd == AEM_F32)
+        e = exact ? dispatch_e<float, true>(g, x, N, k, ksel, idx, val, s)
+                  : dispatch_e<float, false>(g, x, N, k, ksel, idx, val, s);
+    else
+        e = exact ? dispatch_e<__nv_bfloat16, true>(g, x, N, k, ksel, idx, val, s)
+                  : dispatch_e<__nv_bfloat16, false>(g, x, N, k, ksel, idx, val, s);
+    if (e != cudaSuccess) {
+        set_error("gating kernel launch failed: %s", cudaGetErrorString(e));
+        return AEM_ECUDA;
+    }
+    return AEM_OK;
+}
+
+}  // namespace aem
+
+using aem::set_error;
+
+namespace {
+aem_status check_gating_args(const aem::Gate* g, const void* x, aem_dtype xd, int64_t N, int k,
+                             int k_extra, const void* idx, const void* val) {
+    AEM_REQUIRE(g != nullptr, "gating: gate handle is NULL");
+    AEM_REQUIRE(xd == AEM_F32 || xd == AEM_BF16, "gating: hidden dtype must be F32 or BF16");
+    AEM_REQUIRE(N >= 0, "gating: N=%lld must be >= 0", (long long)N);
+    AEM_REQUIRE(k >= 1, "gating: k=%d must be >= 1", k);
+    AEM_REQUIRE(k <= AEM_MAX_TOPK && k <= g->E,
+                "k=%d invalid for num_experts=%lld (MAX_TOPK=%d)", k, (long long)g->E,
+                AEM_MAX_TOPK);
+    AEM_REQUIRE(k_extra == 0 || k_extra == 1, "gating: k_extra=%d must be 0 or 1", k_extra);
+    AEM_REQUIRE(k + k_extra <= g->E,
+                "gating: k + k_extra = %d exceeds num_experts=%lld", k + k_extra, (long long)g->E);
+    AEM_REQUIRE(N == 0 || (x && idx && val), "gating: NULL buffer");
+    return AEM_OK;
+}
+}  // namespace
+
+extern "C" {
+
+aem_status aem_gate_pack(const float* gate_weight, const float* gate_bias, int64_t D, int64_t E,
+                         int device, aem_gate_t* out) {
+    AEM_REQUIRE(out != nullptr, "aem_gate_pack: out is NULL");
+    *out = nullptr;
+    AEM_REQUIRE(gate_weight != nullptr, "aem_gate_pack: gate_weight is NULL");
+    AEM_REQUIRE(D >= 1 && E >= 1, "aem_gate_pack: D=%lld E=%lld must be >= 1", (long long)D,
+                (long long)E);
+    AEM_REQUIRE(E <= AEM_MAX_EXPERTS,
+                "num_experts=%lld exceeds this kernel's MAX_EXPERTS=%d", (long long)E,
+                AEM_MAX_EXPERTS);
+    AEM_REQUIRE(D <= (1ll << 30), "aem_gate_pack: D too large");
+    if (!aem::is_sm100(device)) {
+        set_error("aem_gate_pack: device %d is not an sm_100 (B200) GPU", device);
+        return AEM_EUNSUPPORTED;
+    }
+    AEM_TRY_CUDA(cudaSetDevice(device));
+    auto* g = new aem::Gate();
+    g->device = device;
+    g->D = D;
+    g->E = E;
+    g->Epad = aem::gate_epad(E);
+    g->Dpad = (D + 63) / 64 * 64;
+    float* tmp_w = nullptr;
+    float* tmp_b = nullptr;
+    aem_status st = AEM_OK;
+    do {
+        if (cudaMalloc(&g->wt, sizeof(float) * g->Dpad * g->Epad) != cudaSuccess ||
+            cudaMalloc(&g->bias, sizeof(float) * g->Epad) != cudaSuccess ||
+            cudaMalloc(&tmp_w, sizeof(float) * D * E) != cudaSuccess ||
+            cudaMalloc(&tmp_b, sizeof(float) * E) != cudaSuccess) {
+            set_error("aem_gate_pack: device allocation failed");
+            st = AEM_ENOMEM;
+            break;
+        }
+        if (cudaMemcpy(tmp_w, gate_weight, sizeof(float) * D * E, cudaMemcpyHostToDevice) !=
+                cudaSuccess ||
+            (gate_bias && cudaMemcpy(tmp_b, gate_bias, sizeof(float) * E,
+                                     cudaMemcpyHostToDevice) != cudaSuccess)) {
+            set_error("aem_gate_pack: copy failed");
+            st = AEM_ECUDA;
+            break;
+        }
+        aem::pack_gate_kernel<<<256, 256>>>(tmp_w, gate_bias ? tmp_b : nullptr, D, E, g->Dpad,
+                                             g->Epad, g->wt, g->bias);
+        if (cudaDeviceSynchronize() != cudaSuccess) {
+            set_error("aem_gate_pack: pack kernel failed: %s",
+                      cudaGetErrorString(cudaGetLastError()));
+            st = AEM_ECUDA;
+            break;
+        }
+    } while (0);
+    cudaFree(tmp_w);
+    cudaFree(tmp_b);
+    if (st != AEM_OK) {
+        cudaFree(g->wt);
+        cudaFree(g->bias);
+        delete g;
+        return st;
+    }
+    *out = reinterpret_cast<aem_gate_t>(g);
+    return AEM_OK;
+}
+
+aem_status aem_gate_free(aem_gate_t gate) {
+    if (!gate) return AEM_OK;
+    auto* g = reinterpret_cast<aem::Gate*>(gate);
+    cudaSetDevice(g->device);
+    cudaFree(g->wt);
+    cudaFree(g->bias);
+    delete g;
+    return AEM_OK;
+}
+
+aem_status aem_gating(aem_gate_t gate, const void* hidden, aem_dtype hidden_dtype, int64_t N,
+                      int k, int k_extra, aem_gating_mode mode, int32_t* out_idx, float* out_val,
+                      void* stream) {
+    auto* g = reinterpret_cast<aem::Gate*>(gate);
+    AEM_TRY(check_gating_args(g, hidden, hidden_dtype, N, k, k_extra, out_idx, out_val));
+    return aem::launch_gating(*g, hidden, hidden_dtype, N, k, k + k_extra, mode, out_idx, out_val,
+                              static_cast<cudaStream_t>(stream));
+}
+
+aem_status aem_gating_host(aem_context_t ctx, aem_gate_t gate, const void* hidden,
+                           aem_dtype hidden_dtype, int64_t N, int k, int k_extra,
+                           aem_gating_mode mode, int32_t* out_idx, float* out_val) {
+    AEM_REQUIRE(ctx != nullptr, "aem_gating_host: context is NULL");
+    auto* c = reinterpret_cast<aem::Context*>(ctx);
+    auto* g = reinterpret_cast<aem::Gate*>(gate);
+    AEM_TRY(check_gating_args(g, hidden, hidden_dtype, N, k, k_extra, out_idx, out_val));
+    if (N == 0) return AEM_OK;
+    AEM_TRY_CUDA(cudaSetDevice(c->device));
+    const int ksel = k + k_extra;
+    const size_t xb = static_cast<size_t>(N) * g->D * (hidden_dtype == AEM_F32 ? 4 : 2);
+    const size_t ib = static_cast<size_t>(N) * ksel * 4;
+    const size_t vb = static_cast<size_t>(N) * k * 4;
+    const size_t o1 = aem::align_up(xb, 256), o2 = o1 + aem::align_up(ib, 256);
+    AEM_TRY(c->reserve_device(o2 + vb));
+    char* d = static_cast<char*>(c->dev);
+    AEM_TRY_CUDA(cudaMemcpyAsync(d, hidden, xb, cudaMemcpyHostToDevice, c->stream));
+    AEM_TRY(aem::launch_gating(*g, d, hidden_dtype, N, k, ksel, mode,
+                               reinterpret_cast<int32_t*>(d + o1), reinterpret_cast<float*>(d + o2),
+                               c->stream));
+    AEM_TRY_CUDA(cudaMemcpyAsync(out_idx, d + o1, ib, cudaMemcpyDeviceToHost, c->stream));
+    AEM_TRY_CUDA(cudaMemcpyAsync(out_val, d + o2, vb, cudaMemcpyDeviceToHost, c->stream));
+    AEM_TRY_CUDA(cudaStreamSynchronize(c->stream));
+    return AEM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,46 @@
+// Internal interface of the single-GPU MoE layer (moe.cu), reused by the
+// expert-parallel layer for its local expert FFN.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "aem.h"
+#include "runtime.h"
+
+namespace aem {
+
+aem_status gather_rows(const void* x, aem_dtype xd, const int32_t* src, int64_t rows, int64_t d,
+                       void* out, cudaStream_t s);
+aem_status combine_rows(const float* y, int64_t T, int k, int64_t d, void* out, aem_dtype od,
+                        cudaStream_t s);
+
+struct Moe {
+    aem_moe_config cfg{};
+    Gate* gate = nullptr;
+    QWeight* up = nullptr;
+    QWeight* down = nullptr;
+    int64_t T_cap = 0;
+    int64_t last_T = 0;
+    void* buf = nullptr;
+    int32_t* idx = nullptr;
+    float* val = nullptr;
+    void* route_ws = nullptr;
+    uint32_t* eff = nullptr;
+    int* starts = nullptr;
+    int32_t* src_token = nullptr;
+    int32_t* rowmap = nullptr;
+    float* rowscale = nullptr;
+    void* xperm = nullptr;  // bf16 [U, d]
+    void* h = nullptr;      // bf16 [U, ffn]
+    float* y = nullptr;     // f32 [T*k, d]
+
+    aem_status reserve(int64_t T);
+    aem_status forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dtype od,
+                       cudaStream_t s);
+    // Grouped up GEMM + ReLU, grouped down GEMM (scaled by the gate weight,
+    // scattered to row t*k+j), combine -- on xperm/starts/rowmap/rowscale.
+    aem_status expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaStream_t s);
+};
+
+}  // namespace aem

@@ -1,0 +1,477 @@
+// Grouped INT8 weight-only GEMM on the sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+//   out[r, n] = epilogue( scale[g][n] * sum_k x[r, k] * q[g][n, k] )   for row r of group g
+//
+// This is the B200 form of fused_quantized_matmul (src/kernels/quantized_gemm.py:99-138,
+// :184-226): weights stay INT8 in HBM and are dequantised at multiply time.  The
+// multiply itself runs on the 5th-generation tensor cores, so the kernel is
+// organised weights-stationary: a tile is 128 output channels (the MMA's M) by BT
+// activation rows (the MMA's N, 16..256), which keeps decode-size batches (a handful
+// of rows) on the tensor cores with the int8 weight stream as the only large read.
+//
+// Per CTA (one per SM, persistent over tiles), 10 warps:
+//   warp 8      TMA producer: int8 weight tile [128 x 64 B] (no swizzle) and the bf16
+//               activation tile(s) [BT x 128 B] (128-byte swizzle) into a STAGES ring.
+//   warps 0-3   converters: int8 -> bf16 (exact: |q| <= 127 fits bf16's 8-bit
+//               significand) written straight into the 128-byte-swizzled K-major layout
+//               the MMA reads, then fence.proxy.async + mbarrier arrive.
+//   warp 9      MMA issuer (one thread): 4 x tcgen05.mma kind::f16 (K=16 each) per
+//               64-wide stage, x2 for split float32 activations (hi + lo), accumulating
+//               float32 in a double-buffered TMEM accumulator; tcgen05.commit frees the
+//               smem stage and, at the end of a tile, hands the accumulator over.
+//   warps 4-7   epilogue: tcgen05.ld 32 lanes x 16 columns, per-channel scale, optional
+//               per-row multiplier, ReLU, bf16/f32 store or red.add (split-K), optional
+//               output-row remap (MoE scatter).
+// Every mbarrier wait is bounded (globaltimer); on timeout the kernel records an
+// error bit, all roles drain out, and TMEM is released.  No multicast is used.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "runtime.h"
+
+namespace aem {
+
+aem_status launch_qgemm_simt(const GemmArgs& a, cudaStream_t s);
+
+namespace {
+
+using namespace aem::dev;
+
+constexpr int kCh = 128;      // output channels per tile = MMA M
+constexpr int kKT = 64;       // K per stage: one 128-byte bf16 row
+constexpr int kConvThreads = 128;
+constexpr int kEpiThreads = 128;
+constexpr int kThreads = 320;  // 4 converter + 4 epilogue + producer + MMA warps
+constexpr int kMaxGroups = 256;
+
+struct TcParams {
+    int G;
+    int64_t group_base;
+    int wmod;               // weight group of row group g: group_base + (wmod ? g % wmod : g)
+    const int* group_rows;  // nullptr: one group of M rows
+    int64_t M;
+    int K;
+    int N;
+    int ksplit;
+    const float* scale;     // [Gw][N]
+    void* out;
+    int64_t ldo;
+    int out_bf16;
+    int relu;
+    int atomic_add;
+    const int* rowmap;
+    const float* rowscale;
+    int* err;
+};
+
+template <int BT, int SPLIT>
+struct Cfg {
+    static constexpr int W8 = kCh * kKT;           // int8 staging tile, bytes
+    static constexpr int W16 = kCh * kKT * 2;      // bf16 weight tile (MMA A)
+    static constexpr int XB = BT * kKT * 2;        // bf16 activation tile (MMA B), per part
+    static constexpr int STAGE = W16 + SPLIT * XB + W8;
+    static constexpr int STAGES_RAW = (200 * 1024) / STAGE;
+    static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+    static constexpr int TMEM_COLS = 2 * BT < 32 ? 32 : 2 * BT;
+    static constexpr uint32_t IDESC = idesc_bf16_f32(kCh, BT);
+    static constexpr int BAR_BYTES = (3 * STAGES + 4) * 8 + 16;
+    static constexpr int TAB_BYTES = 2 * (kMaxGroups + 1) * 4;
+    static constexpr int SMEM = 1024 + STAGES * STAGE + BAR_BYTES + TAB_BYTES;
+    static_assert(STAGES >= 2, "pipeline needs two stages");
+    static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N for M=128");
+};
+
+struct TileInfo {
+    int g;
+    int wg;  // weight group (absolute)
+    int n0;
+    int64_t row0;
+    int nrows;
+    int kt0;
+    int kt1;
+};
+
+template <int BT>
+__device__ __forceinline__ TileInfo decode_tile(int t, const int* s_rows, const int* s_tiles,
+                                                const TcParams& p, int nch, int nkt, int kper) {
+    int lo = 0, hi = p.G;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (s_tiles[mid] <= t) lo = mid; else hi = mid;
+    }
+    TileInfo ti;
+    ti.g = lo;
+    ti.wg = static_cast<int>(p.group_base) + (p.wmod ? lo % p.wmod : lo);
+    int r = t - s_tiles[lo];
+    const int cnt = s_rows[lo + 1] - s_rows[lo];
+    const int ntc = (cnt + BT - 1) / BT;
+    const int tc = r % ntc;
+    r /= ntc;
+    const int ks = r % p.ksplit;
+    const int nc = r / p.ksplit;
+    ti.n0 = nc * kCh;
+    ti.row0 = static_cast<int64_t>(s_rows[lo]) + static_cast<int64_t>(tc) * BT;
+    ti.nrows = min(BT, cnt - tc * BT);
+    ti.kt0 = ks * kper;
+    ti.kt1 = min(nkt, ti.kt0 + kper);
+    (void)nch;
+    return ti;
+}
+
+// 4 signed bytes -> 2 words of bf16x2 (exact).  Each byte b becomes the float
+// 2^23 + (b + 128) by byte permutation, minus (2^23 + 128); the bf16 is the
+// float's upper half (integers |b| <= 128 have no low mantissa bits).
+__device__ __forceinline__ uint2 i8x4_to_bf16x4(uint32_t v) {
+    const uint32_t u = v ^ 0x80808080u;
+    const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)) - 8388736.0f;
+    const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441)) - 8388736.0f;
+    const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)) - 8388736.0f;
+    const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443)) - 8388736.0f;
+    uint2 o;
+    o.x = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
+    o.y = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
+    return o;
+}
+
+template <int BT, int SPLIT>
+__global__ void __launch_bounds__(kThreads, 1)
+    qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
+                    const __grid_constant__ CUtensorMap tm_xh,
+                    const __grid_constant__ CUtensorMap tm_xl, const TcParams p) {
+    using C = Cfg<BT, SPLIT>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* stage_base = smem;
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE);
+    uint64_t* conv_bar = full_bar + C::STAGES;
+    uint64_t* empty_bar = conv_bar + C::STAGES;
+    uint64_t* accf_bar = empty_bar + C::STAGES;  // [2]
+    uint64_t* acce_bar = accf_bar + 2;           // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* s_rows = reinterpret_cast<int*>(smem + C::STAGES * C::STAGE + C::BAR_BYTES);
+    int* s_tiles = s_rows + (kMaxGroups + 1);
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+
+    // ---- setup: barriers, group table, TMEM
+    if (tid == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&conv_bar[s], kConvThreads);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&accf_bar[b], 1);
+            mbar_init(&acce_bar[b], kEpiThreads);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    for (int i = tid; i <= p.G; i += kThreads)
+        s_rows[i] = p.group_rows ? p.group_rows[i] : (i == 0 ? 0 : static_cast<int>(p.M));
+    if (warp == 9) {
+        tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    if (warp == 8 && lane == 0) {
+        tma_prefetch_desc(&tm_w);
+        tma_prefetch_desc(&tm_xh);
+        if (SPLIT == 2) tma_prefetch_desc(&tm_xl);
+    }
+    const int nch = (p.N + kCh - 1) / kCh;
+    const int nkt = (p.K + kKT - 1) / kKT;
+    const int kper = (nkt + p.ksplit - 1) / p.ksplit;
+    __syncthreads();
+    if (tid == 0) {
+        int acc = 0;
+        bool bad = false;
+        for (int g = 0; g < p.G; ++g) {
+            s_tiles[g] = acc;
+            const int cnt = s_rows[g + 1] - s_rows[g];
+            if (cnt < 0) bad = true;
+            acc += (cnt > 0 ? (cnt + BT - 1) / BT : 0) * nch * p.ksplit;
+        }
+        s_tiles[p.G] = acc;
+        if (bad) {
+            atomicOr(p.err, ERR_GEMM_GROUPS);
+            s_tiles[p.G] = 0;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total = s_tiles[p.G];
+
+    if (warp == 8) {
+        // ================= TMA producer
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+                const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
+                const int wrow = ti.wg * p.N + ti.n0;
+                for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
+                    if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1, abort_flag, p.err,
+                                           ERR_GEMM_TIMEOUT))
+                        break;
+                    uint8_t* st = stage_base + s * C::STAGE;
+                    mbar_arrive_expect_tx(&full_bar[s], C::W8 + SPLIT * C::XB);
+                    tma_load_2d(st + C::W16 + SPLIT * C::XB, &tm_w, &full_bar[s], kt * kKT, wrow);
+                    tma_load_2d(st + C::W16, &tm_xh, &full_bar[s], kt * kKT,
+                                static_cast<int>(ti.row0));
+                    if (SPLIT == 2)
+                        tma_load_2d(st + C::W16 + C::XB, &tm_xl, &full_bar[s], kt * kKT,
+                                    static_cast<int>(ti.row0));
+                    if (++s == C::STAGES) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp == 9) {
+        // ================= MMA issuer
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            int it = 0;
+            for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++it) {
+                const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
+                const int b = it & 1;
+                const uint32_t aph = (it >> 1) & 1;
+                if (!mbar_wait_bounded(&acce_bar[b], aph ^ 1, abort_flag, p.err, ERR_GEMM_TIMEOUT))
+                    break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BT);
+                bool ok = true;
+                for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
+                    if (!mbar_wait_bounded(&full_bar[s], ph, abort_flag, p.err, ERR_GEMM_TIMEOUT) ||
+                        !mbar_wait_bounded(&conv_bar[s], ph, abort_flag, p.err, ERR_GEMM_TIMEOUT)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint8_t* st = stage_base + s * C::STAGE;
+                    const uint64_t adesc = smem_desc_sw128(smem_u32(st));
+                    const uint64_t bdesc = smem_desc_sw128(smem_u32(st + C::W16));
+                    const uint64_t ldesc = smem_desc_sw128(smem_u32(st + C::W16 + C::XB));
+#pragma unroll
+                    for (int kk = 0; kk < kKT / 16; ++kk) {
+                        // +32 bytes along K per UMMA_K=16 step (start address field, >>4)
+                        tc_mma_f16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, C::IDESC,
+                                   (kt > ti.kt0 || kk > 0) ? 1u : 0u);
+                        if (SPLIT == 2)
+                            tc_mma_f16(d_tmem, adesc + 2 * kk, ldesc + 2 * kk, C::IDESC, 1u);
+                    }
+                    tc_commit(&empty_bar[s]);
+                    if (++s == C::STAGES) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&accf_bar[b]);
+            }
+        }
+    } else if (warp < 4) {
+        // ================= converters: int8 [128 x 64B] -> bf16 SW128 [128 x 128B]
+        int s = 0;
+        uint32_t ph = 0;
+        for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+            const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
+            bool ok = true;
+            for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
+                if (!mbar_wait_bounded(&full_bar[s], ph, abort_flag, p.err, ERR_GEMM_TIMEOUT)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* st = stage_base + s * C::STAGE;
+                const uint8_t* w8 = st + C::W16 + SPLIT * C::XB;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int item = tid + kConvThreads * i;  // 512 items: 128 rows x 4 chunks
+                    const int r = item >> 2;
+                    const int ch = item & 3;
+                    const uint4 v = *reinterpret_cast<const uint4*>(w8 + r * 64 + ch * 16);
+                    const uint2 a0 = i8x4_to_bf16x4(v.x);
+                    const uint2 a1 = i8x4_to_bf16x4(v.y);
+                    const uint2 a2 = i8x4_to_bf16x4(v.z);
+                    const uint2 a3 = i8x4_to_bf16x4(v.w);
+                    uint8_t* row = st + r * 128;
+                    const int sw = r & 7;
+                    *reinterpret_cast<uint4*>(row + (((2 * ch) ^ sw) << 4)) =
+                        make_uint4(a0.x, a0.y, a1.x, a1.y);
+                    *reinterpret_cast<uint4*>(row + (((2 * ch + 1) ^ sw) << 4)) =
+                        make_uint4(a2.x, a2.y, a3.x, a3.y);
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(&conv_bar[s]);
+                if (++s == C::STAGES) {
+                    s = 0;
+                    ph ^= 1;
+                }
+            }
+            if (!ok) break;
+        }
+    } else {
+        // ================= epilogue (warps 4..7 own TMEM lanes 32*(warp%4) ..)
+        const int q = warp & 3;
+        int it = 0;
+        for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++it) {
+            const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
+            const int b = it & 1;
+            const uint32_t aph = (it >> 1) & 1;
+            if (!mbar_wait_bounded(&accf_bar[b], aph, abort_flag, p.err, ERR_GEMM_TIMEOUT)) break;
+            tc_fence_after();
+            const int n = ti.n0 + q * 32 + lane;
+            const bool nvalid = n < p.N;
+            const float sc =
+                nvalid ? __ldg(p.scale + static_cast<int64_t>(ti.wg) * p.N + n) : 0.0f;
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(b * BT);
+#pragma unroll 1
+            for (int c0 = 0; c0 < BT; c0 += 16) {
+                uint32_t r[16];
+                tc_ld_32x32b_x16(tbase + c0, r);
+                tc_wait_ld();
+                if (nvalid) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int m = c0 + j;
+                        if (m < ti.nrows) {
+                            const int64_t row = ti.row0 + m;
+                            float v = __uint_as_float(r[j]) * sc;
+                            if (p.rowscale) v *= __ldg(p.rowscale + row);
+                            if (p.relu) v = fmaxf(v, 0.0f);
+                            const int64_t orow = p.rowmap ? __ldg(p.rowmap + row) : row;
+                            if (p.out_bf16) {
+                                reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + n] =
+                                    __float2bfloat16_rn(v);
+                            } else if (p.atomic_add) {
+                                atomicAdd(reinterpret_cast<float*>(p.out) + orow * p.ldo + n, v);
+                            } else {
+                                reinterpret_cast<float*>(p.out)[orow * p.ldo + n] = v;
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&acce_bar[b]);
+        }
+    }
+
+    // ---- teardown
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 9) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+template <int BT, int SPLIT>
+aem_status launch_tc(const GemmArgs& a, const TcParams& p, int grid, cudaStream_t s) {
+    using C = Cfg<BT, SPLIT>;
+    const QWeight& w = *a.w;
+    CUtensorMap tw, th, tl;
+    AEM_TRY(make_tmap_2d(&tw, w.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, static_cast<uint64_t>(w.K),
+                         static_cast<uint64_t>(w.G * w.N), kKT, kCh,
+                         CU_TENSOR_MAP_SWIZZLE_NONE));
+    AEM_TRY(make_tmap_2d(&th, a.x_hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                         static_cast<uint64_t>(w.K), static_cast<uint64_t>(a.M), kKT, BT,
+                         CU_TENSOR_MAP_SWIZZLE_128B));
+    if (SPLIT == 2)
+        AEM_TRY(make_tmap_2d(&tl, a.x_lo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                             static_cast<uint64_t>(w.K), static_cast<uint64_t>(a.M), kKT, BT,
+                             CU_TENSOR_MAP_SWIZZLE_128B));
+    else
+        tl = th;
+    auto kern = qgemm_tc_kernel<BT, SPLIT>;
+    AEM_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    kern<<<grid, kThreads, C::SMEM, s>>>(tw, th, tl, p);
+    AEM_CHECK_LAUNCH();
+    return AEM_OK;
+}
+
+template <int SPLIT>
+aem_status launch_bt(int bt, const GemmArgs& a, const TcParams& p, int grid, cudaStream_t s) {
+    switch (bt) {
+        case 16: return launch_tc<16, SPLIT>(a, p, grid, s);
+        case 32: return launch_tc<32, SPLIT>(a, p, grid, s);
+        case 64: return launch_tc<64, SPLIT>(a, p, grid, s);
+        case 128: return launch_tc<128, SPLIT>(a, p, grid, s);
+        default: return launch_tc<256, SPLIT>(a, p, grid, s);
+    }
+}
+
+int64_t tiles_estimate(int64_t M, int G, int bt, int64_t nch, int ks) {
+    const int64_t avg = G > 0 ? (M + G - 1) / G : M;
+    const int64_t per = (avg + bt - 1) / bt;
+    return std::max<int64_t>(1, per * G) * nch * ks;
+}
+
+}  // namespace
+
+aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
+    AEM_REQUIRE(a.w != nullptr, "qgemm: weight handle is NULL");
+    const QWeight& w = *a.w;
+    AEM_REQUIRE(a.G >= 1 && a.G <= kMaxGroups, "qgemm: G=%d outside [1, %d]", a.G, kMaxGroups);
+    AEM_REQUIRE(a.group_base >= 0 && a.group_base + (a.wmod ? a.wmod : a.G) <= w.G,
+                "qgemm: weight group out of range");
+    AEM_REQUIRE(!(a.atomic_add && a.out_bf16), "qgemm: split-K needs float32 output");
+    if (a.M == 0) return AEM_OK;
+    if (w.K % 16 != 0) return launch_qgemm_simt(a, s);
+    AEM_REQUIRE(a.M < (1ll << 31) && w.G * w.N < (1ll << 31), "qgemm: too many rows");
+    const int dev = current_device();
+    const int sms = sm_count(dev);
+    const int64_t nch = (w.N + kCh - 1) / kCh;
+    const int64_t nkt = (w.K + kKT - 1) / kKT;
+
+    int bt = a.token_tile;
+    if (bt == 0) {
+        const int64_t avg = (a.M + a.G - 1) / a.G;
+        bt = avg <= 16 ? 16 : avg <= 32 ? 32 : avg <= 64 ? 64 : avg <= 128 ? 128 : 256;
+        while (bt > 64 && tiles_estimate(a.M, a.G, bt, nch, 1) < 2 * sms) bt >>= 1;
+    }
+    int ks = a.ksplit < 1 ? 1 : a.ksplit;
+    if (ks > nkt) ks = static_cast<int>(nkt);
+    const int kper = static_cast<int>((nkt + ks - 1) / ks);
+    ks = static_cast<int>((nkt + kper - 1) / kper);
+
+    int* err = device_error_word(dev);
+    AEM_REQUIRE(err != nullptr, "qgemm: no device error word");
+    TcParams p;
+    p.G = a.G;
+    p.group_base = a.group_base;
+    p.wmod = a.wmod;
+    p.group_rows = a.group_rows;
+    p.M = a.M;
+    p.K = static_cast<int>(w.K);
+    p.N = static_cast<int>(w.N);
+    p.ksplit = ks;
+    p.scale = w.scale;
+    p.out = a.out;
+    p.ldo = a.ldo;
+    p.out_bf16 = a.out_bf16 ? 1 : 0;
+    p.relu = a.relu ? 1 : 0;
+    p.atomic_add = (a.atomic_add || ks > 1) ? 1 : 0;
+    p.rowmap = a.rowmap;
+    p.rowscale = a.rowscale;
+    p.err = err;
+    AEM_REQUIRE(!(ks > 1 && (a.relu || a.out_bf16)), "qgemm: split-K is float32 without ReLU only");
+
+    // Upper bound of the tiles of all groups: sum_g ceil(rows_g / bt) <= ceil(M / bt) + (#non-empty groups).
+    const int64_t rows = a.max_rows > 0 ? a.max_rows : a.M;
+    const int64_t tiles_ub = ((rows + bt - 1) / bt + std::min<int64_t>(a.G, rows)) * nch * ks;
+    const int grid = static_cast<int>(std::min<int64_t>(sms, std::max<int64_t>(1, tiles_ub)));
+    if (a.x_lo) return launch_bt<2>(bt, a, p, grid, s);
+    return launch_bt<1>(bt, a, p, grid, s);
+}
+
+}  // namespace aem

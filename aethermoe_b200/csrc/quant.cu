@@ -1,0 +1,272 @@
+// INT8 weight-only quantisation (bit-exact with the reference's float32
+// NumPy), packing of INT8 expert weights into the output-channel-major
+// layout the GEMM streams, the float32 -> (bf16 hi, bf16 lo) activation
+// split, and the CUDA-core GEMM used when K is not a multiple of 16.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "runtime.h"
+
+namespace aem {
+
+namespace {
+
+// scale[n] = max(max_k |w[k,n]| / 127, 1e-12) and q = clip(rint(w / scale)),
+// in IEEE float32 exactly as prototype/math_proto.py:63-65 evaluates it
+// (correctly rounded division, round-half-even).  One thread per column;
+// consecutive threads read consecutive columns (coalesced rows).
+__global__ void quantize_kernel(const float* __restrict__ w, int64_t K, int64_t N,
+                                int8_t* __restrict__ q, float* __restrict__ scale) {
+    const int64_t n = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (n >= N) return;
+    float amax = 0.0f;
+    for (int64_t k = 0; k < K; ++k) amax = fmaxf(amax, fabsf(w[k * N + n]));
+    float s = __fdiv_rn(amax, 127.0f);
+    s = fmaxf(s, 1e-12f);
+    scale[n] = s;
+    for (int64_t k = 0; k < K; ++k) {
+        float r = rintf(__fdiv_rn(w[k * N + n], s));
+        r = fminf(fmaxf(r, -127.0f), 127.0f);
+        q[k * N + n] = static_cast<int8_t>(static_cast<int>(r));
+    }
+}
+
+// [G][K][N] -> [G][N][K] via 32x32 shared-memory tiles.
+__global__ void transpose_i8_kernel(const int8_t* __restrict__ in, int64_t K, int64_t N,
+                                    int8_t* __restrict__ out) {
+    __shared__ int8_t tile[32][33];
+    const int64_t g = blockIdx.z;
+    const int64_t k0 = static_cast<int64_t>(blockIdx.y) * 32;
+    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * 32;
+    const int8_t* src = in + g * K * N;
+    int8_t* dst = out + g * K * N;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int64_t k = k0 + i, n = n0 + threadIdx.x;
+        if (k < K && n < N) tile[i][threadIdx.x] = src[k * N + n];
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int64_t n = n0 + i, k = k0 + threadIdx.x;
+        if (k < K && n < N) dst[n * K + k] = tile[threadIdx.x][i];
+    }
+}
+
+// x (float32) -> hi = bf16_rn(x), lo = bf16_rn(x - hi); or bf16 copy.
+__global__ void split_kernel(const float* __restrict__ x, int64_t count,
+                             __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float v = x[i];
+        const __nv_bfloat16 h = __float2bfloat16_rn(v);
+        hi[i] = h;
+        if (lo) lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+    }
+}
+
+// CUDA-core fallback, used only when K % 16 != 0 (the tensor-core path's TMA
+// needs 16-byte rows): one thread per output element, activations as the
+// bf16 hi (+ lo) pair the tensor-core path consumes.
+// out[r, n] = scale[n] * sum_k (hi[r,k] + lo[r,k]) * q[n,k].
+__global__ void qgemm_simt_kernel(const __nv_bfloat16* __restrict__ xh,
+                                  const __nv_bfloat16* __restrict__ xl,
+                                  const int8_t* __restrict__ q, const float* __restrict__ scale,
+                                  int64_t M, int64_t K, int64_t N,
+                                  const int* __restrict__ group_rows, int G, int64_t group_base,
+                                  int wmod,
+                                  void* __restrict__ out, int64_t ldo, bool out_bf16, bool relu,
+                                  bool atomic_add, const int* __restrict__ rowmap,
+                                  const float* __restrict__ rowscale) {
+    const int64_t total = M * N;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / N;
+        const int64_t n = i % N;
+        int g = 0;
+        if (group_rows) {
+            if (r < group_rows[0] || r >= group_rows[G]) continue;
+            while (g < G - 1 && r >= group_rows[g + 1]) ++g;
+        }
+        const int64_t wg = group_base + (wmod ? g % wmod : g);
+        const int8_t* qr = q + (wg * N + n) * K;
+        float acc = 0.0f;
+        for (int64_t k = 0; k < K; ++k) {
+            float xv = __bfloat162float(xh[r * K + k]);
+            if (xl) xv += __bfloat162float(xl[r * K + k]);
+            acc = fmaf(xv, static_cast<float>(qr[k]), acc);
+        }
+        float v = acc * scale[wg * N + n];
+        if (rowscale) v *= rowscale[r];
+        if (relu) v = fmaxf(v, 0.0f);
+        const int64_t orow = rowmap ? rowmap[r] : r;
+        if (out_bf16)
+            static_cast<__nv_bfloat16*>(out)[orow * ldo + n] = __float2bfloat16_rn(v);
+        else if (atomic_add)
+            atomicAdd(static_cast<float*>(out) + orow * ldo + n, v);
+        else
+            static_cast<float*>(out)[orow * ldo + n] = v;
+    }
+}
+
+}  // namespace
+
+aem_status launch_split_bf16(const void* x, aem_dtype xd, int64_t count, void* hi, void* lo,
+                             cudaStream_t s) {
+    if (count == 0) return AEM_OK;
+    if (xd == AEM_BF16) {
+        AEM_TRY_CUDA(cudaMemcpyAsync(hi, x, count * 2, cudaMemcpyDeviceToDevice, s));
+        return AEM_OK;
+    }
+    const int64_t blocks = (count + 255) / 256 < 4096 ? (count + 255) / 256 : 4096;
+    split_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        static_cast<const float*>(x), count, static_cast<__nv_bfloat16*>(hi),
+        static_cast<__nv_bfloat16*>(lo));
+    AEM_CHECK_LAUNCH();
+    return AEM_OK;
+}
+
+aem_status launch_qgemm_simt(const GemmArgs& a, cudaStream_t s) {
+    const QWeight& w = *a.w;
+    if (a.M == 0) return AEM_OK;
+    const int64_t total = a.M * w.N;
+    const int64_t blocks = (total + 255) / 256 < 8192 ? (total + 255) / 256 : 8192;
+    qgemm_simt_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(a.x_hi), static_cast<const __nv_bfloat16*>(a.x_lo), w.q,
+        w.scale, a.M, w.K, w.N, a.group_rows, a.G, a.group_base, a.wmod, a.out, a.ldo, a.out_bf16, a.relu,
+        a.atomic_add || a.ksplit > 1, a.rowmap, a.rowscale);
+    AEM_CHECK_LAUNCH();
+    return AEM_OK;
+}
+
+aem_status pack_qweight_device(const int8_t* q, const float* scale, int64_t G, int64_t K,
+                               int64_t N, cudaStream_t s, QWeight* w) {
+    AEM_TRY_CUDA(cudaMallocAsync(&w->q, static_cast<size_t>(G * K * N), s));
+    AEM_TRY_CUDA(cudaMallocAsync(&w->scale, sizeof(float) * G * N, s));
+    dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((K + 31) / 32),
+              static_cast<unsigned>(G));
+    transpose_i8_kernel<<<grid, dim3(32, 8), 0, s>>>(q, K, N, w->q);
+    AEM_CHECK_LAUNCH();
+    AEM_TRY_CUDA(cudaMemcpyAsync(w->scale, scale, sizeof(float) * G * N, cudaMemcpyDeviceToDevice, s));
+    return AEM_OK;
+}
+
+}  // namespace aem
+
+using aem::set_error;
+
+extern "C" {
+
+aem_status aem_quantize_int8(const float* w, int64_t K, int64_t N, int8_t* q, float* scale,
+                             void* stream) {
+    AEM_REQUIRE(K >= 1 && N >= 1, "aem_quantize_int8: K=%lld N=%lld must be >= 1", (long long)K,
+                (long long)N);
+    AEM_REQUIRE(w && q && scale, "aem_quantize_int8: NULL buffer");
+    auto s = static_cast<cudaStream_t>(stream);
+    aem::quantize_kernel<<<static_cast<unsigned>((N + 127) / 128), 128, 0, s>>>(w, K, N, q, scale);
+    AEM_CHECK_LAUNCH();
+    return AEM_OK;
+}
+
+aem_status aem_quantize_int8_host(aem_context_t ctx, const float* w, int64_t K, int64_t N,
+                                  int8_t* q, float* scale) {
+    AEM_REQUIRE(ctx != nullptr, "aem_quantize_int8_host: context is NULL");
+    AEM_REQUIRE(K >= 1 && N >= 1, "aem_quantize_int8_host: K=%lld N=%lld must be >= 1",
+                (long long)K, (long long)N);
+    AEM_REQUIRE(w && q && scale, "aem_quantize_int8_host: NULL buffer");
+    auto* c = reinterpret_cast<aem::Context*>(ctx);
+    AEM_TRY_CUDA(cudaSetDevice(c->device));
+    const size_t wb = sizeof(float) * K * N, qb = static_cast<size_t>(K * N),
+                 sb = sizeof(float) * N;
+    const size_t o1 = aem::align_up(wb, 256), o2 = o1 + aem::align_up(qb, 256);
+    AEM_TRY(c->reserve_device(o2 + sb));
+    char* d = static_cast<char*>(c->dev);
+    AEM_TRY_CUDA(cudaMemcpyAsync(d, w, wb, cudaMemcpyHostToDevice, c->stream));
+    AEM_TRY(aem_quantize_int8(reinterpret_cast<float*>(d), K, N, reinterpret_cast<int8_t*>(d + o1),
+                              reinterpret_cast<float*>(d + o2), c->stream));
+    AEM_TRY_CUDA(cudaMemcpyAsync(q, d + o1, qb, cudaMemcpyDeviceToHost, c->stream));
+    AEM_TRY_CUDA(cudaMemcpyAsync(scale, d + o2, sb, cudaMemcpyDeviceToHost, c->stream));
+    AEM_TRY_CUDA(cudaStreamSynchronize(c->stream));
+    return AEM_OK;
+}
+
+aem_status aem_qweight_pack_device(const int8_t* q, const float* scale, int64_t G, int64_t K,
+                                   int64_t N, void* stream, aem_qweight_t* out) {
+    AEM_REQUIRE(out != nullptr, "aem_qweight_pack: out is NULL");
+    *out = nullptr;
+    AEM_REQUIRE(q && scale, "aem_qweight_pack: NULL buffer");
+    AEM_REQUIRE(G >= 1 && K >= 1 && N >= 1, "aem_qweight_pack: G=%lld K=%lld N=%lld must be >= 1",
+                (long long)G, (long long)K, (long long)N);
+    AEM_REQUIRE(K <= (1ll << 31) && G * N <= (1ll << 31),
+                "aem_qweight_pack: dimensions exceed 2^31");
+    auto* w = new aem::QWeight();
+    w->device = aem::current_device();
+    w->G = G;
+    w->K = K;
+    w->N = N;
+    aem_status st = aem::pack_qweight_device(q, scale, G, K, N, static_cast<cudaStream_t>(stream), w);
+    if (st != AEM_OK) {
+        cudaFree(w->q);
+        cudaFree(w->scale);
+        delete w;
+        return st;
+    }
+    *out = reinterpret_cast<aem_qweight_t>(w);
+    return AEM_OK;
+}
+
+aem_status aem_qweight_pack(const int8_t* q, const float* scale, int64_t G, int64_t K, int64_t N,
+                            int device, aem_qweight_t* out) {
+    AEM_REQUIRE(out != nullptr, "aem_qweight_pack: out is NULL");
+    *out = nullptr;
+    AEM_REQUIRE(q && scale, "aem_qweight_pack: NULL buffer");
+    AEM_REQUIRE(G >= 1 && K >= 1 && N >= 1, "aem_qweight_pack: G=%lld K=%lld N=%lld must be >= 1",
+                (long long)G, (long long)K, (long long)N);
+    if (!aem::is_sm100(device)) {
+        set_error("aem_qweight_pack: device %d is not an sm_100 (B200) GPU", device);
+        return AEM_EUNSUPPORTED;
+    }
+    AEM_TRY_CUDA(cudaSetDevice(device));
+    int8_t* dq = nullptr;
+    float* ds = nullptr;
+    AEM_TRY_CUDA(cudaMalloc(&dq, static_cast<size_t>(G * K * N)));
+    if (cudaMalloc(&ds, sizeof(float) * G * N) != cudaSuccess) {
+        cudaFree(dq);
+        set_error("aem_qweight_pack: device allocation failed");
+        return AEM_ENOMEM;
+    }
+    aem_status st = AEM_OK;
+    if (cudaMemcpy(dq, q, static_cast<size_t>(G * K * N), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(ds, scale, sizeof(float) * G * N, cudaMemcpyHostToDevice) != cudaSuccess) {
+        set_error("aem_qweight_pack: copy failed");
+        st = AEM_ECUDA;
+    }
+    if (st == AEM_OK) st = aem_qweight_pack_device(dq, ds, G, K, N, nullptr, out);
+    if (st == AEM_OK && cudaDeviceSynchronize() != cudaSuccess) {
+        set_error("aem_qweight_pack: %s", cudaGetErrorString(cudaGetLastError()));
+        st = AEM_ECUDA;
+    }
+    cudaFree(dq);
+    cudaFree(ds);
+    return st;
+}
+
+aem_status aem_qweight_free(aem_qweight_t wh) {
+    if (!wh) return AEM_OK;
+    auto* w = reinterpret_cast<aem::QWeight*>(wh);
+    cudaSetDevice(w->device);
+    cudaDeviceSynchronize();
+    cudaFree(w->q);
+    cudaFree(w->scale);
+    delete w;
+    return AEM_OK;
+}
+
+aem_status aem_qweight_shape(aem_qweight_t wh, int64_t* G, int64_t* K, int64_t* N) {
+    AEM_REQUIRE(wh != nullptr, "aem_qweight_shape: handle is NULL");
+    auto* w = reinterpret_cast<aem::QWeight*>(wh);
+    if (G) *G = w->G;
+    if (K) *K = w->K;
+    if (N) *N = w->N;
+    return AEM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,338 @@
+// Capacity-ceiling routing on the GPU -- Router::assign_effective_experts
+// (src/orchestration/router.hpp:249-266): within each primary-expert group,
+// ranked by batch_position, the first `capacity` units keep their primary and
+// the rest take their own secondary (one hop, router.hpp:21-27).
+//
+// The rank of a unit inside its expert group is a stable counting sort over
+// units in batch_position order:
+//   count   -- per chunk of kChunk consecutive positions, a histogram over experts
+//   scan    -- per expert, exclusive prefix over chunks (+ expert totals/starts)
+//   assign  -- per chunk, stable local ranks from warp match masks + a
+//              cross-warp prefix in shared memory; rank = chunk offset + local
+// All integer; bit-exact with the reference by construction.  The same three
+// kernels, keyed by the effective expert, produce the MoE permutation that
+// groups units by expert for the grouped GEMM.
+#include <algorithm>
+
+#include "common.cuh"
+#include "route.h"
+#include "runtime.h"
+
+namespace aem {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kPerThread = 8;
+constexpr int kChunk = kThreads * kPerThread;  // 2048 positions per chunk
+
+// MoE units, slot-major: u = j*T + t, primary = idx[t][j], secondary = idx[t][k]
+// (the (k+1)-th choice; the primary when the gating produced only k).
+__global__ void build_units_kernel(const int32_t* __restrict__ idx, int64_t T, int ldi, int k,
+                                   int E, uint32_t* __restrict__ prim, uint32_t* __restrict__ sec,
+                                   int* err) {
+    const int64_t n = T * k;
+    for (int64_t u = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; u < n;
+         u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t j = u / T, t = u % T;
+        const int32_t p = idx[t * ldi + j];
+        const int32_t s = ldi > k ? idx[t * ldi + k] : p;
+        if (p < 0 || p >= E || s < 0 || s >= E) atomicOr(err, ERR_ROUTE_EXPERT);
+        prim[u] = static_cast<uint32_t>(p);
+        sec[u] = static_cast<uint32_t>(s);
+    }
+}
+
+// inv[pos[i]] = i with a permutation check; then gathers primary/secondary
+// into position order.
+__global__ void invert_positions_kernel(const uint32_t* __restrict__ pos, int64_t n,
+                                        int32_t* __restrict__ inv, int32_t* __restrict__ seen,
+                                        int* err) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t p = pos[i];
+        if (p >= n) {
+            atomicOr(err, ERR_ROUTE_POSITION);
+            continue;
+        }
+        if (atomicExch(&seen[p], 1) != 0) {
+            atomicOr(err, ERR_ROUTE_POSITION);
+            continue;
+        }
+        inv[p] = static_cast<int32_t>(i);
+    }
+}
+
+__global__ void gather_by_position_kernel(const uint32_t* __restrict__ primary,
+                                          const uint32_t* __restrict__ secondary,
+                                          const int32_t* __restrict__ inv, int64_t n, int E,
+                                          uint32_t* __restrict__ prim_s,
+                                          uint32_t* __restrict__ sec_s, int* err) {
+    for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < n;
+         p += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int32_t i = inv[p];
+        if (i < 0 || i >= n) {  // only after a failed permutation check
+            prim_s[p] = 0;
+            sec_s[p] = 0;
+            continue;
+        }
+        const uint32_t a = primary[i], b = secondary[i];
+        if (a >= static_cast<uint32_t>(E) || b >= static_cast<uint32_t>(E)) {
+            atomicOr(err, ERR_ROUTE_EXPERT);
+            prim_s[p] = 0;
+            sec_s[p] = 0;
+            continue;
+        }
+        prim_s[p] = a;
+        sec_s[p] = b;
+    }
+}
+
+// Histogram of keys per chunk: cnt[c][e].
+__global__ void __launch_bounds__(kThreads)
+    chunk_count_kernel(const uint32_t* __restrict__ key, int64_t n, int E, int* __restrict__ cnt) {
+    __shared__ int h[AEM_MAX_EXPERTS];
+    for (int e = threadIdx.x; e < E; e += kThreads) h[e] = 0;
+    __syncthreads();
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * kChunk;
+    for (int i = threadIdx.x; i < kChunk; i += kThreads) {
+        const int64_t p = base + i;
+        if (p < n) {
+            const uint32_t e = key[p];
+            if (e < static_cast<uint32_t>(E)) atomicAdd(&h[e], 1);
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += kThreads) cnt[static_cast<int64_t>(blockIdx.x) * E + e] = h[e];
+}
+
+// In place: cnt[c][e] -> exclusive prefix over c.  Optionally totals[e] and
+// starts[0..E] (exclusive prefix of totals over e).  One CTA.
+__global__ void __launch_bounds__(kThreads)
+    chunk_scan_kernel(int* __restrict__ cnt, int nchunks, int E, int* __restrict__ starts) {
+    __shared__ int tot[AEM_MAX_EXPERTS];
+    for (int e = threadIdx.x; e < E; e += kThreads) {
+        int run = 0;
+        for (int c = 0; c < nchunks; ++c) {
+            const int v = cnt[static_cast<int64_t>(c) * E + e];
+            cnt[static_cast<int64_t>(c) * E + e] = run;
+            run += v;
+        }
+        tot[e] = run;
+    }
+    __syncthreads();
+    if (starts && threadIdx.x == 0) {
+        int run = 0;
+        for (int e = 0; e < E; ++e) {
+            starts[e] = run;
+            run += tot[e];
+        }
+        starts[E] = run;
+    }
+}
+
+// Stable rank of every position of this chunk within its key group:
+// off[c][key] + number of earlier positions in the chunk with the same key.
+// Calls `emit(p, key, rank)` for every valid position.
+template <typename Emit>
+__device__ __forceinline__ void chunk_ranks(const uint32_t* __restrict__ key, int64_t n, int E,
+                                            const int* __restrict__ off, Emit emit) {
+    __shared__ int run[AEM_MAX_EXPERTS];
+    __shared__ int hw[kWarps][AEM_MAX_EXPERTS];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const unsigned lt = (1u << lane) - 1u;
+    for (int e = tid; e < E; e += kThreads) run[e] = off[static_cast<int64_t>(blockIdx.x) * E + e];
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * kChunk;
+    for (int r = 0; r < kPerThread; ++r) {
+        for (int i = tid; i < kWarps * E; i += kThreads) hw[i / E][i % E] = 0;
+        __syncthreads();
+        const int64_t p = base + static_cast<int64_t>(r) * kThreads + tid;
+        const bool valid = p < n;
+        uint32_t e = valid ? key[p] : 0xFFFFFFFFu;
+        if (e >= static_cast<uint32_t>(E)) e = 0xFFFFFFFFu;
+        const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
+        const int in_warp = __popc(peers & lt);
+        if (e != 0xFFFFFFFFu && in_warp == 0) hw[warp][e] = __popc(peers);
+        __syncthreads();
+        for (int x = tid; x < E; x += kThreads) {
+            int acc = run[x];
+            for (int w = 0; w < kWarps; ++w) {
+                const int v = hw[w][x];
+                hw[w][x] = acc;
+                acc += v;
+            }
+            run[x] = acc;
+        }
+        __syncthreads();
+        if (e != 0xFFFFFFFFu) emit(p, e, hw[warp][e] + in_warp);
+        __syncthreads();
+    }
+}
+
+// Pass 1: effective expert of every position.  EP: rank += corr[slot][key]
+// with slot = p / slot_len (corr == nullptr for a single GPU).
+__global__ void __launch_bounds__(kThreads)
+    assign_kernel(const uint32_t* __restrict__ prim, const uint32_t* __restrict__ sec, int64_t n,
+                  int E, const int* __restrict__ off, uint64_t capacity,
+                  const int64_t* __restrict__ corr, int64_t slot_len,
+                  const int32_t* __restrict__ out_index, uint32_t* __restrict__ eff) {
+    chunk_ranks(prim, n, E, off, [&](int64_t p, uint32_t e, int rank) {
+        int64_t rk = rank;
+        if (corr) rk += corr[(p / slot_len) * E + e];
+        const uint32_t v = static_cast<uint64_t>(rk) < capacity ? e : sec[p];
+        const int64_t o = out_index ? out_index[p] : p;
+        if (o >= 0) eff[o] = v;  // o < 0 only after a failed permutation check
+    });
+}
+
+// Pass 2 (MoE permutation): unit u goes to row starts[e] + rank of the
+// expert-grouped layout; records the token it came from, the output row of
+// its expert result (t*k + j) and its gate weight.
+__global__ void __launch_bounds__(kThreads)
+    scatter_kernel(const uint32_t* __restrict__ eff, int64_t n, int E, const int* __restrict__ off,
+                   const int* __restrict__ starts, int64_t T, int k,
+                   const float* __restrict__ val, int32_t* __restrict__ src_token,
+                   int32_t* __restrict__ rowmap, float* __restrict__ rowscale,
+                   int32_t* __restrict__ dest_of) {
+    chunk_ranks(eff, n, E, off, [&](int64_t u, uint32_t e, int rank) {
+        const int64_t dest = starts[e] + rank;
+        const int64_t j = u / T, t = u % T;
+        src_token[dest] = static_cast<int32_t>(t);
+        rowmap[dest] = static_cast<int32_t>(t * k + j);
+        rowscale[dest] = val[t * k + j];
+        if (dest_of) dest_of[u] = static_cast<int32_t>(dest);
+    });
+}
+
+}  // namespace
+
+int64_t route_chunks(int64_t n) { return (n + kChunk - 1) / kChunk; }
+
+size_t moe_route_workspace(int64_t T, int k, int E) {
+    const int64_t n = T * k;
+    const int64_t c = route_chunks(n) > 0 ? route_chunks(n) : 1;
+    size_t b = 0;
+    b += align_up(sizeof(uint32_t) * n, 256) * 3;      // prim, sec, eff
+    b += align_up(sizeof(int) * c * E, 256) * 2;        // cnt1, cnt2
+    b += align_up(sizeof(int) * (E + 1), 256);          // starts
+    return b;
+}
+
+aem_status route_moe(const MoeRouteArgs& a, cudaStream_t s) {
+    const int64_t n = a.T * a.k;
+    if (n == 0) return AEM_OK;
+    const int64_t c = route_chunks(n);
+    char* w = static_cast<char*>(a.workspace);
+    auto take = [&](size_t bytes) {
+        char* p = w;
+        w += align_up(bytes, 256);
+        return p;
+    };
+    uint32_t* prim = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * n));
+    uint32_t* sec = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * n));
+    uint32_t* eff = a.eff_out ? a.eff_out : reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * n));
+    if (a.eff_out) take(sizeof(uint32_t) * n);
+    int* cnt1 = reinterpret_cast<int*>(take(sizeof(int) * c * a.E));
+    int* cnt2 = reinterpret_cast<int*>(take(sizeof(int) * c * a.E));
+    int* starts = a.starts_out;
+    int* err = device_error_word(current_device());
+    AEM_REQUIRE(err != nullptr, "route: no device error word");
+    const unsigned gb = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 4096));
+    build_units_kernel<<<gb, 256, 0, s>>>(a.idx, a.T, a.ldi, a.k, a.E, prim, sec, err);
+    AEM_CHECK_LAUNCH();
+    chunk_count_kernel<<<static_cast<unsigned>(c), kThreads, 0, s>>>(prim, n, a.E, cnt1);
+    AEM_CHECK_LAUNCH();
+    chunk_scan_kernel<<<1, kThreads, 0, s>>>(cnt1, static_cast<int>(c), a.E, nullptr);
+    AEM_CHECK_LAUNCH();
+    assign_kernel<<<static_cast<unsigned>(c), kThreads, 0, s>>>(
+        prim, sec, n, a.E, cnt1, a.capacity, a.corr, a.T, nullptr, eff);
+    AEM_CHECK_LAUNCH();
+    chunk_count_kernel<<<static_cast<unsigned>(c), kThreads, 0, s>>>(eff, n, a.E, cnt2);
+    AEM_CHECK_LAUNCH();
+    chunk_scan_kernel<<<1, kThreads, 0, s>>>(cnt2, static_cast<int>(c), a.E, starts);
+    AEM_CHECK_LAUNCH();
+    scatter_kernel<<<static_cast<unsigned>(c), kThreads, 0, s>>>(
+        eff, n, a.E, cnt2, starts, a.T, a.k, a.val, a.src_token, a.rowmap, a.rowscale, a.dest_of);
+    AEM_CHECK_LAUNCH();
+    return AEM_OK;
+}
+
+}  // namespace aem
+
+using aem::set_error;
+
+extern "C" {
+
+size_t aem_capacity_route_workspace(int64_t n, int E) {
+    if (n < 0 || E < 1) return 0;
+    const int64_t c = aem::route_chunks(n) > 0 ? aem::route_chunks(n) : 1;
+    size_t b = 0;
+    b += aem::align_up(sizeof(int32_t) * n, 256) * 2;   // inv, seen
+    b += aem::align_up(sizeof(uint32_t) * n, 256) * 2;  // prim_s, sec_s
+    b += aem::align_up(sizeof(int) * c * E, 256);       // chunk counts
+    return b;
+}
+
+aem_status aem_capacity_route(const uint32_t* primary, const uint32_t* secondary,
+                              const uint32_t* batch_position, int64_t n, int E, uint64_t capacity,
+                              uint32_t* effective, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+    AEM_REQUIRE(n >= 0, "aem_capacity_route: n=%lld must be >= 0", (long long)n);
+    AEM_REQUIRE(E >= 1 && E <= AEM_MAX_EXPERTS, "aem_capacity_route: E=%d outside [1, %d]", E,
+                AEM_MAX_EXPERTS);
+    AEM_REQUIRE(n < (1ll << 31), "aem_capacity_route: n too large");
+    if (n == 0) return AEM_OK;
+    AEM_REQUIRE(primary && secondary && batch_position && effective,
+                "aem_capacity_route: NULL buffer");
+    auto s = static_cast<cudaStream_t>(stream);
+    const size_t need = aem_capacity_route_workspace(n, E);
+    bool owned = false;
+    if (!workspace) {
+        AEM_TRY_CUDA(cudaMallocAsync(&workspace, need, s));
+        owned = true;
+    } else {
+        AEM_REQUIRE(workspace_bytes >= need, "aem_capacity_route: workspace %zu < %zu bytes",
+                    workspace_bytes, need);
+    }
+    char* w = static_cast<char*>(workspace);
+    int32_t* inv = reinterpret_cast<int32_t*>(w);
+    w += aem::align_up(sizeof(int32_t) * n, 256);
+    int32_t* seen = reinterpret_cast<int32_t*>(w);
+    w += aem::align_up(sizeof(int32_t) * n, 256);
+    uint32_t* prim_s = reinterpret_cast<uint32_t*>(w);
+    w += aem::align_up(sizeof(uint32_t) * n, 256);
+    uint32_t* sec_s = reinterpret_cast<uint32_t*>(w);
+    w += aem::align_up(sizeof(uint32_t) * n, 256);
+    int* cnt = reinterpret_cast<int*>(w);
+    const int64_t c = aem::route_chunks(n);
+    int* err = aem::device_error_word(aem::current_device());
+    AEM_REQUIRE(err != nullptr, "aem_capacity_route: no device error word");
+    aem_status st = AEM_OK;
+    do {
+        if (cudaMemsetAsync(seen, 0, sizeof(int32_t) * n, s) != cudaSuccess ||
+            cudaMemsetAsync(inv, 0xFF, sizeof(int32_t) * n, s) != cudaSuccess) {
+            set_error("aem_capacity_route: memset failed");
+            st = AEM_ECUDA;
+            break;
+        }
+        const unsigned gb = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 4096));
+        aem::invert_positions_kernel<<<gb, 256, 0, s>>>(batch_position, n, inv, seen, err);
+        aem::gather_by_position_kernel<<<gb, 256, 0, s>>>(primary, secondary, inv, n, E, prim_s,
+                                                          sec_s, err);
+        aem::chunk_count_kernel<<<static_cast<unsigned>(c), aem::kThreads, 0, s>>>(prim_s, n, E, cnt);
+        aem::chunk_scan_kernel<<<1, aem::kThreads, 0, s>>>(cnt, static_cast<int>(c), E, nullptr);
+        aem::assign_kernel<<<static_cast<unsigned>(c), aem::kThreads, 0, s>>>(
+            prim_s, sec_s, n, E, cnt, capacity, nullptr, 1, inv, effective);
+        cudaError_t le = cudaGetLastError();
+        if (le != cudaSuccess) {
+            set_error("aem_capacity_route: launch failed: %s", cudaGetErrorString(le));
+            st = AEM_ECUDA;
+        }
+    } while (0);
+    if (owned) cudaFreeAsync(workspace, s);
+    if (st != AEM_OK) return st;
+    return aem::check_device_errors(s, "aem_capacity_route");
+}
+
+}  // extern "C"

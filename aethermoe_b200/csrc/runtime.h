@@ -1,0 +1,86 @@
+// Internal host-side declarations shared by the library's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "aem.h"
+
+namespace aem {
+
+const char* last_error_cstr();
+
+// Host-staging context behind aem_context_t: one stream plus grow-only
+// device and pinned-host buffers for the *_host entry points.
+struct Context {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    void* dev = nullptr;
+    size_t dev_bytes = 0;
+    void* host = nullptr;
+    size_t host_bytes = 0;
+    aem_status reserve_device(size_t bytes);
+    aem_status reserve_host(size_t bytes);
+};
+
+// Packed gating weight (device).  The [D, E] weight is stored as
+// [Dpad/4][Epad][4] float32: for every group of 4 consecutive d, the 4
+// values of each expert are contiguous and experts follow each other, so a
+// chunk of d is one contiguous block that lands in shared memory as is.
+// Epad is E rounded up to the kernel's lane-group width (8/16/32/64/128/256),
+// Dpad is D rounded up to 64; padding is zero.  bias [Epad], zero padded.
+struct Gate {
+    int device = 0;
+    int64_t D = 0, E = 0, Dpad = 0, Epad = 0;
+    float* wt = nullptr;
+    float* bias = nullptr;
+};
+int gate_epad(int64_t E);
+
+// Packed INT8 weight (device): [G][N][K] int8 + scale [G][N] float32.
+struct QWeight {
+    int device = 0;
+    int64_t G = 0, K = 0, N = 0;
+    int8_t* q = nullptr;
+    float* scale = nullptr;
+};
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// ---- kernels' host launchers (defined in the .cu files)
+aem_status launch_gating(const Gate& g, const void* x, aem_dtype xd, int64_t N, int k, int ksel,
+                         aem_gating_mode mode, int32_t* idx, float* val, cudaStream_t s);
+
+// Grouped INT8 GEMM on the tcgen05 tensor cores (or the CUDA-core fallback
+// when K % 16 != 0).  Row group g owns activation rows
+// [group_rows[g], group_rows[g+1]) (device array of G+1 ints; nullptr means
+// one group of M rows) and weight group (group_base + g).
+struct GemmArgs {
+    const QWeight* w = nullptr;
+    int64_t group_base = 0;    // first weight group used
+    int G = 1;                 // number of row groups
+    int wmod = 0;              // weight group of row group g: group_base + (wmod ? g % wmod : g)
+    const int* group_rows = nullptr;
+    int64_t M = 0;             // total activation rows (for the TMA map)
+    int64_t max_rows = 0;      // upper bound of sum_g ceil(rows_g / BT) * BT (grid sizing)
+    const void* x_hi = nullptr;  // bf16 [M, K]
+    const void* x_lo = nullptr;  // bf16 [M, K] or nullptr (split float32 activations)
+    void* out = nullptr;
+    bool out_bf16 = false;
+    int64_t ldo = 0;           // output row stride (elements)
+    bool relu = false;
+    bool atomic_add = false;   // float32 out only: red.add partial sums (split-K)
+    int ksplit = 1;
+    const int* rowmap = nullptr;    // output row of activation row r (nullable)
+    const float* rowscale = nullptr;  // per-activation-row multiplier (nullable)
+    int token_tile = 0;        // 0 = choose from average rows per group
+};
+aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s);
+
+// float32 [M, K] -> bf16 hi [M, K] + bf16 lo [M, K] (lo may be nullptr), or
+// bf16 copy when the input is already bf16 (hi only).
+aem_status launch_split_bf16(const void* x, aem_dtype xd, int64_t count, void* hi, void* lo,
+                             cudaStream_t s);
+
+}  // namespace aem

@@ -1,0 +1,199 @@
+"""The composed MoE layer on B200: single-GPU (``MoELayer``) and expert-parallel
+over NCCL (``EPLayer``), thin Python owners of the C-ABI handles.
+
+Device buffers are torch CUDA tensors (plumbing only); every kernel is in
+``libaethermoe.so``.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+
+_vp = ctypes.c_void_p
+
+
+def _dtype_code(t):
+    import torch
+    if t.dtype == torch.float32:
+        return _lib.F32
+    if t.dtype == torch.bfloat16:
+        return _lib.BF16
+    raise ValueError(f"unsupported dtype {t.dtype} (float32 or bfloat16)")
+
+
+def _stream_ptr(stream):
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+def make_config(d_model, d_ffn, num_experts, top_k, capacity=None, gating_mode=_lib.GATING_EXACT):
+    cfg = _lib.MoeConfig()
+    cfg.d_model = d_model
+    cfg.d_ffn = d_ffn
+    cfg.num_experts = num_experts
+    cfg.top_k = top_k
+    cfg.capacity = _lib.CAPACITY_UNLIMITED if capacity is None else int(capacity)
+    cfg.gating_mode = gating_mode
+    return cfg
+
+
+class MoELayer:
+    """gating -> capacity routing -> grouped INT8 expert FFN (up, ReLU, down) -> combine.
+
+    ``gate_w [d, E]``, ``gate_b [E]``; ``q_up [E, d, ffn]`` int8 with
+    ``s_up [E, ffn]``; ``q_down [E, ffn, d]`` with ``s_down [E, d]`` (the
+    reference's per-output-column quantisation layout, one group per expert).
+    """
+
+    def __init__(self, gate_w, gate_b, q_up, s_up, q_down, s_down, top_k, capacity=None,
+                 gating_mode=_lib.GATING_EXACT, device=0):
+        gate_w = np.asarray(gate_w, np.float32)
+        d, e = gate_w.shape
+        ffn = np.shape(q_up)[2]
+        self.device = device
+        self.gate = _lib.Gate(gate_w, gate_b, device)
+        self.up = _lib.QWeight(q_up, np.asarray(s_up, np.float32).reshape(e, ffn), device)
+        self.down = _lib.QWeight(q_down, np.asarray(s_down, np.float32).reshape(e, d), device)
+        self.cfg = make_config(d, ffn, e, top_k, capacity, gating_mode)
+        h = _vp()
+        _lib.check(_lib.lib().aem_moe_create(ctypes.byref(self.cfg), self.gate.handle,
+                                             self.up.handle, self.down.handle, ctypes.byref(h)),
+                   "aem_moe_create")
+        self.handle = h.value
+        self.d_model, self.d_ffn, self.num_experts, self.top_k = d, ffn, e, top_k
+
+    def forward(self, x, out=None, out_dtype=None, stream=None):
+        """``x`` torch CUDA tensor [T, d] (float32/bfloat16) -> [T, d]."""
+        import torch
+        t = x.shape[0]
+        if out is None:
+            out = torch.empty((t, self.d_model), dtype=out_dtype or x.dtype, device=x.device)
+        _lib.check(_lib.lib().aem_moe_forward(self.handle, x.data_ptr(), _dtype_code(x), t,
+                                              out.data_ptr(), _dtype_code(out), _stream_ptr(stream)),
+                   "aem_moe_forward")
+        return out
+
+    def forward_host(self, x, out_dtype=np.float32):
+        """Host buffers through ``aem_moe_forward_host`` (copies included)."""
+        x = np.ascontiguousarray(x)
+        if x.dtype == np.float32:
+            xd = _lib.F32
+        elif x.dtype == np.uint16:  # raw bfloat16 bits
+            xd = _lib.BF16
+        else:
+            raise ValueError("x must be float32 or raw bfloat16 (uint16)")
+        od = _lib.F32 if np.dtype(out_dtype) == np.float32 else _lib.BF16
+        out = np.empty((x.shape[0], self.d_model), dtype=np.float32 if od == _lib.F32 else np.uint16)
+        _lib.check(_lib.lib().aem_moe_forward_host(_lib.context(self.device), self.handle,
+                                                   x.ctypes.data, xd, x.shape[0], out.ctypes.data,
+                                                   od), "aem_moe_forward_host")
+        return out
+
+    def last_routing(self, T, stream=None):
+        """``(idx [T, k(+1)], val [T, k], effective [T*k])`` of the last forward, as torch tensors."""
+        import torch
+        k, e = self.top_k, self.num_experts
+        ksel = k + 1 if k < e else k
+        dev = torch.device("cuda", self.device)
+        idx = torch.empty((T, ksel), dtype=torch.int32, device=dev)
+        val = torch.empty((T, k), dtype=torch.float32, device=dev)
+        eff = torch.empty((T * k,), dtype=torch.int32, device=dev)
+        _lib.check(_lib.lib().aem_moe_last_routing(self.handle, idx.data_ptr(), val.data_ptr(),
+                                                   eff.data_ptr(), _stream_ptr(stream)),
+                   "aem_moe_last_routing")
+        return idx, val, eff
+
+    def close(self):
+        if getattr(self, "handle", None):
+            _lib.lib().aem_moe_free(self.handle)
+            self.handle = None
+        for w in ("gate", "up", "down"):
+            if getattr(self, w, None) is not None:
+                getattr(self, w).close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def ep_unique_id():
+    buf = (ctypes.c_uint8 * 128)()
+    _lib.check(_lib.lib().aem_ep_unique_id(buf), "aem_ep_unique_id")
+    return bytes(buf)
+
+
+def ep_plan_bases(counts, rank):
+    """Host planning of the distributed capacity rule: ``counts [R, k, E]`` -> ``base [k, E]``."""
+    c = np.ascontiguousarray(counts, dtype=np.int64)
+    r, k, e = c.shape
+    base = np.zeros((k, e), dtype=np.int64)
+    _lib.check(_lib.lib().aem_ep_plan_bases(c.ctypes.data, r, k, e, rank, base.ctypes.data),
+               "aem_ep_plan_bases")
+    return base
+
+
+class EPLayer:
+    """One rank of the expert-parallel MoE layer (experts split contiguously over ranks)."""
+
+    def __init__(self, uid, rank, world, gate_w, gate_b, q_up_local, s_up_local, q_down_local,
+                 s_down_local, top_k, capacity=None, gating_mode=_lib.GATING_EXACT, device=0):
+        gate_w = np.asarray(gate_w, np.float32)
+        d, e = gate_w.shape
+        eloc = e // world
+        ffn = np.shape(q_up_local)[2]
+        self.device = device
+        self.gate = _lib.Gate(gate_w, gate_b, device)
+        self.up = _lib.QWeight(q_up_local, np.asarray(s_up_local, np.float32).reshape(eloc, ffn), device)
+        self.down = _lib.QWeight(q_down_local, np.asarray(s_down_local, np.float32).reshape(eloc, d), device)
+        self.cfg = make_config(d, ffn, e, top_k, capacity, gating_mode)
+        uid_buf = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
+        h = _vp()
+        _lib.check(_lib.lib().aem_ep_create(ctypes.byref(self.cfg), rank, world, uid_buf,
+                                            self.gate.handle, self.up.handle, self.down.handle,
+                                            ctypes.byref(h)), "aem_ep_create")
+        self.handle = h.value
+        self.d_model, self.num_experts, self.top_k = d, e, top_k
+
+    def forward(self, x, out=None, out_dtype=None, stream=None):
+        import torch
+        t = x.shape[0]
+        if out is None:
+            out = torch.empty((t, self.d_model), dtype=out_dtype or x.dtype, device=x.device)
+        _lib.check(_lib.lib().aem_ep_forward(self.handle, x.data_ptr(), _dtype_code(x), t,
+                                             out.data_ptr(), _dtype_code(out), _stream_ptr(stream)),
+                   "aem_ep_forward")
+        return out
+
+    def last_routing(self, T, stream=None):
+        import torch
+        k, e = self.top_k, self.num_experts
+        ksel = k + 1 if k < e else k
+        dev = torch.device("cuda", self.device)
+        idx = torch.empty((T, ksel), dtype=torch.int32, device=dev)
+        val = torch.empty((T, k), dtype=torch.float32, device=dev)
+        eff = torch.empty((T * k,), dtype=torch.int32, device=dev)
+        _lib.check(_lib.lib().aem_ep_last_routing(self.handle, idx.data_ptr(), val.data_ptr(),
+                                                  eff.data_ptr(), _stream_ptr(stream)),
+                   "aem_ep_last_routing")
+        return idx, val, eff
+
+    def close(self):
+        if getattr(self, "handle", None):
+            _lib.lib().aem_ep_free(self.handle)
+            self.handle = None
+        for w in ("gate", "up", "down"):
+            if getattr(self, w, None) is not None:
+                getattr(self, w).close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,246 @@
+/*
+ * aem.h -- C ABI of the B200 (sm_100a) MoE-layer hot path of AetherMoE.
+ *
+ * Plain C: pointers, sizes and opaque handles only.  Every call returns an
+ * aem_status; on failure aem_last_error() holds a thread-local message.  No
+ * C++ exception crosses this boundary.
+ *
+ * Pointer conventions:
+ *   *_host functions take host pointers and copy through the context's
+ *   pinned staging buffers; every other compute call takes DEVICE pointers
+ *   and runs asynchronously on the given stream (a cudaStream_t passed as
+ *   void*; NULL = the legacy default stream).  Packed weight handles are
+ *   immutable after creation and may be shared between threads and streams.
+ *
+ * Layout conventions follow the reference Python API (src/kernels/*.py):
+ *   hidden [N, D] row-major, gate_weight [D, E], gate_bias [E],
+ *   q_int8 [D, E] (= [K, N]) with per-output-column scale [1, E].
+ */
+#ifndef AEM_H
+#define AEM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status, dtypes, limits ------------------------------------------------ */
+
+typedef enum {
+    AEM_OK = 0,
+    AEM_EINVAL = 1,       /* bad argument: shape, limit, null pointer (reference: ValueError) */
+    AEM_ECUDA = 2,        /* a CUDA runtime/driver call failed */
+    AEM_ENCCL = 3,        /* an NCCL call failed */
+    AEM_ETIMEOUT = 4,     /* a bounded device or host wait gave up */
+    AEM_ENOMEM = 5,       /* device or pinned-host allocation failed */
+    AEM_EUNSUPPORTED = 6, /* no sm_100 device, or the build lacks the feature */
+    AEM_EDEVICE = 7       /* a kernel reported a failed in-kernel check (e.g. bad batch_position) */
+} aem_status;
+
+typedef enum { AEM_F32 = 0, AEM_BF16 = 1 } aem_dtype;
+
+/* Gating logit arithmetic.
+ * EXACT: each product is a float32 product and products are summed in
+ *   float32 in increasing d order, bias last -- bit-identical logits to the
+ *   reference's fused_kernel_simulation (prototype/math_proto.py:19-50), so
+ *   indices match it bit-exactly on every row.
+ * FAST: fused multiply-add with a split reduction over d; indices match on
+ *   every row whose k-th/(k+1)-th logit gap exceeds float32 rounding. */
+typedef enum { AEM_GATING_EXACT = 0, AEM_GATING_FAST = 1 } aem_gating_mode;
+
+#define AEM_MAX_EXPERTS 256 /* fused_gating_metal.py:230 MAX_EXPERTS */
+#define AEM_MAX_TOPK 64     /* fused_gating_metal.py:231 MAX_TOPK */
+#define AEM_CAPACITY_UNLIMITED UINT64_MAX /* router.hpp:50 RouterConfig default */
+
+/* Thread-local message of the last failing call on this thread ("" if none). */
+const char* aem_last_error(void);
+/* Library version string. */
+const char* aem_version(void);
+/* Number of sm_100 devices visible (0 on a host without a B200). */
+int aem_device_count(void);
+/* Synchronises `stream` and reports (then clears) the in-kernel check and
+ * bounded-wait failures the library's kernels recorded on the current
+ * device since the last check: AEM_OK, AEM_EDEVICE or AEM_ETIMEOUT. */
+aem_status aem_device_status(void* stream);
+
+/* ---- host-side context (staging for *_host calls) ------------------------- */
+
+typedef struct aem_context_s* aem_context_t;
+/* Creates a context bound to `device`: one stream, grow-only pinned host and
+ * device staging buffers.  Not thread-safe: use one context per thread. */
+aem_status aem_context_create(int device, aem_context_t* out);
+aem_status aem_context_destroy(aem_context_t ctx);
+/* The context's stream (cudaStream_t as void*). */
+void* aem_context_stream(aem_context_t ctx);
+
+/* ---- fused gating ------------------------------------------------------------ */
+
+typedef struct aem_gate_s* aem_gate_t;
+
+/* Packs a gating layer: gate_weight [D, E] and gate_bias [E] float32 from
+ * HOST memory into a device-resident expert-major [E, D] copy.
+ * Replaces _get_transposed_weight, src/kernels/fused_gating_metal.py:328-344
+ * (the cached [E, D] transpose), with caller-owned lifetime.
+ * gate_bias may be NULL (zero bias).  E <= AEM_MAX_EXPERTS. */
+aem_status aem_gate_pack(const float* gate_weight, const float* gate_bias, int64_t D, int64_t E,
+                         int device, aem_gate_t* out);
+aem_status aem_gate_free(aem_gate_t gate);
+
+/* Fused gating: logits = hidden @ gate_weight + gate_bias, top-k by repeated
+ * strict-greater max extraction (ties -> lowest expert id), softmax over the
+ * k selected logits.  Replaces the kernel launch of fused_gating,
+ * src/kernels/fused_gating_metal.py:361-435 (MSL body :236-307).
+ *   hidden   device [N, D], dtype AEM_F32 or AEM_BF16
+ *   out_idx  device int32 [N, k + k_extra]: descending-logit expert ids; the
+ *            k_extra (0 or 1) trailing id is the next choice (the capacity
+ *            reroute target) and gets no weight.  k + k_extra <= E.
+ *   out_val  device float32 [N, k]: softmax weights (row sums to 1).
+ * Errors as the reference (ValueError -> AEM_EINVAL): k > AEM_MAX_TOPK, k > E,
+ * k < 1.  N == 0 is a no-op. */
+aem_status aem_gating(aem_gate_t gate, const void* hidden, aem_dtype hidden_dtype, int64_t N,
+                      int k, int k_extra, aem_gating_mode mode, int32_t* out_idx, float* out_val,
+                      void* stream);
+
+/* Same with HOST buffers (copies in and out through ctx; synchronous).
+ * This is the call the reference-facing Python shim makes. */
+aem_status aem_gating_host(aem_context_t ctx, aem_gate_t gate, const void* hidden,
+                           aem_dtype hidden_dtype, int64_t N, int k, int k_extra,
+                           aem_gating_mode mode, int32_t* out_idx, float* out_val);
+
+/* ---- INT8 weight-only quantisation and GEMM ---------------------------------- */
+
+/* Per-output-column symmetric INT8 quantisation, bit-exact with float32
+ * NumPy: scale[n] = max(max_k |w[k,n]| / 127, 1e-12); q = clip(rint(w/scale),
+ * -127, 127).  Device pointers: w f32 [K, N], q int8 [K, N], scale f32 [N].
+ * Replaces quantize_weights, src/kernels/quantized_gemm.py:70-76
+ * (prototype/math_proto.py:52-66). */
+aem_status aem_quantize_int8(const float* w, int64_t K, int64_t N, int8_t* q, float* scale,
+                             void* stream);
+/* HOST-buffer form of aem_quantize_int8 (synchronous). */
+aem_status aem_quantize_int8_host(aem_context_t ctx, const float* w, int64_t K, int64_t N,
+                                  int8_t* q, float* scale);
+
+typedef struct aem_qweight_s* aem_qweight_t;
+
+/* Packs G groups (experts) of INT8 weights from HOST memory:
+ * q [G][K][N] int8 (reference layout) and scale [G][N] float32 become a
+ * device-resident output-channel-major [G][N][K] copy.
+ * Replaces _get_transposed_qweight, src/kernels/quantized_gemm.py:151-167.
+ * Constraint for the tensor-core path: K % 16 == 0 (other K use a CUDA-core
+ * kernel). */
+aem_status aem_qweight_pack(const int8_t* q, const float* scale, int64_t G, int64_t K, int64_t N,
+                            int device, aem_qweight_t* out);
+/* Same from DEVICE memory (q [G][K][N], scale [G][N]); stream-ordered. */
+aem_status aem_qweight_pack_device(const int8_t* q, const float* scale, int64_t G, int64_t K,
+                                   int64_t N, void* stream, aem_qweight_t* out);
+aem_status aem_qweight_free(aem_qweight_t w);
+/* Dimensions of a packed weight (any pointer may be NULL). */
+aem_status aem_qweight_shape(aem_qweight_t w, int64_t* G, int64_t* K, int64_t* N);
+
+/* out[M, N] (float32) = x[M, K] @ (q[group] * scale[group]).  Dequantises
+ * at multiply time: int8 tiles are converted to bf16 in shared memory and
+ * multiplied on the tcgen05 tensor cores with float32 accumulation in TMEM;
+ * float32 x is split into two bf16 terms (hi + lo).  Device pointers.
+ * Replaces fused_quantized_matmul, src/kernels/quantized_gemm.py:184-226
+ * (MSL body :99-138).  D mismatch -> AEM_EINVAL as the reference (:202-205). */
+aem_status aem_qgemm(aem_qweight_t w, int64_t group, const void* x, aem_dtype x_dtype, int64_t M,
+                     float* out, void* stream);
+/* HOST-buffer form of aem_qgemm (synchronous). */
+aem_status aem_qgemm_host(aem_context_t ctx, aem_qweight_t w, int64_t group, const void* x,
+                          aem_dtype x_dtype, int64_t M, float* out);
+
+/* ---- capacity-ceiling routing -------------------------------------------------- */
+
+/* Effective expert of each of n tokens: within each primary-expert group,
+ * ranked by batch_position, the first `capacity` keep their primary and the
+ * rest take their own secondary (one hop).  Replaces
+ * Router::assign_effective_experts, src/orchestration/router.hpp:249-266.
+ * Device pointers, uint32 [n].  batch_position must be a permutation of
+ * [0, n) (the reference's reassembly rejects anything else,
+ * router.hpp:286-313); a violation returns AEM_EDEVICE.  Expert ids < E.
+ * capacity = AEM_CAPACITY_UNLIMITED keeps every primary.
+ * workspace: device scratch of aem_capacity_route_workspace(n, E) bytes, or
+ * NULL to have the call allocate (stream-ordered) and free it.  The call
+ * synchronises the stream to report in-kernel check failures. */
+size_t aem_capacity_route_workspace(int64_t n, int E);
+aem_status aem_capacity_route(const uint32_t* primary, const uint32_t* secondary,
+                              const uint32_t* batch_position, int64_t n, int E, uint64_t capacity,
+                              uint32_t* effective, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/* ---- MoE layer (gating -> routing -> grouped INT8 expert FFN -> combine) --------- */
+
+typedef struct {
+    int64_t d_model;       /* hidden size d */
+    int64_t d_ffn;         /* expert FFN size */
+    int num_experts;       /* E (global) */
+    int top_k;             /* k */
+    uint64_t capacity;     /* per-expert capacity per step, or AEM_CAPACITY_UNLIMITED */
+    aem_gating_mode gating_mode;
+} aem_moe_config;
+
+typedef struct aem_moe_s* aem_moe_t;
+
+/* A single-GPU MoE layer.  `up` holds E groups of [d_model -> d_ffn]
+ * (q [E][d_model][d_ffn]), `down` E groups of [d_ffn -> d_model].  The
+ * handles are borrowed and must outlive the layer. */
+aem_status aem_moe_create(const aem_moe_config* cfg, aem_gate_t gate, aem_qweight_t up,
+                          aem_qweight_t down, aem_moe_t* out);
+aem_status aem_moe_free(aem_moe_t moe);
+
+/* One layer step on device buffers: x [T, d] (F32/BF16) -> out [T, d]
+ * (F32/BF16).  Units are the (token, slot) pairs in slot-major order
+ * (batch_position = j*T + t); a unit's secondary is the token's (k+1)-th
+ * gating choice; capacity is applied as Router::assign_effective_experts
+ * (router.hpp:249-266); each unit runs relu(x W_up) W_down of its effective
+ * expert and out[t] = sum_j weight[t,j] * y[t,j]. */
+aem_status aem_moe_forward(aem_moe_t moe, const void* x, aem_dtype x_dtype, int64_t T, void* out,
+                           aem_dtype out_dtype, void* stream);
+/* HOST-buffer form of aem_moe_forward (synchronous). */
+aem_status aem_moe_forward_host(aem_context_t ctx, aem_moe_t moe, const void* x, aem_dtype x_dtype,
+                                int64_t T, void* out, aem_dtype out_dtype);
+/* Routing of the last forward (device pointers, stream-ordered copies):
+ * idx int32 [T, k+1] (k+1 clipped to E), val f32 [T, k], effective uint32 [T*k]. */
+aem_status aem_moe_last_routing(aem_moe_t moe, int32_t* idx, float* val, uint32_t* effective,
+                                void* stream);
+
+/* ---- expert parallelism over NCCL ---------------------------------------------------- */
+
+/* Host-side planning of the distributed capacity rule (no GPU needed).
+ * counts: [R][k][E] per-rank primary counts per (slot, expert).  Writes
+ * base [k][E] for `rank`: the global rank offset of this rank's first unit
+ * in each (slot, expert) group, with units ordered slot-major by global
+ * batch_position and tokens split contiguously over ranks. */
+aem_status aem_ep_plan_bases(const int64_t* counts, int R, int k, int E, int rank, int64_t* base);
+
+/* NCCL unique id (128 bytes) for aem_ep_create; made on one rank and
+ * broadcast by the caller. */
+aem_status aem_ep_unique_id(uint8_t out[128]);
+
+typedef struct aem_ep_s* aem_ep_t;
+
+/* One rank of an expert-parallel MoE layer: experts are split contiguously,
+ * E/R per rank (tests/test_orchestration.cpp:25-33 expert->shard map);
+ * `up_local`/`down_local` hold this rank's E/R experts.  Replaces the
+ * Router + ICollectiveTransport scatter/gather (router.hpp:67-100,
+ * collective_transport.hpp:37-51) with NCCL over NVLink. */
+aem_status aem_ep_create(const aem_moe_config* cfg, int rank, int world, const uint8_t uid[128],
+                         aem_gate_t gate, aem_qweight_t up_local, aem_qweight_t down_local,
+                         aem_ep_t* out);
+aem_status aem_ep_free(aem_ep_t ep);
+/* One step: this rank's T_local tokens (global positions rank*T_local ...)
+ * -> its outputs.  Collective: every rank calls it with the same T_local. */
+aem_status aem_ep_forward(aem_ep_t ep, const void* x, aem_dtype x_dtype, int64_t T_local, void* out,
+                          aem_dtype out_dtype, void* stream);
+/* Routing of the last step for this rank's units (device pointers):
+ * idx [T_local, k+1], val [T_local, k], effective [k*T_local] (slot-major). */
+aem_status aem_ep_last_routing(aem_ep_t ep, int32_t* idx, float* val, uint32_t* effective,
+                               void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AEM_H */

@@ -1,0 +1,134 @@
+"""The composed MoE layer on one B200 vs the oracle.
+
+Routing (gating indices and capacity reroutes) is bit-exact; layer outputs
+are within ``1e-3 + 1e-3 * |ref|`` of the float64 oracle that rounds the
+expert hidden activation to bfloat16 like the CUDA path (the layer's stated
+precision: bf16 activations into the expert GEMMs, float32 accumulation,
+float32 expert outputs and combine).
+"""
+import numpy as np
+import pytest
+
+import aem_oracle as O
+import native
+
+pytestmark = pytest.mark.gpu
+
+RTOL = ATOL = 1e-3
+
+
+def _weights(rng, e, d, f, quantize=True):
+    if quantize:
+        qu, su, qd, sd = [], [], [], []
+        for _ in range(e):
+            a, b = O.quantize_int8((rng.normal(size=(d, f)) * 0.02).astype(np.float32))
+            c, g = O.quantize_int8((rng.normal(size=(f, d)) * 0.02).astype(np.float32))
+            qu.append(a); su.append(b); qd.append(c); sd.append(g)
+        return np.stack(qu), np.stack(su), np.stack(qd), np.stack(sd)
+    qu = rng.integers(-127, 128, size=(e, d, f), dtype=np.int8)
+    su = (rng.random(size=(e, 1, f)) * 2e-4 + 5e-4).astype(np.float32)
+    qd = rng.integers(-127, 128, size=(e, f, d), dtype=np.int8)
+    sd = (rng.random(size=(e, 1, d)) * 2e-4 + 5e-4).astype(np.float32)
+    return qu, su, qd, sd
+
+
+def _bf16(x):
+    f = O.bf16_round(x)
+    return f, (f.view(np.uint32) >> 16).astype(np.uint16)
+
+
+def _run(cuda, x_bits, gw, gb, w, k, cap, out_dtype="f32"):
+    import torch
+    from aethermoe_b200.moe import MoELayer
+    layer = MoELayer(gw, gb, w[0], w[1], w[2], w[3], k, capacity=cap)
+    t = x_bits.shape[0]
+    xt = torch.from_numpy(x_bits.view(np.int16)).to(cuda).view(torch.bfloat16)
+    out = layer.forward(xt, out_dtype=torch.float32 if out_dtype == "f32" else torch.bfloat16)
+    idx, val, eff = layer.last_routing(t)
+    torch.cuda.synchronize()
+    res = (out.float().cpu().numpy(), idx.cpu().numpy(), val.cpu().numpy(), eff.cpu().numpy())
+    layer.close()
+    return res
+
+
+def _close(got, ref):
+    err = np.abs(got.astype(np.float64) - ref)
+    bound = ATOL + RTOL * np.abs(ref)
+    assert np.all(err <= bound), f"max excess {(err - bound).max():.3e}"
+
+
+@pytest.mark.parametrize("t,d,f,e,k,cap", [
+    (64, 256, 512, 8, 2, None),
+    (200, 128, 256, 16, 6, 40),      # tight capacity: reroutes
+    (37, 64, 192, 4, 4, None),       # k == E: no reroute target
+    (1, 512, 1024, 8, 2, None),      # decode: split-K down projection
+    (3, 256, 640, 8, 2, 1),          # decode with capacity 1
+    (513, 192, 320, 32, 3, 50),
+])
+def test_small_layer_matches_oracle(cuda, t, d, f, e, k, cap):
+    rng = np.random.default_rng(t * 7 + e)
+    xf, xb = _bf16(rng.normal(size=(t, d)).astype(np.float32))
+    gw = (rng.normal(size=(d, e)) / np.sqrt(d)).astype(np.float32)
+    gb = O.zipf_bias(e)
+    w = _weights(rng, e, d, f)
+    out, idx, val, eff = _run(cuda, xb, gw, gb, w, k, cap)
+    ref, oidx, oval, oeff = O.moe_layer(xf, gw, gb, k, w[0], w[1], w[2], w[3], cap)
+    np.testing.assert_array_equal(idx, oidx)
+    np.testing.assert_allclose(val, oval, atol=1e-6)
+    np.testing.assert_array_equal(eff, oeff)
+    if cap is not None and k < e:
+        assert (eff != O.moe_units(oidx, k, e)[0]).any() or cap >= t * k
+    _close(out, ref)
+
+
+def test_bf16_output(cuda):
+    rng = np.random.default_rng(11)
+    t, d, f, e, k = 48, 128, 256, 8, 2
+    xf, xb = _bf16(rng.normal(size=(t, d)).astype(np.float32))
+    gw = (rng.normal(size=(d, e)) / np.sqrt(d)).astype(np.float32)
+    gb = np.zeros(e, np.float32)
+    w = _weights(rng, e, d, f)
+    out, *_ = _run(cuda, xb, gw, gb, w, k, None, out_dtype="bf16")
+    ref, *_ = O.moe_layer(xf, gw, gb, k, w[0], w[1], w[2], w[3], None)
+    err = np.abs(out - ref)
+    assert np.all(err <= 1e-2 * np.abs(ref) + 1e-2)  # bf16 output rounding
+
+
+def test_expert_parallel_config_on_one_gpu(cuda):
+    """The expert-parallel config on a single GPU: E=64, top-6, d=2048,
+    ffn=1408, T=16384, capacity ceil(1.25*T*k/E)=1920, Zipf(1.1) gate bias.
+    Routing bit-exact on every unit; 24 sampled token rows vs the oracle."""
+    t, d, f, e, k = 16384, 2048, 1408, 64, 6
+    cap = O.default_capacity(t, k, e)
+    rng = np.random.default_rng(64)
+    xf, xb = _bf16(rng.normal(size=(t, d)).astype(np.float32))
+    gw = (rng.normal(size=(d, e)) / np.sqrt(d)).astype(np.float32)
+    gb = O.zipf_bias(e)
+    w = _weights(rng, e, d, f, quantize=False)
+    out, idx, val, eff = _run(cuda, xb, gw, gb, w, k, cap)
+    oidx, oval = O.fused_gating(xf, gw, gb, k, extra=1)
+    np.testing.assert_array_equal(idx, oidx)
+    np.testing.assert_allclose(val, oval, atol=1e-6)
+    oeff = native.moe_route(oidx, k, e, cap)
+    np.testing.assert_array_equal(eff, oeff)
+    assert (eff != O.moe_units(oidx, k, e)[0]).sum() > 0  # the Zipf bias forces reroutes
+    rows = np.unique(np.r_[0, t - 1, rng.integers(0, t, 22)])
+    ref = O.moe_layer_rows(rows, xf, oidx, oval, oeff, k, w[0], w[1], w[2], w[3])
+    _close(out[rows], ref)
+
+
+def test_mixtral_shape_decode(cuda):
+    """Mixtral-8x7B-shaped layer (d=4096, ffn=14336, E=8, top-2) at T=1 and
+    T=32, random INT8 weights; every output row vs the oracle."""
+    d, f, e, k = 4096, 14336, 8, 2
+    rng = np.random.default_rng(8)
+    w = _weights(rng, e, d, f, quantize=False)
+    gw = (rng.normal(size=(d, e)) / np.sqrt(d)).astype(np.float32)
+    gb = np.zeros(e, np.float32)
+    for t in (1, 32):
+        xf, xb = _bf16(rng.normal(size=(t, d)).astype(np.float32))
+        out, idx, val, eff = _run(cuda, xb, gw, gb, w, k, None)
+        oidx, oval = O.fused_gating(xf, gw, gb, k, extra=1)
+        np.testing.assert_array_equal(idx, oidx)
+        ref = O.moe_layer_rows(np.arange(t), xf, oidx, oval, eff, k, *w)
+        _close(out, ref)

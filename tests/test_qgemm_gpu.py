@@ -1,0 +1,163 @@
+"""INT8 quantisation and the tcgen05 INT8-weight GEMM vs the oracle.
+
+Mirrors ``tests/python/test_quantized_gemm.py`` and ``test_math_prototype.py``
+of the reference; quantisation must be bit-exact, GEMM outputs within
+``|gpu - ref| <= 1e-3 + 1e-3 * |ref|`` of the float64 oracle (the reference's
+``FUSED_VS_NAIVE_TOLERANCE = 1e-3`` as rtol and atol).
+"""
+import numpy as np
+import pytest
+
+import aem_oracle as O
+import cases
+
+pytestmark = pytest.mark.gpu
+
+RTOL = ATOL = 1e-3
+
+
+def _close(got, ref, rtol=RTOL, atol=ATOL):
+    err = np.abs(np.asarray(got, np.float64) - ref)
+    bound = atol + rtol * np.abs(ref)
+    assert np.all(err <= bound), f"max excess {(err - bound).max():.3e}, max err {err.max():.3e}"
+
+
+@pytest.fixture(scope="module")
+def qg(cuda):
+    from aethermoe_b200.kernels import quantized_gemm
+    return quantized_gemm
+
+
+@pytest.mark.parametrize("name", sorted(cases.quant_cases()))
+def test_quantize_bit_exact(qg, golden, name):
+    w, x = cases.quant_cases()[name]
+    q, s = qg.quantize_weights(w)
+    np.testing.assert_array_equal(q, golden["quant"][f"{name}/q"])
+    np.testing.assert_array_equal(s, golden["quant"][f"{name}/scale"])
+
+
+def test_quantize_c0_and_large(qg, golden):
+    import hashlib
+    w, x = cases.c0_quant_inputs()
+    q, s = qg.quantize_weights(w)
+    assert hashlib.sha256(q.tobytes()).hexdigest() == str(golden["quant"]["c0/q_digest"])
+    assert hashlib.sha256(s.tobytes()).hexdigest() == str(golden["quant"]["c0/scale_digest"])
+    rng = np.random.default_rng(3)
+    w = (rng.normal(size=(4096, 1536)) * 0.02).astype(np.float32)
+    w[:, 7] = 0.0
+    q, s = qg.quantize_weights(w)
+    oq, os_ = O.quantize_int8(w)
+    np.testing.assert_array_equal(q, oq)
+    np.testing.assert_array_equal(s, os_)
+
+
+@pytest.mark.parametrize("name", sorted(cases.quant_cases()))
+def test_fused_matches_reference_perentry(qg, golden, name):
+    w, x = cases.quant_cases()[name]
+    q, s = O.quantize_int8(w)
+    out = qg.fused_quantized_matmul(x, q, s)
+    _close(out, golden["quant"][f"{name}/perentry"])
+
+
+@pytest.mark.parametrize("n_tokens,d_model,num_experts", [(4, 32, 8), (16, 64, 16), (1, 16, 4)])
+def test_fused_matches_naive(qg, n_tokens, d_model, num_experts):
+    rng = np.random.default_rng(11)
+    x = rng.normal(size=(n_tokens, d_model)).astype(np.float32)
+    w = rng.normal(size=(d_model, num_experts)).astype(np.float32)
+    q, s = qg.quantize_weights(w)
+    naive = qg.naive_quantized_matmul(x, q, s)
+    fused = qg.fused_quantized_matmul(x, q, s)
+    assert np.allclose(naive, fused, atol=1e-3), np.abs(naive - fused).max()
+
+
+def test_quantized_output_within_bound_of_true_fp32(qg):
+    rng = np.random.default_rng(13)
+    x = rng.normal(size=(8, 64)).astype(np.float32)
+    w = rng.normal(size=(64, 16)).astype(np.float32)
+    q, s = qg.quantize_weights(w)
+    out = qg.fused_quantized_matmul(x, q, s)
+    rel = np.abs(out - x @ w) / (np.abs(x @ w) + 1e-6)
+    assert rel.mean() < 0.35
+
+
+def test_all_zero_weight_column(qg):
+    d, e = 16, 4
+    w = np.zeros((d, e), np.float32)
+    w[:, 1] = np.random.default_rng(14).normal(size=d)
+    q, s = qg.quantize_weights(w)
+    x = np.random.default_rng(15).normal(size=(4, d)).astype(np.float32)
+    out = qg.fused_quantized_matmul(x, q, s)
+    assert not np.isnan(out).any()
+    assert np.allclose(out[:, 0], 0.0, atol=1e-5)
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 24, 40), (5, 40, 130), (3, 16, 8), (33, 48, 300),
+                                   (7, 272, 129), (130, 64, 256), (257, 128, 384)])
+def test_odd_shapes(qg, m, k, n):
+    """Tails in every dimension; K % 16 != 0 takes the CUDA-core path."""
+    rng = np.random.default_rng(m * 1000 + k + n)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    q, s = O.quantize_int8((rng.normal(size=(k, n)) * 0.02).astype(np.float32))
+    _close(qg.fused_quantized_matmul(x, q, s), O.qgemm(x, q, s))
+
+
+@pytest.fixture(scope="module")
+def sweep_weight():
+    """K=4096, N=14336, W ~ N(0, 0.02) quantised per output channel, and the
+    float64 dequantised copy the oracle multiplies with."""
+    rng = np.random.default_rng(2024)
+    w = (rng.normal(size=(4096, 14336)) * 0.02).astype(np.float32)
+    q, s = O.quantize_int8(w)
+    return q, s, O.dequantize_int8(q, s).astype(np.float64)
+
+
+@pytest.mark.parametrize("m", [1, 8, 64, 512, 4096])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_sweep(qg, sweep_weight, m, dtype):
+    """INT8 GEMM sweep config: M in {1,8,64,512,4096}, K=4096, N=14336;
+    float32 / bfloat16 x ~ N(0,1).  Rows checked against the float64 oracle:
+    all for M <= 64, 64 sampled rows above (the same kernel tiles computed them)."""
+    q, s, wd = sweep_weight
+    rng = np.random.default_rng(m)
+    x = rng.normal(size=(m, q.shape[0])).astype(np.float32)
+    if dtype == "bf16":
+        xf = O.bf16_round(x)
+        out = _bf16_gemm(q, s, (xf.view(np.uint32) >> 16).astype(np.uint16))
+    else:
+        xf = x
+        out = qg.fused_quantized_matmul(x, q, s)
+    rows = np.arange(m) if m <= 64 else np.unique(np.r_[0, m - 1, rng.integers(0, m, 62)])
+    _close(out[rows], xf[rows].astype(np.float64) @ wd)
+
+
+def _bf16_gemm(q, s, xbits):
+    """aem_qgemm on device with bf16 activations (torch buffers)."""
+    import torch
+    from aethermoe_b200 import _lib
+    w = _lib.QWeight(q, s, 0)
+    dev = torch.device("cuda", 0)
+    xt = torch.from_numpy(xbits.view(np.int16)).to(dev).view(torch.bfloat16)
+    out = torch.empty((xbits.shape[0], q.shape[1]), dtype=torch.float32, device=dev)
+    _lib.check(_lib.lib().aem_qgemm(w.handle, 0, xt.data_ptr(), _lib.BF16, xbits.shape[0],
+                                    out.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def test_groups_select_their_weights(cuda):
+    """A packed weight with G groups; aem_qgemm(group=g) uses group g."""
+    import torch
+    from aethermoe_b200 import _lib
+    rng = np.random.default_rng(9)
+    g, kdim, n, m = 5, 256, 384, 37
+    q = rng.integers(-127, 128, size=(g, kdim, n), dtype=np.int8)
+    s = (rng.random(size=(g, n)) * 1e-3 + 1e-4).astype(np.float32)
+    w = _lib.QWeight(q, s, 0)
+    x = rng.normal(size=(m, kdim)).astype(np.float32)
+    xt = torch.from_numpy(x).to(cuda)
+    out = torch.empty((m, n), dtype=torch.float32, device=cuda)
+    for grp in (0, 3, 4):
+        _lib.check(_lib.lib().aem_qgemm(w.handle, grp, xt.data_ptr(), _lib.F32, m, out.data_ptr(),
+                                        torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        _close(out.cpu().numpy(), O.qgemm(x, q[grp], s[grp:grp + 1]))
