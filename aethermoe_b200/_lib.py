@@ -80,7 +80,14 @@ _SIGS = {
     "aem_ep_free": (_int, [_vp]),
     "aem_ep_forward": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp]),
     "aem_ep_last_routing": (_int, [_vp, _vp, _vp, _vp, _vp]),
+    "aem_kernel_launches": (ctypes.c_uint64, []),
+    "aem_moe_profile": (_int, [_vp, _int]),
+    "aem_moe_profile_read": (_int, [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64)]),
+    "aem_ep_profile": (_int, [_vp, _int]),
+    "aem_ep_profile_read": (_int, [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64)]),
 }
+NUM_PHASES = 8
+PHASES = ["gating", "route", "up_gemm", "down_gemm", "combine", "dispatch", "return", "exchange"]
 
 _lib = None
 _lock = threading.Lock()
@@ -202,3 +209,38 @@ class QWeight:
             self.close()
         except Exception:
             pass
+
+
+class DeviceQWeight(QWeight):
+    """Packed INT8 weight groups built from DEVICE tensors (torch CUDA):
+    ``q [G, K, N]`` int8 and ``scale [G, N]`` float32 (stream-ordered pack)."""
+
+    def __init__(self, q, scale, stream=None):  # noqa: D401 - torch tensors
+        import torch
+        if q.dim() == 2:
+            q = q.unsqueeze(0)
+        g, k, n = q.shape
+        q = q.contiguous()
+        scale = scale.reshape(g, n).contiguous().float()
+        s = stream or torch.cuda.current_stream(q.device)
+        h = _vp()
+        check(lib().aem_qweight_pack_device(q.data_ptr(), scale.data_ptr(), g, k, n,
+                                            ctypes.c_void_p(s.cuda_stream), ctypes.byref(h)),
+              "aem_qweight_pack_device")
+        s.synchronize()
+        self.handle = h.value
+        self.G, self.K, self.N, self.device = g, k, n, q.device.index
+
+
+def quantize_device(w, stream=None):
+    """Bit-exact per-output-column INT8 quantisation of a float32 CUDA tensor
+    ``w [K, N]`` -> ``(q int8 [K, N], scale float32 [N])`` (aem_quantize_int8)."""
+    import torch
+    w = w.contiguous().float()
+    k, n = w.shape
+    q = torch.empty((k, n), dtype=torch.int8, device=w.device)
+    s = torch.empty((n,), dtype=torch.float32, device=w.device)
+    st = stream or torch.cuda.current_stream(w.device)
+    check(lib().aem_quantize_int8(w.data_ptr(), k, n, q.data_ptr(), s.data_ptr(),
+                                  ctypes.c_void_p(st.cuda_stream)), "aem_quantize_int8")
+    return q, s

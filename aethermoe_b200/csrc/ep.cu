@@ -128,6 +128,7 @@ struct Ep {
     float* yr = nullptr;  // f32 [r_cap, d]
     float* yb = nullptr;  // f32 [u_cap, d] expert outputs back in grouped order
     int64_t last_T = 0;
+    PhaseProfiler prof;
 
     aem_status init_buffers();
     aem_status reserve_units(int64_t U);
@@ -186,19 +187,26 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
     AEM_TRY(loc.reserve(std::max<int64_t>(T, 1)));
     AEM_TRY(reserve_units(std::max<int64_t>(U, 1)));
     // 1. gating and local per-(slot, expert) counts
+    prof.begin(AEM_PHASE_GATING, s);
     if (T > 0)
         AEM_TRY(launch_gating(*gate, x, xd, T, k, ksel, cfg.gating_mode, loc.idx, loc.val, s));
+    prof.end(AEM_PHASE_GATING, s);
+    prof.begin(AEM_PHASE_EXCHANGE, s);
     AEM_TRY_CUDA(cudaMemsetAsync(cnt, 0, sizeof(unsigned long long) * k * E, s));
     if (T > 0) {
         const unsigned g = static_cast<unsigned>(std::min<int64_t>((U + 255) / 256, 1024));
         slot_count_kernel<<<g, 256, sizeof(unsigned) * k * E, s>>>(loc.idx, T, ksel, k, E, cnt);
         AEM_CHECK_LAUNCH();
+        count_launches(1);
     }
     // 2. all-gather counts -> global rank offsets
     AEM_TRY_NCCL(ncclAllGather(cnt, cnt_all, static_cast<size_t>(k) * E, ncclInt64, comm, s));
     ep_corr_kernel<<<1, 256, 0, s>>>(cnt_all, R, k, E, rank, corr);
     AEM_CHECK_LAUNCH();
+    count_launches(1);
+    prof.end(AEM_PHASE_EXCHANGE, s);
     // 3. capacity routing with global ranks + expert-grouped permutation
+    prof.begin(AEM_PHASE_ROUTE, s);
     if (T > 0) {
         MoeRouteArgs ra;
         ra.idx = loc.idx;
@@ -221,6 +229,7 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
     } else {
         AEM_TRY_CUDA(cudaMemsetAsync(loc.starts, 0, sizeof(int) * (E + 1), s));
     }
+    prof.end(AEM_PHASE_ROUTE, s);
     // 4. all-gather per-expert starts; sizes to the host (the one sync)
     AEM_TRY_NCCL(ncclAllGather(loc.starts, starts_all, static_cast<size_t>(E + 1), ncclInt32, comm, s));
     AEM_TRY_CUDA(cudaMemcpyAsync(h_starts, starts_all, sizeof(int) * R * (E + 1),
@@ -246,6 +255,7 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
     AEM_TRY_CUDA(cudaMemcpyAsync(d_groups, h_groups, sizeof(int) * (R * e_loc + 1),
                                  cudaMemcpyHostToDevice, s));
     // 5. dispatch: bf16 rows, grouped by destination rank, to the expert owners
+    prof.begin(AEM_PHASE_DISPATCH, s);
     AEM_TRY_NCCL(ncclGroupStart());
     for (int p = 0; p < R; ++p) {
         if (send_cnt[p] > 0)
@@ -256,6 +266,7 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
                                   ncclBfloat16, p, comm, s));
     }
     AEM_TRY_NCCL(ncclGroupEnd());
+    prof.end(AEM_PHASE_DISPATCH, s);
     // 6. local expert FFN on the (source, expert) segments
     if (rtot > 0) {
         GemmArgs up_a;
@@ -270,7 +281,9 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
         up_a.out_bf16 = true;
         up_a.ldo = f;
         up_a.relu = true;
+        prof.begin(AEM_PHASE_UP, s);
         AEM_TRY(launch_qgemm(up_a, s));
+        prof.end(AEM_PHASE_UP, s);
         GemmArgs dn;
         dn.w = down;
         dn.G = R * e_loc;
@@ -281,9 +294,12 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
         dn.x_hi = hr;
         dn.out = yr;
         dn.ldo = d;
+        prof.begin(AEM_PHASE_DOWN, s);
         AEM_TRY(launch_qgemm(dn, s));
+        prof.end(AEM_PHASE_DOWN, s);
     }
     // 7. expert outputs back to the token owners (same segments, reversed)
+    prof.begin(AEM_PHASE_RETURN, s);
     AEM_TRY_NCCL(ncclGroupStart());
     for (int p = 0; p < R; ++p) {
         if (recv_cnt[p] > 0)
@@ -292,7 +308,9 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
             AEM_TRY_NCCL(ncclRecv(yb + send_off[p] * d, send_cnt[p] * d, ncclFloat32, p, comm, s));
     }
     AEM_TRY_NCCL(ncclGroupEnd());
+    prof.end(AEM_PHASE_RETURN, s);
     // 8. weighted combine in token order
+    prof.begin(AEM_PHASE_COMBINE, s);
     if (T > 0) {
         const unsigned g = static_cast<unsigned>(std::min<int64_t>((T * d + 255) / 256, 148 * 16));
         if (od == AEM_BF16)
@@ -302,7 +320,10 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
             combine_gather_kernel<float><<<g, 256, 0, s>>>(yb, dest_of, loc.val, T, k, d,
                                                            static_cast<float*>(out));
         AEM_CHECK_LAUNCH();
+        count_launches(1);
     }
+    prof.end(AEM_PHASE_COMBINE, s);
+    prof.step();
     (void)nccl_dtype;
     return AEM_OK;
 }
@@ -426,6 +447,17 @@ aem_status aem_ep_forward(aem_ep_t h, const void* x, aem_dtype x_dtype, int64_t 
     AEM_REQUIRE(T_local == 0 || (x && out), "aem_ep_forward: NULL buffer");
     auto* ep = reinterpret_cast<aem::Ep*>(h);
     return ep->forward(x, x_dtype, T_local, out, out_dtype, static_cast<cudaStream_t>(stream));
+}
+
+aem_status aem_ep_profile(aem_ep_t h, int enable) {
+    AEM_REQUIRE(h != nullptr, "aem_ep_profile: NULL layer");
+    reinterpret_cast<aem::Ep*>(h)->prof.enable(enable != 0);
+    return AEM_OK;
+}
+
+aem_status aem_ep_profile_read(aem_ep_t h, double* ms, int64_t* steps) {
+    AEM_REQUIRE(h != nullptr, "aem_ep_profile_read: NULL layer");
+    return reinterpret_cast<aem::Ep*>(h)->prof.read(ms, steps);
 }
 
 aem_status aem_ep_last_routing(aem_ep_t h, int32_t* idx, float* val, uint32_t* effective,

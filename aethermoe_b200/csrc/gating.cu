@@ -290,6 +290,7 @@ aem_status launch_gating(const Gate& g, const void* x, aem_dtype xd, int64_t N, 
         set_error("gating kernel launch failed: %s", cudaGetErrorString(e));
         return AEM_ECUDA;
     }
+    count_launches(1);
     return AEM_OK;
 }
 

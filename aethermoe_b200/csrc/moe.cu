@@ -128,6 +128,7 @@ aem_status gather_rows(const void* x, aem_dtype xd, const int32_t* src, int64_t 
         gather_rows_kernel<float><<<g, 256, 0, s>>>(static_cast<const float*>(x), src, rows, d,
                                                     static_cast<__nv_bfloat16*>(out));
     AEM_CHECK_LAUNCH();
+    count_launches(1);
     return AEM_OK;
 }
 
@@ -151,6 +152,7 @@ aem_status combine_rows(const float* y, int64_t T, int k, int64_t d, void* out, 
             combine_kernel<float><<<g, 256, 0, s>>>(y, T, k, d, static_cast<float*>(out));
     }
     AEM_CHECK_LAUNCH();
+    count_launches(1);
     return AEM_OK;
 }
 
@@ -207,7 +209,10 @@ aem_status Moe::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_d
     const int k = cfg.top_k, E = cfg.num_experts;
     const int ksel = k < E ? k + 1 : k;
     const int64_t U = T * k, d = cfg.d_model, f = cfg.d_ffn;
+    prof.begin(AEM_PHASE_GATING, s);
     AEM_TRY(launch_gating(*gate, x, xd, T, k, ksel, cfg.gating_mode, idx, val, s));
+    prof.end(AEM_PHASE_GATING, s);
+    prof.begin(AEM_PHASE_ROUTE, s);
     MoeRouteArgs ra;
     ra.idx = idx;
     ra.T = T;
@@ -224,7 +229,10 @@ aem_status Moe::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_d
     ra.rowscale = rowscale;
     AEM_TRY(route_moe(ra, s));
     AEM_TRY(gather_rows(x, xd, src_token, U, d, xperm, s));
-    return expert_ffn(T, U, out, od, s);
+    prof.end(AEM_PHASE_ROUTE, s);
+    AEM_TRY(expert_ffn(T, U, out, od, s));
+    prof.step();
+    return AEM_OK;
 }
 
 aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaStream_t s) {
@@ -242,7 +250,9 @@ aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaSt
     up_a.out_bf16 = true;
     up_a.ldo = f;
     up_a.relu = true;
+    prof.begin(AEM_PHASE_UP, s);
     AEM_TRY(launch_qgemm(up_a, s));
+    prof.end(AEM_PHASE_UP, s);
 
     GemmArgs dn;
     dn.w = down;
@@ -262,13 +272,18 @@ aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaSt
     const int sms = sm_count(gate->device);
     int ks = 1;
     if (tiles < sms) ks = static_cast<int>(std::min<int64_t>((2 * sms + tiles - 1) / tiles, (f + 63) / 64));
+    prof.begin(AEM_PHASE_DOWN, s);
     if (ks > 1) {
         AEM_TRY_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * U * d, s));
         dn.atomic_add = true;
         dn.ksplit = ks;
     }
     AEM_TRY(launch_qgemm(dn, s));
-    return combine_rows(y, T, k, d, out, od, s);
+    prof.end(AEM_PHASE_DOWN, s);
+    prof.begin(AEM_PHASE_COMBINE, s);
+    AEM_TRY(combine_rows(y, T, k, d, out, od, s));
+    prof.end(AEM_PHASE_COMBINE, s);
+    return AEM_OK;
 }
 
 }  // namespace aem
@@ -345,6 +360,17 @@ aem_status aem_moe_forward_host(aem_context_t ctx, aem_moe_t moe, const void* x,
     AEM_TRY(m->forward(d, x_dtype, T, d + o1, out_dtype, c->stream));
     AEM_TRY_CUDA(cudaMemcpyAsync(out, d + o1, ob, cudaMemcpyDeviceToHost, c->stream));
     return aem::check_device_errors(c->stream, "aem_moe_forward_host");
+}
+
+aem_status aem_moe_profile(aem_moe_t moe, int enable) {
+    AEM_REQUIRE(moe != nullptr, "aem_moe_profile: NULL layer");
+    reinterpret_cast<aem::Moe*>(moe)->prof.enable(enable != 0);
+    return AEM_OK;
+}
+
+aem_status aem_moe_profile_read(aem_moe_t moe, double* ms, int64_t* steps) {
+    AEM_REQUIRE(moe != nullptr, "aem_moe_profile_read: NULL layer");
+    return reinterpret_cast<aem::Moe*>(moe)->prof.read(ms, steps);
 }
 
 aem_status aem_moe_last_routing(aem_moe_t moe, int32_t* idx, float* val, uint32_t* effective,

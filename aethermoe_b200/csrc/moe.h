@@ -34,6 +34,7 @@ struct Moe {
     void* xperm = nullptr;  // bf16 [U, d]
     void* h = nullptr;      // bf16 [U, ffn]
     float* y = nullptr;     // f32 [T*k, d]
+    PhaseProfiler prof;
 
     aem_status reserve(int64_t T);
     aem_status forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dtype od,

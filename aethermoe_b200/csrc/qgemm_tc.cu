@@ -396,6 +396,7 @@ aem_status launch_tc(const GemmArgs& a, const TcParams& p, int grid, cudaStream_
     AEM_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     kern<<<grid, kThreads, C::SMEM, s>>>(tw, th, tl, p);
     AEM_CHECK_LAUNCH();
+    count_launches(1);
     return AEM_OK;
 }
 

@@ -121,6 +121,7 @@ aem_status launch_split_bf16(const void* x, aem_dtype xd, int64_t count, void* h
         static_cast<const float*>(x), count, static_cast<__nv_bfloat16*>(hi),
         static_cast<__nv_bfloat16*>(lo));
     AEM_CHECK_LAUNCH();
+    count_launches(1);
     return AEM_OK;
 }
 
@@ -134,6 +135,7 @@ aem_status launch_qgemm_simt(const GemmArgs& a, cudaStream_t s) {
         w.scale, a.M, w.K, w.N, a.group_rows, a.G, a.group_base, a.wmod, a.out, a.ldo, a.out_bf16, a.relu,
         a.atomic_add || a.ksplit > 1, a.rowmap, a.rowscale);
     AEM_CHECK_LAUNCH();
+    count_launches(1);
     return AEM_OK;
 }
 
@@ -145,6 +147,7 @@ aem_status pack_qweight_device(const int8_t* q, const float* scale, int64_t G, i
               static_cast<unsigned>(G));
     transpose_i8_kernel<<<grid, dim3(32, 8), 0, s>>>(q, K, N, w->q);
     AEM_CHECK_LAUNCH();
+    count_launches(1);
     AEM_TRY_CUDA(cudaMemcpyAsync(w->scale, scale, sizeof(float) * G * N, cudaMemcpyDeviceToDevice, s));
     return AEM_OK;
 }
@@ -163,6 +166,7 @@ aem_status aem_quantize_int8(const float* w, int64_t K, int64_t N, int8_t* q, fl
     auto s = static_cast<cudaStream_t>(stream);
     aem::quantize_kernel<<<static_cast<unsigned>((N + 127) / 128), 128, 0, s>>>(w, K, N, q, scale);
     AEM_CHECK_LAUNCH();
+    aem::count_launches(1);
     return AEM_OK;
 }
 

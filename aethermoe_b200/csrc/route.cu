@@ -255,6 +255,7 @@ aem_status route_moe(const MoeRouteArgs& a, cudaStream_t s) {
     scatter_kernel<<<static_cast<unsigned>(c), kThreads, 0, s>>>(
         eff, n, a.E, cnt2, starts, a.T, a.k, a.val, a.src_token, a.rowmap, a.rowscale, a.dest_of);
     AEM_CHECK_LAUNCH();
+    count_launches(7);
     return AEM_OK;
 }
 
@@ -324,6 +325,7 @@ aem_status aem_capacity_route(const uint32_t* primary, const uint32_t* secondary
         aem::chunk_scan_kernel<<<1, aem::kThreads, 0, s>>>(cnt, static_cast<int>(c), E, nullptr);
         aem::assign_kernel<<<static_cast<unsigned>(c), aem::kThreads, 0, s>>>(
             prim_s, sec_s, n, E, cnt, capacity, nullptr, 1, inv, effective);
+        aem::count_launches(5);
         cudaError_t le = cudaGetLastError();
         if (le != cudaSuccess) {
             set_error("aem_capacity_route: launch failed: %s", cudaGetErrorString(le));

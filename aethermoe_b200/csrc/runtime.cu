@@ -2,6 +2,7 @@
 // TMA descriptor encoding and the host-staging context of the *_host calls.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -149,6 +150,78 @@ aem_status make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType 
     return AEM_OK;
 }
 
+// ------------------------------------------------------------------ launch counter
+namespace {
+std::atomic<uint64_t> g_launches{0};
+}
+void count_launches(int n) { g_launches.fetch_add(static_cast<uint64_t>(n), std::memory_order_relaxed); }
+
+// ------------------------------------------------------------------ profiler
+cudaEvent_t PhaseProfiler::take() {
+    if (!pool.empty()) {
+        cudaEvent_t e = pool.back();
+        pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+void PhaseProfiler::begin(int phase, cudaStream_t s) {
+    if (!on) return;
+    cudaEvent_t e = take();
+    cudaEventRecord(e, s);
+    open_ev[phase] = e;
+}
+
+void PhaseProfiler::end(int phase, cudaStream_t s) {
+    if (!on || !open_ev[phase]) return;
+    cudaEvent_t e = take();
+    cudaEventRecord(e, s);
+    pending[phase].emplace_back(open_ev[phase], e);
+    open_ev[phase] = nullptr;
+}
+
+void PhaseProfiler::enable(bool e) {
+    on = e;
+    steps = 0;
+    for (int p = 0; p < AEM_NUM_PHASES; ++p) {
+        acc_ms[p] = 0;
+        for (auto& pr : pending[p]) {
+            pool.push_back(pr.first);
+            pool.push_back(pr.second);
+        }
+        pending[p].clear();
+    }
+}
+
+aem_status PhaseProfiler::read(double* ms, int64_t* nsteps) {
+    for (int p = 0; p < AEM_NUM_PHASES; ++p) {
+        for (auto& pr : pending[p]) {
+            AEM_TRY_CUDA(cudaEventSynchronize(pr.second));
+            float t = 0.0f;
+            AEM_TRY_CUDA(cudaEventElapsedTime(&t, pr.first, pr.second));
+            acc_ms[p] += t;
+            pool.push_back(pr.first);
+            pool.push_back(pr.second);
+        }
+        pending[p].clear();
+        if (ms) ms[p] = acc_ms[p];
+    }
+    if (nsteps) *nsteps = steps;
+    return AEM_OK;
+}
+
+PhaseProfiler::~PhaseProfiler() {
+    for (int p = 0; p < AEM_NUM_PHASES; ++p)
+        for (auto& pr : pending[p]) {
+            cudaEventDestroy(pr.first);
+            cudaEventDestroy(pr.second);
+        }
+    for (auto e : pool) cudaEventDestroy(e);
+}
+
 // ------------------------------------------------------------------ context
 aem_status Context::reserve_device(size_t bytes) {
     if (bytes <= dev_bytes) return AEM_OK;
@@ -187,6 +260,8 @@ extern "C" {
 const char* aem_last_error(void) { return aem::last_error_cstr(); }
 
 const char* aem_version(void) { return "aethermoe-b200 0.1.0 (sm_100a)"; }
+
+uint64_t aem_kernel_launches(void) { return aem::g_launches.load(std::memory_order_relaxed); }
 
 int aem_device_count(void) {
     int n = 0;

@@ -7,9 +7,34 @@
 
 #include "aem.h"
 
+#include <utility>
+#include <vector>
+
 namespace aem {
 
 const char* last_error_cstr();
+
+// Counts kernel launches made by this library (aem_kernel_launches()).
+void count_launches(int n);
+
+// Per-phase device-time accounting with CUDA events on the step's stream.
+struct PhaseProfiler {
+    bool on = false;
+    int64_t steps = 0;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending[AEM_NUM_PHASES];
+    double acc_ms[AEM_NUM_PHASES] = {0};
+    std::vector<cudaEvent_t> pool;
+    cudaEvent_t open_ev[AEM_NUM_PHASES] = {nullptr};
+    cudaEvent_t take();
+    void begin(int phase, cudaStream_t s);
+    void end(int phase, cudaStream_t s);
+    void step() {
+        if (on) ++steps;
+    }
+    void enable(bool e);
+    aem_status read(double* ms, int64_t* nsteps);
+    ~PhaseProfiler();
+};
 
 // Host-staging context behind aem_context_t: one stream plus grow-only
 // device and pinned-host buffers for the *_host entry points.

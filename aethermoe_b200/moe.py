@@ -54,11 +54,15 @@ class MoELayer:
                  gating_mode=_lib.GATING_EXACT, device=0):
         gate_w = np.asarray(gate_w, np.float32)
         d, e = gate_w.shape
-        ffn = np.shape(q_up)[2]
         self.device = device
         self.gate = _lib.Gate(gate_w, gate_b, device)
-        self.up = _lib.QWeight(q_up, np.asarray(s_up, np.float32).reshape(e, ffn), device)
-        self.down = _lib.QWeight(q_down, np.asarray(s_down, np.float32).reshape(e, d), device)
+        if isinstance(q_up, _lib.QWeight):  # already packed (e.g. DeviceQWeight)
+            self.up, self.down = q_up, q_down
+            ffn = q_up.N
+        else:
+            ffn = np.shape(q_up)[2]
+            self.up = _lib.QWeight(q_up, np.asarray(s_up, np.float32).reshape(e, ffn), device)
+            self.down = _lib.QWeight(q_down, np.asarray(s_down, np.float32).reshape(e, d), device)
         self.cfg = make_config(d, ffn, e, top_k, capacity, gating_mode)
         h = _vp()
         _lib.check(_lib.lib().aem_moe_create(ctypes.byref(self.cfg), self.gate.handle,
@@ -93,6 +97,16 @@ class MoELayer:
                                                    x.ctypes.data, xd, x.shape[0], out.ctypes.data,
                                                    od), "aem_moe_forward_host")
         return out
+
+    def profile(self, enable=True):
+        _lib.check(_lib.lib().aem_moe_profile(self.handle, 1 if enable else 0), "aem_moe_profile")
+
+    def profile_read(self):
+        """``({phase: summed ms}, steps)`` since profiling was enabled."""
+        ms = (ctypes.c_double * _lib.NUM_PHASES)()
+        steps = ctypes.c_int64()
+        _lib.check(_lib.lib().aem_moe_profile_read(self.handle, ms, ctypes.byref(steps)))
+        return dict(zip(_lib.PHASES, list(ms))), steps.value
 
     def last_routing(self, T, stream=None):
         """``(idx [T, k(+1)], val [T, k], effective [T*k])`` of the last forward, as torch tensors."""
@@ -147,11 +161,17 @@ class EPLayer:
         gate_w = np.asarray(gate_w, np.float32)
         d, e = gate_w.shape
         eloc = e // world
-        ffn = np.shape(q_up_local)[2]
         self.device = device
         self.gate = _lib.Gate(gate_w, gate_b, device)
-        self.up = _lib.QWeight(q_up_local, np.asarray(s_up_local, np.float32).reshape(eloc, ffn), device)
-        self.down = _lib.QWeight(q_down_local, np.asarray(s_down_local, np.float32).reshape(eloc, d), device)
+        if isinstance(q_up_local, _lib.QWeight):
+            self.up, self.down = q_up_local, q_down_local
+            ffn = q_up_local.N
+        else:
+            ffn = np.shape(q_up_local)[2]
+            self.up = _lib.QWeight(q_up_local, np.asarray(s_up_local, np.float32).reshape(eloc, ffn),
+                                   device)
+            self.down = _lib.QWeight(q_down_local,
+                                     np.asarray(s_down_local, np.float32).reshape(eloc, d), device)
         self.cfg = make_config(d, ffn, e, top_k, capacity, gating_mode)
         uid_buf = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
         h = _vp()
@@ -170,6 +190,15 @@ class EPLayer:
                                              out.data_ptr(), _dtype_code(out), _stream_ptr(stream)),
                    "aem_ep_forward")
         return out
+
+    def profile(self, enable=True):
+        _lib.check(_lib.lib().aem_ep_profile(self.handle, 1 if enable else 0), "aem_ep_profile")
+
+    def profile_read(self):
+        ms = (ctypes.c_double * _lib.NUM_PHASES)()
+        steps = ctypes.c_int64()
+        _lib.check(_lib.lib().aem_ep_profile_read(self.handle, ms, ctypes.byref(steps)))
+        return dict(zip(_lib.PHASES, list(ms))), steps.value
 
     def last_routing(self, T, stream=None):
         import torch

@@ -1,0 +1,524 @@
+#!/usr/bin/env python
+"""MoE-layer tokens/s on B200 -- the expert-parallel MoE layer workload.
+
+Workload (one step = one layer forward over T tokens):
+  E=64 experts, top-6, d=2048, ffn=1408, INT8 weight-only experts (weights
+  ~ N(0, 0.02) quantised per output channel on the GPU), T=16384 tokens per
+  step (global), capacity ceil(1.25*T*k/E) = 1920 per expert, gate bias
+  log p_e with p_e ~ (e+1)^-1.1 (Zipf) forcing capacity reroutes, x ~ N(0,1)
+  bfloat16.  Random-init weights, synthetic tokens.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N=1 runs the single-GPU layer; N>1 (under torchrun, one rank per GPU) runs
+the expert-parallel layer over NCCL with experts split 64/N per GPU and the
+T tokens split T/N per rank (strong scaling: the global step is fixed).
+Rank 0 prints one JSON line.  ``--impl reference`` times the CPU
+implementation of the same layer (the NumPy/C oracle port of the
+reference's algorithm) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+E, K_TOP, D_MODEL, D_FFN, T_GLOBAL, CF, ZIPF_S = 64, 6, 2048, 1408, 16384, 1.25, 1.1
+N_INPUT_BUFFERS = 4
+METRIC = "MoE-layer tokens/s"
+UNIT = "tokens/s"
+
+
+def capacity(tokens):
+    return int(math.ceil(CF * tokens * K_TOP / E))
+
+
+def workload_name(tokens=T_GLOBAL):
+    return (f"expert-parallel MoE layer: E={E}, top-{K_TOP}, d={D_MODEL}, ffn={D_FFN}, "
+            f"INT8 weight-only experts, T={tokens} tokens/step, capacity {capacity(tokens)} "
+            f"= ceil({CF}*T*k/E), Zipf({ZIPF_S}) gate bias, x bf16")
+
+
+def zipf_bias(e, s=ZIPF_S):
+    import numpy as np
+    p = (np.arange(e, dtype=np.float64) + 1.0) ** (-s)
+    p /= p.sum()
+    return np.log(p).astype(np.float32)
+
+
+def gate_weights():
+    import numpy as np
+    rng = np.random.default_rng(1)
+    return (rng.normal(size=(D_MODEL, E)) / np.sqrt(D_MODEL)).astype(np.float32), zipf_bias(E)
+
+
+def expert_weights(experts, device):
+    """INT8 weights of the given experts, generated and quantised on the GPU.
+    Expert e's weights depend only on e (seeded per expert), not on N."""
+    import torch
+    from aethermoe_b200 import _lib
+    qu, su, qd, sd = [], [], [], []
+    for e in experts:
+        g = torch.Generator(device=device)
+        g.manual_seed(1000 + e)
+        w = torch.randn((D_MODEL, D_FFN), generator=g, device=device) * 0.02
+        q, s = _lib.quantize_device(w)
+        qu.append(q)
+        su.append(s)
+        w = torch.randn((D_FFN, D_MODEL), generator=g, device=device) * 0.02
+        q, s = _lib.quantize_device(w)
+        qd.append(q)
+        sd.append(s)
+        del w
+    up = _lib.DeviceQWeight(torch.stack(qu), torch.stack(su))
+    down = _lib.DeviceQWeight(torch.stack(qd), torch.stack(sd))
+    return up, down, (qu, su, qd, sd)
+
+
+def token_buffers(device, tokens, rank, world):
+    import torch
+    tl = tokens // world
+    bufs = []
+    for b in range(N_INPUT_BUFFERS):
+        g = torch.Generator(device=device)
+        g.manual_seed(7 + b)
+        x = torch.randn((tokens, D_MODEL), generator=g, device=device).to(torch.bfloat16)
+        bufs.append(x[rank * tl:(rank + 1) * tl].contiguous())
+        del x
+    return bufs
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = set(gpus)
+        self.path = tempfile.mktemp(prefix="aem_clocks_", suffix=".csv")
+        self.proc = None
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self, t0, t1):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "note": "nvidia-smi unavailable"}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            try:
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                idx = int(parts[1])
+            except ValueError:
+                continue
+            if idx not in self.gpus:
+                continue
+            rows.append((ts, parts))
+        inside = [p for ts, p in rows if t0 <= ts <= t1]
+        note = "samples inside the timed region"
+        if not inside:
+            # timed region shorter than the sampling period: nearest samples
+            rows.sort(key=lambda r: min(abs(r[0] - t0), abs(r[0] - t1)))
+            inside = [p for _, p in rows[:max(1, len(self.gpus))]]
+            note = "timed region shorter than the 100 ms sampling period: nearest samples"
+        sm = [float(p[2]) for p in inside if p[2].replace(".", "").isdigit()]
+        smax = [float(p[3]) for p in inside if p[3].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for p in inside for i in range(4) if p[6 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
+                "samples": len(inside), "note": note}
+
+
+# ------------------------------------------------------------------ CPU path
+def cpu_layer_step(x, gw, gb, q, cap, pool):
+    """One layer step on the host: the oracle port of the reference algorithm.
+
+    Gating with the sequential float32 arithmetic of fused_kernel_simulation,
+    the capacity rule of Router::assign_effective_experts (C), and per expert
+    the reference's naive tier: dequantise the INT8 weights, then a float32
+    BLAS matmul (quantized_gemm.py:86-92), experts spread over a thread pool.
+    """
+    import numpy as np
+    import aem_oracle as O
+    import native
+    qu, su, qd, sd = q
+    t = x.shape[0]
+    idx, val = O.fused_gating(x, gw, gb, K_TOP, extra=1)
+    eff = native.moe_route(idx, K_TOP, E, cap)
+    tok = np.tile(np.arange(t), K_TOP)
+    slot = np.repeat(np.arange(K_TOP), t)
+    out = np.zeros((t, D_MODEL), np.float32)
+
+    def expert(e):
+        sel = np.flatnonzero(eff == e)
+        if sel.size == 0:
+            return None
+        h = x[tok[sel]] @ O.dequantize_int8(qu[e], su[e])
+        np.maximum(h, 0, out=h)
+        y = h @ O.dequantize_int8(qd[e], sd[e])
+        return sel, y * val[tok[sel], slot[sel]][:, None]
+
+    for r in pool.map(expert, range(E)):
+        if r is not None:
+            np.add.at(out, tok[r[0]], r[1])
+    return out
+
+
+def cpu_baseline(weights_host, sample_tokens=512, budget_s=15.0):
+    import numpy as np
+    import aem_oracle as O
+    gw, gb = gate_weights()
+    rng = np.random.default_rng(3)
+    x = O.bf16_round(rng.normal(size=(sample_tokens, D_MODEL)).astype(np.float32))
+    cap = capacity(sample_tokens)
+    cores = os.cpu_count() or 1
+    with cf.ThreadPoolExecutor(max_workers=cores) as pool:
+        cpu_layer_step(x, gw, gb, weights_host, cap, pool)  # warm-up
+        times = []
+        t_start = time.perf_counter()
+        while len(times) < 20 and (time.perf_counter() - t_start) < budget_s:
+            t0 = time.perf_counter()
+            cpu_layer_step(x, gw, gb, weights_host, cap, pool)
+            times.append(time.perf_counter() - t0)
+    per_step = statistics.median(times)
+    return {"value": sample_tokens / per_step, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": (f"{sample_tokens} tokens of the same layer (same weights, capacity "
+                       f"ceil(1.25*{sample_tokens}*6/64)={cap}), median of {len(times)} steps; "
+                       "NumPy/C oracle port: sequential-fp32 gating, C capacity rule, per-expert "
+                       "dequantise + float32 BLAS matmul on a thread pool")}
+
+
+def host_weights_numpy(lists=None):
+    """All 64 experts' INT8 weights on the host for the CPU path: copied from
+    the GPU-generated ones when given (same weights as the GPU run), else
+    generated and quantised with NumPy."""
+    qu, su, qd, sd = lists if lists is not None else _host_generated()
+    return ([q.cpu().numpy() for q in qu], [s.cpu().numpy().reshape(1, -1) for s in su],
+            [q.cpu().numpy() for q in qd], [s.cpu().numpy().reshape(1, -1) for s in sd])
+
+
+def _host_generated():
+    import numpy as np
+    import torch
+    import aem_oracle as O
+    qu, su, qd, sd = [], [], [], []
+    for e in range(E):
+        rng = np.random.default_rng(1000 + e)
+        a, b = O.quantize_int8((rng.normal(size=(D_MODEL, D_FFN)) * 0.02).astype(np.float32))
+        c, d = O.quantize_int8((rng.normal(size=(D_FFN, D_MODEL)) * 0.02).astype(np.float32))
+        qu.append(torch.from_numpy(a)); su.append(torch.from_numpy(b[0]))
+        qd.append(torch.from_numpy(c)); sd.append(torch.from_numpy(d[0]))
+    return qu, su, qd, sd
+
+
+def run_reference(args):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np
+    import aem_oracle as O
+    wh = host_weights_numpy()
+    gw, gb = gate_weights()
+    sample = args.cpu_sample_tokens
+    rng = np.random.default_rng(3)
+    x = O.bf16_round(rng.normal(size=(sample, D_MODEL)).astype(np.float32))
+    cap = capacity(sample)
+    cores = os.cpu_count() or 1
+    times = []
+    budget_s = 60.0  # keeps --steps K --warmup W within a few minutes on any host
+    with cf.ThreadPoolExecutor(max_workers=cores) as pool:
+        t_start = time.perf_counter()
+        for i in range(args.warmup):
+            if i >= 1 and time.perf_counter() - t_start > budget_s / 4:
+                break
+            cpu_layer_step(x, gw, gb, wh, cap, pool)
+        t_start = time.perf_counter()
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            cpu_layer_step(x, gw, gb, wh, cap, pool)
+            times.append(time.perf_counter() - t0)
+            if len(times) >= 3 and time.perf_counter() - t_start > budget_s:
+                break
+    total = sum(times)
+    value = sample * len(times) / total
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference",
+        "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / len(times), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload_name(sample), "tokens_per_step": sample,
+                   "note": "bounded sample of the layer on host cores (the reference has no GPU path here)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{sample} tokens per step, {len(times)} timed steps"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ GPU path
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            m = json.load(f)
+        return m.get("bf16_tflops_sustained"), m.get("bf16_tflops"), m.get("hbm_gbs"), "measured"
+    return 1400.0, 1590.0, 6650.0, "fallback"
+
+
+def traffic_from_profile():
+    p = os.path.join(ROOT, "profiles", "qgemm_tc_traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return None
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import aethermoe_b200 as aem
+    from aethermoe_b200 import _lib
+    from aethermoe_b200.moe import EPLayer, MoELayer, ep_unique_id
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if aem.device_count() < 1:
+        raise SystemExit("no sm_100 device visible to libaethermoe")
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    tokens = args.tokens
+    assert tokens % world == 0 and E % world == 0
+    tl = tokens // world
+    eloc = E // world
+    cap = capacity(tokens)
+    gw, gb = gate_weights()
+    up, down, qlists = expert_weights(range(rank * eloc, (rank + 1) * eloc), dev)
+    torch.cuda.synchronize()
+    if world == 1:
+        layer = MoELayer(gw, gb, up, None, down, None, K_TOP, capacity=cap, device=local)
+    else:
+        uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(ep_unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        layer = EPLayer(bytes(uid.cpu().numpy()), rank, world, gw, gb, up, None, down, None,
+                        K_TOP, capacity=cap, device=local)
+    xs = token_buffers(dev, tokens, rank, world)
+    outs = [torch.empty((tl, D_MODEL), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        layer.forward(xs[i % N_INPUT_BUFFERS], out=outs[i % 2], stream=stream)
+    barrier()
+    clocks = ClockSampler([local] if world == 1 else list(range(world))) if rank == 0 else None
+    time.sleep(0.3 if clocks else 0.0)
+    barrier()
+    layer.profile(True)
+    launches0 = aem.lib().aem_kernel_launches()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
+    ev0.record(stream)
+    for i in range(args.steps):
+        layer.forward(xs[i % N_INPUT_BUFFERS], out=outs[i % 2], stream=stream)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    launches = aem.lib().aem_kernel_launches() - launches0
+    ms = ev0.elapsed_time(ev1)
+    phases, nsteps = layer.profile_read()
+    layer.profile(False)
+    aem.check(aem.lib().aem_device_status(ctypes_stream(stream)))
+    t_max = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms_max = float(t_max.item())
+    barrier()
+    clock_summary = None
+    if clocks is not None:
+        clocks.stop()
+        clock_summary = clocks.summary(t_wall0, t_wall1)
+
+    # ---- end to end: host buffers in, host buffers out, through the public API
+    e2e = e2e_run(args, layer, world, rank, tl, dev, stream, barrier)
+
+    # ---- roofline of the dominant kernel (the grouped INT8 GEMM, up + down launches)
+    gemm_ms = (phases["up_gemm"] + phases["down_gemm"]) / max(1, nsteps)
+    units_local = tokens * K_TOP / world  # average rows per rank
+    gemm_flops = 2.0 * units_local * D_MODEL * D_FFN * 2
+    tflops = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
+    sustained, burst, hbm, src = measured_peaks()
+    traffic = traffic_from_profile()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        wh = host_weights_numpy(qlists)
+        cpu = cpu_baseline(wh, sample_tokens=args.cpu_sample_tokens)
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        value = tokens * args.steps / (ms_max * 1e-3)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": workload_name(tokens), "tokens_per_step": tokens,
+                       "global_batch": tokens, "parallelism": f"ep{world}",
+                       "l2": (f"inputs rotate over {N_INPUT_BUFFERS} buffers "
+                              f"({N_INPUT_BUFFERS * tokens * D_MODEL * 2 >> 20} MiB > 126 MiB L2); "
+                              "per-step working set > 1 GiB")},
+            "roofline": {"kernel": "qgemm_tc_kernel (grouped INT8-weight GEMM, up + down launches)",
+                         "bound": "tensor", "achieved": tflops,
+                         "peak": sustained, "unit": "TFLOP/s",
+                         "frac": (tflops / sustained) if tflops and sustained else None,
+                         "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step)",
+                         "traffic": (traffic or {}).get("bytes_per_launch"),
+                         "algorithmic_flops_per_step": gemm_flops,
+                         "kernel_ms_per_step": gemm_ms},
+            "phases_ms_per_step": {k: v / max(1, nsteps) for k, v in phases.items() if v > 0},
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "gpu_launches_per_step": launches / args.steps,
+            "clocks": clock_summary,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    layer.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def ctypes_stream(stream):
+    import ctypes
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+def e2e_run(args, layer, world, rank, tl, dev, stream, barrier):
+    """Same step through the public API with pinned HOST buffers each step."""
+    import ctypes
+    import torch
+    import aethermoe_b200 as aem
+    from aethermoe_b200 import _lib
+    steps = max(3, min(args.steps, args.e2e_steps))
+    xh = [torch.empty((tl, D_MODEL), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    for i, x in enumerate(xh):
+        x.copy_(torch.randn((tl, D_MODEL), generator=torch.Generator().manual_seed(50 + i)))
+    oh = torch.empty((tl, D_MODEL), dtype=torch.bfloat16).pin_memory()
+    if world == 1:
+        ctx = _lib.context(dev.index)
+        cstream = torch.cuda.ExternalStream(aem.lib().aem_context_stream(ctx))
+
+        def step(i):
+            _lib.check(aem.lib().aem_moe_forward_host(ctx, layer.handle, xh[i % 2].data_ptr(),
+                                                      _lib.BF16, tl, oh.data_ptr(), _lib.BF16))
+        for i in range(2):
+            step(i)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(cstream)
+        for i in range(steps):
+            step(i)
+        e1.record(cstream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+    else:
+        xd = torch.empty((tl, D_MODEL), dtype=torch.bfloat16, device=dev)
+        od = torch.empty((tl, D_MODEL), dtype=torch.bfloat16, device=dev)
+
+        def step(i):
+            xd.copy_(xh[i % 2], non_blocking=True)
+            layer.forward(xd, out=od, stream=stream)
+            oh.copy_(od, non_blocking=True)
+            stream.synchronize()
+        for i in range(2):
+            step(i)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        import torch.distributed as dist
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    tokens = tl * world
+    return {"value": tokens * steps / (ms * 1e-3), "unit": UNIT,
+            "h2d_bytes_per_step": tokens * D_MODEL * 2, "d2h_bytes_per_step": tokens * D_MODEL * 2,
+            "steps": steps, "api": "aem_moe_forward_host" if world == 1 else
+            "aem_ep_forward + pinned host copies on the same stream"}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=T_GLOBAL)
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--cpu-sample-tokens", type=int, default=256)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

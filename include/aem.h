@@ -65,6 +65,23 @@ int aem_device_count(void);
  * device since the last check: AEM_OK, AEM_EDEVICE or AEM_ETIMEOUT. */
 aem_status aem_device_status(void* stream);
 
+/* Total number of kernels this library has launched in this process (all
+ * devices, all entry points): lets a caller count the launches of a step. */
+uint64_t aem_kernel_launches(void);
+
+/* Phases of a layer step whose device time can be profiled. */
+enum {
+    AEM_PHASE_GATING = 0,   /* fused gating */
+    AEM_PHASE_ROUTE = 1,    /* capacity routing, permutation, row gather */
+    AEM_PHASE_UP = 2,       /* grouped INT8 up GEMM + ReLU */
+    AEM_PHASE_DOWN = 3,     /* grouped INT8 down GEMM */
+    AEM_PHASE_COMBINE = 4,  /* weighted combine */
+    AEM_PHASE_DISPATCH = 5, /* expert parallel: token rows to expert owners */
+    AEM_PHASE_RETURN = 6,   /* expert parallel: expert outputs back */
+    AEM_PHASE_EXCHANGE = 7, /* expert parallel: count all-gathers and the size sync */
+    AEM_NUM_PHASES = 8
+};
+
 /* ---- host-side context (staging for *_host calls) ------------------------- */
 
 typedef struct aem_context_s* aem_context_t;
@@ -201,6 +218,12 @@ aem_status aem_moe_forward(aem_moe_t moe, const void* x, aem_dtype x_dtype, int6
 /* HOST-buffer form of aem_moe_forward (synchronous). */
 aem_status aem_moe_forward_host(aem_context_t ctx, aem_moe_t moe, const void* x, aem_dtype x_dtype,
                                 int64_t T, void* out, aem_dtype out_dtype);
+/* Per-phase profiling with CUDA events recorded on the step's stream.
+ * enable != 0 starts (and clears) accumulation; aem_moe_profile_read
+ * synchronises, then writes the summed milliseconds of each phase
+ * (ms[AEM_NUM_PHASES]) and the number of profiled steps. */
+aem_status aem_moe_profile(aem_moe_t moe, int enable);
+aem_status aem_moe_profile_read(aem_moe_t moe, double* ms, int64_t* steps);
 /* Routing of the last forward (device pointers, stream-ordered copies):
  * idx int32 [T, k+1] (k+1 clipped to E), val f32 [T, k], effective uint32 [T*k]. */
 aem_status aem_moe_last_routing(aem_moe_t moe, int32_t* idx, float* val, uint32_t* effective,
@@ -234,6 +257,9 @@ aem_status aem_ep_free(aem_ep_t ep);
  * -> its outputs.  Collective: every rank calls it with the same T_local. */
 aem_status aem_ep_forward(aem_ep_t ep, const void* x, aem_dtype x_dtype, int64_t T_local, void* out,
                           aem_dtype out_dtype, void* stream);
+/* Per-phase profiling of this rank's steps (see aem_moe_profile). */
+aem_status aem_ep_profile(aem_ep_t ep, int enable);
+aem_status aem_ep_profile_read(aem_ep_t ep, double* ms, int64_t* steps);
 /* Routing of the last step for this rank's units (device pointers):
  * idx [T_local, k+1], val [T_local, k], effective [k*T_local] (slot-major). */
 aem_status aem_ep_last_routing(aem_ep_t ep, int32_t* idx, float* val, uint32_t* effective,
