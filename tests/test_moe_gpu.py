@@ -25,10 +25,12 @@ def _weights(rng, e, d, f, quantize=True):
             c, g = O.quantize_int8((rng.normal(size=(f, d)) * 0.02).astype(np.float32))
             qu.append(a); su.append(b); qd.append(c); sd.append(g)
         return np.stack(qu), np.stack(su), np.stack(qd), np.stack(sd)
+    # uniform int8 (std ~73) with scales ~2.5e-4: weights of std ~0.02 like
+    # N(0, 0.02) quantised per output channel
     qu = rng.integers(-127, 128, size=(e, d, f), dtype=np.int8)
-    su = (rng.random(size=(e, 1, f)) * 2e-4 + 5e-4).astype(np.float32)
+    su = (rng.random(size=(e, 1, f)) * 1e-4 + 2e-4).astype(np.float32)
     qd = rng.integers(-127, 128, size=(e, f, d), dtype=np.int8)
-    sd = (rng.random(size=(e, 1, d)) * 2e-4 + 5e-4).astype(np.float32)
+    sd = (rng.random(size=(e, 1, d)) * 1e-4 + 2e-4).astype(np.float32)
     return qu, su, qd, sd
 
 
