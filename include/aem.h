@@ -46,8 +46,9 @@ typedef enum { AEM_F32 = 0, AEM_BF16 = 1 } aem_dtype;
  *   float32 in increasing d order, bias last -- bit-identical logits to the
  *   reference's fused_kernel_simulation (prototype/math_proto.py:19-50), so
  *   indices match it bit-exactly on every row.
- * FAST: fused multiply-add with a split reduction over d; indices match on
- *   every row whose k-th/(k+1)-th logit gap exceeds float32 rounding. */
+ * FAST: fused multiply-adds (one rounding per term) in the same order;
+ *   indices match on every row whose k-th/(k+1)-th logit gap exceeds
+ *   float32 rounding. */
 typedef enum { AEM_GATING_EXACT = 0, AEM_GATING_FAST = 1 } aem_gating_mode;
 
 #define AEM_MAX_EXPERTS 256 /* fused_gating_metal.py:230 MAX_EXPERTS */
