@@ -13,6 +13,7 @@
 // kernels, keyed by the effective expert, produce the MoE permutation that
 // groups units by expert for the grouped GEMM.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "route.h"
@@ -338,3 +339,109 @@ aem_status aem_capacity_route(const uint32_t* primary, const uint32_t* secondary
 }
 
 }  // extern "C"
+
+// ============================================================================
+// Capacity routing without device allocation.
+//
+// Some callers cannot allocate device memory while they run: a serving loop
+// that reserves its whole memory budget at start-up and forbids growth, or
+// one that cannot afford the device-wide synchronisation that cudaFree (and
+// often cudaMalloc) implies in the middle of a latency-bound step.  For them
+// aem_capacity_route_static keeps its scratch in the file-scope array below,
+// sized for AEM_ROUTE_STATIC_MAX_UNITS units and AEM_MAX_EXPERTS experts;
+// every GPU that loads this library holds the array until the process exits.
+// ============================================================================
+namespace aem {
+namespace {
+
+constexpr size_t a256(size_t v) { return (v + 255) / 256 * 256; }
+constexpr int64_t kStaticUnits = AEM_ROUTE_STATIC_MAX_UNITS;
+constexpr int64_t kStaticChunks = (kStaticUnits + kChunk - 1) / kChunk;
+constexpr size_t kStaticIdxBytes = a256(sizeof(int32_t) * kStaticUnits);
+constexpr size_t kStaticCntBytes = a256(sizeof(int) * kStaticChunks * AEM_MAX_EXPERTS);
+// inv, seen, primary and secondary in position order, chunk counts, error word
+constexpr size_t kStaticBytes = 4 * kStaticIdxBytes + kStaticCntBytes + 256;
+static_assert(kStaticBytes == AEM_ROUTE_STATIC_SCRATCH_BYTES, "scratch size in aem.h");
+
+static __device__ __align__(256) unsigned char g_route_scratch[kStaticBytes];
+
+std::mutex g_route_scratch_mutex;
+void* g_route_scratch_addr[64] = {nullptr};
+
+// Device address of g_route_scratch on the current device, looked up once
+// per device (host code only sees a stand-in symbol, never the address).
+aem_status route_scratch_address(void** out) {
+    int dev = 0;
+    AEM_TRY_CUDA(cudaGetDevice(&dev));
+    AEM_REQUIRE(dev >= 0 && dev < 64, "aem_capacity_route_static: device %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_route_scratch_mutex);
+    if (!g_route_scratch_addr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_route_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            set_error("aem_capacity_route_static: cudaGetSymbolAddress failed: %s",
+                      cudaGetErrorString(e));
+            return AEM_ECUDA;
+        }
+        g_route_scratch_addr[dev] = p;
+    }
+    *out = g_route_scratch_addr[dev];
+    return AEM_OK;
+}
+
+}  // namespace
+}  // namespace aem
+
+extern "C" aem_status aem_capacity_route_static(const uint32_t* primary, const uint32_t* secondary,
+                                                const uint32_t* batch_position, int64_t n, int E,
+                                                uint64_t capacity, uint32_t* effective,
+                                                void* stream) {
+    AEM_REQUIRE(n >= 0, "aem_capacity_route_static: n=%lld must be >= 0", (long long)n);
+    AEM_REQUIRE(n <= AEM_ROUTE_STATIC_MAX_UNITS,
+                "aem_capacity_route_static: n=%lld exceeds the fixed scratch maximum of %d units "
+                "(use aem_capacity_route)",
+                (long long)n, AEM_ROUTE_STATIC_MAX_UNITS);
+    AEM_REQUIRE(E >= 1 && E <= AEM_MAX_EXPERTS, "aem_capacity_route_static: E=%d outside [1, %d]",
+                E, AEM_MAX_EXPERTS);
+    if (n == 0) return AEM_OK;
+    AEM_REQUIRE(primary && secondary && batch_position && effective,
+                "aem_capacity_route_static: NULL buffer");
+    auto s = static_cast<cudaStream_t>(stream);
+    void* base = nullptr;
+    AEM_TRY(aem::route_scratch_address(&base));
+    char* w = static_cast<char*>(base);
+    int32_t* inv = reinterpret_cast<int32_t*>(w);
+    int32_t* seen = reinterpret_cast<int32_t*>(w + aem::kStaticIdxBytes);
+    uint32_t* prim_s = reinterpret_cast<uint32_t*>(w + 2 * aem::kStaticIdxBytes);
+    uint32_t* sec_s = reinterpret_cast<uint32_t*>(w + 3 * aem::kStaticIdxBytes);
+    int* cnt = reinterpret_cast<int*>(w + 4 * aem::kStaticIdxBytes);
+    int* err = reinterpret_cast<int*>(w + 4 * aem::kStaticIdxBytes + aem::kStaticCntBytes);
+    const int64_t c = aem::route_chunks(n);
+    // The array keeps the previous call's contents: reset what must start
+    // known (the permutation marks, the inverse, the error word).
+    AEM_TRY_CUDA(cudaMemsetAsync(seen, 0, sizeof(int32_t) * n, s));
+    AEM_TRY_CUDA(cudaMemsetAsync(inv, 0xFF, sizeof(int32_t) * n, s));
+    AEM_TRY_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+    const unsigned gb = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 4096));
+    aem::invert_positions_kernel<<<gb, 256, 0, s>>>(batch_position, n, inv, seen, err);
+    aem::gather_by_position_kernel<<<gb, 256, 0, s>>>(primary, secondary, inv, n, E, prim_s, sec_s,
+                                                      err);
+    aem::chunk_count_kernel<<<static_cast<unsigned>(c), aem::kThreads, 0, s>>>(prim_s, n, E, cnt);
+    aem::chunk_scan_kernel<<<1, aem::kThreads, 0, s>>>(cnt, static_cast<int>(c), E, nullptr);
+    aem::assign_kernel<<<static_cast<unsigned>(c), aem::kThreads, 0, s>>>(
+        prim_s, sec_s, n, E, cnt, capacity, nullptr, 1, inv, effective);
+    AEM_CHECK_LAUNCH();
+    aem::count_launches(5);
+    int bits = 0;
+    AEM_TRY_CUDA(cudaMemcpyAsync(&bits, err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    AEM_TRY_CUDA(cudaStreamSynchronize(s));
+    if (bits & aem::ERR_ROUTE_POSITION) {
+        set_error("aem_capacity_route_static: batch_position is not a permutation of [0, n)");
+        return AEM_EDEVICE;
+    }
+    if (bits) {
+        set_error("aem_capacity_route_static: expert id out of range (error bits 0x%x)", bits);
+        return AEM_EDEVICE;
+    }
+    return AEM_OK;
+}

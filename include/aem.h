@@ -188,6 +188,29 @@ aem_status aem_capacity_route(const uint32_t* primary, const uint32_t* secondary
                               uint32_t* effective, void* workspace, size_t workspace_bytes,
                               void* stream);
 
+/* Capacity routing that allocates no device memory.  No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc while they
+ * run -- a serving loop that reserves its whole device budget at start-up
+ * and may not grow it, or one that cannot pay the device-wide
+ * synchronisation cudaFree implies in the middle of a step.  Same rule,
+ * arguments and results as aem_capacity_route, but the scratch is a fixed
+ * array of AEM_ROUTE_STATIC_SCRATCH_BYTES in the library's device memory,
+ * held on every GPU that loads the library until the process exits.
+ *   - n > AEM_ROUTE_STATIC_MAX_UNITS (or E > AEM_MAX_EXPERTS) -> AEM_EINVAL.
+ *   - The first call on a device looks the array's address up on that
+ *     device (with the device current); make that first call before any
+ *     stream capture.
+ *   - Every call on a device shares the one array and it keeps the last
+ *     call's contents (each call resets what must start at zero): calls
+ *     that overlap on the GPU -- on different streams or from different
+ *     host threads -- race.  Serialise them.
+ *   - It synchronises `stream` to report in-kernel check failures. */
+#define AEM_ROUTE_STATIC_MAX_UNITS 262144
+#define AEM_ROUTE_STATIC_SCRATCH_BYTES 4325632
+aem_status aem_capacity_route_static(const uint32_t* primary, const uint32_t* secondary,
+                                     const uint32_t* batch_position, int64_t n, int E,
+                                     uint64_t capacity, uint32_t* effective, void* stream);
+
 /* ---- MoE layer (gating -> routing -> grouped INT8 expert FFN -> combine) --------- */
 
 typedef struct {
