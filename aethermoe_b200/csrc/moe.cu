@@ -8,8 +8,8 @@
 //   3. expert-grouped layout    -> rows grouped by effective expert
 //   4. gather                   -> X [U, d] bf16 in grouped order
 //   5. grouped up GEMM + ReLU   -> H [U, ffn] bf16
-//   6. grouped down GEMM        -> Y [T*k, d] f32, row t*k+j, scaled by val[t, j]
-//   7. combine                  -> out[t] = sum_j Y[t*k+j]
+//   6. grouped down GEMM + combine -> out[t] += val[t, j] * y  (float32 red.add
+//                                  from the GEMM epilogue; bf16 output converted after)
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -254,6 +254,10 @@ aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaSt
     AEM_TRY(launch_qgemm(up_a, s));
     prof.end(AEM_PHASE_UP, s);
 
+    // Down projection with the combine fused into its epilogue: every grouped
+    // row's output, scaled by its gate weight, is red.add-ed into its token's
+    // float32 output row (k contributions per token, from different tiles).
+    float* acc = od == AEM_F32 ? static_cast<float*>(out) : y;
     GemmArgs dn;
     dn.w = down;
     dn.G = up_a.G;
@@ -261,28 +265,31 @@ aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaSt
     dn.M = U;
     dn.max_rows = U;
     dn.x_hi = h;
-    dn.out = y;
+    dn.out = acc;
     dn.ldo = d;
-    dn.rowmap = rowmap;
+    dn.rowmap = src_token;
     dn.rowscale = rowscale;
+    dn.atomic_add = true;
     // Split K across CTAs when the tiles cannot fill the GPU (decode sizes).
     const int64_t groups_used = std::min<int64_t>(E, U);
     const int64_t nch = (d + 127) / 128;
-    const int64_t tiles = std::max<int64_t>(1, groups_used) * nch * ((U / std::max<int64_t>(1, groups_used) + 255) / 256);
+    const int64_t tiles = std::max<int64_t>(1, groups_used) * nch *
+                          ((U / std::max<int64_t>(1, groups_used) + 255) / 256);
     const int sms = sm_count(gate->device);
     int ks = 1;
-    if (tiles < sms) ks = static_cast<int>(std::min<int64_t>((2 * sms + tiles - 1) / tiles, (f + 63) / 64));
+    if (tiles < sms)
+        ks = static_cast<int>(std::min<int64_t>((2 * sms + tiles - 1) / tiles, (f + 63) / 64));
+    dn.ksplit = ks;
     prof.begin(AEM_PHASE_DOWN, s);
-    if (ks > 1) {
-        AEM_TRY_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * U * d, s));
-        dn.atomic_add = true;
-        dn.ksplit = ks;
-    }
+    AEM_TRY_CUDA(cudaMemsetAsync(acc, 0, sizeof(float) * T * d, s));
     AEM_TRY(launch_qgemm(dn, s));
     prof.end(AEM_PHASE_DOWN, s);
-    prof.begin(AEM_PHASE_COMBINE, s);
-    AEM_TRY(combine_rows(y, T, k, d, out, od, s));
-    prof.end(AEM_PHASE_COMBINE, s);
+    if (od != AEM_F32) {
+        prof.begin(AEM_PHASE_COMBINE, s);
+        AEM_TRY(combine_rows(acc, T, 1, d, out, od, s));  // float32 -> bf16
+        prof.end(AEM_PHASE_COMBINE, s);
+    }
+    (void)k;
     return AEM_OK;
 }
 

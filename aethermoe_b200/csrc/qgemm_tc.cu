@@ -9,19 +9,21 @@
 // activation rows (the MMA's N, 16..256), which keeps decode-size batches (a handful
 // of rows) on the tensor cores with the int8 weight stream as the only large read.
 //
-// Per CTA (one per SM, persistent over tiles), 10 warps:
-//   warp 8      TMA producer: int8 weight tile [128 x 64 B] (no swizzle) and the bf16
-//               activation tile(s) [BT x 128 B] (128-byte swizzle) into a STAGES ring.
+// Per CTA (one per SM, persistent over tiles), 11 warps:
+//   warp 8      int8 weight producer: TMA of [128 x 64 B] tiles (no swizzle) into a
+//               deep ring (6-8 stages) -- the HBM stream runs ahead of everything else.
+//   warp 10     activation producer: TMA of the bf16 [BT x 128 B] tile(s) (128-byte
+//               swizzle) into the operand ring.
 //   warps 0-3   converters: int8 -> bf16 (exact: |q| <= 127 fits bf16's 8-bit
 //               significand) written straight into the 128-byte-swizzled K-major layout
-//               the MMA reads, then fence.proxy.async + mbarrier arrive.
+//               the MMA reads, then fence.proxy.async and one mbarrier arrival per warp.
 //   warp 9      MMA issuer (one thread): 4 x tcgen05.mma kind::f16 (K=16 each) per
 //               64-wide stage, x2 for split float32 activations (hi + lo), accumulating
 //               float32 in a double-buffered TMEM accumulator; tcgen05.commit frees the
-//               smem stage and, at the end of a tile, hands the accumulator over.
-//   warps 4-7   epilogue: tcgen05.ld 32 lanes x 16 columns, per-channel scale, optional
-//               per-row multiplier, ReLU, bf16/f32 store or red.add (split-K), optional
-//               output-row remap (MoE scatter).
+//               operand stage and, at the end of a tile, hands the accumulator over.
+//   warps 4-7   epilogue: tcgen05.ld 32 lanes x 16 columns, per-channel scale, per-row
+//               output index and multiplier (fetched once per 16 columns, broadcast by
+//               shuffles), ReLU, bf16/f32 store or red.add (split-K / fused combine).
 // Every mbarrier wait is bounded (globaltimer); on timeout the kernel records an
 // error bit, all roles drain out, and TMEM is released.  No multicast is used.
 #include <cuda_bf16.h>
@@ -42,8 +44,9 @@ using namespace aem::dev;
 constexpr int kCh = 128;      // output channels per tile = MMA M
 constexpr int kKT = 64;       // K per stage: one 128-byte bf16 row
 constexpr int kConvThreads = 128;
-constexpr int kEpiThreads = 128;
-constexpr int kThreads = 320;  // 4 converter + 4 epilogue + producer + MMA warps
+constexpr int kConvWarps = 4;
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = 352;  // 4 converter + 4 epilogue + 2 producer + MMA warps
 constexpr int kMaxGroups = 256;
 
 struct TcParams {
@@ -68,18 +71,22 @@ struct TcParams {
 
 template <int BT, int SPLIT>
 struct Cfg {
-    static constexpr int W8 = kCh * kKT;           // int8 staging tile, bytes
+    static constexpr int W8 = kCh * kKT;           // int8 weight tile, bytes
     static constexpr int W16 = kCh * kKT * 2;      // bf16 weight tile (MMA A)
     static constexpr int XB = BT * kKT * 2;        // bf16 activation tile (MMA B), per part
-    static constexpr int STAGE = W16 + SPLIT * XB + W8;
-    static constexpr int STAGES_RAW = (200 * 1024) / STAGE;
-    static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+    static constexpr int MAIN = W16 + SPLIT * XB;  // one stage of the MMA operand ring
+    // The int8 ring runs further ahead than the operand ring: its tiles come
+    // from HBM (the long latency), the activation tiles mostly from L2.
+    static constexpr int S8 = BT <= 128 ? 8 : 6;
+    static constexpr int MS_RAW = (208 * 1024 - S8 * W8) / MAIN;
+    static constexpr int MS = MS_RAW > 8 ? 8 : MS_RAW;
     static constexpr int TMEM_COLS = 2 * BT < 32 ? 32 : 2 * BT;
     static constexpr uint32_t IDESC = idesc_bf16_f32(kCh, BT);
-    static constexpr int BAR_BYTES = (3 * STAGES + 4) * 8 + 16;
+    static constexpr int BAR_BYTES = (3 * MS + 2 * S8 + 4) * 8 + 16;
     static constexpr int TAB_BYTES = 2 * (kMaxGroups + 1) * 4;
-    static constexpr int SMEM = 1024 + STAGES * STAGE + BAR_BYTES + TAB_BYTES;
-    static_assert(STAGES >= 2, "pipeline needs two stages");
+    static constexpr int SMEM = 1024 + MS * MAIN + S8 * W8 + BAR_BYTES + TAB_BYTES;
+    static_assert(MS >= 2, "pipeline needs two operand stages");
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
     static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N for M=128");
 };
 
@@ -144,15 +151,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint8_t* stage_base = smem;
-    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE);
-    uint64_t* conv_bar = full_bar + C::STAGES;
-    uint64_t* empty_bar = conv_bar + C::STAGES;
-    uint64_t* accf_bar = empty_bar + C::STAGES;  // [2]
-    uint64_t* acce_bar = accf_bar + 2;           // [2]
+    uint8_t* main_ring = smem;                      // MS x [bf16 W | X hi | X lo]
+    uint8_t* w8_ring = smem + C::MS * C::MAIN;      // S8 x int8 W
+    uint64_t* x_full = reinterpret_cast<uint64_t*>(w8_ring + C::S8 * C::W8);
+    uint64_t* conv_full = x_full + C::MS;
+    uint64_t* op_empty = conv_full + C::MS;
+    uint64_t* w8_full = op_empty + C::MS;
+    uint64_t* w8_empty = w8_full + C::S8;
+    uint64_t* accf_bar = w8_empty + C::S8;  // [2]
+    uint64_t* acce_bar = accf_bar + 2;      // [2]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    int* s_rows = reinterpret_cast<int*>(smem + C::STAGES * C::STAGE + C::BAR_BYTES);
+    int* s_rows = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(x_full) + C::BAR_BYTES);
     int* s_tiles = s_rows + (kMaxGroups + 1);
 
     const int tid = threadIdx.x;
@@ -161,14 +171,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- setup: barriers, group table, TMEM
     if (tid == 0) {
-        for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&full_bar[s], 1);
-            mbar_init(&conv_bar[s], kConvThreads);
-            mbar_init(&empty_bar[s], 1);
+        for (int s = 0; s < C::MS; ++s) {
+            mbar_init(&x_full[s], 1);
+            mbar_init(&conv_full[s], kConvWarps);
+            mbar_init(&op_empty[s], 1);
+        }
+        for (int s = 0; s < C::S8; ++s) {
+            mbar_init(&w8_full[s], 1);
+            mbar_init(&w8_empty[s], kConvWarps);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&accf_bar[b], 1);
-            mbar_init(&acce_bar[b], kEpiThreads);
+            mbar_init(&acce_bar[b], kEpiWarps);
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -210,30 +224,57 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int total = s_tiles[p.G];
 
     if (warp == 8) {
-        // ================= TMA producer
+        // ================= int8 weight producer (HBM stream)
+        if (lane == 0) {
+            int s8 = 0;
+            uint32_t ph8 = 0;
+            for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+                const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
+                const int wrow = ti.wg * p.N + ti.n0;
+                bool ok = true;
+                for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
+                    if (!mbar_wait_bounded(&w8_empty[s8], ph8 ^ 1, abort_flag, p.err,
+                                           ERR_GEMM_TIMEOUT)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&w8_full[s8], C::W8);
+                    tma_load_2d(w8_ring + s8 * C::W8, &tm_w, &w8_full[s8], kt * kKT, wrow);
+                    if (++s8 == C::S8) {
+                        s8 = 0;
+                        ph8 ^= 1;
+                    }
+                }
+                if (!ok) break;
+            }
+        }
+    } else if (warp == 10) {
+        // ================= activation producer
         if (lane == 0) {
             int s = 0;
             uint32_t ph = 0;
             for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
                 const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
-                const int wrow = ti.wg * p.N + ti.n0;
+                bool ok = true;
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                    if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1, abort_flag, p.err,
-                                           ERR_GEMM_TIMEOUT))
+                    if (!mbar_wait_bounded(&op_empty[s], ph ^ 1, abort_flag, p.err,
+                                           ERR_GEMM_TIMEOUT)) {
+                        ok = false;
                         break;
-                    uint8_t* st = stage_base + s * C::STAGE;
-                    mbar_arrive_expect_tx(&full_bar[s], C::W8 + SPLIT * C::XB);
-                    tma_load_2d(st + C::W16 + SPLIT * C::XB, &tm_w, &full_bar[s], kt * kKT, wrow);
-                    tma_load_2d(st + C::W16, &tm_xh, &full_bar[s], kt * kKT,
+                    }
+                    uint8_t* st = main_ring + s * C::MAIN;
+                    mbar_arrive_expect_tx(&x_full[s], SPLIT * C::XB);
+                    tma_load_2d(st + C::W16, &tm_xh, &x_full[s], kt * kKT,
                                 static_cast<int>(ti.row0));
                     if (SPLIT == 2)
-                        tma_load_2d(st + C::W16 + C::XB, &tm_xl, &full_bar[s], kt * kKT,
+                        tma_load_2d(st + C::W16 + C::XB, &tm_xl, &x_full[s], kt * kKT,
                                     static_cast<int>(ti.row0));
-                    if (++s == C::STAGES) {
+                    if (++s == C::MS) {
                         s = 0;
                         ph ^= 1;
                     }
                 }
+                if (!ok) break;
             }
         }
     } else if (warp == 9) {
@@ -252,13 +293,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BT);
                 bool ok = true;
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                    if (!mbar_wait_bounded(&full_bar[s], ph, abort_flag, p.err, ERR_GEMM_TIMEOUT) ||
-                        !mbar_wait_bounded(&conv_bar[s], ph, abort_flag, p.err, ERR_GEMM_TIMEOUT)) {
+                    if (!mbar_wait_bounded(&x_full[s], ph, abort_flag, p.err, ERR_GEMM_TIMEOUT) ||
+                        !mbar_wait_bounded(&conv_full[s], ph, abort_flag, p.err,
+                                           ERR_GEMM_TIMEOUT)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    uint8_t* st = stage_base + s * C::STAGE;
+                    uint8_t* st = main_ring + s * C::MAIN;
                     const uint64_t adesc = smem_desc_sw128(smem_u32(st));
                     const uint64_t bdesc = smem_desc_sw128(smem_u32(st + C::W16));
                     const uint64_t ldesc = smem_desc_sw128(smem_u32(st + C::W16 + C::XB));
@@ -270,8 +312,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (SPLIT == 2)
                             tc_mma_f16(d_tmem, adesc + 2 * kk, ldesc + 2 * kk, C::IDESC, 1u);
                     }
-                    tc_commit(&empty_bar[s]);
-                    if (++s == C::STAGES) {
+                    tc_commit(&op_empty[s]);
+                    if (++s == C::MS) {
                         s = 0;
                         ph ^= 1;
                     }
@@ -282,18 +324,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp < 4) {
         // ================= converters: int8 [128 x 64B] -> bf16 SW128 [128 x 128B]
-        int s = 0;
-        uint32_t ph = 0;
+        int s = 0, s8 = 0;
+        uint32_t ph = 0, ph8 = 0;
         for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
             const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
             bool ok = true;
             for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                if (!mbar_wait_bounded(&full_bar[s], ph, abort_flag, p.err, ERR_GEMM_TIMEOUT)) {
+                // int8 tile landed, and the operand slot is free (its last MMA retired)
+                if (!mbar_wait_bounded(&w8_full[s8], ph8, abort_flag, p.err, ERR_GEMM_TIMEOUT) ||
+                    !mbar_wait_bounded(&op_empty[s], ph ^ 1, abort_flag, p.err,
+                                       ERR_GEMM_TIMEOUT)) {
                     ok = false;
                     break;
                 }
-                uint8_t* st = stage_base + s * C::STAGE;
-                const uint8_t* w8 = st + C::W16 + SPLIT * C::XB;
+                uint8_t* st = main_ring + s * C::MAIN;
+                const uint8_t* w8 = w8_ring + s8 * C::W8;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const int item = tid + kConvThreads * i;  // 512 items: 128 rows x 4 chunks
@@ -311,11 +356,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     *reinterpret_cast<uint4*>(row + (((2 * ch + 1) ^ sw) << 4)) =
                         make_uint4(a2.x, a2.y, a3.x, a3.y);
                 }
+                // make this thread's generic-proxy stores visible to the tensor core,
+                // then one arrival per warp
                 fence_proxy_async_smem();
-                mbar_arrive(&conv_bar[s]);
-                if (++s == C::STAGES) {
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&conv_full[s]);
+                    mbar_arrive(&w8_empty[s8]);
+                }
+                if (++s == C::MS) {
                     s = 0;
                     ph ^= 1;
+                }
+                if (++s8 == C::S8) {
+                    s8 = 0;
+                    ph8 ^= 1;
                 }
             }
             if (!ok) break;
@@ -337,34 +392,40 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(b * BT);
 #pragma unroll 1
-            for (int c0 = 0; c0 < BT; c0 += 16) {
+            for (int c0 = 0; c0 < BT && c0 < ti.nrows; c0 += 16) {
+                // lanes 0..15 fetch the output row and row multiplier of the 16
+                // columns of this chunk; shuffles hand them to every lane
+                int my_orow = 0;
+                float my_rs = 1.0f;
+                const int64_t my_row = ti.row0 + c0 + (lane & 15);
+                if (lane < 16 && c0 + lane < ti.nrows) {
+                    my_orow = p.rowmap ? __ldg(p.rowmap + my_row) : static_cast<int>(my_row);
+                    if (p.rowscale) my_rs = __ldg(p.rowscale + my_row);
+                }
                 uint32_t r[16];
                 tc_ld_32x32b_x16(tbase + c0, r);
                 tc_wait_ld();
-                if (nvalid) {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int m = c0 + j;
-                        if (m < ti.nrows) {
-                            const int64_t row = ti.row0 + m;
-                            float v = __uint_as_float(r[j]) * sc;
-                            if (p.rowscale) v *= __ldg(p.rowscale + row);
-                            if (p.relu) v = fmaxf(v, 0.0f);
-                            const int64_t orow = p.rowmap ? __ldg(p.rowmap + row) : row;
-                            if (p.out_bf16) {
-                                reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + n] =
-                                    __float2bfloat16_rn(v);
-                            } else if (p.atomic_add) {
-                                atomicAdd(reinterpret_cast<float*>(p.out) + orow * p.ldo + n, v);
-                            } else {
-                                reinterpret_cast<float*>(p.out)[orow * p.ldo + n] = v;
-                            }
+                for (int j = 0; j < 16; ++j) {
+                    const int64_t orow = __shfl_sync(0xFFFFFFFFu, my_orow, j);
+                    const float rs = __shfl_sync(0xFFFFFFFFu, my_rs, j);
+                    if (nvalid && c0 + j < ti.nrows) {
+                        float v = __uint_as_float(r[j]) * sc * rs;
+                        if (p.relu) v = fmaxf(v, 0.0f);
+                        if (p.out_bf16) {
+                            reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + n] =
+                                __float2bfloat16_rn(v);
+                        } else if (p.atomic_add) {
+                            atomicAdd(reinterpret_cast<float*>(p.out) + orow * p.ldo + n, v);
+                        } else {
+                            reinterpret_cast<float*>(p.out)[orow * p.ldo + n] = v;
                         }
                     }
                 }
             }
             tc_fence_before();
-            mbar_arrive(&acce_bar[b]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acce_bar[b]);
         }
     }
 
