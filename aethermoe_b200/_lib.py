@@ -65,6 +65,8 @@ _SIGS = {
                                  ctypes.POINTER(_i64)]),
     "aem_qgemm": (_int, [_vp, _i64, _vp, _int, _i64, _vp, _vp]),
     "aem_qgemm_host": (_int, [_vp, _vp, _i64, _vp, _int, _i64, _vp]),
+    "aem_grouped_qgemm": (_int, [_vp, _vp, _int, _vp, _i64, _vp, _int, _i64, _int, _int, _vp, _vp,
+                                 _int, _int, _vp]),
     "aem_capacity_route_workspace": (ctypes.c_size_t, [_i64, _int]),
     "aem_capacity_route": (_int, [_vp, _vp, _vp, _i64, _int, _u64, _vp, _vp, ctypes.c_size_t,
                                   _vp]),

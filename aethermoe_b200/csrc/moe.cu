@@ -412,13 +412,19 @@ aem_status aem_qgemm(aem_qweight_t wh, int64_t group, const void* x, aem_dtype x
     if (M == 0) return AEM_OK;
     AEM_REQUIRE(x && out, "aem_qgemm: NULL buffer");
     auto s = static_cast<cudaStream_t>(stream);
-    // Activations as bf16 (hi, and lo for float32 input) in a stream-ordered buffer.
+    // float32 activations become a bf16 hi + lo pair in a stream-ordered
+    // buffer; bf16 activations are used in place.
     const size_t half = aem::align_up(static_cast<size_t>(M) * w->K * 2, 256);
     void* tmp = nullptr;
-    AEM_TRY_CUDA(cudaMallocAsync(&tmp, x_dtype == AEM_F32 ? 2 * half : half, s));
-    char* hi = static_cast<char*>(tmp);
-    char* lo = x_dtype == AEM_F32 ? hi + half : nullptr;
-    aem_status st = aem::launch_split_bf16(x, x_dtype, M * w->K, hi, lo, s);
+    const void* hi = x;
+    const void* lo = nullptr;
+    aem_status st = AEM_OK;
+    if (x_dtype == AEM_F32) {
+        AEM_TRY_CUDA(cudaMallocAsync(&tmp, 2 * half, s));
+        hi = tmp;
+        lo = static_cast<char*>(tmp) + half;
+        st = aem::launch_split_bf16(x, x_dtype, M * w->K, tmp, static_cast<char*>(tmp) + half, s);
+    }
     if (st == AEM_OK) {
         aem::GemmArgs a;
         a.w = w;
@@ -432,7 +438,7 @@ aem_status aem_qgemm(aem_qweight_t wh, int64_t group, const void* x, aem_dtype x
         // Split K when the channel tiles alone cannot fill the GPU.
         const int64_t tiles = (w->N + 127) / 128 * ((M + 255) / 256);
         const int sms = aem::sm_count(aem::current_device());
-        if (tiles < sms && w->K % 16 == 0) {
+        if (tiles < sms && w->K % 8 == 0) {
             const int64_t ks = std::min<int64_t>((2 * sms + tiles - 1) / tiles, (w->K + 63) / 64);
             if (ks > 1) {
                 if (cudaMemsetAsync(out, 0, sizeof(float) * M * w->N, s) != cudaSuccess) {
@@ -445,7 +451,7 @@ aem_status aem_qgemm(aem_qweight_t wh, int64_t group, const void* x, aem_dtype x
         }
         if (st == AEM_OK) st = aem::launch_qgemm(a, s);
     }
-    cudaFreeAsync(tmp, s);
+    if (tmp) cudaFreeAsync(tmp, s);
     return st;
 }
 
@@ -470,3 +476,41 @@ aem_status aem_qgemm_host(aem_context_t ctx, aem_qweight_t wh, int64_t group, co
 }
 
 }  // extern "C"
+
+extern "C" aem_status aem_grouped_qgemm(aem_qweight_t wh, const int32_t* group_rows, int G,
+                                        const void* x, int64_t M, void* out, aem_dtype out_dtype,
+                                        int64_t ldo, int relu, int accumulate,
+                                        const int32_t* rowmap, const float* rowscale,
+                                        int token_tile, int ksplit, void* stream) {
+    AEM_REQUIRE(wh != nullptr, "aem_grouped_qgemm: weight handle is NULL");
+    auto* w = reinterpret_cast<aem::QWeight*>(wh);
+    AEM_REQUIRE(G >= 1 && G <= 256 && G <= w->G, "aem_grouped_qgemm: G=%d outside [1, min(256, %lld)]",
+                G, (long long)w->G);
+    AEM_REQUIRE(M >= 0 && ldo >= w->N, "aem_grouped_qgemm: bad M or ldo");
+    AEM_REQUIRE(out_dtype == AEM_F32 || out_dtype == AEM_BF16, "aem_grouped_qgemm: bad out dtype");
+    AEM_REQUIRE(!accumulate || out_dtype == AEM_F32, "aem_grouped_qgemm: accumulate needs float32 out");
+    AEM_REQUIRE(ksplit <= 1 || accumulate, "aem_grouped_qgemm: ksplit > 1 needs accumulate");
+    AEM_REQUIRE(token_tile == 0 || token_tile == 16 || token_tile == 32 || token_tile == 64 ||
+                    token_tile == 128 || token_tile == 256,
+                "aem_grouped_qgemm: token_tile=%d not in {0,16,32,64,128,256}", token_tile);
+    AEM_REQUIRE(!(relu && accumulate), "aem_grouped_qgemm: ReLU of a partial sum is undefined");
+    if (M == 0) return AEM_OK;
+    AEM_REQUIRE(group_rows && x && out, "aem_grouped_qgemm: NULL buffer");
+    aem::GemmArgs a;
+    a.w = w;
+    a.G = G;
+    a.group_rows = group_rows;
+    a.M = M;
+    a.max_rows = M;
+    a.x_hi = x;
+    a.out = out;
+    a.out_bf16 = out_dtype == AEM_BF16;
+    a.ldo = ldo;
+    a.relu = relu != 0;
+    a.atomic_add = accumulate != 0;
+    a.ksplit = ksplit < 1 ? 1 : ksplit;
+    a.rowmap = rowmap;
+    a.rowscale = rowscale;
+    a.token_tile = token_tile;
+    return aem::launch_qgemm(a, static_cast<cudaStream_t>(stream));
+}

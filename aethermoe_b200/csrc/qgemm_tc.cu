@@ -9,20 +9,24 @@
 // activation rows (the MMA's N, 16..256), which keeps decode-size batches (a handful
 // of rows) on the tensor cores with the int8 weight stream as the only large read.
 //
-// Per CTA (one per SM, persistent over tiles), 11 warps:
-//   warp 8      int8 weight producer: TMA of [128 x 64 B] tiles (no swizzle) into a
-//               deep ring (6-8 stages) -- the HBM stream runs ahead of everything else.
-//   warp 10     activation producer: TMA of the bf16 [BT x 128 B] tile(s) (128-byte
-//               swizzle) into the operand ring.
-//   warps 0-3   converters: int8 -> bf16 (exact: |q| <= 127 fits bf16's 8-bit
-//               significand) written straight into the 128-byte-swizzled K-major layout
-//               the MMA reads, then fence.proxy.async and one mbarrier arrival per warp.
-//   warp 9      MMA issuer (one thread): 4 x tcgen05.mma kind::f16 (K=16 each) per
-//               64-wide stage, x2 for split float32 activations (hi + lo), accumulating
+// Per CTA (one per SM, persistent over tiles), 19 warps and three smem rings
+// (int8 weights, converted bf16 weights, activations), each with its own depth:
+//   warp 16     int8 weight producer: one contiguous 8 KB bulk copy per [128 x 64 B]
+//               tile of the pre-tiled weight layout -- the HBM stream.
+//   warp 18     activation producer: TMA of the bf16 [BT x 128 B] tile(s) (128-byte
+//               swizzle); its ring is deep where stages are small, because these
+//               loads queue behind the weight stream's bulk copies.
+//   warps 0-7   converters, in groups that take K steps round-robin: int8 -> bf16
+//               (exact: |q| <= 127 fits bf16's 8-bit significand) written straight
+//               into the 128-byte-swizzled K-major layout the MMA reads, then
+//               fence.proxy.async and one mbarrier arrival per warp.
+//   warp 17     MMA issuer (one thread): 4 x tcgen05.mma kind::f16 (K=16 each) per
+//               64-wide step, x2 for split float32 activations (hi + lo), accumulating
 //               float32 in a double-buffered TMEM accumulator; tcgen05.commit frees the
-//               operand stage and, at the end of a tile, hands the accumulator over.
-//   warps 4-7   epilogue: tcgen05.ld 32 lanes x 16 columns, per-channel scale, per-row
-//               output index and multiplier (fetched once per 16 columns, broadcast by
+//               operand slots and, at the end of a tile, hands the accumulator over.
+//   warps 8-15  epilogue, two warps per TMEM lane quarter splitting the columns:
+//               tcgen05.ld 32 lanes x 16 columns, per-channel scale, per-row output
+//               index and multiplier (fetched once per 16 columns, broadcast by
 //               shuffles), ReLU, bf16/f32 store or red.add (split-K / fused combine).
 // Every mbarrier wait is bounded (globaltimer); on timeout the kernel records an
 // error bit, all roles drain out, and TMEM is released.  No multicast is used.
@@ -43,10 +47,29 @@ using namespace aem::dev;
 
 constexpr int kCh = 128;      // output channels per tile = MMA M
 constexpr int kKT = 64;       // K per stage: one 128-byte bf16 row
-constexpr int kConvThreads = 128;
-constexpr int kConvWarps = 4;
-constexpr int kEpiWarps = 4;
-constexpr int kThreads = 352;  // 4 converter + 4 epilogue + 2 producer + MMA warps
+// Warp roles.  Converter warps come first; the epilogue warps start at a
+// warpgroup boundary so that warp (kEpiWarp0 + i) owns TMEM lanes
+// [32*(i%4), 32*(i%4)+32) -- two epilogue warps per lane quarter, each taking
+// half of the tile's columns.
+constexpr int kConvWarps = 8;
+constexpr int kConvThreads = kConvWarps * 32;
+// Converter warps form groups that take K steps round-robin, so several K
+// steps are in conversion at once (one group's convert -> proxy fence ->
+// arrive latency no longer serialises the stream of K steps).  The group
+// count must not exceed the converted-weight ring depth: a group handling K
+// step kc has finished kc - G, whose wait proved K step kc - G - D retired,
+// so with G <= D the slot's previous phase (kc - D) is at most one phase
+// ahead of the barrier and the parity wait cannot alias an older phase.
+#ifndef AEM_QGEMM_MAX_CONV_GROUPS
+#define AEM_QGEMM_MAX_CONV_GROUPS 4
+#endif
+constexpr int kEpiWarp0 = 8;
+constexpr int kEpiWarps = 8;
+constexpr int kW8Warp = 16;   // int8 weight producer
+constexpr int kMmaWarp = 17;  // MMA issuer + TMEM allocation
+constexpr int kXWarp = 18;    // activation producer
+constexpr int kThreads = 19 * 32;
+static_assert(kEpiWarp0 % 4 == 0, "epilogue warps must start at a warpgroup boundary");
 constexpr int kMaxGroups = 256;
 
 struct TcParams {
@@ -59,6 +82,8 @@ struct TcParams {
     int N;
     int ksplit;
     const float* scale;     // [Gw][N]
+    const int8_t* wq;       // tiled int8 weights [Gw][NT][KT][128][64]
+    int64_t NT, KT;
     void* out;
     int64_t ldo;
     int out_bf16;
@@ -74,18 +99,29 @@ struct Cfg {
     static constexpr int W8 = kCh * kKT;           // int8 weight tile, bytes
     static constexpr int W16 = kCh * kKT * 2;      // bf16 weight tile (MMA A)
     static constexpr int XB = BT * kKT * 2;        // bf16 activation tile (MMA B), per part
-    static constexpr int MAIN = W16 + SPLIT * XB;  // one stage of the MMA operand ring
-    // The int8 ring runs further ahead than the operand ring: its tiles come
-    // from HBM (the long latency), the activation tiles mostly from L2.
-    static constexpr int S8 = BT <= 128 ? 8 : 6;
-    static constexpr int MS_RAW = (208 * 1024 - S8 * W8) / MAIN;
-    static constexpr int MS = MS_RAW > 8 ? 8 : MS_RAW;
+    static constexpr int XS = SPLIT * XB;          // one activation stage
+    // Three rings with their own depths.  The activation ring must cover the
+    // latency of its loads, which queue behind the weight stream's bulk
+    // copies: it is deep where its stages are small (narrow, decode-size
+    // tiles).  The converted-weight ring holds the MMA's A operands.
+    static constexpr int DX = SPLIT == 1
+        ? (BT <= 16 ? 16 : (BT <= 32 ? 12 : (BT <= 64 ? 8 : (BT <= 128 ? 5 : 3))))
+        : (BT <= 16 ? 16 : (BT <= 32 ? 8 : (BT <= 64 ? 4 : 2)));
+    static constexpr int D16 = (BT >= 256 && SPLIT == 2) ? 3 : 4;
+    static constexpr int S8_RAW = (196 * 1024 - DX * XS - D16 * W16) / W8;
+    static constexpr int S8 = S8_RAW > 12 ? 12 : S8_RAW;
     static constexpr int TMEM_COLS = 2 * BT < 32 ? 32 : 2 * BT;
     static constexpr uint32_t IDESC = idesc_bf16_f32(kCh, BT);
-    static constexpr int BAR_BYTES = (3 * MS + 2 * S8 + 4) * 8 + 16;
+    static constexpr int BAR_BYTES = (2 * DX + 2 * D16 + 2 * S8 + 4) * 8 + 16;
     static constexpr int TAB_BYTES = 2 * (kMaxGroups + 1) * 4;
-    static constexpr int SMEM = 1024 + MS * MAIN + S8 * W8 + BAR_BYTES + TAB_BYTES;
-    static_assert(MS >= 2, "pipeline needs two operand stages");
+    static constexpr int SMEM = 1024 + D16 * W16 + DX * XS + S8 * W8 + BAR_BYTES + TAB_BYTES;
+    static constexpr int CG_RAW = D16 >= 4 ? 4 : (D16 >= 2 ? 2 : 1);
+    static constexpr int CG = CG_RAW < AEM_QGEMM_MAX_CONV_GROUPS ? CG_RAW : AEM_QGEMM_MAX_CONV_GROUPS;
+    static constexpr int CG_WARPS = kConvWarps / CG;        // warps per converter group
+    static constexpr int CG_THREADS = CG_WARPS * 32;
+    static constexpr int EPI_COLS = BT >= 32 ? BT / 2 : BT;  // columns per epilogue warp
+    static_assert(CG <= D16 && S8 >= CG && kConvWarps % CG == 0, "converter groups vs rings");
+    static_assert(S8 >= 2 && DX >= 2 && D16 >= 2, "pipeline needs two stages per ring");
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
     static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N for M=128");
 };
@@ -144,19 +180,20 @@ __device__ __forceinline__ uint2 i8x4_to_bf16x4(uint32_t v) {
 
 template <int BT, int SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
-    qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
-                    const __grid_constant__ CUtensorMap tm_xh,
+    qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_xh,
                     const __grid_constant__ CUtensorMap tm_xl, const TcParams p) {
     using C = Cfg<BT, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint8_t* main_ring = smem;                      // MS x [bf16 W | X hi | X lo]
-    uint8_t* w8_ring = smem + C::MS * C::MAIN;      // S8 x int8 W
+    uint8_t* w16_ring = smem;                          // D16 x bf16 W (MMA A, 128B swizzle)
+    uint8_t* x_ring = w16_ring + C::D16 * C::W16;      // DX x [X hi | X lo] (MMA B)
+    uint8_t* w8_ring = x_ring + C::DX * C::XS;         // S8 x int8 W
     uint64_t* x_full = reinterpret_cast<uint64_t*>(w8_ring + C::S8 * C::W8);
-    uint64_t* conv_full = x_full + C::MS;
-    uint64_t* op_empty = conv_full + C::MS;
-    uint64_t* w8_full = op_empty + C::MS;
+    uint64_t* x_empty = x_full + C::DX;
+    uint64_t* w16_full = x_empty + C::DX;
+    uint64_t* w16_empty = w16_full + C::D16;
+    uint64_t* w8_full = w16_empty + C::D16;
     uint64_t* w8_empty = w8_full + C::S8;
     uint64_t* accf_bar = w8_empty + C::S8;  // [2]
     uint64_t* acce_bar = accf_bar + 2;      // [2]
@@ -171,14 +208,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- setup: barriers, group table, TMEM
     if (tid == 0) {
-        for (int s = 0; s < C::MS; ++s) {
+        for (int s = 0; s < C::DX; ++s) {
             mbar_init(&x_full[s], 1);
-            mbar_init(&conv_full[s], kConvWarps);
-            mbar_init(&op_empty[s], 1);
+            mbar_init(&x_empty[s], 1);
+        }
+        for (int s = 0; s < C::D16; ++s) {
+            mbar_init(&w16_full[s], C::CG_WARPS);
+            mbar_init(&w16_empty[s], 1);
         }
         for (int s = 0; s < C::S8; ++s) {
             mbar_init(&w8_full[s], 1);
-            mbar_init(&w8_empty[s], kConvWarps);
+            mbar_init(&w8_empty[s], C::CG_WARPS);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&accf_bar[b], 1);
@@ -189,12 +229,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = tid; i <= p.G; i += kThreads)
         s_rows[i] = p.group_rows ? p.group_rows[i] : (i == 0 ? 0 : static_cast<int>(p.M));
-    if (warp == 9) {
+    if (warp == kMmaWarp) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
         tmem_relinquish();
     }
-    if (warp == 8 && lane == 0) {
-        tma_prefetch_desc(&tm_w);
+    if (warp == kXWarp && lane == 0) {
         tma_prefetch_desc(&tm_xh);
         if (SPLIT == 2) tma_prefetch_desc(&tm_xl);
     }
@@ -223,15 +262,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = *tmem_slot;
     const int total = s_tiles[p.G];
 
-    if (warp == 8) {
+    if (warp == kW8Warp) {
         // ================= int8 weight producer (HBM stream)
         if (lane == 0) {
             int s8 = 0;
             uint32_t ph8 = 0;
-            for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok && !*abort_flag; t += gridDim.x) {
                 const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
-                const int wrow = ti.wg * p.N + ti.n0;
-                bool ok = true;
+                // the tile's 8 KB blocks along K are consecutive in the tiled layout
+                const int8_t* wsrc =
+                    p.wq + ((static_cast<int64_t>(ti.wg) * p.NT + ti.n0 / kCh) * p.KT) * (kCh * kKT);
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
                     if (!mbar_wait_bounded(&w8_empty[s8], ph8 ^ 1, abort_flag, p.err,
                                            ERR_GEMM_TIMEOUT)) {
@@ -239,51 +280,50 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(&w8_full[s8], C::W8);
-                    tma_load_2d(w8_ring + s8 * C::W8, &tm_w, &w8_full[s8], kt * kKT, wrow);
+                    bulk_load(w8_ring + s8 * C::W8, wsrc + static_cast<int64_t>(kt) * C::W8, C::W8,
+                              &w8_full[s8]);
                     if (++s8 == C::S8) {
                         s8 = 0;
                         ph8 ^= 1;
                     }
                 }
-                if (!ok) break;
             }
         }
-    } else if (warp == 10) {
+    } else if (warp == kXWarp) {
         // ================= activation producer
         if (lane == 0) {
-            int s = 0;
-            uint32_t ph = 0;
-            for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+            int sx = 0;
+            uint32_t phx = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok && !*abort_flag; t += gridDim.x) {
                 const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
-                bool ok = true;
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                    if (!mbar_wait_bounded(&op_empty[s], ph ^ 1, abort_flag, p.err,
+                    if (!mbar_wait_bounded(&x_empty[sx], phx ^ 1, abort_flag, p.err,
                                            ERR_GEMM_TIMEOUT)) {
                         ok = false;
                         break;
                     }
-                    uint8_t* st = main_ring + s * C::MAIN;
-                    mbar_arrive_expect_tx(&x_full[s], SPLIT * C::XB);
-                    tma_load_2d(st + C::W16, &tm_xh, &x_full[s], kt * kKT,
-                                static_cast<int>(ti.row0));
+                    uint8_t* st = x_ring + sx * C::XS;
+                    mbar_arrive_expect_tx(&x_full[sx], C::XS);
+                    tma_load_2d(st, &tm_xh, &x_full[sx], kt * kKT, static_cast<int>(ti.row0));
                     if (SPLIT == 2)
-                        tma_load_2d(st + C::W16 + C::XB, &tm_xl, &x_full[s], kt * kKT,
+                        tma_load_2d(st + C::XB, &tm_xl, &x_full[sx], kt * kKT,
                                     static_cast<int>(ti.row0));
-                    if (++s == C::MS) {
-                        s = 0;
-                        ph ^= 1;
+                    if (++sx == C::DX) {
+                        sx = 0;
+                        phx ^= 1;
                     }
                 }
-                if (!ok) break;
             }
         }
-    } else if (warp == 9) {
+    } else if (warp == kMmaWarp) {
         // ================= MMA issuer
         if (lane == 0) {
-            int s = 0;
-            uint32_t ph = 0;
+            int sx = 0, s16 = 0;
+            uint32_t phx = 0, ph16 = 0;
             int it = 0;
-            for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++it) {
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok && !*abort_flag; t += gridDim.x, ++it) {
                 const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
                 const int b = it & 1;
                 const uint32_t aph = (it >> 1) & 1;
@@ -291,19 +331,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BT);
-                bool ok = true;
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                    if (!mbar_wait_bounded(&x_full[s], ph, abort_flag, p.err, ERR_GEMM_TIMEOUT) ||
-                        !mbar_wait_bounded(&conv_full[s], ph, abort_flag, p.err,
+                    if (!mbar_wait_bounded(&x_full[sx], phx, abort_flag, p.err, ERR_GEMM_TIMEOUT) ||
+                        !mbar_wait_bounded(&w16_full[s16], ph16, abort_flag, p.err,
                                            ERR_GEMM_TIMEOUT)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    uint8_t* st = main_ring + s * C::MAIN;
-                    const uint64_t adesc = smem_desc_sw128(smem_u32(st));
-                    const uint64_t bdesc = smem_desc_sw128(smem_u32(st + C::W16));
-                    const uint64_t ldesc = smem_desc_sw128(smem_u32(st + C::W16 + C::XB));
+                    const uint64_t adesc = smem_desc_sw128(smem_u32(w16_ring + s16 * C::W16));
+                    const uint64_t bdesc = smem_desc_sw128(smem_u32(x_ring + sx * C::XS));
+                    const uint64_t ldesc = smem_desc_sw128(smem_u32(x_ring + sx * C::XS + C::XB));
 #pragma unroll
                     for (int kk = 0; kk < kKT / 16; ++kk) {
                         // +32 bytes along K per UMMA_K=16 step (start address field, >>4)
@@ -312,36 +350,48 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (SPLIT == 2)
                             tc_mma_f16(d_tmem, adesc + 2 * kk, ldesc + 2 * kk, C::IDESC, 1u);
                     }
-                    tc_commit(&op_empty[s]);
-                    if (++s == C::MS) {
-                        s = 0;
-                        ph ^= 1;
+                    // both operand slots free once these MMAs retire
+                    tc_commit(&x_empty[sx]);
+                    tc_commit(&w16_empty[s16]);
+                    if (++sx == C::DX) {
+                        sx = 0;
+                        phx ^= 1;
+                    }
+                    if (++s16 == C::D16) {
+                        s16 = 0;
+                        ph16 ^= 1;
                     }
                 }
                 if (!ok) break;
                 tc_commit(&accf_bar[b]);
             }
         }
-    } else if (warp < 4) {
+    } else if (warp < kConvWarps) {
         // ================= converters: int8 [128 x 64B] -> bf16 SW128 [128 x 128B]
-        int s = 0, s8 = 0;
-        uint32_t ph = 0, ph8 = 0;
-        for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+        const int group = warp / C::CG_WARPS;
+        const int gtid = tid % C::CG_THREADS;
+        uint32_t kc = 0;  // K steps so far, in the order every role walks them
+        bool ok = true;
+        for (int t = blockIdx.x; t < total && ok && !*abort_flag; t += gridDim.x) {
             const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
-            bool ok = true;
-            for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                // int8 tile landed, and the operand slot is free (its last MMA retired)
+            for (int kt = ti.kt0; kt < ti.kt1; ++kt, ++kc) {
+                if (static_cast<int>(kc % C::CG) != group) continue;
+                const int s16 = static_cast<int>(kc % C::D16);
+                const uint32_t ph16 = (kc / C::D16) & 1;
+                const int s8 = static_cast<int>(kc % C::S8);
+                const uint32_t ph8 = (kc / C::S8) & 1;
+                // int8 tile landed, and the bf16 slot is free (its last MMA retired)
                 if (!mbar_wait_bounded(&w8_full[s8], ph8, abort_flag, p.err, ERR_GEMM_TIMEOUT) ||
-                    !mbar_wait_bounded(&op_empty[s], ph ^ 1, abort_flag, p.err,
+                    !mbar_wait_bounded(&w16_empty[s16], ph16 ^ 1, abort_flag, p.err,
                                        ERR_GEMM_TIMEOUT)) {
                     ok = false;
                     break;
                 }
-                uint8_t* st = main_ring + s * C::MAIN;
+                uint8_t* st = w16_ring + s16 * C::W16;
                 const uint8_t* w8 = w8_ring + s8 * C::W8;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int item = tid + kConvThreads * i;  // 512 items: 128 rows x 4 chunks
+                for (int i = 0; i < 512 / C::CG_THREADS; ++i) {
+                    const int item = gtid + C::CG_THREADS * i;  // 128 rows x 4 chunks
                     const int r = item >> 2;
                     const int ch = item & 3;
                     const uint4 v = *reinterpret_cast<const uint4*>(w8 + r * 64 + ch * 16);
@@ -361,23 +411,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(&conv_full[s]);
+                    mbar_arrive(&w16_full[s16]);
                     mbar_arrive(&w8_empty[s8]);
                 }
-                if (++s == C::MS) {
-                    s = 0;
-                    ph ^= 1;
-                }
-                if (++s8 == C::S8) {
-                    s8 = 0;
-                    ph8 ^= 1;
-                }
             }
-            if (!ok) break;
         }
-    } else {
-        // ================= epilogue (warps 4..7 own TMEM lanes 32*(warp%4) ..)
-        const int q = warp & 3;
+    } else if (warp < kEpiWarp0 + kEpiWarps) {
+        // ================= epilogue: warp kEpiWarp0+i owns TMEM lanes of quarter q = i%4
+        // and columns [h*EPI_COLS, (h+1)*EPI_COLS) with h = i/4
+        const int ei = warp - kEpiWarp0;
+        const int q = ei & 3;
+        const int h = ei >> 2;
         int it = 0;
         for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++it) {
             const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
@@ -391,8 +435,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 nvalid ? __ldg(p.scale + static_cast<int64_t>(ti.wg) * p.N + n) : 0.0f;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(b * BT);
+            const int cbeg = h * C::EPI_COLS;
+            const int cend = min(cbeg + C::EPI_COLS, ti.nrows);
 #pragma unroll 1
-            for (int c0 = 0; c0 < BT && c0 < ti.nrows; c0 += 16) {
+            for (int c0 = cbeg; c0 < cend; c0 += 16) {
                 // lanes 0..15 fetch the output row and row multiplier of the 16
                 // columns of this chunk; shuffles hand them to every lane
                 int my_orow = 0;
@@ -433,17 +479,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 9) tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if (warp == kMmaWarp) tmem_dealloc(tmem_base, C::TMEM_COLS);
 }
 
 template <int BT, int SPLIT>
 aem_status launch_tc(const GemmArgs& a, const TcParams& p, int grid, cudaStream_t s) {
     using C = Cfg<BT, SPLIT>;
     const QWeight& w = *a.w;
-    CUtensorMap tw, th, tl;
-    AEM_TRY(make_tmap_2d(&tw, w.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, static_cast<uint64_t>(w.K),
-                         static_cast<uint64_t>(w.G * w.N), kKT, kCh,
-                         CU_TENSOR_MAP_SWIZZLE_NONE));
+    CUtensorMap th, tl;
     AEM_TRY(make_tmap_2d(&th, a.x_hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                          static_cast<uint64_t>(w.K), static_cast<uint64_t>(a.M), kKT, BT,
                          CU_TENSOR_MAP_SWIZZLE_128B));
@@ -455,7 +498,7 @@ aem_status launch_tc(const GemmArgs& a, const TcParams& p, int grid, cudaStream_
         tl = th;
     auto kern = qgemm_tc_kernel<BT, SPLIT>;
     AEM_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    kern<<<grid, kThreads, C::SMEM, s>>>(tw, th, tl, p);
+    kern<<<grid, kThreads, C::SMEM, s>>>(th, tl, p);
     AEM_CHECK_LAUNCH();
     count_launches(1);
     return AEM_OK;
@@ -488,7 +531,7 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
                 "qgemm: weight group out of range");
     AEM_REQUIRE(!(a.atomic_add && a.out_bf16), "qgemm: split-K needs float32 output");
     if (a.M == 0) return AEM_OK;
-    if (w.K % 16 != 0) return launch_qgemm_simt(a, s);
+    if (w.K % 8 != 0) return launch_qgemm_simt(a, s);
     AEM_REQUIRE(a.M < (1ll << 31) && w.G * w.N < (1ll << 31), "qgemm: too many rows");
     const int dev = current_device();
     const int sms = sm_count(dev);
@@ -518,6 +561,9 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
     p.N = static_cast<int>(w.N);
     p.ksplit = ks;
     p.scale = w.scale;
+    p.wq = w.q;
+    p.NT = w.NT;
+    p.KT = w.KT;
     p.out = a.out;
     p.ldo = a.ldo;
     p.out_bf16 = a.out_bf16 ? 1 : 0;

@@ -1,7 +1,7 @@
 // INT8 weight-only quantisation (bit-exact with the reference's float32
 // NumPy), packing of INT8 expert weights into the output-channel-major
 // layout the GEMM streams, the float32 -> (bf16 hi, bf16 lo) activation
-// split, and the CUDA-core GEMM used when K is not a multiple of 16.
+// split, and the CUDA-core GEMM used when K is not a multiple of 8.
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -31,15 +31,15 @@ __global__ void quantize_kernel(const float* __restrict__ w, int64_t K, int64_t 
     }
 }
 
-// [G][K][N] -> [G][N][K] via 32x32 shared-memory tiles.
+// [G][K][N] (reference layout) -> the tiled layout of QWeight, via 32x32
+// shared-memory transposes (padding stays zero from the memset before).
 __global__ void transpose_i8_kernel(const int8_t* __restrict__ in, int64_t K, int64_t N,
-                                    int8_t* __restrict__ out) {
+                                    int64_t NT, int64_t KT, int8_t* __restrict__ out) {
     __shared__ int8_t tile[32][33];
     const int64_t g = blockIdx.z;
     const int64_t k0 = static_cast<int64_t>(blockIdx.y) * 32;
     const int64_t n0 = static_cast<int64_t>(blockIdx.x) * 32;
     const int8_t* src = in + g * K * N;
-    int8_t* dst = out + g * K * N;
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
         const int64_t k = k0 + i, n = n0 + threadIdx.x;
         if (k < K && n < N) tile[i][threadIdx.x] = src[k * N + n];
@@ -47,7 +47,7 @@ __global__ void transpose_i8_kernel(const int8_t* __restrict__ in, int64_t K, in
     __syncthreads();
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
         const int64_t n = n0 + i, k = k0 + threadIdx.x;
-        if (k < K && n < N) dst[n * K + k] = tile[threadIdx.x][i];
+        if (k < K && n < N) out[wtile_offset(g, n, k, NT, KT)] = tile[threadIdx.x][i];
     }
 }
 
@@ -63,14 +63,14 @@ __global__ void split_kernel(const float* __restrict__ x, int64_t count,
     }
 }
 
-// CUDA-core fallback, used only when K % 16 != 0 (the tensor-core path's TMA
-// needs 16-byte rows): one thread per output element, activations as the
+// CUDA-core fallback, used only when K % 8 != 0 (the tensor-core path's
+// activation TMA needs 16-byte rows): one thread per output element, activations as the
 // bf16 hi (+ lo) pair the tensor-core path consumes.
 // out[r, n] = scale[n] * sum_k (hi[r,k] + lo[r,k]) * q[n,k].
 __global__ void qgemm_simt_kernel(const __nv_bfloat16* __restrict__ xh,
                                   const __nv_bfloat16* __restrict__ xl,
                                   const int8_t* __restrict__ q, const float* __restrict__ scale,
-                                  int64_t M, int64_t K, int64_t N,
+                                  int64_t M, int64_t K, int64_t N, int64_t NT, int64_t KT,
                                   const int* __restrict__ group_rows, int G, int64_t group_base,
                                   int wmod,
                                   void* __restrict__ out, int64_t ldo, bool out_bf16, bool relu,
@@ -87,12 +87,11 @@ __global__ void qgemm_simt_kernel(const __nv_bfloat16* __restrict__ xh,
             while (g < G - 1 && r >= group_rows[g + 1]) ++g;
         }
         const int64_t wg = group_base + (wmod ? g % wmod : g);
-        const int8_t* qr = q + (wg * N + n) * K;
         float acc = 0.0f;
         for (int64_t k = 0; k < K; ++k) {
             float xv = __bfloat162float(xh[r * K + k]);
             if (xl) xv += __bfloat162float(xl[r * K + k]);
-            acc = fmaf(xv, static_cast<float>(qr[k]), acc);
+            acc = fmaf(xv, static_cast<float>(q[wtile_offset(wg, n, k, NT, KT)]), acc);
         }
         float v = acc * scale[wg * N + n];
         if (rowscale) v *= rowscale[r];
@@ -132,7 +131,7 @@ aem_status launch_qgemm_simt(const GemmArgs& a, cudaStream_t s) {
     const int64_t blocks = (total + 255) / 256 < 8192 ? (total + 255) / 256 : 8192;
     qgemm_simt_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
         static_cast<const __nv_bfloat16*>(a.x_hi), static_cast<const __nv_bfloat16*>(a.x_lo), w.q,
-        w.scale, a.M, w.K, w.N, a.group_rows, a.G, a.group_base, a.wmod, a.out, a.ldo, a.out_bf16, a.relu,
+        w.scale, a.M, w.K, w.N, w.NT, w.KT, a.group_rows, a.G, a.group_base, a.wmod, a.out, a.ldo, a.out_bf16, a.relu,
         a.atomic_add || a.ksplit > 1, a.rowmap, a.rowscale);
     AEM_CHECK_LAUNCH();
     count_launches(1);
@@ -141,11 +140,15 @@ aem_status launch_qgemm_simt(const GemmArgs& a, cudaStream_t s) {
 
 aem_status pack_qweight_device(const int8_t* q, const float* scale, int64_t G, int64_t K,
                                int64_t N, cudaStream_t s, QWeight* w) {
-    AEM_TRY_CUDA(cudaMallocAsync(&w->q, static_cast<size_t>(G * K * N), s));
+    w->NT = (N + kWTileN - 1) / kWTileN;
+    w->KT = (K + kWTileK - 1) / kWTileK;
+    const size_t bytes = static_cast<size_t>(G * w->NT * w->KT * kWTileBytes);
+    AEM_TRY_CUDA(cudaMallocAsync(&w->q, bytes, s));
     AEM_TRY_CUDA(cudaMallocAsync(&w->scale, sizeof(float) * G * N, s));
+    AEM_TRY_CUDA(cudaMemsetAsync(w->q, 0, bytes, s));
     dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((K + 31) / 32),
               static_cast<unsigned>(G));
-    transpose_i8_kernel<<<grid, dim3(32, 8), 0, s>>>(q, K, N, w->q);
+    transpose_i8_kernel<<<grid, dim3(32, 8), 0, s>>>(q, K, N, w->NT, w->KT, w->q);
     AEM_CHECK_LAUNCH();
     count_launches(1);
     AEM_TRY_CUDA(cudaMemcpyAsync(w->scale, scale, sizeof(float) * G * N, cudaMemcpyDeviceToDevice, s));

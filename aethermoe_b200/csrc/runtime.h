@@ -63,13 +63,23 @@ struct Gate {
 };
 int gate_epad(int64_t E);
 
-// Packed INT8 weight (device): [G][N][K] int8 + scale [G][N] float32.
+// Packed INT8 weight (device), pre-tiled for the GEMM's weight stream:
+// [G][NT][KT][128][64] int8 with NT = ceil(N/128), KT = ceil(K/64): every
+// 128-output-channel x 64-K tile is one contiguous 8 KB block (rows of 64
+// K-consecutive bytes), zero padded.  scale [G][N] float32.
+constexpr int64_t kWTileN = 128, kWTileK = 64, kWTileBytes = kWTileN * kWTileK;
 struct QWeight {
     int device = 0;
-    int64_t G = 0, K = 0, N = 0;
+    int64_t G = 0, K = 0, N = 0, NT = 0, KT = 0;
     int8_t* q = nullptr;
     float* scale = nullptr;
 };
+// Byte offset of element (g, n, k) in the tiled layout.
+__host__ __device__ inline int64_t wtile_offset(int64_t g, int64_t n, int64_t k, int64_t NT,
+                                                int64_t KT) {
+    return ((g * NT + n / kWTileN) * KT + k / kWTileK) * kWTileBytes + (n % kWTileN) * kWTileK +
+           (k % kWTileK);
+}
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 

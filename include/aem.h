@@ -12,7 +12,7 @@
  *   void*; NULL = the legacy default stream).  Packed weight handles are
  *   immutable after creation and may be shared between threads and streams.
  *
- * Layout conventions follow the reference Python API (src/kernels/*.py):
+ * Layout conventions follow the reference Python API (the src/kernels modules):
  *   hidden [N, D] row-major, gate_weight [D, E], gate_bias [E],
  *   q_int8 [D, E] (= [K, N]) with per-output-column scale [1, E].
  */
@@ -144,10 +144,11 @@ typedef struct aem_qweight_s* aem_qweight_t;
 
 /* Packs G groups (experts) of INT8 weights from HOST memory:
  * q [G][K][N] int8 (reference layout) and scale [G][N] float32 become a
- * device-resident output-channel-major [G][N][K] copy.
+ * device-resident copy tiled for the GEMM's weight stream (every block of
+ * 128 output channels x 64 K is one contiguous 8 KB tile).
  * Replaces _get_transposed_qweight, src/kernels/quantized_gemm.py:151-167.
- * Constraint for the tensor-core path: K % 16 == 0 (other K use a CUDA-core
- * kernel). */
+ * The tensor-core path needs K % 8 == 0 (16-byte activation rows); other K
+ * use a CUDA-core kernel. */
 aem_status aem_qweight_pack(const int8_t* q, const float* scale, int64_t G, int64_t K, int64_t N,
                             int device, aem_qweight_t* out);
 /* Same from DEVICE memory (q [G][K][N], scale [G][N]); stream-ordered. */
@@ -165,6 +166,20 @@ aem_status aem_qweight_shape(aem_qweight_t w, int64_t* G, int64_t* K, int64_t* N
  * (MSL body :99-138).  D mismatch -> AEM_EINVAL as the reference (:202-205). */
 aem_status aem_qgemm(aem_qweight_t w, int64_t group, const void* x, aem_dtype x_dtype, int64_t M,
                      float* out, void* stream);
+/* Grouped form (the per-expert GEMM of an MoE layer): activation rows
+ * [group_rows[g], group_rows[g+1]) (device int32 array of G+1 offsets) are
+ * multiplied by weight group g of `w` (G <= 256, G <= groups of w):
+ *   out[rowmap ? rowmap[r] : r][n] (=|+=) act(rowscale[r] * scale[g][n] * sum_k x[r,k] q[g][n,k])
+ * x bf16 [M, K] (device); out float32 or bf16 with row stride ldo; act = ReLU
+ * when relu != 0; accumulate != 0 adds with float32 red.add (out must be
+ * float32; rows may repeat); rowmap/rowscale may be NULL.  token_tile is
+ * the rows per tile (16, 32, 64, 128, 256; 0 = chosen from M/G) and ksplit
+ * splits K across CTAs (needs accumulate).  No counterpart call in the
+ * reference: its kernels take one weight matrix per call. */
+aem_status aem_grouped_qgemm(aem_qweight_t w, const int32_t* group_rows, int G, const void* x,
+                             int64_t M, void* out, aem_dtype out_dtype, int64_t ldo, int relu,
+                             int accumulate, const int32_t* rowmap, const float* rowscale,
+                             int token_tile, int ksplit, void* stream);
 /* HOST-buffer form of aem_qgemm (synchronous). */
 aem_status aem_qgemm_host(aem_context_t ctx, aem_qweight_t w, int64_t group, const void* x,
                           aem_dtype x_dtype, int64_t M, float* out);
