@@ -77,6 +77,7 @@ _SIGS = {
     "aem_moe_last_routing": (_int, [_vp, _vp, _vp, _vp, _vp]),
     "aem_ep_plan_bases": (_int, [_vp, _int, _int, _int, _int, _vp]),
     "aem_ep_unique_id": (_int, [_vp]),
+    "aem_ep_plan_exchange": (_int, [_vp, _int, _int, _int, _vp, _vp, _vp, _vp, _vp]),
     "aem_ep_create": (_int, [ctypes.POINTER(MoeConfig), _int, _int, _vp, _vp, _vp, _vp,
                              ctypes.POINTER(_vp)]),
     "aem_ep_free": (_int, [_vp]),

@@ -79,7 +79,7 @@ def build(verbose=False, force=False, ptxas_info=False):
             for o in ex.map(lambda c: _run(c, verbose), jobs):
                 out.append(o)
     if force or jobs or _stale(LIB, objs):
-        _run([nvcc] + ARCH + ["-shared", "-o", LIB] + objs + ["-lnccl", "-lpthread"], verbose)
+        _run([nvcc] + ARCH + ["-shared", "-o", LIB] + objs + ["-ldl", "-lpthread"], verbose)
     if ptxas_info:
         print("\n".join(out))
     return LIB

@@ -16,9 +16,11 @@
 // grouped GEMMs on the received (source, expert) segments -> send/recv of the
 // float32 expert outputs back -> weighted combine in token order.
 #include <cuda_bf16.h>
+#include <dlfcn.h>
 #include <nccl.h>
 
 #include <algorithm>
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -26,13 +28,79 @@
 #include "route.h"
 #include "runtime.h"
 
+namespace aem {
+
+// NCCL is resolved at run time, on the first expert-parallel call, not at
+// link time: a process that already loaded an NCCL (e.g. the one PyTorch
+// ships) keeps using that one, so loading this library never changes which
+// NCCL other components of the process see.
+struct NcclApi {
+    decltype(&::ncclGetUniqueId) GetUniqueId = nullptr;
+    decltype(&::ncclCommInitRank) CommInitRank = nullptr;
+    decltype(&::ncclCommDestroy) CommDestroy = nullptr;
+    decltype(&::ncclAllGather) AllGather = nullptr;
+    decltype(&::ncclGroupStart) GroupStart = nullptr;
+    decltype(&::ncclGroupEnd) GroupEnd = nullptr;
+    decltype(&::ncclSend) Send = nullptr;
+    decltype(&::ncclRecv) Recv = nullptr;
+    decltype(&::ncclGetErrorString) GetErrorString = nullptr;
+};
+
+static std::once_flag g_nccl_once;
+static NcclApi g_nccl;
+static bool g_nccl_ok = false;
+static std::string g_nccl_err;
+
+static const NcclApi* nccl() {
+    std::call_once(g_nccl_once, [] {
+        // an NCCL already in the process wins; otherwise the loader's default
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) {
+            const char* e = dlerror();
+            g_nccl_err = e ? e : "libnccl.so.2 not found";
+            return;
+        }
+        bool ok = true;
+        auto sym = [&](auto& fp, const char* name) {
+            fp = reinterpret_cast<std::remove_reference_t<decltype(fp)>>(dlsym(h, name));
+            if (!fp) {
+                ok = false;
+                g_nccl_err = std::string("NCCL symbol missing: ") + name;
+            }
+        };
+        sym(g_nccl.GetUniqueId, "ncclGetUniqueId");
+        sym(g_nccl.CommInitRank, "ncclCommInitRank");
+        sym(g_nccl.CommDestroy, "ncclCommDestroy");
+        sym(g_nccl.AllGather, "ncclAllGather");
+        sym(g_nccl.GroupStart, "ncclGroupStart");
+        sym(g_nccl.GroupEnd, "ncclGroupEnd");
+        sym(g_nccl.Send, "ncclSend");
+        sym(g_nccl.Recv, "ncclRecv");
+        sym(g_nccl.GetErrorString, "ncclGetErrorString");
+        g_nccl_ok = ok;
+    });
+    return g_nccl_ok ? &g_nccl : nullptr;
+}
+
+}  // namespace aem
+
 #define AEM_TRY_NCCL(expr)                                                              \
     do {                                                                                \
         ncclResult_t aem_n_ = (expr);                                                   \
         if (aem_n_ != ncclSuccess) {                                                    \
             ::aem::set_error("%s:%d: %s failed: %s", __FILE__, __LINE__, #expr,         \
-                             ncclGetErrorString(aem_n_));                               \
+                             ::aem::nccl()->GetErrorString(aem_n_));                    \
             return AEM_ENCCL;                                                           \
+        }                                                                               \
+    } while (0)
+
+#define AEM_NCCL_OR_FAIL()                                                              \
+    do {                                                                                \
+        if (!::aem::nccl()) {                                                           \
+            ::aem::set_error("NCCL unavailable: %s", ::aem::g_nccl_err.c_str());        \
+            return AEM_EUNSUPPORTED;                                                    \
         }                                                                               \
     } while (0)
 
@@ -200,7 +268,7 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
         count_launches(1);
     }
     // 2. all-gather counts -> global rank offsets
-    AEM_TRY_NCCL(ncclAllGather(cnt, cnt_all, static_cast<size_t>(k) * E, ncclInt64, comm, s));
+    AEM_TRY_NCCL(::aem::nccl()->AllGather(cnt, cnt_all, static_cast<size_t>(k) * E, ncclInt64, comm, s));
     ep_corr_kernel<<<1, 256, 0, s>>>(cnt_all, R, k, E, rank, corr);
     AEM_CHECK_LAUNCH();
     count_launches(1);
@@ -231,41 +299,29 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
     }
     prof.end(AEM_PHASE_ROUTE, s);
     // 4. all-gather per-expert starts; sizes to the host (the one sync)
-    AEM_TRY_NCCL(ncclAllGather(loc.starts, starts_all, static_cast<size_t>(E + 1), ncclInt32, comm, s));
+    AEM_TRY_NCCL(::aem::nccl()->AllGather(loc.starts, starts_all, static_cast<size_t>(E + 1), ncclInt32, comm, s));
     AEM_TRY_CUDA(cudaMemcpyAsync(h_starts, starts_all, sizeof(int) * R * (E + 1),
                                  cudaMemcpyDeviceToHost, s));
     AEM_TRY_CUDA(cudaStreamSynchronize(s));
-    const int* my = h_starts + static_cast<int64_t>(rank) * (E + 1);
     std::vector<int64_t> send_off(R), send_cnt(R), recv_off(R), recv_cnt(R);
-    int64_t rtot = 0;
-    h_groups[0] = 0;
-    for (int p = 0; p < R; ++p) {
-        send_off[p] = my[p * e_loc];
-        send_cnt[p] = my[(p + 1) * e_loc] - my[p * e_loc];
-        const int* ps = h_starts + static_cast<int64_t>(p) * (E + 1);
-        recv_off[p] = rtot;
-        for (int e = 0; e < e_loc; ++e) {
-            const int c = ps[rank * e_loc + e + 1] - ps[rank * e_loc + e];
-            rtot += c;
-            h_groups[p * e_loc + e + 1] = static_cast<int>(rtot);
-        }
-        recv_cnt[p] = rtot - recv_off[p];
-    }
+    AEM_TRY(aem_ep_plan_exchange(h_starts, R, E, rank, send_off.data(), send_cnt.data(),
+                                 recv_off.data(), recv_cnt.data(), h_groups));
+    const int64_t rtot = recv_off[R - 1] + recv_cnt[R - 1];
     AEM_TRY(reserve_recv(std::max<int64_t>(rtot, 1)));
     AEM_TRY_CUDA(cudaMemcpyAsync(d_groups, h_groups, sizeof(int) * (R * e_loc + 1),
                                  cudaMemcpyHostToDevice, s));
     // 5. dispatch: bf16 rows, grouped by destination rank, to the expert owners
     prof.begin(AEM_PHASE_DISPATCH, s);
-    AEM_TRY_NCCL(ncclGroupStart());
+    AEM_TRY_NCCL(::aem::nccl()->GroupStart());
     for (int p = 0; p < R; ++p) {
         if (send_cnt[p] > 0)
-            AEM_TRY_NCCL(ncclSend(static_cast<char*>(loc.xperm) + 2 * send_off[p] * d,
+            AEM_TRY_NCCL(::aem::nccl()->Send(static_cast<char*>(loc.xperm) + 2 * send_off[p] * d,
                                   send_cnt[p] * d, ncclBfloat16, p, comm, s));
         if (recv_cnt[p] > 0)
-            AEM_TRY_NCCL(ncclRecv(static_cast<char*>(xr) + 2 * recv_off[p] * d, recv_cnt[p] * d,
+            AEM_TRY_NCCL(::aem::nccl()->Recv(static_cast<char*>(xr) + 2 * recv_off[p] * d, recv_cnt[p] * d,
                                   ncclBfloat16, p, comm, s));
     }
-    AEM_TRY_NCCL(ncclGroupEnd());
+    AEM_TRY_NCCL(::aem::nccl()->GroupEnd());
     prof.end(AEM_PHASE_DISPATCH, s);
     // 6. local expert FFN on the (source, expert) segments
     if (rtot > 0) {
@@ -300,14 +356,14 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
     }
     // 7. expert outputs back to the token owners (same segments, reversed)
     prof.begin(AEM_PHASE_RETURN, s);
-    AEM_TRY_NCCL(ncclGroupStart());
+    AEM_TRY_NCCL(::aem::nccl()->GroupStart());
     for (int p = 0; p < R; ++p) {
         if (recv_cnt[p] > 0)
-            AEM_TRY_NCCL(ncclSend(yr + recv_off[p] * d, recv_cnt[p] * d, ncclFloat32, p, comm, s));
+            AEM_TRY_NCCL(::aem::nccl()->Send(yr + recv_off[p] * d, recv_cnt[p] * d, ncclFloat32, p, comm, s));
         if (send_cnt[p] > 0)
-            AEM_TRY_NCCL(ncclRecv(yb + send_off[p] * d, send_cnt[p] * d, ncclFloat32, p, comm, s));
+            AEM_TRY_NCCL(::aem::nccl()->Recv(yb + send_off[p] * d, send_cnt[p] * d, ncclFloat32, p, comm, s));
     }
-    AEM_TRY_NCCL(ncclGroupEnd());
+    AEM_TRY_NCCL(::aem::nccl()->GroupEnd());
     prof.end(AEM_PHASE_RETURN, s);
     // 8. weighted combine in token order
     prof.begin(AEM_PHASE_COMBINE, s);
@@ -354,11 +410,39 @@ aem_status aem_ep_plan_bases(const int64_t* counts, int R, int k, int E, int ran
     return AEM_OK;
 }
 
+aem_status aem_ep_plan_exchange(const int32_t* starts, int R, int E, int rank, int64_t* send_off,
+                                int64_t* send_cnt, int64_t* recv_off, int64_t* recv_cnt,
+                                int32_t* groups) {
+    AEM_REQUIRE(starts && send_off && send_cnt && recv_off && recv_cnt && groups,
+                "aem_ep_plan_exchange: NULL buffer");
+    AEM_REQUIRE(R >= 1 && E >= R && E % R == 0 && rank >= 0 && rank < R,
+                "aem_ep_plan_exchange: bad R=%d E=%d rank=%d", R, E, rank);
+    const int e_loc = E / R;
+    const int32_t* my = starts + static_cast<int64_t>(rank) * (E + 1);
+    int64_t rtot = 0;
+    groups[0] = 0;
+    for (int p = 0; p < R; ++p) {
+        send_off[p] = my[p * e_loc];
+        send_cnt[p] = my[(p + 1) * e_loc] - my[p * e_loc];
+        const int32_t* ps = starts + static_cast<int64_t>(p) * (E + 1);
+        recv_off[p] = rtot;
+        for (int e = 0; e < e_loc; ++e) {
+            const int64_t c = ps[rank * e_loc + e + 1] - ps[rank * e_loc + e];
+            AEM_REQUIRE(c >= 0, "aem_ep_plan_exchange: rank %d's expert starts decrease", p);
+            rtot += c;
+            groups[p * e_loc + e + 1] = static_cast<int32_t>(rtot);
+        }
+        recv_cnt[p] = rtot - recv_off[p];
+    }
+    return AEM_OK;
+}
+
 aem_status aem_ep_unique_id(uint8_t out[128]) {
     AEM_REQUIRE(out != nullptr, "aem_ep_unique_id: out is NULL");
     static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId size");
+    AEM_NCCL_OR_FAIL();
     ncclUniqueId id;
-    AEM_TRY_NCCL(ncclGetUniqueId(&id));
+    AEM_TRY_NCCL(::aem::nccl()->GetUniqueId(&id));
     memcpy(out, &id, 128);
     return AEM_OK;
 }
@@ -385,6 +469,7 @@ aem_status aem_ep_create(const aem_moe_config* cfg, int rank, int world, const u
                 (long long)cfg->d_model, (long long)cfg->d_ffn);
     AEM_REQUIRE(dn->G == e_loc && dn->K == cfg->d_ffn && dn->N == cfg->d_model,
                 "aem_ep_create: down weight shape");
+    AEM_NCCL_OR_FAIL();
     auto* ep = new aem::Ep();
     ep->cfg = *cfg;
     ep->rank = rank;
@@ -401,15 +486,15 @@ aem_status aem_ep_create(const aem_moe_config* cfg, int rank, int world, const u
     cudaSetDevice(g->device);
     ncclUniqueId id;
     memcpy(&id, uid, 128);
-    ncclResult_t r = ncclCommInitRank(&ep->comm, world, id, rank);
+    ncclResult_t r = ::aem::nccl()->CommInitRank(&ep->comm, world, id, rank);
     if (r != ncclSuccess) {
-        set_error("aem_ep_create: ncclCommInitRank failed: %s", ncclGetErrorString(r));
+        set_error("aem_ep_create: ncclCommInitRank failed: %s", ::aem::nccl()->GetErrorString(r));
         delete ep;
         return AEM_ENCCL;
     }
     aem_status st = ep->init_buffers();
     if (st != AEM_OK) {
-        ncclCommDestroy(ep->comm);
+        ::aem::nccl()->CommDestroy(ep->comm);
         delete ep;
         return st;
     }
@@ -422,7 +507,7 @@ aem_status aem_ep_free(aem_ep_t h) {
     auto* ep = reinterpret_cast<aem::Ep*>(h);
     cudaSetDevice(ep->device);
     cudaDeviceSynchronize();
-    if (ep->comm) ncclCommDestroy(ep->comm);
+    if (ep->comm && aem::nccl()) aem::nccl()->CommDestroy(ep->comm);
     cudaFree(ep->cnt);
     cudaFree(ep->cnt_all);
     cudaFree(ep->corr);

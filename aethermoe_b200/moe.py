@@ -153,6 +153,20 @@ def ep_plan_bases(counts, rank):
     return base
 
 
+def ep_plan_exchange(starts, rank):
+    """Host planning of one exchange: ``starts [R, E+1]`` (every rank's expert
+    starts) -> ``(send_off, send_cnt, recv_off, recv_cnt, groups)`` for ``rank``."""
+    st = np.ascontiguousarray(starts, dtype=np.int32)
+    r, e1 = st.shape
+    e = e1 - 1
+    so, sc, ro, rc = (np.zeros(r, np.int64) for _ in range(4))
+    groups = np.zeros(e + 1, np.int32)
+    _lib.check(_lib.lib().aem_ep_plan_exchange(st.ctypes.data, r, e, rank, so.ctypes.data,
+                                               sc.ctypes.data, ro.ctypes.data, rc.ctypes.data,
+                                               groups.ctypes.data), "aem_ep_plan_exchange")
+    return so, sc, ro, rc, groups
+
+
 class EPLayer:
     """One rank of the expert-parallel MoE layer (experts split contiguously over ranks)."""
 

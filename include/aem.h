@@ -277,6 +277,18 @@ aem_status aem_moe_last_routing(aem_moe_t moe, int32_t* idx, float* val, uint32_
  * batch_position and tokens split contiguously over ranks. */
 aem_status aem_ep_plan_bases(const int64_t* counts, int R, int k, int E, int rank, int64_t* base);
 
+/* Host-side planning of one expert-parallel exchange (no GPU needed).
+ * starts: [R][E+1] every rank's first expert-grouped row per expert (the
+ * all-gathered output of the routing step).  For `rank`, writes the
+ * contiguous send segment to each peer p (send_off/send_cnt[p], rows of its
+ * expert-grouped buffer holding experts p*E/R .. (p+1)*E/R-1), the receive
+ * segment from each peer (recv_off/recv_cnt[p], peers in rank order), and
+ * groups [R*E/R + 1]: row offsets of the received (peer, local expert)
+ * segments -- the grouped GEMM's row groups. */
+aem_status aem_ep_plan_exchange(const int32_t* starts, int R, int E, int rank, int64_t* send_off,
+                                int64_t* send_cnt, int64_t* recv_off, int64_t* recv_cnt,
+                                int32_t* groups);
+
 /* NCCL unique id (128 bytes) for aem_ep_create; made on one rank and
  * broadcast by the caller. */
 aem_status aem_ep_unique_id(uint8_t out[128]);

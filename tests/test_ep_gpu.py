@@ -1,0 +1,107 @@
+"""Expert-parallel MoE layer over NCCL on 2+ GPUs vs the single-process oracle.
+
+One process per GPU (spawned here), experts split contiguously, tokens split
+contiguously.  The routing of every (token, slot) unit must equal the
+capacity rule applied to the GLOBAL batch (bit-exact, the contract of
+Router::assign_effective_experts in src/orchestration/router.hpp:249-266),
+and every output row must match the float64 layer oracle within the layer
+tolerance ``1e-3 + 1e-3 * |ref|``.  Skipped on hosts with fewer than 2 GPUs.
+"""
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+
+import aem_oracle as O
+import native
+
+pytestmark = pytest.mark.gpu
+
+CFG = dict(T=2048, d=256, f=384, E=16, k=4)
+
+
+def _weights(seed, e, d, f):
+    rng = np.random.default_rng(seed)
+    qu = rng.integers(-127, 128, size=(e, d, f), dtype=np.int8)
+    su = (rng.random(size=(e, 1, f)) * 1e-4 + 2e-4).astype(np.float32)
+    qd = rng.integers(-127, 128, size=(e, f, d), dtype=np.int8)
+    sd = (rng.random(size=(e, 1, d)) * 1e-4 + 2e-4).astype(np.float32)
+    gw = (rng.normal(size=(d, e)) / np.sqrt(d)).astype(np.float32)
+    gb = O.zipf_bias(e)
+    x = O.bf16_round(rng.normal(size=(CFG["T"], d)).astype(np.float32))
+    return gw, gb, qu, su, qd, sd, x
+
+
+def _worker(rank, world, port, outdir):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from aethermoe_b200.moe import EPLayer, ep_unique_id
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    T, d, f, E, k = CFG["T"], CFG["d"], CFG["f"], CFG["E"], CFG["k"]
+    cap = O.default_capacity(T, k, E)
+    gw, gb, qu, su, qd, sd, x = _weights(7, E, d, f)
+    el = E // world
+    uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+    if rank == 0:
+        uid.copy_(torch.frombuffer(bytearray(ep_unique_id()), dtype=torch.uint8))
+    dist.broadcast(uid, 0)
+    lo, hi = rank * el, (rank + 1) * el
+    layer = EPLayer(bytes(uid.cpu().numpy()), rank, world, gw, gb, qu[lo:hi], su[lo:hi],
+                    qd[lo:hi], sd[lo:hi], k, capacity=cap, device=rank)
+    tl = T // world
+    bits = (x[rank * tl:(rank + 1) * tl].view(np.uint32) >> 16).astype(np.uint16)
+    xt = torch.from_numpy(bits.view(np.int16)).to(dev).view(torch.bfloat16)
+    outs = []
+    for _ in range(2):  # two steps: the second reuses the grown buffers
+        outs.append(layer.forward(xt, out_dtype=torch.float32))
+    idx, val, eff = layer.last_routing(tl)
+    torch.cuda.synchronize()
+    np.savez(os.path.join(outdir, f"rank{rank}.npz"), out=outs[-1].cpu().numpy(),
+             out0=outs[0].cpu().numpy(), idx=idx.cpu().numpy(), val=val.cpu().numpy(),
+             eff=eff.cpu().numpy())
+    layer.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_expert_parallel_matches_global_oracle(cuda, world):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    T, d, f, E, k = CFG["T"], CFG["d"], CFG["f"], CFG["E"], CFG["k"]
+    with tempfile.TemporaryDirectory() as outdir:
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        mp.start_processes(_worker, args=(world, _free_port(), outdir), nprocs=world,
+                           join=True, start_method="spawn")
+        res = [np.load(os.path.join(outdir, f"rank{r}.npz")) for r in range(world)]
+    tl = T // world
+    gw, gb, qu, su, qd, sd, x = _weights(7, E, d, f)
+    cap = O.default_capacity(T, k, E)
+    oidx, oval = O.fused_gating(x, gw, gb, k, extra=1)
+    idx = np.concatenate([r["idx"] for r in res])
+    np.testing.assert_array_equal(idx, oidx)
+    # local slot-major units -> global slot-major order u = j*T + r*tl + t
+    eff = np.concatenate([r["eff"].reshape(k, tl) for r in res], axis=1).reshape(-1)
+    oeff = native.moe_route(oidx, k, E, cap)
+    np.testing.assert_array_equal(eff, oeff)
+    assert (oeff != O.moe_units(oidx, k, E)[0]).any()  # capacity reroutes happened
+    out = np.concatenate([r["out"] for r in res])
+    ref = O.moe_layer_rows(np.arange(T), x, oidx, oval, oeff, k, qu, su, qd, sd)
+    err = np.abs(out.astype(np.float64) - ref)
+    assert np.all(err <= 1e-3 + 1e-3 * np.abs(ref)), err.max()
+    np.testing.assert_allclose(np.concatenate([r["out0"] for r in res]), out, rtol=0, atol=1e-5)
