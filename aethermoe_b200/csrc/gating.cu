@@ -5,7 +5,8 @@
 // specification fused_kernel_simulation (prototype/math_proto.py:19-50).
 //
 // Design (B200): lanes own experts, not slices of d.  A warp is split into
-// lane groups of GROUP lanes (8, 16 or 32); a group owns TPG tokens and lane
+// lane groups of GROUP lanes (8, 16 or 32); a group owns kTPG tokens (4, or 8
+// for many tokens) and lane
 // `le` of the group owns experts le, le+GROUP, ...  Every (token, expert)
 // logit is therefore one sequential dot product inside one thread -- no
 // cross-lane reduction -- which makes the EXACT mode possible: float32
@@ -29,7 +30,6 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kTPG = 4;  // tokens per lane group
 
 template <typename XT>
 __device__ __forceinline__ float load_x(const XT* p);
@@ -59,7 +59,7 @@ __device__ __forceinline__ float4 load_x4<__nv_bfloat16>(const __nv_bfloat16* p)
     return f;
 }
 
-template <int GROUP, int NSLOT, typename XT, bool EXACT>
+template <int GROUP, int NSLOT, int kTPG, typename XT, bool EXACT>
 __global__ void __launch_bounds__(kThreads)
     gating_kernel(const XT* __restrict__ x, const float4* __restrict__ wpk,
                   const float* __restrict__ bias, int64_t N, int D, int E, int k, int ksel,
@@ -67,15 +67,13 @@ __global__ void __launch_bounds__(kThreads)
     constexpr int GPW = 32 / GROUP;
     constexpr int TOK = kWarps * GPW * kTPG;  // tokens per CTA
     constexpr int EPAD = GROUP * NSLOT;
-    constexpr int DK = EPAD <= 64 ? 64 : (EPAD <= 128 ? 32 : 16);
+    constexpr int DK_E = EPAD <= 64 ? 64 : (EPAD <= 128 ? 32 : 16);
+    constexpr int DK = (TOK * (DK_E + 4) * 4 > 36 * 1024) ? DK_E / 2 : DK_E;
     constexpr int DK4 = DK / 4;
     constexpr int XS = DK + 4;                // padded row of the activation chunk
-    constexpr int KS = EPAD < 65 ? EPAD : 65;  // stored selections per token
 
     __shared__ float4 ws[DK4 * EPAD];
     __shared__ __align__(16) float xs[TOK * XS];
-    __shared__ float tv[TOK * KS];
-    __shared__ int te[TOK * KS];
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -93,33 +91,61 @@ __global__ void __launch_bounds__(kThreads)
 
     const bool vec_ok = (D & 3) == 0;
     const int nchunks = (D + DK - 1) / DK;
-    for (int c = 0; c < nchunks; ++c) {
+    // The next chunk's weights and activations are loaded into registers while
+    // the current chunk is multiplied out of shared memory.
+    constexpr int PW = (DK4 * EPAD + kThreads - 1) / kThreads;
+    constexpr int PX = (TOK * DK4 + kThreads - 1) / kThreads;
+    float4 pw[PW], px[PX];
+    auto fetch = [&](int c) {
         const int d0 = c * DK;
-        // weight chunk: contiguous DK4*EPAD float4 in the packed layout
         const float4* wsrc = wpk + static_cast<int64_t>(c) * DK4 * EPAD;
-        for (int i = tid; i < DK4 * EPAD; i += kThreads) ws[i] = __ldg(wsrc + i);
-        // activation chunk (zero beyond D and beyond N)
-        for (int i = tid; i < TOK * DK4; i += kThreads) {
-            const int t = i / DK4;
-            const int q = i % DK4;
-            const int64_t tg = tok0 + t;
-            const int d = d0 + 4 * q;
+#pragma unroll
+        for (int j = 0; j < PW; ++j) {
+            const int i = tid + j * kThreads;
+            if (i < DK4 * EPAD) pw[j] = __ldg(wsrc + i);
+        }
+#pragma unroll
+        for (int j = 0; j < PX; ++j) {
+            const int i = tid + j * kThreads;
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (tg < N) {
-                const XT* row = x + tg * static_cast<int64_t>(D);
-                if (vec_ok) {
-                    if (d < D) v = load_x4<XT>(row + d);
-                } else {
-                    if (d + 0 < D) v.x = load_x<XT>(row + d + 0);
-                    if (d + 1 < D) v.y = load_x<XT>(row + d + 1);
-                    if (d + 2 < D) v.z = load_x<XT>(row + d + 2);
-                    if (d + 3 < D) v.w = load_x<XT>(row + d + 3);
+            if (i < TOK * DK4) {
+                const int t = i / DK4;
+                const int q = i % DK4;
+                const int64_t tg = tok0 + t;
+                const int d = d0 + 4 * q;
+                if (tg < N) {
+                    const XT* row = x + tg * static_cast<int64_t>(D);
+                    if (vec_ok) {
+                        if (d < D) v = load_x4<XT>(row + d);
+                    } else {
+                        if (d + 0 < D) v.x = load_x<XT>(row + d + 0);
+                        if (d + 1 < D) v.y = load_x<XT>(row + d + 1);
+                        if (d + 2 < D) v.z = load_x<XT>(row + d + 2);
+                        if (d + 3 < D) v.w = load_x<XT>(row + d + 3);
+                    }
                 }
             }
-            *reinterpret_cast<float4*>(&xs[t * XS + 4 * q]) = v;
+            px[j] = v;
         }
-        __syncthreads();
-
+    };
+    auto stage = [&]() {
+#pragma unroll
+        for (int j = 0; j < PW; ++j) {
+            const int i = tid + j * kThreads;
+            if (i < DK4 * EPAD) ws[i] = pw[j];
+        }
+#pragma unroll
+        for (int j = 0; j < PX; ++j) {
+            const int i = tid + j * kThreads;
+            if (i < TOK * DK4)
+                *reinterpret_cast<float4*>(&xs[(i / DK4) * XS + 4 * (i % DK4)]) = px[j];
+        }
+    };
+    fetch(0);
+    stage();
+    __syncthreads();
+    for (int c = 0; c < nchunks; ++c) {
+        if (c + 1 < nchunks) fetch(c + 1);
 #pragma unroll 4
         for (int q = 0; q < DK4; ++q) {
             float4 xv[kTPG];
@@ -158,6 +184,10 @@ __global__ void __launch_bounds__(kThreads)
             }
         }
         __syncthreads();
+        if (c + 1 < nchunks) {
+            stage();
+            __syncthreads();
+        }
     }
 
     // ---- bias, top-k selection, softmax (per lane group, per token)
@@ -179,6 +209,9 @@ __global__ void __launch_bounds__(kThreads)
             const int e = le + GROUP * s;
             v[s] = e < E ? __fadd_rn(acc[i][s], bv[s]) : -FLT_MAX;
         }
+        // every lane of the group learns each winner; lane 0 of the group
+        // writes it (weight un-normalised), then the group normalises
+        float m = 0.0f, sum = 0.0f;
         for (int kk = 0; kk < ksel; ++kk) {
             float best = -INFINITY;
             int beste = 0x7FFFFFFF;
@@ -203,31 +236,28 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
             for (int s = 0; s < NSLOT; ++s)
                 if (le + GROUP * s == beste) v[s] = -INFINITY;
-            if (le == 0 && kk < KS) {
-                tv[tl * KS + kk] = best;
-                te[tl * KS + kk] = beste;
+            if (kk == 0) m = best;
+            const float ev = kk < k ? expf(best - m) : 0.0f;
+            if (kk < k) sum = __fadd_rn(sum, ev);
+            if (le == 0 && tg < N) {
+                idx_out[tg * ksel + kk] = beste;
+                if (kk < k) val_out[tg * k + kk] = ev;
             }
         }
         __syncwarp(gmask);
-        if (tg < N) {
-            const float m = tv[tl * KS];
-            float sum = 0.0f;
-            for (int kk = 0; kk < k; ++kk) sum = __fadd_rn(sum, expf(tv[tl * KS + kk] - m));
-            for (int kk = le; kk < ksel; kk += GROUP) {
-                idx_out[tg * ksel + kk] = te[tl * KS + kk];
-                if (kk < k) val_out[tg * k + kk] = __fdiv_rn(expf(tv[tl * KS + kk] - m), sum);
-            }
-        }
+        if (tg < N)
+            for (int kk = le; kk < k; kk += GROUP)
+                val_out[tg * k + kk] = __fdiv_rn(val_out[tg * k + kk], sum);
         __syncwarp(gmask);
     }
 }
 
-template <int GROUP, int NSLOT, typename XT, bool EXACT>
+template <int GROUP, int NSLOT, int TPG, typename XT, bool EXACT>
 cudaError_t launch_one(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
                        float* val, cudaStream_t s) {
-    constexpr int TOK = kWarps * (32 / GROUP) * kTPG;
+    constexpr int TOK = kWarps * (32 / GROUP) * TPG;
     const int64_t blocks = (N + TOK - 1) / TOK;
-    gating_kernel<GROUP, NSLOT, XT, EXACT><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(
+    gating_kernel<GROUP, NSLOT, TPG, XT, EXACT><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(
         static_cast<const XT*>(x), reinterpret_cast<const float4*>(g.wt), g.bias, N,
         static_cast<int>(g.D), static_cast<int>(g.E), k, ksel, idx, val);
     return cudaGetLastError();
@@ -236,13 +266,24 @@ cudaError_t launch_one(const Gate& g, const void* x, int64_t N, int k, int ksel,
 template <typename XT, bool EXACT>
 cudaError_t dispatch_e(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
                        float* val, cudaStream_t s) {
+    // Many tokens: 8 tokens per lane group halves the weight loads per
+    // multiply-add; few tokens: 4, for more CTAs.
+    if (N >= 8192) {
+        switch (g.Epad) {
+            case 8: return launch_one<8, 1, 8, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+            case 16: return launch_one<16, 1, 8, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+            case 32: return launch_one<32, 1, 8, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+            case 64: return launch_one<32, 2, 8, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+            default: break;
+        }
+    }
     switch (g.Epad) {
-        case 8: return launch_one<8, 1, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
-        case 16: return launch_one<16, 1, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
-        case 32: return launch_one<32, 1, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
-        case 64: return launch_one<32, 2, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
-        case 128: return launch_one<32, 4, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
-        default: return launch_one<32, 8, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+        case 8: return launch_one<8, 1, 4, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+        case 16: return launch_one<16, 1, 4, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+        case 32: return launch_one<32, 1, 4, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+        case 64: return launch_one<32, 2, 4, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+        case 128: return launch_one<32, 4, 4, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+        default: return launch_one<32, 8, 4, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
     }
 }
 

@@ -227,3 +227,18 @@ def test_device_pointer_entry_point(cuda):
     oidx, oval = O.fused_gating(xf, w, b, k, extra=1)
     np.testing.assert_array_equal(idx.cpu().numpy(), oidx)
     np.testing.assert_allclose(val.cpu().numpy(), oval, atol=1e-6)
+
+
+@pytest.mark.parametrize("e,k,d", [(17, 3, 37), (33, 6, 64), (64, 6, 130), (8, 2, 96), (5, 5, 16)])
+def test_many_tokens_kernel_bit_exact(shim, e, k, d):
+    """>= 4096 tokens take the token-major kernel (experts split over threads);
+    padding of E and D, k == E, and the reroute choice included."""
+    fg, _ = shim
+    h, w, b = cases._gating_inputs(np.random.default_rng(e * 100 + d), 5000, d, e)
+    w[:, e - 1] = w[:, 0]
+    b[e - 1] = b[0]  # exact tie between the first and the last expert
+    extra = 1 if k < e else 0
+    idx, val = fg.gating(h, w, b, k, k_extra=extra)
+    oidx, oval = O.fused_gating(h, w, b, k, extra=extra)
+    np.testing.assert_array_equal(idx, oidx)
+    np.testing.assert_allclose(val, oval, atol=1e-6)
