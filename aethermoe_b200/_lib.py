@@ -44,6 +44,20 @@ class MoeConfig(ctypes.Structure):
                 ("capacity", _u64), ("gating_mode", _int)]
 
 
+EP_MAX_RANKS = 64
+
+
+class EpPeerPlan(ctypes.Structure):
+    """``aem_ep_peer_plan``: where one rank's rows go in one peer-memory exchange."""
+    _fields_ = [("ok", ctypes.c_int32), ("units_in", ctypes.c_int32),
+                ("pairs_in", ctypes.c_int32), ("pairs_out", ctypes.c_int32),
+                ("dst_unit_off", ctypes.c_int32 * EP_MAX_RANKS),
+                ("dst_pair_off", ctypes.c_int32 * EP_MAX_RANKS),
+                ("send_pair_off", ctypes.c_int32 * EP_MAX_RANKS),
+                ("recv_pair_off", ctypes.c_int32 * (EP_MAX_RANKS + 1)),
+                ("ret_off", ctypes.c_int32 * EP_MAX_RANKS)]
+
+
 _SIGS = {
     "aem_last_error": (ctypes.c_char_p, []),
     "aem_version": (ctypes.c_char_p, []),
@@ -78,8 +92,10 @@ _SIGS = {
     "aem_ep_plan_bases": (_int, [_vp, _int, _int, _int, _int, _vp]),
     "aem_ep_unique_id": (_int, [_vp]),
     "aem_ep_plan_exchange": (_int, [_vp, _int, _int, _int, _vp, _vp, _vp, _vp, _vp]),
-    "aem_ep_create": (_int, [ctypes.POINTER(MoeConfig), _int, _int, _vp, _vp, _vp, _vp,
-                             ctypes.POINTER(_vp)]),
+    "aem_ep_plan_peer": (_int, [_vp, _int, _int, _int, _i64, _i64, _i64,
+                                ctypes.POINTER(EpPeerPlan), _vp]),
+    "aem_ep_create": (_int, [ctypes.POINTER(MoeConfig), _int, _int, _vp, _vp, _vp, _vp, _vp,
+                             _i64, ctypes.POINTER(_vp)]),
     "aem_ep_free": (_int, [_vp]),
     "aem_ep_forward": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp]),
     "aem_ep_last_routing": (_int, [_vp, _vp, _vp, _vp, _vp]),

@@ -53,6 +53,8 @@ enum : int {
     ERR_ROUTE_EXPERT = 1 << 1,    // expert id >= E
     ERR_GEMM_TIMEOUT = 1 << 2,    // a bounded mbarrier wait in the GEMM gave up
     ERR_GEMM_GROUPS = 1 << 3,     // group table inconsistent
+    ERR_EP_PLAN = 1 << 4,         // expert-parallel counts do not fit the receive buffers
+    ERR_EP_BOUNDS = 1 << 5,       // expert-parallel row index outside its buffer (skipped)
 };
 
 // Device int that kernels atomicOr error bits into (one per device, lazily

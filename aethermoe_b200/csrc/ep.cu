@@ -1,4 +1,5 @@
-// Expert-parallel MoE layer over NCCL (one process per GPU, NVLink/NVSwitch).
+// Expert-parallel MoE layer: one process per GPU, activations and expert
+// outputs exchanged by stores into the peers' memory over NVLink/NVSwitch.
 //
 // Replaces the reference's Router scatter/gather over ICollectiveTransport
 // (src/orchestration/router.hpp:67-100, collective_transport.hpp:37-51): the
@@ -10,17 +11,29 @@
 //   slot j on rank r come after all units of slots < j (every rank) and after
 //   slot j of ranks < r.  One all-gather of per-(slot, expert) counts gives
 //   each rank that offset; local stable ranks do the rest.
-// Step: gating -> slot counts -> all-gather -> capacity routing (global ranks)
-// -> expert-grouped send buffer -> all-gather of per-expert send counts (the
-// one host sync: NCCL needs sizes) -> grouped send/recv dispatch -> local
-// grouped GEMMs on the received (source, expert) segments -> send/recv of the
-// float32 expert outputs back -> weighted combine in token order.
+//
+// Data movement (no host synchronisation in a step):
+//   pairs  -- (token, destination rank): a token's activation row crosses
+//             NVLink once per destination rank, not once per unit;
+//   units  -- (token, slot): the destination gets, per unit, the row of its
+//             pair and its gate weight, at the unit's row in the destination's
+//             (source, expert)-grouped layout.
+//   Step: gating -> slot counts -> all-gather -> capacity routing (global
+//   ranks) -> pair numbering -> all-gather of expert starts + pair counts ->
+//   on-device plan -> push pairs + unit metadata into the destinations ->
+//   barrier -> expand pairs to units -> grouped up GEMM (+ReLU) -> grouped down
+//   GEMM, gate-weighted and pre-reduced per pair -> push the pair sums back
+//   into the sources -> barrier -> per-token sum over destination ranks.
+// Receive buffers are sized for the worst case at creation and mapped by
+// every peer once (CUDA IPC), so a step never allocates or re-maps.  NCCL
+// carries only the two small all-gathers and the two barriers.
 #include <cuda_bf16.h>
 #include <dlfcn.h>
 #include <nccl.h>
 
 #include <algorithm>
 #include <mutex>
+#include <string>
 #include <vector>
 
 #include "common.cuh"
@@ -39,10 +52,7 @@ struct NcclApi {
     decltype(&::ncclCommInitRank) CommInitRank = nullptr;
     decltype(&::ncclCommDestroy) CommDestroy = nullptr;
     decltype(&::ncclAllGather) AllGather = nullptr;
-    decltype(&::ncclGroupStart) GroupStart = nullptr;
-    decltype(&::ncclGroupEnd) GroupEnd = nullptr;
-    decltype(&::ncclSend) Send = nullptr;
-    decltype(&::ncclRecv) Recv = nullptr;
+    decltype(&::ncclAllReduce) AllReduce = nullptr;
     decltype(&::ncclGetErrorString) GetErrorString = nullptr;
 };
 
@@ -74,10 +84,7 @@ static const NcclApi* nccl() {
         sym(g_nccl.CommInitRank, "ncclCommInitRank");
         sym(g_nccl.CommDestroy, "ncclCommDestroy");
         sym(g_nccl.AllGather, "ncclAllGather");
-        sym(g_nccl.GroupStart, "ncclGroupStart");
-        sym(g_nccl.GroupEnd, "ncclGroupEnd");
-        sym(g_nccl.Send, "ncclSend");
-        sym(g_nccl.Recv, "ncclRecv");
+        sym(g_nccl.AllReduce, "ncclAllReduce");
         sym(g_nccl.GetErrorString, "ncclGetErrorString");
         g_nccl_ok = ok;
     });
@@ -106,7 +113,105 @@ static const NcclApi* nccl() {
 
 namespace aem {
 
+// Per-step plan of one rank (see aem_ep_peer_plan).  `all` is [R][E+1+R]:
+// every rank's expert starts, then its pair counts per destination.  Every
+// rank runs this on the same all-gathered data, so all agree on `ok`.
+__host__ __device__ inline void plan_peer(const int32_t* all, int R, int E, int me, int64_t ucap,
+                                          int64_t pcap, int64_t rcap, aem_ep_peer_plan* pl,
+                                          int32_t* groups) {
+    const int W = E + 1 + R;
+    const int el = E / R;
+    bool ok = true;
+    for (int s = 0; s < R && ok; ++s) {
+        const int32_t* a = all + static_cast<int64_t>(s) * W;
+        if (a[0] != 0) ok = false;
+        for (int e = 0; e < E; ++e)
+            if (a[e + 1] < a[e]) ok = false;
+        int64_t pout = 0;
+        for (int r = 0; r < R; ++r) {
+            const int64_t units = a[(r + 1) * el] - a[r * el];
+            const int64_t pairs = a[E + 1 + r];
+            // a pair exists exactly when the token has a unit there
+            if (pairs < 0 || pairs > units || ((units > 0) != (pairs > 0))) ok = false;
+            pout += pairs;
+        }
+        if (pout > rcap) ok = false;
+    }
+    for (int r = 0; r < R && ok; ++r) {
+        int64_t u = 0, p = 0;
+        for (int s = 0; s < R; ++s) {
+            const int32_t* a = all + static_cast<int64_t>(s) * W;
+            u += a[(r + 1) * el] - a[r * el];
+            p += a[E + 1 + r];
+        }
+        if (u > ucap || p > pcap) ok = false;
+    }
+    pl->ok = ok ? 1 : 0;
+    pl->units_in = pl->pairs_in = pl->pairs_out = 0;
+    for (int r = 0; r < AEM_EP_MAX_RANKS; ++r) {
+        pl->dst_unit_off[r] = pl->dst_pair_off[r] = pl->send_pair_off[r] = 0;
+        pl->recv_pair_off[r] = pl->ret_off[r] = 0;
+    }
+    pl->recv_pair_off[AEM_EP_MAX_RANKS] = 0;
+    for (int i = 0; i <= E; ++i) groups[i] = 0;
+    if (!ok) return;
+    const int32_t* mine = all + static_cast<int64_t>(me) * W;
+    int64_t acc = 0;
+    for (int r = 0; r < R; ++r) {
+        pl->send_pair_off[r] = static_cast<int32_t>(acc);
+        acc += mine[E + 1 + r];
+    }
+    pl->pairs_out = static_cast<int32_t>(acc);
+    for (int r = 0; r < R; ++r) {
+        int64_t u = 0, p = 0;
+        for (int s = 0; s < me; ++s) {
+            const int32_t* a = all + static_cast<int64_t>(s) * W;
+            u += a[(r + 1) * el] - a[r * el];
+            p += a[E + 1 + r];
+        }
+        pl->dst_unit_off[r] = static_cast<int32_t>(u);
+        pl->dst_pair_off[r] = static_cast<int32_t>(p);
+    }
+    acc = 0;
+    for (int s = 0; s < R; ++s) {
+        const int32_t* a = all + static_cast<int64_t>(s) * W;
+        pl->recv_pair_off[s] = static_cast<int32_t>(acc);
+        acc += a[E + 1 + me];
+        int64_t before = 0;
+        for (int r = 0; r < me; ++r) before += a[E + 1 + r];
+        pl->ret_off[s] = static_cast<int32_t>(before);
+    }
+    pl->recv_pair_off[R] = static_cast<int32_t>(acc);
+    pl->pairs_in = static_cast<int32_t>(acc);
+    int64_t g = 0;
+    for (int s = 0; s < R; ++s) {
+        const int32_t* a = all + static_cast<int64_t>(s) * W;
+        for (int e = 0; e < el; ++e) {
+            g += a[me * el + e + 1] - a[me * el + e];
+            groups[s * el + e + 1] = static_cast<int32_t>(g);
+        }
+    }
+    pl->units_in = static_cast<int32_t>(g);
+}
+
 namespace {
+
+constexpr int kCopyThreads = 256;
+
+// Base pointers of every rank's exchange region (this rank's own at [me]).
+struct EpPeers {
+    char* base[AEM_EP_MAX_RANKS];
+};
+
+// Byte offsets of the buffers inside an exchange region (identical on all
+// ranks because every rank sizes them from the same config and capacity).
+struct ExchangeLayout {
+    size_t xpair;     // bf16 [pairs_cap][d]    activation rows received
+    size_t rowmap;    // int32 [units_cap]      unit -> received pair row
+    size_t rowscale;  // f32 [units_cap]        unit -> gate weight
+    size_t ret;       // f32 [ret_cap][d]       pair sums returned to this rank
+    size_t bytes;
+};
 
 // cnt[j][e] = number of local tokens whose slot-j choice is e.
 __global__ void slot_count_kernel(const int32_t* __restrict__ idx, int64_t T, int ldi, int k, int E,
@@ -146,28 +251,268 @@ __global__ void ep_corr_kernel(const long long* __restrict__ all, int R, int k, 
     }
 }
 
-// out[t] = sum_j val[t,j] * y[dest_of[j*T + t]]  (j in increasing order).
-template <typename OT>
-__global__ void combine_gather_kernel(const float* __restrict__ y, const int32_t* __restrict__ dest_of,
-                                      const float* __restrict__ val, int64_t T, int k, int64_t d,
-                                      OT* __restrict__ out) {
-    const int64_t total = T * d;
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t t = i / d, c = i % d;
-        float acc = 0.0f;
-        for (int j = 0; j < k; ++j) {
-            const int64_t row = dest_of[static_cast<int64_t>(j) * T + t];
-            acc += val[t * k + j] * y[row * d + c];
+// Expert ids of the gating output in placement order: pos[e] = rank(e)*el +
+// (index of e among its rank's experts), so every rank's experts are one
+// contiguous range of the routing's expert-sorted units.
+__global__ void relabel_kernel(const int32_t* __restrict__ in, int64_t n,
+                               const int32_t* __restrict__ pos, int32_t* __restrict__ out) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        out[i] = pos[in[i]];
+}
+
+// Back to expert ids: out[i] = expert[in[i]] (placement position -> id).
+__global__ void unlabel_kernel(const uint32_t* __restrict__ in, int64_t n,
+                               const int32_t* __restrict__ expert, uint32_t* __restrict__ out) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        out[i] = static_cast<uint32_t>(expert[in[i]]);
+}
+
+// Block r numbers the tokens that have at least one unit on rank r, in token
+// order: pair_local[r][t] = that number, or -1.  Writes the pair count per
+// destination after the expert starts into the all-gather payload.
+__global__ void __launch_bounds__(1024)
+    ep_pairs_kernel(const uint32_t* __restrict__ eff, int64_t T, int k, int el, int E,
+                    const int* __restrict__ starts, int32_t* __restrict__ pair_local,
+                    int32_t* __restrict__ payload) {
+    __shared__ int wsum[32];
+    __shared__ int running;
+    const int r = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nwarps = blockDim.x >> 5;
+    if (r == 0)
+        for (int i = tid; i <= E; i += blockDim.x) payload[i] = starts[i];
+    if (tid == 0) running = 0;
+    __syncthreads();
+    for (int64_t base = 0; base < T; base += blockDim.x) {
+        const int64_t t = base + tid;
+        bool f = false;
+        if (t < T)
+            for (int j = 0; j < k; ++j)
+                f |= static_cast<int>(eff[static_cast<int64_t>(j) * T + t]) / el == r;
+        const unsigned b = __ballot_sync(0xFFFFFFFFu, f);
+        const int pre = __popc(b & ((1u << lane) - 1u));
+        if (lane == 0) wsum[warp] = __popc(b);
+        __syncthreads();
+        if (warp == 0) {
+            int v = lane < nwarps ? wsum[lane] : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xFFFFFFFFu, v, o);
+                if (lane >= o) v += n;
+            }
+            wsum[lane] = v;  // inclusive
         }
-        if constexpr (sizeof(OT) == 2)
-            out[i] = __float2bfloat16_rn(acc);
-        else
-            out[i] = acc;
+        __syncthreads();
+        const int run = running;
+        const int wbase = warp ? wsum[warp - 1] : 0;
+        if (t < T) pair_local[static_cast<int64_t>(r) * T + t] = f ? run + wbase + pre : -1;
+        __syncthreads();
+        if (tid == 0) running = run + wsum[nwarps - 1];
+        __syncthreads();
+    }
+    if (tid == 0) payload[E + 1 + r] = running;
+}
+
+__global__ void ep_plan_kernel(const int32_t* __restrict__ all, int R, int E, int me, int64_t ucap,
+                               int64_t pcap, int64_t rcap, aem_ep_peer_plan* __restrict__ plan,
+                               int32_t* __restrict__ groups, int* __restrict__ err) {
+    plan_peer(all, R, E, me, ucap, pcap, rcap, plan, groups);
+    if (!plan->ok) atomicOr(err, ERR_EP_PLAN);
+}
+
+// One warp copies one row of d elements (d % 8 == 0) to bf16.
+template <typename XT>
+__device__ __forceinline__ void copy_row_bf16(const XT* __restrict__ in, __nv_bfloat16* out,
+                                              int64_t d, int lane) {
+    if constexpr (sizeof(XT) == 2) {
+        const uint4* vi = reinterpret_cast<const uint4*>(in);
+        uint4* vo = reinterpret_cast<uint4*>(out);
+        for (int64_t i = lane; i < d / 8; i += 32) vo[i] = __ldg(vi + i);
+    } else {
+        const float4* vi = reinterpret_cast<const float4*>(in);
+        uint4* vo = reinterpret_cast<uint4*>(out);
+        for (int64_t i = lane; i < d / 8; i += 32) {
+            const float4 a = __ldg(vi + 2 * i), b = __ldg(vi + 2 * i + 1);
+            __nv_bfloat162 p0 = __floats2bfloat162_rn(a.x, a.y);
+            __nv_bfloat162 p1 = __floats2bfloat162_rn(a.z, a.w);
+            __nv_bfloat162 p2 = __floats2bfloat162_rn(b.x, b.y);
+            __nv_bfloat162 p3 = __floats2bfloat162_rn(b.z, b.w);
+            uint4 u;
+            u.x = *reinterpret_cast<uint32_t*>(&p0);
+            u.y = *reinterpret_cast<uint32_t*>(&p1);
+            u.z = *reinterpret_cast<uint32_t*>(&p2);
+            u.w = *reinterpret_cast<uint32_t*>(&p3);
+            vo[i] = u;
+        }
     }
 }
 
-ncclDataType_t nccl_dtype(int bytes) { return bytes == 2 ? ncclBfloat16 : ncclFloat32; }
+// Push: (a) each (destination, token) pair's activation row into the
+// destination's pair rows; (b) each unit's (pair row, gate weight) into the
+// destination's unit row.  Units of this rank are expert-sorted, so those
+// for rank r are the contiguous range [starts[r*el], starts[(r+1)*el]).
+template <typename XT>
+__global__ void __launch_bounds__(kCopyThreads)
+    ep_dispatch_kernel(const XT* __restrict__ x, int64_t T, int64_t d, int R, int el,
+                       const int32_t* __restrict__ pair_local, const int* __restrict__ starts,
+                       const int32_t* __restrict__ src_token, const float* __restrict__ rowscale,
+                       int k, const aem_ep_peer_plan* __restrict__ plan, EpPeers peers,
+                       ExchangeLayout lay, int64_t ucap, int64_t pcap, int* __restrict__ err) {
+    __shared__ int bnd[AEM_EP_MAX_RANKS + 1];
+    __shared__ int upos[AEM_EP_MAX_RANKS];
+    __shared__ int ppos[AEM_EP_MAX_RANKS];
+    if (!plan->ok) return;
+    for (int i = threadIdx.x; i <= R; i += blockDim.x) bnd[i] = starts[i * el];
+    for (int i = threadIdx.x; i < R; i += blockDim.x) {
+        upos[i] = plan->dst_unit_off[i];
+        ppos[i] = plan->dst_pair_off[i];
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+         i < R * T; i += nw) {
+        const int pl = pair_local[i];
+        if (pl < 0) continue;
+        const int r = static_cast<int>(i / T);
+        const int64_t t = i - static_cast<int64_t>(r) * T;
+        const int64_t row = static_cast<int64_t>(ppos[r]) + pl;
+        if (row >= pcap) {
+            if (lane == 0) atomicOr(err, ERR_EP_BOUNDS);
+            continue;
+        }
+        auto* dst = reinterpret_cast<__nv_bfloat16*>(peers.base[r] + lay.xpair) + row * d;
+        copy_row_bf16<XT>(x + t * d, dst, d, lane);
+    }
+    const int64_t U = min(static_cast<int64_t>(bnd[R]), T * k);
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < U;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int r = 0;
+        while (r + 1 < R && i >= bnd[r + 1]) ++r;
+        const int64_t t = src_token[i];
+        const int pl = (t >= 0 && t < T) ? pair_local[static_cast<int64_t>(r) * T + t] : -1;
+        const int64_t pos = upos[r] + (i - bnd[r]);
+        if (pl < 0 || pos >= ucap) {
+            atomicOr(err, ERR_EP_BOUNDS);
+            continue;
+        }
+        reinterpret_cast<int32_t*>(peers.base[r] + lay.rowmap)[pos] = ppos[r] + pl;
+        reinterpret_cast<float*>(peers.base[r] + lay.rowscale)[pos] = __ldg(rowscale + i);
+    }
+}
+
+// Destination side, after the barrier: unit rows from the received pair rows
+// (the grouped GEMM input), and zeroed pair sums for the down GEMM to
+// accumulate into.
+__global__ void __launch_bounds__(kCopyThreads)
+    ep_expand_kernel(const __nv_bfloat16* __restrict__ xpair, int32_t* __restrict__ rowmap_in,
+                     float* __restrict__ rowscale_in, const aem_ep_peer_plan* __restrict__ plan,
+                     int64_t d,
+                     __nv_bfloat16* __restrict__ xu, float* __restrict__ ret_acc,
+                     int* __restrict__ err) {
+    if (!plan->ok) return;
+    const int64_t units = plan->units_in, pairs = plan->pairs_in;
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t u = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+         u < units; u += nw) {
+        const int64_t p = rowmap_in[u];
+        uint4* vo = reinterpret_cast<uint4*>(xu + u * d);
+        if (p < 0 || p >= pairs) {  // a unit row no source wrote: contributes nothing
+            __syncwarp();
+            if (lane == 0) {
+                atomicOr(err, ERR_EP_BOUNDS);
+                rowmap_in[u] = 0;
+                rowscale_in[u] = 0.0f;
+            }
+            for (int64_t i = lane; i < d / 8; i += 32) vo[i] = make_uint4(0, 0, 0, 0);
+            continue;
+        }
+        const uint4* vi = reinterpret_cast<const uint4*>(xpair + p * d);
+        for (int64_t i = lane; i < d / 8; i += 32) vo[i] = vi[i];
+    }
+    float4* z = reinterpret_cast<float4*>(ret_acc);
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < pairs * d / 4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        z[i] = zero;
+}
+
+// Return: pair sum p (from source s) into row ret_off[s] + (p - recv_pair_off[s])
+// of s's return rows.
+__global__ void __launch_bounds__(kCopyThreads)
+    ep_return_kernel(const float* __restrict__ ret_acc, const aem_ep_peer_plan* __restrict__ plan,
+                     int R, int64_t d, EpPeers peers, ExchangeLayout lay, int64_t rcap,
+                     int* __restrict__ err) {
+    __shared__ int off[AEM_EP_MAX_RANKS + 1];
+    __shared__ int ret[AEM_EP_MAX_RANKS];
+    if (!plan->ok) return;
+    for (int i = threadIdx.x; i <= R; i += blockDim.x) off[i] = plan->recv_pair_off[i];
+    for (int i = threadIdx.x; i < R; i += blockDim.x) ret[i] = plan->ret_off[i];
+    __syncthreads();
+    const int64_t pairs = off[R];
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+         p < pairs; p += nw) {
+        int s = 0;
+        while (s + 1 < R && p >= off[s + 1]) ++s;
+        const int64_t row = ret[s] + (p - off[s]);
+        if (row >= rcap) {
+            if (lane == 0) atomicOr(err, ERR_EP_BOUNDS);
+            continue;
+        }
+        const float4* vi = reinterpret_cast<const float4*>(ret_acc + p * d);
+        float4* vo = reinterpret_cast<float4*>(reinterpret_cast<float*>(peers.base[s] + lay.ret) +
+                                               row * d);
+        for (int64_t i = lane; i < d / 4; i += 32) vo[i] = vi[i];
+    }
+}
+
+// out[t] = sum over destination ranks r (increasing) of the returned pair sum.
+template <typename OT>
+__global__ void __launch_bounds__(kCopyThreads)
+    ep_combine_kernel(const float* __restrict__ ret_in, const int32_t* __restrict__ pair_local,
+                      const aem_ep_peer_plan* __restrict__ plan, int64_t T, int R, int64_t d,
+                      OT* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const bool ok = plan->ok != 0;
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+         t < T; t += nw) {
+        int64_t row = -1;
+        if (ok && lane < R) {
+            const int pl = pair_local[static_cast<int64_t>(lane) * T + t];
+            if (pl >= 0) row = static_cast<int64_t>(plan->send_pair_off[lane]) + pl;
+        }
+        for (int64_t c = lane; c < d / 4; c += 32) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r = 0; r < R; ++r) {
+                const int64_t rr = __shfl_sync(0xFFFFFFFFu, row, r);
+                if (rr < 0) continue;
+                const float4 v = reinterpret_cast<const float4*>(ret_in + rr * d)[c];
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+            }
+            if constexpr (sizeof(OT) == 2) {
+                __nv_bfloat162 a = __floats2bfloat162_rn(acc.x, acc.y);
+                __nv_bfloat162 b = __floats2bfloat162_rn(acc.z, acc.w);
+                uint2 u;
+                u.x = *reinterpret_cast<uint32_t*>(&a);
+                u.y = *reinterpret_cast<uint32_t*>(&b);
+                reinterpret_cast<uint2*>(out + t * d)[c] = u;
+            } else {
+                reinterpret_cast<float4*>(out + t * d)[c] = acc;
+            }
+        }
+    }
+}
+
+size_t align256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
 
 }  // namespace
 
@@ -178,106 +523,235 @@ struct Ep {
     Gate* gate = nullptr;
     QWeight* up = nullptr;
     QWeight* down = nullptr;
-    Moe loc;  // local buffers (routing, send rows) of the single-GPU layer
-    // collective scratch
+    Moe loc;  // routing buffers of the single-GPU layer (sized for T_cap tokens)
+    int64_t T_cap = 0;
+    int64_t units_cap = 0, pairs_cap = 0, ret_cap = 0;
+    // exchange region: this rank's own, and every rank's mapping of it
+    ExchangeLayout lay{};
+    void* xreg = nullptr;
+    EpPeers peers{};
+    bool mapped[AEM_EP_MAX_RANKS] = {};
+    // local buffers
+    void* lbuf = nullptr;
     unsigned long long* cnt = nullptr;  // [k][E]
     long long* cnt_all = nullptr;       // [R][k][E]
     long long* corr = nullptr;          // [k][E]
-    int* starts_all = nullptr;          // [R][E+1]
-    int32_t* dest_of = nullptr;         // [U]
-    int* h_starts = nullptr;            // pinned [R][E+1]
-    int* h_groups = nullptr;            // pinned [R*e_loc+1]
-    int* d_groups = nullptr;            // [R*e_loc+1]
-    int64_t u_cap = 0;                  // capacity of dest_of
-    // receive side (grow-only)
-    int64_t r_cap = 0;
-    void* xr = nullptr;   // bf16 [r_cap, d]
-    void* hr = nullptr;   // bf16 [r_cap, ffn]
-    float* yr = nullptr;  // f32 [r_cap, d]
-    float* yb = nullptr;  // f32 [u_cap, d] expert outputs back in grouped order
+    int32_t* payload = nullptr;         // [E+1+R] this rank's starts + pair counts
+    int32_t* payload_all = nullptr;     // [R][E+1+R]
+    aem_ep_peer_plan* plan = nullptr;
+    int32_t* groups = nullptr;          // [E+1]
+    int32_t* pair_local = nullptr;      // [R][T]
+    int* bar = nullptr;                 // barrier word
+    void* xu = nullptr;                 // bf16 [units_cap][d]
+    void* hu = nullptr;                 // bf16 [units_cap][ffn]
+    float* ret_acc = nullptr;           // f32 [pairs_cap][d]
+    int32_t* idx_pos = nullptr;         // [T_cap][ksel] gating ids in placement order
+    int32_t* pos_of = nullptr;          // [E] expert id -> placement position
+    int32_t* expert_at = nullptr;       // [E] placement position -> expert id
+    bool placed = false;                // placement is not the contiguous map
+    std::vector<int32_t> h_pos;         // host copy of pos_of
     int64_t last_T = 0;
     PhaseProfiler prof;
 
-    aem_status init_buffers();
-    aem_status reserve_units(int64_t U);
-    aem_status reserve_recv(int64_t rows);
+    aem_status init(int64_t max_tokens);
+    aem_status map_peers(cudaStream_t s);
+    aem_status barrier(cudaStream_t s);
+    void release();
     aem_status forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dtype od,
                        cudaStream_t s);
 };
 
-aem_status Ep::init_buffers() {
+aem_status Ep::init(int64_t max_tokens) {
     const int k = cfg.top_k, E = cfg.num_experts, R = world;
-    AEM_TRY_CUDA(cudaMalloc(&cnt, sizeof(unsigned long long) * k * E));
-    AEM_TRY_CUDA(cudaMalloc(&cnt_all, sizeof(long long) * R * k * E));
-    AEM_TRY_CUDA(cudaMalloc(&corr, sizeof(long long) * k * E));
-    AEM_TRY_CUDA(cudaMalloc(&starts_all, sizeof(int) * R * (E + 1)));
-    AEM_TRY_CUDA(cudaMalloc(&d_groups, sizeof(int) * (R * e_loc + 1)));
-    AEM_TRY_CUDA(cudaMallocHost(&h_starts, sizeof(int) * R * (E + 1)));
-    AEM_TRY_CUDA(cudaMallocHost(&h_groups, sizeof(int) * (R * e_loc + 1)));
+    const int64_t d = cfg.d_model, f = cfg.d_ffn;
+    T_cap = std::max<int64_t>(max_tokens, 1);
+    units_cap = static_cast<int64_t>(R) * T_cap * k;  // every unit of every rank
+    pairs_cap = static_cast<int64_t>(R) * T_cap;      // every token of every rank
+    ret_cap = T_cap * std::min(R, k);                 // a token has <= min(R, k) destinations
+    AEM_REQUIRE(units_cap < (1ll << 31) && pairs_cap * d < (1ll << 40),
+                "aem_ep_create: max_tokens_local=%lld too large for %d ranks x top-%d",
+                (long long)max_tokens, R, k);
+    AEM_TRY(loc.reserve(T_cap, false));
+    size_t off = 0;
+    auto slot = [&](size_t bytes) {
+        const size_t o = off;
+        off += align256(bytes);
+        return o;
+    };
+    lay.xpair = slot(2 * pairs_cap * d);
+    lay.rowmap = slot(sizeof(int32_t) * units_cap);
+    lay.rowscale = slot(sizeof(float) * units_cap);
+    lay.ret = slot(sizeof(float) * ret_cap * d);
+    lay.bytes = off;
+    AEM_TRY_CUDA(cudaMalloc(&xreg, lay.bytes));
+    AEM_TRY_CUDA(cudaMemset(xreg, 0, lay.bytes));
+    off = 0;
+    const size_t o_cnt = slot(sizeof(unsigned long long) * k * E);
+    const size_t o_cnt_all = slot(sizeof(long long) * R * k * E);
+    const size_t o_corr = slot(sizeof(long long) * k * E);
+    const size_t o_pay = slot(sizeof(int32_t) * (E + 1 + R));
+    const size_t o_pay_all = slot(sizeof(int32_t) * R * (E + 1 + R));
+    const size_t o_plan = slot(sizeof(aem_ep_peer_plan));
+    const size_t o_groups = slot(sizeof(int32_t) * (E + 1));
+    const size_t o_pl = slot(sizeof(int32_t) * R * T_cap);
+    const size_t o_bar = slot(sizeof(int));
+    const int ksel = k < E ? k + 1 : k;
+    const size_t o_ipos = slot(sizeof(int32_t) * T_cap * ksel);
+    const size_t o_pos = slot(sizeof(int32_t) * E);
+    const size_t o_exp = slot(sizeof(int32_t) * E);
+    const size_t o_xu = slot(2 * units_cap * d);
+    const size_t o_hu = slot(2 * units_cap * f);
+    const size_t o_ret = slot(sizeof(float) * pairs_cap * d);
+    AEM_TRY_CUDA(cudaMalloc(&lbuf, off));
+    AEM_TRY_CUDA(cudaMemset(lbuf, 0, o_xu));  // everything but the big row buffers
+    char* b = static_cast<char*>(lbuf);
+    cnt = reinterpret_cast<unsigned long long*>(b + o_cnt);
+    cnt_all = reinterpret_cast<long long*>(b + o_cnt_all);
+    corr = reinterpret_cast<long long*>(b + o_corr);
+    payload = reinterpret_cast<int32_t*>(b + o_pay);
+    payload_all = reinterpret_cast<int32_t*>(b + o_pay_all);
+    plan = reinterpret_cast<aem_ep_peer_plan*>(b + o_plan);
+    groups = reinterpret_cast<int32_t*>(b + o_groups);
+    pair_local = reinterpret_cast<int32_t*>(b + o_pl);
+    bar = reinterpret_cast<int*>(b + o_bar);
+    idx_pos = reinterpret_cast<int32_t*>(b + o_ipos);
+    pos_of = reinterpret_cast<int32_t*>(b + o_pos);
+    expert_at = reinterpret_cast<int32_t*>(b + o_exp);
+    std::vector<int32_t> at(E);
+    for (int e = 0; e < E; ++e) at[h_pos[e]] = e;
+    AEM_TRY_CUDA(cudaMemcpy(pos_of, h_pos.data(), sizeof(int32_t) * E, cudaMemcpyHostToDevice));
+    AEM_TRY_CUDA(cudaMemcpy(expert_at, at.data(), sizeof(int32_t) * E, cudaMemcpyHostToDevice));
+    xu = b + o_xu;
+    hu = b + o_hu;
+    ret_acc = reinterpret_cast<float*>(b + o_ret);
     return AEM_OK;
 }
 
-aem_status Ep::reserve_units(int64_t U) {
-    if (U <= u_cap) return AEM_OK;
-    AEM_TRY_CUDA(cudaDeviceSynchronize());
-    cudaFree(dest_of);
-    cudaFree(yb);
-    dest_of = nullptr;
-    yb = nullptr;
-    AEM_TRY_CUDA(cudaMalloc(&dest_of, sizeof(int32_t) * U));
-    AEM_TRY_CUDA(cudaMalloc(&yb, sizeof(float) * U * cfg.d_model));
-    u_cap = U;
+// All-gathers every rank's IPC handle and sizes; maps every peer's region.
+aem_status Ep::map_peers(cudaStream_t s) {
+    const int R = world;
+    struct Record {
+        cudaIpcMemHandle_t h;
+        int64_t bytes, T_cap, d, f, E, k, placement;
+        uint8_t pad[128 - sizeof(cudaIpcMemHandle_t) - 7 * sizeof(int64_t)];
+    };
+    static_assert(sizeof(Record) == 128, "record size");
+    Record mine{};
+    AEM_TRY_CUDA(cudaIpcGetMemHandle(&mine.h, xreg));
+    mine.bytes = static_cast<int64_t>(lay.bytes);
+    mine.T_cap = T_cap;
+    mine.d = cfg.d_model;
+    mine.f = cfg.d_ffn;
+    mine.E = cfg.num_experts;
+    mine.k = cfg.top_k;
+    uint64_t hsh = 1469598103934665603ull;  // FNV-1a of the placement
+    for (int32_t p : h_pos) hsh = (hsh ^ static_cast<uint32_t>(p)) * 1099511628211ull;
+    mine.placement = static_cast<int64_t>(hsh);
+    void* dev = nullptr;
+    AEM_TRY_CUDA(cudaMalloc(&dev, sizeof(Record) * R));
+    std::vector<Record> all(R);
+    aem_status st = AEM_OK;
+    do {
+        cudaError_t e = cudaMemcpyAsync(static_cast<char*>(dev) + sizeof(Record) * rank, &mine,
+                                        sizeof(Record), cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) {
+            set_error("aem_ep_create: %s", cudaGetErrorString(e));
+            st = AEM_ECUDA;
+            break;
+        }
+        ncclResult_t n = nccl()->AllGather(static_cast<char*>(dev) + sizeof(Record) * rank, dev,
+                                           sizeof(Record), ncclUint8, comm, s);
+        if (n != ncclSuccess) {
+            set_error("aem_ep_create: handle all-gather failed: %s", nccl()->GetErrorString(n));
+            st = AEM_ENCCL;
+            break;
+        }
+        e = cudaMemcpyAsync(all.data(), dev, sizeof(Record) * R, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) {
+            set_error("aem_ep_create: %s", cudaGetErrorString(e));
+            st = AEM_ECUDA;
+        }
+    } while (0);
+    cudaFree(dev);
+    if (st != AEM_OK) return st;
+    for (int r = 0; r < R; ++r) {
+        const Record& a = all[r];
+        AEM_REQUIRE(a.bytes == mine.bytes && a.T_cap == mine.T_cap && a.d == mine.d &&
+                        a.f == mine.f && a.E == mine.E && a.k == mine.k &&
+                        a.placement == mine.placement,
+                    "aem_ep_create: rank %d has a different config, placement or "
+                    "max_tokens_local", r);
+    }
+    peers.base[rank] = static_cast<char*>(xreg);
+    for (int r = 0; r < R; ++r) {
+        if (r == rank) continue;
+        void* p = nullptr;
+        AEM_TRY_CUDA(cudaIpcOpenMemHandle(&p, all[r].h, cudaIpcMemLazyEnablePeerAccess));
+        peers.base[r] = static_cast<char*>(p);
+        mapped[r] = true;
+    }
     return AEM_OK;
 }
 
-aem_status Ep::reserve_recv(int64_t rows) {
-    if (rows <= r_cap) return AEM_OK;
-    AEM_TRY_CUDA(cudaDeviceSynchronize());
-    cudaFree(xr);
-    cudaFree(hr);
-    cudaFree(yr);
-    xr = hr = nullptr;
-    yr = nullptr;
-    const int64_t want = rows + rows / 4 + 256;
-    AEM_TRY_CUDA(cudaMalloc(&xr, 2 * want * cfg.d_model));
-    AEM_TRY_CUDA(cudaMalloc(&hr, 2 * want * cfg.d_ffn));
-    AEM_TRY_CUDA(cudaMalloc(&yr, sizeof(float) * want * cfg.d_model));
-    r_cap = want;
+aem_status Ep::barrier(cudaStream_t s) {
+    AEM_TRY_NCCL(nccl()->AllReduce(bar, bar, 1, ncclInt32, ncclSum, comm, s));
     return AEM_OK;
+}
+
+void Ep::release() {
+    for (int r = 0; r < world; ++r)
+        if (mapped[r]) {
+            cudaIpcCloseMemHandle(peers.base[r]);
+            mapped[r] = false;
+        }
 }
 
 aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dtype od,
                        cudaStream_t s) {
-    const int k = cfg.top_k, E = cfg.num_experts, R = world;
+    const int k = cfg.top_k, E = cfg.num_experts, R = world, el = e_loc;
     const int ksel = k < E ? k + 1 : k;
     const int64_t d = cfg.d_model, f = cfg.d_ffn, U = T * k;
+    AEM_REQUIRE(T <= T_cap, "aem_ep_forward: T_local=%lld > max_tokens_local=%lld", (long long)T,
+                (long long)T_cap);
+    const int dev = current_device();
+    const int sms = sm_count(dev);
+    int* err = device_error_word(dev);
+    AEM_REQUIRE(err != nullptr, "aem_ep_forward: no device error word");
     last_T = T;
-    AEM_TRY(loc.reserve(std::max<int64_t>(T, 1)));
-    AEM_TRY(reserve_units(std::max<int64_t>(U, 1)));
     // 1. gating and local per-(slot, expert) counts
     prof.begin(AEM_PHASE_GATING, s);
     if (T > 0)
         AEM_TRY(launch_gating(*gate, x, xd, T, k, ksel, cfg.gating_mode, loc.idx, loc.val, s));
+    const int32_t* ridx = loc.idx;  // routing works on placement positions
+    if (placed && T > 0) {
+        const unsigned g = static_cast<unsigned>(std::min<int64_t>((T * ksel + 255) / 256, 1024));
+        relabel_kernel<<<g, 256, 0, s>>>(loc.idx, T * ksel, pos_of, idx_pos);
+        AEM_CHECK_LAUNCH();
+        count_launches(1);
+        ridx = idx_pos;
+    }
     prof.end(AEM_PHASE_GATING, s);
     prof.begin(AEM_PHASE_EXCHANGE, s);
     AEM_TRY_CUDA(cudaMemsetAsync(cnt, 0, sizeof(unsigned long long) * k * E, s));
     if (T > 0) {
         const unsigned g = static_cast<unsigned>(std::min<int64_t>((U + 255) / 256, 1024));
-        slot_count_kernel<<<g, 256, sizeof(unsigned) * k * E, s>>>(loc.idx, T, ksel, k, E, cnt);
+        slot_count_kernel<<<g, 256, sizeof(unsigned) * k * E, s>>>(ridx, T, ksel, k, E, cnt);
         AEM_CHECK_LAUNCH();
         count_launches(1);
     }
     // 2. all-gather counts -> global rank offsets
-    AEM_TRY_NCCL(::aem::nccl()->AllGather(cnt, cnt_all, static_cast<size_t>(k) * E, ncclInt64, comm, s));
+    AEM_TRY_NCCL(nccl()->AllGather(cnt, cnt_all, static_cast<size_t>(k) * E, ncclInt64, comm, s));
     ep_corr_kernel<<<1, 256, 0, s>>>(cnt_all, R, k, E, rank, corr);
     AEM_CHECK_LAUNCH();
     count_launches(1);
     prof.end(AEM_PHASE_EXCHANGE, s);
-    // 3. capacity routing with global ranks + expert-grouped permutation
+    // 3. capacity routing with global ranks + expert-grouped permutation,
+    //    then the (destination, token) pairs
     prof.begin(AEM_PHASE_ROUTE, s);
     if (T > 0) {
         MoeRouteArgs ra;
-        ra.idx = loc.idx;
+        ra.idx = ridx;
         ra.T = T;
         ra.ldi = ksel;
         ra.k = k;
@@ -291,49 +765,65 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
         ra.src_token = loc.src_token;
         ra.rowmap = loc.rowmap;
         ra.rowscale = loc.rowscale;
-        ra.dest_of = dest_of;
         AEM_TRY(route_moe(ra, s));
-        AEM_TRY(gather_rows(x, xd, loc.src_token, U, d, loc.xperm, s));
     } else {
         AEM_TRY_CUDA(cudaMemsetAsync(loc.starts, 0, sizeof(int) * (E + 1), s));
     }
+    ep_pairs_kernel<<<R, 1024, 0, s>>>(loc.eff, T, k, el, E, loc.starts, pair_local, payload);
+    AEM_CHECK_LAUNCH();
+    count_launches(1);
     prof.end(AEM_PHASE_ROUTE, s);
-    // 4. all-gather per-expert starts; sizes to the host (the one sync)
-    AEM_TRY_NCCL(::aem::nccl()->AllGather(loc.starts, starts_all, static_cast<size_t>(E + 1), ncclInt32, comm, s));
-    AEM_TRY_CUDA(cudaMemcpyAsync(h_starts, starts_all, sizeof(int) * R * (E + 1),
-                                 cudaMemcpyDeviceToHost, s));
-    AEM_TRY_CUDA(cudaStreamSynchronize(s));
-    std::vector<int64_t> send_off(R), send_cnt(R), recv_off(R), recv_cnt(R);
-    AEM_TRY(aem_ep_plan_exchange(h_starts, R, E, rank, send_off.data(), send_cnt.data(),
-                                 recv_off.data(), recv_cnt.data(), h_groups));
-    const int64_t rtot = recv_off[R - 1] + recv_cnt[R - 1];
-    AEM_TRY(reserve_recv(std::max<int64_t>(rtot, 1)));
-    AEM_TRY_CUDA(cudaMemcpyAsync(d_groups, h_groups, sizeof(int) * (R * e_loc + 1),
-                                 cudaMemcpyHostToDevice, s));
-    // 5. dispatch: bf16 rows, grouped by destination rank, to the expert owners
+    // 4. all-gather expert starts + pair counts; every rank plans on the device
+    prof.begin(AEM_PHASE_EXCHANGE, s);
+    AEM_TRY_NCCL(nccl()->AllGather(payload, payload_all, static_cast<size_t>(E + 1 + R), ncclInt32,
+                                   comm, s));
+    ep_plan_kernel<<<1, 1, 0, s>>>(payload_all, R, E, rank, units_cap, pairs_cap, ret_cap, plan,
+                                   groups, err);
+    AEM_CHECK_LAUNCH();
+    count_launches(1);
+    prof.end(AEM_PHASE_EXCHANGE, s);
+    // 5. dispatch: push pair rows and unit metadata into the destinations
     prof.begin(AEM_PHASE_DISPATCH, s);
-    AEM_TRY_NCCL(::aem::nccl()->GroupStart());
-    for (int p = 0; p < R; ++p) {
-        if (send_cnt[p] > 0)
-            AEM_TRY_NCCL(::aem::nccl()->Send(static_cast<char*>(loc.xperm) + 2 * send_off[p] * d,
-                                  send_cnt[p] * d, ncclBfloat16, p, comm, s));
-        if (recv_cnt[p] > 0)
-            AEM_TRY_NCCL(::aem::nccl()->Recv(static_cast<char*>(xr) + 2 * recv_off[p] * d, recv_cnt[p] * d,
-                                  ncclBfloat16, p, comm, s));
+    {
+        const unsigned g = static_cast<unsigned>(sms * 4);
+        if (xd == AEM_BF16)
+            ep_dispatch_kernel<__nv_bfloat16><<<g, kCopyThreads, 0, s>>>(
+                static_cast<const __nv_bfloat16*>(x), T, d, R, el, pair_local, loc.starts,
+                loc.src_token, loc.rowscale, k, plan, peers, lay, units_cap, pairs_cap, err);
+        else
+            ep_dispatch_kernel<float><<<g, kCopyThreads, 0, s>>>(
+                static_cast<const float*>(x), T, d, R, el, pair_local, loc.starts, loc.src_token,
+                loc.rowscale, k, plan, peers, lay, units_cap, pairs_cap, err);
+        AEM_CHECK_LAUNCH();
+        count_launches(1);
     }
-    AEM_TRY_NCCL(::aem::nccl()->GroupEnd());
+    AEM_TRY(barrier(s));
+    {
+        char* mine = static_cast<char*>(xreg);
+        ep_expand_kernel<<<static_cast<unsigned>(sms * 4), kCopyThreads, 0, s>>>(
+            reinterpret_cast<const __nv_bfloat16*>(mine + lay.xpair),
+            reinterpret_cast<int32_t*>(mine + lay.rowmap),
+            reinterpret_cast<float*>(mine + lay.rowscale), plan, d,
+            static_cast<__nv_bfloat16*>(xu), ret_acc, err);
+        AEM_CHECK_LAUNCH();
+        count_launches(1);
+    }
     prof.end(AEM_PHASE_DISPATCH, s);
-    // 6. local expert FFN on the (source, expert) segments
-    if (rtot > 0) {
+    // 6. local expert FFN on the (source, expert) groups; the down GEMM
+    //    scales by the gate weight and sums the units of each pair
+    {
+        char* mine = static_cast<char*>(xreg);
+        const int64_t hint = std::max<int64_t>(U, 1);  // expected received units
         GemmArgs up_a;
         up_a.w = up;
-        up_a.G = R * e_loc;
-        up_a.wmod = e_loc;
-        up_a.group_rows = d_groups;
-        up_a.M = rtot;
-        up_a.max_rows = rtot;
-        up_a.x_hi = xr;
-        up_a.out = hr;
+        up_a.G = R * el;
+        up_a.wmod = el;
+        up_a.group_rows = groups;
+        up_a.M = units_cap;
+        up_a.max_rows = units_cap;
+        up_a.rows_hint = hint;
+        up_a.x_hi = xu;
+        up_a.out = hu;
         up_a.out_bf16 = true;
         up_a.ldo = f;
         up_a.relu = true;
@@ -342,45 +832,46 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
         prof.end(AEM_PHASE_UP, s);
         GemmArgs dn;
         dn.w = down;
-        dn.G = R * e_loc;
-        dn.wmod = e_loc;
-        dn.group_rows = d_groups;
-        dn.M = rtot;
-        dn.max_rows = rtot;
-        dn.x_hi = hr;
-        dn.out = yr;
+        dn.G = R * el;
+        dn.wmod = el;
+        dn.group_rows = groups;
+        dn.M = units_cap;
+        dn.max_rows = units_cap;
+        dn.rows_hint = hint;
+        dn.x_hi = hu;
+        dn.out = ret_acc;
         dn.ldo = d;
+        dn.atomic_add = true;
+        dn.rowmap = reinterpret_cast<const int32_t*>(mine + lay.rowmap);
+        dn.rowscale = reinterpret_cast<const float*>(mine + lay.rowscale);
         prof.begin(AEM_PHASE_DOWN, s);
         AEM_TRY(launch_qgemm(dn, s));
         prof.end(AEM_PHASE_DOWN, s);
     }
-    // 7. expert outputs back to the token owners (same segments, reversed)
+    // 7. pair sums back into the sources
     prof.begin(AEM_PHASE_RETURN, s);
-    AEM_TRY_NCCL(::aem::nccl()->GroupStart());
-    for (int p = 0; p < R; ++p) {
-        if (recv_cnt[p] > 0)
-            AEM_TRY_NCCL(::aem::nccl()->Send(yr + recv_off[p] * d, recv_cnt[p] * d, ncclFloat32, p, comm, s));
-        if (send_cnt[p] > 0)
-            AEM_TRY_NCCL(::aem::nccl()->Recv(yb + send_off[p] * d, send_cnt[p] * d, ncclFloat32, p, comm, s));
-    }
-    AEM_TRY_NCCL(::aem::nccl()->GroupEnd());
+    ep_return_kernel<<<static_cast<unsigned>(sms * 4), kCopyThreads, 0, s>>>(
+        ret_acc, plan, R, d, peers, lay, ret_cap, err);
+    AEM_CHECK_LAUNCH();
+    count_launches(1);
+    AEM_TRY(barrier(s));
     prof.end(AEM_PHASE_RETURN, s);
-    // 8. weighted combine in token order
+    // 8. per-token sum over destination ranks
     prof.begin(AEM_PHASE_COMBINE, s);
     if (T > 0) {
-        const unsigned g = static_cast<unsigned>(std::min<int64_t>((T * d + 255) / 256, 148 * 16));
+        const float* ret_in = reinterpret_cast<const float*>(static_cast<char*>(xreg) + lay.ret);
+        const unsigned g = static_cast<unsigned>(std::min<int64_t>((T + 7) / 8, sms * 8));
         if (od == AEM_BF16)
-            combine_gather_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(
-                yb, dest_of, loc.val, T, k, d, static_cast<__nv_bfloat16*>(out));
+            ep_combine_kernel<__nv_bfloat16><<<g, kCopyThreads, 0, s>>>(
+                ret_in, pair_local, plan, T, R, d, static_cast<__nv_bfloat16*>(out));
         else
-            combine_gather_kernel<float><<<g, 256, 0, s>>>(yb, dest_of, loc.val, T, k, d,
-                                                           static_cast<float*>(out));
+            ep_combine_kernel<float><<<g, kCopyThreads, 0, s>>>(ret_in, pair_local, plan, T, R, d,
+                                                                static_cast<float*>(out));
         AEM_CHECK_LAUNCH();
         count_launches(1);
     }
     prof.end(AEM_PHASE_COMBINE, s);
     prof.step();
-    (void)nccl_dtype;
     return AEM_OK;
 }
 
@@ -437,6 +928,16 @@ aem_status aem_ep_plan_exchange(const int32_t* starts, int R, int E, int rank, i
     return AEM_OK;
 }
 
+aem_status aem_ep_plan_peer(const int32_t* all, int R, int E, int rank, int64_t units_cap,
+                            int64_t pairs_cap, int64_t ret_cap, aem_ep_peer_plan* plan,
+                            int32_t* groups) {
+    AEM_REQUIRE(all && plan && groups, "aem_ep_plan_peer: NULL buffer");
+    AEM_REQUIRE(R >= 1 && R <= AEM_EP_MAX_RANKS && E >= R && E % R == 0 && rank >= 0 && rank < R,
+                "aem_ep_plan_peer: bad R=%d E=%d rank=%d", R, E, rank);
+    aem::plan_peer(all, R, E, rank, units_cap, pairs_cap, ret_cap, plan, groups);
+    return AEM_OK;
+}
+
 aem_status aem_ep_unique_id(uint8_t out[128]) {
     AEM_REQUIRE(out != nullptr, "aem_ep_unique_id: out is NULL");
     static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId size");
@@ -447,16 +948,29 @@ aem_status aem_ep_unique_id(uint8_t out[128]) {
     return AEM_OK;
 }
 
+static void ep_destroy(aem::Ep* ep) {
+    ep->release();
+    if (ep->comm && aem::nccl()) aem::nccl()->CommDestroy(ep->comm);
+    cudaFree(ep->xreg);
+    cudaFree(ep->lbuf);
+    cudaFree(ep->loc.buf);
+    delete ep;
+}
+
 aem_status aem_ep_create(const aem_moe_config* cfg, int rank, int world, const uint8_t uid[128],
                          aem_gate_t gate, aem_qweight_t up_local, aem_qweight_t down_local,
-                         aem_ep_t* out) {
+                         const int32_t* expert_to_rank, int64_t max_tokens_local, aem_ep_t* out) {
     AEM_REQUIRE(out != nullptr, "aem_ep_create: out is NULL");
     *out = nullptr;
     AEM_REQUIRE(cfg && uid && gate && up_local && down_local, "aem_ep_create: NULL argument");
-    AEM_REQUIRE(world >= 1 && rank >= 0 && rank < world, "aem_ep_create: bad rank %d / world %d",
-                rank, world);
+    AEM_REQUIRE(world >= 1 && world <= AEM_EP_MAX_RANKS && rank >= 0 && rank < world,
+                "aem_ep_create: bad rank %d / world %d (at most %d ranks)", rank, world,
+                AEM_EP_MAX_RANKS);
     AEM_REQUIRE(cfg->num_experts % world == 0,
                 "aem_ep_create: num_experts=%d not divisible by world=%d", cfg->num_experts, world);
+    AEM_REQUIRE(max_tokens_local >= 1, "aem_ep_create: max_tokens_local must be >= 1");
+    AEM_REQUIRE(cfg->d_model % 8 == 0, "aem_ep_create: d_model=%lld must be a multiple of 8",
+                (long long)cfg->d_model);
     auto* g = reinterpret_cast<aem::Gate*>(gate);
     auto* u = reinterpret_cast<aem::QWeight*>(up_local);
     auto* dn = reinterpret_cast<aem::QWeight*>(down_local);
@@ -469,8 +983,24 @@ aem_status aem_ep_create(const aem_moe_config* cfg, int rank, int world, const u
                 (long long)cfg->d_model, (long long)cfg->d_ffn);
     AEM_REQUIRE(dn->G == e_loc && dn->K == cfg->d_ffn && dn->N == cfg->d_model,
                 "aem_ep_create: down weight shape");
+    std::vector<int32_t> pos(cfg->num_experts);
+    bool placed = false;
+    {
+        std::vector<int> fill(world, 0);
+        for (int e = 0; e < cfg->num_experts; ++e) {
+            const int r = expert_to_rank ? expert_to_rank[e] : e / e_loc;
+            AEM_REQUIRE(r >= 0 && r < world, "aem_ep_create: expert_to_rank[%d]=%d outside [0, %d)",
+                        e, r, world);
+            AEM_REQUIRE(fill[r] < e_loc, "aem_ep_create: rank %d is given more than %d experts", r,
+                        e_loc);
+            pos[e] = r * e_loc + fill[r]++;
+            placed |= pos[e] != e;
+        }
+    }
     AEM_NCCL_OR_FAIL();
     auto* ep = new aem::Ep();
+    ep->h_pos = pos;
+    ep->placed = placed;
     ep->cfg = *cfg;
     ep->rank = rank;
     ep->world = world;
@@ -492,10 +1022,19 @@ aem_status aem_ep_create(const aem_moe_config* cfg, int rank, int world, const u
         delete ep;
         return AEM_ENCCL;
     }
-    aem_status st = ep->init_buffers();
+    aem_status st = ep->init(max_tokens_local);
+    if (st == AEM_OK) {
+        cudaStream_t s = nullptr;
+        if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) {
+            set_error("aem_ep_create: cudaStreamCreate failed");
+            st = AEM_ECUDA;
+        } else {
+            st = ep->map_peers(s);
+            cudaStreamDestroy(s);
+        }
+    }
     if (st != AEM_OK) {
-        ::aem::nccl()->CommDestroy(ep->comm);
-        delete ep;
+        ep_destroy(ep);
         return st;
     }
     *out = reinterpret_cast<aem_ep_t>(ep);
@@ -507,22 +1046,20 @@ aem_status aem_ep_free(aem_ep_t h) {
     auto* ep = reinterpret_cast<aem::Ep*>(h);
     cudaSetDevice(ep->device);
     cudaDeviceSynchronize();
-    if (ep->comm && aem::nccl()) aem::nccl()->CommDestroy(ep->comm);
-    cudaFree(ep->cnt);
-    cudaFree(ep->cnt_all);
-    cudaFree(ep->corr);
-    cudaFree(ep->starts_all);
-    cudaFree(ep->dest_of);
-    cudaFree(ep->d_groups);
-    cudaFree(ep->xr);
-    cudaFree(ep->hr);
-    cudaFree(ep->yr);
-    cudaFree(ep->yb);
-    cudaFree(ep->loc.buf);
-    cudaFreeHost(ep->h_starts);
-    cudaFreeHost(ep->h_groups);
-    delete ep;
-    return AEM_OK;
+    // Collective: nobody unmaps or frees until every rank's last step ended,
+    // and nobody frees its region while a peer still maps it.
+    cudaStream_t s = nullptr;
+    aem_status st = AEM_OK;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess) {
+        st = ep->barrier(s);
+        if (st == AEM_OK) cudaStreamSynchronize(s);
+        ep->release();
+        if (st == AEM_OK) st = ep->barrier(s);
+        if (st == AEM_OK) cudaStreamSynchronize(s);
+        cudaStreamDestroy(s);
+    }
+    ep_destroy(ep);
+    return st;
 }
 
 aem_status aem_ep_forward(aem_ep_t h, const void* x, aem_dtype x_dtype, int64_t T_local, void* out,
@@ -530,6 +1067,8 @@ aem_status aem_ep_forward(aem_ep_t h, const void* x, aem_dtype x_dtype, int64_t 
     AEM_REQUIRE(h != nullptr, "aem_ep_forward: NULL layer");
     AEM_REQUIRE(T_local >= 0 && T_local < (1ll << 28), "aem_ep_forward: T out of range");
     AEM_REQUIRE(T_local == 0 || (x && out), "aem_ep_forward: NULL buffer");
+    AEM_REQUIRE(x_dtype == AEM_F32 || x_dtype == AEM_BF16, "aem_ep_forward: bad x dtype");
+    AEM_REQUIRE(out_dtype == AEM_F32 || out_dtype == AEM_BF16, "aem_ep_forward: bad out dtype");
     auto* ep = reinterpret_cast<aem::Ep*>(h);
     return ep->forward(x, x_dtype, T_local, out, out_dtype, static_cast<cudaStream_t>(stream));
 }
@@ -560,9 +1099,17 @@ aem_status aem_ep_last_routing(aem_ep_t h, int32_t* idx, float* val, uint32_t* e
     if (val)
         AEM_TRY_CUDA(cudaMemcpyAsync(val, ep->loc.val, sizeof(float) * T * k,
                                      cudaMemcpyDeviceToDevice, s));
-    if (effective)
-        AEM_TRY_CUDA(cudaMemcpyAsync(effective, ep->loc.eff, sizeof(uint32_t) * T * k,
-                                     cudaMemcpyDeviceToDevice, s));
+    if (effective) {
+        if (ep->placed) {
+            const unsigned g = static_cast<unsigned>(std::min<int64_t>((T * k + 255) / 256, 1024));
+            aem::unlabel_kernel<<<g, 256, 0, s>>>(ep->loc.eff, T * k, ep->expert_at, effective);
+            AEM_CHECK_LAUNCH();
+            aem::count_launches(1);
+        } else {
+            AEM_TRY_CUDA(cudaMemcpyAsync(effective, ep->loc.eff, sizeof(uint32_t) * T * k,
+                                         cudaMemcpyDeviceToDevice, s));
+        }
+    }
     return AEM_OK;
 }
 

@@ -157,7 +157,7 @@ aem_status combine_rows(const float* y, int64_t T, int k, int64_t d, void* out, 
 }
 
 // ------------------------------------------------------------------ Moe
-aem_status Moe::reserve(int64_t T) {
+aem_status Moe::reserve(int64_t T, bool expert_buffers) {
     if (T <= T_cap && buf) return AEM_OK;
     if (buf) {
         cudaDeviceSynchronize();
@@ -181,9 +181,10 @@ aem_status Moe::reserve(int64_t T) {
     const size_t o_src = slot(sizeof(int32_t) * U);
     const size_t o_map = slot(sizeof(int32_t) * U);
     const size_t o_rs = slot(sizeof(float) * U);
-    const size_t o_x = slot(2 * U * d);
-    const size_t o_h = slot(2 * U * f);
-    const size_t o_y = slot(sizeof(float) * U * d);
+    const int64_t Ux = expert_buffers ? U : 0;
+    const size_t o_x = slot(2 * Ux * d);
+    const size_t o_h = slot(2 * Ux * f);
+    const size_t o_y = slot(sizeof(float) * Ux * d);
     AEM_TRY_CUDA(cudaMalloc(&buf, off));
     char* b = static_cast<char*>(buf);
     idx = reinterpret_cast<int32_t*>(b + o_idx);
@@ -194,9 +195,9 @@ aem_status Moe::reserve(int64_t T) {
     src_token = reinterpret_cast<int32_t*>(b + o_src);
     rowmap = reinterpret_cast<int32_t*>(b + o_map);
     rowscale = reinterpret_cast<float*>(b + o_rs);
-    xperm = b + o_x;
-    h = b + o_h;
-    y = reinterpret_cast<float*>(b + o_y);
+    xperm = expert_buffers ? b + o_x : nullptr;
+    h = expert_buffers ? b + o_h : nullptr;
+    y = expert_buffers ? reinterpret_cast<float*>(b + o_y) : nullptr;
     T_cap = T;
     return AEM_OK;
 }

@@ -36,7 +36,9 @@ struct Moe {
     float* y = nullptr;     // f32 [T*k, d]
     PhaseProfiler prof;
 
-    aem_status reserve(int64_t T);
+    // Routing buffers for T tokens, plus the expert-FFN buffers (xperm, h, y)
+    // unless expert_buffers is false (the expert-parallel layer has its own).
+    aem_status reserve(int64_t T, bool expert_buffers = true);
     aem_status forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dtype od,
                        cudaStream_t s);
     // Grouped up GEMM + ReLU, grouped down GEMM (scaled by the gate weight,

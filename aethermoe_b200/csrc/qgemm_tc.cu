@@ -540,9 +540,10 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
 
     int bt = a.token_tile;
     if (bt == 0) {
-        const int64_t avg = (a.M + a.G - 1) / a.G;
+        const int64_t m = a.rows_hint > 0 ? a.rows_hint : a.M;
+        const int64_t avg = (m + a.G - 1) / a.G;
         bt = avg <= 16 ? 16 : avg <= 32 ? 32 : avg <= 64 ? 64 : avg <= 128 ? 128 : 256;
-        while (bt > 64 && tiles_estimate(a.M, a.G, bt, nch, 1) < 2 * sms) bt >>= 1;
+        while (bt > 64 && tiles_estimate(m, a.G, bt, nch, 1) < 2 * sms) bt >>= 1;
     }
     int ks = a.ksplit < 1 ? 1 : a.ksplit;
     if (ks > nkt) ks = static_cast<int>(nkt);

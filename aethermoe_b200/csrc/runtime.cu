@@ -111,6 +111,11 @@ aem_status check_device_errors(cudaStream_t stream, const char* what) {
         set_error("%s: expert id out of range (error bits 0x%x)", what, bits);
         return AEM_EDEVICE;
     }
+    if (bits & ERR_EP_PLAN) {
+        set_error("%s: expert-parallel step exceeds the receive capacity (error bits 0x%x)",
+                  what, bits);
+        return AEM_EDEVICE;
+    }
     set_error("%s: in-kernel check failed (error bits 0x%x)", what, bits);
     return AEM_EDEVICE;
 }

@@ -110,6 +110,8 @@ struct GemmArgs {
     const int* rowmap = nullptr;    // output row of activation row r (nullable)
     const float* rowscale = nullptr;  // per-activation-row multiplier (nullable)
     int token_tile = 0;        // 0 = choose from average rows per group
+    int64_t rows_hint = 0;     // expected rows when the group sizes live only on the
+                               // device (0 = use M); only picks the token tile
 };
 aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s);
 

@@ -167,11 +167,37 @@ def ep_plan_exchange(starts, rank):
     return so, sc, ro, rc, groups
 
 
+def ep_plan_peer(payload, rank, units_cap, pairs_cap, ret_cap):
+    """Host form of the per-step peer-exchange plan: ``payload [R, E+1+R]``
+    (every rank's expert starts, then its pair counts per destination) ->
+    ``(plan dict, groups [E+1])`` for ``rank``."""
+    pay = np.ascontiguousarray(payload, dtype=np.int32)
+    r, w = pay.shape
+    e = w - 1 - r
+    plan = _lib.EpPeerPlan()
+    groups = np.zeros(e + 1, np.int32)
+    _lib.check(_lib.lib().aem_ep_plan_peer(pay.ctypes.data, r, e, rank, units_cap, pairs_cap,
+                                           ret_cap, ctypes.byref(plan), groups.ctypes.data),
+               "aem_ep_plan_peer")
+    out = dict(ok=plan.ok, units_in=plan.units_in, pairs_in=plan.pairs_in,
+               pairs_out=plan.pairs_out)
+    for name in ("dst_unit_off", "dst_pair_off", "send_pair_off", "ret_off"):
+        out[name] = np.array(getattr(plan, name)[:r], np.int64)
+    out["recv_pair_off"] = np.array(plan.recv_pair_off[:r + 1], np.int64)
+    return out, groups
+
+
 class EPLayer:
-    """One rank of the expert-parallel MoE layer (experts split contiguously over ranks)."""
+    """One rank of the expert-parallel MoE layer (experts split contiguously over ranks).
+
+    Collective: every rank constructs it with the same config, placement and
+    ``max_tokens`` (the most tokens one rank passes to one ``forward``).
+    ``expert_to_rank`` [E] places the experts (None = contiguous blocks); the
+    local weights hold this rank's experts in increasing expert id."""
 
     def __init__(self, uid, rank, world, gate_w, gate_b, q_up_local, s_up_local, q_down_local,
-                 s_down_local, top_k, capacity=None, gating_mode=_lib.GATING_EXACT, device=0):
+                 s_down_local, top_k, capacity=None, gating_mode=_lib.GATING_EXACT, device=0,
+                 max_tokens=16384, expert_to_rank=None):
         gate_w = np.asarray(gate_w, np.float32)
         d, e = gate_w.shape
         eloc = e // world
@@ -188,10 +214,17 @@ class EPLayer:
                                      np.asarray(s_down_local, np.float32).reshape(eloc, d), device)
         self.cfg = make_config(d, ffn, e, top_k, capacity, gating_mode)
         uid_buf = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
+        place = None
+        if expert_to_rank is not None:
+            self._place = np.ascontiguousarray(expert_to_rank, dtype=np.int32)
+            if self._place.shape != (e,):
+                raise ValueError(f"expert_to_rank must have {e} entries")
+            place = self._place.ctypes.data
         h = _vp()
         _lib.check(_lib.lib().aem_ep_create(ctypes.byref(self.cfg), rank, world, uid_buf,
                                             self.gate.handle, self.up.handle, self.down.handle,
-                                            ctypes.byref(h)), "aem_ep_create")
+                                            place, int(max_tokens), ctypes.byref(h)),
+                   "aem_ep_create")
         self.handle = h.value
         self.d_model, self.num_experts, self.top_k = d, e, top_k
 

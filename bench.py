@@ -328,10 +328,11 @@ def run_ours(args):
     tokens = args.tokens
     assert tokens % world == 0 and E % world == 0
     tl = tokens // world
-    eloc = E // world
     cap = capacity(tokens)
     gw, gb = gate_weights()
-    up, down, qlists = expert_weights(range(rank * eloc, (rank + 1) * eloc), dev)
+    # round-robin placement (expert e on rank e % R): the Zipf-skewed load of
+    # the hot low-id experts spreads over all ranks
+    up, down, qlists = expert_weights(range(rank, E, world), dev)
     torch.cuda.synchronize()
     if world == 1:
         layer = MoELayer(gw, gb, up, None, down, None, K_TOP, capacity=cap, device=local)
@@ -341,7 +342,8 @@ def run_ours(args):
             uid.copy_(torch.frombuffer(bytearray(ep_unique_id()), dtype=torch.uint8))
         dist.broadcast(uid, 0)
         layer = EPLayer(bytes(uid.cpu().numpy()), rank, world, gw, gb, up, None, down, None,
-                        K_TOP, capacity=cap, device=local)
+                        K_TOP, capacity=cap, device=local, max_tokens=tl,
+                        expert_to_rank=[e % world for e in range(E)])
     xs = token_buffers(dev, tokens, rank, world)
     outs = [torch.empty((tl, D_MODEL), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     stream = torch.cuda.current_stream()
@@ -410,6 +412,7 @@ def run_ours(args):
             "dtype": "bf16", "data": "synthetic",
             "config": {"workload": workload_name(tokens), "tokens_per_step": tokens,
                        "global_batch": tokens, "parallelism": f"ep{world}",
+                       "expert_placement": "round-robin (expert e on rank e % R)",
                        "l2": (f"inputs rotate over {N_INPUT_BUFFERS} buffers "
                               f"({N_INPUT_BUFFERS * tokens * D_MODEL * 2 >> 20} MiB > 126 MiB L2); "
                               "per-step working set > 1 GiB")},

@@ -98,7 +98,9 @@ void* aem_context_stream(aem_context_t ctx);
 typedef struct aem_gate_s* aem_gate_t;
 
 /* Packs a gating layer: gate_weight [D, E] and gate_bias [E] float32 from
- * HOST memory into a device-resident expert-major [E, D] copy.
+ * HOST memory into a device-resident copy laid out [ceil(D/4)][Epad][4]
+ * (Epad = E rounded up to 8..256): every 4 consecutive d of one expert are one
+ * 16-byte vector, and one chunk of d is contiguous for all experts.
  * Replaces _get_transposed_weight, src/kernels/fused_gating_metal.py:328-344
  * (the cached [E, D] transpose), with caller-owned lifetime.
  * gate_bias may be NULL (zero bias).  E <= AEM_MAX_EXPERTS. */
@@ -289,23 +291,64 @@ aem_status aem_ep_plan_exchange(const int32_t* starts, int R, int E, int rank, i
                                 int64_t* send_cnt, int64_t* recv_off, int64_t* recv_cnt,
                                 int32_t* groups);
 
+/* Largest expert-parallel world (ranks that map each other's memory). */
+#define AEM_EP_MAX_RANKS 64
+
+/* Where one rank's rows go in the peer-memory exchange of one step.  Units
+ * are (token, slot) rows; pairs are (token, destination rank) rows -- a
+ * token's activation crosses NVLink once per destination rank, and the
+ * destination returns one pre-reduced float32 row per pair. */
+typedef struct aem_ep_peer_plan {
+    int32_t ok;         /* 1 when every rank's segments fit the receive capacities */
+    int32_t units_in;   /* units this rank receives (rows of its grouped GEMMs) */
+    int32_t pairs_in;   /* pairs this rank receives */
+    int32_t pairs_out;  /* pairs this rank sends (rows of its return buffer) */
+    int32_t dst_unit_off[AEM_EP_MAX_RANKS];      /* this rank's first unit row in rank r's buffer */
+    int32_t dst_pair_off[AEM_EP_MAX_RANKS];      /* this rank's first pair row in rank r's buffer */
+    int32_t send_pair_off[AEM_EP_MAX_RANKS];     /* this rank's pairs for rank r start here */
+    int32_t recv_pair_off[AEM_EP_MAX_RANKS + 1]; /* pairs received from source s start here */
+    int32_t ret_off[AEM_EP_MAX_RANKS];           /* row in s's return buffer of s's first pair here */
+} aem_ep_peer_plan;
+
+/* Host form of the per-step plan the expert-parallel layer computes on the
+ * device (no GPU needed).  all: [R][E+1+R] int32, every rank's expert
+ * starts [E+1] followed by its pair counts per destination rank [R].
+ * Capacities: units_cap (received units), pairs_cap (received pairs),
+ * ret_cap (return rows), the same on every rank.  Writes the plan of `rank`
+ * and groups [E+1] (R*(E/R) = E row groups): the row offsets of the
+ * received (source, local expert) segments, sources outer.  A plan whose counts do not fit
+ * has ok = 0 (every rank derives the same verdict from the same data). */
+aem_status aem_ep_plan_peer(const int32_t* all, int R, int E, int rank, int64_t units_cap,
+                            int64_t pairs_cap, int64_t ret_cap, aem_ep_peer_plan* plan,
+                            int32_t* groups);
+
 /* NCCL unique id (128 bytes) for aem_ep_create; made on one rank and
  * broadcast by the caller. */
 aem_status aem_ep_unique_id(uint8_t out[128]);
 
 typedef struct aem_ep_s* aem_ep_t;
 
-/* One rank of an expert-parallel MoE layer: experts are split contiguously,
- * E/R per rank (tests/test_orchestration.cpp:25-33 expert->shard map);
- * `up_local`/`down_local` hold this rank's E/R experts.  Replaces the
+/* One rank of an expert-parallel MoE layer: E/R experts per rank, placed by
+ * expert_to_rank [E] (the reference Router's expert_to_shard,
+ * router.hpp:55-60; NULL = contiguous blocks, e / (E/R), the map of
+ * tests/test_orchestration.cpp:25-33).  `up_local`/`down_local` hold this
+ * rank's experts in increasing expert id.  Routing does not depend on the
+ * placement (bit-exact either way); load balance does.  Replaces the
  * Router + ICollectiveTransport scatter/gather (router.hpp:67-100,
- * collective_transport.hpp:37-51) with NCCL over NVLink. */
+ * collective_transport.hpp:37-51): activations and expert outputs move by
+ * stores into the peers' memory over NVLink (CUDA IPC, mapped once here),
+ * NCCL carries the small per-step all-gathers and barriers.  Collective:
+ * every rank calls it with the same config and max_tokens_local, the most
+ * tokens any rank passes to one aem_ep_forward (receive buffers are sized
+ * for the worst case, so a step never allocates). */
 aem_status aem_ep_create(const aem_moe_config* cfg, int rank, int world, const uint8_t uid[128],
                          aem_gate_t gate, aem_qweight_t up_local, aem_qweight_t down_local,
-                         aem_ep_t* out);
+                         const int32_t* expert_to_rank, int64_t max_tokens_local, aem_ep_t* out);
 aem_status aem_ep_free(aem_ep_t ep);
 /* One step: this rank's T_local tokens (global positions rank*T_local ...)
- * -> its outputs.  Collective: every rank calls it with the same T_local. */
+ * -> its outputs.  Collective: every rank calls it with the same T_local
+ * (<= max_tokens_local).  Asynchronous on `stream` (no host synchronisation);
+ * a receive-capacity or peer failure is reported by aem_device_status. */
 aem_status aem_ep_forward(aem_ep_t ep, const void* x, aem_dtype x_dtype, int64_t T_local, void* out,
                           aem_dtype out_dtype, void* stream);
 /* Per-phase profiling of this rank's steps (see aem_moe_profile). */

@@ -1,7 +1,7 @@
 """Expert-parallel MoE layer over NCCL on 2+ GPUs vs the single-process oracle.
 
-One process per GPU (spawned here), experts split contiguously, tokens split
-contiguously.  The routing of every (token, slot) unit must equal the
+One process per GPU (spawned here), experts placed in contiguous blocks or
+round-robin (expert e on rank e % R), tokens split contiguously.  The routing of every (token, slot) unit must equal the
 capacity rule applied to the GLOBAL batch (bit-exact, the contract of
 Router::assign_effective_experts in src/orchestration/router.hpp:249-266),
 and every output row must match the float64 layer oracle within the layer
@@ -34,7 +34,14 @@ def _weights(seed, e, d, f):
     return gw, gb, qu, su, qd, sd, x
 
 
-def _worker(rank, world, port, outdir):
+def _local_experts(rank, world, E, placement):
+    if placement == "strided":
+        return np.arange(rank, E, world), np.arange(E) % world
+    el = E // world
+    return np.arange(rank * el, (rank + 1) * el), None
+
+
+def _worker(rank, world, port, outdir, placement):
     import datetime
     import torch
     import torch.distributed as dist
@@ -47,25 +54,28 @@ def _worker(rank, world, port, outdir):
     T, d, f, E, k = CFG["T"], CFG["d"], CFG["f"], CFG["E"], CFG["k"]
     cap = O.default_capacity(T, k, E)
     gw, gb, qu, su, qd, sd, x = _weights(7, E, d, f)
-    el = E // world
     uid = torch.zeros(128, dtype=torch.uint8, device=dev)
     if rank == 0:
         uid.copy_(torch.frombuffer(bytearray(ep_unique_id()), dtype=torch.uint8))
     dist.broadcast(uid, 0)
-    lo, hi = rank * el, (rank + 1) * el
-    layer = EPLayer(bytes(uid.cpu().numpy()), rank, world, gw, gb, qu[lo:hi], su[lo:hi],
-                    qd[lo:hi], sd[lo:hi], k, capacity=cap, device=rank)
+    mine, place = _local_experts(rank, world, E, placement)
     tl = T // world
+    layer = EPLayer(bytes(uid.cpu().numpy()), rank, world, gw, gb, qu[mine], su[mine],
+                    qd[mine], sd[mine], k, capacity=cap, device=rank, max_tokens=tl,
+                    expert_to_rank=place)
     bits = (x[rank * tl:(rank + 1) * tl].view(np.uint32) >> 16).astype(np.uint16)
     xt = torch.from_numpy(bits.view(np.int16)).to(dev).view(torch.bfloat16)
     outs = []
-    for _ in range(2):  # two steps: the second reuses the grown buffers
+    for _ in range(2):  # two steps through the same exchange buffers
         outs.append(layer.forward(xt, out_dtype=torch.float32))
     idx, val, eff = layer.last_routing(tl)
+    ob = layer.forward(xt, out_dtype=torch.bfloat16)  # bf16 output of the same step
     torch.cuda.synchronize()
+    from aethermoe_b200 import _lib
+    _lib.check(_lib.lib().aem_device_status(None), "aem_device_status")
     np.savez(os.path.join(outdir, f"rank{rank}.npz"), out=outs[-1].cpu().numpy(),
              out0=outs[0].cpu().numpy(), idx=idx.cpu().numpy(), val=val.cpu().numpy(),
-             eff=eff.cpu().numpy())
+             eff=eff.cpu().numpy(), outb=ob.float().cpu().numpy())
     layer.close()
     dist.barrier()
     dist.destroy_process_group()
@@ -77,8 +87,9 @@ def _free_port():
         return s.getsockname()[1]
 
 
+@pytest.mark.parametrize("placement", ["contiguous", "strided"])
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_expert_parallel_matches_global_oracle(cuda, world):
+def test_expert_parallel_matches_global_oracle(cuda, world, placement):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < world:
@@ -86,7 +97,7 @@ def test_expert_parallel_matches_global_oracle(cuda, world):
     T, d, f, E, k = CFG["T"], CFG["d"], CFG["f"], CFG["E"], CFG["k"]
     with tempfile.TemporaryDirectory() as outdir:
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        mp.start_processes(_worker, args=(world, _free_port(), outdir), nprocs=world,
+        mp.start_processes(_worker, args=(world, _free_port(), outdir, placement), nprocs=world,
                            join=True, start_method="spawn")
         res = [np.load(os.path.join(outdir, f"rank{r}.npz")) for r in range(world)]
     tl = T // world
@@ -105,3 +116,5 @@ def test_expert_parallel_matches_global_oracle(cuda, world):
     err = np.abs(out.astype(np.float64) - ref)
     assert np.all(err <= 1e-3 + 1e-3 * np.abs(ref)), err.max()
     np.testing.assert_allclose(np.concatenate([r["out0"] for r in res]), out, rtol=0, atol=1e-5)
+    outb = np.concatenate([r["outb"] for r in res])  # bf16 rounding of the same sums
+    assert np.all(np.abs(outb - out) <= 2.0 ** -8 * np.abs(out) + 1e-6)
