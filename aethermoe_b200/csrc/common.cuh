@@ -55,7 +55,10 @@ enum : int {
     ERR_GEMM_GROUPS = 1 << 3,     // group table inconsistent
     ERR_EP_PLAN = 1 << 4,         // expert-parallel counts do not fit the receive buffers
     ERR_EP_BOUNDS = 1 << 5,       // expert-parallel row index outside its buffer (skipped)
+    ERR_EP_PEER_TIMEOUT = 1 << 6, // a peer rank did not signal within the deadline
+    ERR_EP_PEER_FAILED = 1 << 7,  // a peer rank signalled that its step failed
 };
+
 
 // Device int that kernels atomicOr error bits into (one per device, lazily
 // allocated, zero-initialised).  Returns nullptr on allocation failure.
@@ -89,6 +92,16 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
+}
+
+// System-scope acquire load / release store (flags written by peer GPUs).
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 // ---- mbarrier

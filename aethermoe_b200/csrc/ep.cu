@@ -1,8 +1,10 @@
-// Expert-parallel MoE layer: one process per GPU, activations and expert
-// outputs exchanged by stores into the peers' memory over NVLink/NVSwitch.
+// Expert-parallel MoE layer: one process per GPU, activations, expert
+// outputs and the step's small all-gathers and barriers exchanged by stores
+// into the peers' memory over NVLink/NVSwitch.
 //
 // Replaces the reference's Router scatter/gather over ICollectiveTransport
-// (src/orchestration/router.hpp:67-100, collective_transport.hpp:37-51): the
+// (src/orchestration/router.hpp:67-100, collective_transport.hpp:37-51) and
+// its tolerant variant (route_batch_tolerant, router.hpp:127-234): the
 // routing decision stays Router::assign_effective_experts (router.hpp:249-266)
 // and is bit-exact with a single-process run over the global batch, because
 // every rank ranks its units by GLOBAL batch_position:
@@ -18,20 +20,28 @@
 //   units  -- (token, slot): the destination gets, per unit, the row of its
 //             pair and its gate weight, at the unit's row in the destination's
 //             (source, expert)-grouped layout.
-//   Step: gating -> slot counts -> all-gather -> capacity routing (global
-//   ranks) -> pair numbering -> all-gather of expert starts + pair counts ->
-//   on-device plan -> push pairs + unit metadata into the destinations ->
-//   barrier -> expand pairs to units -> grouped up GEMM (+ReLU) -> grouped down
-//   GEMM, gate-weighted and pre-reduced per pair -> push the pair sums back
-//   into the sources -> barrier -> per-token sum over destination ranks.
+//   Step: gating -> slot counts -> [all-gather] -> capacity routing (global
+//   ranks) -> pair numbering -> [all-gather of expert starts + pair counts]
+//   -> on-device plan -> push pairs + unit metadata into the destinations ->
+//   [barrier] -> expand pairs to units -> grouped up GEMM (+ReLU) -> grouped
+//   down GEMM, gate-weighted and pre-reduced per pair -> push the pair sums
+//   back into the sources -> [barrier] -> per-token sum over destinations.
+// The bracketed steps are peer-memory mailboxes and per-step flags: a rank
+// writes its payload into every live peer's mailbox, then a flag holding
+// (step << 1 | failed) with a system-scope release; a waiter spins on its own
+// copy of the flags with a deadline.  A peer that stays silent is recorded
+// as suspect and fails the step; a failed step is signalled onward in the
+// flags, so every rank that takes part fails it too and every unit of it
+// resolves to exactly one outcome (the tolerant contract).
 // Receive buffers are sized for the worst case at creation and mapped by
-// every peer once (CUDA IPC), so a step never allocates or re-maps.  NCCL
-// carries only the two small all-gathers and the two barriers.
+// every peer once (CUDA IPC), so a step never allocates or re-maps.  NCCL only
+// bootstraps the mapping and tears it down.
 #include <cuda_bf16.h>
 #include <dlfcn.h>
 #include <nccl.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -51,6 +61,7 @@ struct NcclApi {
     decltype(&::ncclGetUniqueId) GetUniqueId = nullptr;
     decltype(&::ncclCommInitRank) CommInitRank = nullptr;
     decltype(&::ncclCommDestroy) CommDestroy = nullptr;
+    decltype(&::ncclCommAbort) CommAbort = nullptr;
     decltype(&::ncclAllGather) AllGather = nullptr;
     decltype(&::ncclAllReduce) AllReduce = nullptr;
     decltype(&::ncclGetErrorString) GetErrorString = nullptr;
@@ -83,6 +94,7 @@ static const NcclApi* nccl() {
         sym(g_nccl.GetUniqueId, "ncclGetUniqueId");
         sym(g_nccl.CommInitRank, "ncclCommInitRank");
         sym(g_nccl.CommDestroy, "ncclCommDestroy");
+        sym(g_nccl.CommAbort, "ncclCommAbort");
         sym(g_nccl.AllGather, "ncclAllGather");
         sym(g_nccl.AllReduce, "ncclAllReduce");
         sym(g_nccl.GetErrorString, "ncclGetErrorString");
@@ -113,36 +125,42 @@ static const NcclApi* nccl() {
 
 namespace aem {
 
-// Per-step plan of one rank (see aem_ep_peer_plan).  `all` is [R][E+1+R]:
-// every rank's expert starts, then its pair counts per destination.  Every
-// rank runs this on the same all-gathered data, so all agree on `ok`.
-__host__ __device__ inline void plan_peer(const int32_t* all, int R, int E, int me, int64_t ucap,
-                                          int64_t pcap, int64_t rcap, aem_ep_peer_plan* pl,
-                                          int32_t* groups) {
-    const int W = E + 1 + R;
+// Per-step plan of one rank (see aem_ep_peer_plan).  Row s of `all` (stride
+// `ld` int32) holds rank s's expert starts [E+1], then its pair counts per
+// destination [R].  Only ranks in `live` take part: other rows are ignored,
+// and units or pairs addressed to other ranks count as absent.  Every rank
+// runs this on the same data, so all agree on `ok`.
+__host__ __device__ inline void plan_peer(const int32_t* all, int ld, int R, int E, int me,
+                                          uint64_t live, int64_t ucap, int64_t pcap, int64_t rcap,
+                                          aem_ep_peer_plan* pl, int32_t* groups) {
     const int el = E / R;
-    bool ok = true;
+    auto in = [&](int r) { return ((live >> r) & 1ull) != 0; };
+    auto row = [&](int s) { return all + static_cast<int64_t>(s) * ld; };
+    auto units = [&](int s, int r) -> int64_t {
+        return (in(s) && in(r)) ? row(s)[(r + 1) * el] - row(s)[r * el] : 0;
+    };
+    auto pairs = [&](int s, int r) -> int64_t { return (in(s) && in(r)) ? row(s)[E + 1 + r] : 0; };
+    bool ok = in(me);
     for (int s = 0; s < R && ok; ++s) {
-        const int32_t* a = all + static_cast<int64_t>(s) * W;
+        if (!in(s)) continue;
+        const int32_t* a = row(s);
         if (a[0] != 0) ok = false;
         for (int e = 0; e < E; ++e)
             if (a[e + 1] < a[e]) ok = false;
         int64_t pout = 0;
         for (int r = 0; r < R; ++r) {
-            const int64_t units = a[(r + 1) * el] - a[r * el];
-            const int64_t pairs = a[E + 1 + r];
+            const int64_t u = units(s, r), p = pairs(s, r);
             // a pair exists exactly when the token has a unit there
-            if (pairs < 0 || pairs > units || ((units > 0) != (pairs > 0))) ok = false;
-            pout += pairs;
+            if (p < 0 || p > u || ((u > 0) != (p > 0))) ok = false;
+            pout += p;
         }
         if (pout > rcap) ok = false;
     }
     for (int r = 0; r < R && ok; ++r) {
         int64_t u = 0, p = 0;
         for (int s = 0; s < R; ++s) {
-            const int32_t* a = all + static_cast<int64_t>(s) * W;
-            u += a[(r + 1) * el] - a[r * el];
-            p += a[E + 1 + r];
+            u += units(s, r);
+            p += pairs(s, r);
         }
         if (u > ucap || p > pcap) ok = false;
     }
@@ -155,39 +173,35 @@ __host__ __device__ inline void plan_peer(const int32_t* all, int R, int E, int 
     pl->recv_pair_off[AEM_EP_MAX_RANKS] = 0;
     for (int i = 0; i <= E; ++i) groups[i] = 0;
     if (!ok) return;
-    const int32_t* mine = all + static_cast<int64_t>(me) * W;
     int64_t acc = 0;
     for (int r = 0; r < R; ++r) {
         pl->send_pair_off[r] = static_cast<int32_t>(acc);
-        acc += mine[E + 1 + r];
+        acc += pairs(me, r);
     }
     pl->pairs_out = static_cast<int32_t>(acc);
     for (int r = 0; r < R; ++r) {
         int64_t u = 0, p = 0;
         for (int s = 0; s < me; ++s) {
-            const int32_t* a = all + static_cast<int64_t>(s) * W;
-            u += a[(r + 1) * el] - a[r * el];
-            p += a[E + 1 + r];
+            u += units(s, r);
+            p += pairs(s, r);
         }
         pl->dst_unit_off[r] = static_cast<int32_t>(u);
         pl->dst_pair_off[r] = static_cast<int32_t>(p);
     }
     acc = 0;
     for (int s = 0; s < R; ++s) {
-        const int32_t* a = all + static_cast<int64_t>(s) * W;
         pl->recv_pair_off[s] = static_cast<int32_t>(acc);
-        acc += a[E + 1 + me];
+        acc += pairs(s, me);
         int64_t before = 0;
-        for (int r = 0; r < me; ++r) before += a[E + 1 + r];
+        for (int r = 0; r < me; ++r) before += pairs(s, r);
         pl->ret_off[s] = static_cast<int32_t>(before);
     }
     pl->recv_pair_off[R] = static_cast<int32_t>(acc);
     pl->pairs_in = static_cast<int32_t>(acc);
     int64_t g = 0;
     for (int s = 0; s < R; ++s) {
-        const int32_t* a = all + static_cast<int64_t>(s) * W;
         for (int e = 0; e < el; ++e) {
-            g += a[me * el + e + 1] - a[me * el + e];
+            if (in(s)) g += row(s)[me * el + e + 1] - row(s)[me * el + e];
             groups[s * el + e + 1] = static_cast<int32_t>(g);
         }
     }
@@ -196,7 +210,12 @@ __host__ __device__ inline void plan_peer(const int32_t* all, int R, int E, int 
 
 namespace {
 
+using namespace aem::dev;
+
 constexpr int kCopyThreads = 256;
+
+// Synchronisation points of a step, one flag per (point, source rank).
+enum { SYNC_COUNTS = 0, SYNC_PLAN = 1, SYNC_DISPATCH = 2, SYNC_RETURN = 3, kSyncPoints = 4 };
 
 // Base pointers of every rank's exchange region (this rank's own at [me]).
 struct EpPeers {
@@ -210,8 +229,83 @@ struct ExchangeLayout {
     size_t rowmap;    // int32 [units_cap]      unit -> received pair row
     size_t rowscale;  // f32 [units_cap]        unit -> gate weight
     size_t ret;       // f32 [ret_cap][d]       pair sums returned to this rank
+    size_t mail_cnt;  // int64 [R][k*E]         every rank's slot counts
+    size_t mail_pay;  // int32 [R][pay_ld]      every rank's starts, pair counts, live mask
+    size_t flags;     // uint64 [kSyncPoints][R] (step << 1 | failed) per source rank
     size_t bytes;
 };
+
+// Step state on this rank's device.
+struct StepState {
+    unsigned long long suspect;  // ranks found silent (kept until the host reads them)
+    int failed;                  // this step failed (a silent or failed peer, a bad plan)
+    int bar;                     // all-reduce word of the teardown barrier
+};
+
+// The waits of one synchronisation point: thread r waits for live peer r's
+// flag to reach `seq` (or a later step), at most `timeout_ns`.  A silent peer
+// becomes suspect; a peer that signalled failure fails this step.  Peers
+// already suspect are not waited for.  Ends with __syncthreads().
+__device__ void wait_point(const uint64_t* __restrict__ flags, int R, int me, uint64_t live,
+                           uint64_t seq, uint64_t timeout_ns, bool tolerant, StepState* st,
+                           int* err) {
+    const int r = threadIdx.x;
+    if (r < R && r != me && ((live >> r) & 1ull) &&
+        !((*reinterpret_cast<volatile unsigned long long*>(&st->suspect) >> r) & 1ull)) {
+        const uint64_t t0 = globaltimer_ns();
+        while (true) {
+            const uint64_t v = ld_acquire_sys(flags + r);
+            if ((v >> 1) >= seq) {
+                if ((v >> 1) == seq && (v & 1ull)) {
+                    atomicExch(&st->failed, 1);
+                    if (!tolerant) atomicOr(err, ERR_EP_PEER_FAILED);
+                }
+                break;
+            }
+            if (globaltimer_ns() - t0 > timeout_ns) {
+                atomicOr(&st->suspect, 1ull << r);
+                atomicExch(&st->failed, 1);
+                if (!tolerant) atomicOr(err, ERR_EP_PEER_TIMEOUT);
+                break;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ uint64_t usable(uint64_t live, const StepState* st) {
+    return live & ~*reinterpret_cast<const volatile unsigned long long*>(&st->suspect);
+}
+
+// Writes `words` 32-bit words of `src` into slot `me` of every usable rank's
+// mailbox (offset `slot_off`, slot stride `slot_words`), then, per rank, a
+// system-scope fence and the flag (seq << 1 | failed) of `point`.
+__global__ void ep_publish_kernel(const uint32_t* __restrict__ src, int words, int slot_words,
+                                  EpPeers peers, size_t slot_off, size_t flag_off, int point,
+                                  int me, int R, uint64_t live, uint64_t seq, StepState* st) {
+    const uint64_t to = usable(live, st);
+    for (int r = 0; r < R; ++r) {
+        if (!((to >> r) & 1ull)) continue;
+        uint32_t* dst = reinterpret_cast<uint32_t*>(peers.base[r] + slot_off) +
+                        static_cast<int64_t>(me) * slot_words;
+        for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+    }
+    __syncthreads();
+    const int r = threadIdx.x;
+    if (r < R && ((to >> r) & 1ull)) {
+        const uint64_t failed = *reinterpret_cast<volatile int*>(&st->failed) ? 1ull : 0ull;
+        __threadfence_system();
+        uint64_t* f = reinterpret_cast<uint64_t*>(peers.base[r] + flag_off) +
+                      static_cast<int64_t>(point) * R + me;
+        st_release_sys(f, (seq << 1) | failed);
+    }
+}
+
+__global__ void ep_wait_kernel(const uint64_t* __restrict__ flags, int R, int me, uint64_t live,
+                               uint64_t seq, uint64_t timeout_ns, int tolerant, StepState* st,
+                               int* err) {
+    wait_point(flags, R, me, live, seq, timeout_ns, tolerant != 0, st, err);
+}
 
 // cnt[j][e] = number of local tokens whose slot-j choice is e.
 __global__ void slot_count_kernel(const int32_t* __restrict__ idx, int64_t T, int ldi, int k, int E,
@@ -231,15 +325,21 @@ __global__ void slot_count_kernel(const int32_t* __restrict__ idx, int64_t T, in
         if (h[i]) atomicAdd(&cnt[i], static_cast<unsigned long long>(h[i]));
 }
 
-// corr[j][e] = base[j][e] - (local units of expert e in slots < j), where
-// base[j][e] = sum_{j'<j} sum_r' all[r'][j'][e] + sum_{r'<r} all[r'][j][e].
-__global__ void ep_corr_kernel(const long long* __restrict__ all, int R, int k, int E, int rank,
+// After the counts' point: corr[j][e] = base[j][e] - (local units of expert e
+// in slots < j), where base[j][e] = sum_{j'<j} sum_r' all[r'][j'][e] +
+// sum_{r'<r} all[r'][j][e] over the usable ranks.
+__global__ void ep_corr_kernel(const long long* __restrict__ all, const uint64_t* __restrict__ flags,
+                               int R, int k, int E, int rank, uint64_t live, uint64_t seq,
+                               uint64_t timeout_ns, int tolerant, StepState* st, int* err,
                                long long* __restrict__ corr) {
+    wait_point(flags, R, rank, live, seq, timeout_ns, tolerant != 0, st, err);
+    const uint64_t use = usable(live, st) | (1ull << rank);
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         long long before_slots = 0, local_before = 0;
         for (int j = 0; j < k; ++j) {
             long long before_ranks = 0, slot_total = 0;
             for (int r = 0; r < R; ++r) {
+                if (!((use >> r) & 1ull)) continue;
                 const long long v = all[(static_cast<int64_t>(r) * k + j) * E + e];
                 if (r < rank) before_ranks += v;
                 slot_total += v;
@@ -270,25 +370,32 @@ __global__ void unlabel_kernel(const uint32_t* __restrict__ in, int64_t n,
 }
 
 // Block r numbers the tokens that have at least one unit on rank r, in token
-// order: pair_local[r][t] = that number, or -1.  Writes the pair count per
-// destination after the expert starts into the all-gather payload.
+// order: pair_local[r][t] = that number, or -1 (always -1 for a rank outside
+// `live`: its units fail).  Writes the all-gather payload: the expert starts,
+// the pair count per destination, the live mask.
 __global__ void __launch_bounds__(1024)
-    ep_pairs_kernel(const uint32_t* __restrict__ eff, int64_t T, int k, int el, int E,
-                    const int* __restrict__ starts, int32_t* __restrict__ pair_local,
+    ep_pairs_kernel(const uint32_t* __restrict__ eff, int64_t T, int k, int el, int E, int R,
+                    uint64_t live, const int* __restrict__ starts, int32_t* __restrict__ pair_local,
                     int32_t* __restrict__ payload) {
     __shared__ int wsum[32];
     __shared__ int running;
     const int r = blockIdx.x;
+    const bool on = ((live >> r) & 1ull) != 0;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nwarps = blockDim.x >> 5;
-    if (r == 0)
+    if (r == 0) {
         for (int i = tid; i <= E; i += blockDim.x) payload[i] = starts[i];
+        if (tid == 0) {
+            payload[E + 1 + R] = static_cast<int32_t>(live & 0xFFFFFFFFull);
+            payload[E + 2 + R] = static_cast<int32_t>(live >> 32);
+        }
+    }
     if (tid == 0) running = 0;
     __syncthreads();
     for (int64_t base = 0; base < T; base += blockDim.x) {
         const int64_t t = base + tid;
         bool f = false;
-        if (t < T)
+        if (on && t < T)
             for (int j = 0; j < k; ++j)
                 f |= static_cast<int>(eff[static_cast<int64_t>(j) * T + t]) / el == r;
         const unsigned b = __ballot_sync(0xFFFFFFFFu, f);
@@ -315,11 +422,30 @@ __global__ void __launch_bounds__(1024)
     if (tid == 0) payload[E + 1 + r] = running;
 }
 
-__global__ void ep_plan_kernel(const int32_t* __restrict__ all, int R, int E, int me, int64_t ucap,
-                               int64_t pcap, int64_t rcap, aem_ep_peer_plan* __restrict__ plan,
-                               int32_t* __restrict__ groups, int* __restrict__ err) {
-    plan_peer(all, R, E, me, ucap, pcap, rcap, plan, groups);
-    if (!plan->ok) atomicOr(err, ERR_EP_PLAN);
+// After the plan's point: the plan over the usable ranks.  Every taking-part
+// rank must report the same live mask; a failed step plans nothing.
+__global__ void ep_plan_kernel(const int32_t* __restrict__ all, int ld,
+                               const uint64_t* __restrict__ flags, int R, int E, int me,
+                               uint64_t live, uint64_t seq, uint64_t timeout_ns, int tolerant,
+                               int64_t ucap, int64_t pcap, int64_t rcap, StepState* st,
+                               aem_ep_peer_plan* __restrict__ plan, int32_t* __restrict__ groups,
+                               int* __restrict__ err) {
+    wait_point(flags, R, me, live, seq, timeout_ns, tolerant != 0, st, err);
+    if (threadIdx.x != 0) return;
+    const uint64_t use = usable(live, st);
+    for (int s = 0; s < R; ++s) {
+        if (!((use >> s) & 1ull)) continue;
+        const int32_t* a = all + static_cast<int64_t>(s) * ld;
+        const uint64_t m = static_cast<uint32_t>(a[E + 1 + R]) |
+                           (static_cast<uint64_t>(static_cast<uint32_t>(a[E + 2 + R])) << 32);
+        if (m != live) st->failed = 1;  // the ranks disagree on who takes part
+    }
+    plan_peer(all, ld, R, E, me, use, ucap, pcap, rcap, plan, groups);
+    if (!plan->ok && !st->failed) {
+        atomicOr(err, ERR_EP_PLAN);
+        st->failed = 1;
+    }
+    if (st->failed) plan->ok = 0;
 }
 
 // One warp copies one row of d elements (d % 8 == 0) to bf16.
@@ -353,6 +479,7 @@ __device__ __forceinline__ void copy_row_bf16(const XT* __restrict__ in, __nv_bf
 // destination's pair rows; (b) each unit's (pair row, gate weight) into the
 // destination's unit row.  Units of this rank are expert-sorted, so those
 // for rank r are the contiguous range [starts[r*el], starts[(r+1)*el]).
+// Units for a rank outside the step have no pair and are skipped (they fail).
 template <typename XT>
 __global__ void __launch_bounds__(kCopyThreads)
     ep_dispatch_kernel(const XT* __restrict__ x, int64_t T, int64_t d, int R, int el,
@@ -393,8 +520,9 @@ __global__ void __launch_bounds__(kCopyThreads)
         while (r + 1 < R && i >= bnd[r + 1]) ++r;
         const int64_t t = src_token[i];
         const int pl = (t >= 0 && t < T) ? pair_local[static_cast<int64_t>(r) * T + t] : -1;
+        if (pl < 0) continue;  // a rank outside the step: the unit fails
         const int64_t pos = upos[r] + (i - bnd[r]);
-        if (pl < 0 || pos >= ucap) {
+        if (pos >= ucap) {
             atomicOr(err, ERR_EP_BOUNDS);
             continue;
         }
@@ -403,16 +531,15 @@ __global__ void __launch_bounds__(kCopyThreads)
     }
 }
 
-// Destination side, after the barrier: unit rows from the received pair rows
-// (the grouped GEMM input), and zeroed pair sums for the down GEMM to
-// accumulate into.
+// Destination side, after the dispatch point: unit rows from the received
+// pair rows (the grouped GEMM input), and zeroed pair sums for the down GEMM
+// to accumulate into.
 __global__ void __launch_bounds__(kCopyThreads)
     ep_expand_kernel(const __nv_bfloat16* __restrict__ xpair, int32_t* __restrict__ rowmap_in,
                      float* __restrict__ rowscale_in, const aem_ep_peer_plan* __restrict__ plan,
-                     int64_t d,
-                     __nv_bfloat16* __restrict__ xu, float* __restrict__ ret_acc,
-                     int* __restrict__ err) {
-    if (!plan->ok) return;
+                     const StepState* st, int64_t d, __nv_bfloat16* __restrict__ xu,
+                     float* __restrict__ ret_acc, int* __restrict__ err) {
+    if (!plan->ok || *reinterpret_cast<const volatile int*>(&st->failed)) return;
     const int64_t units = plan->units_in, pairs = plan->pairs_in;
     const int lane = threadIdx.x & 31;
     const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
@@ -444,11 +571,11 @@ __global__ void __launch_bounds__(kCopyThreads)
 // of s's return rows.
 __global__ void __launch_bounds__(kCopyThreads)
     ep_return_kernel(const float* __restrict__ ret_acc, const aem_ep_peer_plan* __restrict__ plan,
-                     int R, int64_t d, EpPeers peers, ExchangeLayout lay, int64_t rcap,
-                     int* __restrict__ err) {
+                     const StepState* st, int R, int64_t d, EpPeers peers, ExchangeLayout lay,
+                     int64_t rcap, int* __restrict__ err) {
     __shared__ int off[AEM_EP_MAX_RANKS + 1];
     __shared__ int ret[AEM_EP_MAX_RANKS];
-    if (!plan->ok) return;
+    if (!plan->ok || *reinterpret_cast<const volatile int*>(&st->failed)) return;
     for (int i = threadIdx.x; i <= R; i += blockDim.x) off[i] = plan->recv_pair_off[i];
     for (int i = threadIdx.x; i < R; i += blockDim.x) ret[i] = plan->ret_off[i];
     __syncthreads();
@@ -471,17 +598,26 @@ __global__ void __launch_bounds__(kCopyThreads)
     }
 }
 
-// out[t] = sum over destination ranks r (increasing) of the returned pair sum.
+// After the return point: out[t] = sum over destination ranks r (increasing)
+// of the returned pair sum; unit_failed[j*T + t] = 1 for a unit whose expert's
+// rank is outside the step, or for every unit of a failed step (out = 0).
 template <typename OT>
 __global__ void __launch_bounds__(kCopyThreads)
     ep_combine_kernel(const float* __restrict__ ret_in, const int32_t* __restrict__ pair_local,
-                      const aem_ep_peer_plan* __restrict__ plan, int64_t T, int R, int64_t d,
-                      OT* __restrict__ out) {
+                      const aem_ep_peer_plan* __restrict__ plan, const StepState* st,
+                      const uint32_t* __restrict__ eff, int k, int el, uint64_t live, int64_t T,
+                      int R, int64_t d, OT* __restrict__ out, uint8_t* __restrict__ unit_failed) {
     const int lane = threadIdx.x & 31;
-    const bool ok = plan->ok != 0;
+    const bool ok = plan->ok != 0 && !*reinterpret_cast<const volatile int*>(&st->failed);
     const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
          t < T; t += nw) {
+        if (unit_failed)
+            for (int j = lane; j < k; j += 32) {
+                const int64_t u = static_cast<int64_t>(j) * T + t;
+                const int r = static_cast<int>(eff[u]) / el;
+                unit_failed[u] = (!ok || !((live >> r) & 1ull)) ? 1 : 0;
+            }
         int64_t row = -1;
         if (ok && lane < R) {
             const int pl = pair_local[static_cast<int64_t>(lane) * T + t];
@@ -526,6 +662,7 @@ struct Ep {
     Moe loc;  // routing buffers of the single-GPU layer (sized for T_cap tokens)
     int64_t T_cap = 0;
     int64_t units_cap = 0, pairs_cap = 0, ret_cap = 0;
+    int pay_ld = 0;  // int32 words per payload row: starts [E+1], pairs [R], live mask [2]
     // exchange region: this rank's own, and every rank's mapping of it
     ExchangeLayout lay{};
     void* xreg = nullptr;
@@ -534,14 +671,12 @@ struct Ep {
     // local buffers
     void* lbuf = nullptr;
     unsigned long long* cnt = nullptr;  // [k][E]
-    long long* cnt_all = nullptr;       // [R][k][E]
     long long* corr = nullptr;          // [k][E]
-    int32_t* payload = nullptr;         // [E+1+R] this rank's starts + pair counts
-    int32_t* payload_all = nullptr;     // [R][E+1+R]
+    int32_t* payload = nullptr;         // [pay_ld]
     aem_ep_peer_plan* plan = nullptr;
     int32_t* groups = nullptr;          // [E+1]
     int32_t* pair_local = nullptr;      // [R][T]
-    int* bar = nullptr;                 // barrier word
+    StepState* st = nullptr;
     void* xu = nullptr;                 // bf16 [units_cap][d]
     void* hu = nullptr;                 // bf16 [units_cap][ffn]
     float* ret_acc = nullptr;           // f32 [pairs_cap][d]
@@ -550,15 +685,20 @@ struct Ep {
     int32_t* expert_at = nullptr;       // [E] placement position -> expert id
     bool placed = false;                // placement is not the contiguous map
     std::vector<int32_t> h_pos;         // host copy of pos_of
+    // health
+    uint64_t seq = 0;                   // steps issued (every taking-part rank in lockstep)
+    uint64_t unhealthy = 0;             // ranks left out of every later step
+    uint64_t timeout_ns = 2000000000ull;
+    unsigned long long* h_suspect = nullptr;  // pinned copy for aem_ep_health
     int64_t last_T = 0;
     PhaseProfiler prof;
 
     aem_status init(int64_t max_tokens);
     aem_status map_peers(cudaStream_t s);
-    aem_status barrier(cudaStream_t s);
     void release();
+    uint64_t all_mask() const { return world >= 64 ? ~0ull : ((1ull << world) - 1ull); }
     aem_status forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dtype od,
-                       cudaStream_t s);
+                       uint8_t* unit_failed, bool tolerant, cudaStream_t s);
 };
 
 aem_status Ep::init(int64_t max_tokens) {
@@ -568,6 +708,7 @@ aem_status Ep::init(int64_t max_tokens) {
     units_cap = static_cast<int64_t>(R) * T_cap * k;  // every unit of every rank
     pairs_cap = static_cast<int64_t>(R) * T_cap;      // every token of every rank
     ret_cap = T_cap * std::min(R, k);                 // a token has <= min(R, k) destinations
+    pay_ld = (E + 1 + R + 2 + 3) & ~3;                // 16-byte rows
     AEM_REQUIRE(units_cap < (1ll << 31) && pairs_cap * d < (1ll << 40),
                 "aem_ep_create: max_tokens_local=%lld too large for %d ranks x top-%d",
                 (long long)max_tokens, R, k);
@@ -582,20 +723,21 @@ aem_status Ep::init(int64_t max_tokens) {
     lay.rowmap = slot(sizeof(int32_t) * units_cap);
     lay.rowscale = slot(sizeof(float) * units_cap);
     lay.ret = slot(sizeof(float) * ret_cap * d);
+    lay.mail_cnt = slot(sizeof(long long) * R * k * E);
+    lay.mail_pay = slot(sizeof(int32_t) * R * pay_ld);
+    lay.flags = slot(sizeof(uint64_t) * kSyncPoints * R);
     lay.bytes = off;
     AEM_TRY_CUDA(cudaMalloc(&xreg, lay.bytes));
     AEM_TRY_CUDA(cudaMemset(xreg, 0, lay.bytes));
     off = 0;
+    const int ksel = k < E ? k + 1 : k;
     const size_t o_cnt = slot(sizeof(unsigned long long) * k * E);
-    const size_t o_cnt_all = slot(sizeof(long long) * R * k * E);
     const size_t o_corr = slot(sizeof(long long) * k * E);
-    const size_t o_pay = slot(sizeof(int32_t) * (E + 1 + R));
-    const size_t o_pay_all = slot(sizeof(int32_t) * R * (E + 1 + R));
+    const size_t o_pay = slot(sizeof(int32_t) * pay_ld);
     const size_t o_plan = slot(sizeof(aem_ep_peer_plan));
     const size_t o_groups = slot(sizeof(int32_t) * (E + 1));
     const size_t o_pl = slot(sizeof(int32_t) * R * T_cap);
-    const size_t o_bar = slot(sizeof(int));
-    const int ksel = k < E ? k + 1 : k;
+    const size_t o_st = slot(sizeof(StepState));
     const size_t o_ipos = slot(sizeof(int32_t) * T_cap * ksel);
     const size_t o_pos = slot(sizeof(int32_t) * E);
     const size_t o_exp = slot(sizeof(int32_t) * E);
@@ -606,36 +748,36 @@ aem_status Ep::init(int64_t max_tokens) {
     AEM_TRY_CUDA(cudaMemset(lbuf, 0, o_xu));  // everything but the big row buffers
     char* b = static_cast<char*>(lbuf);
     cnt = reinterpret_cast<unsigned long long*>(b + o_cnt);
-    cnt_all = reinterpret_cast<long long*>(b + o_cnt_all);
     corr = reinterpret_cast<long long*>(b + o_corr);
     payload = reinterpret_cast<int32_t*>(b + o_pay);
-    payload_all = reinterpret_cast<int32_t*>(b + o_pay_all);
     plan = reinterpret_cast<aem_ep_peer_plan*>(b + o_plan);
     groups = reinterpret_cast<int32_t*>(b + o_groups);
     pair_local = reinterpret_cast<int32_t*>(b + o_pl);
-    bar = reinterpret_cast<int*>(b + o_bar);
+    st = reinterpret_cast<StepState*>(b + o_st);
     idx_pos = reinterpret_cast<int32_t*>(b + o_ipos);
     pos_of = reinterpret_cast<int32_t*>(b + o_pos);
     expert_at = reinterpret_cast<int32_t*>(b + o_exp);
+    xu = b + o_xu;
+    hu = b + o_hu;
+    ret_acc = reinterpret_cast<float*>(b + o_ret);
     std::vector<int32_t> at(E);
     for (int e = 0; e < E; ++e) at[h_pos[e]] = e;
     AEM_TRY_CUDA(cudaMemcpy(pos_of, h_pos.data(), sizeof(int32_t) * E, cudaMemcpyHostToDevice));
     AEM_TRY_CUDA(cudaMemcpy(expert_at, at.data(), sizeof(int32_t) * E, cudaMemcpyHostToDevice));
-    xu = b + o_xu;
-    hu = b + o_hu;
-    ret_acc = reinterpret_cast<float*>(b + o_ret);
+    AEM_TRY_CUDA(cudaMallocHost(&h_suspect, sizeof(unsigned long long)));
     return AEM_OK;
 }
 
-// All-gathers every rank's IPC handle and sizes; maps every peer's region.
+// All-gathers every rank's IPC handle, device and sizes; maps every peer's region.
 aem_status Ep::map_peers(cudaStream_t s) {
     const int R = world;
     struct Record {
         cudaIpcMemHandle_t h;
         int64_t bytes, T_cap, d, f, E, k, placement;
-        uint8_t pad[128 - sizeof(cudaIpcMemHandle_t) - 7 * sizeof(int64_t)];
+        uint8_t uuid[16];
+        uint8_t pad[256 - sizeof(cudaIpcMemHandle_t) - 7 * sizeof(int64_t) - 16];
     };
-    static_assert(sizeof(Record) == 128, "record size");
+    static_assert(sizeof(Record) == 256, "record size");
     Record mine{};
     AEM_TRY_CUDA(cudaIpcGetMemHandle(&mine.h, xreg));
     mine.bytes = static_cast<int64_t>(lay.bytes);
@@ -647,34 +789,37 @@ aem_status Ep::map_peers(cudaStream_t s) {
     uint64_t hsh = 1469598103934665603ull;  // FNV-1a of the placement
     for (int32_t p : h_pos) hsh = (hsh ^ static_cast<uint32_t>(p)) * 1099511628211ull;
     mine.placement = static_cast<int64_t>(hsh);
+    cudaDeviceProp prop;
+    AEM_TRY_CUDA(cudaGetDeviceProperties(&prop, device));
+    memcpy(mine.uuid, &prop.uuid, 16);
     void* dev = nullptr;
     AEM_TRY_CUDA(cudaMalloc(&dev, sizeof(Record) * R));
     std::vector<Record> all(R);
-    aem_status st = AEM_OK;
+    aem_status st_ = AEM_OK;
     do {
         cudaError_t e = cudaMemcpyAsync(static_cast<char*>(dev) + sizeof(Record) * rank, &mine,
                                         sizeof(Record), cudaMemcpyHostToDevice, s);
         if (e != cudaSuccess) {
             set_error("aem_ep_create: %s", cudaGetErrorString(e));
-            st = AEM_ECUDA;
+            st_ = AEM_ECUDA;
             break;
         }
         ncclResult_t n = nccl()->AllGather(static_cast<char*>(dev) + sizeof(Record) * rank, dev,
                                            sizeof(Record), ncclUint8, comm, s);
         if (n != ncclSuccess) {
             set_error("aem_ep_create: handle all-gather failed: %s", nccl()->GetErrorString(n));
-            st = AEM_ENCCL;
+            st_ = AEM_ENCCL;
             break;
         }
         e = cudaMemcpyAsync(all.data(), dev, sizeof(Record) * R, cudaMemcpyDeviceToHost, s);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
         if (e != cudaSuccess) {
             set_error("aem_ep_create: %s", cudaGetErrorString(e));
-            st = AEM_ECUDA;
+            st_ = AEM_ECUDA;
         }
     } while (0);
     cudaFree(dev);
-    if (st != AEM_OK) return st;
+    if (st_ != AEM_OK) return st_;
     for (int r = 0; r < R; ++r) {
         const Record& a = all[r];
         AEM_REQUIRE(a.bytes == mine.bytes && a.T_cap == mine.T_cap && a.d == mine.d &&
@@ -682,6 +827,9 @@ aem_status Ep::map_peers(cudaStream_t s) {
                         a.placement == mine.placement,
                     "aem_ep_create: rank %d has a different config, placement or "
                     "max_tokens_local", r);
+        for (int q = 0; q < r; ++q)
+            AEM_REQUIRE(memcmp(all[q].uuid, a.uuid, 16) != 0,
+                        "aem_ep_create: ranks %d and %d share one GPU (one rank per GPU)", q, r);
     }
     peers.base[rank] = static_cast<char*>(xreg);
     for (int r = 0; r < R; ++r) {
@@ -694,11 +842,6 @@ aem_status Ep::map_peers(cudaStream_t s) {
     return AEM_OK;
 }
 
-aem_status Ep::barrier(cudaStream_t s) {
-    AEM_TRY_NCCL(nccl()->AllReduce(bar, bar, 1, ncclInt32, ncclSum, comm, s));
-    return AEM_OK;
-}
-
 void Ep::release() {
     for (int r = 0; r < world; ++r)
         if (mapped[r]) {
@@ -708,17 +851,29 @@ void Ep::release() {
 }
 
 aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dtype od,
-                       cudaStream_t s) {
+                       uint8_t* unit_failed, bool tolerant, cudaStream_t s) {
     const int k = cfg.top_k, E = cfg.num_experts, R = world, el = e_loc;
     const int ksel = k < E ? k + 1 : k;
     const int64_t d = cfg.d_model, f = cfg.d_ffn, U = T * k;
     AEM_REQUIRE(T <= T_cap, "aem_ep_forward: T_local=%lld > max_tokens_local=%lld", (long long)T,
                 (long long)T_cap);
+    const uint64_t live = (all_mask() & ~unhealthy) | (1ull << rank);
+    if (!tolerant && live != all_mask()) {
+        set_error("aem_ep_forward: rank(s) 0x%llx are unhealthy; aem_ep_forward_tolerant "
+                  "routes around them",
+                  static_cast<unsigned long long>(all_mask() & ~live));
+        return AEM_ETIMEOUT;
+    }
     const int dev = current_device();
     const int sms = sm_count(dev);
     int* err = device_error_word(dev);
     AEM_REQUIRE(err != nullptr, "aem_ep_forward: no device error word");
+    const int tol = tolerant ? 1 : 0;
+    const uint64_t q = ++seq;
+    char* mine = static_cast<char*>(xreg);
+    const uint64_t* flags = reinterpret_cast<const uint64_t*>(mine + lay.flags);
     last_T = T;
+    AEM_TRY_CUDA(cudaMemsetAsync(&st->failed, 0, sizeof(int), s));
     // 1. gating and local per-(slot, expert) counts
     prof.begin(AEM_PHASE_GATING, s);
     if (T > 0)
@@ -741,10 +896,15 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
         count_launches(1);
     }
     // 2. all-gather counts -> global rank offsets
-    AEM_TRY_NCCL(nccl()->AllGather(cnt, cnt_all, static_cast<size_t>(k) * E, ncclInt64, comm, s));
-    ep_corr_kernel<<<1, 256, 0, s>>>(cnt_all, R, k, E, rank, corr);
+    ep_publish_kernel<<<1, 256, 0, s>>>(reinterpret_cast<const uint32_t*>(cnt), 2 * k * E, 2 * k * E,
+                                        peers, lay.mail_cnt, lay.flags, SYNC_COUNTS, rank, R, live,
+                                        q, st);
     AEM_CHECK_LAUNCH();
-    count_launches(1);
+    ep_corr_kernel<<<1, 256, 0, s>>>(reinterpret_cast<const long long*>(mine + lay.mail_cnt),
+                                     flags + SYNC_COUNTS * R, R, k, E, rank, live, q, timeout_ns,
+                                     tol, st, err, corr);
+    AEM_CHECK_LAUNCH();
+    count_launches(2);
     prof.end(AEM_PHASE_EXCHANGE, s);
     // 3. capacity routing with global ranks + expert-grouped permutation,
     //    then the (destination, token) pairs
@@ -769,18 +929,22 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
     } else {
         AEM_TRY_CUDA(cudaMemsetAsync(loc.starts, 0, sizeof(int) * (E + 1), s));
     }
-    ep_pairs_kernel<<<R, 1024, 0, s>>>(loc.eff, T, k, el, E, loc.starts, pair_local, payload);
+    ep_pairs_kernel<<<R, 1024, 0, s>>>(loc.eff, T, k, el, E, R, live, loc.starts, pair_local,
+                                       payload);
     AEM_CHECK_LAUNCH();
     count_launches(1);
     prof.end(AEM_PHASE_ROUTE, s);
     // 4. all-gather expert starts + pair counts; every rank plans on the device
     prof.begin(AEM_PHASE_EXCHANGE, s);
-    AEM_TRY_NCCL(nccl()->AllGather(payload, payload_all, static_cast<size_t>(E + 1 + R), ncclInt32,
-                                   comm, s));
-    ep_plan_kernel<<<1, 1, 0, s>>>(payload_all, R, E, rank, units_cap, pairs_cap, ret_cap, plan,
-                                   groups, err);
+    ep_publish_kernel<<<1, 256, 0, s>>>(reinterpret_cast<const uint32_t*>(payload), pay_ld, pay_ld,
+                                        peers, lay.mail_pay, lay.flags, SYNC_PLAN, rank, R, live, q,
+                                        st);
     AEM_CHECK_LAUNCH();
-    count_launches(1);
+    ep_plan_kernel<<<1, 64, 0, s>>>(reinterpret_cast<const int32_t*>(mine + lay.mail_pay), pay_ld,
+                                    flags + SYNC_PLAN * R, R, E, rank, live, q, timeout_ns, tol,
+                                    units_cap, pairs_cap, ret_cap, st, plan, groups, err);
+    AEM_CHECK_LAUNCH();
+    count_launches(2);
     prof.end(AEM_PHASE_EXCHANGE, s);
     // 5. dispatch: push pair rows and unit metadata into the destinations
     prof.begin(AEM_PHASE_DISPATCH, s);
@@ -795,24 +959,24 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
                 static_cast<const float*>(x), T, d, R, el, pair_local, loc.starts, loc.src_token,
                 loc.rowscale, k, plan, peers, lay, units_cap, pairs_cap, err);
         AEM_CHECK_LAUNCH();
-        count_launches(1);
-    }
-    AEM_TRY(barrier(s));
-    {
-        char* mine = static_cast<char*>(xreg);
+        ep_publish_kernel<<<1, 64, 0, s>>>(nullptr, 0, 0, peers, 0, lay.flags, SYNC_DISPATCH, rank,
+                                           R, live, q, st);
+        AEM_CHECK_LAUNCH();
+        ep_wait_kernel<<<1, 64, 0, s>>>(flags + SYNC_DISPATCH * R, R, rank, live, q, timeout_ns,
+                                        tol, st, err);
+        AEM_CHECK_LAUNCH();
         ep_expand_kernel<<<static_cast<unsigned>(sms * 4), kCopyThreads, 0, s>>>(
             reinterpret_cast<const __nv_bfloat16*>(mine + lay.xpair),
             reinterpret_cast<int32_t*>(mine + lay.rowmap),
-            reinterpret_cast<float*>(mine + lay.rowscale), plan, d,
+            reinterpret_cast<float*>(mine + lay.rowscale), plan, st, d,
             static_cast<__nv_bfloat16*>(xu), ret_acc, err);
         AEM_CHECK_LAUNCH();
-        count_launches(1);
+        count_launches(4);
     }
     prof.end(AEM_PHASE_DISPATCH, s);
     // 6. local expert FFN on the (source, expert) groups; the down GEMM
     //    scales by the gate weight and sums the units of each pair
     {
-        char* mine = static_cast<char*>(xreg);
         const int64_t hint = std::max<int64_t>(U, 1);  // expected received units
         GemmArgs up_a;
         up_a.w = up;
@@ -851,22 +1015,29 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
     // 7. pair sums back into the sources
     prof.begin(AEM_PHASE_RETURN, s);
     ep_return_kernel<<<static_cast<unsigned>(sms * 4), kCopyThreads, 0, s>>>(
-        ret_acc, plan, R, d, peers, lay, ret_cap, err);
+        ret_acc, plan, st, R, d, peers, lay, ret_cap, err);
     AEM_CHECK_LAUNCH();
-    count_launches(1);
-    AEM_TRY(barrier(s));
+    ep_publish_kernel<<<1, 64, 0, s>>>(nullptr, 0, 0, peers, 0, lay.flags, SYNC_RETURN, rank, R,
+                                       live, q, st);
+    AEM_CHECK_LAUNCH();
+    ep_wait_kernel<<<1, 64, 0, s>>>(flags + SYNC_RETURN * R, R, rank, live, q, timeout_ns, tol, st,
+                                    err);
+    AEM_CHECK_LAUNCH();
+    count_launches(3);
     prof.end(AEM_PHASE_RETURN, s);
-    // 8. per-token sum over destination ranks
+    // 8. per-token sum over destination ranks, failed flags
     prof.begin(AEM_PHASE_COMBINE, s);
     if (T > 0) {
-        const float* ret_in = reinterpret_cast<const float*>(static_cast<char*>(xreg) + lay.ret);
+        const float* ret_in = reinterpret_cast<const float*>(mine + lay.ret);
         const unsigned g = static_cast<unsigned>(std::min<int64_t>((T + 7) / 8, sms * 8));
         if (od == AEM_BF16)
             ep_combine_kernel<__nv_bfloat16><<<g, kCopyThreads, 0, s>>>(
-                ret_in, pair_local, plan, T, R, d, static_cast<__nv_bfloat16*>(out));
+                ret_in, pair_local, plan, st, loc.eff, k, el, live, T, R, d,
+                static_cast<__nv_bfloat16*>(out), unit_failed);
         else
-            ep_combine_kernel<float><<<g, kCopyThreads, 0, s>>>(ret_in, pair_local, plan, T, R, d,
-                                                                static_cast<float*>(out));
+            ep_combine_kernel<float><<<g, kCopyThreads, 0, s>>>(
+                ret_in, pair_local, plan, st, loc.eff, k, el, live, T, R, d,
+                static_cast<float*>(out), unit_failed);
         AEM_CHECK_LAUNCH();
         count_launches(1);
     }
@@ -928,13 +1099,13 @@ aem_status aem_ep_plan_exchange(const int32_t* starts, int R, int E, int rank, i
     return AEM_OK;
 }
 
-aem_status aem_ep_plan_peer(const int32_t* all, int R, int E, int rank, int64_t units_cap,
-                            int64_t pairs_cap, int64_t ret_cap, aem_ep_peer_plan* plan,
-                            int32_t* groups) {
+aem_status aem_ep_plan_peer(const int32_t* all, int R, int E, int rank, uint64_t live,
+                            int64_t units_cap, int64_t pairs_cap, int64_t ret_cap,
+                            aem_ep_peer_plan* plan, int32_t* groups) {
     AEM_REQUIRE(all && plan && groups, "aem_ep_plan_peer: NULL buffer");
     AEM_REQUIRE(R >= 1 && R <= AEM_EP_MAX_RANKS && E >= R && E % R == 0 && rank >= 0 && rank < R,
                 "aem_ep_plan_peer: bad R=%d E=%d rank=%d", R, E, rank);
-    aem::plan_peer(all, R, E, rank, units_cap, pairs_cap, ret_cap, plan, groups);
+    aem::plan_peer(all, E + 1 + R, R, E, rank, live, units_cap, pairs_cap, ret_cap, plan, groups);
     return AEM_OK;
 }
 
@@ -948,12 +1119,18 @@ aem_status aem_ep_unique_id(uint8_t out[128]) {
     return AEM_OK;
 }
 
-static void ep_destroy(aem::Ep* ep) {
+static void ep_destroy(aem::Ep* ep, bool abort_comm) {
     ep->release();
-    if (ep->comm && aem::nccl()) aem::nccl()->CommDestroy(ep->comm);
+    if (ep->comm && aem::nccl()) {
+        if (abort_comm)
+            aem::nccl()->CommAbort(ep->comm);
+        else
+            aem::nccl()->CommDestroy(ep->comm);
+    }
     cudaFree(ep->xreg);
     cudaFree(ep->lbuf);
     cudaFree(ep->loc.buf);
+    cudaFreeHost(ep->h_suspect);
     delete ep;
 }
 
@@ -1034,7 +1211,7 @@ aem_status aem_ep_create(const aem_moe_config* cfg, int rank, int world, const u
         }
     }
     if (st != AEM_OK) {
-        ep_destroy(ep);
+        ep_destroy(ep, true);
         return st;
     }
     *out = reinterpret_cast<aem_ep_t>(ep);
@@ -1046,31 +1223,85 @@ aem_status aem_ep_free(aem_ep_t h) {
     auto* ep = reinterpret_cast<aem::Ep*>(h);
     cudaSetDevice(ep->device);
     cudaDeviceSynchronize();
-    // Collective: nobody unmaps or frees until every rank's last step ended,
-    // and nobody frees its region while a peer still maps it.
-    cudaStream_t s = nullptr;
+    unsigned long long suspect = 0;
+    cudaMemcpy(&suspect, &ep->st->suspect, sizeof(suspect), cudaMemcpyDeviceToHost);
+    const bool healthy = ep->unhealthy == 0 && suspect == 0;
     aem_status st = AEM_OK;
-    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess) {
-        st = ep->barrier(s);
-        if (st == AEM_OK) cudaStreamSynchronize(s);
-        ep->release();
-        if (st == AEM_OK) st = ep->barrier(s);
-        if (st == AEM_OK) cudaStreamSynchronize(s);
-        cudaStreamDestroy(s);
+    if (healthy) {
+        // Collective: nobody unmaps or frees until every rank's last step
+        // ended, and nobody frees its region while a peer still maps it.
+        int* bar = &ep->st->bar;
+        cudaStream_t s = nullptr;
+        if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess) {
+            ncclResult_t n = aem::nccl()->AllReduce(bar, bar, 1, ncclInt32, ncclSum, ep->comm, s);
+            if (n == ncclSuccess) cudaStreamSynchronize(s);
+            ep->release();
+            if (n == ncclSuccess)
+                n = aem::nccl()->AllReduce(bar, bar, 1, ncclInt32, ncclSum, ep->comm, s);
+            if (n == ncclSuccess) cudaStreamSynchronize(s);
+            if (n != ncclSuccess) {
+                set_error("aem_ep_free: %s", aem::nccl()->GetErrorString(n));
+                st = AEM_ENCCL;
+            }
+            cudaStreamDestroy(s);
+        }
     }
-    ep_destroy(ep);
+    // With a rank gone there is no collective to wait on: unmap, free, abort.
+    ep_destroy(ep, !healthy || st != AEM_OK);
     return st;
 }
 
-aem_status aem_ep_forward(aem_ep_t h, const void* x, aem_dtype x_dtype, int64_t T_local, void* out,
-                          aem_dtype out_dtype, void* stream) {
+static aem_status ep_forward_checked(aem_ep_t h, const void* x, aem_dtype x_dtype, int64_t T_local,
+                                     void* out, aem_dtype out_dtype, uint8_t* unit_failed,
+                                     bool tolerant, void* stream) {
     AEM_REQUIRE(h != nullptr, "aem_ep_forward: NULL layer");
     AEM_REQUIRE(T_local >= 0 && T_local < (1ll << 28), "aem_ep_forward: T out of range");
     AEM_REQUIRE(T_local == 0 || (x && out), "aem_ep_forward: NULL buffer");
     AEM_REQUIRE(x_dtype == AEM_F32 || x_dtype == AEM_BF16, "aem_ep_forward: bad x dtype");
     AEM_REQUIRE(out_dtype == AEM_F32 || out_dtype == AEM_BF16, "aem_ep_forward: bad out dtype");
     auto* ep = reinterpret_cast<aem::Ep*>(h);
-    return ep->forward(x, x_dtype, T_local, out, out_dtype, static_cast<cudaStream_t>(stream));
+    return ep->forward(x, x_dtype, T_local, out, out_dtype, unit_failed, tolerant,
+                       static_cast<cudaStream_t>(stream));
+}
+
+aem_status aem_ep_forward(aem_ep_t h, const void* x, aem_dtype x_dtype, int64_t T_local, void* out,
+                          aem_dtype out_dtype, void* stream) {
+    return ep_forward_checked(h, x, x_dtype, T_local, out, out_dtype, nullptr, false, stream);
+}
+
+aem_status aem_ep_forward_tolerant(aem_ep_t h, const void* x, aem_dtype x_dtype, int64_t T_local,
+                                   void* out, aem_dtype out_dtype, uint8_t* unit_failed,
+                                   void* stream) {
+    return ep_forward_checked(h, x, x_dtype, T_local, out, out_dtype, unit_failed, true, stream);
+}
+
+aem_status aem_ep_mark_unhealthy(aem_ep_t h, int rank) {
+    AEM_REQUIRE(h != nullptr, "aem_ep_mark_unhealthy: NULL layer");
+    auto* ep = reinterpret_cast<aem::Ep*>(h);
+    AEM_REQUIRE(rank >= 0 && rank < ep->world, "aem_ep_mark_unhealthy: bad rank %d", rank);
+    AEM_REQUIRE(rank != ep->rank, "aem_ep_mark_unhealthy: rank %d is this rank", rank);
+    ep->unhealthy |= 1ull << rank;
+    return AEM_OK;
+}
+
+aem_status aem_ep_health(aem_ep_t h, uint64_t* unhealthy, void* stream) {
+    AEM_REQUIRE(h != nullptr && unhealthy != nullptr, "aem_ep_health: NULL argument");
+    auto* ep = reinterpret_cast<aem::Ep*>(h);
+    auto s = static_cast<cudaStream_t>(stream);
+    AEM_TRY_CUDA(cudaMemcpyAsync(ep->h_suspect, &ep->st->suspect, sizeof(unsigned long long),
+                                 cudaMemcpyDeviceToHost, s));
+    AEM_TRY_CUDA(cudaStreamSynchronize(s));
+    ep->unhealthy |= *ep->h_suspect & ~(1ull << ep->rank);
+    *unhealthy = ep->unhealthy;
+    return AEM_OK;
+}
+
+aem_status aem_ep_set_timeout(aem_ep_t h, double seconds) {
+    AEM_REQUIRE(h != nullptr, "aem_ep_set_timeout: NULL layer");
+    AEM_REQUIRE(seconds > 0.0 && seconds <= 3600.0, "aem_ep_set_timeout: %g s out of range",
+                seconds);
+    reinterpret_cast<aem::Ep*>(h)->timeout_ns = static_cast<uint64_t>(seconds * 1e9);
+    return AEM_OK;
 }
 
 aem_status aem_ep_profile(aem_ep_t h, int enable) {

@@ -102,6 +102,13 @@ aem_status check_device_errors(cudaStream_t stream, const char* what) {
         set_error("%s: a bounded device wait timed out (error bits 0x%x)", what, bits);
         return AEM_ETIMEOUT;
     }
+    if (bits & (ERR_EP_PEER_TIMEOUT | ERR_EP_PEER_FAILED)) {
+        set_error("%s: an expert-parallel peer %s (error bits 0x%x)", what,
+                  (bits & ERR_EP_PEER_TIMEOUT) ? "did not signal within the deadline"
+                                               : "reported a failed step",
+                  bits);
+        return AEM_ETIMEOUT;
+    }
     if (bits & ERR_ROUTE_POSITION) {
         set_error("%s: batch_position is not a permutation of [0, n) (error bits 0x%x)", what,
                   bits);

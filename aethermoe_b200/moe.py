@@ -167,18 +167,21 @@ def ep_plan_exchange(starts, rank):
     return so, sc, ro, rc, groups
 
 
-def ep_plan_peer(payload, rank, units_cap, pairs_cap, ret_cap):
+def ep_plan_peer(payload, rank, units_cap, pairs_cap, ret_cap, live=None):
     """Host form of the per-step peer-exchange plan: ``payload [R, E+1+R]``
     (every rank's expert starts, then its pair counts per destination) ->
-    ``(plan dict, groups [E+1])`` for ``rank``."""
+    ``(plan dict, groups [E+1])`` for ``rank``; ``live`` is the bit mask of
+    the ranks taking part (default: all)."""
     pay = np.ascontiguousarray(payload, dtype=np.int32)
     r, w = pay.shape
     e = w - 1 - r
+    if live is None:
+        live = (1 << r) - 1
     plan = _lib.EpPeerPlan()
     groups = np.zeros(e + 1, np.int32)
-    _lib.check(_lib.lib().aem_ep_plan_peer(pay.ctypes.data, r, e, rank, units_cap, pairs_cap,
-                                           ret_cap, ctypes.byref(plan), groups.ctypes.data),
-               "aem_ep_plan_peer")
+    _lib.check(_lib.lib().aem_ep_plan_peer(pay.ctypes.data, r, e, rank, int(live), units_cap,
+                                           pairs_cap, ret_cap, ctypes.byref(plan),
+                                           groups.ctypes.data), "aem_ep_plan_peer")
     out = dict(ok=plan.ok, units_in=plan.units_in, pairs_in=plan.pairs_in,
                pairs_out=plan.pairs_out)
     for name in ("dst_unit_off", "dst_pair_off", "send_pair_off", "ret_off"):
@@ -237,6 +240,33 @@ class EPLayer:
                                              out.data_ptr(), _dtype_code(out), _stream_ptr(stream)),
                    "aem_ep_forward")
         return out
+
+    def forward_tolerant(self, x, out=None, out_dtype=None, stream=None):
+        """``Router::route_batch_tolerant``: returns ``(out, unit_failed)`` with
+        ``unit_failed [k*T]`` uint8 (slot-major); never raises for a peer failure."""
+        import torch
+        t = x.shape[0]
+        if out is None:
+            out = torch.empty((t, self.d_model), dtype=out_dtype or x.dtype, device=x.device)
+        failed = torch.empty((self.top_k * t,), dtype=torch.uint8, device=x.device)
+        _lib.check(_lib.lib().aem_ep_forward_tolerant(self.handle, x.data_ptr(), _dtype_code(x), t,
+                                                      out.data_ptr(), _dtype_code(out),
+                                                      failed.data_ptr(), _stream_ptr(stream)),
+                   "aem_ep_forward_tolerant")
+        return out, failed
+
+    def mark_unhealthy(self, rank):
+        _lib.check(_lib.lib().aem_ep_mark_unhealthy(self.handle, rank), "aem_ep_mark_unhealthy")
+
+    def health(self, stream=None):
+        """Set of ranks left out of later steps (host-marked or found silent)."""
+        m = ctypes.c_uint64()
+        _lib.check(_lib.lib().aem_ep_health(self.handle, ctypes.byref(m), _stream_ptr(stream)),
+                   "aem_ep_health")
+        return {r for r in range(64) if (m.value >> r) & 1}
+
+    def set_timeout(self, seconds):
+        _lib.check(_lib.lib().aem_ep_set_timeout(self.handle, float(seconds)), "aem_ep_set_timeout")
 
     def profile(self, enable=True):
         _lib.check(_lib.lib().aem_ep_profile(self.handle, 1 if enable else 0), "aem_ep_profile")

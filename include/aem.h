@@ -313,14 +313,16 @@ typedef struct aem_ep_peer_plan {
 /* Host form of the per-step plan the expert-parallel layer computes on the
  * device (no GPU needed).  all: [R][E+1+R] int32, every rank's expert
  * starts [E+1] followed by its pair counts per destination rank [R].
+ * live: bit r set when rank r takes part in the step; the rows of other
+ * ranks are ignored, and so are units for them (those units fail).
  * Capacities: units_cap (received units), pairs_cap (received pairs),
  * ret_cap (return rows), the same on every rank.  Writes the plan of `rank`
  * and groups [E+1] (R*(E/R) = E row groups): the row offsets of the
  * received (source, local expert) segments, sources outer.  A plan whose counts do not fit
  * has ok = 0 (every rank derives the same verdict from the same data). */
-aem_status aem_ep_plan_peer(const int32_t* all, int R, int E, int rank, int64_t units_cap,
-                            int64_t pairs_cap, int64_t ret_cap, aem_ep_peer_plan* plan,
-                            int32_t* groups);
+aem_status aem_ep_plan_peer(const int32_t* all, int R, int E, int rank, uint64_t live,
+                            int64_t units_cap, int64_t pairs_cap, int64_t ret_cap,
+                            aem_ep_peer_plan* plan, int32_t* groups);
 
 /* NCCL unique id (128 bytes) for aem_ep_create; made on one rank and
  * broadcast by the caller. */
@@ -337,7 +339,9 @@ typedef struct aem_ep_s* aem_ep_t;
  * Router + ICollectiveTransport scatter/gather (router.hpp:67-100,
  * collective_transport.hpp:37-51): activations and expert outputs move by
  * stores into the peers' memory over NVLink (CUDA IPC, mapped once here),
- * NCCL carries the small per-step all-gathers and barriers.  Collective:
+ * and so do the step's small all-gathers and barriers (flags with a
+ * deadline); NCCL only bootstraps the mapping here and tears it down in
+ * aem_ep_free.  Every rank must run on its own GPU.  Collective:
  * every rank calls it with the same config and max_tokens_local, the most
  * tokens any rank passes to one aem_ep_forward (receive buffers are sized
  * for the worst case, so a step never allocates). */
@@ -348,9 +352,34 @@ aem_status aem_ep_free(aem_ep_t ep);
 /* One step: this rank's T_local tokens (global positions rank*T_local ...)
  * -> its outputs.  Collective: every rank calls it with the same T_local
  * (<= max_tokens_local).  Asynchronous on `stream` (no host synchronisation);
- * a receive-capacity or peer failure is reported by aem_device_status. */
+ * a receive-capacity or peer failure is reported by aem_device_status
+ * (AEM_ETIMEOUT for a silent peer), the way route_batch throws. */
 aem_status aem_ep_forward(aem_ep_t ep, const void* x, aem_dtype x_dtype, int64_t T_local, void* out,
                           aem_dtype out_dtype, void* stream);
+/* Tolerant step: Router::route_batch_tolerant (router.hpp:127-234).  Never
+ * reports a peer failure as an error: every (token, slot) unit gets exactly
+ * one outcome, unit_failed[j*T_local + t] = 0 (its expert output is in
+ * out[t]) or 1 (it contributes nothing).  A unit fails when its effective
+ * expert lives on a rank marked unhealthy, or when the step itself fails
+ * because a peer did not signal within the deadline (every unit of the step
+ * then fails, on every rank that took part, and out is zero).  A rank that
+ * timed out is remembered as unhealthy by aem_ep_health and left out of later
+ * steps, like the Router's unhealthy_shards_ (no reconnection).
+ * unit_failed: device uint8 [k*T_local] (slot-major) or NULL. */
+aem_status aem_ep_forward_tolerant(aem_ep_t ep, const void* x, aem_dtype x_dtype, int64_t T_local,
+                                   void* out, aem_dtype out_dtype, uint8_t* unit_failed,
+                                   void* stream);
+/* The host learned that `rank` is gone (a store, a heartbeat, a process
+ * exit): later steps leave it out and never touch its memory again.  A rank
+ * that exited must be marked here before the next step; the in-step deadline
+ * covers a rank that stops taking part but keeps its process. */
+aem_status aem_ep_mark_unhealthy(aem_ep_t ep, int rank);
+/* Synchronises `stream`, folds the ranks the device found silent into the
+ * unhealthy set and writes that set (bit r = rank r) to *unhealthy.
+ * Router::is_shard_unhealthy / unhealthy_shard_count (router.hpp:236-240). */
+aem_status aem_ep_health(aem_ep_t ep, uint64_t* unhealthy, void* stream);
+/* Deadline of every in-step wait on a peer (default 2 s). */
+aem_status aem_ep_set_timeout(aem_ep_t ep, double seconds);
 /* Per-phase profiling of this rank's steps (see aem_moe_profile). */
 aem_status aem_ep_profile(aem_ep_t ep, int enable);
 aem_status aem_ep_profile_read(aem_ep_t ep, double* ms, int64_t* steps);

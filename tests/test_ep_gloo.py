@@ -67,7 +67,7 @@ def _rank(rank, world, port, outdir):
     allp = [torch.zeros_like(payload) for _ in range(world)]
     dist.all_gather(allp, payload)
     caps = (world * tl * K_TOP, world * tl, tl * min(world, K_TOP))
-    pp, pg = ep_plan_peer(torch.stack(allp).numpy(), rank, *caps)
+    pp, pg = ep_plan_peer(torch.stack(allp).numpy(), rank, *caps)  # every rank live
     np.savez(os.path.join(outdir, f"r{rank}.npz"), eff=eff, starts=starts,
              so=plan[0], sc=plan[1], ro=plan[2], rc=plan[3], groups=plan[4], pgroups=pg,
              **{"p_" + key: np.asarray(v) for key, v in pp.items()})
@@ -183,3 +183,79 @@ def test_peer_plan_rejects_overflow():
     pay2 = pay.copy()
     pay2[0, E_ + 1] = 3  # 2 units to rank 0 but 3 pairs
     assert ep_plan_peer(pay2, 0, 100, 100, 100)[0]["ok"] == 0
+
+
+def test_peer_exchange_plan_with_a_rank_left_out():
+    """A rank marked unhealthy takes no part: its tokens leave the batch, the
+    capacity rule runs over the live ranks' tokens only, units whose expert
+    lives on the dead rank fail, and the live ranks' pushes still tile every
+    receive range exactly (host replay of the plans for live mask 0b1011)."""
+    from aethermoe_b200.moe import ep_plan_peer
+    world, dead = 4, 2
+    live = [r for r in range(world) if r != dead]
+    mask = sum(1 << r for r in live)
+    idx = _inputs()
+    tl = T // world
+    el = E // world
+    cap = O.default_capacity(T, K_TOP, E)
+    # the distributed rule with the dead rank's counts absent == the rule on the live tokens
+    sub = np.concatenate([idx[r * tl:(r + 1) * tl] for r in live])
+    eff_all = O.moe_route(sub, K_TOP, E, cap).reshape(K_TOP, len(live) * tl)
+    res = {}
+    payload = np.zeros((world, E + 1 + world), np.int32)
+    for i, r in enumerate(live):
+        eff = eff_all[:, i * tl:(i + 1) * tl].reshape(-1)
+        starts = np.zeros(E + 1, np.int32)
+        starts[1:] = np.cumsum(np.bincount(eff, minlength=E))
+        dest = eff.reshape(K_TOP, tl) // el
+        pcnt = np.array([(dest == q).any(axis=0).sum() if q != dead else 0 for q in range(world)])
+        payload[r] = np.concatenate([starts, pcnt])
+        res[r] = dict(eff=eff, starts=starts)
+    payload[dead] = 12345  # whatever a dead rank left behind is ignored
+    caps = (world * tl * K_TOP, world * tl, tl * min(world, K_TOP))
+    for r in live:
+        pp, pg = ep_plan_peer(payload, r, *caps, live=mask)
+        assert pp["ok"] == 1
+        res[r].update(pgroups=pg, **{"p_" + key: np.asarray(v) for key, v in pp.items()})
+    # replay the pushes of the live ranks
+    xpair = {r: {} for r in live}
+    units = {r: {} for r in live}
+    ret = {r: {} for r in live}
+    failed = 0
+    for s_ in live:
+        eff, starts = res[s_]["eff"], res[s_]["starts"]
+        order = np.argsort(eff, kind="stable")
+        dest = eff.reshape(K_TOP, tl) // el
+        pl = np.full((world, tl), -1)
+        for r in live:
+            has = (dest == r).any(axis=0)
+            pl[r, has] = np.arange(has.sum())
+            for t in np.nonzero(has)[0]:
+                row = int(res[s_]["p_dst_pair_off"][r]) + pl[r, t]
+                assert row not in xpair[r]
+                xpair[r][row] = (s_, t)
+            lo, hi = starts[r * el], starts[(r + 1) * el]
+            for i in range(lo, hi):
+                pos = int(res[s_]["p_dst_unit_off"][r]) + (i - lo)
+                assert pos not in units[r]
+                units[r][pos] = (s_, order[i])
+        failed += int((dest == dead).sum())
+        res[s_]["_pl"] = pl
+    assert failed > 0  # the dead rank's experts had units: those fail
+    for r in live:
+        p = res[r]
+        assert sorted(xpair[r]) == list(range(int(p["p_pairs_in"])))
+        assert sorted(units[r]) == list(range(int(p["p_units_in"])))
+        for pos, (s_, u) in units[r].items():
+            e = int(res[s_]["eff"][u])
+            grp = np.searchsorted(p["pgroups"], pos, side="right") - 1
+            assert grp == s_ * el + (e - r * el)
+        roff = p["p_recv_pair_off"]
+        for prow, (s_, t) in xpair[r].items():
+            row = int(p["p_ret_off"][s_]) + prow - int(roff[s_])
+            assert row not in ret[s_]
+            ret[s_][row] = (r, t)
+    for s_ in live:
+        assert sorted(ret[s_]) == list(range(int(res[s_]["p_pairs_out"])))
+        for row, (r, t) in ret[s_].items():
+            assert int(res[s_]["p_send_pair_off"][r]) + res[s_]["_pl"][r, t] == row
