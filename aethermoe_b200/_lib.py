@@ -51,7 +51,7 @@ class EpPeerPlan(ctypes.Structure):
     """``aem_ep_peer_plan``: where one rank's rows go in one peer-memory exchange."""
     _fields_ = [("ok", ctypes.c_int32), ("units_in", ctypes.c_int32),
                 ("pairs_in", ctypes.c_int32), ("pairs_out", ctypes.c_int32),
-                ("dst_unit_off", ctypes.c_int32 * EP_MAX_RANKS),
+                ("dst_unit_off", ctypes.c_int32 * 256),
                 ("dst_pair_off", ctypes.c_int32 * EP_MAX_RANKS),
                 ("send_pair_off", ctypes.c_int32 * EP_MAX_RANKS),
                 ("recv_pair_off", ctypes.c_int32 * (EP_MAX_RANKS + 1)),

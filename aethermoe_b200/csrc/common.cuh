@@ -94,6 +94,13 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
+// Vector float32 reduction into global memory (16-byte aligned address).
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+                 "f"(d)
+                 : "memory");
+}
+
 // System-scope acquire load / release store (flags written by peer GPUs).
 __device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
     uint64_t v;

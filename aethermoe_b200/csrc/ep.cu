@@ -19,7 +19,7 @@
 //             NVLink once per destination rank, not once per unit;
 //   units  -- (token, slot): the destination gets, per unit, the row of its
 //             pair and its gate weight, at the unit's row in the destination's
-//             (source, expert)-grouped layout.
+//             expert-grouped layout (sources in rank order inside an expert).
 //   Step: gating -> slot counts -> [all-gather] -> capacity routing (global
 //   ranks) -> pair numbering -> [all-gather of expert starts + pair counts]
 //   -> on-device plan -> push pairs + unit metadata into the destinations ->
@@ -167,12 +167,17 @@ __host__ __device__ inline void plan_peer(const int32_t* all, int ld, int R, int
     pl->ok = ok ? 1 : 0;
     pl->units_in = pl->pairs_in = pl->pairs_out = 0;
     for (int r = 0; r < AEM_EP_MAX_RANKS; ++r) {
-        pl->dst_unit_off[r] = pl->dst_pair_off[r] = pl->send_pair_off[r] = 0;
+        pl->dst_pair_off[r] = pl->send_pair_off[r] = 0;
         pl->recv_pair_off[r] = pl->ret_off[r] = 0;
     }
+    for (int e = 0; e < AEM_MAX_EXPERTS; ++e) pl->dst_unit_off[e] = 0;
     pl->recv_pair_off[AEM_EP_MAX_RANKS] = 0;
-    for (int i = 0; i <= E; ++i) groups[i] = 0;
+    for (int i = 0; i <= el; ++i) groups[i] = 0;
     if (!ok) return;
+    // units of expert e from source s (placement positions)
+    auto eu = [&](int s, int e) -> int64_t {
+        return (in(s) && in(e / el)) ? row(s)[e + 1] - row(s)[e] : 0;
+    };
     int64_t acc = 0;
     for (int r = 0; r < R; ++r) {
         pl->send_pair_off[r] = static_cast<int32_t>(acc);
@@ -180,13 +185,21 @@ __host__ __device__ inline void plan_peer(const int32_t* all, int ld, int R, int
     }
     pl->pairs_out = static_cast<int32_t>(acc);
     for (int r = 0; r < R; ++r) {
-        int64_t u = 0, p = 0;
-        for (int s = 0; s < me; ++s) {
-            u += units(s, r);
-            p += pairs(s, r);
-        }
-        pl->dst_unit_off[r] = static_cast<int32_t>(u);
+        int64_t p = 0;
+        for (int s = 0; s < me; ++s) p += pairs(s, r);
         pl->dst_pair_off[r] = static_cast<int32_t>(p);
+        // rank r receives expert-major: its local experts in order, every
+        // source's units of one expert contiguous, sources in rank order
+        int64_t u = 0;
+        for (int e = r * el; e < (r + 1) * el; ++e) {
+            int64_t before = 0, all_s = 0;
+            for (int s = 0; s < R; ++s) {
+                if (s < me) before += eu(s, e);
+                all_s += eu(s, e);
+            }
+            pl->dst_unit_off[e] = static_cast<int32_t>(u + before);
+            u += all_s;
+        }
     }
     acc = 0;
     for (int s = 0; s < R; ++s) {
@@ -199,11 +212,9 @@ __host__ __device__ inline void plan_peer(const int32_t* all, int ld, int R, int
     pl->recv_pair_off[R] = static_cast<int32_t>(acc);
     pl->pairs_in = static_cast<int32_t>(acc);
     int64_t g = 0;
-    for (int s = 0; s < R; ++s) {
-        for (int e = 0; e < el; ++e) {
-            if (in(s)) g += row(s)[me * el + e + 1] - row(s)[me * el + e];
-            groups[s * el + e + 1] = static_cast<int32_t>(g);
-        }
+    for (int e = 0; e < el; ++e) {
+        for (int s = 0; s < R; ++s) g += eu(s, me * el + e);
+        groups[e + 1] = static_cast<int32_t>(g);
     }
     pl->units_in = static_cast<int32_t>(g);
 }
@@ -477,9 +488,10 @@ __device__ __forceinline__ void copy_row_bf16(const XT* __restrict__ in, __nv_bf
 
 // Push: (a) each (destination, token) pair's activation row into the
 // destination's pair rows; (b) each unit's (pair row, gate weight) into the
-// destination's unit row.  Units of this rank are expert-sorted, so those
-// for rank r are the contiguous range [starts[r*el], starts[(r+1)*el]).
-// Units for a rank outside the step have no pair and are skipped (they fail).
+// destination's unit row.  Units of this rank are expert-sorted, so those of
+// expert e are the contiguous range [starts[e], starts[e+1]), landing from
+// dst_unit_off[e] on in e's owner.  Units for a rank outside the step have no
+// pair and are skipped (they fail).
 template <typename XT>
 __global__ void __launch_bounds__(kCopyThreads)
     ep_dispatch_kernel(const XT* __restrict__ x, int64_t T, int64_t d, int R, int el,
@@ -487,15 +499,14 @@ __global__ void __launch_bounds__(kCopyThreads)
                        const int32_t* __restrict__ src_token, const float* __restrict__ rowscale,
                        int k, const aem_ep_peer_plan* __restrict__ plan, EpPeers peers,
                        ExchangeLayout lay, int64_t ucap, int64_t pcap, int* __restrict__ err) {
-    __shared__ int bnd[AEM_EP_MAX_RANKS + 1];
-    __shared__ int upos[AEM_EP_MAX_RANKS];
+    __shared__ int bnd[AEM_MAX_EXPERTS + 1];
+    __shared__ int upos[AEM_MAX_EXPERTS];
     __shared__ int ppos[AEM_EP_MAX_RANKS];
     if (!plan->ok) return;
-    for (int i = threadIdx.x; i <= R; i += blockDim.x) bnd[i] = starts[i * el];
-    for (int i = threadIdx.x; i < R; i += blockDim.x) {
-        upos[i] = plan->dst_unit_off[i];
-        ppos[i] = plan->dst_pair_off[i];
-    }
+    const int E = R * el;
+    for (int i = threadIdx.x; i <= E; i += blockDim.x) bnd[i] = starts[i];
+    for (int i = threadIdx.x; i < E; i += blockDim.x) upos[i] = plan->dst_unit_off[i];
+    for (int i = threadIdx.x; i < R; i += blockDim.x) ppos[i] = plan->dst_pair_off[i];
     __syncthreads();
     const int lane = threadIdx.x & 31;
     const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
@@ -513,15 +524,20 @@ __global__ void __launch_bounds__(kCopyThreads)
         auto* dst = reinterpret_cast<__nv_bfloat16*>(peers.base[r] + lay.xpair) + row * d;
         copy_row_bf16<XT>(x + t * d, dst, d, lane);
     }
-    const int64_t U = min(static_cast<int64_t>(bnd[R]), T * k);
+    const int64_t U = min(static_cast<int64_t>(bnd[E]), T * k);
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < U;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        int r = 0;
-        while (r + 1 < R && i >= bnd[r + 1]) ++r;
+        int lo = 0, hi = E - 1;  // the expert segment holding sorted unit i
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (bnd[mid] <= i) lo = mid; else hi = mid - 1;
+        }
+        const int e = lo;
+        const int r = e / el;
         const int64_t t = src_token[i];
         const int pl = (t >= 0 && t < T) ? pair_local[static_cast<int64_t>(r) * T + t] : -1;
         if (pl < 0) continue;  // a rank outside the step: the unit fails
-        const int64_t pos = upos[r] + (i - bnd[r]);
+        const int64_t pos = upos[e] + (i - bnd[e]);
         if (pos >= ucap) {
             atomicOr(err, ERR_EP_BOUNDS);
             continue;
@@ -674,7 +690,7 @@ struct Ep {
     long long* corr = nullptr;          // [k][E]
     int32_t* payload = nullptr;         // [pay_ld]
     aem_ep_peer_plan* plan = nullptr;
-    int32_t* groups = nullptr;          // [E+1]
+    int32_t* groups = nullptr;          // [E/R+1] received rows per local expert
     int32_t* pair_local = nullptr;      // [R][T]
     StepState* st = nullptr;
     void* xu = nullptr;                 // bf16 [units_cap][d]
@@ -974,14 +990,13 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
         count_launches(4);
     }
     prof.end(AEM_PHASE_DISPATCH, s);
-    // 6. local expert FFN on the (source, expert) groups; the down GEMM
+    // 6. local expert FFN, one row group per local expert; the down GEMM
     //    scales by the gate weight and sums the units of each pair
     {
         const int64_t hint = std::max<int64_t>(U, 1);  // expected received units
         GemmArgs up_a;
         up_a.w = up;
-        up_a.G = R * el;
-        up_a.wmod = el;
+        up_a.G = el;
         up_a.group_rows = groups;
         up_a.M = units_cap;
         up_a.max_rows = units_cap;
@@ -996,8 +1011,7 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
         prof.end(AEM_PHASE_UP, s);
         GemmArgs dn;
         dn.w = down;
-        dn.G = R * el;
-        dn.wmod = el;
+        dn.G = el;
         dn.group_rows = groups;
         dn.M = units_cap;
         dn.max_rows = units_cap;

@@ -59,13 +59,14 @@ __device__ __forceinline__ float4 load_x4<__nv_bfloat16>(const __nv_bfloat16* p)
     return f;
 }
 
-template <int GROUP, int NSLOT, int kTPG, typename XT, bool EXACT>
-__global__ void __launch_bounds__(kThreads)
+template <int GROUP, int NSLOT, int kTPG, int WARPS, typename XT, bool EXACT>
+__global__ void __launch_bounds__(WARPS * 32)
     gating_kernel(const XT* __restrict__ x, const float4* __restrict__ wpk,
                   const float* __restrict__ bias, int64_t N, int D, int E, int k, int ksel,
                   int32_t* __restrict__ idx_out, float* __restrict__ val_out) {
+    constexpr int kThreads = WARPS * 32;
     constexpr int GPW = 32 / GROUP;
-    constexpr int TOK = kWarps * GPW * kTPG;  // tokens per CTA
+    constexpr int TOK = WARPS * GPW * kTPG;  // tokens per CTA
     constexpr int EPAD = GROUP * NSLOT;
     constexpr int DK_E = EPAD <= 64 ? 64 : (EPAD <= 128 ? 32 : 16);
     constexpr int DK = (TOK * (DK_E + 4) * 4 > 36 * 1024) ? DK_E / 2 : DK_E;
@@ -252,12 +253,13 @@ __global__ void __launch_bounds__(kThreads)
     }
 }
 
-template <int GROUP, int NSLOT, int TPG, typename XT, bool EXACT>
+template <int GROUP, int NSLOT, int TPG, typename XT, bool EXACT, int WARPS = kWarps>
 cudaError_t launch_one(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
                        float* val, cudaStream_t s) {
-    constexpr int TOK = kWarps * (32 / GROUP) * TPG;
+    constexpr int TOK = WARPS * (32 / GROUP) * TPG;
     const int64_t blocks = (N + TOK - 1) / TOK;
-    gating_kernel<GROUP, NSLOT, TPG, XT, EXACT><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(
+    gating_kernel<GROUP, NSLOT, TPG, WARPS, XT, EXACT>
+        <<<static_cast<unsigned>(blocks), WARPS * 32, 0, s>>>(
         static_cast<const XT*>(x), reinterpret_cast<const float4*>(g.wt), g.bias, N,
         static_cast<int>(g.D), static_cast<int>(g.E), k, ksel, idx, val);
     return cudaGetLastError();
@@ -274,6 +276,18 @@ cudaError_t dispatch_e(const Gate& g, const void* x, int64_t N, int k, int ksel,
             case 16: return launch_one<16, 1, 8, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
             case 32: return launch_one<32, 1, 8, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
             case 64: return launch_one<32, 2, 8, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+            default: break;
+        }
+    }
+    if (N <= 4096) {
+        // Few tokens: 2 tokens per lane group and 4 warps per CTA, so that
+        // even T = 2048 spreads over 256 CTAs; the weights' chunks then come
+        // from L2 once per 8 tokens.
+        switch (g.Epad) {
+            case 32: return launch_one<32, 1, 2, XT, EXACT, 4>(g, x, N, k, ksel, idx, val, s);
+            case 64: return launch_one<32, 2, 2, XT, EXACT, 4>(g, x, N, k, ksel, idx, val, s);
+            case 128: return launch_one<32, 4, 2, XT, EXACT, 4>(g, x, N, k, ksel, idx, val, s);
+            case 256: return launch_one<32, 8, 2, XT, EXACT, 4>(g, x, N, k, ksel, idx, val, s);
             default: break;
         }
     }

@@ -89,6 +89,7 @@ struct TcParams {
     int out_bf16;
     int relu;
     int atomic_add;
+    int red_v4;             // atomic_add with N, ldo multiples of 4: 16-byte reductions
     const int* rowmap;
     const float* rowscale;
     int* err;
@@ -451,6 +452,52 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t r[16];
                 tc_ld_32x32b_x16(tbase + c0, r);
                 tc_wait_ld();
+                if (p.red_v4) {
+                    // 16-byte reductions: a 4x4 transpose inside each lane quad
+                    // gives lane 4m+i the four channels of quad m at column i,
+                    // so one red.v4 replaces four scalar ones.
+                    const int qi = lane & 3;
+                    const bool qvalid = ti.n0 + q * 32 + (lane & ~3) < p.N;  // N % 4 == 0
+                    float* obase = reinterpret_cast<float*>(p.out) + ti.n0 + q * 32 + (lane & ~3);
+#pragma unroll
+                    for (int j4 = 0; j4 < 16; j4 += 4) {
+                        float a[4];
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
+                            a[c] = __uint_as_float(r[j4 + c]) * sc *
+                                   __shfl_sync(0xFFFFFFFFu, my_rs, j4 + c);
+                        {
+                            const float s0 = (qi & 1) ? a[0] : a[1];
+                            const float s1 = (qi & 1) ? a[2] : a[3];
+                            const float t0 = __shfl_xor_sync(0xFFFFFFFFu, s0, 1);
+                            const float t1 = __shfl_xor_sync(0xFFFFFFFFu, s1, 1);
+                            if (qi & 1) {
+                                a[0] = t0;
+                                a[2] = t1;
+                            } else {
+                                a[1] = t0;
+                                a[3] = t1;
+                            }
+                        }
+                        {
+                            const float s0 = (qi & 2) ? a[0] : a[2];
+                            const float s1 = (qi & 2) ? a[1] : a[3];
+                            const float t0 = __shfl_xor_sync(0xFFFFFFFFu, s0, 2);
+                            const float t1 = __shfl_xor_sync(0xFFFFFFFFu, s1, 2);
+                            if (qi & 2) {
+                                a[0] = t0;
+                                a[1] = t1;
+                            } else {
+                                a[2] = t0;
+                                a[3] = t1;
+                            }
+                        }
+                        const int64_t orow = __shfl_sync(0xFFFFFFFFu, my_orow, j4 + qi);
+                        if (qvalid && c0 + j4 + qi < ti.nrows)
+                            red_add_v4(obase + orow * p.ldo, a[0], a[1], a[2], a[3]);
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int64_t orow = __shfl_sync(0xFFFFFFFFu, my_orow, j);
@@ -570,6 +617,10 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
     p.out_bf16 = a.out_bf16 ? 1 : 0;
     p.relu = a.relu ? 1 : 0;
     p.atomic_add = (a.atomic_add || ks > 1) ? 1 : 0;
+    p.red_v4 = (p.atomic_add && !a.relu && w.N % 4 == 0 && a.ldo % 4 == 0 &&
+                (reinterpret_cast<uintptr_t>(a.out) & 15) == 0)
+                   ? 1
+                   : 0;
     p.rowmap = a.rowmap;
     p.rowscale = a.rowscale;
     p.err = err;

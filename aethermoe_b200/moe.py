@@ -170,8 +170,8 @@ def ep_plan_exchange(starts, rank):
 def ep_plan_peer(payload, rank, units_cap, pairs_cap, ret_cap, live=None):
     """Host form of the per-step peer-exchange plan: ``payload [R, E+1+R]``
     (every rank's expert starts, then its pair counts per destination) ->
-    ``(plan dict, groups [E+1])`` for ``rank``; ``live`` is the bit mask of
-    the ranks taking part (default: all)."""
+    ``(plan dict, groups [E/R+1])`` for ``rank`` (received rows per local
+    expert); ``live`` is the bit mask of the ranks taking part (default: all)."""
     pay = np.ascontiguousarray(payload, dtype=np.int32)
     r, w = pay.shape
     e = w - 1 - r
@@ -184,10 +184,11 @@ def ep_plan_peer(payload, rank, units_cap, pairs_cap, ret_cap, live=None):
                                            groups.ctypes.data), "aem_ep_plan_peer")
     out = dict(ok=plan.ok, units_in=plan.units_in, pairs_in=plan.pairs_in,
                pairs_out=plan.pairs_out)
-    for name in ("dst_unit_off", "dst_pair_off", "send_pair_off", "ret_off"):
+    for name in ("dst_pair_off", "send_pair_off", "ret_off"):
         out[name] = np.array(getattr(plan, name)[:r], np.int64)
+    out["dst_unit_off"] = np.array(plan.dst_unit_off[:e], np.int64)  # per expert position
     out["recv_pair_off"] = np.array(plan.recv_pair_off[:r + 1], np.int64)
-    return out, groups
+    return out, groups[:e // r + 1]
 
 
 class EPLayer:

@@ -303,7 +303,8 @@ typedef struct aem_ep_peer_plan {
     int32_t units_in;   /* units this rank receives (rows of its grouped GEMMs) */
     int32_t pairs_in;   /* pairs this rank receives */
     int32_t pairs_out;  /* pairs this rank sends (rows of its return buffer) */
-    int32_t dst_unit_off[AEM_EP_MAX_RANKS];      /* this rank's first unit row in rank r's buffer */
+    int32_t dst_unit_off[AEM_MAX_EXPERTS];       /* this rank's first unit row of expert e (by
+                                                    placement position) in its owner's buffer */
     int32_t dst_pair_off[AEM_EP_MAX_RANKS];      /* this rank's first pair row in rank r's buffer */
     int32_t send_pair_off[AEM_EP_MAX_RANKS];     /* this rank's pairs for rank r start here */
     int32_t recv_pair_off[AEM_EP_MAX_RANKS + 1]; /* pairs received from source s start here */
@@ -317,8 +318,9 @@ typedef struct aem_ep_peer_plan {
  * ranks are ignored, and so are units for them (those units fail).
  * Capacities: units_cap (received units), pairs_cap (received pairs),
  * ret_cap (return rows), the same on every rank.  Writes the plan of `rank`
- * and groups [E+1] (R*(E/R) = E row groups): the row offsets of the
- * received (source, local expert) segments, sources outer.  A plan whose counts do not fit
+ * and groups [E/R+1]: the row offsets of the received units of each local
+ * expert (all sources' units of one expert are contiguous, sources in rank
+ * order inside).  A plan whose counts do not fit
  * has ok = 0 (every rank derives the same verdict from the same data). */
 aem_status aem_ep_plan_peer(const int32_t* all, int R, int E, int rank, uint64_t live,
                             int64_t units_cap, int64_t pairs_cap, int64_t ret_cap,

@@ -10,7 +10,7 @@ send segments.  It then replays one peer-memory exchange with the plans of
 ``aem_ep_plan_peer`` (the function the layer runs on the device): every
 pushed pair and unit lands on a distinct row inside the destination's
 received range, every unit row of the destination's grouped GEMM holds a unit
-of the right (source, expert) group pointing at its token's pair, and every
+of that row group's expert pointing at its token's pair, and every
 pair sum returned lands on the row the source's combine reads for that
 (token, destination).  No GPU involved.
 """
@@ -125,12 +125,12 @@ def _replay_peer_exchange(res, world, tl):
                 row = int(plans[s_]["dst_pair_off"][r]) + pl[r, t]
                 assert row not in xpair[r]
                 xpair[r][row] = (s_, t)
-            lo, hi = starts[r * el], starts[(r + 1) * el]
-            for i in range(lo, hi):
-                u = order[i]
-                pos = int(plans[s_]["dst_unit_off"][r]) + (i - lo)
-                assert pos not in units[r]
-                units[r][pos] = (s_, u, int(plans[s_]["dst_pair_off"][r]) + pl[r, u % tl])
+            for e in range(r * el, (r + 1) * el):
+                for i in range(starts[e], starts[e + 1]):
+                    u = order[i]
+                    pos = int(plans[s_]["dst_unit_off"][e]) + (i - starts[e])
+                    assert pos not in units[r]
+                    units[r][pos] = (s_, u, int(plans[s_]["dst_pair_off"][r]) + pl[r, u % tl])
         res[s_]["_pl"] = pl
     ret = [dict() for _ in range(world)]  # source-side return rows
     for r in range(world):
@@ -141,7 +141,7 @@ def _replay_peer_exchange(res, world, tl):
         for pos, (s_, u, prow) in units[r].items():
             e = int(res[s_]["eff"][u])
             grp = np.searchsorted(g, pos, side="right") - 1
-            assert grp == s_ * el + (e - r * el)            # (source, local expert) group
+            assert grp == e - r * el                        # the local expert's row group
             assert xpair[r][prow] == (s_, u % tl)           # the unit's token
         roff = p["recv_pair_off"]
         for prow, (s_, t) in xpair[r].items():
@@ -234,11 +234,11 @@ def test_peer_exchange_plan_with_a_rank_left_out():
                 row = int(res[s_]["p_dst_pair_off"][r]) + pl[r, t]
                 assert row not in xpair[r]
                 xpair[r][row] = (s_, t)
-            lo, hi = starts[r * el], starts[(r + 1) * el]
-            for i in range(lo, hi):
-                pos = int(res[s_]["p_dst_unit_off"][r]) + (i - lo)
-                assert pos not in units[r]
-                units[r][pos] = (s_, order[i])
+            for e in range(r * el, (r + 1) * el):
+                for i in range(starts[e], starts[e + 1]):
+                    pos = int(res[s_]["p_dst_unit_off"][e]) + (i - starts[e])
+                    assert pos not in units[r]
+                    units[r][pos] = (s_, order[i])
         failed += int((dest == dead).sum())
         res[s_]["_pl"] = pl
     assert failed > 0  # the dead rank's experts had units: those fail
@@ -249,7 +249,7 @@ def test_peer_exchange_plan_with_a_rank_left_out():
         for pos, (s_, u) in units[r].items():
             e = int(res[s_]["eff"][u])
             grp = np.searchsorted(p["pgroups"], pos, side="right") - 1
-            assert grp == s_ * el + (e - r * el)
+            assert grp == e - r * el
         roff = p["p_recv_pair_off"]
         for prow, (s_, t) in xpair[r].items():
             row = int(p["p_ret_off"][s_]) + prow - int(roff[s_])

@@ -231,8 +231,9 @@ def test_device_pointer_entry_point(cuda):
 
 @pytest.mark.parametrize("e,k,d", [(17, 3, 37), (33, 6, 64), (64, 6, 130), (8, 2, 96), (5, 5, 16)])
 def test_many_tokens_kernel_bit_exact(shim, e, k, d):
-    """>= 4096 tokens take the token-major kernel (experts split over threads);
-    padding of E and D, k == E, and the reroute choice included."""
+    """More than 4096 tokens take the large-batch configuration (several
+    tokens per lane group); padding of E and D, k == E, and the reroute
+    choice included."""
     fg, _ = shim
     h, w, b = cases._gating_inputs(np.random.default_rng(e * 100 + d), 5000, d, e)
     w[:, e - 1] = w[:, 0]
@@ -240,5 +241,20 @@ def test_many_tokens_kernel_bit_exact(shim, e, k, d):
     extra = 1 if k < e else 0
     idx, val = fg.gating(h, w, b, k, k_extra=extra)
     oidx, oval = O.fused_gating(h, w, b, k, extra=extra)
+    np.testing.assert_array_equal(idx, oidx)
+    np.testing.assert_allclose(val, oval, atol=1e-6)
+
+
+@pytest.mark.parametrize("e", [100, 200, 256])
+@pytest.mark.parametrize("t", [7, 3000, 9000])
+def test_wide_gates_bit_exact(shim, e, t):
+    """128- and 256-expert gates across the few-token (<= 4096) and
+    many-token configurations, with an exact tie and the reroute choice."""
+    fg, _ = shim
+    h, w, b = cases._gating_inputs(np.random.default_rng(e + t), t, 72, e)
+    w[:, e - 1] = w[:, 3]
+    b[e - 1] = b[3]
+    idx, val = fg.gating(h, w, b, 4, k_extra=1)
+    oidx, oval = O.fused_gating(h, w, b, 4, extra=1)
     np.testing.assert_array_equal(idx, oidx)
     np.testing.assert_allclose(val, oval, atol=1e-6)
