@@ -44,7 +44,24 @@ class MoeConfig(ctypes.Structure):
                 ("capacity", _u64), ("gating_mode", _int)]
 
 
+class SeqSlice(ctypes.Structure):
+    """``aem_seq_slice``: one sequence's rows in a continuous-batching iteration."""
+    _fields_ = [("seq_id", ctypes.c_uint64), ("x", ctypes.c_void_p), ("out", ctypes.c_void_p),
+                ("tokens", ctypes.c_int64)]
+
+
 EP_MAX_RANKS = 64
+METRIC_MOE_STEP, METRIC_EP_STEP = 0, 1
+
+
+class MetricStats(ctypes.Structure):
+    """``aem_metric_stats`` (the reference's MetricStats, src/core/telemetry.hpp:35-42)."""
+    _fields_ = [("count", ctypes.c_uint64), ("mean_ns", ctypes.c_double),
+                ("p50_ns", ctypes.c_double), ("p95_ns", ctypes.c_double),
+                ("p99_ns", ctypes.c_double), ("max_ns", ctypes.c_double)]
+
+    def as_dict(self):
+        return {name: getattr(self, name) for name, _ in self._fields_}
 
 
 class EpPeerPlan(ctypes.Structure):
@@ -109,6 +126,12 @@ _SIGS = {
     "aem_moe_profile_read": (_int, [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64)]),
     "aem_ep_profile": (_int, [_vp, _int]),
     "aem_ep_profile_read": (_int, [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64)]),
+    "aem_moe_forward_slices": (_int, [_vp, ctypes.POINTER(SeqSlice), _int, _int, _int, _vp]),
+    "aem_telemetry_enable": (None, [_int]),
+    "aem_telemetry_enabled": (_int, []),
+    "aem_telemetry_snapshot": (_int, [_int, ctypes.POINTER(MetricStats), ctypes.POINTER(_u64)]),
+    "aem_telemetry_reset": (_int, []),
+    "aem_metric_stats_of": (_int, [_vp, _i64, ctypes.POINTER(MetricStats)]),
 }
 NUM_PHASES = 8
 PHASES = ["gating", "route", "up_gemm", "down_gemm", "combine", "dispatch", "return", "exchange"]
@@ -268,3 +291,31 @@ def quantize_device(w, stream=None):
     check(lib().aem_quantize_int8(w.data_ptr(), k, n, q.data_ptr(), s.data_ptr(),
                                   ctypes.c_void_p(st.cuda_stream)), "aem_quantize_int8")
     return q, s
+
+
+def telemetry_enable(enabled=True):
+    """Per-step device-time telemetry of the MoE layers (process-wide switch)."""
+    lib().aem_telemetry_enable(1 if enabled else 0)
+
+
+def telemetry_snapshot(metric=METRIC_MOE_STEP):
+    """``(stats dict, dropped)`` of every completed step of ``metric`` so far."""
+    st = MetricStats()
+    dropped = ctypes.c_uint64()
+    check(lib().aem_telemetry_snapshot(metric, ctypes.byref(st), ctypes.byref(dropped)),
+          "aem_telemetry_snapshot")
+    return st.as_dict(), dropped.value
+
+
+def telemetry_reset():
+    check(lib().aem_telemetry_reset(), "aem_telemetry_reset")
+
+
+def metric_stats_of(latencies_ns):
+    """Nearest-rank statistics of host latencies (the snapshot's arithmetic)."""
+    import numpy as np
+    a = np.ascontiguousarray(latencies_ns, dtype=np.uint64)
+    st = MetricStats()
+    check(lib().aem_metric_stats_of(a.ctypes.data if a.size else None, a.size, ctypes.byref(st)),
+          "aem_metric_stats_of")
+    return st.as_dict()

@@ -885,6 +885,7 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
     int* err = device_error_word(dev);
     AEM_REQUIRE(err != nullptr, "aem_ep_forward: no device error word");
     const int tol = tolerant ? 1 : 0;
+    StepTimer timer(AEM_METRIC_EP_STEP, s);
     const uint64_t q = ++seq;
     char* mine = static_cast<char*>(xreg);
     const uint64_t* flags = reinterpret_cast<const uint64_t*>(mine + lay.flags);

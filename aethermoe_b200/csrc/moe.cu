@@ -207,6 +207,7 @@ aem_status Moe::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_d
     last_T = T;
     if (T == 0) return AEM_OK;
     AEM_TRY(reserve(T));
+    StepTimer timer(AEM_METRIC_MOE_STEP, s);
     const int k = cfg.top_k, E = cfg.num_experts;
     const int ksel = k < E ? k + 1 : k;
     const int64_t U = T * k, d = cfg.d_model, f = cfg.d_ffn;
@@ -335,6 +336,7 @@ aem_status aem_moe_free(aem_moe_t moe) {
     cudaSetDevice(m->gate->device);
     cudaDeviceSynchronize();
     cudaFree(m->buf);
+    aem::seam_free(m);
     delete m;
     return AEM_OK;
 }

@@ -35,6 +35,8 @@ struct Moe {
     void* h = nullptr;      // bf16 [U, ffn]
     float* y = nullptr;     // f32 [T*k, d]
     PhaseProfiler prof;
+    // scheduler seam (seam.cu): staged rows of one iteration and its slice table
+    struct SeamStage* seam = nullptr;
 
     // Routing buffers for T tokens, plus the expert-FFN buffers (xperm, h, y)
     // unless expert_buffers is false (the expert-parallel layer has its own).
@@ -45,5 +47,7 @@ struct Moe {
     // scattered to row t*k+j), combine -- on xperm/starts/rowmap/rowscale.
     aem_status expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaStream_t s);
 };
+
+void seam_free(Moe* m);  // releases the scheduler seam's buffers (seam.cu)
 
 }  // namespace aem

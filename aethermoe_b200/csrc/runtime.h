@@ -18,6 +18,23 @@ const char* last_error_cstr();
 void count_launches(int n);
 
 // Per-phase device-time accounting with CUDA events on the step's stream.
+// Telemetry of one layer step (telemetry.cu): when telemetry is on, records
+// a CUDA event on `s` at construction and at destruction, and hands the pair
+// to the process-wide recorder.  No cost beyond one atomic load when off.
+class StepTimer {
+public:
+    StepTimer(int metric, cudaStream_t s);
+    ~StepTimer();
+    StepTimer(const StepTimer&) = delete;
+    StepTimer& operator=(const StepTimer&) = delete;
+
+private:
+    int metric_;
+    cudaStream_t stream_;
+    int device_ = 0;
+    cudaEvent_t a_ = nullptr, b_ = nullptr;
+};
+
 struct PhaseProfiler {
     bool on = false;
     int64_t steps = 0;

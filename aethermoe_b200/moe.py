@@ -82,6 +82,28 @@ class MoELayer:
                    "aem_moe_forward")
         return out
 
+    def forward_slices(self, slices, out_dtype=None, stream=None):
+        """One scheduler iteration as one batch: ``slices`` is a list of
+        ``(seq_id, x)`` with ``x`` a CUDA tensor [tokens, d] (decode steps and
+        prefill chunks, in the scheduler's order).  Returns the output tensors
+        in the same order (``aem_moe_forward_slices``)."""
+        import torch
+        if not slices:
+            return []
+        xd = slices[0][1]
+        outs = [torch.empty((x.shape[0], self.d_model), dtype=out_dtype or xd.dtype,
+                            device=x.device) for _, x in slices]
+        arr = (_lib.SeqSlice * len(slices))()
+        for i, ((sid, x), o) in enumerate(zip(slices, outs)):
+            if x.dtype != xd.dtype:
+                raise ValueError("all slices must share one dtype")
+            arr[i] = _lib.SeqSlice(int(sid), x.data_ptr(), o.data_ptr(), int(x.shape[0]))
+        _lib.check(_lib.lib().aem_moe_forward_slices(self.handle, arr, len(slices),
+                                                     _dtype_code(xd), _dtype_code(outs[0]),
+                                                     _stream_ptr(stream)),
+                   "aem_moe_forward_slices")
+        return outs
+
     def forward_host(self, x, out_dtype=np.float32):
         """Host buffers through ``aem_moe_forward_host`` (copies included)."""
         x = np.ascontiguousarray(x)

@@ -310,6 +310,7 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
     import aethermoe_b200 as aem
+    from aethermoe_b200 import _lib as aem_lib
     from aethermoe_b200 import _lib
     from aethermoe_b200.moe import EPLayer, MoELayer, ep_unique_id
 
@@ -361,6 +362,8 @@ def run_ours(args):
     time.sleep(0.3 if clocks else 0.0)
     barrier()
     layer.profile(True)
+    aem_lib.telemetry_reset()
+    aem_lib.telemetry_enable(True)
     launches0 = aem.lib().aem_kernel_launches()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
@@ -373,6 +376,9 @@ def run_ours(args):
     t_wall1 = time.time()
     launches = aem.lib().aem_kernel_launches() - launches0
     ms = ev0.elapsed_time(ev1)
+    step_stats, _ = aem_lib.telemetry_snapshot(aem_lib.METRIC_MOE_STEP if world == 1
+                                               else aem_lib.METRIC_EP_STEP)
+    aem_lib.telemetry_enable(False)
     phases, nsteps = layer.profile_read()
     layer.profile(False)
     aem.check(aem.lib().aem_device_status(ctypes_stream(stream)))
@@ -427,6 +433,12 @@ def run_ours(args):
             "phases_ms_per_step": {k: v / max(1, nsteps) for k, v in phases.items() if v > 0},
             "e2e": e2e,
             "gpu_launches": int(launches),
+            "step_latency_us": {"count": step_stats["count"],
+                                "p50": step_stats["p50_ns"] / 1e3,
+                                "p99": step_stats["p99_ns"] / 1e3,
+                                "max": step_stats["max_ns"] / 1e3,
+                                "source": "aem_telemetry_snapshot: device time of each step "
+                                          "(rank 0)"},
             "gpu_launches_per_step": launches / args.steps,
             "clocks": clock_summary,
         }

@@ -390,6 +390,54 @@ aem_status aem_ep_profile_read(aem_ep_t ep, double* ms, int64_t* steps);
 aem_status aem_ep_last_routing(aem_ep_t ep, int32_t* idx, float* val, uint32_t* effective,
                                void* stream);
 
+/* ---- scheduler -> MoE layer seam ----------------------------------------------------- */
+
+/* One sequence's share of a continuous-batching iteration: the reference's
+ * StepResult (src/core/scheduler.hpp:43-48) plus where that sequence's rows
+ * live -- `tokens` consecutive hidden rows (a prefill chunk, or 1 for a
+ * decode step). */
+typedef struct aem_seq_slice {
+    uint64_t seq_id;
+    const void* x; /* device [tokens, d_model], x dtype */
+    void* out;     /* device [tokens, d_model], out dtype */
+    int64_t tokens;
+} aem_seq_slice;
+
+/* Runs one ContinuousBatchingScheduler::step() iteration
+ * (src/core/scheduler.hpp:75-146) through the MoE layer as ONE batch, in the
+ * order of `slices` (the scheduler's result order: decode steps, then prefill
+ * chunks): batch_position follows that order, so capacity routing ranks the
+ * iteration's tokens exactly as over their concatenation.  One kernel gathers
+ * the slices' rows, aem_moe_forward runs, one kernel scatters the outputs.
+ * No counterpart in the reference, which never connects its scheduler to the
+ * kernels (README.md:392-397).  Slices with tokens == 0 are allowed. */
+aem_status aem_moe_forward_slices(aem_moe_t moe, const aem_seq_slice* slices, int n_slices,
+                                  aem_dtype x_dtype, aem_dtype out_dtype, void* stream);
+
+/* ---- per-step telemetry ---------------------------------------------------------- */
+
+/* The reference's TelemetryRecorder / TelemetryFlusher pattern
+ * (src/core/telemetry.hpp:131-250) for MoE-layer steps: a process-wide
+ * switch (default off; one relaxed atomic load per step when off); when on,
+ * every aem_moe_forward / aem_ep_forward(_tolerant) records its device time
+ * with a CUDA event pair on its stream, harvested without ever waiting on an
+ * unfinished step. */
+enum { AEM_METRIC_MOE_STEP = 0, AEM_METRIC_EP_STEP = 1, AEM_NUM_METRICS = 2 };
+typedef struct aem_metric_stats {
+    uint64_t count; /* MetricStats (telemetry.hpp:35-42): nearest-rank percentiles */
+    double mean_ns, p50_ns, p95_ns, p99_ns, max_ns;
+} aem_metric_stats;
+void aem_telemetry_enable(int enabled); /* TelemetryRecorder::set_enabled */
+int aem_telemetry_enabled(void);
+/* Statistics of every completed step of `metric` so far
+ * (TelemetryFlusher::snapshot); *dropped (nullable) = steps not recorded
+ * because too many were in flight or the sample store was full. */
+aem_status aem_telemetry_snapshot(int metric, aem_metric_stats* out, uint64_t* dropped);
+aem_status aem_telemetry_reset(void); /* TelemetryRecorder::reset_for_testing */
+/* The snapshot's arithmetic on given latencies (host, no GPU):
+ * detail::compute_stats, telemetry.hpp:88-113. */
+aem_status aem_metric_stats_of(const uint64_t* latencies_ns, int64_t n, aem_metric_stats* out);
+
 #ifdef __cplusplus
 }
 #endif
