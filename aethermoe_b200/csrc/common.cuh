@@ -175,17 +175,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, uint64_t
         : "memory");
 }
 
-// Four rows y0..y3 of a 2-D tensor map whose box is one row high, columns
-// [x, x + box width), into 4 consecutive box rows at dst (no multicast).
-__device__ __forceinline__ void tma_gather4(void* dst, const void* map, uint64_t* bar, int x,
-                                            int y0, int y1, int y2, int y3) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
-        "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3)
-        : "memory");
-}
-
 // Non-tensor bulk copy global -> shared (16-byte aligned, size a multiple of 16).
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
                                           uint64_t* bar) {

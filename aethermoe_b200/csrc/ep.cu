@@ -23,8 +23,7 @@
 //   Step: gating -> slot counts -> [all-gather] -> capacity routing (global
 //   ranks) -> pair numbering -> [all-gather of expert starts + pair counts]
 //   -> on-device plan -> push pairs + unit metadata into the destinations ->
-//   [barrier] -> grouped up GEMM (+ReLU) gathering unit rows from the
-//   received pair rows -> grouped
+//   [barrier] -> expand pairs to units -> grouped up GEMM (+ReLU) -> grouped
 //   down GEMM, gate-weighted and pre-reduced per pair -> push the pair sums
 //   back into the sources -> [barrier] -> per-token sum over destinations.
 // The bracketed steps are peer-memory mailboxes and per-step flags: a rank
@@ -548,25 +547,34 @@ __global__ void __launch_bounds__(kCopyThreads)
     }
 }
 
-// Destination side, after the dispatch point: every received unit's pair row
-// is checked (the up GEMM gathers its activation through it and the down
-// GEMM accumulates into it; a row no source wrote is pointed at row 0 with
-// weight 0, so it contributes nothing), and the pair sums are zeroed for the
-// down GEMM to accumulate into.
+// Destination side, after the dispatch point: unit rows from the received
+// pair rows (the grouped GEMM input), and zeroed pair sums for the down GEMM
+// to accumulate into.
 __global__ void __launch_bounds__(kCopyThreads)
-    ep_receive_kernel(int32_t* __restrict__ rowmap_in, float* __restrict__ rowscale_in,
-                      const aem_ep_peer_plan* __restrict__ plan, const StepState* st, int64_t d,
-                      float* __restrict__ ret_acc, int* __restrict__ err) {
+    ep_expand_kernel(const __nv_bfloat16* __restrict__ xpair, int32_t* __restrict__ rowmap_in,
+                     float* __restrict__ rowscale_in, const aem_ep_peer_plan* __restrict__ plan,
+                     const StepState* st, int64_t d, __nv_bfloat16* __restrict__ xu,
+                     float* __restrict__ ret_acc, int* __restrict__ err) {
     if (!plan->ok || *reinterpret_cast<const volatile int*>(&st->failed)) return;
     const int64_t units = plan->units_in, pairs = plan->pairs_in;
-    for (int64_t u = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; u < units;
-         u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t u = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+         u < units; u += nw) {
         const int64_t p = rowmap_in[u];
-        if (p < 0 || p >= pairs) {
-            atomicOr(err, ERR_EP_BOUNDS);
-            rowmap_in[u] = 0;
-            rowscale_in[u] = 0.0f;
+        uint4* vo = reinterpret_cast<uint4*>(xu + u * d);
+        if (p < 0 || p >= pairs) {  // a unit row no source wrote: contributes nothing
+            __syncwarp();
+            if (lane == 0) {
+                atomicOr(err, ERR_EP_BOUNDS);
+                rowmap_in[u] = 0;
+                rowscale_in[u] = 0.0f;
+            }
+            for (int64_t i = lane; i < d / 8; i += 32) vo[i] = make_uint4(0, 0, 0, 0);
+            continue;
         }
+        const uint4* vi = reinterpret_cast<const uint4*>(xpair + p * d);
+        for (int64_t i = lane; i < d / 8; i += 32) vo[i] = vi[i];
     }
     float4* z = reinterpret_cast<float4*>(ret_acc);
     const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -685,6 +693,7 @@ struct Ep {
     int32_t* groups = nullptr;          // [E/R+1] received rows per local expert
     int32_t* pair_local = nullptr;      // [R][T]
     StepState* st = nullptr;
+    void* xu = nullptr;                 // bf16 [units_cap][d]
     void* hu = nullptr;                 // bf16 [units_cap][ffn]
     float* ret_acc = nullptr;           // f32 [pairs_cap][d]
     int32_t* idx_pos = nullptr;         // [T_cap][ksel] gating ids in placement order
@@ -748,10 +757,11 @@ aem_status Ep::init(int64_t max_tokens) {
     const size_t o_ipos = slot(sizeof(int32_t) * T_cap * ksel);
     const size_t o_pos = slot(sizeof(int32_t) * E);
     const size_t o_exp = slot(sizeof(int32_t) * E);
+    const size_t o_xu = slot(2 * units_cap * d);
     const size_t o_hu = slot(2 * units_cap * f);
     const size_t o_ret = slot(sizeof(float) * pairs_cap * d);
     AEM_TRY_CUDA(cudaMalloc(&lbuf, off));
-    AEM_TRY_CUDA(cudaMemset(lbuf, 0, o_hu));  // everything but the big row buffers
+    AEM_TRY_CUDA(cudaMemset(lbuf, 0, o_xu));  // everything but the big row buffers
     char* b = static_cast<char*>(lbuf);
     cnt = reinterpret_cast<unsigned long long*>(b + o_cnt);
     corr = reinterpret_cast<long long*>(b + o_corr);
@@ -763,6 +773,7 @@ aem_status Ep::init(int64_t max_tokens) {
     idx_pos = reinterpret_cast<int32_t*>(b + o_ipos);
     pos_of = reinterpret_cast<int32_t*>(b + o_pos);
     expert_at = reinterpret_cast<int32_t*>(b + o_exp);
+    xu = b + o_xu;
     hu = b + o_hu;
     ret_acc = reinterpret_cast<float*>(b + o_ret);
     std::vector<int32_t> at(E);
@@ -971,9 +982,11 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
         ep_wait_kernel<<<1, 64, 0, s>>>(flags + SYNC_DISPATCH * R, R, rank, live, q, timeout_ns,
                                         tol, st, err);
         AEM_CHECK_LAUNCH();
-        ep_receive_kernel<<<static_cast<unsigned>(sms * 4), kCopyThreads, 0, s>>>(
+        ep_expand_kernel<<<static_cast<unsigned>(sms * 4), kCopyThreads, 0, s>>>(
+            reinterpret_cast<const __nv_bfloat16*>(mine + lay.xpair),
             reinterpret_cast<int32_t*>(mine + lay.rowmap),
-            reinterpret_cast<float*>(mine + lay.rowscale), plan, st, d, ret_acc, err);
+            reinterpret_cast<float*>(mine + lay.rowscale), plan, st, d,
+            static_cast<__nv_bfloat16*>(xu), ret_acc, err);
         AEM_CHECK_LAUNCH();
         count_launches(4);
     }
@@ -989,10 +1002,7 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
         up_a.M = units_cap;
         up_a.max_rows = units_cap;
         up_a.rows_hint = hint;
-        // unit rows gathered from the received pair rows by the GEMM itself
-        up_a.x_hi = mine + lay.xpair;
-        up_a.xrows = reinterpret_cast<const int32_t*>(mine + lay.rowmap);
-        up_a.x_src_rows = pairs_cap;
+        up_a.x_hi = xu;
         up_a.out = hu;
         up_a.out_bf16 = true;
         up_a.ldo = f;

@@ -230,19 +230,14 @@ aem_status Moe::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_d
     ra.rowmap = rowmap;
     ra.rowscale = rowscale;
     AEM_TRY(route_moe(ra, s));
-    // bf16 tokens go straight into the up GEMM, whose producer gathers each
-    // grouped row from its token (TMA 4-row gathers); float32 tokens are
-    // gathered and rounded to bf16 here first
-    const bool direct = xd == AEM_BF16 && d % 8 == 0;
-    if (!direct) AEM_TRY(gather_rows(x, xd, src_token, U, d, xperm, s));
+    AEM_TRY(gather_rows(x, xd, src_token, U, d, xperm, s));
     prof.end(AEM_PHASE_ROUTE, s);
-    AEM_TRY(expert_ffn(T, U, direct ? x : nullptr, out, od, s));
+    AEM_TRY(expert_ffn(T, U, out, od, s));
     prof.step();
     return AEM_OK;
 }
 
-aem_status Moe::expert_ffn(int64_t T, int64_t U, const void* xtok, void* out, aem_dtype od,
-                           cudaStream_t s) {
+aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaStream_t s) {
     const int k = cfg.top_k, E = cfg.num_experts;
     const int64_t d = cfg.d_model, f = cfg.d_ffn;
     GemmArgs up_a;
@@ -252,13 +247,7 @@ aem_status Moe::expert_ffn(int64_t T, int64_t U, const void* xtok, void* out, ae
     up_a.group_rows = starts;
     up_a.M = U;
     up_a.max_rows = U;
-    if (xtok) {  // bf16 token rows gathered by the GEMM through src_token
-        up_a.x_hi = xtok;
-        up_a.xrows = src_token;
-        up_a.x_src_rows = T;
-    } else {
-        up_a.x_hi = xperm;
-    }
+    up_a.x_hi = xperm;
     up_a.out = h;
     up_a.out_bf16 = true;
     up_a.ldo = f;

@@ -44,10 +44,8 @@ struct Moe {
     aem_status forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dtype od,
                        cudaStream_t s);
     // Grouped up GEMM + ReLU, grouped down GEMM (scaled by the gate weight,
-    // red.add-ed into the token's row) -- on starts/src_token/rowscale; the
-    // up GEMM reads bf16 token rows xtok through src_token, or xperm if null.
-    aem_status expert_ffn(int64_t T, int64_t U, const void* xtok, void* out, aem_dtype od,
-                          cudaStream_t s);
+    // scattered to row t*k+j), combine -- on xperm/starts/rowmap/rowscale.
+    aem_status expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaStream_t s);
 };
 
 void seam_free(Moe* m);  // releases the scheduler seam's buffers (seam.cu)

@@ -90,7 +90,6 @@ struct TcParams {
     int relu;
     int atomic_add;
     int red_v4;             // atomic_add with N, ldo multiples of 4: 16-byte reductions
-    const int* xrows;       // gathered activation rows (tensor map box one row high)
     const int* rowmap;
     const float* rowscale;
     int* err;
@@ -288,55 +287,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                         s8 = 0;
                         ph8 ^= 1;
                     }
-                }
-            }
-        }
-    } else if (warp == kXWarp && p.xrows != nullptr) {
-        // ================= activation producer, gathered rows: every lane
-        // issues the 4-row gathers of its row groups into the swizzled slot
-        // (the swizzle follows the shared-memory address, so the slot holds
-        // exactly what one box load of the same rows would)
-        constexpr int NG = BT / 4;
-        constexpr int GPL = (NG + 31) / 32;
-        int sx = 0;
-        uint32_t phx = 0;
-        bool ok = true;
-        for (int t = blockIdx.x; t < total && ok && !*abort_flag; t += gridDim.x) {
-            const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
-            const int pad = __ldg(p.xrows + ti.row0);  // rows past the tile's end repeat a valid one
-            int rows[GPL][4];
-#pragma unroll
-            for (int gi = 0; gi < GPL; ++gi)
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int r = 4 * (lane + 32 * gi) + q;
-                    rows[gi][q] = r < ti.nrows ? __ldg(p.xrows + ti.row0 + r) : pad;
-                }
-            for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                int got = 1;
-                if (lane == 0) {
-                    got = mbar_wait_bounded(&x_empty[sx], phx ^ 1, abort_flag, p.err,
-                                            ERR_GEMM_TIMEOUT)
-                              ? 1
-                              : 0;
-                    if (got) mbar_arrive_expect_tx(&x_full[sx], C::XB);
-                }
-                __syncwarp();
-                if (!__shfl_sync(0xFFFFFFFFu, got, 0)) {
-                    ok = false;
-                    break;
-                }
-                uint8_t* st = x_ring + sx * C::XS;
-#pragma unroll
-                for (int gi = 0; gi < GPL; ++gi) {
-                    const int g = lane + 32 * gi;
-                    if (g < NG)
-                        tma_gather4(st + g * 4 * (kKT * 2), &tm_xh, &x_full[sx], kt * kKT,
-                                    rows[gi][0], rows[gi][1], rows[gi][2], rows[gi][3]);
-                }
-                if (++sx == C::DX) {
-                    sx = 0;
-                    phx ^= 1;
                 }
             }
         }
@@ -584,14 +534,9 @@ aem_status launch_tc(const GemmArgs& a, const TcParams& p, int grid, cudaStream_
     using C = Cfg<BT, SPLIT>;
     const QWeight& w = *a.w;
     CUtensorMap th, tl;
-    if (a.xrows)  // gathered rows: a box one row high, 4 rows per gather
-        AEM_TRY(make_tmap_2d(&th, a.x_hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                             static_cast<uint64_t>(w.K), static_cast<uint64_t>(a.x_src_rows), kKT,
-                             1, CU_TENSOR_MAP_SWIZZLE_128B));
-    else
-        AEM_TRY(make_tmap_2d(&th, a.x_hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                             static_cast<uint64_t>(w.K), static_cast<uint64_t>(a.M), kKT, BT,
-                             CU_TENSOR_MAP_SWIZZLE_128B));
+    AEM_TRY(make_tmap_2d(&th, a.x_hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                         static_cast<uint64_t>(w.K), static_cast<uint64_t>(a.M), kKT, BT,
+                         CU_TENSOR_MAP_SWIZZLE_128B));
     if (SPLIT == 2)
         AEM_TRY(make_tmap_2d(&tl, a.x_lo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                              static_cast<uint64_t>(w.K), static_cast<uint64_t>(a.M), kKT, BT,
@@ -633,10 +578,7 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
                 "qgemm: weight group out of range");
     AEM_REQUIRE(!(a.atomic_add && a.out_bf16), "qgemm: split-K needs float32 output");
     if (a.M == 0) return AEM_OK;
-    if (w.K % 8 != 0) {
-        AEM_REQUIRE(!a.xrows, "qgemm: gathered activation rows need K %% 8 == 0");
-        return launch_qgemm_simt(a, s);
-    }
+    if (w.K % 8 != 0) return launch_qgemm_simt(a, s);
     AEM_REQUIRE(a.M < (1ll << 31) && w.G * w.N < (1ll << 31), "qgemm: too many rows");
     const int dev = current_device();
     const int sms = sm_count(dev);
@@ -681,10 +623,7 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
                    : 0;
     p.rowmap = a.rowmap;
     p.rowscale = a.rowscale;
-    p.xrows = a.xrows;
     p.err = err;
-    AEM_REQUIRE(!a.xrows || (!a.x_lo && a.x_src_rows > 0),
-                "qgemm: gathered activation rows need bf16 x and its row count");
     AEM_REQUIRE(!(ks > 1 && (a.relu || a.out_bf16)), "qgemm: split-K is float32 without ReLU only");
 
     // Upper bound of the tiles of all groups: sum_g ceil(rows_g / bt) <= ceil(M / bt) + (#non-empty groups).

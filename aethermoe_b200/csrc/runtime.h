@@ -116,9 +116,7 @@ struct GemmArgs {
     const int* group_rows = nullptr;
     int64_t M = 0;             // total activation rows (for the TMA map)
     int64_t max_rows = 0;      // upper bound of sum_g ceil(rows_g / BT) * BT (grid sizing)
-    const void* x_hi = nullptr;  // bf16 [M, K], or [x_src_rows, K] gathered through xrows
-    const int* xrows = nullptr;  // activation row r is x_hi row xrows[r] (bf16 only; nullable)
-    int64_t x_src_rows = 0;      // rows of x_hi when xrows is set
+    const void* x_hi = nullptr;  // bf16 [M, K]
     const void* x_lo = nullptr;  // bf16 [M, K] or nullptr (split float32 activations)
     void* out = nullptr;
     bool out_bf16 = false;
