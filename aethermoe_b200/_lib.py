@@ -111,6 +111,8 @@ _SIGS = {
     "aem_ep_plan_exchange": (_int, [_vp, _int, _int, _int, _vp, _vp, _vp, _vp, _vp]),
     "aem_ep_plan_peer": (_int, [_vp, _int, _int, _int, _u64, _i64, _i64, _i64,
                                 ctypes.POINTER(EpPeerPlan), _vp]),
+    "aem_ep_plan_peer_device": (_int, [_vp, _int, _int, _int, _u64, _i64, _i64, _i64, _vp, _vp,
+                                       _vp]),
     "aem_ep_forward_tolerant": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp, _vp]),
     "aem_ep_mark_unhealthy": (_int, [_vp, _int]),
     "aem_ep_health": (_int, [_vp, ctypes.POINTER(_u64), _vp]),

@@ -433,8 +433,144 @@ __global__ void __launch_bounds__(1024)
     if (tid == 0) payload[E + 1 + r] = running;
 }
 
-// After the plan's point: the plan over the usable ranks.  Every taking-part
-// rank must report the same live mask; a failed step plans nothing.
+// plan_peer for one thread block, in parallel over ranks and experts, on a
+// shared-memory copy of the payload rows (the single-thread form is
+// latency-bound on thousands of dependent loads).  Same results as
+// plan_peer, field by field; `check_masks` also requires every usable row's
+// live mask (words E+1+R, E+2+R) to equal `live`.  Dynamic shared memory:
+// plan_block_smem(R, E, ld) bytes.  Returns in every thread whether the plan
+// is ok.
+__host__ __device__ constexpr size_t plan_block_smem(int R, int E, int ld) {
+    return sizeof(int32_t) * (static_cast<size_t>(R) * ld + 2 * R * R + 2 * E) + 16;
+}
+
+__device__ bool plan_peer_block(const int32_t* __restrict__ all, int ld, int R, int E, int me,
+                                uint64_t live, bool check_masks, bool already_failed, int64_t ucap,
+                                int64_t pcap, int64_t rcap, aem_ep_peer_plan* __restrict__ pl,
+                                int32_t* __restrict__ groups) {
+    extern __shared__ int32_t sm[];
+    int32_t* A = sm;                      // [R][ld]
+    int32_t* U = A + R * ld;              // [R][R] units s -> r
+    int32_t* P = U + R * R;               // [R][R] pairs s -> r
+    int32_t* colsum = P + R * R;          // [E] units of expert e, every source
+    int32_t* before = colsum + E;         // [E] units of expert e from sources < me
+    __shared__ int bad;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const int el = E / R;
+    auto in = [&](int r) { return ((live >> r) & 1ull) != 0; };
+    if (tid == 0) bad = (already_failed || !in(me)) ? 1 : 0;
+    for (int i = tid; i < R * ld; i += nt) A[i] = all[i];
+    __syncthreads();
+    for (int i = tid; i < R * (E + 1); i += nt) {
+        const int sr = i / (E + 1), e = i % (E + 1);
+        if (!in(sr)) continue;
+        const int32_t* a = A + sr * ld;
+        if (e == 0 ? a[0] != 0 : a[e] < a[e - 1]) bad = 1;
+    }
+    for (int i = tid; i < R * R; i += nt) {
+        const int sr = i / R, r = i % R;
+        const bool on = in(sr) && in(r);
+        const int32_t* a = A + sr * ld;
+        const int32_t u = on ? a[(r + 1) * el] - a[r * el] : 0;
+        const int32_t p = on ? a[E + 1 + r] : 0;
+        U[i] = u;
+        P[i] = p;
+        if (p < 0 || p > u || ((u > 0) != (p > 0))) bad = 1;  // a pair exists iff a unit does
+    }
+    if (check_masks)
+        for (int sr = tid; sr < R; sr += nt) {
+            if (!in(sr)) continue;
+            const int32_t* a = A + sr * ld;
+            const uint64_t m = static_cast<uint32_t>(a[E + 1 + R]) |
+                               (static_cast<uint64_t>(static_cast<uint32_t>(a[E + 2 + R])) << 32);
+            if (m != live) bad = 1;  // the ranks disagree on who takes part
+        }
+    for (int e = tid; e < E; e += nt) {
+        int32_t cs = 0, bf = 0;
+        const bool on = in(e / el);
+        for (int sr = 0; sr < R; ++sr) {
+            if (!on || !in(sr)) continue;
+            const int32_t v = A[sr * ld + e + 1] - A[sr * ld + e];
+            cs += v;
+            if (sr < me) bf += v;
+        }
+        colsum[e] = cs;
+        before[e] = bf;
+    }
+    __syncthreads();
+    for (int i = tid; i < 2 * R; i += nt) {
+        const int r = i % R;
+        int64_t sum = 0;
+        if (i < R) {  // everything rank r sends
+            for (int q = 0; q < R; ++q) sum += P[r * R + q];
+            if (sum > rcap) bad = 1;
+        } else {      // everything rank r receives
+            int64_t u = 0;
+            for (int q = 0; q < R; ++q) {
+                u += U[q * R + r];
+                sum += P[q * R + r];
+            }
+            if (u > ucap || sum > pcap) bad = 1;
+        }
+    }
+    __syncthreads();
+    const bool ok = bad == 0;
+    // every field is written (zeros past R, past E, or for a bad plan)
+    for (int i = tid; i < AEM_MAX_EXPERTS; i += nt) pl->dst_unit_off[i] = 0;
+    for (int i = tid; i <= AEM_EP_MAX_RANKS; i += nt) {
+        if (i < AEM_EP_MAX_RANKS) {
+            pl->dst_pair_off[i] = 0;
+            pl->send_pair_off[i] = 0;
+            pl->ret_off[i] = 0;
+        }
+        pl->recv_pair_off[i] = 0;
+    }
+    for (int i = tid; i <= el; i += nt) groups[i] = 0;
+    __syncthreads();
+    if (!ok) {
+        if (tid == 0) {
+            pl->ok = 0;
+            pl->units_in = pl->pairs_in = pl->pairs_out = 0;
+        }
+        return false;
+    }
+    for (int r = tid; r < R; r += nt) {
+        int32_t so = 0, dp = 0, ro = 0, rt = 0;
+        for (int q = 0; q < r; ++q) so += P[me * R + q];   // my pairs for ranks < r
+        for (int q = 0; q < me; ++q) dp += P[q * R + r];   // pairs to r from ranks < me
+        for (int q = 0; q < r; ++q) ro += P[q * R + me];   // pairs I receive from ranks < r
+        for (int q = 0; q < me; ++q) rt += P[r * R + q];   // r's pairs for ranks < me
+        pl->send_pair_off[r] = so;
+        pl->dst_pair_off[r] = dp;
+        pl->recv_pair_off[r] = ro;
+        pl->ret_off[r] = rt;
+        int32_t u = 0;  // rank r receives expert-major, sources in rank order inside
+        for (int e = r * el; e < (r + 1) * el; ++e) {
+            pl->dst_unit_off[e] = u + before[e];
+            u += colsum[e];
+        }
+    }
+    if (tid == 0) {
+        int32_t out = 0, inn = 0, g = 0;
+        for (int q = 0; q < R; ++q) {
+            out += P[me * R + q];
+            inn += P[q * R + me];
+        }
+        for (int le = 0; le < el; ++le) {
+            g += colsum[me * el + le];
+            groups[le + 1] = g;
+        }
+        pl->pairs_out = out;
+        pl->pairs_in = inn;
+        pl->recv_pair_off[R] = inn;
+        pl->units_in = g;
+        pl->ok = 1;
+    }
+    return true;
+}
+
+// After the plan's point: the plan over the usable ranks; a failed step
+// plans nothing.
 __global__ void ep_plan_kernel(const int32_t* __restrict__ all, int ld,
                                const uint64_t* __restrict__ flags, int R, int E, int me,
                                uint64_t live, uint64_t seq, uint64_t timeout_ns, int tolerant,
@@ -442,21 +578,23 @@ __global__ void ep_plan_kernel(const int32_t* __restrict__ all, int ld,
                                aem_ep_peer_plan* __restrict__ plan, int32_t* __restrict__ groups,
                                int* __restrict__ err) {
     wait_point(flags, R, me, live, seq, timeout_ns, tolerant != 0, st, err);
-    if (threadIdx.x != 0) return;
     const uint64_t use = usable(live, st);
-    for (int s = 0; s < R; ++s) {
-        if (!((use >> s) & 1ull)) continue;
-        const int32_t* a = all + static_cast<int64_t>(s) * ld;
-        const uint64_t m = static_cast<uint32_t>(a[E + 1 + R]) |
-                           (static_cast<uint64_t>(static_cast<uint32_t>(a[E + 2 + R])) << 32);
-        if (m != live) st->failed = 1;  // the ranks disagree on who takes part
-    }
-    plan_peer(all, ld, R, E, me, use, ucap, pcap, rcap, plan, groups);
-    if (!plan->ok && !st->failed) {
+    const bool failed = *reinterpret_cast<volatile int*>(&st->failed) != 0;
+    const bool ok = plan_peer_block(all, ld, R, E, me, use, true, failed, ucap, pcap, rcap, plan,
+                                    groups);
+    if (threadIdx.x == 0 && !ok && !failed) {
         atomicOr(err, ERR_EP_PLAN);
         st->failed = 1;
     }
-    if (st->failed) plan->ok = 0;
+}
+
+// The block plan on given rows (no waits): the device twin of
+// aem_ep_plan_peer, for tests.
+__global__ void ep_plan_test_kernel(const int32_t* __restrict__ all, int R, int E, int me,
+                                    uint64_t live, int64_t ucap, int64_t pcap, int64_t rcap,
+                                    aem_ep_peer_plan* __restrict__ plan,
+                                    int32_t* __restrict__ groups) {
+    plan_peer_block(all, E + 1 + R, R, E, me, live, false, false, ucap, pcap, rcap, plan, groups);
 }
 
 // One warp copies one row of d elements (d % 8 == 0) to bf16.
@@ -887,6 +1025,11 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
     const int tol = tolerant ? 1 : 0;
     StepTimer timer(AEM_METRIC_EP_STEP, s);
     const uint64_t q = ++seq;
+    const size_t plan_smem = plan_block_smem(R, E, pay_ld);
+    if (plan_smem > 48 * 1024)
+        AEM_TRY_CUDA(cudaFuncSetAttribute(ep_plan_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(plan_smem)));
     char* mine = static_cast<char*>(xreg);
     const uint64_t* flags = reinterpret_cast<const uint64_t*>(mine + lay.flags);
     last_T = T;
@@ -957,9 +1100,9 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
                                         peers, lay.mail_pay, lay.flags, SYNC_PLAN, rank, R, live, q,
                                         st);
     AEM_CHECK_LAUNCH();
-    ep_plan_kernel<<<1, 64, 0, s>>>(reinterpret_cast<const int32_t*>(mine + lay.mail_pay), pay_ld,
-                                    flags + SYNC_PLAN * R, R, E, rank, live, q, timeout_ns, tol,
-                                    units_cap, pairs_cap, ret_cap, st, plan, groups, err);
+    ep_plan_kernel<<<1, 256, plan_smem, s>>>(
+        reinterpret_cast<const int32_t*>(mine + lay.mail_pay), pay_ld, flags + SYNC_PLAN * R, R,
+        E, rank, live, q, timeout_ns, tol, units_cap, pairs_cap, ret_cap, st, plan, groups, err);
     AEM_CHECK_LAUNCH();
     count_launches(2);
     prof.end(AEM_PHASE_EXCHANGE, s);
@@ -1121,6 +1264,25 @@ aem_status aem_ep_plan_peer(const int32_t* all, int R, int E, int rank, uint64_t
     AEM_REQUIRE(R >= 1 && R <= AEM_EP_MAX_RANKS && E >= R && E % R == 0 && rank >= 0 && rank < R,
                 "aem_ep_plan_peer: bad R=%d E=%d rank=%d", R, E, rank);
     aem::plan_peer(all, E + 1 + R, R, E, rank, live, units_cap, pairs_cap, ret_cap, plan, groups);
+    return AEM_OK;
+}
+
+aem_status aem_ep_plan_peer_device(const int32_t* all, int R, int E, int rank, uint64_t live,
+                                   int64_t units_cap, int64_t pairs_cap, int64_t ret_cap,
+                                   aem_ep_peer_plan* plan, int32_t* groups, void* stream) {
+    AEM_REQUIRE(all && plan && groups, "aem_ep_plan_peer_device: NULL buffer");
+    AEM_REQUIRE(R >= 1 && R <= AEM_EP_MAX_RANKS && E >= R && E % R == 0 && E <= AEM_MAX_EXPERTS &&
+                    rank >= 0 && rank < R,
+                "aem_ep_plan_peer_device: bad R=%d E=%d rank=%d", R, E, rank);
+    const size_t smem = aem::plan_block_smem(R, E, E + 1 + R);
+    if (smem > 48 * 1024)
+        AEM_TRY_CUDA(cudaFuncSetAttribute(aem::ep_plan_test_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(smem)));
+    aem::ep_plan_test_kernel<<<1, 256, smem, static_cast<cudaStream_t>(stream)>>>(
+        all, R, E, rank, live, units_cap, pairs_cap, ret_cap, plan, groups);
+    AEM_CHECK_LAUNCH();
+    aem::count_launches(1);
     return AEM_OK;
 }
 

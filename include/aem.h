@@ -325,6 +325,12 @@ typedef struct aem_ep_peer_plan {
 aem_status aem_ep_plan_peer(const int32_t* all, int R, int E, int rank, uint64_t live,
                             int64_t units_cap, int64_t pairs_cap, int64_t ret_cap,
                             aem_ep_peer_plan* plan, int32_t* groups);
+/* The same plan computed by the layer's device code (one thread block, in
+ * parallel over ranks and experts) on DEVICE buffers, asynchronously on
+ * `stream`: lets a caller check the device plan against aem_ep_plan_peer. */
+aem_status aem_ep_plan_peer_device(const int32_t* all, int R, int E, int rank, uint64_t live,
+                                   int64_t units_cap, int64_t pairs_cap, int64_t ret_cap,
+                                   aem_ep_peer_plan* plan, int32_t* groups, void* stream);
 
 /* NCCL unique id (128 bytes) for aem_ep_create; made on one rank and
  * broadcast by the caller. */
