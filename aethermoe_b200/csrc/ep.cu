@@ -755,34 +755,62 @@ __global__ void __launch_bounds__(kCopyThreads)
 // After the return point: out[t] = sum over destination ranks r (increasing)
 // of the returned pair sum; unit_failed[j*T + t] = 1 for a unit whose expert's
 // rank is outside the step, or for every unit of a failed step (out = 0).
+// One warp per token: the token's present pair rows are compacted once (in
+// rank order), then every 16-byte column block loads them independently.
 template <typename OT>
 __global__ void __launch_bounds__(kCopyThreads)
     ep_combine_kernel(const float* __restrict__ ret_in, const int32_t* __restrict__ pair_local,
                       const aem_ep_peer_plan* __restrict__ plan, const StepState* st,
                       const uint32_t* __restrict__ eff, int k, int el, uint64_t live, int64_t T,
                       int R, int64_t d, OT* __restrict__ out, uint8_t* __restrict__ unit_failed) {
+    __shared__ int32_t rows_s[kCopyThreads / 32][AEM_EP_MAX_RANKS];
     const int lane = threadIdx.x & 31;
+    const int wib = threadIdx.x >> 5;
     const bool ok = plan->ok != 0 && !*reinterpret_cast<const volatile int*>(&st->failed);
     const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
-         t < T; t += nw) {
+    const int64_t d4 = d / 4;
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + wib; t < T; t += nw) {
         if (unit_failed)
             for (int j = lane; j < k; j += 32) {
                 const int64_t u = static_cast<int64_t>(j) * T + t;
                 const int r = static_cast<int>(eff[u]) / el;
                 unit_failed[u] = (!ok || !((live >> r) & 1ull)) ? 1 : 0;
             }
-        int64_t row = -1;
-        if (ok && lane < R) {
-            const int pl = pair_local[static_cast<int64_t>(lane) * T + t];
-            if (pl >= 0) row = static_cast<int64_t>(plan->send_pair_off[lane]) + pl;
-        }
-        for (int64_t c = lane; c < d / 4; c += 32) {
+        int n = 0;  // compact this token's pair rows, rank order
+        if (ok)
+            for (int r0 = 0; r0 < R; r0 += 32) {
+                const int r = r0 + lane;
+                int32_t row = -1;
+                if (r < R) {
+                    const int pl = pair_local[static_cast<int64_t>(r) * T + t];
+                    if (pl >= 0) row = plan->send_pair_off[r] + pl;
+                }
+                const unsigned m = __ballot_sync(0xFFFFFFFFu, row >= 0);
+                if (row >= 0) rows_s[wib][n + __popc(m & ((1u << lane) - 1u))] = row;
+                n += __popc(m);
+            }
+        __syncwarp();
+        for (int64_t c = lane; c < d4; c += 32) {
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int r = 0; r < R; ++r) {
-                const int64_t rr = __shfl_sync(0xFFFFFFFFu, row, r);
-                if (rr < 0) continue;
-                const float4 v = reinterpret_cast<const float4*>(ret_in + rr * d)[c];
+            int i = 0;
+            for (; i + 4 <= n; i += 4) {
+                float4 v[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    v[q] = reinterpret_cast<const float4*>(ret_in + static_cast<int64_t>(
+                                                                        rows_s[wib][i + q]) * d)[c];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {  // rank order kept: ((a + b) + c) + d
+                    acc.x += v[q].x;
+                    acc.y += v[q].y;
+                    acc.z += v[q].z;
+                    acc.w += v[q].w;
+                }
+            }
+            for (; i < n; ++i) {
+                const float4 v =
+                    reinterpret_cast<const float4*>(ret_in + static_cast<int64_t>(rows_s[wib][i]) *
+                                                                 d)[c];
                 acc.x += v.x;
                 acc.y += v.y;
                 acc.z += v.z;
@@ -799,6 +827,7 @@ __global__ void __launch_bounds__(kCopyThreads)
                 reinterpret_cast<float4*>(out + t * d)[c] = acc;
             }
         }
+        __syncwarp();
     }
 }
 

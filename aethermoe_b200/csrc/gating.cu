@@ -29,7 +29,6 @@ namespace aem {
 namespace {
 
 constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
 
 template <typename XT>
 __device__ __forceinline__ float load_x(const XT* p);
@@ -42,39 +41,69 @@ __device__ __forceinline__ float load_x<__nv_bfloat16>(const __nv_bfloat16* p) {
     return __bfloat162float(*p);
 }
 
-template <typename XT>
-__device__ __forceinline__ float4 load_x4(const XT* p);
-template <>
-__device__ __forceinline__ float4 load_x4<float>(const float* p) {
-    return *reinterpret_cast<const float4*>(p);
+constexpr int kStages = 3;  // depth of the cp.async ring
+
+__device__ __forceinline__ void cp_async_16(void* dst, const void* src, int src_bytes) {
+    // copies src_bytes (0..16) and zero-fills the rest of the 16 bytes
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dev::smem_u32(dst)),
+                 "l"(src), "r"(src_bytes)
+                 : "memory");
 }
-template <>
-__device__ __forceinline__ float4 load_x4<__nv_bfloat16>(const __nv_bfloat16* p) {
-    uint2 u = *reinterpret_cast<const uint2*>(p);
-    float4 f;
-    f.x = __uint_as_float(u.x << 16);
-    f.y = __uint_as_float(u.x & 0xFFFF0000u);
-    f.z = __uint_as_float(u.y << 16);
-    f.w = __uint_as_float(u.y & 0xFFFF0000u);
-    return f;
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
 }
+template <int NPENDING>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(NPENDING) : "memory");
+}
+
+// Compile-time shape of one kernel configuration.
+template <int GROUP, int NSLOT, int TPG, int WARPS, typename XT>
+struct GatingCfg {
+    static constexpr int kThreads = WARPS * 32;
+    static constexpr int GPW = 32 / GROUP;
+    static constexpr int TOK = WARPS * GPW * TPG;  // tokens per CTA
+    static constexpr int EPAD = GROUP * NSLOT;
+    static constexpr int DK_E = EPAD <= 64 ? 64 : (EPAD <= 128 ? 32 : 16);
+    static constexpr int DK = (TOK * (DK_E + 4) * 4 > 36 * 1024) ? DK_E / 2 : DK_E;
+    static constexpr int DK4 = DK / 4;
+    static constexpr int XS = DK + 4;  // padded float32 row of the activation chunk
+    static constexpr int XB = static_cast<int>(sizeof(XT));
+    static constexpr int XPC = 16 / XB;     // activation elements per 16-byte piece
+    static constexpr int XCH = DK / XPC;    // pieces per token row of a chunk
+    static constexpr int WST = DK4 * EPAD;  // float4 per weight stage
+    static constexpr int XST = TOK * XCH;   // 16-byte pieces per activation stage
+    static constexpr size_t SMEM =
+        16 * static_cast<size_t>(kStages) * (WST + XST) + 4 * static_cast<size_t>(TOK) * XS;
+    static_assert(DK % XPC == 0, "activation chunk must be whole 16-byte pieces");
+};
 
 template <int GROUP, int NSLOT, int kTPG, int WARPS, typename XT, bool EXACT>
 __global__ void __launch_bounds__(WARPS * 32)
     gating_kernel(const XT* __restrict__ x, const float4* __restrict__ wpk,
                   const float* __restrict__ bias, int64_t N, int D, int E, int k, int ksel,
                   int32_t* __restrict__ idx_out, float* __restrict__ val_out) {
-    constexpr int kThreads = WARPS * 32;
-    constexpr int GPW = 32 / GROUP;
-    constexpr int TOK = WARPS * GPW * kTPG;  // tokens per CTA
-    constexpr int EPAD = GROUP * NSLOT;
-    constexpr int DK_E = EPAD <= 64 ? 64 : (EPAD <= 128 ? 32 : 16);
-    constexpr int DK = (TOK * (DK_E + 4) * 4 > 36 * 1024) ? DK_E / 2 : DK_E;
-    constexpr int DK4 = DK / 4;
-    constexpr int XS = DK + 4;                // padded row of the activation chunk
+    using C = GatingCfg<GROUP, NSLOT, kTPG, WARPS, XT>;
+    constexpr int kThreads = C::kThreads;
+    constexpr int GPW = C::GPW;
+    constexpr int TOK = C::TOK;
+    constexpr int EPAD = C::EPAD;
+    constexpr int DK = C::DK;
+    constexpr int DK4 = C::DK4;
+    constexpr int XS = C::XS;
+    constexpr int XB = C::XB;
+    constexpr int XPC = C::XPC;
+    constexpr int XCH = C::XCH;
+    constexpr int WST = C::WST;
+    constexpr int XST = C::XST;
 
-    __shared__ float4 ws[DK4 * EPAD];
-    __shared__ __align__(16) float xs[TOK * XS];
+    // Shared memory: a kStages-deep ring of weight chunks and raw activation
+    // chunks filled by cp.async (16-byte asynchronous copies, zero-filled past
+    // the end of the data), and the current chunk's activations as float32.
+    extern __shared__ __align__(16) unsigned char gsm[];
+    float4* wring = reinterpret_cast<float4*>(gsm);
+    uint4* xring = reinterpret_cast<uint4*>(gsm + sizeof(float4) * kStages * WST);
+    float* xs = reinterpret_cast<float*>(xring + kStages * XST);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -90,63 +119,55 @@ __global__ void __launch_bounds__(WARPS * 32)
 #pragma unroll
         for (int s = 0; s < NSLOT; ++s) acc[i][s] = 0.0f;
 
-    const bool vec_ok = (D & 3) == 0;
+    // activation rows can be copied in 16-byte pieces when every row start is aligned
+    const bool xvec = (static_cast<int64_t>(D) * XB) % 16 == 0 &&
+                      (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     const int nchunks = (D + DK - 1) / DK;
-    // The next chunk's weights and activations are loaded into registers while
-    // the current chunk is multiplied out of shared memory.
-    constexpr int PW = (DK4 * EPAD + kThreads - 1) / kThreads;
-    constexpr int PX = (TOK * DK4 + kThreads - 1) / kThreads;
-    float4 pw[PW], px[PX];
-    auto fetch = [&](int c) {
-        const int d0 = c * DK;
-        const float4* wsrc = wpk + static_cast<int64_t>(c) * DK4 * EPAD;
-#pragma unroll
-        for (int j = 0; j < PW; ++j) {
-            const int i = tid + j * kThreads;
-            if (i < DK4 * EPAD) pw[j] = __ldg(wsrc + i);
-        }
-#pragma unroll
-        for (int j = 0; j < PX; ++j) {
-            const int i = tid + j * kThreads;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (i < TOK * DK4) {
-                const int t = i / DK4;
-                const int q = i % DK4;
-                const int64_t tg = tok0 + t;
-                const int d = d0 + 4 * q;
-                if (tg < N) {
-                    const XT* row = x + tg * static_cast<int64_t>(D);
-                    if (vec_ok) {
-                        if (d < D) v = load_x4<XT>(row + d);
-                    } else {
-                        if (d + 0 < D) v.x = load_x<XT>(row + d + 0);
-                        if (d + 1 < D) v.y = load_x<XT>(row + d + 1);
-                        if (d + 2 < D) v.z = load_x<XT>(row + d + 2);
-                        if (d + 3 < D) v.w = load_x<XT>(row + d + 3);
-                    }
+    // Issues chunk c's copies (if it exists) and always commits a group, so
+    // that "all but the newest kStages-1 groups complete" means chunk c landed.
+    auto issue = [&](int c) {
+        if (c < nchunks) {
+            const int st = c % kStages;
+            const float4* wsrc = wpk + static_cast<int64_t>(c) * WST;  // Dpad covers every chunk
+            float4* wdst = wring + st * WST;
+            for (int i = tid; i < WST; i += kThreads) cp_async_16(wdst + i, wsrc + i, 16);
+            if (xvec) {
+                const int d0 = c * DK;
+                uint4* xdst = xring + st * XST;
+                for (int i = tid; i < XST; i += kThreads) {
+                    const int t = i / XCH;
+                    const int d = d0 + (i % XCH) * XPC;
+                    const int64_t tg = tok0 + t;
+                    const bool in = tg < N && d < D;
+                    const XT* src = in ? x + tg * static_cast<int64_t>(D) + d : x;
+                    cp_async_16(xdst + i, src, in ? min(16, (D - d) * XB) : 0);
                 }
             }
-            px[j] = v;
         }
+        cp_async_commit();
     };
-    auto stage = [&]() {
-#pragma unroll
-        for (int j = 0; j < PW; ++j) {
-            const int i = tid + j * kThreads;
-            if (i < DK4 * EPAD) ws[i] = pw[j];
-        }
-#pragma unroll
-        for (int j = 0; j < PX; ++j) {
-            const int i = tid + j * kThreads;
-            if (i < TOK * DK4)
-                *reinterpret_cast<float4*>(&xs[(i / DK4) * XS + 4 * (i % DK4)]) = px[j];
-        }
-    };
-    fetch(0);
-    stage();
-    __syncthreads();
+    for (int c = 0; c < kStages - 1; ++c) issue(c);
     for (int c = 0; c < nchunks; ++c) {
-        if (c + 1 < nchunks) fetch(c + 1);
+        issue(c + kStages - 1);
+        cp_async_wait<kStages - 1>();
+        __syncthreads();  // chunk c is in its stage, from every thread's copies
+        const int st = c % kStages;
+        const float4* ws = wring + st * WST;
+        // the chunk's activations as float32 rows (padded against bank conflicts)
+        if (xvec) {
+            const XT* xr = reinterpret_cast<const XT*>(xring + st * XST);
+            for (int i = tid; i < TOK * DK; i += kThreads)
+                xs[(i / DK) * XS + (i % DK)] = load_x<XT>(xr + i);
+        } else {
+            const int d0 = c * DK;
+            for (int i = tid; i < TOK * DK; i += kThreads) {
+                const int64_t tg = tok0 + i / DK;
+                const int d = d0 + i % DK;
+                xs[(i / DK) * XS + (i % DK)] =
+                    (tg < N && d < D) ? load_x<XT>(x + tg * static_cast<int64_t>(D) + d) : 0.0f;
+            }
+        }
+        __syncthreads();
 #pragma unroll 4
         for (int q = 0; q < DK4; ++q) {
             float4 xv[kTPG];
@@ -184,12 +205,9 @@ __global__ void __launch_bounds__(WARPS * 32)
                 }
             }
         }
-        __syncthreads();
-        if (c + 1 < nchunks) {
-            stage();
-            __syncthreads();
-        }
+        __syncthreads();  // the stage and xs are rewritten next
     }
+    cp_async_wait<0>();
 
     // ---- bias, top-k selection, softmax (per lane group, per token)
     float bv[NSLOT];
@@ -256,10 +274,15 @@ __global__ void __launch_bounds__(WARPS * 32)
 template <int GROUP, int NSLOT, int TPG, typename XT, bool EXACT, int WARPS = kWarps>
 cudaError_t launch_one(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
                        float* val, cudaStream_t s) {
-    constexpr int TOK = WARPS * (32 / GROUP) * TPG;
-    const int64_t blocks = (N + TOK - 1) / TOK;
-    gating_kernel<GROUP, NSLOT, TPG, WARPS, XT, EXACT>
-        <<<static_cast<unsigned>(blocks), WARPS * 32, 0, s>>>(
+    using C = GatingCfg<GROUP, NSLOT, TPG, WARPS, XT>;
+    const int64_t blocks = (N + C::TOK - 1) / C::TOK;
+    auto kern = gating_kernel<GROUP, NSLOT, TPG, WARPS, XT, EXACT>;
+    if (C::SMEM > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(
+            kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM));
+        if (e != cudaSuccess) return e;
+    }
+    kern<<<static_cast<unsigned>(blocks), WARPS * 32, C::SMEM, s>>>(
         static_cast<const XT*>(x), reinterpret_cast<const float4*>(g.wt), g.bias, N,
         static_cast<int>(g.D), static_cast<int>(g.E), k, ksel, idx, val);
     return cudaGetLastError();
@@ -269,8 +292,8 @@ template <typename XT, bool EXACT>
 cudaError_t dispatch_e(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
                        float* val, cudaStream_t s) {
     // Many tokens: 8 tokens per lane group halves the weight loads per
-    // multiply-add; few tokens: 4, for more CTAs.
-    if (N >= 8192) {
+    // multiply-add; fewer: 4, for more CTAs.
+    if (N >= 12288) {
         switch (g.Epad) {
             case 8: return launch_one<8, 1, 8, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
             case 16: return launch_one<16, 1, 8, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
