@@ -722,11 +722,12 @@ __global__ void __launch_bounds__(kCopyThreads)
 }
 
 // Return: pair sum p (from source s) into row ret_off[s] + (p - recv_pair_off[s])
-// of s's return rows.
+// of s's return rows; the sums of this rank's own pairs are not copied (the
+// combine reads them where the down GEMM left them).
 __global__ void __launch_bounds__(kCopyThreads)
     ep_return_kernel(const float* __restrict__ ret_acc, const aem_ep_peer_plan* __restrict__ plan,
-                     const StepState* st, int R, int64_t d, EpPeers peers, ExchangeLayout lay,
-                     int64_t rcap, int* __restrict__ err) {
+                     const StepState* st, int R, int me, int64_t d, EpPeers peers,
+                     ExchangeLayout lay, int64_t rcap, int* __restrict__ err) {
     __shared__ int off[AEM_EP_MAX_RANKS + 1];
     __shared__ int ret[AEM_EP_MAX_RANKS];
     if (!plan->ok || *reinterpret_cast<const volatile int*>(&st->failed)) return;
@@ -740,6 +741,7 @@ __global__ void __launch_bounds__(kCopyThreads)
          p < pairs; p += nw) {
         int s = 0;
         while (s + 1 < R && p >= off[s + 1]) ++s;
+        if (s == me) continue;  // this rank's own pair sums stay where they are
         const int64_t row = ret[s] + (p - off[s]);
         if (row >= rcap) {
             if (lane == 0) atomicOr(err, ERR_EP_BOUNDS);
@@ -759,11 +761,13 @@ __global__ void __launch_bounds__(kCopyThreads)
 // rank order), then every 16-byte column block loads them independently.
 template <typename OT>
 __global__ void __launch_bounds__(kCopyThreads)
-    ep_combine_kernel(const float* __restrict__ ret_in, const int32_t* __restrict__ pair_local,
+    ep_combine_kernel(const float* __restrict__ ret_in, const float* __restrict__ ret_own,
+                      const int32_t* __restrict__ pair_local,
                       const aem_ep_peer_plan* __restrict__ plan, const StepState* st,
                       const uint32_t* __restrict__ eff, int k, int el, uint64_t live, int64_t T,
-                      int R, int64_t d, OT* __restrict__ out, uint8_t* __restrict__ unit_failed) {
-    __shared__ int32_t rows_s[kCopyThreads / 32][AEM_EP_MAX_RANKS];
+                      int R, int me, int64_t d, OT* __restrict__ out,
+                      uint8_t* __restrict__ unit_failed) {
+    __shared__ const float* rows_s[kCopyThreads / 32][AEM_EP_MAX_RANKS];
     const int lane = threadIdx.x & 31;
     const int wib = threadIdx.x >> 5;
     const bool ok = plan->ok != 0 && !*reinterpret_cast<const volatile int*>(&st->failed);
@@ -780,13 +784,17 @@ __global__ void __launch_bounds__(kCopyThreads)
         if (ok)
             for (int r0 = 0; r0 < R; r0 += 32) {
                 const int r = r0 + lane;
-                int32_t row = -1;
+                const float* row = nullptr;
                 if (r < R) {
                     const int pl = pair_local[static_cast<int64_t>(r) * T + t];
-                    if (pl >= 0) row = plan->send_pair_off[r] + pl;
+                    if (pl >= 0)  // own pairs: the down GEMM's sums, at this rank's receive rows
+                        row = r == me ? ret_own + (static_cast<int64_t>(plan->recv_pair_off[me]) +
+                                                   pl) * d
+                                      : ret_in + (static_cast<int64_t>(plan->send_pair_off[r]) +
+                                                  pl) * d;
                 }
-                const unsigned m = __ballot_sync(0xFFFFFFFFu, row >= 0);
-                if (row >= 0) rows_s[wib][n + __popc(m & ((1u << lane) - 1u))] = row;
+                const unsigned m = __ballot_sync(0xFFFFFFFFu, row != nullptr);
+                if (row) rows_s[wib][n + __popc(m & ((1u << lane) - 1u))] = row;
                 n += __popc(m);
             }
         __syncwarp();
@@ -796,9 +804,7 @@ __global__ void __launch_bounds__(kCopyThreads)
             for (; i + 4 <= n; i += 4) {
                 float4 v[4];
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    v[q] = reinterpret_cast<const float4*>(ret_in + static_cast<int64_t>(
-                                                                        rows_s[wib][i + q]) * d)[c];
+                for (int q = 0; q < 4; ++q) v[q] = reinterpret_cast<const float4*>(rows_s[wib][i + q])[c];
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {  // rank order kept: ((a + b) + c) + d
                     acc.x += v[q].x;
@@ -808,9 +814,7 @@ __global__ void __launch_bounds__(kCopyThreads)
                 }
             }
             for (; i < n; ++i) {
-                const float4 v =
-                    reinterpret_cast<const float4*>(ret_in + static_cast<int64_t>(rows_s[wib][i]) *
-                                                                 d)[c];
+                const float4 v = reinterpret_cast<const float4*>(rows_s[wib][i])[c];
                 acc.x += v.x;
                 acc.y += v.y;
                 acc.z += v.z;
@@ -1202,7 +1206,7 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
     // 7. pair sums back into the sources
     prof.begin(AEM_PHASE_RETURN, s);
     ep_return_kernel<<<static_cast<unsigned>(sms * 4), kCopyThreads, 0, s>>>(
-        ret_acc, plan, st, R, d, peers, lay, ret_cap, err);
+        ret_acc, plan, st, R, rank, d, peers, lay, ret_cap, err);
     AEM_CHECK_LAUNCH();
     ep_publish_kernel<<<1, 64, 0, s>>>(nullptr, 0, 0, peers, 0, lay.flags, SYNC_RETURN, rank, R,
                                        live, q, st);
@@ -1219,11 +1223,11 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
         const unsigned g = static_cast<unsigned>(std::min<int64_t>((T + 7) / 8, sms * 8));
         if (od == AEM_BF16)
             ep_combine_kernel<__nv_bfloat16><<<g, kCopyThreads, 0, s>>>(
-                ret_in, pair_local, plan, st, loc.eff, k, el, live, T, R, d,
+                ret_in, ret_acc, pair_local, plan, st, loc.eff, k, el, live, T, R, rank, d,
                 static_cast<__nv_bfloat16*>(out), unit_failed);
         else
             ep_combine_kernel<float><<<g, kCopyThreads, 0, s>>>(
-                ret_in, pair_local, plan, st, loc.eff, k, el, live, T, R, d,
+                ret_in, ret_acc, pair_local, plan, st, loc.eff, k, el, live, T, R, rank, d,
                 static_cast<float*>(out), unit_failed);
         AEM_CHECK_LAUNCH();
         count_launches(1);

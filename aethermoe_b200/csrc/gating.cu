@@ -294,11 +294,13 @@ cudaError_t dispatch_e(const Gate& g, const void* x, int64_t N, int k, int ksel,
     // Many tokens: 8 tokens per lane group halves the weight loads per
     // multiply-add; fewer: 4, for more CTAs.
     if (N >= 12288) {
+        // 7 warps: 56 tokens per CTA, so 16384 tokens make 293 CTAs -- two
+        // per SM on all 148 SMs instead of two on 108 and one on 40
         switch (g.Epad) {
-            case 8: return launch_one<8, 1, 8, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
-            case 16: return launch_one<16, 1, 8, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
-            case 32: return launch_one<32, 1, 8, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
-            case 64: return launch_one<32, 2, 8, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+            case 8: return launch_one<8, 1, 8, XT, EXACT, 7>(g, x, N, k, ksel, idx, val, s);
+            case 16: return launch_one<16, 1, 8, XT, EXACT, 7>(g, x, N, k, ksel, idx, val, s);
+            case 32: return launch_one<32, 1, 8, XT, EXACT, 7>(g, x, N, k, ksel, idx, val, s);
+            case 64: return launch_one<32, 2, 8, XT, EXACT, 7>(g, x, N, k, ksel, idx, val, s);
             default: break;
         }
     }
