@@ -67,15 +67,21 @@ struct GatingCfg {
     static constexpr int DK_E = EPAD <= 64 ? 64 : (EPAD <= 128 ? 32 : 16);
     static constexpr int DK = (TOK * (DK_E + 4) * 4 > 36 * 1024) ? DK_E / 2 : DK_E;
     static constexpr int DK4 = DK / 4;
-    static constexpr int XS = DK + 4;  // padded float32 row of the activation chunk
+    // float32 activations of a chunk, token pairs interleaved: pair p's row
+    // holds, for every 4 consecutive d, (t0 d0, t1 d0, t0 d1, t1 d1, t0 d2,
+    // t1 d2, t0 d3, t1 d3) with t0 = 2p, t1 = 2p+1 -- each 16-byte load
+    // yields two (token 2p, token 2p+1) operand pairs of the packed fp32x2
+    // multiply; rows padded against bank conflicts
+    static constexpr int XS = 2 * DK + 4;
     static constexpr int XB = static_cast<int>(sizeof(XT));
     static constexpr int XPC = 16 / XB;     // activation elements per 16-byte piece
     static constexpr int XCH = DK / XPC;    // pieces per token row of a chunk
     static constexpr int WST = DK4 * EPAD;  // float4 per weight stage
     static constexpr int XST = TOK * XCH;   // 16-byte pieces per activation stage
     static constexpr size_t SMEM =
-        16 * static_cast<size_t>(kStages) * (WST + XST) + 4 * static_cast<size_t>(TOK) * XS;
+        16 * static_cast<size_t>(kStages) * (WST + XST) + 4 * static_cast<size_t>(TOK / 2) * XS;
     static_assert(DK % XPC == 0, "activation chunk must be whole 16-byte pieces");
+    static_assert(TPG % 2 == 0, "tokens are processed in pairs");
 };
 
 template <int GROUP, int NSLOT, int kTPG, int WARPS, typename XT, bool EXACT>
@@ -113,11 +119,11 @@ __global__ void __launch_bounds__(WARPS * 32)
     const int64_t tok0 = static_cast<int64_t>(blockIdx.x) * TOK;
     const int tbase = (warp * GPW + grp) * kTPG;  // first local token of this lane group
 
-    float acc[kTPG][NSLOT];
+    float2 acc[kTPG / 2][NSLOT];  // (token 2p, token 2p+1) of this lane group
 #pragma unroll
-    for (int i = 0; i < kTPG; ++i)
+    for (int i = 0; i < kTPG / 2; ++i)
 #pragma unroll
-        for (int s = 0; s < NSLOT; ++s) acc[i][s] = 0.0f;
+        for (int s = 0; s < NSLOT; ++s) acc[i][s] = make_float2(0.0f, 0.0f);
 
     // activation rows can be copied in 16-byte pieces when every row start is aligned
     const bool xvec = (static_cast<int64_t>(D) * XB) % 16 == 0 &&
@@ -154,54 +160,61 @@ __global__ void __launch_bounds__(WARPS * 32)
         const int st = c % kStages;
         const float4* ws = wring + st * WST;
         // the chunk's activations as float32 rows (padded against bank conflicts)
+        auto xpos = [&](int i) {  // element (token i / DK, d i % DK) in the pair layout
+            const int t = i / DK, dd = i % DK;
+            return (t >> 1) * XS + (dd >> 2) * 8 + (dd & 3) * 2 + (t & 1);
+        };
         if (xvec) {
             const XT* xr = reinterpret_cast<const XT*>(xring + st * XST);
-            for (int i = tid; i < TOK * DK; i += kThreads)
-                xs[(i / DK) * XS + (i % DK)] = load_x<XT>(xr + i);
+            for (int i = tid; i < TOK * DK; i += kThreads) xs[xpos(i)] = load_x<XT>(xr + i);
         } else {
             const int d0 = c * DK;
             for (int i = tid; i < TOK * DK; i += kThreads) {
                 const int64_t tg = tok0 + i / DK;
                 const int d = d0 + i % DK;
-                xs[(i / DK) * XS + (i % DK)] =
+                xs[xpos(i)] =
                     (tg < N && d < D) ? load_x<XT>(x + tg * static_cast<int64_t>(D) + d) : 0.0f;
             }
         }
         __syncthreads();
 #pragma unroll 4
         for (int q = 0; q < DK4; ++q) {
-            float4 xv[kTPG];
+            // xa[p] = (t0 d0, t1 d0, t0 d1, t1 d1), xb[p] = (t0 d2, t1 d2, t0 d3, t1 d3)
+            float4 xa[kTPG / 2], xb[kTPG / 2];
 #pragma unroll
-            for (int i = 0; i < kTPG; ++i)
-                xv[i] = *reinterpret_cast<const float4*>(&xs[(tbase + i) * XS + 4 * q]);
+            for (int p = 0; p < kTPG / 2; ++p) {
+                const float* row = &xs[(tbase / 2 + p) * XS + 8 * q];
+                xa[p] = *reinterpret_cast<const float4*>(row);
+                xb[p] = *reinterpret_cast<const float4*>(row + 4);
+            }
 #pragma unroll
             for (int s = 0; s < NSLOT; ++s) {
                 const float4 wv = ws[q * EPAD + le + GROUP * s];
-                if constexpr (EXACT) {
-                    // float32 product, then float32 add, d in increasing order;
-                    // two tokens per packed fp32x2 op.
 #pragma unroll
-                    for (int i = 0; i < kTPG; i += 2) {
-                        float2 a = make_float2(acc[i][s], acc[i + 1][s]);
-                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xv[i].x, xv[i + 1].x),
+                for (int p = 0; p < kTPG / 2; ++p) {
+                    float2 a = acc[p][s];
+                    if constexpr (EXACT) {
+                        // float32 product, then float32 add, d in increasing order,
+                        // two tokens per packed fp32x2 op
+                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xa[p].x, xa[p].y),
                                                      make_float2(wv.x, wv.x)));
-                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xv[i].y, xv[i + 1].y),
+                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xa[p].z, xa[p].w),
                                                      make_float2(wv.y, wv.y)));
-                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xv[i].z, xv[i + 1].z),
+                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xb[p].x, xb[p].y),
                                                      make_float2(wv.z, wv.z)));
-                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xv[i].w, xv[i + 1].w),
+                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xb[p].z, xb[p].w),
                                                      make_float2(wv.w, wv.w)));
-                        acc[i][s] = a.x;
-                        acc[i + 1][s] = a.y;
+                    } else {
+                        a.x = fmaf(xa[p].x, wv.x, a.x);
+                        a.y = fmaf(xa[p].y, wv.x, a.y);
+                        a.x = fmaf(xa[p].z, wv.y, a.x);
+                        a.y = fmaf(xa[p].w, wv.y, a.y);
+                        a.x = fmaf(xb[p].x, wv.z, a.x);
+                        a.y = fmaf(xb[p].y, wv.z, a.y);
+                        a.x = fmaf(xb[p].z, wv.w, a.x);
+                        a.y = fmaf(xb[p].w, wv.w, a.y);
                     }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < kTPG; ++i) {
-                        acc[i][s] = fmaf(xv[i].x, wv.x, acc[i][s]);
-                        acc[i][s] = fmaf(xv[i].y, wv.y, acc[i][s]);
-                        acc[i][s] = fmaf(xv[i].z, wv.z, acc[i][s]);
-                        acc[i][s] = fmaf(xv[i].w, wv.w, acc[i][s]);
-                    }
+                    acc[p][s] = a;
                 }
             }
         }
@@ -226,7 +239,8 @@ __global__ void __launch_bounds__(WARPS * 32)
 #pragma unroll
         for (int s = 0; s < NSLOT; ++s) {
             const int e = le + GROUP * s;
-            v[s] = e < E ? __fadd_rn(acc[i][s], bv[s]) : -FLT_MAX;
+            const float lg = (i & 1) ? acc[i >> 1][s].y : acc[i >> 1][s].x;
+            v[s] = e < E ? __fadd_rn(lg, bv[s]) : -FLT_MAX;
         }
         // every lane of the group learns each winner; lane 0 of the group
         // writes it (weight un-normalised), then the group normalises
