@@ -112,7 +112,6 @@ struct Cfg {
     static constexpr int S8_RAW = (196 * 1024 - DX * XS - D16 * W16) / W8;
     static constexpr int S8 = S8_RAW > 12 ? 12 : S8_RAW;
     static constexpr int TMEM_COLS = 2 * BT < 32 ? 32 : 2 * BT;
-    static constexpr uint32_t IDESC = idesc_bf16_f32(kCh, BT);
     static constexpr int BAR_BYTES = (2 * DX + 2 * D16 + 2 * S8 + 4) * 8 + 16;
     static constexpr int TAB_BYTES = 2 * (kMaxGroups + 1) * 4;
     static constexpr int SMEM = 1024 + D16 * W16 + DX * XS + S8 * W8 + BAR_BYTES + TAB_BYTES;
@@ -169,13 +168,16 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const int* s_rows, const 
 // float's upper half (integers |b| <= 128 have no low mantissa bits).
 __device__ __forceinline__ uint2 i8x4_to_bf16x4(uint32_t v) {
     const uint32_t u = v ^ 0x80808080u;
-    const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)) - 8388736.0f;
-    const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441)) - 8388736.0f;
-    const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)) - 8388736.0f;
-    const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443)) - 8388736.0f;
+    const float2 m = make_float2(-8388736.0f, -8388736.0f);  // two subtractions per packed op
+    const float2 f01 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)),
+                                              __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441))),
+                                  m);
+    const float2 f23 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)),
+                                              __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443))),
+                                  m);
     uint2 o;
-    o.x = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
-    o.y = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
+    o.x = __byte_perm(__float_as_uint(f01.x), __float_as_uint(f01.y), 0x7632);
+    o.y = __byte_perm(__float_as_uint(f23.x), __float_as_uint(f23.y), 0x7632);
     return o;
 }
 
@@ -332,6 +334,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BT);
+                // a group's last tile may hold fewer rows: the MMA's N covers
+                // only those (a multiple of 16), the rest of the slot is unused
+                const int n_eff = min(BT, (ti.nrows + 15) & ~15);
+                const uint32_t idesc = idesc_bf16_f32(kCh, static_cast<uint32_t>(n_eff));
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
                     if (!mbar_wait_bounded(&x_full[sx], phx, abort_flag, p.err, ERR_GEMM_TIMEOUT) ||
                         !mbar_wait_bounded(&w16_full[s16], ph16, abort_flag, p.err,
@@ -346,10 +352,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int kk = 0; kk < kKT / 16; ++kk) {
                         // +32 bytes along K per UMMA_K=16 step (start address field, >>4)
-                        tc_mma_f16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, C::IDESC,
+                        tc_mma_f16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc,
                                    (kt > ti.kt0 || kk > 0) ? 1u : 0u);
                         if (SPLIT == 2)
-                            tc_mma_f16(d_tmem, adesc + 2 * kk, ldesc + 2 * kk, C::IDESC, 1u);
+                            tc_mma_f16(d_tmem, adesc + 2 * kk, ldesc + 2 * kk, idesc, 1u);
                     }
                     // both operand slots free once these MMAs retire
                     tc_commit(&x_empty[sx]);
