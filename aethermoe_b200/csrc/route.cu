@@ -25,8 +25,14 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kPerThread = 8;
-constexpr int kChunk = kThreads * kPerThread;  // 2048 positions per chunk
+// Positions per thread of the chunk kernels: the stand-alone capacity rule
+// uses 2048-position chunks (its scratch sizes are part of the ABI), the MoE
+// routing 512-position ones (4x the CTAs for the same batch).
+constexpr int kPerThreadApi = 8;
+constexpr int kPerThreadMoe = 2;
+constexpr int kChunk = kThreads * kPerThreadApi;
+constexpr int kChunkMoe = kThreads * kPerThreadMoe;
+constexpr int kScanThreads = 1024;
 
 // MoE units, slot-major: u = j*T + t, primary = idx[t][j], secondary = idx[t][k]
 // (the (k+1)-th choice; the primary when the gating produced only k).
@@ -91,13 +97,15 @@ __global__ void gather_by_position_kernel(const uint32_t* __restrict__ primary,
 }
 
 // Histogram of keys per chunk: cnt[c][e].
+template <int PT>
 __global__ void __launch_bounds__(kThreads)
     chunk_count_kernel(const uint32_t* __restrict__ key, int64_t n, int E, int* __restrict__ cnt) {
+    constexpr int CH = kThreads * PT;
     __shared__ int h[AEM_MAX_EXPERTS];
     for (int e = threadIdx.x; e < E; e += kThreads) h[e] = 0;
     __syncthreads();
-    const int64_t base = static_cast<int64_t>(blockIdx.x) * kChunk;
-    for (int i = threadIdx.x; i < kChunk; i += kThreads) {
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * CH;
+    for (int i = threadIdx.x; i < CH; i += kThreads) {
         const int64_t p = base + i;
         if (p < n) {
             const uint32_t e = key[p];
@@ -110,17 +118,27 @@ __global__ void __launch_bounds__(kThreads)
 
 // In place: cnt[c][e] -> exclusive prefix over c.  Optionally totals[e] and
 // starts[0..E] (exclusive prefix of totals over e).  One CTA.
-__global__ void __launch_bounds__(kThreads)
+// Exclusive prefix of every expert's per-chunk counts over the chunks (in
+// place), one warp per expert; then the expert starts.
+__global__ void __launch_bounds__(kScanThreads)
     chunk_scan_kernel(int* __restrict__ cnt, int nchunks, int E, int* __restrict__ starts) {
     __shared__ int tot[AEM_MAX_EXPERTS];
-    for (int e = threadIdx.x; e < E; e += kThreads) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int e = warp; e < E; e += kScanThreads / 32) {
         int run = 0;
-        for (int c = 0; c < nchunks; ++c) {
-            const int v = cnt[static_cast<int64_t>(c) * E + e];
-            cnt[static_cast<int64_t>(c) * E + e] = run;
-            run += v;
+        for (int c0 = 0; c0 < nchunks; c0 += 32) {
+            const int c = c0 + lane;
+            const int v = c < nchunks ? cnt[static_cast<int64_t>(c) * E + e] : 0;
+            int inc = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int nb = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+                if (lane >= o) inc += nb;
+            }
+            if (c < nchunks) cnt[static_cast<int64_t>(c) * E + e] = run + inc - v;
+            run += __shfl_sync(0xFFFFFFFFu, inc, 31);
         }
-        tot[e] = run;
+        if (lane == 0) tot[e] = run;
     }
     __syncthreads();
     if (starts && threadIdx.x == 0) {
@@ -133,19 +151,17 @@ __global__ void __launch_bounds__(kThreads)
     }
 }
 
-// Stable rank of every position of this chunk within its key group:
-// off[c][key] + number of earlier positions in the chunk with the same key.
-// Calls `emit(p, key, rank)` for every valid position.
-template <typename Emit>
+template <int PT, typename Emit>
 __device__ __forceinline__ void chunk_ranks(const uint32_t* __restrict__ key, int64_t n, int E,
                                             const int* __restrict__ off, Emit emit) {
+    constexpr int CH = kThreads * PT;
     __shared__ int run[AEM_MAX_EXPERTS];
     __shared__ int hw[kWarps][AEM_MAX_EXPERTS];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const unsigned lt = (1u << lane) - 1u;
     for (int e = tid; e < E; e += kThreads) run[e] = off[static_cast<int64_t>(blockIdx.x) * E + e];
-    const int64_t base = static_cast<int64_t>(blockIdx.x) * kChunk;
-    for (int r = 0; r < kPerThread; ++r) {
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * CH;
+    for (int r = 0; r < PT; ++r) {
         for (int i = tid; i < kWarps * E; i += kThreads) hw[i / E][i % E] = 0;
         __syncthreads();
         const int64_t p = base + static_cast<int64_t>(r) * kThreads + tid;
@@ -173,12 +189,13 @@ __device__ __forceinline__ void chunk_ranks(const uint32_t* __restrict__ key, in
 
 // Pass 1: effective expert of every position.  EP: rank += corr[slot][key]
 // with slot = p / slot_len (corr == nullptr for a single GPU).
+template <int PT>
 __global__ void __launch_bounds__(kThreads)
     assign_kernel(const uint32_t* __restrict__ prim, const uint32_t* __restrict__ sec, int64_t n,
                   int E, const int* __restrict__ off, uint64_t capacity,
                   const int64_t* __restrict__ corr, int64_t slot_len,
                   const int32_t* __restrict__ out_index, uint32_t* __restrict__ eff) {
-    chunk_ranks(prim, n, E, off, [&](int64_t p, uint32_t e, int rank) {
+    chunk_ranks<PT>(prim, n, E, off, [&](int64_t p, uint32_t e, int rank) {
         int64_t rk = rank;
         if (corr) rk += corr[(p / slot_len) * E + e];
         const uint32_t v = static_cast<uint64_t>(rk) < capacity ? e : sec[p];
@@ -190,13 +207,14 @@ __global__ void __launch_bounds__(kThreads)
 // Pass 2 (MoE permutation): unit u goes to row starts[e] + rank of the
 // expert-grouped layout; records the token it came from, the output row of
 // its expert result (t*k + j) and its gate weight.
+template <int PT>
 __global__ void __launch_bounds__(kThreads)
     scatter_kernel(const uint32_t* __restrict__ eff, int64_t n, int E, const int* __restrict__ off,
                    const int* __restrict__ starts, int64_t T, int k,
                    const float* __restrict__ val, int32_t* __restrict__ src_token,
                    int32_t* __restrict__ rowmap, float* __restrict__ rowscale,
                    int32_t* __restrict__ dest_of) {
-    chunk_ranks(eff, n, E, off, [&](int64_t u, uint32_t e, int rank) {
+    chunk_ranks<PT>(eff, n, E, off, [&](int64_t u, uint32_t e, int rank) {
         const int64_t dest = starts[e] + rank;
         const int64_t j = u / T, t = u % T;
         src_token[dest] = static_cast<int32_t>(t);
@@ -209,10 +227,11 @@ __global__ void __launch_bounds__(kThreads)
 }  // namespace
 
 int64_t route_chunks(int64_t n) { return (n + kChunk - 1) / kChunk; }
+static int64_t route_chunks_moe(int64_t n) { return (n + kChunkMoe - 1) / kChunkMoe; }
 
 size_t moe_route_workspace(int64_t T, int k, int E) {
     const int64_t n = T * k;
-    const int64_t c = route_chunks(n) > 0 ? route_chunks(n) : 1;
+    const int64_t c = route_chunks_moe(n) > 0 ? route_chunks_moe(n) : 1;
     size_t b = 0;
     b += align_up(sizeof(uint32_t) * n, 256) * 3;      // prim, sec, eff
     b += align_up(sizeof(int) * c * E, 256) * 2;        // cnt1, cnt2
@@ -223,7 +242,7 @@ size_t moe_route_workspace(int64_t T, int k, int E) {
 aem_status route_moe(const MoeRouteArgs& a, cudaStream_t s) {
     const int64_t n = a.T * a.k;
     if (n == 0) return AEM_OK;
-    const int64_t c = route_chunks(n);
+    const int64_t c = route_chunks_moe(n);
     char* w = static_cast<char*>(a.workspace);
     auto take = [&](size_t bytes) {
         char* p = w;
@@ -242,18 +261,20 @@ aem_status route_moe(const MoeRouteArgs& a, cudaStream_t s) {
     const unsigned gb = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 4096));
     build_units_kernel<<<gb, 256, 0, s>>>(a.idx, a.T, a.ldi, a.k, a.E, prim, sec, err);
     AEM_CHECK_LAUNCH();
-    chunk_count_kernel<<<static_cast<unsigned>(c), kThreads, 0, s>>>(prim, n, a.E, cnt1);
+    chunk_count_kernel<kPerThreadMoe><<<static_cast<unsigned>(c), kThreads, 0, s>>>(prim, n, a.E,
+                                                                                 cnt1);
     AEM_CHECK_LAUNCH();
-    chunk_scan_kernel<<<1, kThreads, 0, s>>>(cnt1, static_cast<int>(c), a.E, nullptr);
+    chunk_scan_kernel<<<1, kScanThreads, 0, s>>>(cnt1, static_cast<int>(c), a.E, nullptr);
     AEM_CHECK_LAUNCH();
-    assign_kernel<<<static_cast<unsigned>(c), kThreads, 0, s>>>(
+    assign_kernel<kPerThreadMoe><<<static_cast<unsigned>(c), kThreads, 0, s>>>(
         prim, sec, n, a.E, cnt1, a.capacity, a.corr, a.T, nullptr, eff);
     AEM_CHECK_LAUNCH();
-    chunk_count_kernel<<<static_cast<unsigned>(c), kThreads, 0, s>>>(eff, n, a.E, cnt2);
+    chunk_count_kernel<kPerThreadMoe><<<static_cast<unsigned>(c), kThreads, 0, s>>>(eff, n, a.E,
+                                                                                 cnt2);
     AEM_CHECK_LAUNCH();
-    chunk_scan_kernel<<<1, kThreads, 0, s>>>(cnt2, static_cast<int>(c), a.E, starts);
+    chunk_scan_kernel<<<1, kScanThreads, 0, s>>>(cnt2, static_cast<int>(c), a.E, starts);
     AEM_CHECK_LAUNCH();
-    scatter_kernel<<<static_cast<unsigned>(c), kThreads, 0, s>>>(
+    scatter_kernel<kPerThreadMoe><<<static_cast<unsigned>(c), kThreads, 0, s>>>(
         eff, n, a.E, cnt2, starts, a.T, a.k, a.val, a.src_token, a.rowmap, a.rowscale, a.dest_of);
     AEM_CHECK_LAUNCH();
     count_launches(7);
@@ -322,9 +343,10 @@ aem_status aem_capacity_route(const uint32_t* primary, const uint32_t* secondary
         aem::invert_positions_kernel<<<gb, 256, 0, s>>>(batch_position, n, inv, seen, err);
         aem::gather_by_position_kernel<<<gb, 256, 0, s>>>(primary, secondary, inv, n, E, prim_s,
                                                           sec_s, err);
-        aem::chunk_count_kernel<<<static_cast<unsigned>(c), aem::kThreads, 0, s>>>(prim_s, n, E, cnt);
-        aem::chunk_scan_kernel<<<1, aem::kThreads, 0, s>>>(cnt, static_cast<int>(c), E, nullptr);
-        aem::assign_kernel<<<static_cast<unsigned>(c), aem::kThreads, 0, s>>>(
+        aem::chunk_count_kernel<aem::kPerThreadApi><<<static_cast<unsigned>(c), aem::kThreads, 0, s>>>(
+        prim_s, n, E, cnt);
+        aem::chunk_scan_kernel<<<1, aem::kScanThreads, 0, s>>>(cnt, static_cast<int>(c), E, nullptr);
+        aem::assign_kernel<aem::kPerThreadApi><<<static_cast<unsigned>(c), aem::kThreads, 0, s>>>(
             prim_s, sec_s, n, E, cnt, capacity, nullptr, 1, inv, effective);
         aem::count_launches(5);
         cudaError_t le = cudaGetLastError();
@@ -426,9 +448,10 @@ extern "C" aem_status aem_capacity_route_static(const uint32_t* primary, const u
     aem::invert_positions_kernel<<<gb, 256, 0, s>>>(batch_position, n, inv, seen, err);
     aem::gather_by_position_kernel<<<gb, 256, 0, s>>>(primary, secondary, inv, n, E, prim_s, sec_s,
                                                       err);
-    aem::chunk_count_kernel<<<static_cast<unsigned>(c), aem::kThreads, 0, s>>>(prim_s, n, E, cnt);
-    aem::chunk_scan_kernel<<<1, aem::kThreads, 0, s>>>(cnt, static_cast<int>(c), E, nullptr);
-    aem::assign_kernel<<<static_cast<unsigned>(c), aem::kThreads, 0, s>>>(
+    aem::chunk_count_kernel<aem::kPerThreadApi><<<static_cast<unsigned>(c), aem::kThreads, 0, s>>>(
+        prim_s, n, E, cnt);
+    aem::chunk_scan_kernel<<<1, aem::kScanThreads, 0, s>>>(cnt, static_cast<int>(c), E, nullptr);
+    aem::assign_kernel<aem::kPerThreadApi><<<static_cast<unsigned>(c), aem::kThreads, 0, s>>>(
         prim_s, sec_s, n, E, cnt, capacity, nullptr, 1, inv, effective);
     AEM_CHECK_LAUNCH();
     aem::count_launches(5);
