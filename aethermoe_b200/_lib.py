@@ -67,12 +67,20 @@ class MetricStats(ctypes.Structure):
 class EpPeerPlan(ctypes.Structure):
     """``aem_ep_peer_plan``: where one rank's rows go in one peer-memory exchange."""
     _fields_ = [("ok", ctypes.c_int32), ("units_in", ctypes.c_int32),
+                ("units_in_a", ctypes.c_int32),
                 ("pairs_in", ctypes.c_int32), ("pairs_out", ctypes.c_int32),
-                ("dst_unit_off", ctypes.c_int32 * 256),
+                ("dst_unit_off", (ctypes.c_int32 * 256) * 2),
                 ("dst_pair_off", ctypes.c_int32 * EP_MAX_RANKS),
                 ("send_pair_off", ctypes.c_int32 * EP_MAX_RANKS),
+                ("send_pair_a", ctypes.c_int32 * EP_MAX_RANKS),
                 ("recv_pair_off", ctypes.c_int32 * (EP_MAX_RANKS + 1)),
+                ("recv_pair_a", ctypes.c_int32 * EP_MAX_RANKS),
                 ("ret_off", ctypes.c_int32 * EP_MAX_RANKS)]
+
+
+def ep_payload_words(E, R):
+    """``AEM_EP_PAYLOAD(E, R)``: int32 words of one rank's exchange payload."""
+    return (2 * E + 3 + 2 * R + 3) & ~3
 
 
 _SIGS = {
@@ -117,6 +125,7 @@ _SIGS = {
     "aem_ep_mark_unhealthy": (_int, [_vp, _int]),
     "aem_ep_health": (_int, [_vp, ctypes.POINTER(_u64), _vp]),
     "aem_ep_set_timeout": (_int, [_vp, ctypes.c_double]),
+    "aem_ep_set_pipeline": (_int, [_vp, _int]),
     "aem_ep_create": (_int, [ctypes.POINTER(MoeConfig), _int, _int, _vp, _vp, _vp, _vp, _vp,
                              _i64, ctypes.POINTER(_vp)]),
     "aem_ep_free": (_int, [_vp]),

@@ -125,33 +125,51 @@ static const NcclApi* nccl() {
 
 namespace aem {
 
+// Payload word offsets (see AEM_EP_PAYLOAD): expert starts [E+1], pairs per
+// destination [R], live mask [2], half-A units per expert [E], half-A pairs
+// per destination [R].
+__host__ __device__ constexpr int pay_pairs(int E) { return E + 1; }
+__host__ __device__ constexpr int pay_mask(int E, int R) { return E + 1 + R; }
+__host__ __device__ constexpr int pay_units_a(int E, int R) { return E + 3 + R; }
+__host__ __device__ constexpr int pay_pairs_a(int E, int R) { return 2 * E + 3 + R; }
+
 // Per-step plan of one rank (see aem_ep_peer_plan).  Row s of `all` (stride
-// `ld` int32) holds rank s's expert starts [E+1], then its pair counts per
-// destination [R].  Only ranks in `live` take part: other rows are ignored,
-// and units or pairs addressed to other ranks count as absent.  Every rank
-// runs this on the same data, so all agree on `ok`.
+// `ld` int32) is rank s's payload.  Only ranks in `live` take part: other
+// rows are ignored, and units or pairs addressed to other ranks count as
+// absent.  Every rank runs this on the same data, so all agree on `ok`.
+// groups: [2][E/R+1], half A's row groups then half B's.
 __host__ __device__ inline void plan_peer(const int32_t* all, int ld, int R, int E, int me,
                                           uint64_t live, int64_t ucap, int64_t pcap, int64_t rcap,
                                           aem_ep_peer_plan* pl, int32_t* groups) {
     const int el = E / R;
+    const int PP = pay_pairs(E), PUA = pay_units_a(E, R), PPA = pay_pairs_a(E, R);
     auto in = [&](int r) { return ((live >> r) & 1ull) != 0; };
     auto row = [&](int s) { return all + static_cast<int64_t>(s) * ld; };
-    auto units = [&](int s, int r) -> int64_t {
-        return (in(s) && in(r)) ? row(s)[(r + 1) * el] - row(s)[r * el] : 0;
+    auto ut = [&](int s, int e) -> int64_t {  // units of expert e from s
+        return (in(s) && in(e / el)) ? row(s)[e + 1] - row(s)[e] : 0;
     };
-    auto pairs = [&](int s, int r) -> int64_t { return (in(s) && in(r)) ? row(s)[E + 1 + r] : 0; };
+    auto ua = [&](int s, int e) -> int64_t { return (in(s) && in(e / el)) ? row(s)[PUA + e] : 0; };
+    auto pairs = [&](int s, int r) -> int64_t { return (in(s) && in(r)) ? row(s)[PP + r] : 0; };
+    auto pairs_a = [&](int s, int r) -> int64_t { return (in(s) && in(r)) ? row(s)[PPA + r] : 0; };
     bool ok = in(me);
     for (int s = 0; s < R && ok; ++s) {
         if (!in(s)) continue;
         const int32_t* a = row(s);
         if (a[0] != 0) ok = false;
         for (int e = 0; e < E; ++e)
-            if (a[e + 1] < a[e]) ok = false;
+            if (a[e + 1] < a[e] || a[PUA + e] < 0 || a[PUA + e] > a[e + 1] - a[e]) ok = false;
         int64_t pout = 0;
         for (int r = 0; r < R; ++r) {
-            const int64_t u = units(s, r), p = pairs(s, r);
-            // a pair exists exactly when the token has a unit there
+            int64_t u = 0, uA = 0;
+            for (int e = r * el; e < (r + 1) * el; ++e) {
+                u += ut(s, e);
+                uA += ua(s, e);
+            }
+            const int64_t p = pairs(s, r), pA = pairs_a(s, r);
+            // a pair (of a half) exists exactly when the token has a unit there
             if (p < 0 || p > u || ((u > 0) != (p > 0))) ok = false;
+            if (pA < 0 || pA > p || pA > uA || ((uA > 0) != (pA > 0))) ok = false;
+            if (p - pA > u - uA || ((u - uA > 0) != (p - pA > 0))) ok = false;
             pout += p;
         }
         if (pout > rcap) ok = false;
@@ -159,28 +177,25 @@ __host__ __device__ inline void plan_peer(const int32_t* all, int ld, int R, int
     for (int r = 0; r < R && ok; ++r) {
         int64_t u = 0, p = 0;
         for (int s = 0; s < R; ++s) {
-            u += units(s, r);
+            for (int e = r * el; e < (r + 1) * el; ++e) u += ut(s, e);
             p += pairs(s, r);
         }
         if (u > ucap || p > pcap) ok = false;
     }
     pl->ok = ok ? 1 : 0;
-    pl->units_in = pl->pairs_in = pl->pairs_out = 0;
+    pl->units_in = pl->units_in_a = pl->pairs_in = pl->pairs_out = 0;
     for (int r = 0; r < AEM_EP_MAX_RANKS; ++r) {
-        pl->dst_pair_off[r] = pl->send_pair_off[r] = 0;
-        pl->recv_pair_off[r] = pl->ret_off[r] = 0;
+        pl->dst_pair_off[r] = pl->send_pair_off[r] = pl->send_pair_a[r] = 0;
+        pl->recv_pair_off[r] = pl->recv_pair_a[r] = pl->ret_off[r] = 0;
     }
-    for (int e = 0; e < AEM_MAX_EXPERTS; ++e) pl->dst_unit_off[e] = 0;
+    for (int e = 0; e < AEM_MAX_EXPERTS; ++e) pl->dst_unit_off[0][e] = pl->dst_unit_off[1][e] = 0;
     pl->recv_pair_off[AEM_EP_MAX_RANKS] = 0;
-    for (int i = 0; i <= el; ++i) groups[i] = 0;
+    for (int i = 0; i < 2 * (el + 1); ++i) groups[i] = 0;
     if (!ok) return;
-    // units of expert e from source s (placement positions)
-    auto eu = [&](int s, int e) -> int64_t {
-        return (in(s) && in(e / el)) ? row(s)[e + 1] - row(s)[e] : 0;
-    };
     int64_t acc = 0;
     for (int r = 0; r < R; ++r) {
         pl->send_pair_off[r] = static_cast<int32_t>(acc);
+        pl->send_pair_a[r] = static_cast<int32_t>(pairs_a(me, r));
         acc += pairs(me, r);
     }
     pl->pairs_out = static_cast<int32_t>(acc);
@@ -188,22 +203,33 @@ __host__ __device__ inline void plan_peer(const int32_t* all, int ld, int R, int
         int64_t p = 0;
         for (int s = 0; s < me; ++s) p += pairs(s, r);
         pl->dst_pair_off[r] = static_cast<int32_t>(p);
-        // rank r receives expert-major: its local experts in order, every
+        // rank r receives half A then half B, each expert-major with every
         // source's units of one expert contiguous, sources in rank order
-        int64_t u = 0;
+        int64_t uA_r = 0;
+        for (int e = r * el; e < (r + 1) * el; ++e)
+            for (int s = 0; s < R; ++s) uA_r += ua(s, e);
+        int64_t u0 = 0, u1 = uA_r;
         for (int e = r * el; e < (r + 1) * el; ++e) {
-            int64_t before = 0, all_s = 0;
+            int64_t b0 = 0, b1 = 0, t0 = 0, t1 = 0;
             for (int s = 0; s < R; ++s) {
-                if (s < me) before += eu(s, e);
-                all_s += eu(s, e);
+                const int64_t a0 = ua(s, e), a1 = ut(s, e) - ua(s, e);
+                if (s < me) {
+                    b0 += a0;
+                    b1 += a1;
+                }
+                t0 += a0;
+                t1 += a1;
             }
-            pl->dst_unit_off[e] = static_cast<int32_t>(u + before);
-            u += all_s;
+            pl->dst_unit_off[0][e] = static_cast<int32_t>(u0 + b0);
+            pl->dst_unit_off[1][e] = static_cast<int32_t>(u1 + b1);
+            u0 += t0;
+            u1 += t1;
         }
     }
     acc = 0;
     for (int s = 0; s < R; ++s) {
         pl->recv_pair_off[s] = static_cast<int32_t>(acc);
+        pl->recv_pair_a[s] = static_cast<int32_t>(pairs_a(s, me));
         acc += pairs(s, me);
         int64_t before = 0;
         for (int r = 0; r < me; ++r) before += pairs(s, r);
@@ -212,9 +238,16 @@ __host__ __device__ inline void plan_peer(const int32_t* all, int ld, int R, int
     pl->recv_pair_off[R] = static_cast<int32_t>(acc);
     pl->pairs_in = static_cast<int32_t>(acc);
     int64_t g = 0;
-    for (int e = 0; e < el; ++e) {
-        for (int s = 0; s < R; ++s) g += eu(s, me * el + e);
-        groups[e + 1] = static_cast<int32_t>(g);
+    for (int h = 0; h < 2; ++h) {
+        groups[h * (el + 1)] = static_cast<int32_t>(g);
+        for (int e = 0; e < el; ++e) {
+            for (int s = 0; s < R; ++s) {
+                const int64_t a0 = ua(s, me * el + e);
+                g += h == 0 ? a0 : ut(s, me * el + e) - a0;
+            }
+            groups[h * (el + 1) + e + 1] = static_cast<int32_t>(g);
+        }
+        if (h == 0) pl->units_in_a = static_cast<int32_t>(g);
     }
     pl->units_in = static_cast<int32_t>(g);
 }
@@ -226,7 +259,15 @@ using namespace aem::dev;
 constexpr int kCopyThreads = 256;
 
 // Synchronisation points of a step, one flag per (point, source rank).
-enum { SYNC_COUNTS = 0, SYNC_PLAN = 1, SYNC_DISPATCH = 2, SYNC_RETURN = 3, kSyncPoints = 4 };
+enum {
+    SYNC_COUNTS = 0,
+    SYNC_PLAN = 1,
+    SYNC_DISPATCH_A = 2,
+    SYNC_DISPATCH_B = 3,
+    SYNC_RETURN_A = 4,
+    SYNC_RETURN_B = 5,
+    kSyncPoints = 6
+};
 
 // Base pointers of every rank's exchange region (this rank's own at [me]).
 struct EpPeers {
@@ -382,26 +423,38 @@ __global__ void unlabel_kernel(const uint32_t* __restrict__ in, int64_t n,
 
 // Block r numbers the tokens that have at least one unit on rank r, in token
 // order: pair_local[r][t] = that number, or -1 (always -1 for a rank outside
-// `live`: its units fail).  Writes the all-gather payload: the expert starts,
-// the pair count per destination, the live mask.
+// `live`: its units fail); half-A tokens (t < half_T) come first.  Writes the
+// all-gather payload: the expert starts, the pair count per destination, the
+// live mask, the half-A units per expert (block 0) and the half-A pairs per
+// destination.
 __global__ void __launch_bounds__(1024)
-    ep_pairs_kernel(const uint32_t* __restrict__ eff, int64_t T, int k, int el, int E, int R,
-                    uint64_t live, const int* __restrict__ starts, int32_t* __restrict__ pair_local,
-                    int32_t* __restrict__ payload) {
+    ep_pairs_kernel(const uint32_t* __restrict__ eff, int64_t T, int64_t half_T, int k, int el,
+                    int E, int R, uint64_t live, const int* __restrict__ starts,
+                    int32_t* __restrict__ pair_local, int32_t* __restrict__ payload) {
     __shared__ int wsum[32];
-    __shared__ int running;
+    __shared__ int running, running_a;
+    __shared__ int hist[AEM_MAX_EXPERTS];
     const int r = blockIdx.x;
     const bool on = ((live >> r) & 1ull) != 0;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nwarps = blockDim.x >> 5;
     if (r == 0) {
         for (int i = tid; i <= E; i += blockDim.x) payload[i] = starts[i];
+        for (int i = tid; i < E; i += blockDim.x) hist[i] = 0;
         if (tid == 0) {
-            payload[E + 1 + R] = static_cast<int32_t>(live & 0xFFFFFFFFull);
-            payload[E + 2 + R] = static_cast<int32_t>(live >> 32);
+            payload[pay_mask(E, R)] = static_cast<int32_t>(live & 0xFFFFFFFFull);
+            payload[pay_mask(E, R) + 1] = static_cast<int32_t>(live >> 32);
         }
+        __syncthreads();
+        for (int64_t i = tid; i < half_T * k; i += blockDim.x) {  // half-A units per expert
+            const int64_t j = i / half_T, t = i % half_T;
+            const uint32_t e = eff[j * T + t];
+            if (e < static_cast<uint32_t>(E)) atomicAdd(&hist[e], 1);
+        }
+        __syncthreads();
+        for (int i = tid; i < E; i += blockDim.x) payload[pay_units_a(E, R) + i] = hist[i];
     }
-    if (tid == 0) running = 0;
+    if (tid == 0) running = running_a = 0;
     __syncthreads();
     for (int64_t base = 0; base < T; base += blockDim.x) {
         const int64_t t = base + tid;
@@ -410,6 +463,8 @@ __global__ void __launch_bounds__(1024)
             for (int j = 0; j < k; ++j)
                 f |= static_cast<int>(eff[static_cast<int64_t>(j) * T + t]) / el == r;
         const unsigned b = __ballot_sync(0xFFFFFFFFu, f);
+        const unsigned ba = __ballot_sync(0xFFFFFFFFu, f && t < half_T);
+        if (lane == 0 && ba) atomicAdd(&running_a, __popc(ba));
         const int pre = __popc(b & ((1u << lane) - 1u));
         if (lane == 0) wsum[warp] = __popc(b);
         __syncthreads();
@@ -430,18 +485,21 @@ __global__ void __launch_bounds__(1024)
         if (tid == 0) running = run + wsum[nwarps - 1];
         __syncthreads();
     }
-    if (tid == 0) payload[E + 1 + r] = running;
+    if (tid == 0) {
+        payload[pay_pairs(E) + r] = running;
+        payload[pay_pairs_a(E, R) + r] = running_a;
+    }
 }
 
-// plan_peer for one thread block, in parallel over ranks and experts, on a
-// shared-memory copy of the payload rows (the single-thread form is
+// plan_peer for one thread block, in parallel over ranks and experts, with
+// the per-rank tables in shared memory (the single-thread form is
 // latency-bound on thousands of dependent loads).  Same results as
 // plan_peer, field by field; `check_masks` also requires every usable row's
 // live mask (words E+1+R, E+2+R) to equal `live`.  Dynamic shared memory:
 // plan_block_smem(R, E, ld) bytes.  Returns in every thread whether the plan
 // is ok.
 __host__ __device__ constexpr size_t plan_block_smem(int R, int E, int ld) {
-    return sizeof(int32_t) * (static_cast<size_t>(R) * ld + 2 * R * R + 2 * E) + 16;
+    return (void)ld, sizeof(int32_t) * (4 * static_cast<size_t>(R) * R + 4 * E) + 16;
 }
 
 __device__ bool plan_peer_block(const int32_t* __restrict__ all, int ld, int R, int E, int me,
@@ -449,53 +507,79 @@ __device__ bool plan_peer_block(const int32_t* __restrict__ all, int ld, int R, 
                                 int64_t pcap, int64_t rcap, aem_ep_peer_plan* __restrict__ pl,
                                 int32_t* __restrict__ groups) {
     extern __shared__ int32_t sm[];
-    int32_t* A = sm;                      // [R][ld]
-    int32_t* U = A + R * ld;              // [R][R] units s -> r
-    int32_t* P = U + R * R;               // [R][R] pairs s -> r
-    int32_t* colsum = P + R * R;          // [E] units of expert e, every source
-    int32_t* before = colsum + E;         // [E] units of expert e from sources < me
+    const int32_t* A = all;               // [R][ld] payload rows (L2; every load independent)
+    int32_t* U = sm;                      // [R][R] units s -> r
+    int32_t* UA = U + R * R;              // [R][R] half-A units s -> r
+    int32_t* P = UA + R * R;              // [R][R] pairs s -> r
+    int32_t* PA = P + R * R;              // [R][R] half-A pairs s -> r
+    int32_t* colA = PA + R * R;           // [E] half-A units of expert e, every source
+    int32_t* colB = colA + E;             // [E] half-B units
+    int32_t* befA = colB + E;             // [E] half-A units from sources < me
+    int32_t* befB = befA + E;             // [E] half-B units from sources < me
     __shared__ int bad;
     const int tid = threadIdx.x, nt = blockDim.x;
     const int el = E / R;
+    const int PP = pay_pairs(E), PM = pay_mask(E, R), PUA = pay_units_a(E, R),
+              PPA = pay_pairs_a(E, R);
     auto in = [&](int r) { return ((live >> r) & 1ull) != 0; };
     if (tid == 0) bad = (already_failed || !in(me)) ? 1 : 0;
-    for (int i = tid; i < R * ld; i += nt) A[i] = all[i];
     __syncthreads();
     for (int i = tid; i < R * (E + 1); i += nt) {
         const int sr = i / (E + 1), e = i % (E + 1);
         if (!in(sr)) continue;
         const int32_t* a = A + sr * ld;
-        if (e == 0 ? a[0] != 0 : a[e] < a[e - 1]) bad = 1;
+        if (e == 0) {
+            if (a[0] != 0) bad = 1;
+        } else if (a[e] < a[e - 1] || a[PUA + e - 1] < 0 || a[PUA + e - 1] > a[e] - a[e - 1]) {
+            bad = 1;
+        }
     }
     for (int i = tid; i < R * R; i += nt) {
         const int sr = i / R, r = i % R;
         const bool on = in(sr) && in(r);
         const int32_t* a = A + sr * ld;
-        const int32_t u = on ? a[(r + 1) * el] - a[r * el] : 0;
-        const int32_t p = on ? a[E + 1 + r] : 0;
+        int32_t u = 0, ua = 0;
+        if (on) {
+            u = a[(r + 1) * el] - a[r * el];
+            for (int e = r * el; e < (r + 1) * el; ++e) ua += a[PUA + e];
+        }
+        const int32_t p = on ? a[PP + r] : 0;
+        const int32_t pa = on ? a[PPA + r] : 0;
         U[i] = u;
+        UA[i] = ua;
         P[i] = p;
-        if (p < 0 || p > u || ((u > 0) != (p > 0))) bad = 1;  // a pair exists iff a unit does
+        PA[i] = pa;
+        // a pair (of a half) exists exactly when the token has a unit there
+        if (p < 0 || p > u || ((u > 0) != (p > 0))) bad = 1;
+        if (pa < 0 || pa > p || pa > ua || ((ua > 0) != (pa > 0))) bad = 1;
+        if (p - pa > u - ua || ((u - ua > 0) != (p - pa > 0))) bad = 1;
     }
     if (check_masks)
         for (int sr = tid; sr < R; sr += nt) {
             if (!in(sr)) continue;
             const int32_t* a = A + sr * ld;
-            const uint64_t m = static_cast<uint32_t>(a[E + 1 + R]) |
-                               (static_cast<uint64_t>(static_cast<uint32_t>(a[E + 2 + R])) << 32);
+            const uint64_t m = static_cast<uint32_t>(a[PM]) |
+                               (static_cast<uint64_t>(static_cast<uint32_t>(a[PM + 1])) << 32);
             if (m != live) bad = 1;  // the ranks disagree on who takes part
         }
     for (int e = tid; e < E; e += nt) {
-        int32_t cs = 0, bf = 0;
+        int32_t ca = 0, cb = 0, ba = 0, bb = 0;
         const bool on = in(e / el);
         for (int sr = 0; sr < R; ++sr) {
             if (!on || !in(sr)) continue;
-            const int32_t v = A[sr * ld + e + 1] - A[sr * ld + e];
-            cs += v;
-            if (sr < me) bf += v;
+            const int32_t* a = A + sr * ld;
+            const int32_t va = a[PUA + e], vb = a[e + 1] - a[e] - va;
+            ca += va;
+            cb += vb;
+            if (sr < me) {
+                ba += va;
+                bb += vb;
+            }
         }
-        colsum[e] = cs;
-        before[e] = bf;
+        colA[e] = ca;
+        colB[e] = cb;
+        befA[e] = ba;
+        befB[e] = bb;
     }
     __syncthreads();
     for (int i = tid; i < 2 * R; i += nt) {
@@ -516,21 +600,26 @@ __device__ bool plan_peer_block(const int32_t* __restrict__ all, int ld, int R, 
     __syncthreads();
     const bool ok = bad == 0;
     // every field is written (zeros past R, past E, or for a bad plan)
-    for (int i = tid; i < AEM_MAX_EXPERTS; i += nt) pl->dst_unit_off[i] = 0;
+    for (int i = tid; i < AEM_MAX_EXPERTS; i += nt) {
+        pl->dst_unit_off[0][i] = 0;
+        pl->dst_unit_off[1][i] = 0;
+    }
     for (int i = tid; i <= AEM_EP_MAX_RANKS; i += nt) {
         if (i < AEM_EP_MAX_RANKS) {
             pl->dst_pair_off[i] = 0;
             pl->send_pair_off[i] = 0;
+            pl->send_pair_a[i] = 0;
+            pl->recv_pair_a[i] = 0;
             pl->ret_off[i] = 0;
         }
         pl->recv_pair_off[i] = 0;
     }
-    for (int i = tid; i <= el; i += nt) groups[i] = 0;
+    for (int i = tid; i < 2 * (el + 1); i += nt) groups[i] = 0;
     __syncthreads();
     if (!ok) {
         if (tid == 0) {
             pl->ok = 0;
-            pl->units_in = pl->pairs_in = pl->pairs_out = 0;
+            pl->units_in = pl->units_in_a = pl->pairs_in = pl->pairs_out = 0;
         }
         return false;
     }
@@ -541,13 +630,21 @@ __device__ bool plan_peer_block(const int32_t* __restrict__ all, int ld, int R, 
         for (int q = 0; q < r; ++q) ro += P[q * R + me];   // pairs I receive from ranks < r
         for (int q = 0; q < me; ++q) rt += P[r * R + q];   // r's pairs for ranks < me
         pl->send_pair_off[r] = so;
+        pl->send_pair_a[r] = PA[me * R + r];
         pl->dst_pair_off[r] = dp;
         pl->recv_pair_off[r] = ro;
+        pl->recv_pair_a[r] = PA[r * R + me];
         pl->ret_off[r] = rt;
-        int32_t u = 0;  // rank r receives expert-major, sources in rank order inside
+        // rank r receives half A then half B, each expert-major, sources in
+        // rank order inside an expert
+        int32_t ua_r = 0;
+        for (int e = r * el; e < (r + 1) * el; ++e) ua_r += colA[e];
+        int32_t u0 = 0, u1 = ua_r;
         for (int e = r * el; e < (r + 1) * el; ++e) {
-            pl->dst_unit_off[e] = u + before[e];
-            u += colsum[e];
+            pl->dst_unit_off[0][e] = u0 + befA[e];
+            pl->dst_unit_off[1][e] = u1 + befB[e];
+            u0 += colA[e];
+            u1 += colB[e];
         }
     }
     if (tid == 0) {
@@ -556,9 +653,13 @@ __device__ bool plan_peer_block(const int32_t* __restrict__ all, int ld, int R, 
             out += P[me * R + q];
             inn += P[q * R + me];
         }
-        for (int le = 0; le < el; ++le) {
-            g += colsum[me * el + le];
-            groups[le + 1] = g;
+        for (int h = 0; h < 2; ++h) {
+            groups[h * (el + 1)] = g;
+            for (int le = 0; le < el; ++le) {
+                g += h == 0 ? colA[me * el + le] : colB[me * el + le];
+                groups[h * (el + 1) + le + 1] = g;
+            }
+            if (h == 0) pl->units_in_a = g;
         }
         pl->pairs_out = out;
         pl->pairs_in = inn;
@@ -594,7 +695,8 @@ __global__ void ep_plan_test_kernel(const int32_t* __restrict__ all, int R, int 
                                     uint64_t live, int64_t ucap, int64_t pcap, int64_t rcap,
                                     aem_ep_peer_plan* __restrict__ plan,
                                     int32_t* __restrict__ groups) {
-    plan_peer_block(all, E + 1 + R, R, E, me, live, false, false, ucap, pcap, rcap, plan, groups);
+    plan_peer_block(all, AEM_EP_PAYLOAD(E, R), R, E, me, live, false, false, ucap, pcap, rcap, plan,
+                    groups);
 }
 
 // One warp copies one row of d elements (d % 8 == 0) to bf16.
@@ -624,36 +726,43 @@ __device__ __forceinline__ void copy_row_bf16(const XT* __restrict__ in, __nv_bf
     }
 }
 
-// Push: (a) each (destination, token) pair's activation row into the
-// destination's pair rows; (b) each unit's (pair row, gate weight) into the
-// destination's unit row.  Units of this rank are expert-sorted, so those of
-// expert e are the contiguous range [starts[e], starts[e+1]), landing from
-// dst_unit_off[e] on in e's owner.  Units for a rank outside the step have no
-// pair and are skipped (they fail).
+// Push one half (0 = A: tokens t < half_T, 1 = B): (a) each of its
+// (destination, token) pairs' activation row into the destination's pair
+// rows; (b) each of its units' (pair row, gate weight) into the destination's
+// unit row.  Units of this rank are expert-sorted with half A first inside
+// every expert (cnt_a[e] of them), so unit i of expert e lands at
+// dst_unit_off[half][e] + its index inside its half.  Units for a rank outside
+// the step have no pair and are skipped (they fail).
 template <typename XT>
 __global__ void __launch_bounds__(kCopyThreads)
-    ep_dispatch_kernel(const XT* __restrict__ x, int64_t T, int64_t d, int R, int el,
-                       const int32_t* __restrict__ pair_local, const int* __restrict__ starts,
+    ep_dispatch_kernel(const XT* __restrict__ x, int64_t T, int64_t half_T, int half, int64_t d,
+                       int R, int el, const int32_t* __restrict__ pair_local,
+                       const int* __restrict__ starts, const int32_t* __restrict__ cnt_a,
                        const int32_t* __restrict__ src_token, const float* __restrict__ rowscale,
                        int k, const aem_ep_peer_plan* __restrict__ plan, EpPeers peers,
                        ExchangeLayout lay, int64_t ucap, int64_t pcap, int* __restrict__ err) {
     __shared__ int bnd[AEM_MAX_EXPERTS + 1];
+    __shared__ int ca[AEM_MAX_EXPERTS];
     __shared__ int upos[AEM_MAX_EXPERTS];
     __shared__ int ppos[AEM_EP_MAX_RANKS];
     if (!plan->ok) return;
     const int E = R * el;
     for (int i = threadIdx.x; i <= E; i += blockDim.x) bnd[i] = starts[i];
-    for (int i = threadIdx.x; i < E; i += blockDim.x) upos[i] = plan->dst_unit_off[i];
+    for (int i = threadIdx.x; i < E; i += blockDim.x) {
+        ca[i] = cnt_a[i];
+        upos[i] = plan->dst_unit_off[half][i];
+    }
     for (int i = threadIdx.x; i < R; i += blockDim.x) ppos[i] = plan->dst_pair_off[i];
     __syncthreads();
     const int lane = threadIdx.x & 31;
+    const int64_t t_lo = half ? half_T : 0, t_hi = half ? T : half_T, tn = t_hi - t_lo;
     const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
-         i < R * T; i += nw) {
-        const int pl = pair_local[i];
+         i < R * tn; i += nw) {
+        const int r = static_cast<int>(i / tn);
+        const int64_t t = t_lo + (i - static_cast<int64_t>(r) * tn);
+        const int pl = pair_local[static_cast<int64_t>(r) * T + t];
         if (pl < 0) continue;
-        const int r = static_cast<int>(i / T);
-        const int64_t t = i - static_cast<int64_t>(r) * T;
         const int64_t row = static_cast<int64_t>(ppos[r]) + pl;
         if (row >= pcap) {
             if (lane == 0) atomicOr(err, ERR_EP_BOUNDS);
@@ -671,11 +780,14 @@ __global__ void __launch_bounds__(kCopyThreads)
             if (bnd[mid] <= i) lo = mid; else hi = mid - 1;
         }
         const int e = lo;
+        const int64_t q = i - bnd[e];
+        const bool in_a = q < ca[e];
+        if (in_a != (half == 0)) continue;
         const int r = e / el;
         const int64_t t = src_token[i];
         const int pl = (t >= 0 && t < T) ? pair_local[static_cast<int64_t>(r) * T + t] : -1;
         if (pl < 0) continue;  // a rank outside the step: the unit fails
-        const int64_t pos = upos[e] + (i - bnd[e]);
+        const int64_t pos = upos[e] + (in_a ? q : q - ca[e]);
         if (pos >= ucap) {
             atomicOr(err, ERR_EP_BOUNDS);
             continue;
@@ -685,20 +797,39 @@ __global__ void __launch_bounds__(kCopyThreads)
     }
 }
 
-// Destination side, after the dispatch point: unit rows from the received
-// pair rows (the grouped GEMM input), and zeroed pair sums for the down GEMM
-// to accumulate into.
+// The pair row p received by this rank belongs to half A when it is among the
+// first recv_pair_a[s] rows from its source s.  Returns s and sets *in_a.
+__device__ __forceinline__ int pair_source(int64_t p, const int* off, const int* pa, int R,
+                                           bool* in_a) {
+    int s = 0;
+    while (s + 1 < R && p >= off[s + 1]) ++s;
+    *in_a = p - off[s] < pa[s];
+    return s;
+}
+
+// Destination side, after one half's dispatch point: that half's unit rows
+// from the received pair rows (the grouped GEMM input), and its zeroed pair
+// sums for the down GEMM to accumulate into.
 __global__ void __launch_bounds__(kCopyThreads)
     ep_expand_kernel(const __nv_bfloat16* __restrict__ xpair, int32_t* __restrict__ rowmap_in,
                      float* __restrict__ rowscale_in, const aem_ep_peer_plan* __restrict__ plan,
-                     const StepState* st, int64_t d, __nv_bfloat16* __restrict__ xu,
-                     float* __restrict__ ret_acc, int* __restrict__ err) {
+                     const StepState* st, int half, int R, int64_t d,
+                     __nv_bfloat16* __restrict__ xu, float* __restrict__ ret_acc,
+                     int* __restrict__ err) {
+    __shared__ int off[AEM_EP_MAX_RANKS + 1];
+    __shared__ int pa[AEM_EP_MAX_RANKS];
     if (!plan->ok || *reinterpret_cast<const volatile int*>(&st->failed)) return;
-    const int64_t units = plan->units_in, pairs = plan->pairs_in;
+    for (int i = threadIdx.x; i <= R; i += blockDim.x) off[i] = plan->recv_pair_off[i];
+    for (int i = threadIdx.x; i < R; i += blockDim.x) pa[i] = plan->recv_pair_a[i];
+    __syncthreads();
+    const int64_t u_lo = half ? plan->units_in_a : 0;
+    const int64_t u_hi = half ? plan->units_in : plan->units_in_a;
+    const int64_t pairs = plan->pairs_in;
     const int lane = threadIdx.x & 31;
     const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-    for (int64_t u = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
-         u < units; u += nw) {
+    for (int64_t u = u_lo + blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) +
+                     (threadIdx.x >> 5);
+         u < u_hi; u += nw) {
         const int64_t p = rowmap_in[u];
         uint4* vo = reinterpret_cast<uint4*>(xu + u * d);
         if (p < 0 || p >= pairs) {  // a unit row no source wrote: contributes nothing
@@ -714,34 +845,42 @@ __global__ void __launch_bounds__(kCopyThreads)
         const uint4* vi = reinterpret_cast<const uint4*>(xpair + p * d);
         for (int64_t i = lane; i < d / 8; i += 32) vo[i] = vi[i];
     }
-    float4* z = reinterpret_cast<float4*>(ret_acc);
-    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < pairs * d / 4;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-        z[i] = zero;
+    // zero this half's pair sums: one warp per pair row
+    for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+         p < pairs; p += nw) {
+        bool in_a;
+        pair_source(p, off, pa, R, &in_a);
+        if (in_a != (half == 0)) continue;
+        float4* z = reinterpret_cast<float4*>(ret_acc + p * d);
+        for (int64_t i = lane; i < d / 4; i += 32) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 }
 
-// Return: pair sum p (from source s) into row ret_off[s] + (p - recv_pair_off[s])
-// of s's return rows; the sums of this rank's own pairs are not copied (the
-// combine reads them where the down GEMM left them).
+// Return one half: pair sum p (from source s) into row ret_off[s] +
+// (p - recv_pair_off[s]) of s's return rows; the sums of this rank's own
+// pairs are not copied (the combine reads them where the down GEMM left them).
 __global__ void __launch_bounds__(kCopyThreads)
     ep_return_kernel(const float* __restrict__ ret_acc, const aem_ep_peer_plan* __restrict__ plan,
-                     const StepState* st, int R, int me, int64_t d, EpPeers peers,
+                     const StepState* st, int half, int R, int me, int64_t d, EpPeers peers,
                      ExchangeLayout lay, int64_t rcap, int* __restrict__ err) {
     __shared__ int off[AEM_EP_MAX_RANKS + 1];
+    __shared__ int pa[AEM_EP_MAX_RANKS];
     __shared__ int ret[AEM_EP_MAX_RANKS];
     if (!plan->ok || *reinterpret_cast<const volatile int*>(&st->failed)) return;
     for (int i = threadIdx.x; i <= R; i += blockDim.x) off[i] = plan->recv_pair_off[i];
-    for (int i = threadIdx.x; i < R; i += blockDim.x) ret[i] = plan->ret_off[i];
+    for (int i = threadIdx.x; i < R; i += blockDim.x) {
+        pa[i] = plan->recv_pair_a[i];
+        ret[i] = plan->ret_off[i];
+    }
     __syncthreads();
     const int64_t pairs = off[R];
     const int lane = threadIdx.x & 31;
     const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
          p < pairs; p += nw) {
-        int s = 0;
-        while (s + 1 < R && p >= off[s + 1]) ++s;
-        if (s == me) continue;  // this rank's own pair sums stay where they are
+        bool in_a;
+        const int s = pair_source(p, off, pa, R, &in_a);
+        if (s == me || in_a != (half == 0)) continue;  // own sums stay where they are
         const int64_t row = ret[s] + (p - off[s]);
         if (row >= rcap) {
             if (lane == 0) atomicOr(err, ERR_EP_BOUNDS);
@@ -849,7 +988,7 @@ struct Ep {
     Moe loc;  // routing buffers of the single-GPU layer (sized for T_cap tokens)
     int64_t T_cap = 0;
     int64_t units_cap = 0, pairs_cap = 0, ret_cap = 0;
-    int pay_ld = 0;  // int32 words per payload row: starts [E+1], pairs [R], live mask [2]
+    int pay_ld = 0;  // int32 words per payload row, AEM_EP_PAYLOAD(E, R)
     // exchange region: this rank's own, and every rank's mapping of it
     ExchangeLayout lay{};
     void* xreg = nullptr;
@@ -861,7 +1000,7 @@ struct Ep {
     long long* corr = nullptr;          // [k][E]
     int32_t* payload = nullptr;         // [pay_ld]
     aem_ep_peer_plan* plan = nullptr;
-    int32_t* groups = nullptr;          // [E/R+1] received rows per local expert
+    int32_t* groups = nullptr;          // [2][E/R+1] received rows per local expert, per half
     int32_t* pair_local = nullptr;      // [R][T]
     StepState* st = nullptr;
     void* xu = nullptr;                 // bf16 [units_cap][d]
@@ -877,6 +1016,10 @@ struct Ep {
     uint64_t unhealthy = 0;             // ranks left out of every later step
     uint64_t timeout_ns = 2000000000ull;
     unsigned long long* h_suspect = nullptr;  // pinned copy for aem_ep_health
+    int pipeline = -1;                  // two-half pipeline: -1 automatic (off), 0 off, 1 on
+    // second stream of the two-half pipeline and its joins
+    cudaStream_t aux = nullptr;
+    cudaEvent_t ev_plan = nullptr, ev_disp_b = nullptr, ev_down_a = nullptr, ev_ret_a = nullptr;
     int64_t last_T = 0;
     PhaseProfiler prof;
 
@@ -895,7 +1038,7 @@ aem_status Ep::init(int64_t max_tokens) {
     units_cap = static_cast<int64_t>(R) * T_cap * k;  // every unit of every rank
     pairs_cap = static_cast<int64_t>(R) * T_cap;      // every token of every rank
     ret_cap = T_cap * std::min(R, k);                 // a token has <= min(R, k) destinations
-    pay_ld = (E + 1 + R + 2 + 3) & ~3;                // 16-byte rows
+    pay_ld = AEM_EP_PAYLOAD(E, R);                    // 16-byte rows
     AEM_REQUIRE(units_cap < (1ll << 31) && pairs_cap * d < (1ll << 40),
                 "aem_ep_create: max_tokens_local=%lld too large for %d ranks x top-%d",
                 (long long)max_tokens, R, k);
@@ -922,7 +1065,7 @@ aem_status Ep::init(int64_t max_tokens) {
     const size_t o_corr = slot(sizeof(long long) * k * E);
     const size_t o_pay = slot(sizeof(int32_t) * pay_ld);
     const size_t o_plan = slot(sizeof(aem_ep_peer_plan));
-    const size_t o_groups = slot(sizeof(int32_t) * (E + 1));
+    const size_t o_groups = slot(sizeof(int32_t) * 2 * (E + 1));
     const size_t o_pl = slot(sizeof(int32_t) * R * T_cap);
     const size_t o_st = slot(sizeof(StepState));
     const size_t o_ipos = slot(sizeof(int32_t) * T_cap * ksel);
@@ -952,6 +1095,9 @@ aem_status Ep::init(int64_t max_tokens) {
     AEM_TRY_CUDA(cudaMemcpy(pos_of, h_pos.data(), sizeof(int32_t) * E, cudaMemcpyHostToDevice));
     AEM_TRY_CUDA(cudaMemcpy(expert_at, at.data(), sizeof(int32_t) * E, cudaMemcpyHostToDevice));
     AEM_TRY_CUDA(cudaMallocHost(&h_suspect, sizeof(unsigned long long)));
+    AEM_TRY_CUDA(cudaStreamCreateWithFlags(&aux, cudaStreamNonBlocking));
+    for (cudaEvent_t* e : {&ev_plan, &ev_disp_b, &ev_down_a, &ev_ret_a})
+        AEM_TRY_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
     return AEM_OK;
 }
 
@@ -1099,8 +1245,14 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
     AEM_CHECK_LAUNCH();
     count_launches(2);
     prof.end(AEM_PHASE_EXCHANGE, s);
-    // 3. capacity routing with global ranks + expert-grouped permutation,
-    //    then the (destination, token) pairs
+    // 3. capacity routing with global ranks + expert-grouped permutation
+    //    (half A's units first inside every expert), then the
+    //    (destination, token) pairs
+    // two-half pipeline: off unless asked for (at 2 and 4 ranks of a
+    // 16384-token batch the halves' smaller GEMMs and the pushes' SMs beside
+    // them cost more than the hidden transfers save)
+    const bool split = pipeline > 0;
+    const int64_t half_T = split ? (T + 1) / 2 : T;
     prof.begin(AEM_PHASE_ROUTE, s);
     if (T > 0) {
         MoeRouteArgs ra;
@@ -1118,16 +1270,17 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
         ra.src_token = loc.src_token;
         ra.rowmap = loc.rowmap;
         ra.rowscale = loc.rowscale;
+        ra.half_T = half_T;
         AEM_TRY(route_moe(ra, s));
     } else {
         AEM_TRY_CUDA(cudaMemsetAsync(loc.starts, 0, sizeof(int) * (E + 1), s));
     }
-    ep_pairs_kernel<<<R, 1024, 0, s>>>(loc.eff, T, k, el, E, R, live, loc.starts, pair_local,
-                                       payload);
+    ep_pairs_kernel<<<R, 1024, 0, s>>>(loc.eff, T, half_T, k, el, E, R, live, loc.starts,
+                                       pair_local, payload);
     AEM_CHECK_LAUNCH();
     count_launches(1);
     prof.end(AEM_PHASE_ROUTE, s);
-    // 4. all-gather expert starts + pair counts; every rank plans on the device
+    // 4. all-gather every rank's payload; every rank plans on the device
     prof.begin(AEM_PHASE_EXCHANGE, s);
     ep_publish_kernel<<<1, 256, 0, s>>>(reinterpret_cast<const uint32_t*>(payload), pay_ld, pay_ld,
                                         peers, lay.mail_pay, lay.flags, SYNC_PLAN, rank, R, live, q,
@@ -1139,42 +1292,50 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
     AEM_CHECK_LAUNCH();
     count_launches(2);
     prof.end(AEM_PHASE_EXCHANGE, s);
-    // 5. dispatch: push pair rows and unit metadata into the destinations
-    prof.begin(AEM_PHASE_DISPATCH, s);
-    {
+    // 5-7. two-half pipeline: half B's dispatch (second stream) runs under
+    //    half A's GEMMs, half A's return (second stream) under half B's GEMMs
+    const int32_t* cnt_a = payload + pay_units_a(E, R);
+    auto dispatch = [&](int half, cudaStream_t st_) -> aem_status {
         const unsigned g = static_cast<unsigned>(sms * 4);
         if (xd == AEM_BF16)
-            ep_dispatch_kernel<__nv_bfloat16><<<g, kCopyThreads, 0, s>>>(
-                static_cast<const __nv_bfloat16*>(x), T, d, R, el, pair_local, loc.starts,
-                loc.src_token, loc.rowscale, k, plan, peers, lay, units_cap, pairs_cap, err);
+            ep_dispatch_kernel<__nv_bfloat16><<<g, kCopyThreads, 0, st_>>>(
+                static_cast<const __nv_bfloat16*>(x), T, half_T, half, d, R, el, pair_local,
+                loc.starts, cnt_a, loc.src_token, loc.rowscale, k, plan, peers, lay, units_cap,
+                pairs_cap, err);
         else
-            ep_dispatch_kernel<float><<<g, kCopyThreads, 0, s>>>(
-                static_cast<const float*>(x), T, d, R, el, pair_local, loc.starts, loc.src_token,
-                loc.rowscale, k, plan, peers, lay, units_cap, pairs_cap, err);
+            ep_dispatch_kernel<float><<<g, kCopyThreads, 0, st_>>>(
+                static_cast<const float*>(x), T, half_T, half, d, R, el, pair_local, loc.starts,
+                cnt_a, loc.src_token, loc.rowscale, k, plan, peers, lay, units_cap, pairs_cap,
+                err);
         AEM_CHECK_LAUNCH();
-        ep_publish_kernel<<<1, 64, 0, s>>>(nullptr, 0, 0, peers, 0, lay.flags, SYNC_DISPATCH, rank,
-                                           R, live, q, st);
+        ep_publish_kernel<<<1, 64, 0, st_>>>(nullptr, 0, 0, peers, 0, lay.flags,
+                                             half ? SYNC_DISPATCH_B : SYNC_DISPATCH_A, rank, R,
+                                             live, q, st);
         AEM_CHECK_LAUNCH();
-        ep_wait_kernel<<<1, 64, 0, s>>>(flags + SYNC_DISPATCH * R, R, rank, live, q, timeout_ns,
-                                        tol, st, err);
+        count_launches(2);
+        return AEM_OK;
+    };
+    auto receive = [&](int half) -> aem_status {
+        ep_wait_kernel<<<1, 64, 0, s>>>(flags + (half ? SYNC_DISPATCH_B : SYNC_DISPATCH_A) * R, R,
+                                        rank, live, q, timeout_ns, tol, st, err);
         AEM_CHECK_LAUNCH();
         ep_expand_kernel<<<static_cast<unsigned>(sms * 4), kCopyThreads, 0, s>>>(
             reinterpret_cast<const __nv_bfloat16*>(mine + lay.xpair),
             reinterpret_cast<int32_t*>(mine + lay.rowmap),
-            reinterpret_cast<float*>(mine + lay.rowscale), plan, st, d,
+            reinterpret_cast<float*>(mine + lay.rowscale), plan, st, half, R, d,
             static_cast<__nv_bfloat16*>(xu), ret_acc, err);
         AEM_CHECK_LAUNCH();
-        count_launches(4);
-    }
-    prof.end(AEM_PHASE_DISPATCH, s);
-    // 6. local expert FFN, one row group per local expert; the down GEMM
-    //    scales by the gate weight and sums the units of each pair
-    {
-        const int64_t hint = std::max<int64_t>(U, 1);  // expected received units
+        count_launches(2);
+        return AEM_OK;
+    };
+    // local expert FFN of one half, one row group per local expert; the down
+    // GEMM scales by the gate weight and sums the units of each pair
+    auto ffn = [&](int half) -> aem_status {
+        const int64_t hint = std::max<int64_t>(U / 2, 1);  // expected received units
         GemmArgs up_a;
         up_a.w = up;
         up_a.G = el;
-        up_a.group_rows = groups;
+        up_a.group_rows = groups + half * (el + 1);
         up_a.M = units_cap;
         up_a.max_rows = units_cap;
         up_a.rows_hint = hint;
@@ -1189,7 +1350,7 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
         GemmArgs dn;
         dn.w = down;
         dn.G = el;
-        dn.group_rows = groups;
+        dn.group_rows = groups + half * (el + 1);
         dn.M = units_cap;
         dn.max_rows = units_cap;
         dn.rows_hint = hint;
@@ -1202,19 +1363,58 @@ aem_status Ep::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dt
         prof.begin(AEM_PHASE_DOWN, s);
         AEM_TRY(launch_qgemm(dn, s));
         prof.end(AEM_PHASE_DOWN, s);
+        return AEM_OK;
+    };
+    auto give_back = [&](int half, cudaStream_t st_) -> aem_status {
+        const unsigned g = static_cast<unsigned>(sms * 4);
+        ep_return_kernel<<<g, kCopyThreads, 0, st_>>>(
+            ret_acc, plan, st, half, R, rank, d, peers, lay, ret_cap, err);
+        AEM_CHECK_LAUNCH();
+        ep_publish_kernel<<<1, 64, 0, st_>>>(nullptr, 0, 0, peers, 0, lay.flags,
+                                             half ? SYNC_RETURN_B : SYNC_RETURN_A, rank, R, live,
+                                             q, st);
+        AEM_CHECK_LAUNCH();
+        count_launches(2);
+        return AEM_OK;
+    };
+    prof.begin(AEM_PHASE_DISPATCH, s);
+    AEM_TRY(dispatch(0, s));
+    if (split) {
+        // half B's pushes start once half A's are out, under half A's receive and GEMMs
+        AEM_TRY_CUDA(cudaEventRecord(ev_plan, s));
+        AEM_TRY_CUDA(cudaStreamWaitEvent(aux, ev_plan, 0));
+        AEM_TRY(dispatch(1, aux));
+        AEM_TRY_CUDA(cudaEventRecord(ev_disp_b, aux));
     }
-    // 7. pair sums back into the sources
+    AEM_TRY(receive(0));
+    prof.end(AEM_PHASE_DISPATCH, s);
+    AEM_TRY(ffn(0));
+    if (split) {
+        AEM_TRY_CUDA(cudaEventRecord(ev_down_a, s));
+        AEM_TRY_CUDA(cudaStreamWaitEvent(aux, ev_down_a, 0));
+        AEM_TRY(give_back(0, aux));  // half A's sums go back under half B's GEMMs
+        AEM_TRY_CUDA(cudaEventRecord(ev_ret_a, aux));
+        prof.begin(AEM_PHASE_DISPATCH, s);
+        AEM_TRY_CUDA(cudaStreamWaitEvent(s, ev_disp_b, 0));  // this rank's own half-B pushes
+        AEM_TRY(receive(1));
+        prof.end(AEM_PHASE_DISPATCH, s);
+        AEM_TRY(ffn(1));
+    }
     prof.begin(AEM_PHASE_RETURN, s);
-    ep_return_kernel<<<static_cast<unsigned>(sms * 4), kCopyThreads, 0, s>>>(
-        ret_acc, plan, st, R, rank, d, peers, lay, ret_cap, err);
+    if (split) {
+        AEM_TRY(give_back(1, s));
+        AEM_TRY_CUDA(cudaStreamWaitEvent(s, ev_ret_a, 0));  // joins the second stream
+        ep_wait_kernel<<<1, 64, 0, s>>>(flags + SYNC_RETURN_B * R, R, rank, live, q, timeout_ns,
+                                        tol, st, err);
+        AEM_CHECK_LAUNCH();
+        count_launches(1);
+    } else {
+        AEM_TRY(give_back(0, s));
+    }
+    ep_wait_kernel<<<1, 64, 0, s>>>(flags + SYNC_RETURN_A * R, R, rank, live, q, timeout_ns, tol,
+                                    st, err);
     AEM_CHECK_LAUNCH();
-    ep_publish_kernel<<<1, 64, 0, s>>>(nullptr, 0, 0, peers, 0, lay.flags, SYNC_RETURN, rank, R,
-                                       live, q, st);
-    AEM_CHECK_LAUNCH();
-    ep_wait_kernel<<<1, 64, 0, s>>>(flags + SYNC_RETURN * R, R, rank, live, q, timeout_ns, tol, st,
-                                    err);
-    AEM_CHECK_LAUNCH();
-    count_launches(3);
+    count_launches(1);
     prof.end(AEM_PHASE_RETURN, s);
     // 8. per-token sum over destination ranks, failed flags
     prof.begin(AEM_PHASE_COMBINE, s);
@@ -1296,7 +1496,8 @@ aem_status aem_ep_plan_peer(const int32_t* all, int R, int E, int rank, uint64_t
     AEM_REQUIRE(all && plan && groups, "aem_ep_plan_peer: NULL buffer");
     AEM_REQUIRE(R >= 1 && R <= AEM_EP_MAX_RANKS && E >= R && E % R == 0 && rank >= 0 && rank < R,
                 "aem_ep_plan_peer: bad R=%d E=%d rank=%d", R, E, rank);
-    aem::plan_peer(all, E + 1 + R, R, E, rank, live, units_cap, pairs_cap, ret_cap, plan, groups);
+    aem::plan_peer(all, AEM_EP_PAYLOAD(E, R), R, E, rank, live, units_cap, pairs_cap, ret_cap, plan,
+                   groups);
     return AEM_OK;
 }
 
@@ -1307,7 +1508,7 @@ aem_status aem_ep_plan_peer_device(const int32_t* all, int R, int E, int rank, u
     AEM_REQUIRE(R >= 1 && R <= AEM_EP_MAX_RANKS && E >= R && E % R == 0 && E <= AEM_MAX_EXPERTS &&
                     rank >= 0 && rank < R,
                 "aem_ep_plan_peer_device: bad R=%d E=%d rank=%d", R, E, rank);
-    const size_t smem = aem::plan_block_smem(R, E, E + 1 + R);
+    const size_t smem = aem::plan_block_smem(R, E, AEM_EP_PAYLOAD(E, R));
     if (smem > 48 * 1024)
         AEM_TRY_CUDA(cudaFuncSetAttribute(aem::ep_plan_test_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1341,6 +1542,9 @@ static void ep_destroy(aem::Ep* ep, bool abort_comm) {
     cudaFree(ep->lbuf);
     cudaFree(ep->loc.buf);
     cudaFreeHost(ep->h_suspect);
+    if (ep->aux) cudaStreamDestroy(ep->aux);
+    for (cudaEvent_t e : {ep->ev_plan, ep->ev_disp_b, ep->ev_down_a, ep->ev_ret_a})
+        if (e) cudaEventDestroy(e);
     delete ep;
 }
 
@@ -1503,6 +1707,13 @@ aem_status aem_ep_health(aem_ep_t h, uint64_t* unhealthy, void* stream) {
     AEM_TRY_CUDA(cudaStreamSynchronize(s));
     ep->unhealthy |= *ep->h_suspect & ~(1ull << ep->rank);
     *unhealthy = ep->unhealthy;
+    return AEM_OK;
+}
+
+aem_status aem_ep_set_pipeline(aem_ep_t h, int mode) {
+    AEM_REQUIRE(h != nullptr, "aem_ep_set_pipeline: NULL layer");
+    AEM_REQUIRE(mode >= -1 && mode <= 1, "aem_ep_set_pipeline: mode %d not in {-1, 0, 1}", mode);
+    reinterpret_cast<aem::Ep*>(h)->pipeline = mode;
     return AEM_OK;
 }
 

@@ -97,9 +97,22 @@ __global__ void gather_by_position_kernel(const uint32_t* __restrict__ primary,
 }
 
 // Histogram of keys per chunk: cnt[c][e].
+// Enumeration of the n = k*T units for grouping: identity when half_T == 0;
+// otherwise every unit of the first half_T tokens (slot-major among them)
+// comes first, then those of the other tokens, so each expert's group lists
+// the first half's units first.  Units are u = j*T + t.
+__device__ __forceinline__ int64_t unit_at(int64_t p, int64_t T, int64_t half_T, int k) {
+    if (half_T <= 0 || half_T >= T) return p;
+    const int64_t n_a = static_cast<int64_t>(k) * half_T;
+    if (p < n_a) return (p / half_T) * T + p % half_T;
+    const int64_t q = p - n_a, tb = T - half_T;
+    return (q / tb) * T + half_T + q % tb;
+}
+
 template <int PT>
 __global__ void __launch_bounds__(kThreads)
-    chunk_count_kernel(const uint32_t* __restrict__ key, int64_t n, int E, int* __restrict__ cnt) {
+    chunk_count_kernel(const uint32_t* __restrict__ key, int64_t n, int E, int* __restrict__ cnt,
+                       int64_t T = 0, int64_t half_T = 0, int k = 1) {
     constexpr int CH = kThreads * PT;
     __shared__ int h[AEM_MAX_EXPERTS];
     for (int e = threadIdx.x; e < E; e += kThreads) h[e] = 0;
@@ -108,7 +121,7 @@ __global__ void __launch_bounds__(kThreads)
     for (int i = threadIdx.x; i < CH; i += kThreads) {
         const int64_t p = base + i;
         if (p < n) {
-            const uint32_t e = key[p];
+            const uint32_t e = key[unit_at(p, T, half_T, k)];
             if (e < static_cast<uint32_t>(E)) atomicAdd(&h[e], 1);
         }
     }
@@ -153,7 +166,8 @@ __global__ void __launch_bounds__(kScanThreads)
 
 template <int PT, typename Emit>
 __device__ __forceinline__ void chunk_ranks(const uint32_t* __restrict__ key, int64_t n, int E,
-                                            const int* __restrict__ off, Emit emit) {
+                                            const int* __restrict__ off, Emit emit,
+                                            int64_t T = 0, int64_t half_T = 0, int k = 1) {
     constexpr int CH = kThreads * PT;
     __shared__ int run[AEM_MAX_EXPERTS];
     __shared__ int hw[kWarps][AEM_MAX_EXPERTS];
@@ -166,7 +180,8 @@ __device__ __forceinline__ void chunk_ranks(const uint32_t* __restrict__ key, in
         __syncthreads();
         const int64_t p = base + static_cast<int64_t>(r) * kThreads + tid;
         const bool valid = p < n;
-        uint32_t e = valid ? key[p] : 0xFFFFFFFFu;
+        const int64_t u = valid ? unit_at(p, T, half_T, k) : 0;
+        uint32_t e = valid ? key[u] : 0xFFFFFFFFu;
         if (e >= static_cast<uint32_t>(E)) e = 0xFFFFFFFFu;
         const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
         const int in_warp = __popc(peers & lt);
@@ -182,7 +197,7 @@ __device__ __forceinline__ void chunk_ranks(const uint32_t* __restrict__ key, in
             run[x] = acc;
         }
         __syncthreads();
-        if (e != 0xFFFFFFFFu) emit(p, e, hw[warp][e] + in_warp);
+        if (e != 0xFFFFFFFFu) emit(u, e, hw[warp][e] + in_warp);
         __syncthreads();
     }
 }
@@ -213,7 +228,7 @@ __global__ void __launch_bounds__(kThreads)
                    const int* __restrict__ starts, int64_t T, int k,
                    const float* __restrict__ val, int32_t* __restrict__ src_token,
                    int32_t* __restrict__ rowmap, float* __restrict__ rowscale,
-                   int32_t* __restrict__ dest_of) {
+                   int32_t* __restrict__ dest_of, int64_t half_T) {
     chunk_ranks<PT>(eff, n, E, off, [&](int64_t u, uint32_t e, int rank) {
         const int64_t dest = starts[e] + rank;
         const int64_t j = u / T, t = u % T;
@@ -221,7 +236,7 @@ __global__ void __launch_bounds__(kThreads)
         rowmap[dest] = static_cast<int32_t>(t * k + j);
         rowscale[dest] = val[t * k + j];
         if (dest_of) dest_of[u] = static_cast<int32_t>(dest);
-    });
+    }, T, half_T, k);
 }
 
 }  // namespace
@@ -269,13 +284,14 @@ aem_status route_moe(const MoeRouteArgs& a, cudaStream_t s) {
     assign_kernel<kPerThreadMoe><<<static_cast<unsigned>(c), kThreads, 0, s>>>(
         prim, sec, n, a.E, cnt1, a.capacity, a.corr, a.T, nullptr, eff);
     AEM_CHECK_LAUNCH();
-    chunk_count_kernel<kPerThreadMoe><<<static_cast<unsigned>(c), kThreads, 0, s>>>(eff, n, a.E,
-                                                                                 cnt2);
+    chunk_count_kernel<kPerThreadMoe><<<static_cast<unsigned>(c), kThreads, 0, s>>>(
+        eff, n, a.E, cnt2, a.T, a.half_T, a.k);
     AEM_CHECK_LAUNCH();
     chunk_scan_kernel<<<1, kScanThreads, 0, s>>>(cnt2, static_cast<int>(c), a.E, starts);
     AEM_CHECK_LAUNCH();
     scatter_kernel<kPerThreadMoe><<<static_cast<unsigned>(c), kThreads, 0, s>>>(
-        eff, n, a.E, cnt2, starts, a.T, a.k, a.val, a.src_token, a.rowmap, a.rowscale, a.dest_of);
+        eff, n, a.E, cnt2, starts, a.T, a.k, a.val, a.src_token, a.rowmap, a.rowscale, a.dest_of,
+        a.half_T);
     AEM_CHECK_LAUNCH();
     count_launches(7);
     return AEM_OK;

@@ -27,6 +27,9 @@ struct MoeRouteArgs {
     int32_t* rowmap = nullptr;      // [T*k] grouped row -> t*k + j
     float* rowscale = nullptr;      // [T*k] grouped row -> gate weight
     int32_t* dest_of = nullptr;     // [T*k] unit -> grouped row (nullable)
+    // > 0: inside every expert's group, the units of tokens [0, half_T) come
+    // first (each part in unit order); the capacity rule is unchanged
+    int64_t half_T = 0;
 };
 
 int64_t route_chunks(int64_t n);

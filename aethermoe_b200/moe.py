@@ -189,28 +189,57 @@ def ep_plan_exchange(starts, rank):
     return so, sc, ro, rc, groups
 
 
+def ep_payload(eff, T, E, R, live=None):
+    """One rank's exchange payload from its routing (``eff`` slot-major
+    ``[k*T]`` expert positions, experts in contiguous blocks of E/R per rank):
+    expert starts, pair counts per destination, live mask, half-A units per
+    expert, half-A pairs per destination (half A = the first ceil(T/2))."""
+    eff = np.asarray(eff).reshape(-1, T)
+    el, half = E // R, (T + 1) // 2
+    if live is None:
+        live = (1 << R) - 1
+    row = np.zeros(_lib.ep_payload_words(E, R), np.int32)
+    row[1:E + 1] = np.cumsum(np.bincount(eff.reshape(-1), minlength=E))
+    dest = eff // el
+    for r in range(R):
+        if (live >> r) & 1:
+            on = (dest == r).any(axis=0)
+            row[E + 1 + r] = on.sum()
+            row[2 * E + 3 + R + r] = on[:half].sum()
+    row[E + 1 + R:E + 3 + R] = np.array([live & 0xFFFFFFFF, (live >> 32) & 0xFFFFFFFF],
+                                        np.uint32).view(np.int32)
+    row[E + 3 + R:2 * E + 3 + R] = np.bincount(eff[:, :half].reshape(-1), minlength=E)
+    return row
+
+
 def ep_plan_peer(payload, rank, units_cap, pairs_cap, ret_cap, live=None):
-    """Host form of the per-step peer-exchange plan: ``payload [R, E+1+R]``
-    (every rank's expert starts, then its pair counts per destination) ->
-    ``(plan dict, groups [E/R+1])`` for ``rank`` (received rows per local
-    expert); ``live`` is the bit mask of the ranks taking part (default: all)."""
+    """Host form of the per-step peer-exchange plan: ``payload [R, W]``
+    (every rank's ``ep_payload``) -> ``(plan dict, groups [2, E/R+1])`` for
+    ``rank`` (received rows per local expert, per half); ``live`` is the bit
+    mask of the ranks taking part (default: all)."""
     pay = np.ascontiguousarray(payload, dtype=np.int32)
-    r, w = pay.shape
-    e = w - 1 - r
+    r = pay.shape[0]
+    e = None
+    for cand in range(1, 257):  # E from the row width
+        if _lib.ep_payload_words(cand, r) == pay.shape[1] and cand % r == 0:
+            e = cand
+    if e is None:
+        raise ValueError(f"payload width {pay.shape[1]} fits no expert count for {r} ranks")
     if live is None:
         live = (1 << r) - 1
     plan = _lib.EpPeerPlan()
-    groups = np.zeros(e + 1, np.int32)
+    groups = np.zeros(2 * (e + 1), np.int32)
     _lib.check(_lib.lib().aem_ep_plan_peer(pay.ctypes.data, r, e, rank, int(live), units_cap,
                                            pairs_cap, ret_cap, ctypes.byref(plan),
                                            groups.ctypes.data), "aem_ep_plan_peer")
-    out = dict(ok=plan.ok, units_in=plan.units_in, pairs_in=plan.pairs_in,
-               pairs_out=plan.pairs_out)
-    for name in ("dst_pair_off", "send_pair_off", "ret_off"):
+    el = e // r
+    out = dict(ok=plan.ok, units_in=plan.units_in, units_in_a=plan.units_in_a,
+               pairs_in=plan.pairs_in, pairs_out=plan.pairs_out)
+    for name in ("dst_pair_off", "send_pair_off", "send_pair_a", "recv_pair_a", "ret_off"):
         out[name] = np.array(getattr(plan, name)[:r], np.int64)
-    out["dst_unit_off"] = np.array(plan.dst_unit_off[:e], np.int64)  # per expert position
+    out["dst_unit_off"] = np.array([list(plan.dst_unit_off[h])[:e] for h in range(2)], np.int64)
     out["recv_pair_off"] = np.array(plan.recv_pair_off[:r + 1], np.int64)
-    return out, groups[:e // r + 1]
+    return out, groups[:2 * (el + 1)].reshape(2, el + 1)
 
 
 class EPLayer:
@@ -287,6 +316,10 @@ class EPLayer:
         _lib.check(_lib.lib().aem_ep_health(self.handle, ctypes.byref(m), _stream_ptr(stream)),
                    "aem_ep_health")
         return {r for r in range(64) if (m.value >> r) & 1}
+
+    def set_pipeline(self, mode):
+        """Two-half pipeline: -1 automatic (off), 0 off, 1 on (collective)."""
+        _lib.check(_lib.lib().aem_ep_set_pipeline(self.handle, int(mode)), "aem_ep_set_pipeline")
 
     def set_timeout(self, seconds):
         _lib.check(_lib.lib().aem_ep_set_timeout(self.handle, float(seconds)), "aem_ep_set_timeout")

@@ -345,6 +345,8 @@ def run_ours(args):
         layer = EPLayer(bytes(uid.cpu().numpy()), rank, world, gw, gb, up, None, down, None,
                         K_TOP, capacity=cap, device=local, max_tokens=tl,
                         expert_to_rank=[e % world for e in range(E)])
+        if args.ep_pipeline != "auto":
+            layer.set_pipeline(1 if args.ep_pipeline == "on" else 0)
     xs = token_buffers(dev, tokens, rank, world)
     outs = [torch.empty((tl, D_MODEL), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     stream = torch.cuda.current_stream()
@@ -419,6 +421,7 @@ def run_ours(args):
             "config": {"workload": workload_name(tokens), "tokens_per_step": tokens,
                        "global_batch": tokens, "parallelism": f"ep{world}",
                        "expert_placement": "round-robin (expert e on rank e % R)",
+                       "ep_pipeline": (args.ep_pipeline if world > 1 else None),
                        "l2": (f"inputs rotate over {N_INPUT_BUFFERS} buffers "
                               f"({N_INPUT_BUFFERS * tokens * D_MODEL * 2 >> 20} MiB > 126 MiB L2); "
                               "per-step working set > 1 GiB")},
@@ -527,6 +530,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-sample-tokens", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep-pipeline", choices=["auto", "on", "off"], default="auto",
+                    help="expert-parallel two-half pipeline (auto: off)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

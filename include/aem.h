@@ -297,31 +297,42 @@ aem_status aem_ep_plan_exchange(const int32_t* starts, int R, int E, int rank, i
 /* Where one rank's rows go in the peer-memory exchange of one step.  Units
  * are (token, slot) rows; pairs are (token, destination rank) rows -- a
  * token's activation crosses NVLink once per destination rank, and the
- * destination returns one pre-reduced float32 row per pair. */
+ * destination returns one pre-reduced float32 row per pair.  Every rank's
+ * tokens are split in two halves (A = the first ceil(T/2), B = the rest) that
+ * travel and compute as a two-stage pipeline: a destination holds its half-A
+ * units first, then its half-B units, each expert-major with sources in rank
+ * order inside; a source's pairs for one destination list half-A tokens
+ * first. */
 typedef struct aem_ep_peer_plan {
     int32_t ok;         /* 1 when every rank's segments fit the receive capacities */
-    int32_t units_in;   /* units this rank receives (rows of its grouped GEMMs) */
+    int32_t units_in;   /* units this rank receives, both halves */
+    int32_t units_in_a; /* of which half A (rows [0, units_in_a)) */
     int32_t pairs_in;   /* pairs this rank receives */
     int32_t pairs_out;  /* pairs this rank sends (rows of its return buffer) */
-    int32_t dst_unit_off[AEM_MAX_EXPERTS];       /* this rank's first unit row of expert e (by
-                                                    placement position) in its owner's buffer */
+    int32_t dst_unit_off[2][AEM_MAX_EXPERTS]; /* [half][expert position]: this rank's first
+                                                 unit row of that expert in its owner's buffer */
     int32_t dst_pair_off[AEM_EP_MAX_RANKS];      /* this rank's first pair row in rank r's buffer */
     int32_t send_pair_off[AEM_EP_MAX_RANKS];     /* this rank's pairs for rank r start here */
+    int32_t send_pair_a[AEM_EP_MAX_RANKS];       /* ... of which the first send_pair_a are half A */
     int32_t recv_pair_off[AEM_EP_MAX_RANKS + 1]; /* pairs received from source s start here */
+    int32_t recv_pair_a[AEM_EP_MAX_RANKS];       /* ... of which the first recv_pair_a are half A */
     int32_t ret_off[AEM_EP_MAX_RANKS];           /* row in s's return buffer of s's first pair here */
 } aem_ep_peer_plan;
 
 /* Host form of the per-step plan the expert-parallel layer computes on the
- * device (no GPU needed).  all: [R][E+1+R] int32, every rank's expert
- * starts [E+1] followed by its pair counts per destination rank [R].
- * live: bit r set when rank r takes part in the step; the rows of other
- * ranks are ignored, and so are units for them (those units fail).
- * Capacities: units_cap (received units), pairs_cap (received pairs),
- * ret_cap (return rows), the same on every rank.  Writes the plan of `rank`
- * and groups [E/R+1]: the row offsets of the received units of each local
- * expert (all sources' units of one expert are contiguous, sources in rank
- * order inside).  A plan whose counts do not fit
- * has ok = 0 (every rank derives the same verdict from the same data). */
+ * device (no GPU needed).  all: [R][AEM_EP_PAYLOAD(E, R)] int32, every rank's
+ * payload: expert starts [E+1] (units grouped by expert position, half A
+ * first inside each expert), pair counts per destination [R], its live mask
+ * [2] (not read here), half-A units per expert [E], half-A pairs per
+ * destination [R].  live: bit r set when rank r takes part in the step; the
+ * rows of other ranks are ignored, and so are units for them (those units
+ * fail).  Capacities: units_cap (received units), pairs_cap (received
+ * pairs), ret_cap (return rows), the same on every rank.  Writes the plan of
+ * `rank` and groups [2][E/R+1]: for each half, the row offsets of the received
+ * units of each local expert (half B's offsets continue after half A's).  A
+ * plan whose counts do not fit or do not add up has ok = 0 (every rank
+ * derives the same verdict from the same data). */
+#define AEM_EP_PAYLOAD(E, R) ((((E) * 2 + 3 + (R) * 2) + 3) & ~3)
 aem_status aem_ep_plan_peer(const int32_t* all, int R, int E, int rank, uint64_t live,
                             int64_t units_cap, int64_t pairs_cap, int64_t ret_cap,
                             aem_ep_peer_plan* plan, int32_t* groups);
@@ -386,6 +397,11 @@ aem_status aem_ep_mark_unhealthy(aem_ep_t ep, int rank);
  * unhealthy set and writes that set (bit r = rank r) to *unhealthy.
  * Router::is_shard_unhealthy / unhealthy_shard_count (router.hpp:236-240). */
 aem_status aem_ep_health(aem_ep_t ep, uint64_t* unhealthy, void* stream);
+/* Two-half pipeline of a step (half B's dispatch under half A's GEMMs, half
+ * A's return under half B's): mode -1 = automatic (currently off: measured
+ * slower at 2 and 4 ranks), 0 = off, 1 = on.  Collective: every rank must use
+ * the same mode. */
+aem_status aem_ep_set_pipeline(aem_ep_t ep, int mode);
 /* Deadline of every in-step wait on a peer (default 2 s). */
 aem_status aem_ep_set_timeout(aem_ep_t ep, double seconds);
 /* Per-phase profiling of this rank's steps (see aem_moe_profile). */

@@ -35,7 +35,7 @@ def _inputs():
 def _rank(rank, world, port, outdir):
     import torch
     import torch.distributed as dist
-    from aethermoe_b200.moe import ep_plan_bases, ep_plan_exchange, ep_plan_peer
+    from aethermoe_b200.moe import ep_plan_bases, ep_plan_exchange, ep_plan_peer, ep_payload
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                             world_size=world)
     idx = _inputs()
@@ -59,18 +59,15 @@ def _rank(rank, world, port, outdir):
     alls = [torch.zeros(E + 1, dtype=torch.int32) for _ in range(world)]
     dist.all_gather(alls, torch.from_numpy(starts))
     plan = ep_plan_exchange(torch.stack(alls).numpy(), rank)
-    # peer-memory exchange plan: starts + pair counts per destination rank
-    el = E // world
-    dest = (eff.reshape(K_TOP, tl) // el)  # destination rank of every unit
-    pcnt = np.array([(dest == r).any(axis=0).sum() for r in range(world)], np.int32)
-    payload = torch.from_numpy(np.concatenate([starts, pcnt]).astype(np.int32))
+    # peer-memory exchange plan: starts, pair counts, half-A counts per rank
+    payload = torch.from_numpy(ep_payload(eff, tl, E, world))
     allp = [torch.zeros_like(payload) for _ in range(world)]
     dist.all_gather(allp, payload)
     caps = (world * tl * K_TOP, world * tl, tl * min(world, K_TOP))
     pp, pg = ep_plan_peer(torch.stack(allp).numpy(), rank, *caps)  # every rank live
     np.savez(os.path.join(outdir, f"r{rank}.npz"), eff=eff, starts=starts,
              so=plan[0], sc=plan[1], ro=plan[2], rc=plan[3], groups=plan[4], pgroups=pg,
-             **{"p_" + key: np.asarray(v) for key, v in pp.items()})
+             payload=payload.numpy(), **{"p_" + key: np.asarray(v) for key, v in pp.items()})
     dist.barrier()
     dist.destroy_process_group()
 
@@ -104,57 +101,93 @@ def test_distributed_routing_and_exchange_plan(world):
         assert np.all(np.diff(res[r]["groups"]) >= 0)
 
 
-def _replay_peer_exchange(res, world, tl):
-    """Simulates the pushes of one step from the saved per-rank plans."""
+def _half_major_order(eff, tl):
+    """The source's expert-sorted units, half A (tokens < ceil(tl/2)) first
+    inside every expert, each part in unit order u = j*tl + t."""
+    half = (tl + 1) // 2
+    u = np.arange(len(eff))
+    return np.lexsort((u, (u % tl) >= half, eff))
+
+
+def _replay(res, world, tl, live):
+    """Simulates the pushes of one step from the saved per-rank plans: every
+    pair and unit lands on a distinct row of the destination's received range
+    for its half, every unit row lies in its half's row group of its expert and
+    points at its token's pair, and every returned pair sum lands on the row
+    the source's combine reads for that (token, destination)."""
     el = E // world
-    plans = [{k[2:]: r[k] for k in r if k.startswith("p_")} for r in res]
-    assert all(int(p["ok"]) == 1 for p in plans)
-    # destination-side arrays, filled by the sources' pushes
-    xpair = [dict() for _ in range(world)]  # row -> (source, token)
-    units = [dict() for _ in range(world)]  # row -> (source, unit, pair row)
-    for s_ in range(world):
+    half_t = (tl + 1) // 2
+    ranks = [r for r in range(world) if (live >> r) & 1]
+    xpair = {r: {} for r in ranks}  # row -> (source, token)
+    units = {r: {} for r in ranks}  # row -> (source, unit)
+    failed = 0
+    for s_ in ranks:
+        p = res[s_]["plan"]
         eff = res[s_]["eff"]
-        order = np.argsort(eff, kind="stable")  # expert-grouped units, position order inside
-        starts = res[s_]["starts"]
+        order = _half_major_order(eff, tl)
+        starts = np.zeros(E + 1, np.int64)
+        starts[1:] = np.cumsum(np.bincount(eff, minlength=E))
         dest = eff.reshape(K_TOP, tl) // el
         pl = np.full((world, tl), -1)
         for r in range(world):
+            if not (live >> r) & 1:
+                failed += int((dest == r).sum())
+                continue
             has = (dest == r).any(axis=0)
             pl[r, has] = np.arange(has.sum())
+            assert has[:half_t].sum() == p["send_pair_a"][r]
             for t in np.nonzero(has)[0]:
-                row = int(plans[s_]["dst_pair_off"][r]) + pl[r, t]
+                row = int(p["dst_pair_off"][r]) + pl[r, t]
                 assert row not in xpair[r]
                 xpair[r][row] = (s_, t)
             for e in range(r * el, (r + 1) * el):
-                for i in range(starts[e], starts[e + 1]):
-                    u = order[i]
-                    pos = int(plans[s_]["dst_unit_off"][e]) + (i - starts[e])
-                    assert pos not in units[r]
-                    units[r][pos] = (s_, u, int(plans[s_]["dst_pair_off"][r]) + pl[r, u % tl])
+                seg = order[starts[e]:starts[e + 1]]
+                in_a = (seg % tl) < half_t
+                for h, part in ((0, seg[in_a]), (1, seg[~in_a])):
+                    for q, u in enumerate(part):
+                        pos = int(p["dst_unit_off"][h][e]) + q
+                        assert pos not in units[r]
+                        units[r][pos] = (s_, u, h)
         res[s_]["_pl"] = pl
-    ret = [dict() for _ in range(world)]  # source-side return rows
-    for r in range(world):
-        p = plans[r]
+    ret = {r: {} for r in ranks}
+    for r in ranks:
+        p = res[r]["plan"]
+        g = res[r]["groups"]
+        na = int(p["units_in_a"])
         assert sorted(xpair[r]) == list(range(int(p["pairs_in"])))
         assert sorted(units[r]) == list(range(int(p["units_in"])))
-        g = res[r]["pgroups"]
-        for pos, (s_, u, prow) in units[r].items():
+        assert g[0][0] == 0 and g[0][-1] == na == g[1][0] and g[1][-1] == p["units_in"]
+        for pos, (s_, u, h) in units[r].items():
             e = int(res[s_]["eff"][u])
-            grp = np.searchsorted(g, pos, side="right") - 1
-            assert grp == e - r * el                        # the local expert's row group
-            assert xpair[r][prow] == (s_, u % tl)           # the unit's token
-        roff = p["recv_pair_off"]
+            assert (pos < na) == (h == 0)
+            grp = np.searchsorted(g[h], pos, side="right") - 1
+            assert grp == e - r * el                      # the local expert's row group
+            prow = int(res[s_]["plan"]["dst_pair_off"][r]) + res[s_]["_pl"][r, u % tl]
+            assert xpair[r][prow] == (s_, u % tl)         # the unit's token
+        roff, pa = p["recv_pair_off"], p["recv_pair_a"]
         for prow, (s_, t) in xpair[r].items():
             assert roff[s_] <= prow < roff[s_ + 1]
+            assert (prow - roff[s_] < pa[s_]) == (t < half_t)  # the pair's half
             row = int(p["ret_off"][s_]) + prow - int(roff[s_])
             assert row not in ret[s_]
             ret[s_][row] = (r, t)
-    for s_ in range(world):
-        p = plans[s_]
+    for s_ in ranks:
+        p = res[s_]["plan"]
         assert sorted(ret[s_]) == list(range(int(p["pairs_out"])))
-        pl = res[s_]["_pl"]
         for row, (r, t) in ret[s_].items():  # the combine reads send_pair_off[r] + pl[r][t]
-            assert int(p["send_pair_off"][r]) + pl[r, t] == row
+            assert int(p["send_pair_off"][r]) + res[s_]["_pl"][r, t] == row
+    return failed
+
+
+def _replay_peer_exchange(res, world, tl):
+    from aethermoe_b200.moe import ep_plan_peer
+    pay = np.stack([r["payload"] for r in res])
+    caps = (world * tl * K_TOP, world * tl, tl * min(world, K_TOP))
+    for rank, r in enumerate(res):
+        plan, groups = ep_plan_peer(pay, rank, *caps)
+        assert plan["ok"] == 1
+        r["plan"], r["groups"] = plan, groups
+    _replay(dict(enumerate(res)), world, tl, (1 << world) - 1)
 
 
 @pytest.mark.parametrize("world", [2, 4])
@@ -190,72 +223,44 @@ def test_peer_exchange_plan_with_a_rank_left_out():
     capacity rule runs over the live ranks' tokens only, units whose expert
     lives on the dead rank fail, and the live ranks' pushes still tile every
     receive range exactly (host replay of the plans for live mask 0b1011)."""
-    from aethermoe_b200.moe import ep_plan_peer
+    from aethermoe_b200.moe import ep_plan_peer, ep_payload
     world, dead = 4, 2
-    live = [r for r in range(world) if r != dead]
-    mask = sum(1 << r for r in live)
+    live_ranks = [r for r in range(world) if r != dead]
+    mask = sum(1 << r for r in live_ranks)
     idx = _inputs()
     tl = T // world
-    el = E // world
     cap = O.default_capacity(T, K_TOP, E)
     # the distributed rule with the dead rank's counts absent == the rule on the live tokens
-    sub = np.concatenate([idx[r * tl:(r + 1) * tl] for r in live])
-    eff_all = O.moe_route(sub, K_TOP, E, cap).reshape(K_TOP, len(live) * tl)
+    sub = np.concatenate([idx[r * tl:(r + 1) * tl] for r in live_ranks])
+    eff_all = O.moe_route(sub, K_TOP, E, cap).reshape(K_TOP, len(live_ranks) * tl)
     res = {}
-    payload = np.zeros((world, E + 1 + world), np.int32)
-    for i, r in enumerate(live):
+    payload = np.full((world, ep_payload(np.zeros(K_TOP * tl, np.int64), tl, E, world).size),
+                      12345, np.int32)  # whatever a dead rank left behind is ignored
+    for i, r in enumerate(live_ranks):
         eff = eff_all[:, i * tl:(i + 1) * tl].reshape(-1)
-        starts = np.zeros(E + 1, np.int32)
-        starts[1:] = np.cumsum(np.bincount(eff, minlength=E))
-        dest = eff.reshape(K_TOP, tl) // el
-        pcnt = np.array([(dest == q).any(axis=0).sum() if q != dead else 0 for q in range(world)])
-        payload[r] = np.concatenate([starts, pcnt])
-        res[r] = dict(eff=eff, starts=starts)
-    payload[dead] = 12345  # whatever a dead rank left behind is ignored
+        payload[r] = ep_payload(eff, tl, E, world, mask)
+        res[r] = dict(eff=eff)
     caps = (world * tl * K_TOP, world * tl, tl * min(world, K_TOP))
-    for r in live:
-        pp, pg = ep_plan_peer(payload, r, *caps, live=mask)
-        assert pp["ok"] == 1
-        res[r].update(pgroups=pg, **{"p_" + key: np.asarray(v) for key, v in pp.items()})
-    # replay the pushes of the live ranks
-    xpair = {r: {} for r in live}
-    units = {r: {} for r in live}
-    ret = {r: {} for r in live}
-    failed = 0
-    for s_ in live:
-        eff, starts = res[s_]["eff"], res[s_]["starts"]
-        order = np.argsort(eff, kind="stable")
-        dest = eff.reshape(K_TOP, tl) // el
-        pl = np.full((world, tl), -1)
-        for r in live:
-            has = (dest == r).any(axis=0)
-            pl[r, has] = np.arange(has.sum())
-            for t in np.nonzero(has)[0]:
-                row = int(res[s_]["p_dst_pair_off"][r]) + pl[r, t]
-                assert row not in xpair[r]
-                xpair[r][row] = (s_, t)
-            for e in range(r * el, (r + 1) * el):
-                for i in range(starts[e], starts[e + 1]):
-                    pos = int(res[s_]["p_dst_unit_off"][e]) + (i - starts[e])
-                    assert pos not in units[r]
-                    units[r][pos] = (s_, order[i])
-        failed += int((dest == dead).sum())
-        res[s_]["_pl"] = pl
-    assert failed > 0  # the dead rank's experts had units: those fail
-    for r in live:
-        p = res[r]
-        assert sorted(xpair[r]) == list(range(int(p["p_pairs_in"])))
-        assert sorted(units[r]) == list(range(int(p["p_units_in"])))
-        for pos, (s_, u) in units[r].items():
-            e = int(res[s_]["eff"][u])
-            grp = np.searchsorted(p["pgroups"], pos, side="right") - 1
-            assert grp == e - r * el
-        roff = p["p_recv_pair_off"]
-        for prow, (s_, t) in xpair[r].items():
-            row = int(p["p_ret_off"][s_]) + prow - int(roff[s_])
-            assert row not in ret[s_]
-            ret[s_][row] = (r, t)
-    for s_ in live:
-        assert sorted(ret[s_]) == list(range(int(res[s_]["p_pairs_out"])))
-        for row, (r, t) in ret[s_].items():
-            assert int(res[s_]["p_send_pair_off"][r]) + res[s_]["_pl"][r, t] == row
+    for r in live_ranks:
+        plan, groups = ep_plan_peer(payload, r, *caps, live=mask)
+        assert plan["ok"] == 1
+        res[r]["plan"], res[r]["groups"] = plan, groups
+    assert _replay(res, world, tl, mask) > 0  # the dead rank's experts had units: they fail
+
+
+def test_peer_plan_rejects_overflow():
+    """Counts beyond a receive capacity or inconsistent counts give ok = 0."""
+    from aethermoe_b200.moe import ep_plan_peer, ep_payload
+    R, E_, tl, k = 2, 4, 6, 2
+    rng = np.random.default_rng(5)
+    effs = [rng.integers(0, E_, size=k * tl) for _ in range(R)]
+    pay = np.stack([ep_payload(e, tl, E_, R) for e in effs])
+    units_to = [sum(int((e // 2 == r).sum()) for e in effs) for r in range(R)]
+    for rank in range(R):
+        assert ep_plan_peer(pay, rank, 100, 100, 100)[0]["ok"] == 1
+        bad, groups = ep_plan_peer(pay, rank, max(units_to) - 1, 100, 100)
+        assert bad["ok"] == 0 and bad["units_in"] == 0 and not groups.any()
+    for col, delta in ((E_ + 1, 1000), (2 * E_ + 3 + R, 1000), (E_ + 3 + R, 1000), (0, 1)):
+        p2 = pay.copy()
+        p2[0, col] += delta  # too many pairs / half-A pairs / half-A units; starts not at 0
+        assert ep_plan_peer(p2, 0, 100, 100, 100)[0]["ok"] == 0

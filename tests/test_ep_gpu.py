@@ -1,7 +1,8 @@
 """Expert-parallel MoE layer over NCCL on 2+ GPUs vs the single-process oracle.
 
 One process per GPU (spawned here), experts placed in contiguous blocks or
-round-robin (expert e on rank e % R), tokens split contiguously.  The routing of every (token, slot) unit must equal the
+round-robin (expert e on rank e % R), tokens split contiguously; the step's
+two-half pipeline automatic, forced on and forced off.  The routing of every (token, slot) unit must equal the
 capacity rule applied to the GLOBAL batch (bit-exact, the contract of
 Router::assign_effective_experts in src/orchestration/router.hpp:249-266),
 and every output row must match the float64 layer oracle within the layer
@@ -41,7 +42,7 @@ def _local_experts(rank, world, E, placement):
     return np.arange(rank * el, (rank + 1) * el), None
 
 
-def _worker(rank, world, port, outdir, placement):
+def _worker(rank, world, port, outdir, placement, pipeline=-1):
     import datetime
     import torch
     import torch.distributed as dist
@@ -63,6 +64,7 @@ def _worker(rank, world, port, outdir, placement):
     layer = EPLayer(bytes(uid.cpu().numpy()), rank, world, gw, gb, qu[mine], su[mine],
                     qd[mine], sd[mine], k, capacity=cap, device=rank, max_tokens=tl,
                     expert_to_rank=place)
+    layer.set_pipeline(pipeline)
     bits = (x[rank * tl:(rank + 1) * tl].view(np.uint32) >> 16).astype(np.uint16)
     xt = torch.from_numpy(bits.view(np.int16)).to(dev).view(torch.bfloat16)
     outs = []
@@ -87,9 +89,10 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("placement", ["contiguous", "strided"])
+@pytest.mark.parametrize("placement,pipeline", [("contiguous", -1), ("strided", 1),
+                                                ("strided", 0)])
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_expert_parallel_matches_global_oracle(cuda, world, placement):
+def test_expert_parallel_matches_global_oracle(cuda, world, placement, pipeline):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < world:
@@ -97,7 +100,8 @@ def test_expert_parallel_matches_global_oracle(cuda, world, placement):
     T, d, f, E, k = CFG["T"], CFG["d"], CFG["f"], CFG["E"], CFG["k"]
     with tempfile.TemporaryDirectory() as outdir:
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        mp.start_processes(_worker, args=(world, _free_port(), outdir, placement), nprocs=world,
+        mp.start_processes(_worker, args=(world, _free_port(), outdir, placement, pipeline),
+                           nprocs=world,
                            join=True, start_method="spawn")
         res = [np.load(os.path.join(outdir, f"rank{r}.npz")) for r in range(world)]
     tl = T // world

@@ -14,27 +14,24 @@ pytestmark = pytest.mark.gpu
 
 
 def _payloads(rng, R, E, k, tl, live):
-    el = E // R
-    pay = np.zeros((R, E + 1 + R), np.int32)
+    from aethermoe_b200.moe import ep_payload
+    rows = []
     for s in range(R):
         logits = rng.normal(size=(tl, E)).astype(np.float32) + O.zipf_bias(E)
         idx = O.topk_strict(logits, k + 1).astype(np.int32)
         eff = O.moe_route(idx, k, E, O.default_capacity(tl * R, k, E))
-        pay[s, 1:E + 1] = np.cumsum(np.bincount(eff, minlength=E))
-        dest = eff.reshape(k, tl) // el
-        pay[s, E + 1:] = [(dest == r).any(axis=0).sum() if (live >> r) & 1 else 0
-                          for r in range(R)]
-    return pay
+        rows.append(ep_payload(eff, tl, E, R, live))
+    return np.stack(rows)
 
 
 def _device_plan(cuda, pay, rank, live, caps):
     import torch
     from aethermoe_b200 import _lib
-    R, w = pay.shape
-    E = w - 1 - R
+    R = pay.shape[0]
+    E = _width_to_experts(pay.shape[1], R)
     all_d = torch.from_numpy(pay).to(cuda)
     plan_d = torch.zeros(ctypes.sizeof(_lib.EpPeerPlan), dtype=torch.uint8, device=cuda)
-    groups_d = torch.full((E + 1,), -7, dtype=torch.int32, device=cuda)
+    groups_d = torch.full((2 * (E + 1),), -7, dtype=torch.int32, device=cuda)
     _lib.check(_lib.lib().aem_ep_plan_peer_device(all_d.data_ptr(), R, E, rank, live, *caps,
                                                   plan_d.data_ptr(), groups_d.data_ptr(), None),
                "aem_ep_plan_peer_device")
@@ -45,20 +42,24 @@ def _device_plan(cuda, pay, rank, live, caps):
 
 def _host_plan(pay, rank, live, caps):
     from aethermoe_b200 import _lib
-    R, w = pay.shape
-    E = w - 1 - R
+    R = pay.shape[0]
+    E = _width_to_experts(pay.shape[1], R)
     plan = _lib.EpPeerPlan()
-    groups = np.full(E + 1, -7, np.int32)
+    groups = np.full(2 * (E + 1), -7, np.int32)
     p = np.ascontiguousarray(pay)
     _lib.check(_lib.lib().aem_ep_plan_peer(p.ctypes.data, R, E, rank, live, *caps,
                                            ctypes.byref(plan), groups.ctypes.data))
     return plan, groups
 
 
-def _same(a, b, ga, gb, el):
+def _width_to_experts(w, R):
     from aethermoe_b200 import _lib
+    return next(e for e in range(R, 257, R) if _lib.ep_payload_words(e, R) == w)
+
+
+def _same(a, b, ga, gb, el):
     assert bytes(a) == bytes(b)
-    np.testing.assert_array_equal(ga[:el + 1], gb[:el + 1])
+    np.testing.assert_array_equal(ga[:2 * (el + 1)], gb[:2 * (el + 1)])
 
 
 @pytest.mark.parametrize("R,E,k", [(2, 8, 2), (4, 64, 6), (8, 64, 6), (8, 256, 8), (64, 256, 4)])
@@ -87,6 +88,8 @@ def test_device_plan_rejects_what_the_host_rejects(cuda):
     b = pay.copy(); b[1, E + 1] += 1_000_000; bads.append((b, caps))   # more pairs than units
     b = pay.copy(); b[2, 3] = b[2, 2] - 1; bads.append((b, caps))         # starts decrease
     b = pay.copy(); b[0, 0] = 5; bads.append((b, caps))                   # starts not at 0
+    b = pay.copy(); b[3, E + 3 + R] += 1000; bads.append((b, caps))       # half-A units > units
+    b = pay.copy(); b[1, 2 * E + 3 + R] += 1000; bads.append((b, caps))   # half-A pairs > pairs
     bads.append((pay, (10, caps[1], caps[2])))                            # units over capacity
     bads.append((pay, (caps[0], 10, caps[2])))                            # pairs over capacity
     bads.append((pay, (caps[0], caps[1], 10)))                            # returns over capacity
