@@ -23,6 +23,8 @@ LIB = os.path.join(HERE, "libaethermoe.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr", "-I", INCLUDE, "-I", CSRC]
+# Per-file extra flags (none at present).
+FILE_FLAGS: dict = {}
 
 
 def _nvcc():
@@ -69,9 +71,9 @@ def build(verbose=False, force=False, ptxas_info=False):
     for src in _sources():
         obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
         objs.append(obj)
-        if force or _stale(obj, [src] + headers):
-            cmd = [nvcc] + ARCH + FLAGS + (["-Xptxas", "-v"] if ptxas_info else []) + \
-                ["-c", src, "-o", obj]
+        if force or _stale(obj, [src, os.path.abspath(__file__)] + headers):
+            cmd = [nvcc] + ARCH + FLAGS + FILE_FLAGS.get(os.path.basename(src), []) + \
+                (["-Xptxas", "-v"] if ptxas_info else []) + ["-c", src, "-o", obj]
             jobs.append(cmd)
     out = []
     if jobs:

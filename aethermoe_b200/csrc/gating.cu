@@ -69,9 +69,9 @@ struct GatingCfg {
     static constexpr int DK4 = DK / 4;
     // float32 activations of a chunk, token pairs interleaved: pair p's row
     // holds, for every 4 consecutive d, (t0 d0, t1 d0, t0 d1, t1 d1, t0 d2,
-    // t1 d2, t0 d3, t1 d3) with t0 = 2p, t1 = 2p+1 -- each 16-byte load
-    // yields two (token 2p, token 2p+1) operand pairs of the packed fp32x2
-    // multiply; rows padded against bank conflicts
+    // t1 d2, t0 d3, t1 d3) with t0 = 2p, t1 = 2p+1 -- two 16-byte loads
+    // give both tokens' activations for the 4 d of one weight float4; rows
+    // padded against bank conflicts
     static constexpr int XS = 2 * DK + 4;
     static constexpr int XB = static_cast<int>(sizeof(XT));
     static constexpr int XPC = 16 / XB;     // activation elements per 16-byte piece
@@ -194,16 +194,19 @@ __global__ void __launch_bounds__(WARPS * 32)
                 for (int p = 0; p < kTPG / 2; ++p) {
                     float2 a = acc[p][s];
                     if constexpr (EXACT) {
-                        // float32 product, then float32 add, d in increasing order,
-                        // two tokens per packed fp32x2 op
-                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xa[p].x, xa[p].y),
-                                                     make_float2(wv.x, wv.x)));
-                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xa[p].z, xa[p].w),
-                                                     make_float2(wv.y, wv.y)));
-                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xb[p].x, xb[p].y),
-                                                     make_float2(wv.z, wv.z)));
-                        a = __fadd2_rn(a, __fmul2_rn(make_float2(xb[p].z, xb[p].w),
-                                                     make_float2(wv.w, wv.w)));
+                        // float32 product, then float32 add, d in increasing order.
+                        // Scalar ops: a packed fp32x2 multiply followed by a packed
+                        // add (as intrinsics or as explicit mul.rn/add.rn.f32x2)
+                        // was measured to round like one fused multiply-add,
+                        // which reorders experts whose logits are 1 ulp apart.
+                        a.x = __fadd_rn(a.x, __fmul_rn(xa[p].x, wv.x));
+                        a.y = __fadd_rn(a.y, __fmul_rn(xa[p].y, wv.x));
+                        a.x = __fadd_rn(a.x, __fmul_rn(xa[p].z, wv.y));
+                        a.y = __fadd_rn(a.y, __fmul_rn(xa[p].w, wv.y));
+                        a.x = __fadd_rn(a.x, __fmul_rn(xb[p].x, wv.z));
+                        a.y = __fadd_rn(a.y, __fmul_rn(xb[p].y, wv.z));
+                        a.x = __fadd_rn(a.x, __fmul_rn(xb[p].z, wv.w));
+                        a.y = __fadd_rn(a.y, __fmul_rn(xb[p].w, wv.w));
                     } else {
                         a.x = fmaf(xa[p].x, wv.x, a.x);
                         a.y = fmaf(xa[p].y, wv.x, a.y);

@@ -430,11 +430,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = ei & 3;
         const int h = ei >> 2;
         int it = 0;
-        for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++it) {
+        // loop exits are warp-uniform: the TMEM loads below are warp-collective
+        for (int t = blockIdx.x; t < total && !__any_sync(0xFFFFFFFFu, *abort_flag != 0);
+             t += gridDim.x, ++it) {
             const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
             const int b = it & 1;
             const uint32_t aph = (it >> 1) & 1;
-            if (!mbar_wait_bounded(&accf_bar[b], aph, abort_flag, p.err, ERR_GEMM_TIMEOUT)) break;
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&accf_bar[b], aph, abort_flag, p.err,
+                                                           ERR_GEMM_TIMEOUT)))
+                break;
             tc_fence_after();
             const int n = ti.n0 + q * 32 + lane;
             const bool nvalid = n < p.N;

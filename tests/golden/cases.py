@@ -56,6 +56,20 @@ def gating_cases():
     return c
 
 
+# (n, d, e, k, seed) of _gating_inputs draws holding a row whose k-th and
+# (k+1)-th (or two neighbouring) logits are adjacent float32 values: the
+# sequential float32 sum and a fused multiply-add sum order them differently,
+# so these cases tell the two apart (found by a random sweep of 86895 draws).
+NEAR_TIE_GATING = [(38, 44, 19, 12, 1595066796), (46, 58, 20, 17, 2056578468),
+                   (48, 32, 23, 18, 115215509), (38, 61, 29, 19, 1082537402),
+                   (36, 7, 30, 24, 608740648)]
+
+
+def near_tie_gating_cases():
+    return {f"near_tie_{n}_{d}_{e}_{k}": _gating_inputs(np.random.default_rng(seed), n, d, e) + (k,)
+            for n, d, e, k, seed in NEAR_TIE_GATING}
+
+
 def c0_inputs():
     """CPU-runnable config: x [256,512], W_gate [512,8] ~ N(0,1/d), bias 0,
     expert weight [512,1024] ~ N(0,0.02); one generator, seed 0."""

@@ -125,6 +125,17 @@ def test_small_shape_grid(shim, e):
                 np.testing.assert_allclose(val, oval, atol=1e-6)
 
 
+@pytest.mark.parametrize("name", sorted(cases.near_tie_gating_cases()))
+def test_exact_mode_near_ties(shim, name):
+    """Rows with adjacent-float32 logits: EXACT mode rounds every product and
+    partial sum like the reference loop, so even these orders match."""
+    fg, _ = shim
+    h, w, b, k = cases.near_tie_gating_cases()[name]
+    idx, _ = fg.fused_gating(h, w, b, k)
+    oidx, _ = O.fused_gating(h, w, b, k)
+    np.testing.assert_array_equal(idx, oidx)
+
+
 def test_ties_pick_lowest_ids(shim):
     fg, _ = shim
     for name, want in (("tie_2_5", [2, 5]), ("tie_1_4", [1, 4])):

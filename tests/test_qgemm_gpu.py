@@ -161,3 +161,57 @@ def test_groups_select_their_weights(cuda):
                                         torch.cuda.current_stream().cuda_stream))
         torch.cuda.synchronize()
         _close(out.cpu().numpy(), O.qgemm(x, q[grp], s[grp:grp + 1]))
+
+
+@pytest.mark.parametrize("tile", [256, 128, 64])
+@pytest.mark.parametrize("mode", ["relu_bf16", "scaled_add"])
+def test_grouped_ragged_tiles(cuda, tile, mode):
+    """aem_grouped_qgemm over ragged groups (empty, 1 row, 191-193 rows,
+    several tiles) at token tiles 256, 128 and 64; a partial output-channel
+    block (N = 300).
+    relu_bf16: the up projection's epilogue; scaled_add: the down
+    projection's (gate-weight row scale, float32 red.add into mapped rows)."""
+    import torch
+    from aethermoe_b200 import _lib
+    rng = np.random.default_rng(tile + len(mode))
+    sizes = [0, 1, 15, 191, 192, 193, 700, 37]
+    G, K, N = len(sizes), 448, 300
+    q = rng.integers(-127, 128, size=(G, K, N), dtype=np.int8)
+    s = (rng.random(size=(G, N)) * 1e-3 + 1e-4).astype(np.float32)
+    w = _lib.QWeight(q, s, 0)
+    rows = np.r_[0, np.cumsum(sizes)].astype(np.int32)
+    M = int(rows[-1])
+    x = O.bf16_round(rng.normal(size=(M, K)).astype(np.float32))
+    xbits = (x.view(np.uint32) >> 16).astype(np.uint16)
+    xt = torch.from_numpy(xbits.view(np.int16)).to(cuda).view(torch.bfloat16)
+    rt = torch.from_numpy(rows).to(cuda)
+    ref = np.zeros((M, N))
+    for g in range(G):
+        a, b = rows[g], rows[g + 1]
+        ref[a:b] = x[a:b].astype(np.float64) @ (q[g].astype(np.float64) * s[g].astype(np.float64))
+    stream = torch.cuda.current_stream().cuda_stream
+    if mode == "relu_bf16":
+        out = torch.zeros((M, N), dtype=torch.bfloat16, device=cuda)
+        _lib.check(_lib.lib().aem_grouped_qgemm(w.handle, rt.data_ptr(), G, xt.data_ptr(), M,
+                                                out.data_ptr(), _lib.BF16, N, 1, 0, None, None,
+                                                tile, 1, stream), "aem_grouped_qgemm")
+        torch.cuda.synchronize()
+        got = out.float().cpu().numpy()
+        want = O.bf16_round(np.maximum(ref, 0.0).astype(np.float32))
+        # bf16 output: within one bf16 rounding of the float64 result
+        _close(got, np.maximum(ref, 0.0), rtol=2 ** -8 + 1e-3, atol=1e-3)
+        assert np.mean(got == want) > 0.99
+    else:
+        rmap = rng.permutation(M).astype(np.int32)
+        rscale = (rng.random(M) + 0.5).astype(np.float32)
+        base = rng.normal(size=(M, N)).astype(np.float32)
+        out = torch.from_numpy(base.copy()).to(cuda)
+        mt = torch.from_numpy(rmap).to(cuda)
+        st = torch.from_numpy(rscale).to(cuda)
+        _lib.check(_lib.lib().aem_grouped_qgemm(w.handle, rt.data_ptr(), G, xt.data_ptr(), M,
+                                                out.data_ptr(), _lib.F32, N, 0, 1, mt.data_ptr(),
+                                                st.data_ptr(), tile, 1, stream), "aem_grouped_qgemm")
+        torch.cuda.synchronize()
+        want = base.astype(np.float64).copy()
+        want[rmap] += ref * rscale[:, None].astype(np.float64)
+        _close(out.cpu().numpy(), want)
