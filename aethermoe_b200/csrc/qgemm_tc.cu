@@ -9,21 +9,23 @@
 // activation rows (the MMA's N, 16..256), which keeps decode-size batches (a handful
 // of rows) on the tensor cores with the int8 weight stream as the only large read.
 //
-// Per CTA (one per SM, persistent over tiles), 19 warps and three smem rings
-// (int8 weights, converted bf16 weights, activations), each with its own depth:
+// Per CTA (one per SM, persistent over tiles), 19 warps and two smem rings: the
+// int8 weight ring and the operand ring, whose stage holds one K step's
+// activation tile and its converted bf16 weights under one full and one empty
+// barrier:
 //   warp 16     int8 weight producer: one contiguous 8 KB bulk copy per [128 x 64 B]
 //               tile of the pre-tiled weight layout -- the HBM stream.
 //   warp 18     activation producer: TMA of the bf16 [BT x 128 B] tile(s) (128-byte
-//               swizzle); its ring is deep where stages are small, because these
-//               loads queue behind the weight stream's bulk copies.
+//               swizzle) into the stage, arriving on its full barrier.
 //   warps 0-7   converters, in groups that take K steps round-robin: int8 -> bf16
 //               (exact: |q| <= 127 fits bf16's 8-bit significand) written straight
 //               into the 128-byte-swizzled K-major layout the MMA reads, then
-//               fence.proxy.async and one mbarrier arrival per warp.
-//   warp 17     MMA issuer (one thread): 4 x tcgen05.mma kind::f16 (K=16 each) per
-//               64-wide step, x2 for split float32 activations (hi + lo), accumulating
-//               float32 in a double-buffered TMEM accumulator; tcgen05.commit frees the
-//               operand slots and, at the end of a tile, hands the accumulator over.
+//               fence.proxy.async and one arrival per warp on the stage's full barrier.
+//   warp 17     MMA issuer (one thread): one wait per K step, 4 x tcgen05.mma
+//               kind::f16 (K=16 each), x2 for split float32 activations (hi + lo),
+//               accumulating float32 in a double-buffered TMEM accumulator; one
+//               tcgen05.commit frees the stage and, at the end of a tile, one hands
+//               the accumulator over.
 //   warps 8-15  epilogue, two warps per TMEM lane quarter splitting the columns:
 //               tcgen05.ld 32 lanes x 16 columns, per-channel scale, per-row output
 //               index and multiplier (fetched once per 16 columns, broadcast by
@@ -40,6 +42,7 @@
 namespace aem {
 
 aem_status launch_qgemm_simt(const GemmArgs& a, cudaStream_t s);
+aem_status launch_qgemm_decode(const GemmArgs& a, cudaStream_t s);
 
 namespace {
 
@@ -56,10 +59,11 @@ constexpr int kConvThreads = kConvWarps * 32;
 // Converter warps form groups that take K steps round-robin, so several K
 // steps are in conversion at once (one group's convert -> proxy fence ->
 // arrive latency no longer serialises the stream of K steps).  The group
-// count must not exceed the converted-weight ring depth: a group handling K
-// step kc has finished kc - G, whose wait proved K step kc - G - D retired,
-// so with G <= D the slot's previous phase (kc - D) is at most one phase
-// ahead of the barrier and the parity wait cannot alias an older phase.
+// count must not exceed the operand ring depth: a group handling K step kc
+// has finished kc - G, whose wait proved K step kc - G - D retired, so with
+// G <= D the slot's previous phase (kc - D) is at most one phase ahead of the
+// barrier and the parity wait cannot alias an older phase.  The int8 ring's
+// depth is a multiple of G, for the same reason (see Cfg::S8).
 #ifndef AEM_QGEMM_MAX_CONV_GROUPS
 #define AEM_QGEMM_MAX_CONV_GROUPS 4
 #endif
@@ -101,27 +105,36 @@ struct Cfg {
     static constexpr int W16 = kCh * kKT * 2;      // bf16 weight tile (MMA A)
     static constexpr int XB = BT * kKT * 2;        // bf16 activation tile (MMA B), per part
     static constexpr int XS = SPLIT * XB;          // one activation stage
-    // Three rings with their own depths.  The activation ring must cover the
-    // latency of its loads, which queue behind the weight stream's bulk
-    // copies: it is deep where its stages are small (narrow, decode-size
-    // tiles).  The converted-weight ring holds the MMA's A operands.
-    static constexpr int DX = SPLIT == 1
-        ? (BT <= 16 ? 16 : (BT <= 32 ? 12 : (BT <= 64 ? 8 : (BT <= 128 ? 5 : 3))))
-        : (BT <= 16 ? 16 : (BT <= 32 ? 8 : (BT <= 64 ? 4 : 2)));
-    static constexpr int D16 = (BT >= 256 && SPLIT == 2) ? 3 : 4;
-    static constexpr int S8_RAW = (196 * 1024 - DX * XS - D16 * W16) / W8;
-    static constexpr int S8 = S8_RAW > 12 ? 12 : S8_RAW;
-    static constexpr int TMEM_COLS = 2 * BT < 32 ? 32 : 2 * BT;
-    static constexpr int BAR_BYTES = (2 * DX + 2 * D16 + 2 * S8 + 4) * 8 + 16;
-    static constexpr int TAB_BYTES = 2 * (kMaxGroups + 1) * 4;
-    static constexpr int SMEM = 1024 + D16 * W16 + DX * XS + S8 * W8 + BAR_BYTES + TAB_BYTES;
-    static constexpr int CG_RAW = D16 >= 4 ? 4 : (D16 >= 2 ? 2 : 1);
+    // Two rings.  A stage of the operand ring holds one K step's activation
+    // tile (TMA) and its converted bf16 weights; one barrier says both are
+    // in (the TMA's bytes plus one arrival per converter warp) and one
+    // commit frees both, so the single MMA-issuing thread does one wait and
+    // one commit per K step -- its synchronisation, not the tensor core,
+    // bounded the step rate when each ring had its own barriers.  The int8
+    // ring streams the weights from HBM; it gets what the operand ring
+    // leaves of the budget.
+    static constexpr int BUDGET = 216 * 1024;
+    static constexpr int DS_RAW = (BUDGET - 8 * W8) / (W16 + XS);  // 8 int8 stages first
+    static constexpr int DS = DS_RAW > 8 ? 8 : (DS_RAW < 2 ? 2 : DS_RAW);
+    static constexpr int S8_RAW = (BUDGET - DS * (W16 + XS)) / W8;
+    static constexpr int CG_RAW = DS >= 4 ? 4 : (DS >= 2 ? 2 : 1);
     static constexpr int CG = CG_RAW < AEM_QGEMM_MAX_CONV_GROUPS ? CG_RAW : AEM_QGEMM_MAX_CONV_GROUPS;
+    // The int8 ring's depth is a multiple of the group count: then the
+    // previous fill of the slot a group waits on (K step kc - S8) was that same
+    // group's, so it has landed, and the parity wait for kc cannot mistake the
+    // slot's older phase for kc's (bulk copies may land out of order, so a
+    // fill owned by another group would give no such guarantee).
+    static constexpr int S8 = ((S8_RAW > 12 ? 12 : S8_RAW) / CG) * CG;
+    static constexpr int TMEM_COLS = 2 * BT < 32 ? 32 : 2 * BT;
+    static constexpr int BAR_BYTES = (2 * DS + 2 * S8 + 4) * 8 + 16;
+    static constexpr int TAB_BYTES = 2 * (kMaxGroups + 1) * 4;
+    static constexpr int SMEM = 1024 + DS * (W16 + XS) + S8 * W8 + BAR_BYTES + TAB_BYTES;
     static constexpr int CG_WARPS = kConvWarps / CG;        // warps per converter group
     static constexpr int CG_THREADS = CG_WARPS * 32;
     static constexpr int EPI_COLS = BT >= 32 ? BT / 2 : BT;  // columns per epilogue warp
-    static_assert(CG <= D16 && S8 >= CG && kConvWarps % CG == 0, "converter groups vs rings");
-    static_assert(S8 >= 2 && DX >= 2 && D16 >= 2, "pipeline needs two stages per ring");
+    static_assert(CG <= DS && S8 >= CG && S8 % CG == 0 && kConvWarps % CG == 0,
+                  "converter groups vs rings");
+    static_assert(S8 >= 2 && DS >= 2, "pipeline needs two stages per ring");
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
     static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N for M=128");
 };
@@ -189,20 +202,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint8_t* w16_ring = smem;                          // D16 x bf16 W (MMA A, 128B swizzle)
-    uint8_t* x_ring = w16_ring + C::D16 * C::W16;      // DX x [X hi | X lo] (MMA B)
-    uint8_t* w8_ring = x_ring + C::DX * C::XS;         // S8 x int8 W
-    uint64_t* x_full = reinterpret_cast<uint64_t*>(w8_ring + C::S8 * C::W8);
-    uint64_t* x_empty = x_full + C::DX;
-    uint64_t* w16_full = x_empty + C::DX;
-    uint64_t* w16_empty = w16_full + C::D16;
-    uint64_t* w8_full = w16_empty + C::D16;
+    uint8_t* w16_ring = smem;                          // DS x bf16 W (MMA A, 128B swizzle)
+    uint8_t* x_ring = w16_ring + C::DS * C::W16;       // DS x [X hi | X lo] (MMA B)
+    uint8_t* w8_ring = x_ring + C::DS * C::XS;         // S8 x int8 W
+    uint64_t* st_full = reinterpret_cast<uint64_t*>(w8_ring + C::S8 * C::W8);
+    uint64_t* st_empty = st_full + C::DS;
+    uint64_t* w8_full = st_empty + C::DS;
     uint64_t* w8_empty = w8_full + C::S8;
     uint64_t* accf_bar = w8_empty + C::S8;  // [2]
     uint64_t* acce_bar = accf_bar + 2;      // [2]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    int* s_rows = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(x_full) + C::BAR_BYTES);
+    int* s_rows = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(st_full) + C::BAR_BYTES);
     int* s_tiles = s_rows + (kMaxGroups + 1);
 
     const int tid = threadIdx.x;
@@ -211,13 +222,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- setup: barriers, group table, TMEM
     if (tid == 0) {
-        for (int s = 0; s < C::DX; ++s) {
-            mbar_init(&x_full[s], 1);
-            mbar_init(&x_empty[s], 1);
-        }
-        for (int s = 0; s < C::D16; ++s) {
-            mbar_init(&w16_full[s], C::CG_WARPS);
-            mbar_init(&w16_empty[s], 1);
+        for (int s = 0; s < C::DS; ++s) {
+            // the activation producer's arrive.expect_tx + one arrival per converter warp
+            mbar_init(&st_full[s], C::CG_WARPS + 1);
+            mbar_init(&st_empty[s], 1);
         }
         for (int s = 0; s < C::S8; ++s) {
             mbar_init(&w8_full[s], 1);
@@ -301,18 +309,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = blockIdx.x; t < total && ok && !*abort_flag; t += gridDim.x) {
                 const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                    if (!mbar_wait_bounded(&x_empty[sx], phx ^ 1, abort_flag, p.err,
+                    if (!mbar_wait_bounded(&st_empty[sx], phx ^ 1, abort_flag, p.err,
                                            ERR_GEMM_TIMEOUT)) {
                         ok = false;
                         break;
                     }
                     uint8_t* st = x_ring + sx * C::XS;
-                    mbar_arrive_expect_tx(&x_full[sx], C::XS);
-                    tma_load_2d(st, &tm_xh, &x_full[sx], kt * kKT, static_cast<int>(ti.row0));
+                    mbar_arrive_expect_tx(&st_full[sx], C::XS);
+                    tma_load_2d(st, &tm_xh, &st_full[sx], kt * kKT, static_cast<int>(ti.row0));
                     if (SPLIT == 2)
-                        tma_load_2d(st + C::XB, &tm_xl, &x_full[sx], kt * kKT,
+                        tma_load_2d(st + C::XB, &tm_xl, &st_full[sx], kt * kKT,
                                     static_cast<int>(ti.row0));
-                    if (++sx == C::DX) {
+                    if (++sx == C::DS) {
                         sx = 0;
                         phx ^= 1;
                     }
@@ -322,8 +330,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == kMmaWarp) {
         // ================= MMA issuer
         if (lane == 0) {
-            int sx = 0, s16 = 0;
-            uint32_t phx = 0, ph16 = 0;
+            int ss = 0;  // operand-ring stage
+            uint32_t phs = 0;
             int it = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok && !*abort_flag; t += gridDim.x, ++it) {
@@ -339,16 +347,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int n_eff = min(BT, (ti.nrows + 15) & ~15);
                 const uint32_t idesc = idesc_bf16_f32(kCh, static_cast<uint32_t>(n_eff));
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                    if (!mbar_wait_bounded(&x_full[sx], phx, abort_flag, p.err, ERR_GEMM_TIMEOUT) ||
-                        !mbar_wait_bounded(&w16_full[s16], ph16, abort_flag, p.err,
-                                           ERR_GEMM_TIMEOUT)) {
+                    // activations and converted weights of this K step are in
+                    if (!mbar_wait_bounded(&st_full[ss], phs, abort_flag, p.err, ERR_GEMM_TIMEOUT)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t adesc = smem_desc_sw128(smem_u32(w16_ring + s16 * C::W16));
-                    const uint64_t bdesc = smem_desc_sw128(smem_u32(x_ring + sx * C::XS));
-                    const uint64_t ldesc = smem_desc_sw128(smem_u32(x_ring + sx * C::XS + C::XB));
+                    const uint64_t adesc = smem_desc_sw128(smem_u32(w16_ring + ss * C::W16));
+                    const uint64_t bdesc = smem_desc_sw128(smem_u32(x_ring + ss * C::XS));
+                    const uint64_t ldesc = smem_desc_sw128(smem_u32(x_ring + ss * C::XS + C::XB));
 #pragma unroll
                     for (int kk = 0; kk < kKT / 16; ++kk) {
                         // +32 bytes along K per UMMA_K=16 step (start address field, >>4)
@@ -357,16 +364,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (SPLIT == 2)
                             tc_mma_f16(d_tmem, adesc + 2 * kk, ldesc + 2 * kk, idesc, 1u);
                     }
-                    // both operand slots free once these MMAs retire
-                    tc_commit(&x_empty[sx]);
-                    tc_commit(&w16_empty[s16]);
-                    if (++sx == C::DX) {
-                        sx = 0;
-                        phx ^= 1;
-                    }
-                    if (++s16 == C::D16) {
-                        s16 = 0;
-                        ph16 ^= 1;
+                    // the stage is free once these MMAs retire
+                    tc_commit(&st_empty[ss]);
+                    if (++ss == C::DS) {
+                        ss = 0;
+                        phs ^= 1;
                     }
                 }
                 if (!ok) break;
@@ -383,13 +385,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
             for (int kt = ti.kt0; kt < ti.kt1; ++kt, ++kc) {
                 if (static_cast<int>(kc % C::CG) != group) continue;
-                const int s16 = static_cast<int>(kc % C::D16);
-                const uint32_t ph16 = (kc / C::D16) & 1;
+                const int s16 = static_cast<int>(kc % C::DS);
+                const uint32_t ph16 = (kc / C::DS) & 1;
                 const int s8 = static_cast<int>(kc % C::S8);
                 const uint32_t ph8 = (kc / C::S8) & 1;
                 // int8 tile landed, and the bf16 slot is free (its last MMA retired)
                 if (!mbar_wait_bounded(&w8_full[s8], ph8, abort_flag, p.err, ERR_GEMM_TIMEOUT) ||
-                    !mbar_wait_bounded(&w16_empty[s16], ph16 ^ 1, abort_flag, p.err,
+                    !mbar_wait_bounded(&st_empty[s16], ph16 ^ 1, abort_flag, p.err,
                                        ERR_GEMM_TIMEOUT)) {
                     ok = false;
                     break;
@@ -418,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(&w16_full[s16]);
+                    mbar_arrive(&st_full[s16]);
                     mbar_arrive(&w8_empty[s8]);
                 }
             }
@@ -588,6 +590,8 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
                 "qgemm: weight group out of range");
     AEM_REQUIRE(!(a.atomic_add && a.out_bf16), "qgemm: split-K needs float32 output");
     if (a.M == 0) return AEM_OK;
+    // decode sizes (at most 4 rows, so at most 4 per group): CUDA cores
+    if (a.M <= 4 && a.token_tile == 0) return launch_qgemm_decode(a, s);
     if (w.K % 8 != 0) return launch_qgemm_simt(a, s);
     AEM_REQUIRE(a.M < (1ll << 31) && w.G * w.N < (1ll << 31), "qgemm: too many rows");
     const int dev = current_device();

@@ -4,6 +4,8 @@
 // split, and the CUDA-core GEMM used when K is not a multiple of 8.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "runtime.h"
 
@@ -106,7 +108,190 @@ __global__ void qgemm_simt_kernel(const __nv_bfloat16* __restrict__ xh,
     }
 }
 
+// Decode-size INT8 GEMM on the CUDA cores (at most MAXM <= 4 rows per weight
+// group).  At these sizes the tensor-core kernel's per-K-step issue loop, not
+// the weight stream, sets the time; here every SM streams weights at memory
+// speed.  One CTA of 128 threads per (row group, 128-channel block, K range).
+// Thread t owns 16-byte chunk c = t % 4 (16 consecutive K) of channel rows
+// t/4 + 32j (j < 4) of every 8 KB weight tile, so each warp load reads 512
+// contiguous bytes and the chunk's 16 activations serve four rows.  int8 ->
+// float is exact (2^23 + 128 + b as a float bit pattern, minus 2^23 + 128);
+// products are summed by packed float32 FMAs (even and odd K in two lanes);
+// the four owners of a row combine by shuffles.  Split-K partial sums (KS > 1)
+// are added with float32 atomics into a float32 output.
+constexpr int kDecodeThreads = 128;
+constexpr int kDecodeStageK = 8;  // 64-wide K blocks of activations staged at once
+constexpr int kDecodeXRow = kDecodeStageK * 64 + kDecodeStageK * 8;  // padded row
+
+// Staged activation k (relative to the chunk) -> its padded position: 4 floats
+// of padding after every 32, so the four chunk owners' 16-byte loads of one
+// quarter warp fall in distinct banks.
+__device__ __forceinline__ int xpad(int kk) { return kk + 4 * (kk >> 5); }
+
+template <int MAXM>
+__global__ void __launch_bounds__(kDecodeThreads)
+    qgemm_decode_kernel(const __nv_bfloat16* __restrict__ xh, const __nv_bfloat16* __restrict__ xl,
+                        const int8_t* __restrict__ q, const float* __restrict__ scale, int64_t M,
+                        int64_t K, int64_t N, int64_t NT, int64_t KT,
+                        const int* __restrict__ group_rows, int64_t group_base, int wmod, int KS,
+                        int kper, void* __restrict__ out, int64_t ldo, int out_bf16, int relu,
+                        int atomic_add, const int* __restrict__ rowmap,
+                        const float* __restrict__ rowscale, int* __restrict__ err) {
+    __shared__ __align__(16) float xs[MAXM][kDecodeXRow];
+    int64_t b = blockIdx.x;
+    const int ks = static_cast<int>(b % KS);
+    b /= KS;
+    const int64_t nb = b % NT;
+    const int g = static_cast<int>(b / NT);
+    const int r0 = group_rows ? group_rows[g] : 0;
+    const int r1 = group_rows ? group_rows[g + 1] : static_cast<int>(M);
+    const int m = r1 - r0;
+    if (m < 0 || m > MAXM || r0 < 0 || r1 > M) {  // group table inconsistent with M
+        if (threadIdx.x == 0) atomicOr(err, ERR_GEMM_GROUPS);
+        return;
+    }
+    const int kt0 = ks * kper;
+    const int kt1 = static_cast<int>(min(KT, static_cast<int64_t>(kt0 + kper)));
+    if (m <= 0 || kt0 >= kt1) return;  // uniform over the CTA
+    const int64_t wg = group_base + (wmod ? g % wmod : g);
+    const int t = threadIdx.x;
+    const int c = t & 3;
+    const int8_t* wtile = q + ((wg * NT + nb) * KT) * kWTileBytes + t * 16;  // + j * 2048
+    float2 acc[4][MAXM];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int i = 0; i < MAXM; ++i) acc[j][i] = make_float2(0.0f, 0.0f);
+    const float2 magic = make_float2(-8388736.0f, -8388736.0f);
+    for (int kc = kt0; kc < kt1; kc += kDecodeStageK) {
+        const int nkb = min(kDecodeStageK, kt1 - kc);
+        __syncthreads();  // the previous chunk's activations are consumed
+        for (int i = t; i < MAXM * kDecodeStageK * 64; i += kDecodeThreads) {
+            const int mm = i / (kDecodeStageK * 64), kk = i % (kDecodeStageK * 64);
+            const int64_t k = static_cast<int64_t>(kc) * 64 + kk;
+            float v = 0.0f;
+            if (mm < m && kk < nkb * 64 && k < K) {
+                const int64_t o = static_cast<int64_t>(r0 + mm) * K + k;
+                v = __bfloat162float(xh[o]);
+                if (xl) v += __bfloat162float(xl[o]);
+            }
+            xs[mm][xpad(kk)] = v;
+        }
+        __syncthreads();
+#pragma unroll 2
+        for (int kb = 0; kb < nkb; ++kb) {
+            const int8_t* src = wtile + static_cast<int64_t>(kc + kb) * kWTileBytes;
+            uint4 wv[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                             : "=r"(wv[j].x), "=r"(wv[j].y), "=r"(wv[j].z), "=r"(wv[j].w)
+                             : "l"(src + 2048 * j));
+            }
+            float4 xv[MAXM][4];  // this chunk's 16 activations of each row
+#pragma unroll
+            for (int mm = 0; mm < MAXM; ++mm)
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    xv[mm][e] = *reinterpret_cast<const float4*>(
+                        &xs[mm][xpad(kb * 64 + c * 16) + 4 * e]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t words[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const uint32_t u = words[e] ^ 0x80808080u;
+                    const float2 w01 = __fadd2_rn(
+                        make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)),
+                                    __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441))),
+                        magic);
+                    const float2 w23 = __fadd2_rn(
+                        make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)),
+                                    __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443))),
+                        magic);
+#pragma unroll
+                    for (int mm = 0; mm < MAXM; ++mm) {
+                        acc[j][mm] = __ffma2_rn(w01, make_float2(xv[mm][e].x, xv[mm][e].y),
+                                                acc[j][mm]);
+                        acc[j][mm] = __ffma2_rn(w23, make_float2(xv[mm][e].z, xv[mm][e].w),
+                                                acc[j][mm]);
+                    }
+                }
+            }
+        }
+    }
+    // the four chunk owners of a row (lanes 4i..4i+3) combine; lane c == 0 stores
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int64_t n = nb * kWTileN + (t >> 2) + 32 * j;
+        const float sc = (n < N) ? scale[wg * N + n] : 0.0f;
+#pragma unroll
+        for (int mm = 0; mm < MAXM; ++mm) {
+            float v = acc[j][mm].x + acc[j][mm].y;
+            v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
+            v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
+            if (c != 0 || mm >= m || n >= N) continue;
+            const int r = r0 + mm;
+            v *= sc;
+            if (rowscale) v *= rowscale[r];
+            if (relu) v = fmaxf(v, 0.0f);
+            const int64_t orow = rowmap ? rowmap[r] : r;
+            if (out_bf16)
+                static_cast<__nv_bfloat16*>(out)[orow * ldo + n] = __float2bfloat16_rn(v);
+            else if (atomic_add)
+                atomicAdd(static_cast<float*>(out) + orow * ldo + n, v);
+            else
+                static_cast<float*>(out)[orow * ldo + n] = v;
+        }
+    }
+}
+
 }  // namespace
+
+aem_status launch_qgemm_decode(const GemmArgs& a, cudaStream_t s) {
+    const QWeight& w = *a.w;
+    if (a.M == 0) return AEM_OK;
+    AEM_REQUIRE(a.M <= 4, "qgemm decode path: M=%lld > 4", (long long)a.M);
+    const int dev = current_device();
+    const int sms = sm_count(dev);
+    int* err = device_error_word(dev);
+    AEM_REQUIRE(err != nullptr, "qgemm: no device error word");
+    // at most M row groups hold rows
+    const int64_t busy = static_cast<int64_t>(a.group_rows ? std::min<int64_t>(a.G, a.M) : 1) * w.NT;
+    // split K across CTAs when partial sums may be added: float32 output
+    // without ReLU, and either an accumulating caller or a plain store into
+    // rows that are zeroed first (no row map)
+    const bool can_split = !a.out_bf16 && !a.relu && (a.atomic_add || a.rowmap == nullptr);
+    int64_t ks = 1;
+    if (can_split) {
+        ks = std::max<int64_t>(1, (8 * static_cast<int64_t>(sms) + busy - 1) / busy);
+        ks = std::min<int64_t>(ks, w.KT);
+    }
+    const int kper = static_cast<int>((w.KT + ks - 1) / ks);
+    ks = (w.KT + kper - 1) / kper;
+    const bool add = a.atomic_add || ks > 1;
+    if (ks > 1 && !a.atomic_add) {
+        // a plain store split over K: start the rows at zero, then add
+        AEM_TRY_CUDA(cudaMemset2DAsync(a.out, static_cast<size_t>(a.ldo) * 4, 0,
+                                       static_cast<size_t>(w.N) * 4, static_cast<size_t>(a.M), s));
+    }
+    const int64_t grid = static_cast<int64_t>(a.group_rows ? a.G : 1) * w.NT * ks;
+    AEM_REQUIRE(grid < (1ll << 31), "qgemm decode path: grid too large");
+    const int m_max = static_cast<int>(a.M);
+    auto go = [&](auto kern) {
+        kern<<<static_cast<unsigned>(grid), kDecodeThreads, 0, s>>>(
+            static_cast<const __nv_bfloat16*>(a.x_hi), static_cast<const __nv_bfloat16*>(a.x_lo),
+            w.q, w.scale, a.M, w.K, w.N, w.NT, w.KT, a.group_rows, a.group_base, a.wmod,
+            static_cast<int>(ks), kper, a.out, a.ldo, a.out_bf16 ? 1 : 0, a.relu ? 1 : 0,
+            add ? 1 : 0, a.rowmap, a.rowscale, err);
+    };
+    if (m_max <= 1) go(qgemm_decode_kernel<1>);
+    else if (m_max <= 2) go(qgemm_decode_kernel<2>);
+    else go(qgemm_decode_kernel<4>);
+    AEM_CHECK_LAUNCH();
+    count_launches(1);
+    return AEM_OK;
+}
 
 aem_status launch_split_bf16(const void* x, aem_dtype xd, int64_t count, void* hi, void* lo,
                              cudaStream_t s) {

@@ -520,6 +520,134 @@ def e2e_run(args, layer, world, rank, tl, dev, stream, barrier):
             "aem_ep_forward + pinned host copies on the same stream"}
 
 
+# ------------------------------------------------------------------ other configs
+FP32_OPS_NOMINAL = 148 * 128 * 1.965e9  # float32 lane-ops/s of the CUDA cores at max clock
+
+
+def run_suite(args):
+    """The path's other configurations, one JSON line each (1 GPU).
+
+    C1 gating sweep (EXACT mode: a float32 multiply and add per term):
+    T in {1,16,128,1024,8192}, D=4096, E=8 (top-2) and E=64 (top-6), x bf16
+    and float32.  C2 INT8 GEMM sweep: M in {1,8,64,512,4096}, K=4096,
+    N=14336, x bf16 and float32 (float32 = two bf16 MMAs, hi + lo).  C3
+    Mixtral-shaped MoE layer: d=4096, ffn=14336, E=8, top-2, no capacity
+    limit, T in {1,32,512,4096}, x bf16.  Every call is timed alone with CUDA
+    events on its stream after a 256 MiB write that flushes L2; the median of
+    the timed calls is reported.  Roofline: bytes and flops are the
+    algorithmic figures (unique bytes, 2*M*N*K flops); peaks are the measured
+    HBM copy bandwidth and burst bf16 GEMM rate, and for exact gating the
+    nominal float32 CUDA-core rate (148 SMs x 128 lanes x 1.965 GHz).
+    """
+    import numpy as np
+    import torch
+    from aethermoe_b200 import _lib
+    from aethermoe_b200.moe import MoELayer
+    _, bf16_burst, hbm, peak_src = measured_peaks()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    L = _lib.lib()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    reps = max(5, min(args.steps, 30))
+
+    def timed(fn):
+        for i in range(args.warmup):
+            fn(i)
+        pairs = []
+        for i in range(reps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn(i)
+            b.record(stream)
+            pairs.append((a, b))
+        torch.cuda.synchronize()
+        _lib.check(L.aem_device_status(None), "aem_device_status")
+        return statistics.median(a.elapsed_time(b) for a, b in pairs) * 1e-3  # seconds
+
+    def emit(suite, config, sec, bytes_, flops, bound, extra=None):
+        line = {"suite": suite, "config": config, "us": round(sec * 1e6, 2),
+                "bytes": bytes_, "flops": flops, "bound": bound,
+                "hbm_gbs": round(bytes_ / sec / 1e9, 1), "hbm_frac": round(bytes_ / sec / 1e9 / hbm, 3)}
+        if bound == "tensor":
+            line["tensor_tflops"] = round(flops / sec / 1e12, 1)
+            line["tensor_frac"] = round(flops / sec / 1e12 / bf16_burst, 3)
+        if bound == "fp32":
+            line["fp32_frac"] = round(flops / sec / FP32_OPS_NOMINAL, 3)
+        line["peaks"] = f"{peak_src}: hbm {hbm} GB/s, bf16 burst {bf16_burst} TFLOP/s"
+        if extra:
+            line.update(extra)
+        print(json.dumps(line), flush=True)
+
+    clocks = ClockSampler([0])
+    t_start = time.time()
+    rng = np.random.default_rng(0)
+    # ---- C1: gating sweep
+    D = 4096
+    for e, k in ((8, 2), (64, 6)):
+        w = (rng.normal(size=(D, e)) / np.sqrt(D)).astype(np.float32)
+        gate = _lib.Gate(w, np.zeros(e, np.float32), 0)
+        for xdt, sx, code in ((torch.bfloat16, 2, _lib.BF16), (torch.float32, 4, _lib.F32)):
+            for t in (1, 16, 128, 1024, 8192):
+                xs = [torch.randn(t, D, device=dev).to(xdt) for _ in range(2)]
+                idx = torch.empty((t, k), dtype=torch.int32, device=dev)
+                val = torch.empty((t, k), dtype=torch.float32, device=dev)
+                sec = timed(lambda i: _lib.check(L.aem_gating(
+                    gate.handle, xs[i % 2].data_ptr(), code, t, k, 0, _lib.GATING_EXACT,
+                    idx.data_ptr(), val.data_ptr(), sp), "aem_gating"))
+                bytes_ = t * D * sx + e * D * 4 + 4 * e + 8 * k * t
+                flops = 2 * t * D * e
+                emit("C1 gating", {"T": t, "D": D, "E": e, "k": k, "x": str(xdt).split(".")[-1],
+                                   "mode": "exact"}, sec, bytes_, flops,
+                     "fp32" if e == 64 else "hbm")
+                del xs
+        del gate
+    # ---- C2: INT8 GEMM sweep
+    K, N = 4096, 14336
+    q = torch.randint(-127, 128, (1, K, N), dtype=torch.int8, device=dev)
+    wq = _lib.DeviceQWeight(q, torch.full((1, N), 2.5e-4, device=dev))
+    del q
+    for xdt, sx, code in ((torch.bfloat16, 2, _lib.BF16), (torch.float32, 4, _lib.F32)):
+        for m in (1, 8, 64, 512, 4096):
+            xs = [torch.randn(m, K, device=dev).to(xdt) for _ in range(2)]
+            out = torch.empty((m, N), dtype=torch.float32, device=dev)
+            sec = timed(lambda i: _lib.check(L.aem_qgemm(wq.handle, 0, xs[i % 2].data_ptr(), code, m,
+                                                         out.data_ptr(), sp), "aem_qgemm"))
+            bytes_ = K * N + 4 * N + m * K * sx + 4 * m * N
+            emit("C2 int8 gemm", {"M": m, "K": K, "N": N, "x": str(xdt).split(".")[-1],
+                                  "mmas": 2 if sx == 4 else 1}, sec, bytes_, 2 * m * N * K,
+                 "hbm" if m <= 64 else "tensor")
+            del xs, out
+    del wq
+    # ---- C3: Mixtral-shaped single-GPU MoE layer
+    d, f, e, k = 4096, 14336, 8, 2
+    qu = torch.randint(-127, 128, (e, d, f), dtype=torch.int8, device=dev)
+    up = _lib.DeviceQWeight(qu, torch.full((e, f), 2.5e-4, device=dev))
+    del qu
+    qd = torch.randint(-127, 128, (e, f, d), dtype=torch.int8, device=dev)
+    down = _lib.DeviceQWeight(qd, torch.full((e, d), 2.5e-4, device=dev))
+    del qd
+    gw = (rng.normal(size=(d, e)) / np.sqrt(d)).astype(np.float32)
+    layer = MoELayer(gw, np.zeros(e, np.float32), up, None, down, None, k)
+    for t in (1, 32, 512, 4096):
+        xs = [torch.randn(t, d, device=dev).to(torch.bfloat16) for _ in range(2)]
+        out = torch.empty((t, d), dtype=torch.bfloat16, device=dev)
+        sec = timed(lambda i: layer.forward(xs[i % 2], out=out))
+        touched = min(e, t * k)
+        bytes_ = touched * 2 * d * f + 2 * t * d * 2 + d * e * 4
+        flops = t * k * 2 * (2 * d * f)
+        emit("C3 moe layer", {"T": t, "d": d, "ffn": f, "E": e, "k": k, "x": "bfloat16",
+                              "capacity": "unlimited"}, sec, bytes_, flops,
+             "hbm" if t <= 512 else "tensor", {"tokens_per_s": round(t / sec, 1)})
+        del xs, out
+    t_end = time.time()
+    clocks.stop()
+    print(json.dumps({"suite": "clocks", "clocks": clocks.summary(t_start, t_end)}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
@@ -532,9 +660,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep-pipeline", choices=["auto", "on", "off"], default="auto",
                     help="expert-parallel two-half pipeline (auto: off)")
+    ap.add_argument("--suite", action="store_true",
+                    help="instead of the headline step: one JSON line per gating, INT8 GEMM and "
+                         "Mixtral-shaped MoE-layer configuration (1 GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    if args.suite:
+        return run_suite(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -215,3 +215,101 @@ def test_grouped_ragged_tiles(cuda, tile, mode):
         want = base.astype(np.float64).copy()
         want[rmap] += ref * rscale[:, None].astype(np.float64)
         _close(out.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("mode", ["relu_bf16", "scaled_add"])
+def test_grouped_decode_sizes(cuda, mode):
+    """At most 4 rows (decode sizes) take the CUDA-core path: groups of 0-2
+    rows, a partial output-channel block, K not a multiple of 64."""
+    import torch
+    from aethermoe_b200 import _lib
+    rng = np.random.default_rng(31 + len(mode))
+    sizes = [0, 1, 2, 0, 1]
+    G, K, N = len(sizes), 200, 300
+    q = rng.integers(-127, 128, size=(G, K, N), dtype=np.int8)
+    s = (rng.random(size=(G, N)) * 1e-3 + 1e-4).astype(np.float32)
+    w = _lib.QWeight(q, s, 0)
+    rows = np.r_[0, np.cumsum(sizes)].astype(np.int32)
+    M = int(rows[-1])
+    x = O.bf16_round(rng.normal(size=(M, K)).astype(np.float32))
+    xt = torch.from_numpy((x.view(np.uint32) >> 16).astype(np.uint16).view(np.int16)).to(cuda)
+    xt = xt.view(torch.bfloat16)
+    rt = torch.from_numpy(rows).to(cuda)
+    ref = np.zeros((M, N))
+    for g in range(G):
+        a, b = rows[g], rows[g + 1]
+        ref[a:b] = x[a:b].astype(np.float64) @ (q[g].astype(np.float64) * s[g].astype(np.float64))
+    stream = torch.cuda.current_stream().cuda_stream
+    if mode == "relu_bf16":
+        out = torch.zeros((M, N), dtype=torch.bfloat16, device=cuda)
+        _lib.check(_lib.lib().aem_grouped_qgemm(w.handle, rt.data_ptr(), G, xt.data_ptr(), M,
+                                                out.data_ptr(), _lib.BF16, N, 1, 0, None, None,
+                                                0, 1, stream), "aem_grouped_qgemm")
+        torch.cuda.synchronize()
+        _close(out.float().cpu().numpy(), np.maximum(ref, 0.0), rtol=2 ** -8 + 1e-3, atol=1e-3)
+    else:
+        rmap = np.array([5, 2, 7, 2], np.int32)[:M]  # output row 2 receives two rows
+        rscale = (rng.random(M) + 0.5).astype(np.float32)
+        base = rng.normal(size=(8, N)).astype(np.float32)
+        out = torch.from_numpy(base.copy()).to(cuda)
+        # device copies held in names: a temporary's memory could be reused by
+        # the next argument before the kernel reads it
+        mt = torch.from_numpy(rmap).to(cuda)
+        st = torch.from_numpy(rscale).to(cuda)
+        _lib.check(_lib.lib().aem_grouped_qgemm(
+            w.handle, rt.data_ptr(), G, xt.data_ptr(), M, out.data_ptr(), _lib.F32, N, 0, 1,
+            mt.data_ptr(), st.data_ptr(), 0, 1, stream), "aem_grouped_qgemm")
+        torch.cuda.synchronize()
+        want = base.astype(np.float64).copy()
+        np.add.at(want, rmap, ref * rscale[:, None].astype(np.float64))
+        _close(out.cpu().numpy(), want)
+    _lib.check(_lib.lib().aem_device_status(None), "aem_device_status")
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 4096, 14336), (2, 448, 300), (3, 40, 130), (4, 200, 129)])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_decode_sizes_dense(qg, m, k, n, dtype):
+    """aem_qgemm with at most 4 rows: the CUDA-core path with K split across
+    CTAs (float32 plain store: rows zeroed, partial sums added)."""
+    rng = np.random.default_rng(m * 7 + k + n)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    q, s = O.quantize_int8((rng.normal(size=(k, n)) * 0.02).astype(np.float32))
+    if dtype == "bf16":
+        xf = O.bf16_round(x)
+        out = _bf16_gemm(q, s, (xf.view(np.uint32) >> 16).astype(np.uint16))
+    else:
+        xf = x
+        out = qg.fused_quantized_matmul(x, q, s)
+    _close(out, xf.astype(np.float64) @ O.dequantize_int8(q, s).astype(np.float64))
+
+
+@pytest.mark.parametrize("m", [16, 40, 64, 200, 1000])
+def test_repeated_launches_stay_consistent(cuda, m):
+    """Forty back-to-back launches per token tile (16 .. 256 rows): every
+    output equal to the first up to split-K reassociation, and no bounded wait
+    ran out.  Guards the ring
+    protocol (a parity wait that could read an older phase of a slot showed
+    up only in some launches)."""
+    import torch
+    from aethermoe_b200 import _lib
+    rng = np.random.default_rng(m)
+    K, N = 4096, 1536
+    q = rng.integers(-127, 128, size=(K, N), dtype=np.int8)
+    s = (rng.random(size=(1, N)) * 1e-3 + 1e-4).astype(np.float32)
+    w = _lib.QWeight(q, s, 0)
+    x = O.bf16_round(rng.normal(size=(m, K)).astype(np.float32))
+    xt = torch.from_numpy((x.view(np.uint32) >> 16).astype(np.uint16).view(np.int16)).to(cuda)
+    xt = xt.view(torch.bfloat16)
+    outs = [torch.empty((m, N), dtype=torch.float32, device=cuda) for _ in range(40)]
+    stream = torch.cuda.current_stream().cuda_stream
+    for o in outs:
+        _lib.check(_lib.lib().aem_qgemm(w.handle, 0, xt.data_ptr(), _lib.BF16, m, o.data_ptr(),
+                                        stream), "aem_qgemm")
+    torch.cuda.synchronize()
+    _lib.check(_lib.lib().aem_device_status(None), "aem_device_status")
+    first = outs[0].cpu().numpy()
+    _close(first, x.astype(np.float64) @ (q.astype(np.float64) * s.astype(np.float64)))
+    for o in outs[1:]:
+        # split-K adds partial sums with float32 atomics in any order: a few
+        # ulp of reassociation; stale operands would be off by O(1)
+        np.testing.assert_allclose(o.cpu().numpy(), first, rtol=1e-5, atol=1e-5)
