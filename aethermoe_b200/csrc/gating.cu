@@ -58,13 +58,13 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // Compile-time shape of one kernel configuration.
-template <int GROUP, int NSLOT, int TPG, int WARPS, typename XT>
+template <int GROUP, int NSLOT, int TPG, int WARPS, typename XT, int DKO = 0>
 struct GatingCfg {
     static constexpr int kThreads = WARPS * 32;
     static constexpr int GPW = 32 / GROUP;
     static constexpr int TOK = WARPS * GPW * TPG;  // tokens per CTA
     static constexpr int EPAD = GROUP * NSLOT;
-    static constexpr int DK_E = EPAD <= 64 ? 64 : (EPAD <= 128 ? 32 : 16);
+    static constexpr int DK_E = DKO ? DKO : (EPAD <= 64 ? 64 : (EPAD <= 128 ? 32 : 16));
     static constexpr int DK = (TOK * (DK_E + 4) * 4 > 36 * 1024) ? DK_E / 2 : DK_E;
     static constexpr int DK4 = DK / 4;
     // float32 activations of a chunk, token pairs interleaved: pair p's row
@@ -84,12 +84,62 @@ struct GatingCfg {
     static_assert(TPG % 2 == 0, "tokens are processed in pairs");
 };
 
-template <int GROUP, int NSLOT, int kTPG, int WARPS, typename XT, bool EXACT>
+// Top-k of one token's logits held by a group of GROUP lanes (lane le owns
+// experts le + GROUP*s; v = logit + bias, -FLT_MAX past E): ksel rounds of a
+// strict-greater maximum (lowest id on ties), every lane learns each winner,
+// lane 0 writes the index and exp(logit - max); the first k are normalised
+// by their float32 sum in selection order.
+template <int GROUP, int NSLOT>
+__device__ __forceinline__ void topk_select(float (&v)[NSLOT], int le, unsigned gmask, int64_t tg,
+                                            int64_t N, int E, int k, int ksel,
+                                            int32_t* __restrict__ idx_out,
+                                            float* __restrict__ val_out) {
+    float m = 0.0f, sum = 0.0f;
+    for (int kk = 0; kk < ksel; ++kk) {
+        float best = -INFINITY;
+        int beste = 0x7FFFFFFF;
+#pragma unroll
+        for (int s = 0; s < NSLOT; ++s) {
+            const int e = le + GROUP * s;
+            if (e < E && v[s] > best) {  // strict: lowest id wins ties within the lane
+                best = v[s];
+                beste = e;
+            }
+        }
+#pragma unroll
+        for (int off = GROUP / 2; off >= 1; off >>= 1) {
+            const float ob = __shfl_xor_sync(gmask, best, off, GROUP);
+            const int oe = __shfl_xor_sync(gmask, beste, off, GROUP);
+            if (ob > best || (ob == best && oe < beste)) {
+                best = ob;
+                beste = oe;
+            }
+        }
+        // remove the winner from its owner lane
+#pragma unroll
+        for (int s = 0; s < NSLOT; ++s)
+            if (le + GROUP * s == beste) v[s] = -INFINITY;
+        if (kk == 0) m = best;
+        const float ev = kk < k ? expf(best - m) : 0.0f;
+        if (kk < k) sum = __fadd_rn(sum, ev);
+        if (le == 0 && tg < N) {
+            idx_out[tg * ksel + kk] = beste;
+            if (kk < k) val_out[tg * k + kk] = ev;
+        }
+    }
+    __syncwarp(gmask);
+    if (tg < N)
+        for (int kk = le; kk < k; kk += GROUP)
+            val_out[tg * k + kk] = __fdiv_rn(val_out[tg * k + kk], sum);
+    __syncwarp(gmask);
+}
+
+template <int GROUP, int NSLOT, int kTPG, int WARPS, typename XT, bool EXACT, int DKO = 0>
 __global__ void __launch_bounds__(WARPS * 32)
     gating_kernel(const XT* __restrict__ x, const float4* __restrict__ wpk,
                   const float* __restrict__ bias, int64_t N, int D, int E, int k, int ksel,
                   int32_t* __restrict__ idx_out, float* __restrict__ val_out) {
-    using C = GatingCfg<GROUP, NSLOT, kTPG, WARPS, XT>;
+    using C = GatingCfg<GROUP, NSLOT, kTPG, WARPS, XT, DKO>;
     constexpr int kThreads = C::kThreads;
     constexpr int GPW = C::GPW;
     constexpr int TOK = C::TOK;
@@ -134,7 +184,7 @@ __global__ void __launch_bounds__(WARPS * 32)
     auto issue = [&](int c) {
         if (c < nchunks) {
             const int st = c % kStages;
-            const float4* wsrc = wpk + static_cast<int64_t>(c) * WST;  // Dpad covers every chunk
+            const float4* wsrc = wpk + static_cast<int64_t>(c) * WST;  // Dpad: whole chunks of <= 256
             float4* wdst = wring + st * WST;
             for (int i = tid; i < WST; i += kThreads) cp_async_16(wdst + i, wsrc + i, 16);
             if (xvec) {
@@ -245,55 +295,16 @@ __global__ void __launch_bounds__(WARPS * 32)
             const float lg = (i & 1) ? acc[i >> 1][s].y : acc[i >> 1][s].x;
             v[s] = e < E ? __fadd_rn(lg, bv[s]) : -FLT_MAX;
         }
-        // every lane of the group learns each winner; lane 0 of the group
-        // writes it (weight un-normalised), then the group normalises
-        float m = 0.0f, sum = 0.0f;
-        for (int kk = 0; kk < ksel; ++kk) {
-            float best = -INFINITY;
-            int beste = 0x7FFFFFFF;
-#pragma unroll
-            for (int s = 0; s < NSLOT; ++s) {
-                const int e = le + GROUP * s;
-                if (e < E && v[s] > best) {  // strict: lowest id wins ties within the lane
-                    best = v[s];
-                    beste = e;
-                }
-            }
-#pragma unroll
-            for (int off = GROUP / 2; off >= 1; off >>= 1) {
-                const float ob = __shfl_xor_sync(gmask, best, off, GROUP);
-                const int oe = __shfl_xor_sync(gmask, beste, off, GROUP);
-                if (ob > best || (ob == best && oe < beste)) {
-                    best = ob;
-                    beste = oe;
-                }
-            }
-            // remove the winner from its owner lane
-#pragma unroll
-            for (int s = 0; s < NSLOT; ++s)
-                if (le + GROUP * s == beste) v[s] = -INFINITY;
-            if (kk == 0) m = best;
-            const float ev = kk < k ? expf(best - m) : 0.0f;
-            if (kk < k) sum = __fadd_rn(sum, ev);
-            if (le == 0 && tg < N) {
-                idx_out[tg * ksel + kk] = beste;
-                if (kk < k) val_out[tg * k + kk] = ev;
-            }
-        }
-        __syncwarp(gmask);
-        if (tg < N)
-            for (int kk = le; kk < k; kk += GROUP)
-                val_out[tg * k + kk] = __fdiv_rn(val_out[tg * k + kk], sum);
-        __syncwarp(gmask);
+        topk_select<GROUP, NSLOT>(v, le, gmask, tg, N, E, k, ksel, idx_out, val_out);
     }
 }
 
-template <int GROUP, int NSLOT, int TPG, typename XT, bool EXACT, int WARPS = kWarps>
+template <int GROUP, int NSLOT, int TPG, typename XT, bool EXACT, int WARPS = kWarps, int DKO = 0>
 cudaError_t launch_one(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
                        float* val, cudaStream_t s) {
-    using C = GatingCfg<GROUP, NSLOT, TPG, WARPS, XT>;
+    using C = GatingCfg<GROUP, NSLOT, TPG, WARPS, XT, DKO>;
     const int64_t blocks = (N + C::TOK - 1) / C::TOK;
-    auto kern = gating_kernel<GROUP, NSLOT, TPG, WARPS, XT, EXACT>;
+    auto kern = gating_kernel<GROUP, NSLOT, TPG, WARPS, XT, EXACT, DKO>;
     if (C::SMEM > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(
             kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM));
@@ -308,6 +319,18 @@ cudaError_t launch_one(const Gate& g, const void* x, int64_t N, int k, int ksel,
 template <typename XT, bool EXACT>
 cudaError_t dispatch_e(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
                        float* val, cudaStream_t s) {
+    // Few tokens through a narrow gate: few CTAs, each walking all of D, so
+    // the time is the number of chunk rounds; 256-wide chunks (a 2-8 KB
+    // weight stage) take a quarter of the rounds (154 -> 65 us at D=4096,
+    // E=8).  Wider gates keep 64-wide chunks: a 64 KB stage lands slower
+    // than the barriers it saves (78 -> 94 us at E=64).
+    if (N <= 1024) {
+        switch (g.Epad) {
+            case 8: return launch_one<8, 1, 2, XT, EXACT, 4, 256>(g, x, N, k, ksel, idx, val, s);
+            case 16: return launch_one<16, 1, 2, XT, EXACT, 4, 256>(g, x, N, k, ksel, idx, val, s);
+            default: break;
+        }
+    }
     // Many tokens: 8 tokens per lane group halves the weight loads per
     // multiply-add; fewer: 4, for more CTAs.
     if (N >= 12288) {
@@ -436,7 +459,7 @@ aem_status aem_gate_pack(const float* gate_weight, const float* gate_bias, int64
     g->D = D;
     g->E = E;
     g->Epad = aem::gate_epad(E);
-    g->Dpad = (D + 63) / 64 * 64;
+    g->Dpad = (D + 255) / 256 * 256;  // a whole number of the widest chunk (256)
     float* tmp_w = nullptr;
     float* tmp_b = nullptr;
     aem_status st = AEM_OK;

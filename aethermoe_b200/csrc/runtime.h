@@ -71,7 +71,8 @@ struct Context {
 // values of each expert are contiguous and experts follow each other, so a
 // chunk of d is one contiguous block that lands in shared memory as is.
 // Epad is E rounded up to the kernel's lane-group width (8/16/32/64/128/256),
-// Dpad is D rounded up to 64; padding is zero.  bias [Epad], zero padded.
+// Dpad is D rounded up to 256 (the widest chunk a gating kernel reads);
+// padding is zero.  bias [Epad], zero padded.
 struct Gate {
     int device = 0;
     int64_t D = 0, E = 0, Dpad = 0, Epad = 0;
