@@ -84,11 +84,27 @@ struct GatingCfg {
     static_assert(TPG % 2 == 0, "tokens are processed in pairs");
 };
 
+// Selection key of a logit in np.argmax order: every NaN ranks above every
+// number (np.argmax returns the first NaN), -0.0 ranks equal to +0.0, and
+// otherwise the float order; the low word (0xFFFFFFFF - expert) makes the
+// lowest expert id win between equal keys.  Keys of real experts are > 0.
+__device__ __forceinline__ uint64_t select_key(float v, int e) {
+    uint32_t u = __float_as_uint(__fadd_rn(v, 0.0f));  // -0.0 + 0.0 = +0.0
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);     // monotone map of the float order
+    if (v != v) u = 0xFFFFFFFFu;                         // NaN above +inf
+    return (static_cast<uint64_t>(u) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(e));
+}
+
 // Top-k of one token's logits held by a group of GROUP lanes (lane le owns
-// experts le + GROUP*s; v = logit + bias, -FLT_MAX past E): ksel rounds of a
-// strict-greater maximum (lowest id on ties), every lane learns each winner,
-// lane 0 writes the index and exp(logit - max); the first k are normalised
-// by their float32 sum in selection order.
+// experts le + GROUP*s; v = logit + bias): ksel rounds of np.argmax over the
+// row (prototype/math_proto.py:38-42; for finite logits the strict-greater
+// scan of fused_gating_metal.py:284-293, lowest id on ties), every lane
+// learns each winner, lane 0 writes the index and exp(value - first value).
+// Like the reference, a winner is not removed but overwritten with -inf, so a
+// row with fewer than ksel logits above -inf selects its lowest -inf id
+// again, and the value recorded is the row's current one (NaN for a NaN, -inf
+// for a repeat).  The first k are normalised by their float32 sum in
+// selection order.
 template <int GROUP, int NSLOT>
 __device__ __forceinline__ void topk_select(float (&v)[NSLOT], int le, unsigned gmask, int64_t tg,
                                             int64_t N, int E, int k, int ksel,
@@ -96,26 +112,28 @@ __device__ __forceinline__ void topk_select(float (&v)[NSLOT], int le, unsigned 
                                             float* __restrict__ val_out) {
     float m = 0.0f, sum = 0.0f;
     for (int kk = 0; kk < ksel; ++kk) {
-        float best = -INFINITY;
-        int beste = 0x7FFFFFFF;
+        uint64_t bkey = 0;  // below every real expert's key
+        float best = 0.0f;
 #pragma unroll
         for (int s = 0; s < NSLOT; ++s) {
             const int e = le + GROUP * s;
-            if (e < E && v[s] > best) {  // strict: lowest id wins ties within the lane
+            const uint64_t key = select_key(v[s], e);
+            if (e < E && key > bkey) {
+                bkey = key;
                 best = v[s];
-                beste = e;
             }
         }
 #pragma unroll
         for (int off = GROUP / 2; off >= 1; off >>= 1) {
+            const uint64_t ok = __shfl_xor_sync(gmask, bkey, off, GROUP);
             const float ob = __shfl_xor_sync(gmask, best, off, GROUP);
-            const int oe = __shfl_xor_sync(gmask, beste, off, GROUP);
-            if (ob > best || (ob == best && oe < beste)) {
+            if (ok > bkey) {
+                bkey = ok;
                 best = ob;
-                beste = oe;
             }
         }
-        // remove the winner from its owner lane
+        const int beste = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(bkey));
+        // overwrite the winner in its owner lane (np.argmax's `local[best] = -inf`)
 #pragma unroll
         for (int s = 0; s < NSLOT; ++s)
             if (le + GROUP * s == beste) v[s] = -INFINITY;

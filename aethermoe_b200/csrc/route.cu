@@ -13,7 +13,6 @@
 // kernels, keyed by the effective expert, produce the MoE permutation that
 // groups units by expert for the grouped GEMM.
 #include <algorithm>
-#include <mutex>
 
 #include "common.cuh"
 #include "route.h"
@@ -403,27 +402,20 @@ static_assert(kStaticBytes == AEM_ROUTE_STATIC_SCRATCH_BYTES, "scratch size in a
 
 static __device__ __align__(256) unsigned char g_route_scratch[kStaticBytes];
 
-std::mutex g_route_scratch_mutex;
-void* g_route_scratch_addr[64] = {nullptr};
-
-// Device address of g_route_scratch on the current device, looked up once
-// per device (host code only sees a stand-in symbol, never the address).
+// Device address of g_route_scratch on the current device.  Host code only
+// sees a stand-in symbol, never the address, so it is looked up with the
+// device current -- on every call: the lookup allocates nothing, and an
+// address cached across calls would dangle after cudaDeviceReset (the
+// module, and with it the array, is loaded again into the new context).
 aem_status route_scratch_address(void** out) {
-    int dev = 0;
-    AEM_TRY_CUDA(cudaGetDevice(&dev));
-    AEM_REQUIRE(dev >= 0 && dev < 64, "aem_capacity_route_static: device %d out of range", dev);
-    std::lock_guard<std::mutex> lk(g_route_scratch_mutex);
-    if (!g_route_scratch_addr[dev]) {
-        void* p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_route_scratch);
-        if (e != cudaSuccess || p == nullptr) {
-            set_error("aem_capacity_route_static: cudaGetSymbolAddress failed: %s",
-                      cudaGetErrorString(e));
-            return AEM_ECUDA;
-        }
-        g_route_scratch_addr[dev] = p;
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_route_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+        set_error("aem_capacity_route_static: cudaGetSymbolAddress failed: %s",
+                  cudaGetErrorString(e));
+        return AEM_ECUDA;
     }
-    *out = g_route_scratch_addr[dev];
+    *out = p;
     return AEM_OK;
 }
 

@@ -112,6 +112,11 @@ aem_status aem_gate_free(aem_gate_t gate);
  * strict-greater max extraction (ties -> lowest expert id), softmax over the
  * k selected logits.  Replaces the kernel launch of fused_gating,
  * src/kernels/fused_gating_metal.py:361-435 (MSL body :236-307).
+ * Non-finite logits select as np.argmax in the reference's specification
+ * (prototype/math_proto.py:38-42): NaN ranks above every number (the first
+ * NaN first), and a winner is overwritten with -inf rather than removed, so
+ * a row with fewer than k + k_extra logits above -inf repeats its lowest
+ * -inf id; every written id is in [0, E).
  *   hidden   device [N, D], dtype AEM_F32 or AEM_BF16
  *   out_idx  device int32 [N, k + k_extra]: descending-logit expert ids; the
  *            k_extra (0 or 1) trailing id is the next choice (the capacity
@@ -214,9 +219,10 @@ aem_status aem_capacity_route(const uint32_t* primary, const uint32_t* secondary
  * array of AEM_ROUTE_STATIC_SCRATCH_BYTES in the library's device memory,
  * held on every GPU that loads the library until the process exits.
  *   - n > AEM_ROUTE_STATIC_MAX_UNITS (or E > AEM_MAX_EXPERTS) -> AEM_EINVAL.
- *   - The first call on a device looks the array's address up on that
- *     device (with the device current); make that first call before any
- *     stream capture.
+ *   - Every call looks the array's address up on the current device (a
+ *     lookup that allocates nothing; the first one on a device loads the
+ *     library's device code there), so a cudaDeviceReset between calls is
+ *     safe; make the first call on a device before any stream capture.
  *   - Every call on a device shares the one array and it keeps the last
  *     call's contents (each call resets what must start at zero): calls
  *     that overlap on the GPU -- on different streams or from different

@@ -59,24 +59,30 @@ def gating_logits_seq(hidden, gate_weight, gate_bias):
     return (acc + b[None, :]).astype(np.float32)
 
 
-def topk_strict(logits, k):
+def topk_strict(logits, k, return_values=False):
     """Iterative strict-``>`` max extraction, ties to the lowest expert id.
 
     Follows the kernel's selection loop ``src/kernels/fused_gating_metal.py:281-293``
-    and its NumPy twin ``prototype/math_proto.py:38-43`` (``np.argmax`` returns
-    the lowest index of equal maxima).  Returns int64 ``[N, k]`` ordered by
-    descending logit.
+    and its NumPy twin ``prototype/math_proto.py:38-43``: ``np.argmax`` (the
+    lowest index of equal maxima; the first NaN when the row holds one), then
+    the winner is overwritten with ``-inf`` -- it is not removed, so a row with
+    fewer than ``k`` entries above ``-inf`` selects its lowest ``-inf`` index
+    again.  Returns int64 ``[N, k]`` ordered by descending logit and, with
+    ``return_values``, the float32 values recorded at each selection (the
+    row's current entry, as ``math_proto.py:40`` records ``local[best_idx]``).
     """
     local = np.array(logits, dtype=np.float32, copy=True)
     n, e = local.shape
     assert 0 <= k <= e
     out = np.zeros((n, k), dtype=np.int64)
+    vals = np.zeros((n, k), dtype=np.float32)
     rows = np.arange(n)
     for kk in range(k):
         best = np.argmax(local, axis=1)
         out[:, kk] = best
+        vals[:, kk] = local[rows, best]
         local[rows, best] = -np.inf
-    return out
+    return (out, vals) if return_values else out
 
 
 def softmax_selected(vals):
@@ -101,9 +107,8 @@ def fused_gating(hidden, gate_weight, gate_bias, k, extra=0):
     logits = gating_logits_seq(hidden, gate_weight, gate_bias)
     e = logits.shape[1]
     ksel = min(k + extra, e)
-    idx = topk_strict(logits, ksel)
-    sel = np.take_along_axis(logits, idx[:, :k], axis=1)
-    return idx.astype(np.int32), softmax_selected(sel)
+    idx, sel = topk_strict(logits, ksel, return_values=True)
+    return idx.astype(np.int32), softmax_selected(sel[:, :k])
 
 
 def reference_gating(hidden, gate_weight, gate_bias, k):

@@ -70,6 +70,37 @@ def near_tie_gating_cases():
             for n, d, e, k, seed in NEAR_TIE_GATING}
 
 
+def nonfinite_gating_cases():
+    """Rows whose logits hold NaN, +inf or -inf (through the bias or the
+    activations).  The reference's selection is np.argmax
+    (prototype/math_proto.py:38-42): the first NaN wins, ties go to the lowest
+    id, and a winner is overwritten with -inf rather than removed."""
+    c = {}
+    h, w, b = _gating_inputs(np.random.default_rng(21), 6, 16, 8)
+    b[[3, 5]] = np.nan
+    c["nan_bias"] = (h, w, b, 3)
+    h, w, b = _gating_inputs(np.random.default_rng(22), 4, 16, 8)
+    b[:] = -np.inf
+    c["neg_inf_all"] = (h, w, b, 3)
+    h, w, b = _gating_inputs(np.random.default_rng(23), 4, 16, 8)
+    b[:] = -np.inf
+    b[4] = 0.5
+    c["neg_inf_but_one"] = (h, w, b, 3)
+    h, w, b = _gating_inputs(np.random.default_rng(24), 4, 16, 8)
+    b[[1, 6]] = np.inf
+    c["pos_inf_pair"] = (h, w, b, 3)
+    h, w, b = _gating_inputs(np.random.default_rng(25), 5, 16, 8)
+    h[1, 7] = np.nan
+    h[3, :] = np.nan
+    c["nan_rows"] = (h, w, b, 3)
+    h, w, b = _gating_inputs(np.random.default_rng(26), 5, 16, 8)
+    w[0, :] = np.array([1.0, -1.0, 0.0, 2.0, -0.5, 0.0, 1.0, -3.0], np.float32)
+    h[0, 0] = np.inf   # logits +inf, -inf or NaN (inf * 0) by the sign of w[0, e]
+    h[2, 0] = -np.inf
+    c["inf_activation"] = (h, w, b, 4)
+    return c
+
+
 def c0_inputs():
     """CPU-runnable config: x [256,512], W_gate [512,8] ~ N(0,1/d), bias 0,
     expert weight [512,1024] ~ N(0,0.02); one generator, seed 0."""

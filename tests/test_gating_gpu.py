@@ -38,6 +38,29 @@ def test_exact_matches_reference_simulation(shim, golden, name):
     np.testing.assert_allclose(val, golden["gating"][f"{name}/sim_val"], rtol=0, atol=1e-6)
 
 
+@pytest.mark.parametrize("mode", ["exact", "fast"])
+@pytest.mark.parametrize("name", sorted(cases.nonfinite_gating_cases()))
+def test_nonfinite_logits_match_reference_simulation(cuda, golden, name, mode):
+    """NaN / +-inf logits select like np.argmax in fused_kernel_simulation
+    (prototype/math_proto.py:38-42): first NaN first, lowest id on ties, a
+    winner overwritten by -inf (so -inf ids repeat); values NaN-equal."""
+    from aethermoe_b200 import _lib
+    from aethermoe_b200.kernels.fused_gating_metal import gating
+    h, w, b, k = cases.nonfinite_gating_cases()[name]
+    md = _lib.GATING_EXACT if mode == "exact" else _lib.GATING_FAST
+    idx, val = gating(h, w, b, k, mode=md)
+    np.testing.assert_array_equal(idx, golden["gating"][f"{name}/sim_idx"])
+    np.testing.assert_allclose(val, golden["gating"][f"{name}/sim_val"], rtol=0, atol=1e-6,
+                               equal_nan=True)
+    assert idx.min() >= 0 and idx.max() < w.shape[1]
+    # the next choice for capacity rerouting follows the same order
+    with np.errstate(invalid="ignore"):
+        oidx, oval = O.fused_gating(h, w, b, k, extra=1)
+    idx2, val2 = gating(h, w, b, k, mode=md, k_extra=1)
+    np.testing.assert_array_equal(idx2, oidx)
+    np.testing.assert_allclose(val2, oval, rtol=0, atol=1e-6, equal_nan=True)
+
+
 def test_exact_c0(shim, golden):
     fg, _ = shim
     h, w, b, k = cases.c0_gating_inputs()
