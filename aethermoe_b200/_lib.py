@@ -134,6 +134,7 @@ _SIGS = {
     "aem_capacity_route_static": (_int, [_vp, _vp, _vp, _i64, _int, _u64, _vp, _vp]),
     "aem_kernel_launches": (ctypes.c_uint64, []),
     "aem_moe_profile": (_int, [_vp, _int]),
+    "aem_moe_set_hidden_dtype": (_int, [_vp, _int]),
     "aem_moe_profile_read": (_int, [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64)]),
     "aem_ep_profile": (_int, [_vp, _int]),
     "aem_ep_profile_read": (_int, [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64)]),

@@ -6,10 +6,16 @@
 //   2. capacity routing         -> effective expert per (token, slot) unit,
 //                                  slot-major batch_position u = j*T + t
 //   3. expert-grouped layout    -> rows grouped by effective expert
-//   4. gather                   -> X [U, d] bf16 in grouped order
-//   5. grouped up GEMM + ReLU   -> H [U, ffn] bf16
+//   4. gather                   -> X [U, d] in grouped order: bf16, or for
+//                                  float32 x the bf16 pair hi + lo (x = hi + lo
+//                                  to about 16 significant bits)
+//   5. grouped up GEMM + ReLU   -> H [U, ffn]: bf16, or the bf16 pair hi + lo
 //   6. grouped down GEMM + combine -> out[t] += val[t, j] * y  (float32 red.add
 //                                  from the GEMM epilogue; bf16 output converted after)
+// A split operand costs a second MMA per K step (hi and lo against the same
+// exact bf16 copy of the int8 weights), so float32 callers get the
+// float32-activation contract of fused_quantized_matmul
+// (src/kernels/quantized_gemm.py:184-226) at the price of twice the MMAs.
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -23,10 +29,12 @@ namespace aem {
 
 namespace {
 
-// X[dest] = bf16(x[src[dest]]): one warp per row, 16-byte vectors when aligned.
+// X[dest] = bf16(x[src[dest]]) (and, for float32 x with lo != nullptr,
+// lo[dest] = bf16(x - X[dest])): one warp per row, 16-byte vectors when aligned.
 template <typename XT>
 __global__ void gather_rows_kernel(const XT* __restrict__ x, const int32_t* __restrict__ src,
-                                   int64_t rows, int64_t d, __nv_bfloat16* __restrict__ out) {
+                                   int64_t rows, int64_t d, __nv_bfloat16* __restrict__ out,
+                                   __nv_bfloat16* __restrict__ lo) {
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     const int lane = threadIdx.x & 31;
     for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -43,6 +51,7 @@ __global__ void gather_rows_kernel(const XT* __restrict__ x, const int32_t* __re
                 for (int64_t i = lane; i < d; i += 32) o[i] = in[i];
             }
         } else {
+            __nv_bfloat16* ol = lo ? lo + r * d : nullptr;
             if ((d & 3) == 0) {
                 const float4* vi = reinterpret_cast<const float4*>(in);
                 uint2* vo = reinterpret_cast<uint2*>(o);
@@ -54,9 +63,21 @@ __global__ void gather_rows_kernel(const XT* __restrict__ x, const int32_t* __re
                     u.x = *reinterpret_cast<uint32_t*>(&a);
                     u.y = *reinterpret_cast<uint32_t*>(&b);
                     vo[i] = u;
+                    if (ol) {
+                        const float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
+                        __nv_bfloat162 la = __floats2bfloat162_rn(f.x - fa.x, f.y - fa.y);
+                        __nv_bfloat162 lb = __floats2bfloat162_rn(f.z - fb.x, f.w - fb.y);
+                        u.x = *reinterpret_cast<uint32_t*>(&la);
+                        u.y = *reinterpret_cast<uint32_t*>(&lb);
+                        reinterpret_cast<uint2*>(ol)[i] = u;
+                    }
                 }
             } else {
-                for (int64_t i = lane; i < d; i += 32) o[i] = __float2bfloat16_rn(in[i]);
+                for (int64_t i = lane; i < d; i += 32) {
+                    const __nv_bfloat16 h = __float2bfloat16_rn(in[i]);
+                    o[i] = h;
+                    if (ol) ol[i] = __float2bfloat16_rn(in[i] - __bfloat162float(h));
+                }
             }
         }
     }
@@ -118,15 +139,17 @@ unsigned grid_for(int64_t work, int per_block) {
 }  // namespace
 
 aem_status gather_rows(const void* x, aem_dtype xd, const int32_t* src, int64_t rows, int64_t d,
-                       void* out, cudaStream_t s) {
+                       void* out, cudaStream_t s, void* out_lo) {
     if (rows == 0) return AEM_OK;
     const unsigned g = grid_for(rows, 8);
     if (xd == AEM_BF16)
         gather_rows_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(
-            static_cast<const __nv_bfloat16*>(x), src, rows, d, static_cast<__nv_bfloat16*>(out));
+            static_cast<const __nv_bfloat16*>(x), src, rows, d, static_cast<__nv_bfloat16*>(out),
+            nullptr);
     else
         gather_rows_kernel<float><<<g, 256, 0, s>>>(static_cast<const float*>(x), src, rows, d,
-                                                    static_cast<__nv_bfloat16*>(out));
+                                                    static_cast<__nv_bfloat16*>(out),
+                                                    static_cast<__nv_bfloat16*>(out_lo));
     AEM_CHECK_LAUNCH();
     count_launches(1);
     return AEM_OK;
@@ -157,6 +180,23 @@ aem_status combine_rows(const float* y, int64_t T, int k, int64_t d, void* out, 
 }
 
 // ------------------------------------------------------------------ Moe
+aem_status Moe::reserve_split(int64_t T) {
+    if (T <= split_cap && split_buf) return AEM_OK;
+    if (split_buf) {
+        cudaDeviceSynchronize();
+        cudaFree(split_buf);
+        split_buf = nullptr;
+        split_cap = 0;
+    }
+    const int64_t U = T * cfg.top_k;
+    const size_t ox = align_up(2 * static_cast<size_t>(U) * cfg.d_model, 256);
+    AEM_TRY_CUDA(cudaMalloc(&split_buf, ox + 2 * static_cast<size_t>(U) * cfg.d_ffn));
+    xperm_lo = split_buf;
+    h_lo = static_cast<char*>(split_buf) + ox;
+    split_cap = T;
+    return AEM_OK;
+}
+
 aem_status Moe::reserve(int64_t T, bool expert_buffers) {
     if (T <= T_cap && buf) return AEM_OK;
     if (buf) {
@@ -230,14 +270,21 @@ aem_status Moe::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_d
     ra.rowmap = rowmap;
     ra.rowscale = rowscale;
     AEM_TRY(route_moe(ra, s));
-    AEM_TRY(gather_rows(x, xd, src_token, U, d, xperm, s));
+    // operand precision: float32 x enters the up GEMM as a bf16 pair; the
+    // hidden activation is a pair when hidden_dtype says so (by default when x
+    // is float32)
+    const bool split_x = xd == AEM_F32;
+    const bool split_h = hidden_dtype < 0 ? split_x : hidden_dtype == AEM_F32;
+    if (split_x || split_h) AEM_TRY(reserve_split(T));
+    AEM_TRY(gather_rows(x, xd, src_token, U, d, xperm, s, split_x ? xperm_lo : nullptr));
     prof.end(AEM_PHASE_ROUTE, s);
-    AEM_TRY(expert_ffn(T, U, out, od, s));
+    AEM_TRY(expert_ffn(T, U, out, od, s, split_x, split_h));
     prof.step();
     return AEM_OK;
 }
 
-aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaStream_t s) {
+aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaStream_t s,
+                           bool split_x, bool split_h) {
     const int k = cfg.top_k, E = cfg.num_experts;
     const int64_t d = cfg.d_model, f = cfg.d_ffn;
     GemmArgs up_a;
@@ -248,7 +295,9 @@ aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaSt
     up_a.M = U;
     up_a.max_rows = U;
     up_a.x_hi = xperm;
+    up_a.x_lo = split_x ? xperm_lo : nullptr;
     up_a.out = h;
+    up_a.out_lo = split_h ? h_lo : nullptr;
     up_a.out_bf16 = true;
     up_a.ldo = f;
     up_a.relu = true;
@@ -267,6 +316,7 @@ aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaSt
     dn.M = U;
     dn.max_rows = U;
     dn.x_hi = h;
+    dn.x_lo = split_h ? h_lo : nullptr;
     dn.out = acc;
     dn.ldo = d;
     dn.rowmap = src_token;
@@ -336,6 +386,7 @@ aem_status aem_moe_free(aem_moe_t moe) {
     cudaSetDevice(m->gate->device);
     cudaDeviceSynchronize();
     cudaFree(m->buf);
+    cudaFree(m->split_buf);
     aem::seam_free(m);
     delete m;
     return AEM_OK;
@@ -370,6 +421,14 @@ aem_status aem_moe_forward_host(aem_context_t ctx, aem_moe_t moe, const void* x,
     AEM_TRY(m->forward(d, x_dtype, T, d + o1, out_dtype, c->stream));
     AEM_TRY_CUDA(cudaMemcpyAsync(out, d + o1, ob, cudaMemcpyDeviceToHost, c->stream));
     return aem::check_device_errors(c->stream, "aem_moe_forward_host");
+}
+
+aem_status aem_moe_set_hidden_dtype(aem_moe_t moe, int hidden_dtype) {
+    AEM_REQUIRE(moe != nullptr, "aem_moe_set_hidden_dtype: NULL layer");
+    AEM_REQUIRE(hidden_dtype == -1 || hidden_dtype == AEM_F32 || hidden_dtype == AEM_BF16,
+                "aem_moe_set_hidden_dtype: %d is not -1, AEM_F32 or AEM_BF16", hidden_dtype);
+    reinterpret_cast<aem::Moe*>(moe)->hidden_dtype = hidden_dtype;
+    return AEM_OK;
 }
 
 aem_status aem_moe_profile(aem_moe_t moe, int enable) {

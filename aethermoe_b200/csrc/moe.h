@@ -11,7 +11,7 @@
 namespace aem {
 
 aem_status gather_rows(const void* x, aem_dtype xd, const int32_t* src, int64_t rows, int64_t d,
-                       void* out, cudaStream_t s);
+                       void* out, cudaStream_t s, void* out_lo = nullptr);
 aem_status combine_rows(const float* y, int64_t T, int k, int64_t d, void* out, aem_dtype od,
                         cudaStream_t s);
 
@@ -34,6 +34,13 @@ struct Moe {
     void* xperm = nullptr;  // bf16 [U, d]
     void* h = nullptr;      // bf16 [U, ffn]
     float* y = nullptr;     // f32 [T*k, d]
+    // split-precision operands (float32 x, float32-class hidden activation):
+    // the low halves of the bf16 pairs, allocated on the first step that needs them
+    int hidden_dtype = -1;  // -1: follow x's dtype; AEM_F32: bf16 pair; AEM_BF16: bf16
+    void* split_buf = nullptr;
+    int64_t split_cap = 0;
+    void* xperm_lo = nullptr;  // bf16 [U, d]
+    void* h_lo = nullptr;      // bf16 [U, ffn]
     PhaseProfiler prof;
     // scheduler seam (seam.cu): staged rows of one iteration and its slice table
     struct SeamStage* seam = nullptr;
@@ -41,11 +48,13 @@ struct Moe {
     // Routing buffers for T tokens, plus the expert-FFN buffers (xperm, h, y)
     // unless expert_buffers is false (the expert-parallel layer has its own).
     aem_status reserve(int64_t T, bool expert_buffers = true);
+    aem_status reserve_split(int64_t T);
     aem_status forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_dtype od,
                        cudaStream_t s);
     // Grouped up GEMM + ReLU, grouped down GEMM (scaled by the gate weight,
     // scattered to row t*k+j), combine -- on xperm/starts/rowmap/rowscale.
-    aem_status expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaStream_t s);
+    aem_status expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaStream_t s,
+                          bool split_x = false, bool split_h = false);
 };
 
 void seam_free(Moe* m);  // releases the scheduler seam's buffers (seam.cu)

@@ -89,6 +89,7 @@ struct TcParams {
     const int8_t* wq;       // tiled int8 weights [Gw][NT][KT][128][64]
     int64_t NT, KT;
     void* out;
+    void* out_lo;           // bf16 out only: low half of a split output (nullable)
     int64_t ldo;
     int out_bf16;
     int relu;
@@ -518,8 +519,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         float v = __uint_as_float(r[j]) * sc * rs;
                         if (p.relu) v = fmaxf(v, 0.0f);
                         if (p.out_bf16) {
-                            reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + n] =
-                                __float2bfloat16_rn(v);
+                            const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+                            reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + n] = hi;
+                            if (p.out_lo)
+                                reinterpret_cast<__nv_bfloat16*>(p.out_lo)[orow * p.ldo + n] =
+                                    __float2bfloat16_rn(v - __bfloat162float(hi));
                         } else if (p.atomic_add) {
                             atomicAdd(reinterpret_cast<float*>(p.out) + orow * p.ldo + n, v);
                         } else {
@@ -627,6 +631,7 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
     p.NT = w.NT;
     p.KT = w.KT;
     p.out = a.out;
+    p.out_lo = a.out_bf16 ? a.out_lo : nullptr;
     p.ldo = a.ldo;
     p.out_bf16 = a.out_bf16 ? 1 : 0;
     p.relu = a.relu ? 1 : 0;

@@ -75,7 +75,8 @@ __global__ void qgemm_simt_kernel(const __nv_bfloat16* __restrict__ xh,
                                   int64_t M, int64_t K, int64_t N, int64_t NT, int64_t KT,
                                   const int* __restrict__ group_rows, int G, int64_t group_base,
                                   int wmod,
-                                  void* __restrict__ out, int64_t ldo, bool out_bf16, bool relu,
+                                  void* __restrict__ out, void* __restrict__ out_lo, int64_t ldo,
+                                  bool out_bf16, bool relu,
                                   bool atomic_add, const int* __restrict__ rowmap,
                                   const float* __restrict__ rowscale) {
     const int64_t total = M * N;
@@ -99,12 +100,17 @@ __global__ void qgemm_simt_kernel(const __nv_bfloat16* __restrict__ xh,
         if (rowscale) v *= rowscale[r];
         if (relu) v = fmaxf(v, 0.0f);
         const int64_t orow = rowmap ? rowmap[r] : r;
-        if (out_bf16)
-            static_cast<__nv_bfloat16*>(out)[orow * ldo + n] = __float2bfloat16_rn(v);
-        else if (atomic_add)
+        if (out_bf16) {
+            const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+            static_cast<__nv_bfloat16*>(out)[orow * ldo + n] = hi;
+            if (out_lo)
+                static_cast<__nv_bfloat16*>(out_lo)[orow * ldo + n] =
+                    __float2bfloat16_rn(v - __bfloat162float(hi));
+        } else if (atomic_add) {
             atomicAdd(static_cast<float*>(out) + orow * ldo + n, v);
-        else
+        } else {
             static_cast<float*>(out)[orow * ldo + n] = v;
+        }
     }
 }
 
@@ -134,7 +140,8 @@ __global__ void __launch_bounds__(kDecodeThreads)
                         const int8_t* __restrict__ q, const float* __restrict__ scale, int64_t M,
                         int64_t K, int64_t N, int64_t NT, int64_t KT,
                         const int* __restrict__ group_rows, int64_t group_base, int wmod, int KS,
-                        int kper, void* __restrict__ out, int64_t ldo, int out_bf16, int relu,
+                        int kper, void* __restrict__ out, void* __restrict__ out_lo, int64_t ldo,
+                        int out_bf16, int relu,
                         int atomic_add, const int* __restrict__ rowmap,
                         const float* __restrict__ rowscale, int* __restrict__ err) {
     __shared__ __align__(16) float xs[MAXM][kDecodeXRow];
@@ -236,12 +243,17 @@ __global__ void __launch_bounds__(kDecodeThreads)
             if (rowscale) v *= rowscale[r];
             if (relu) v = fmaxf(v, 0.0f);
             const int64_t orow = rowmap ? rowmap[r] : r;
-            if (out_bf16)
-                static_cast<__nv_bfloat16*>(out)[orow * ldo + n] = __float2bfloat16_rn(v);
-            else if (atomic_add)
+            if (out_bf16) {
+                const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+                static_cast<__nv_bfloat16*>(out)[orow * ldo + n] = hi;
+                if (out_lo)
+                    static_cast<__nv_bfloat16*>(out_lo)[orow * ldo + n] =
+                        __float2bfloat16_rn(v - __bfloat162float(hi));
+            } else if (atomic_add) {
                 atomicAdd(static_cast<float*>(out) + orow * ldo + n, v);
-            else
+            } else {
                 static_cast<float*>(out)[orow * ldo + n] = v;
+            }
         }
     }
 }
@@ -282,7 +294,8 @@ aem_status launch_qgemm_decode(const GemmArgs& a, cudaStream_t s) {
         kern<<<static_cast<unsigned>(grid), kDecodeThreads, 0, s>>>(
             static_cast<const __nv_bfloat16*>(a.x_hi), static_cast<const __nv_bfloat16*>(a.x_lo),
             w.q, w.scale, a.M, w.K, w.N, w.NT, w.KT, a.group_rows, a.group_base, a.wmod,
-            static_cast<int>(ks), kper, a.out, a.ldo, a.out_bf16 ? 1 : 0, a.relu ? 1 : 0,
+            static_cast<int>(ks), kper, a.out, a.out_bf16 ? a.out_lo : nullptr, a.ldo,
+            a.out_bf16 ? 1 : 0, a.relu ? 1 : 0,
             add ? 1 : 0, a.rowmap, a.rowscale, err);
     };
     if (m_max <= 1) go(qgemm_decode_kernel<1>);
@@ -316,8 +329,9 @@ aem_status launch_qgemm_simt(const GemmArgs& a, cudaStream_t s) {
     const int64_t blocks = (total + 255) / 256 < 8192 ? (total + 255) / 256 : 8192;
     qgemm_simt_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
         static_cast<const __nv_bfloat16*>(a.x_hi), static_cast<const __nv_bfloat16*>(a.x_lo), w.q,
-        w.scale, a.M, w.K, w.N, w.NT, w.KT, a.group_rows, a.G, a.group_base, a.wmod, a.out, a.ldo, a.out_bf16, a.relu,
-        a.atomic_add || a.ksplit > 1, a.rowmap, a.rowscale);
+        w.scale, a.M, w.K, w.N, w.NT, w.KT, a.group_rows, a.G, a.group_base, a.wmod, a.out,
+        a.out_bf16 ? a.out_lo : nullptr, a.ldo, a.out_bf16, a.relu, a.atomic_add || a.ksplit > 1,
+        a.rowmap, a.rowscale);
     AEM_CHECK_LAUNCH();
     count_launches(1);
     return AEM_OK;

@@ -121,6 +121,11 @@ struct GemmArgs {
     const void* x_lo = nullptr;  // bf16 [M, K] or nullptr (split float32 activations)
     void* out = nullptr;
     bool out_bf16 = false;
+    // bf16 output only: when set, the output is written as a bf16 pair,
+    // out = bf16(v) and out_lo = bf16(v - out) (same layout and stride), so
+    // out + out_lo carries v to about 16 significant bits -- the split form a
+    // following GEMM takes as x_hi / x_lo
+    void* out_lo = nullptr;
     int64_t ldo = 0;           // output row stride (elements)
     bool relu = false;
     bool atomic_add = false;   // float32 out only: red.add partial sums (split-K)

@@ -120,6 +120,12 @@ class MoELayer:
                                                    od), "aem_moe_forward_host")
         return out
 
+    def set_hidden_dtype(self, dtype):
+        """Storage of the hidden activation: ``None`` (follow x), ``"f32"``
+        (a bf16 hi + lo pair) or ``"bf16"`` (``aem_moe_set_hidden_dtype``)."""
+        code = {None: -1, "f32": _lib.F32, "bf16": _lib.BF16}[dtype]
+        _lib.check(_lib.lib().aem_moe_set_hidden_dtype(self.handle, code), "aem_moe_set_hidden_dtype")
+
     def profile(self, enable=True):
         _lib.check(_lib.lib().aem_moe_profile(self.handle, 1 if enable else 0), "aem_moe_profile")
 

@@ -259,9 +259,26 @@ aem_status aem_moe_free(aem_moe_t moe);
  * (batch_position = j*T + t); a unit's secondary is the token's (k+1)-th
  * gating choice; capacity is applied as Router::assign_effective_experts
  * (router.hpp:249-266); each unit runs relu(x W_up) W_down of its effective
- * expert and out[t] = sum_j weight[t,j] * y[t,j]. */
+ * expert and out[t] = sum_j weight[t,j] * y[t,j].
+ * Precision (the int8 weights are exact in bf16; every product is summed in
+ * float32; gating always reads x in its own dtype):
+ *   x AEM_F32  -- x enters the up GEMM as a bf16 pair hi + lo (x to about 16
+ *                 significant bits, two MMAs per K step) and, by default,
+ *                 so does the hidden activation relu(x W_up) in the down
+ *                 GEMM: the float32-activation contract of
+ *                 fused_quantized_matmul (quantized_gemm.py:184-226).
+ *   x AEM_BF16 -- x is used as is; the hidden activation is stored as bf16
+ *                 (one MMA per K step) unless aem_moe_set_hidden_dtype
+ *                 selects the pair.
+ * out AEM_BF16 rounds the float32 layer output once at the end. */
 aem_status aem_moe_forward(aem_moe_t moe, const void* x, aem_dtype x_dtype, int64_t T, void* out,
                            aem_dtype out_dtype, void* stream);
+/* Storage of the hidden activation relu(x W_up) between the expert GEMMs:
+ * -1 (default) follows x's dtype, AEM_F32 keeps it as a bf16 pair hi + lo
+ * (about 16 significant bits; the down GEMM then issues two MMAs per K
+ * step), AEM_BF16 rounds it to bf16.  No counterpart in the reference, whose
+ * kernels never compose an FFN. */
+aem_status aem_moe_set_hidden_dtype(aem_moe_t moe, int hidden_dtype);
 /* HOST-buffer form of aem_moe_forward (synchronous). */
 aem_status aem_moe_forward_host(aem_context_t ctx, aem_moe_t moe, const void* x, aem_dtype x_dtype,
                                 int64_t T, void* out, aem_dtype out_dtype);
@@ -375,7 +392,10 @@ aem_status aem_ep_create(const aem_moe_config* cfg, int rank, int world, const u
                          const int32_t* expert_to_rank, int64_t max_tokens_local, aem_ep_t* out);
 aem_status aem_ep_free(aem_ep_t ep);
 /* One step: this rank's T_local tokens (global positions rank*T_local ...)
- * -> its outputs.  Collective: every rank calls it with the same T_local
+ * -> its outputs.  Precision: activations cross NVLink and enter the expert
+ * GEMMs as bf16 -- float32 x is rounded to bf16 once, at dispatch -- and the
+ * hidden activation is stored as bf16; products are summed in float32 and
+ * outputs are float32 sums (the single-GPU layer's bf16 mode).  Collective: every rank calls it with the same T_local
  * (<= max_tokens_local).  Asynchronous on `stream` (no host synchronisation);
  * a receive-capacity or peer failure is reported by aem_device_status
  * (AEM_ETIMEOUT for a silent peer), the way route_batch throws. */

@@ -309,21 +309,26 @@ def zipf_bias(num_experts, s=1.1):
     return np.log(p).astype(np.float32)
 
 
-def _expert_rows(xrow, qup, sup, qdn, sdn):
+def _expert_rows(xrow, qup, sup, qdn, sdn, hidden="bf16"):
     h = xrow.astype(np.float64) @ dequantize_int8(qup, sup).astype(np.float64)
-    h = bf16_round(np.maximum(h, 0.0).astype(np.float32)).astype(np.float64)
+    h = np.maximum(h, 0.0)
+    if hidden == "bf16":
+        h = bf16_round(h.astype(np.float32)).astype(np.float64)
     return h @ dequantize_int8(qdn, sdn).astype(np.float64)
 
 
-def moe_layer(x, gate_w, gate_b, k, q_up, s_up, q_down, s_down, capacity=None):
+def moe_layer(x, gate_w, gate_b, k, q_up, s_up, q_down, s_down, capacity=None, hidden="bf16"):
     """Oracle of one MoE layer: gating -> capacity routing -> expert FFN -> combine.
 
-    ``x`` [T,d] (values already representable in the input dtype);
-    ``q_up[e]`` [d,ffn] int8 with ``s_up[e]`` [1,ffn]; ``q_down[e]`` [ffn,d]
-    with ``s_down[e]`` [1,d].  The expert FFN is
-    ``relu(x @ deq(q_up)) -> bf16 -> @ deq(q_down)`` in float64 with the
-    hidden activation rounded to bfloat16 (the precision the CUDA path
-    stores it in); the layer output is ``sum_j val[t,j] * y[t,j]``.
+    ``x`` [T,d] float32 (the values the layer receives: float32 inputs as
+    they are, bfloat16 inputs as their float32 values); ``q_up[e]`` [d,ffn]
+    int8 with ``s_up[e]`` [1,ffn]; ``q_down[e]`` [ffn,d] with ``s_down[e]``
+    [1,d].  The expert FFN is ``relu(x @ deq(q_up)) @ deq(q_down)`` in float64
+    -- the float32-activation GEMM contract of
+    ``src/kernels/quantized_gemm.py:184-226`` / ``prototype/math_proto.py:71-86``
+    evaluated exactly -- with the hidden activation rounded to bfloat16 only
+    when ``hidden == "bf16"`` (a layer that stores it in bf16).  The layer
+    output is ``sum_j val[t,j] * y[t,j]``.
     Returns ``(out f64 [T,d], idx int32 [T,k(+1)], val f32 [T,k], eff int32 [T*k])``.
     """
     x = np.asarray(x, np.float32)
@@ -337,13 +342,13 @@ def moe_layer(x, gate_w, gate_b, k, q_up, s_up, q_down, s_down, capacity=None):
         sel = np.flatnonzero(eff == ex)
         if sel.size == 0:
             continue
-        y = _expert_rows(x[tok[sel]], q_up[ex], s_up[ex], q_down[ex], s_down[ex])
+        y = _expert_rows(x[tok[sel]], q_up[ex], s_up[ex], q_down[ex], s_down[ex], hidden)
         w = val[tok[sel], slot[sel]].astype(np.float64)[:, None]
         np.add.at(out, tok[sel], w * y)
     return out, idx, val, eff
 
 
-def moe_layer_rows(rows, x, idx, val, eff, k, q_up, s_up, q_down, s_down):
+def moe_layer_rows(rows, x, idx, val, eff, k, q_up, s_up, q_down, s_down, hidden="bf16"):
     """Layer output for a subset of token ``rows`` given the routing decision.
 
     Used to check sampled rows of full-size runs without the whole layer;
@@ -359,7 +364,7 @@ def moe_layer_rows(rows, x, idx, val, eff, k, q_up, s_up, q_down, s_down):
     for ex in np.unique(unit_eff):
         sel = np.flatnonzero(unit_eff == ex)
         y = _expert_rows(np.asarray(x, np.float32)[unit_tok[sel]], q_up[ex], s_up[ex],
-                         q_down[ex], s_down[ex])
+                         q_down[ex], s_down[ex], hidden)
         w = np.asarray(val)[unit_tok[sel], unit_slot[sel]].astype(np.float64)[:, None]
         np.add.at(out, unit_row[sel], w * y)
     return out

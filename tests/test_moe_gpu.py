@@ -1,10 +1,13 @@
 """The composed MoE layer on one B200 vs the oracle.
 
 Routing (gating indices and capacity reroutes) is bit-exact; layer outputs
-are within ``1e-3 + 1e-3 * |ref|`` of the float64 oracle that rounds the
-expert hidden activation to bfloat16 like the CUDA path (the layer's stated
-precision: bf16 activations into the expert GEMMs, float32 accumulation,
-float32 expert outputs and combine).
+are within ``1e-3 + 1e-3 * |ref|`` of the float64 oracle.
+* bf16 inputs: the oracle rounds the expert hidden activation to bfloat16,
+  the precision the bf16 layer stores it in;
+* float32 inputs (raw values, not bf16-representable): the oracle keeps x
+  and the hidden activation exact -- the float32-activation contract of
+  ``quantized_gemm.py:184-226`` -- and the layer must meet it (x and the
+  hidden activation travel as bf16 hi + lo pairs).
 """
 import numpy as np
 import pytest
@@ -39,12 +42,18 @@ def _bf16(x):
     return f, (f.view(np.uint32) >> 16).astype(np.uint16)
 
 
-def _run(cuda, x_bits, gw, gb, w, k, cap, out_dtype="f32"):
+def _run(cuda, x_bits, gw, gb, w, k, cap, out_dtype="f32", hidden=None):
+    """x_bits: raw bfloat16 bits (uint16) or float32 values."""
     import torch
     from aethermoe_b200.moe import MoELayer
     layer = MoELayer(gw, gb, w[0], w[1], w[2], w[3], k, capacity=cap)
+    if hidden is not None:
+        layer.set_hidden_dtype(hidden)
     t = x_bits.shape[0]
-    xt = torch.from_numpy(x_bits.view(np.int16)).to(cuda).view(torch.bfloat16)
+    if x_bits.dtype == np.float32:
+        xt = torch.from_numpy(x_bits).to(cuda)
+    else:
+        xt = torch.from_numpy(x_bits.view(np.int16)).to(cuda).view(torch.bfloat16)
     out = layer.forward(xt, out_dtype=torch.float32 if out_dtype == "f32" else torch.bfloat16)
     idx, val, eff = layer.last_routing(t)
     torch.cuda.synchronize()
@@ -83,6 +92,70 @@ def test_small_layer_matches_oracle(cuda, t, d, f, e, k, cap):
     _close(out, ref)
 
 
+F32_CASES = [
+    (64, 256, 512, 8, 2, None),
+    (200, 128, 256, 16, 6, 40),
+    (1, 512, 1024, 8, 2, None),      # decode: CUDA-core GEMMs with split operands
+    (3, 256, 640, 8, 2, 1),
+    (513, 192, 320, 32, 3, 50),
+    (300, 4096, 1408, 8, 2, None),   # K = 4096: where a plain bf16 x would miss 1e-3
+]
+
+
+@pytest.mark.parametrize("t,d,f,e,k,cap", F32_CASES)
+def test_f32_layer_meets_fp32_contract(cuda, t, d, f, e, k, cap):
+    """Raw float32 inputs against the float64 layer with x and the hidden
+    activation unrounded."""
+    rng = np.random.default_rng(t * 5 + d)
+    x = rng.normal(size=(t, d)).astype(np.float32)
+    assert not np.array_equal(O.bf16_round(x), x)
+    gw = (rng.normal(size=(d, e)) / np.sqrt(d)).astype(np.float32)
+    gb = O.zipf_bias(e)
+    w = _weights(rng, e, d, f, quantize=(d * f <= 1 << 20))
+    out, idx, val, eff = _run(cuda, x, gw, gb, w, k, cap)
+    ref, oidx, oval, oeff = O.moe_layer(x, gw, gb, k, w[0], w[1], w[2], w[3], cap, hidden="f32")
+    np.testing.assert_array_equal(idx, oidx)
+    np.testing.assert_allclose(val, oval, atol=1e-6)
+    np.testing.assert_array_equal(eff, oeff)
+    _close(out, ref)
+
+
+def test_f32_layer_is_not_bf16_layer(cuda):
+    """The float32 layer is measurably closer to the exact layer than a
+    layer that rounds x and the hidden activation to bf16 would be."""
+    t, d, f, e, k = 96, 1024, 2048, 8, 2
+    rng = np.random.default_rng(5)
+    x = rng.normal(size=(t, d)).astype(np.float32)
+    gw = (rng.normal(size=(d, e)) / np.sqrt(d)).astype(np.float32)
+    gb = np.zeros(e, np.float32)
+    w = _weights(rng, e, d, f, quantize=False)
+    out, *_ = _run(cuda, x, gw, gb, w, k, None)
+    exact, *_ = O.moe_layer(x, gw, gb, k, *w, None, hidden="f32")
+    rounded, *_ = O.moe_layer(O.bf16_round(x), gw, gb, k, *w, None, hidden="bf16")
+    err_gpu = np.abs(out - exact).max()
+    err_bf16 = np.abs(rounded - exact).max()
+    assert err_gpu < err_bf16 / 20, (err_gpu, err_bf16)
+
+
+def test_bf16_input_f32_hidden(cuda):
+    """bf16 inputs with the hidden activation kept as a bf16 pair, and
+    float32 inputs with it forced to bf16."""
+    rng = np.random.default_rng(12)
+    t, d, f, e, k, cap = 150, 256, 768, 16, 4, 45
+    xf, xb = _bf16(rng.normal(size=(t, d)).astype(np.float32))
+    gw = (rng.normal(size=(d, e)) / np.sqrt(d)).astype(np.float32)
+    gb = O.zipf_bias(e)
+    w = _weights(rng, e, d, f)
+    out, idx, val, eff = _run(cuda, xb, gw, gb, w, k, cap, hidden="f32")
+    ref, oidx, oval, oeff = O.moe_layer(xf, gw, gb, k, *w, cap, hidden="f32")
+    np.testing.assert_array_equal(eff, oeff)
+    _close(out, ref)
+    x = rng.normal(size=(t, d)).astype(np.float32)
+    out, *_ = _run(cuda, x, gw, gb, w, k, cap, hidden="bf16")
+    h_ref, *_ = O.moe_layer(x, gw, gb, k, *w, cap, hidden="bf16")
+    _close(out, h_ref)
+
+
 def test_bf16_output(cuda):
     rng = np.random.default_rng(11)
     t, d, f, e, k = 48, 128, 256, 8, 2
@@ -116,6 +189,15 @@ def test_expert_parallel_config_on_one_gpu(cuda):
     assert (eff != O.moe_units(oidx, k, e)[0]).sum() > 0  # the Zipf bias forces reroutes
     rows = np.unique(np.r_[0, t - 1, rng.integers(0, t, 22)])
     ref = O.moe_layer_rows(rows, xf, oidx, oval, oeff, k, w[0], w[1], w[2], w[3])
+    _close(out[rows], ref)
+    # the same configuration with raw float32 tokens: the float32 layer
+    x = rng.normal(size=(t, d)).astype(np.float32)
+    out, idx, val, eff = _run(cuda, x, gw, gb, w, k, cap)
+    oidx, oval = O.fused_gating(x, gw, gb, k, extra=1)
+    np.testing.assert_array_equal(idx, oidx)
+    oeff = native.moe_route(oidx, k, e, cap)
+    np.testing.assert_array_equal(eff, oeff)
+    ref = O.moe_layer_rows(rows, x, oidx, oval, oeff, k, *w, hidden="f32")
     _close(out[rows], ref)
 
 

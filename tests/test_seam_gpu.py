@@ -12,11 +12,12 @@ import aem_oracle as O
 pytestmark = pytest.mark.gpu
 
 
-def _iteration(rng, d):
-    """Decode steps first, then prefill chunks -- the order step() emits."""
+def _iteration(rng, d, dtype):
+    """Decode steps first, then prefill chunks -- the order step() emits.
+    float32 slices hold raw float32 values; bf16 slices bf16 values."""
     sizes = [1] * 37 + [int(v) for v in rng.integers(2, 513, size=5)] + [0, 3]
-    # bf16-representable values: the expert GEMMs take x in bf16 for either input dtype
-    return [(100 + i, O.bf16_round(rng.normal(size=(n, d)).astype(np.float32)))
+    rnd = (lambda a: a) if dtype == "f32" else O.bf16_round
+    return [(100 + i, rnd(rng.normal(size=(n, d)).astype(np.float32)))
             for i, n in enumerate(sizes)]
 
 
@@ -33,7 +34,7 @@ def test_iteration_slices_equal_concatenated_batch(cuda, dtype):
     sd = (rng.random(size=(e, 1, d)) * 1e-4 + 2e-4).astype(np.float32)
     gw = (rng.normal(size=(d, e)) / np.sqrt(d)).astype(np.float32)
     gb = O.zipf_bias(e)
-    its = _iteration(rng, d)
+    its = _iteration(rng, d, dtype)
     T = sum(x.shape[0] for _, x in its)
     cap = O.default_capacity(T, k, e)
     layer = MoELayer(gw, gb, qu, su, qd, sd, k, capacity=cap)
@@ -55,6 +56,8 @@ def test_iteration_slices_equal_concatenated_batch(cuda, dtype):
     oidx, oval = O.fused_gating(xh, gw, gb, k, extra=1)
     oeff = O.moe_route(oidx, k, e, cap)
     np.testing.assert_array_equal(eff_s, oeff)
-    ref = O.moe_layer_rows(np.arange(T), xh, oidx, oval, oeff, k, qu, su, qd, sd)
+    # float32 slices: the float32 layer (x and hidden activation unrounded)
+    ref = O.moe_layer_rows(np.arange(T), xh, oidx, oval, oeff, k, qu, su, qd, sd,
+                           hidden="f32" if dtype == "f32" else "bf16")
     assert np.all(np.abs(got - ref) <= 1e-3 + 1e-3 * np.abs(ref))
     layer.close()
