@@ -130,6 +130,7 @@ _SIGS = {
                              _i64, ctypes.POINTER(_vp)]),
     "aem_ep_free": (_int, [_vp]),
     "aem_ep_forward": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp]),
+    "aem_ep_forward_host": (_int, [_vp, _vp, _vp, _int, _i64, _vp, _int]),
     "aem_ep_last_routing": (_int, [_vp, _vp, _vp, _vp, _vp]),
     "aem_capacity_route_static": (_int, [_vp, _vp, _vp, _i64, _int, _u64, _vp, _vp]),
     "aem_kernel_launches": (ctypes.c_uint64, []),

@@ -1689,6 +1689,27 @@ aem_status aem_ep_forward_tolerant(aem_ep_t h, const void* x, aem_dtype x_dtype,
     return ep_forward_checked(h, x, x_dtype, T_local, out, out_dtype, unit_failed, true, stream);
 }
 
+aem_status aem_ep_forward_host(aem_context_t ctx, aem_ep_t h, const void* x, aem_dtype x_dtype,
+                               int64_t T_local, void* out, aem_dtype out_dtype) {
+    AEM_REQUIRE(ctx != nullptr && h != nullptr, "aem_ep_forward_host: NULL argument");
+    AEM_REQUIRE(T_local >= 0 && T_local < (1ll << 28), "aem_ep_forward_host: T out of range");
+    AEM_REQUIRE(T_local == 0 || (x && out), "aem_ep_forward_host: NULL buffer");
+    auto* c = reinterpret_cast<aem::Context*>(ctx);
+    auto* ep = reinterpret_cast<aem::Ep*>(h);
+    AEM_TRY_CUDA(cudaSetDevice(c->device));
+    const int64_t d = ep->cfg.d_model;
+    const size_t xb = static_cast<size_t>(T_local) * d * (x_dtype == AEM_F32 ? 4 : 2);
+    const size_t ob = static_cast<size_t>(T_local) * d * (out_dtype == AEM_F32 ? 4 : 2);
+    const size_t o1 = aem::align_up(xb, 256);
+    AEM_TRY(c->reserve_device(o1 + ob + 256));
+    char* dv = static_cast<char*>(c->dev);
+    if (xb) AEM_TRY_CUDA(cudaMemcpyAsync(dv, x, xb, cudaMemcpyHostToDevice, c->stream));
+    AEM_TRY(ep_forward_checked(h, dv, x_dtype, T_local, dv + o1, out_dtype, nullptr, false,
+                               c->stream));
+    if (ob) AEM_TRY_CUDA(cudaMemcpyAsync(out, dv + o1, ob, cudaMemcpyDeviceToHost, c->stream));
+    return aem::check_device_errors(c->stream, "aem_ep_forward_host");
+}
+
 aem_status aem_ep_mark_unhealthy(aem_ep_t h, int rank) {
     AEM_REQUIRE(h != nullptr, "aem_ep_mark_unhealthy: NULL layer");
     auto* ep = reinterpret_cast<aem::Ep*>(h);

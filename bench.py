@@ -86,17 +86,138 @@ def expert_weights(experts, device):
     return up, down, (qu, su, qd, sd)
 
 
-def token_buffers(device, tokens, rank, world):
+def token_buffer(device, tokens, b):
+    """Input buffer b of the whole global batch (every rank draws the same)."""
     import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(7 + b)
+    return torch.randn((tokens, D_MODEL), generator=g, device=device).to(torch.bfloat16)
+
+
+def token_buffers(device, tokens, rank, world):
     tl = tokens // world
     bufs = []
     for b in range(N_INPUT_BUFFERS):
-        g = torch.Generator(device=device)
-        g.manual_seed(7 + b)
-        x = torch.randn((tokens, D_MODEL), generator=g, device=device).to(torch.bfloat16)
+        x = token_buffer(device, tokens, b)
         bufs.append(x[rank * tl:(rank + 1) * tl].contiguous())
         del x
     return bufs
+
+
+def exchange_compare(layer, x_local, world, rank, tl, dev, stream, place, phases, nsteps,
+                     reps=20):
+    """The step's token exchange through NCCL, for comparison with the
+    layer's peer-memory exchange: the same pair rows -- one bf16 row per
+    (token, destination rank) with at least one unit there, out; one float32
+    row per pair, back -- as two torch.distributed.all_to_all_single calls
+    (NCCL grouped send/recv), timed with CUDA events (max over ranks).  The
+    layer's own dispatch / return times are its profiled phases of the timed
+    steps.  Returns the line's object on every rank."""
+    import torch
+    import torch.distributed as dist
+    out = torch.empty((tl, D_MODEL), dtype=torch.bfloat16, device=dev)
+    layer.forward(x_local, out=out, stream=stream)
+    _, _, eff = layer.last_routing(tl, stream=stream)
+    torch.cuda.synchronize()
+    place_t = torch.tensor(place, dtype=torch.long, device=dev)
+    dest = place_t[eff.long()].view(K_TOP, tl)
+    pair = torch.zeros((world, tl), dtype=torch.bool, device=dev)
+    pair[dest, torch.arange(tl, device=dev).expand(K_TOP, tl)] = True
+    send = pair.sum(1).to(torch.int64)
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send)
+    sc, rc = send.tolist(), recv.tolist()
+    xs = torch.randn((sum(sc), D_MODEL), device=dev).to(torch.bfloat16)
+    xr = torch.empty((sum(rc), D_MODEL), dtype=torch.bfloat16, device=dev)
+    ys = torch.randn((sum(rc), D_MODEL), device=dev)
+    yr = torch.empty((sum(sc), D_MODEL), dtype=torch.float32, device=dev)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b) / reps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    d_ms = timed(lambda: dist.all_to_all_single(xr, xs, rc, sc))
+    r_ms = timed(lambda: dist.all_to_all_single(yr, ys, sc, rc))
+    remote = sum(c for r, c in enumerate(sc) if r != rank)
+    return {"nccl_dispatch_ms": d_ms, "nccl_return_ms": r_ms,
+            "peer_dispatch_ms": phases.get("dispatch", 0.0) / max(1, nsteps),
+            "peer_return_ms": phases.get("return", 0.0) / max(1, nsteps),
+            "pairs_sent_rank0": sum(sc), "pairs_sent_remote_rank0": remote,
+            "bytes_out_rank0": remote * D_MODEL * 2, "bytes_back_rank0": remote * D_MODEL * 4,
+            "how": ("torch.distributed.all_to_all_single (NCCL) of the step's pair rows: bf16 "
+                    "out, float32 back, same per-destination counts; peer_* are the layer's "
+                    "profiled dispatch/return phases (CUDA events, rank 0)")}
+
+
+def ep_parity(layer, x_local, world, rank, tokens, dev, stream, gw, gb, cap):
+    """Checks one expert-parallel step against the single-GPU layer run on
+    the GLOBAL batch (before the timed region).
+
+    Every rank runs one step on its slice of input buffer 0; the routing
+    (gating ids and the effective expert of every (token, slot) unit) and
+    the float32 outputs are gathered to every rank; rank 0 builds the
+    single-GPU layer with all E experts (the same seeded weights), runs it
+    over the whole batch and compares: routing bit-exact -- the capacity rule
+    of Router::assign_effective_experts over the global batch, decided here
+    by the distributed count exchange -- and outputs within the layer
+    tolerance 1e-3 + 1e-3 |ref| (float32 sums in another order).  The
+    single-GPU layer is the one the tests pin to the oracle.  Returns the
+    line's "parity" object on rank 0, None elsewhere."""
+    import torch
+    import torch.distributed as dist
+    from aethermoe_b200.moe import MoELayer
+    tl = tokens // world
+    out = torch.empty((tl, D_MODEL), dtype=torch.float32, device=dev)
+    layer.forward(x_local, out=out, stream=stream)
+    idx, _, eff = layer.last_routing(tl, stream=stream)
+    torch.cuda.synchronize()
+    g_idx = torch.empty((world,) + tuple(idx.shape), dtype=idx.dtype, device=dev)
+    g_eff = torch.empty((world,) + tuple(eff.shape), dtype=eff.dtype, device=dev)
+    g_out = torch.empty((world, tl, D_MODEL), dtype=torch.float32, device=dev)
+    dist.all_gather_into_tensor(g_idx, idx.contiguous())
+    dist.all_gather_into_tensor(g_eff, eff.contiguous())
+    dist.all_gather_into_tensor(g_out, out)
+    torch.cuda.synchronize()
+    res = None
+    if rank == 0:
+        up, down, _ = expert_weights(range(E), dev)
+        one = MoELayer(gw, gb, up, None, down, None, K_TOP, capacity=cap, device=dev.index)
+        x = token_buffer(dev, tokens, 0)
+        ref = one.forward(x, out_dtype=torch.float32, stream=stream)
+        r_idx, _, r_eff = one.last_routing(tokens, stream=stream)
+        torch.cuda.synchronize()
+        idx_all = g_idx.reshape(tokens, -1)
+        # per-rank slot-major units [k][tl] -> global slot-major [k][T]
+        eff_all = g_eff.reshape(world, K_TOP, tl).permute(1, 0, 2).reshape(-1).to(r_eff.dtype)
+        routing_ok = bool(torch.equal(idx_all, r_idx) and torch.equal(eff_all, r_eff))
+        primaries = r_idx[:, :K_TOP].t().reshape(-1).to(r_eff.dtype)
+        got = g_out.reshape(tokens, D_MODEL).double()
+        r = ref.double()
+        excess = ((got - r).abs() - (1e-3 + 1e-3 * r.abs())).max().item()
+        res = {"routing_bit_exact": routing_ok, "units": K_TOP * tokens,
+               "units_rerouted_by_capacity": int((r_eff != primaries).sum().item()),
+               "units_mismatched": int((eff_all != r_eff).sum().item()),
+               "rows_checked": tokens, "max_abs_diff": float((got - r).abs().max().item()),
+               "max_excess_over_tol": float(excess), "rows_within_tol": bool(excess <= 0),
+               "tolerance": "1e-3 + 1e-3*|ref|",
+               "reference": (f"single-GPU layer (aem_moe_forward, all {E} experts) on the "
+                             f"global batch of {tokens} tokens, input buffer 0")}
+        one.close()
+        del up, down, x, ref
+        torch.cuda.empty_cache()
+    dist.barrier()
+    return res
 
 
 # ------------------------------------------------------------------ clocks
@@ -298,6 +419,9 @@ def measured_peaks():
 
 
 def traffic_from_profile():
+    """DRAM bytes per launch of the dominant kernel, from the committed ncu
+    capture of the same kernel on the N=1 workload (bench.py cannot run ncu
+    on itself); the line names the file and what it measured."""
     p = os.path.join(ROOT, "profiles", "qgemm_tc_traffic.json")
     if os.path.exists(p):
         with open(p) as f:
@@ -350,6 +474,9 @@ def run_ours(args):
     xs = token_buffers(dev, tokens, rank, world)
     outs = [torch.empty((tl, D_MODEL), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     stream = torch.cuda.current_stream()
+    parity = None
+    if world > 1 and not args.no_parity:
+        parity = ep_parity(layer, xs[0], world, rank, tokens, dev, stream, gw, gb, cap)
 
     def barrier():
         torch.cuda.synchronize()
@@ -396,6 +523,10 @@ def run_ours(args):
 
     # ---- end to end: host buffers in, host buffers out, through the public API
     e2e = e2e_run(args, layer, world, rank, tl, dev, stream, barrier)
+    xchg = None
+    if world > 1 and args.exchange_compare:
+        xchg = exchange_compare(layer, xs[0], world, rank, tl, dev, stream,
+                                [e % world for e in range(E)], phases, nsteps)
 
     # ---- roofline of the dominant kernel (the grouped INT8 GEMM, up + down launches)
     gemm_ms = (phases["up_gemm"] + phases["down_gemm"]) / max(1, nsteps)
@@ -403,7 +534,12 @@ def run_ours(args):
     gemm_flops = 2.0 * units_local * D_MODEL * D_FFN * 2
     tflops = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
     sustained, burst, hbm, src = measured_peaks()
-    traffic = traffic_from_profile()
+    # a timed region of a fraction of a second runs at full clock: compare
+    # with the burst GEMM peak; a region of seconds settles under the power
+    # cap: compare with the sustained one
+    long_region = ms_max >= 2000.0
+    peak = sustained if long_region else burst
+    traffic = traffic_from_profile() if world == 1 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -427,10 +563,20 @@ def run_ours(args):
                               "per-step working set > 1 GiB")},
             "roofline": {"kernel": "qgemm_tc_kernel (grouped INT8-weight GEMM, up + down launches)",
                          "bound": "tensor", "achieved": tflops,
-                         "peak": sustained, "unit": "TFLOP/s",
-                         "frac": (tflops / sustained) if tflops and sustained else None,
-                         "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step)",
+                         "peak": peak, "unit": "TFLOP/s",
+                         "frac": (tflops / peak) if tflops and peak else None,
+                         "peak_source": (f"{src} bf16_tflops_sustained (timed region "
+                                         f"{ms_max / 1e3:.2f} s >= 2 s: power-capped clocks)"
+                                         if long_region else
+                                         f"{src} bf16_tflops burst (timed region "
+                                         f"{ms_max:.0f} ms < 2 s: full clocks)"),
                          "traffic": (traffic or {}).get("bytes_per_launch"),
+                         "traffic_source": (("profiles/qgemm_tc_traffic.json: ncu capture of "
+                                             f"{traffic.get('kernel')} on {traffic.get('workload')}"
+                                             " (mean of the up and down launches)")
+                                            if traffic else
+                                            "null: the committed ncu capture is of the N=1 "
+                                            "workload" if world > 1 else None),
                          "algorithmic_flops_per_step": gemm_flops,
                          "kernel_ms_per_step": gemm_ms},
             "phases_ms_per_step": {k: v / max(1, nsteps) for k, v in phases.items() if v > 0},
@@ -447,6 +593,10 @@ def run_ours(args):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if parity is not None:
+            line["parity"] = parity
+        if xchg is not None:
+            line["exchange_compare"] = xchg
         print(json.dumps(line), flush=True)
     layer.close()
     if world > 1:
@@ -490,23 +640,21 @@ def e2e_run(args, layer, world, rank, tl, dev, stream, barrier):
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
     else:
-        xd = torch.empty((tl, D_MODEL), dtype=torch.bfloat16, device=dev)
-        od = torch.empty((tl, D_MODEL), dtype=torch.bfloat16, device=dev)
+        ctx = _lib.context(dev.index)
+        cstream = torch.cuda.ExternalStream(aem.lib().aem_context_stream(ctx))
 
         def step(i):
-            xd.copy_(xh[i % 2], non_blocking=True)
-            layer.forward(xd, out=od, stream=stream)
-            oh.copy_(od, non_blocking=True)
-            stream.synchronize()
+            _lib.check(aem.lib().aem_ep_forward_host(ctx, layer.handle, xh[i % 2].data_ptr(),
+                                                     _lib.BF16, tl, oh.data_ptr(), _lib.BF16))
         for i in range(2):
             step(i)
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
+        e0.record(cstream)
         for i in range(steps):
             step(i)
-        e1.record(stream)
+        e1.record(cstream)
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
         import torch.distributed as dist
@@ -517,7 +665,7 @@ def e2e_run(args, layer, world, rank, tl, dev, stream, barrier):
     return {"value": tokens * steps / (ms * 1e-3), "unit": UNIT,
             "h2d_bytes_per_step": tokens * D_MODEL * 2, "d2h_bytes_per_step": tokens * D_MODEL * 2,
             "steps": steps, "api": "aem_moe_forward_host" if world == 1 else
-            "aem_ep_forward + pinned host copies on the same stream"}
+            "aem_ep_forward_host (every rank)"}
 
 
 # ------------------------------------------------------------------ other configs
@@ -658,6 +806,10 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-sample-tokens", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange-compare", action="store_true",
+                    help="N>1: also time the step's token exchange through NCCL all-to-all")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="N>1: skip the check of one step against the single-GPU layer")
     ap.add_argument("--ep-pipeline", choices=["auto", "on", "off"], default="auto",
                     help="expert-parallel two-half pipeline (auto: off)")
     ap.add_argument("--suite", action="store_true",

@@ -414,6 +414,11 @@ aem_status aem_ep_forward(aem_ep_t ep, const void* x, aem_dtype x_dtype, int64_t
 aem_status aem_ep_forward_tolerant(aem_ep_t ep, const void* x, aem_dtype x_dtype, int64_t T_local,
                                    void* out, aem_dtype out_dtype, uint8_t* unit_failed,
                                    void* stream);
+/* HOST-buffer form of aem_ep_forward: copies x in and out through ctx (whose
+ * device must be this rank's) and synchronises; collective like
+ * aem_ep_forward.  A peer failure is returned as AEM_ETIMEOUT / AEM_EDEVICE. */
+aem_status aem_ep_forward_host(aem_context_t ctx, aem_ep_t ep, const void* x, aem_dtype x_dtype,
+                               int64_t T_local, void* out, aem_dtype out_dtype);
 /* The host learned that `rank` is gone (a store, a heartbeat, a process
  * exit): later steps leave it out and never touch its memory again.  A rank
  * that exited must be marked here before the next step; the in-step deadline
