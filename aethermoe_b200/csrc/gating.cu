@@ -317,6 +317,240 @@ __global__ void __launch_bounds__(WARPS * 32)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Small batches (decode sizes): experts split over the CTAs of a cluster.
+//
+// With few tokens the work is a handful of long sequential dot products, so
+// the time is one float32 add chain of D steps, as long as the operands keep
+// flowing.  The kernel spreads the gate's experts over the CL CTAs of a
+// thread-block cluster (EB experts each) and the tokens over clusters (TT per
+// CTA); every consumer thread owns ONE (token, expert) logit and walks d in
+// increasing order (EXACT: float32 product, float32 add).  A producer warp
+// streams 128-wide chunks of d -- the CTA's expert block of the weights (one
+// contiguous bulk copy in the expert-block layout) and its tokens' activation
+// rows (one bulk copy per row) -- through a ring of mbarrier-tracked stages,
+// so no CTA-wide barrier interrupts the chains.  At the end every thread
+// stores its logit + bias into the leader CTA's shared memory (DSMEM), the
+// cluster synchronises, and the leader selects the top-k of each token with
+// the same selection as the large-batch kernel.  Every mbarrier wait is
+// bounded (globaltimer); a timeout sets an error bit and the roles run out,
+// so the cluster barrier is always reached by every thread.
+constexpr int kSmallDK = 128;     // d per stage
+constexpr int kSmallStages = 6;
+constexpr int kSmallCons = 128;   // consumer threads (warps 0-3); warp 4 produces
+constexpr int kSmallThreads = kSmallCons + 32;
+
+template <int EPAD, typename XT>
+struct SmallCfg {
+    static constexpr int EB = EPAD / 8 > 8 ? EPAD / 8 : 8;  // experts per CTA
+    static constexpr int CL = EPAD / EB;                   // CTAs per cluster (<= 8)
+    static constexpr int TT = kSmallCons / EB;             // tokens per CTA
+    static constexpr int XB = static_cast<int>(sizeof(XT));
+    static constexpr int XROW = kSmallDK * XB + 16;        // padded activation row, bytes
+    static constexpr int WST = kSmallDK / 4 * EB * 16;     // weight stage, bytes
+    static constexpr int XST = TT * XROW;                  // activation stage, bytes
+    static constexpr int LG = TT * EPAD * 4;               // gathered logits, bytes
+    static constexpr int SMEM = kSmallStages * (WST + XST) + LG + 2 * kSmallStages * 8 + 16;
+    static_assert(CL >= 1 && CL <= 8 && EB * CL == EPAD && TT * EB == kSmallCons, "shape");
+    static_assert((kSmallDK * XB) % 16 == 0 && XROW % 16 == 0 && WST % 16 == 0, "16-byte copies");
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+                 "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Stores v at the same shared-memory offset as `local` in CTA `rank` of the cluster.
+__device__ __forceinline__ void st_cluster_f32(const float* local, uint32_t rank, float v) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                 : "=r"(remote)
+                 : "r"(dev::smem_u32(local)), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+}
+
+template <typename XT>
+__device__ __forceinline__ float4 load_x4(const unsigned char* p);
+template <>
+__device__ __forceinline__ float4 load_x4<float>(const unsigned char* p) {
+    return *reinterpret_cast<const float4*>(p);
+}
+template <>
+__device__ __forceinline__ float4 load_x4<__nv_bfloat16>(const unsigned char* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+}
+
+template <int EPAD, typename XT, bool EXACT>
+__global__ void __launch_bounds__(kSmallThreads)
+    gating_small_kernel(const XT* __restrict__ x, const float4* __restrict__ wblk,
+                        const float* __restrict__ bias, int64_t N, int D, int64_t Dpad, int E,
+                        int k, int ksel, int32_t* __restrict__ idx_out,
+                        float* __restrict__ val_out, int* __restrict__ err) {
+    using C = SmallCfg<EPAD, XT>;
+    constexpr int EB = C::EB;
+    constexpr int TT = C::TT;
+    extern __shared__ __align__(128) unsigned char ssm[];
+    unsigned char* wring = ssm;
+    unsigned char* xring = wring + kSmallStages * C::WST;
+    float* lg = reinterpret_cast<float*>(xring + kSmallStages * C::XST);
+    uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(lg) + C::LG);
+    uint64_t* empty = full + kSmallStages;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kSmallStages);
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int cb = blockIdx.y;  // expert block = rank in the (1, CL, 1) cluster
+    const int64_t tok0 = static_cast<int64_t>(blockIdx.x) * TT;
+    const int rows = static_cast<int>(min(static_cast<int64_t>(TT), N - tok0));
+    const int nch = (D + kSmallDK - 1) / kSmallDK;
+    if (tid == 0) {
+        for (int st = 0; st < kSmallStages; ++st) {
+            dev::mbar_init(&full[st], 1);
+            dev::mbar_init(&empty[st], kSmallCons / 32);
+        }
+        *abort_flag = 0;
+        dev::fence_barrier_init();
+    }
+    __syncthreads();
+
+    float acc = 0.0f;
+    const int tl = tid / EB;  // consumer: local token
+    const int el = tid % EB;  //           expert within the block
+    if (warp == kSmallCons / 32) {
+        // ---- producer: one lane issues the bulk copies of every chunk
+        if (lane == 0) {
+            const float4* wsrc = wblk + static_cast<int64_t>(cb) * (Dpad / 4) * EB;
+            for (int c = 0; c < nch; ++c) {
+                const int st = c % kSmallStages;
+                const uint32_t ph = (c / kSmallStages) & 1;
+                if (!dev::mbar_wait_bounded(&empty[st], ph ^ 1, abort_flag, err, ERR_GEMM_TIMEOUT))
+                    break;
+                const int dd = min(kSmallDK, D - c * kSmallDK);
+                const uint32_t xb = static_cast<uint32_t>(dd * C::XB);
+                dev::mbar_arrive_expect_tx(&full[st], C::WST + rows * xb);
+                dev::bulk_load(wring + st * C::WST, wsrc + static_cast<int64_t>(c) * (kSmallDK / 4) * EB,
+                               C::WST, &full[st]);
+                for (int r = 0; r < rows; ++r)
+                    dev::bulk_load(xring + st * C::XST + r * C::XROW,
+                                   x + (tok0 + r) * static_cast<int64_t>(D) + c * kSmallDK, xb,
+                                   &full[st]);
+            }
+        }
+    } else {
+        // ---- consumers: one sequential chain each
+        for (int c = 0; c < nch; ++c) {
+            const int st = c % kSmallStages;
+            const uint32_t ph = (c / kSmallStages) & 1;
+            if (!dev::mbar_wait_bounded(&full[st], ph, abort_flag, err, ERR_GEMM_TIMEOUT)) break;
+            const int n4 = min(kSmallDK, D - c * kSmallDK) >> 2;
+            const float4* ws = reinterpret_cast<const float4*>(wring + st * C::WST) + el;
+            const unsigned char* xs = xring + st * C::XST + tl * C::XROW;
+#pragma unroll 8
+            for (int q = 0; q < n4; ++q) {
+                const float4 wv = ws[q * EB];
+                const float4 xv = load_x4<XT>(xs + q * 4 * C::XB);
+                if constexpr (EXACT) {
+                    acc = __fadd_rn(acc, __fmul_rn(xv.x, wv.x));
+                    acc = __fadd_rn(acc, __fmul_rn(xv.y, wv.y));
+                    acc = __fadd_rn(acc, __fmul_rn(xv.z, wv.z));
+                    acc = __fadd_rn(acc, __fmul_rn(xv.w, wv.w));
+                } else {
+                    acc = fmaf(xv.x, wv.x, acc);
+                    acc = fmaf(xv.y, wv.y, acc);
+                    acc = fmaf(xv.z, wv.z, acc);
+                    acc = fmaf(xv.w, wv.w, acc);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) dev::mbar_arrive(&empty[st]);
+        }
+        const int e = cb * EB + el;
+        const float v = __fadd_rn(acc, __ldg(bias + e));  // bias padded to EPAD with zeros
+        if constexpr (C::CL == 1)
+            lg[tl * EPAD + e] = v;
+        else
+            st_cluster_f32(&lg[tl * EPAD + e], 0, v);
+    }
+    __syncwarp();
+    if constexpr (C::CL == 1)
+        __syncthreads();
+    else
+        cluster_sync_all();  // every CTA's logits are in the leader's shared memory
+    if (cb != 0 || warp >= kSmallCons / 32) return;
+
+    // ---- leader: top-k of each token (lane groups own experts)
+    constexpr int GROUP = EPAD >= 32 ? 32 : EPAD;
+    constexpr int NSLOT = EPAD / GROUP;
+    constexpr int GPW = 32 / GROUP;
+    const int grp = lane / GROUP;
+    const int le = lane % GROUP;
+    const unsigned gmask = GROUP == 32 ? 0xFFFFFFFFu : (((1u << GROUP) - 1u) << (grp * GROUP));
+    for (int t = warp * GPW + grp; t < rows; t += (kSmallCons / 32) * GPW) {
+        float v[NSLOT];
+#pragma unroll
+        for (int s2 = 0; s2 < NSLOT; ++s2) v[s2] = lg[t * EPAD + le + GROUP * s2];
+        topk_select<GROUP, NSLOT>(v, le, gmask, tok0 + t, N, E, k, ksel, idx_out, val_out);
+    }
+}
+
+template <int EPAD, typename XT, bool EXACT>
+cudaError_t launch_small_e(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
+                           float* val, int* err, cudaStream_t s) {
+    using C = SmallCfg<EPAD, XT>;
+    auto kern = gating_small_kernel<EPAD, XT, EXACT>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((N + C::TT - 1) / C::TT), C::CL, 1);
+    cfg.blockDim = dim3(kSmallThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = C::CL;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<const XT*>(x),
+                              reinterpret_cast<const float4*>(g.wblk),
+                              static_cast<const float*>(g.bias), N, static_cast<int>(g.D), g.Dpad,
+                              static_cast<int>(g.E), k, ksel, idx, val, err);
+}
+
+template <typename XT, bool EXACT>
+cudaError_t launch_small(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
+                         float* val, int* err, cudaStream_t s) {
+    switch (g.Epad) {
+        case 8: return launch_small_e<8, XT, EXACT>(g, x, N, k, ksel, idx, val, err, s);
+        case 16: return launch_small_e<16, XT, EXACT>(g, x, N, k, ksel, idx, val, err, s);
+        case 32: return launch_small_e<32, XT, EXACT>(g, x, N, k, ksel, idx, val, err, s);
+        case 64: return launch_small_e<64, XT, EXACT>(g, x, N, k, ksel, idx, val, err, s);
+        case 128: return launch_small_e<128, XT, EXACT>(g, x, N, k, ksel, idx, val, err, s);
+        default: return launch_small_e<256, XT, EXACT>(g, x, N, k, ksel, idx, val, err, s);
+    }
+}
+
+// [Dpad/4][Epad][4] -> [Epad/eb][Dpad/4][eb][4]
+__global__ void block_gate_kernel(const float4* __restrict__ wt, int64_t D4, int64_t Epad, int eb,
+                                  float4* __restrict__ out) {
+    const int64_t total = D4 * Epad;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t el = i % eb;
+        const int64_t d4 = (i / eb) % D4;
+        const int64_t b = i / (eb * D4);
+        out[i] = wt[d4 * Epad + b * eb + el];
+    }
+}
+
 template <int GROUP, int NSLOT, int TPG, typename XT, bool EXACT, int WARPS = kWarps, int DKO = 0>
 cudaError_t launch_one(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
                        float* val, cudaStream_t s) {
@@ -404,6 +638,11 @@ __global__ void pack_gate_kernel(const float* __restrict__ w, const float* __res
 
 }  // namespace
 
+int gate_small_eb(int64_t Epad) { return Epad / 8 > 8 ? static_cast<int>(Epad / 8) : 8; }
+
+// Up to this many tokens the small-batch kernel runs (measured crossover).
+constexpr int64_t kSmallBatchMax = 512;
+
 int gate_epad(int64_t E) {
     if (E <= 8) return 8;
     if (E <= 16) return 16;
@@ -418,7 +657,23 @@ aem_status launch_gating(const Gate& g, const void* x, aem_dtype xd, int64_t N, 
     if (N == 0) return AEM_OK;
     cudaError_t e;
     const bool exact = mode == AEM_GATING_EXACT;
-    if (xd == AEM_F32)
+    const int xbytes = xd == AEM_F32 ? 4 : 2;
+    // the small-batch kernel copies whole 16-byte pieces of activation rows
+    const bool small = N <= kSmallBatchMax && g.wblk != nullptr &&
+                       (g.D * xbytes) % 16 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    if (small) {
+        int* err = device_error_word(g.device);
+        if (!err) {
+            set_error("gating: no device error word");
+            return AEM_ENOMEM;
+        }
+        if (xd == AEM_F32)
+            e = exact ? launch_small<float, true>(g, x, N, k, ksel, idx, val, err, s)
+                      : launch_small<float, false>(g, x, N, k, ksel, idx, val, err, s);
+        else
+            e = exact ? launch_small<__nv_bfloat16, true>(g, x, N, k, ksel, idx, val, err, s)
+                      : launch_small<__nv_bfloat16, false>(g, x, N, k, ksel, idx, val, err, s);
+    } else if (xd == AEM_F32)
         e = exact ? dispatch_e<float, true>(g, x, N, k, ksel, idx, val, s)
                   : dispatch_e<float, false>(g, x, N, k, ksel, idx, val, s);
     else
@@ -500,6 +755,14 @@ aem_status aem_gate_pack(const float* gate_weight, const float* gate_bias, int64
         }
         aem::pack_gate_kernel<<<256, 256>>>(tmp_w, gate_bias ? tmp_b : nullptr, D, E, g->Dpad,
                                              g->Epad, g->wt, g->bias);
+        g->eb = aem::gate_small_eb(g->Epad);
+        if (cudaMalloc(&g->wblk, sizeof(float) * g->Dpad * g->Epad) != cudaSuccess) {
+            set_error("aem_gate_pack: device allocation failed");
+            st = AEM_ENOMEM;
+            break;
+        }
+        aem::block_gate_kernel<<<256, 256>>>(reinterpret_cast<const float4*>(g->wt), g->Dpad / 4,
+                                              g->Epad, g->eb, reinterpret_cast<float4*>(g->wblk));
         if (cudaDeviceSynchronize() != cudaSuccess) {
             set_error("aem_gate_pack: pack kernel failed: %s",
                       cudaGetErrorString(cudaGetLastError()));
@@ -512,6 +775,7 @@ aem_status aem_gate_pack(const float* gate_weight, const float* gate_bias, int64
     if (st != AEM_OK) {
         cudaFree(g->wt);
         cudaFree(g->bias);
+        cudaFree(g->wblk);
         delete g;
         return st;
     }
@@ -525,6 +789,7 @@ aem_status aem_gate_free(aem_gate_t gate) {
     cudaSetDevice(g->device);
     cudaFree(g->wt);
     cudaFree(g->bias);
+    cudaFree(g->wblk);
     delete g;
     return AEM_OK;
 }

@@ -35,6 +35,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 #include "runtime.h"
@@ -545,6 +546,475 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kMmaWarp) tmem_dealloc(tmem_base, C::TMEM_COLS);
 }
 
+// ============================================================================
+// SM-pair form (tcgen05 cta_group::2) for large token tiles.
+//
+// A cluster of two CTAs on two SMs shares one tile of 256 output channels x BT
+// token rows: CTA c converts ITS 128 channels (channel block 2*pair + c) into
+// its own shared memory -- the A operand is split by M over the pair -- and
+// TMA-loads HALF of the tile's token rows -- the B operand is split by N -- so
+// one tcgen05.mma.cta_group::2 (M = 256) issued by the even CTA multiplies
+// both SMs' halves, and each CTA's TMEM receives its 128 channels x all BT
+// columns.  Per SM and K step this moves 8 + 16 + BT/2*128 bytes into shared
+// memory instead of 8 + 16 + BT*128 (and reads as much back), and one thread
+// issues the MMAs of two SMs.
+// Synchronisation (same barrier offsets in both CTAs):
+//   st_full[s]   local: the stage's activation bytes + one arrival per converter warp;
+//   peer_full[s] even CTA only: the odd CTA's relay thread arrives (remote,
+//                release.cluster) once the odd CTA's st_full[s] completed;
+//   st_empty[s]  both: one tcgen05.commit multicast to the pair frees both stages;
+//   accf[b]      both: the commit of a tile's last K step (multicast);
+//   acce[b]      even CTA: 8 local + 8 remote epilogue-warp arrivals.
+// Every wait is bounded; a timeout sets the abort flag in both CTAs.  The pair
+// meets at a cluster barrier after set-up and before teardown, so no CTA
+// exits while its peer may still touch its shared memory.
+constexpr int kPairWarpRelay = kMmaWarp;  // odd CTA: warp 17 relays stage readiness
+
+template <int BT, int SPLIT>
+struct Cfg2 {
+    static constexpr int HB = BT / 2;              // token rows per CTA (MMA N / 2)
+    static constexpr int W8 = kCh * kKT;
+    static constexpr int W16 = kCh * kKT * 2;
+    static constexpr int XB = HB * kKT * 2;        // bf16 activation half-tile, per part
+    static constexpr int XS = SPLIT * XB;
+    static constexpr int BUDGET = 216 * 1024;
+    static constexpr int DS_RAW = (BUDGET - 8 * W8) / (W16 + XS);
+    static constexpr int DS = DS_RAW > 8 ? 8 : (DS_RAW < 2 ? 2 : DS_RAW);
+    static constexpr int S8_RAW = (BUDGET - DS * (W16 + XS)) / W8;
+    static constexpr int CG_RAW = DS >= 4 ? 4 : (DS >= 2 ? 2 : 1);
+    static constexpr int CG = CG_RAW < AEM_QGEMM_MAX_CONV_GROUPS ? CG_RAW : AEM_QGEMM_MAX_CONV_GROUPS;
+    static constexpr int S8 = ((S8_RAW > 12 ? 12 : S8_RAW) / CG) * CG;
+    static constexpr int TMEM_COLS = 2 * BT < 32 ? 32 : 2 * BT;
+    static constexpr int BAR_BYTES = (3 * DS + 2 * S8 + 4) * 8 + 16;
+    static constexpr int TAB_BYTES = 2 * (kMaxGroups + 1) * 4;
+    static constexpr int SMEM = 1024 + DS * (W16 + XS) + S8 * W8 + BAR_BYTES + TAB_BYTES;
+    static constexpr int CG_WARPS = kConvWarps / CG;
+    static constexpr int CG_THREADS = CG_WARPS * 32;
+    static constexpr int EPI_COLS = BT >= 32 ? BT / 2 : BT;
+    static_assert(CG <= DS && S8 >= CG && S8 % CG == 0 && kConvWarps % CG == 0,
+                  "converter groups vs rings");
+    static_assert(S8 >= 2 && DS >= 2, "pipeline needs two stages per ring");
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
+    static_assert(BT % 32 == 0 && BT >= 32 && BT <= 256, "MMA N for M=256 (N/2 rows per CTA)");
+};
+
+// Tile t of the pair schedule: group g, channel pair pb (channels
+// [256 pb, 256 pb + 256)), token tile tc, K range.
+template <int BT>
+__device__ __forceinline__ TileInfo decode_tile_pair(int t, const int* s_rows, const int* s_tiles,
+                                                     const TcParams& p, int npair, int nkt,
+                                                     int kper) {
+    int lo = 0, hi = p.G;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (s_tiles[mid] <= t) lo = mid; else hi = mid;
+    }
+    TileInfo ti;
+    ti.g = lo;
+    ti.wg = static_cast<int>(p.group_base) + (p.wmod ? lo % p.wmod : lo);
+    int r = t - s_tiles[lo];
+    const int cnt = s_rows[lo + 1] - s_rows[lo];
+    const int ntc = (cnt + BT - 1) / BT;
+    const int tc = r % ntc;
+    r /= ntc;
+    const int ks = r % p.ksplit;
+    const int pb = r / p.ksplit;
+    ti.n0 = pb * 2 * kCh;  // first channel of the pair; CTA c owns [n0 + 128 c, +128)
+    ti.row0 = static_cast<int64_t>(s_rows[lo]) + static_cast<int64_t>(tc) * BT;
+    ti.nrows = min(BT, cnt - tc * BT);
+    ti.kt0 = ks * kper;
+    ti.kt1 = min(nkt, ti.kt0 + kper);
+    (void)npair;
+    return ti;
+}
+
+// Bounded wait that, on giving up, raises the abort flag of both CTAs.
+__device__ __forceinline__ bool pair_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          uint32_t peer, int* err, bool cluster_scope) {
+    auto probe = [&]() {
+        return cluster_scope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+    };
+    if (probe()) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        if (probe()) return true;
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > 2000000000ull) {
+            *abort_flag = 1;
+            st_remote_u32(const_cast<int*>(abort_flag), peer, 1u);
+            atomicOr(err, ERR_GEMM_TIMEOUT);
+            return false;
+        }
+    }
+}
+
+template <int BT, int SPLIT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    qgemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_xh,
+                         const __grid_constant__ CUtensorMap tm_xl, const TcParams p) {
+    using C = Cfg2<BT, SPLIT>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* w16_ring = smem;
+    uint8_t* x_ring = w16_ring + C::DS * C::W16;
+    uint8_t* w8_ring = x_ring + C::DS * C::XS;
+    uint64_t* st_full = reinterpret_cast<uint64_t*>(w8_ring + C::S8 * C::W8);
+    uint64_t* st_empty = st_full + C::DS;
+    uint64_t* peer_full = st_empty + C::DS;
+    uint64_t* w8_full = peer_full + C::DS;
+    uint64_t* w8_empty = w8_full + C::S8;
+    uint64_t* accf_bar = w8_empty + C::S8;  // [2]
+    uint64_t* acce_bar = accf_bar + 2;      // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* s_rows = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(st_full) + C::BAR_BYTES);
+    int* s_tiles = s_rows + (kMaxGroups + 1);
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const uint32_t cta = cluster_rank();  // 0: issues the MMAs; 1: its peer
+    const uint32_t peer = cta ^ 1u;
+    const int pair = blockIdx.x >> 1;
+    const int npairs = gridDim.x >> 1;
+
+    if (tid == 0) {
+        for (int s = 0; s < C::DS; ++s) {
+            mbar_init(&st_full[s], C::CG_WARPS + 1);
+            mbar_init(&st_empty[s], 1);
+            mbar_init(&peer_full[s], 1);
+        }
+        for (int s = 0; s < C::S8; ++s) {
+            mbar_init(&w8_full[s], 1);
+            mbar_init(&w8_empty[s], C::CG_WARPS);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&accf_bar[b], 1);
+            mbar_init(&acce_bar[b], 2 * kEpiWarps);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    for (int i = tid; i <= p.G; i += kThreads)
+        s_rows[i] = p.group_rows ? p.group_rows[i] : (i == 0 ? 0 : static_cast<int>(p.M));
+    if (warp == kMmaWarp) {
+        tmem_alloc_pair(tmem_slot, C::TMEM_COLS);  // the same warp of both CTAs
+        tmem_relinquish_pair();
+    }
+    if (warp == kXWarp && lane == 0) {
+        tma_prefetch_desc(&tm_xh);
+        if (SPLIT == 2) tma_prefetch_desc(&tm_xl);
+    }
+    const int nch = (p.N + kCh - 1) / kCh;
+    const int npair = (nch + 1) / 2;
+    const int nkt = (p.K + kKT - 1) / kKT;
+    const int kper = (nkt + p.ksplit - 1) / p.ksplit;
+    __syncthreads();
+    if (tid == 0) {
+        int acc = 0;
+        bool bad = false;
+        for (int g = 0; g < p.G; ++g) {
+            s_tiles[g] = acc;
+            const int cnt = s_rows[g + 1] - s_rows[g];
+            if (cnt < 0) bad = true;
+            acc += (cnt > 0 ? (cnt + BT - 1) / BT : 0) * npair * p.ksplit;
+        }
+        s_tiles[p.G] = acc;
+        if (bad) {
+            atomicOr(p.err, ERR_GEMM_GROUPS);
+            s_tiles[p.G] = 0;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers are initialised before any remote arrival
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total = s_tiles[p.G];
+
+    if (warp == kW8Warp) {
+        // ================= int8 weight producer: this CTA's 128-channel block
+        if (lane == 0) {
+            int s8 = 0;
+            uint32_t ph8 = 0;
+            bool ok = true;
+            for (int t = pair; t < total && ok && !*abort_flag; t += npairs) {
+                const TileInfo ti = decode_tile_pair<BT>(t, s_rows, s_tiles, p, npair, nkt, kper);
+                // an odd channel count leaves the last pair's odd block past N: it
+                // streams the last real block again (results past N are never stored)
+                const int nb = min(ti.n0 / kCh + static_cast<int>(cta), nch - 1);
+                const int8_t* wsrc =
+                    p.wq + ((static_cast<int64_t>(ti.wg) * p.NT + nb) * p.KT) * (kCh * kKT);
+                for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
+                    if (!pair_wait(&w8_empty[s8], ph8 ^ 1, abort_flag, peer, p.err, false)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&w8_full[s8], C::W8);
+                    bulk_load(w8_ring + s8 * C::W8, wsrc + static_cast<int64_t>(kt) * C::W8, C::W8,
+                              &w8_full[s8]);
+                    if (++s8 == C::S8) {
+                        s8 = 0;
+                        ph8 ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp == kXWarp) {
+        // ================= activation producer: this CTA's half of the token rows
+        if (lane == 0) {
+            int sx = 0;
+            uint32_t phx = 0;
+            bool ok = true;
+            for (int t = pair; t < total && ok && !*abort_flag; t += npairs) {
+                const TileInfo ti = decode_tile_pair<BT>(t, s_rows, s_tiles, p, npair, nkt, kper);
+                const int n_eff = min(BT, (ti.nrows + 31) & ~31);  // MMA N: halves of >= 16 rows
+                const int row = static_cast<int>(ti.row0) + static_cast<int>(cta) * (n_eff / 2);
+                for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
+                    if (!pair_wait(&st_empty[sx], phx ^ 1, abort_flag, peer, p.err, true)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = x_ring + sx * C::XS;
+                    mbar_arrive_expect_tx(&st_full[sx], C::XS);
+                    tma_load_2d(st, &tm_xh, &st_full[sx], kt * kKT, row);
+                    if (SPLIT == 2) tma_load_2d(st + C::XB, &tm_xl, &st_full[sx], kt * kKT, row);
+                    if (++sx == C::DS) {
+                        sx = 0;
+                        phx ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (cta == 0 && lane == 0) {
+            // ================= MMA issuer of the pair
+            int ss = 0;
+            uint32_t phs = 0;
+            int it = 0;
+            bool ok = true;
+            for (int t = pair; t < total && ok && !*abort_flag; t += npairs, ++it) {
+                const TileInfo ti = decode_tile_pair<BT>(t, s_rows, s_tiles, p, npair, nkt, kper);
+                const int b = it & 1;
+                const uint32_t aph = (it >> 1) & 1;
+                // both CTAs' epilogues have drained accumulator b
+                if (!pair_wait(&acce_bar[b], aph ^ 1, abort_flag, peer, p.err, true)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BT);
+                const int n_eff = min(BT, (ti.nrows + 31) & ~31);
+                const uint32_t idesc = idesc_bf16_f32(2 * kCh, static_cast<uint32_t>(n_eff));
+                for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
+                    if (!pair_wait(&st_full[ss], phs, abort_flag, peer, p.err, false) ||
+                        !pair_wait(&peer_full[ss], phs, abort_flag, peer, p.err, true)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t adesc = smem_desc_sw128(smem_u32(w16_ring + ss * C::W16));
+                    const uint64_t bdesc = smem_desc_sw128(smem_u32(x_ring + ss * C::XS));
+                    const uint64_t ldesc = smem_desc_sw128(smem_u32(x_ring + ss * C::XS + C::XB));
+#pragma unroll
+                    for (int kk = 0; kk < kKT / 16; ++kk) {
+                        tc_mma_f16_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc,
+                                        (kt > ti.kt0 || kk > 0) ? 1u : 0u);
+                        if (SPLIT == 2)
+                            tc_mma_f16_pair(d_tmem, adesc + 2 * kk, ldesc + 2 * kk, idesc, 1u);
+                    }
+                    tc_commit_pair(&st_empty[ss], 0x3);  // frees the stage in both CTAs
+                    if (++ss == C::DS) {
+                        ss = 0;
+                        phs ^= 1;
+                    }
+                }
+                if (!ok) break;
+                tc_commit_pair(&accf_bar[b], 0x3);
+            }
+        } else if (cta == 1 && lane == 0) {
+            // ================= relay: this CTA's stage is in -> the even CTA's peer_full
+            int ss = 0;
+            uint32_t phs = 0;
+            bool ok = true;
+            for (int t = pair; t < total && ok && !*abort_flag; t += npairs) {
+                const TileInfo ti = decode_tile_pair<BT>(t, s_rows, s_tiles, p, npair, nkt, kper);
+                for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
+                    if (!pair_wait(&st_full[ss], phs, abort_flag, peer, p.err, false)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_remote(&peer_full[ss], 0);
+                    if (++ss == C::DS) {
+                        ss = 0;
+                        phs ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp < kConvWarps) {
+        // ================= converters (this CTA's channel block)
+        const int group = warp / C::CG_WARPS;
+        const int gtid = tid % C::CG_THREADS;
+        uint32_t kc = 0;
+        bool ok = true;
+        for (int t = pair; t < total && ok && !*abort_flag; t += npairs) {
+            const TileInfo ti = decode_tile_pair<BT>(t, s_rows, s_tiles, p, npair, nkt, kper);
+            for (int kt = ti.kt0; kt < ti.kt1; ++kt, ++kc) {
+                if (static_cast<int>(kc % C::CG) != group) continue;
+                const int s16 = static_cast<int>(kc % C::DS);
+                const uint32_t ph16 = (kc / C::DS) & 1;
+                const int s8 = static_cast<int>(kc % C::S8);
+                const uint32_t ph8 = (kc / C::S8) & 1;
+                if (!pair_wait(&w8_full[s8], ph8, abort_flag, peer, p.err, false) ||
+                    !pair_wait(&st_empty[s16], ph16 ^ 1, abort_flag, peer, p.err, true)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* st = w16_ring + s16 * C::W16;
+                const uint8_t* w8 = w8_ring + s8 * C::W8;
+#pragma unroll
+                for (int i = 0; i < 512 / C::CG_THREADS; ++i) {
+                    const int item = gtid + C::CG_THREADS * i;
+                    const int r = item >> 2;
+                    const int ch = item & 3;
+                    const uint4 v = *reinterpret_cast<const uint4*>(w8 + r * 64 + ch * 16);
+                    const uint2 a0 = i8x4_to_bf16x4(v.x);
+                    const uint2 a1 = i8x4_to_bf16x4(v.y);
+                    const uint2 a2 = i8x4_to_bf16x4(v.z);
+                    const uint2 a3 = i8x4_to_bf16x4(v.w);
+                    uint8_t* row = st + r * 128;
+                    const int sw = r & 7;
+                    *reinterpret_cast<uint4*>(row + (((2 * ch) ^ sw) << 4)) =
+                        make_uint4(a0.x, a0.y, a1.x, a1.y);
+                    *reinterpret_cast<uint4*>(row + (((2 * ch + 1) ^ sw) << 4)) =
+                        make_uint4(a2.x, a2.y, a3.x, a3.y);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&st_full[s16]);
+                    mbar_arrive(&w8_empty[s8]);
+                }
+            }
+        }
+    } else if (warp < kEpiWarp0 + kEpiWarps) {
+        // ================= epilogue: this CTA's 128 channels x the tile's columns
+        const int ei = warp - kEpiWarp0;
+        const int q = ei & 3;
+        const int h = ei >> 2;
+        int it = 0;
+        for (int t = pair; t < total && !__any_sync(0xFFFFFFFFu, *abort_flag != 0);
+             t += npairs, ++it) {
+            const TileInfo ti = decode_tile_pair<BT>(t, s_rows, s_tiles, p, npair, nkt, kper);
+            const int b = it & 1;
+            const uint32_t aph = (it >> 1) & 1;
+            if (!__all_sync(0xFFFFFFFFu,
+                            pair_wait(&accf_bar[b], aph, abort_flag, peer, p.err, true)))
+                break;
+            tc_fence_after();
+            const int n0 = ti.n0 + static_cast<int>(cta) * kCh;
+            const int n = n0 + q * 32 + lane;
+            const bool nvalid = n < p.N;
+            const float sc =
+                nvalid ? __ldg(p.scale + static_cast<int64_t>(ti.wg) * p.N + n) : 0.0f;
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(b * BT);
+            const int cbeg = h * C::EPI_COLS;
+            const int cend = min(cbeg + C::EPI_COLS, ti.nrows);
+#pragma unroll 1
+            for (int c0 = cbeg; c0 < cend; c0 += 16) {
+                int my_orow = 0;
+                float my_rs = 1.0f;
+                const int64_t my_row = ti.row0 + c0 + (lane & 15);
+                if (lane < 16 && c0 + lane < ti.nrows) {
+                    my_orow = p.rowmap ? __ldg(p.rowmap + my_row) : static_cast<int>(my_row);
+                    if (p.rowscale) my_rs = __ldg(p.rowscale + my_row);
+                }
+                uint32_t r[16];
+                tc_ld_32x32b_x16(tbase + c0, r);
+                tc_wait_ld();
+                if (p.red_v4) {
+                    const int qi = lane & 3;
+                    const bool qvalid = n0 + q * 32 + (lane & ~3) < p.N;
+                    float* obase = reinterpret_cast<float*>(p.out) + n0 + q * 32 + (lane & ~3);
+#pragma unroll
+                    for (int j4 = 0; j4 < 16; j4 += 4) {
+                        float a[4];
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
+                            a[c] = __uint_as_float(r[j4 + c]) * sc *
+                                   __shfl_sync(0xFFFFFFFFu, my_rs, j4 + c);
+                        {
+                            const float s0 = (qi & 1) ? a[0] : a[1];
+                            const float s1 = (qi & 1) ? a[2] : a[3];
+                            const float t0 = __shfl_xor_sync(0xFFFFFFFFu, s0, 1);
+                            const float t1 = __shfl_xor_sync(0xFFFFFFFFu, s1, 1);
+                            if (qi & 1) {
+                                a[0] = t0;
+                                a[2] = t1;
+                            } else {
+                                a[1] = t0;
+                                a[3] = t1;
+                            }
+                        }
+                        {
+                            const float s0 = (qi & 2) ? a[0] : a[2];
+                            const float s1 = (qi & 2) ? a[1] : a[3];
+                            const float t0 = __shfl_xor_sync(0xFFFFFFFFu, s0, 2);
+                            const float t1 = __shfl_xor_sync(0xFFFFFFFFu, s1, 2);
+                            if (qi & 2) {
+                                a[0] = t0;
+                                a[1] = t1;
+                            } else {
+                                a[2] = t0;
+                                a[3] = t1;
+                            }
+                        }
+                        const int64_t orow = __shfl_sync(0xFFFFFFFFu, my_orow, j4 + qi);
+                        if (qvalid && c0 + j4 + qi < ti.nrows)
+                            red_add_v4(obase + orow * p.ldo, a[0], a[1], a[2], a[3]);
+                    }
+                    continue;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int64_t orow = __shfl_sync(0xFFFFFFFFu, my_orow, j);
+                    const float rs = __shfl_sync(0xFFFFFFFFu, my_rs, j);
+                    if (nvalid && c0 + j < ti.nrows) {
+                        float v = __uint_as_float(r[j]) * sc * rs;
+                        if (p.relu) v = fmaxf(v, 0.0f);
+                        if (p.out_bf16) {
+                            const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+                            reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + n] = hi;
+                            if (p.out_lo)
+                                reinterpret_cast<__nv_bfloat16*>(p.out_lo)[orow * p.ldo + n] =
+                                    __float2bfloat16_rn(v - __bfloat162float(hi));
+                        } else if (p.atomic_add) {
+                            atomicAdd(reinterpret_cast<float*>(p.out) + orow * p.ldo + n, v);
+                        } else {
+                            reinterpret_cast<float*>(p.out)[orow * p.ldo + n] = v;
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (cta == 0)
+                    mbar_arrive(&acce_bar[b]);
+                else
+                    mbar_arrive_remote(&acce_bar[b], 0);
+            }
+        }
+    }
+
+    // ---- teardown: the pair's MMAs, commits and remote arrivals are all done
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    if (warp == kMmaWarp) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+}
+
 template <int BT, int SPLIT>
 aem_status launch_tc(const GemmArgs& a, const TcParams& p, int grid, cudaStream_t s) {
     using C = Cfg<BT, SPLIT>;
@@ -567,6 +1037,60 @@ aem_status launch_tc(const GemmArgs& a, const TcParams& p, int grid, cudaStream_
     return AEM_OK;
 }
 
+template <int BT, int SPLIT>
+aem_status launch_tc_pair(const GemmArgs& a, const TcParams& p, int pairs, cudaStream_t s) {
+    using C = Cfg2<BT, SPLIT>;
+    const QWeight& w = *a.w;
+    CUtensorMap th, tl;
+    AEM_TRY(make_tmap_2d(&th, a.x_hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                         static_cast<uint64_t>(w.K), static_cast<uint64_t>(a.M), kKT, C::HB,
+                         CU_TENSOR_MAP_SWIZZLE_128B));
+    if (SPLIT == 2)
+        AEM_TRY(make_tmap_2d(&tl, a.x_lo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                             static_cast<uint64_t>(w.K), static_cast<uint64_t>(a.M), kKT, C::HB,
+                             CU_TENSOR_MAP_SWIZZLE_128B));
+    else
+        tl = th;
+    auto kern = qgemm_tc_pair_kernel<BT, SPLIT>;
+    AEM_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    kern<<<2 * pairs, kThreads, C::SMEM, s>>>(th, tl, p);
+    AEM_CHECK_LAUNCH();
+    count_launches(1);
+    return AEM_OK;
+}
+
+template <int SPLIT>
+aem_status launch_pair_bt(int bt, const GemmArgs& a, const TcParams& p, int pairs,
+                          cudaStream_t s) {
+    switch (bt) {
+        case 64: return launch_tc_pair<64, SPLIT>(a, p, pairs, s);
+        case 128: return launch_tc_pair<128, SPLIT>(a, p, pairs, s);
+        default: return launch_tc_pair<256, SPLIT>(a, p, pairs, s);
+    }
+}
+
+// Pairs of SMs that can run the pair kernel at once on `dev` (one CTA per SM).
+int max_pairs(int dev) {
+    static int cache[64] = {0};
+    if (dev < 0 || dev >= 64) return 0;
+    if (cache[dev] == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * 512, 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = Cfg2<256, 1>::SMEM;
+        int n = 0;
+        auto kern = qgemm_tc_pair_kernel<256, 1>;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Cfg2<256, 1>::SMEM) != cudaSuccess ||
+            cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+            cudaGetLastError();
+            n = sm_count(dev) / 2;
+        }
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
 template <int SPLIT>
 aem_status launch_bt(int bt, const GemmArgs& a, const TcParams& p, int grid, cudaStream_t s) {
     switch (bt) {
@@ -585,6 +1109,12 @@ int64_t tiles_estimate(int64_t M, int G, int bt, int64_t nch, int ks) {
 }
 
 }  // namespace
+
+namespace {
+std::atomic<int> g_pair_mode{-1};
+}  // namespace
+
+int gemm_pair_mode() { return g_pair_mode.load(std::memory_order_relaxed); }
 
 aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
     AEM_REQUIRE(a.w != nullptr, "qgemm: weight handle is NULL");
@@ -648,9 +1178,27 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
     // Upper bound of the tiles of all groups: sum_g ceil(rows_g / bt) <= ceil(M / bt) + (#non-empty groups).
     const int64_t rows = a.max_rows > 0 ? a.max_rows : a.M;
     const int64_t tiles_ub = ((rows + bt - 1) / bt + std::min<int64_t>(a.G, rows)) * nch * ks;
+    // SM pairs (cta_group::2) for large token tiles: half the activation bytes
+    // per SM and half the MMA issue per FLOP
+    const int mode = gemm_pair_mode();
+    if (bt >= 64 && (mode == 1 || (mode < 0 && bt >= 128))) {
+        const int64_t ptiles = ((rows + bt - 1) / bt + std::min<int64_t>(a.G, rows)) *
+                               ((nch + 1) / 2) * ks;
+        const int pairs =
+            static_cast<int>(std::min<int64_t>(max_pairs(dev), std::max<int64_t>(1, ptiles)));
+        if (a.x_lo) return launch_pair_bt<2>(bt, a, p, pairs, s);
+        return launch_pair_bt<1>(bt, a, p, pairs, s);
+    }
     const int grid = static_cast<int>(std::min<int64_t>(sms, std::max<int64_t>(1, tiles_ub)));
     if (a.x_lo) return launch_bt<2>(bt, a, p, grid, s);
     return launch_bt<1>(bt, a, p, grid, s);
 }
 
 }  // namespace aem
+
+extern "C" aem_status aem_set_gemm_pairs(int mode) {
+    AEM_REQUIRE(mode == -1 || mode == 0 || mode == 1,
+                "aem_set_gemm_pairs: mode %d is not -1, 0 or 1", mode);
+    aem::g_pair_mode.store(mode, std::memory_order_relaxed);
+    return AEM_OK;
+}

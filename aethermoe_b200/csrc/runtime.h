@@ -78,8 +78,14 @@ struct Gate {
     int64_t D = 0, E = 0, Dpad = 0, Epad = 0;
     float* wt = nullptr;
     float* bias = nullptr;
+    // The same weights in expert blocks for the small-batch kernel:
+    // [Epad/eb][Dpad/4][eb][4] float32 -- block b holds experts
+    // [b*eb, (b+1)*eb), and one chunk of d of one block is contiguous.
+    float* wblk = nullptr;
+    int eb = 0;
 };
 int gate_epad(int64_t E);
+int gate_small_eb(int64_t Epad);  // experts per CTA of the small-batch kernel
 
 // Packed INT8 weight (device), pre-tiled for the GEMM's weight stream:
 // [G][NT][KT][128][64] int8 with NT = ceil(N/128), KT = ceil(K/64): every
@@ -137,6 +143,7 @@ struct GemmArgs {
                                // device (0 = use M); only picks the token tile
 };
 aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s);
+int gemm_pair_mode();  // aem_set_gemm_pairs: -1 automatic, 0 never, 1 from 64-row tiles
 
 // float32 [M, K] -> bf16 hi [M, K] + bf16 lo [M, K] (lo may be nullptr), or
 // bf16 copy when the input is already bf16 (hi only).

@@ -163,12 +163,23 @@ def test_groups_select_their_weights(cuda):
         _close(out.cpu().numpy(), O.qgemm(x, q[grp], s[grp:grp + 1]))
 
 
+@pytest.fixture(params=["single", "pairs"])
+def gemm_form(cuda, request):
+    """Runs a test with the single-SM GEMM only (aem_set_gemm_pairs(0)) and
+    with SM pairs from 64-row token tiles on (aem_set_gemm_pairs(1))."""
+    from aethermoe_b200 import _lib
+    _lib.check(_lib.lib().aem_set_gemm_pairs(0 if request.param == "single" else 1))
+    yield request.param
+    _lib.check(_lib.lib().aem_set_gemm_pairs(-1))
+
+
 @pytest.mark.parametrize("tile", [256, 128, 64])
 @pytest.mark.parametrize("mode", ["relu_bf16", "scaled_add"])
-def test_grouped_ragged_tiles(cuda, tile, mode):
+def test_grouped_ragged_tiles(cuda, gemm_form, tile, mode):
     """aem_grouped_qgemm over ragged groups (empty, 1 row, 191-193 rows,
-    several tiles) at token tiles 256, 128 and 64; a partial output-channel
-    block (N = 300).
+    several tiles) at token tiles 256, 128 and 64, on single SMs and on SM
+    pairs; a partial output-channel block (N = 300: three 128-channel blocks,
+    so the last SM pair has a block past N).
     relu_bf16: the up projection's epilogue; scaled_add: the down
     projection's (gate-weight row scale, float32 red.add into mapped rows)."""
     import torch
@@ -284,7 +295,7 @@ def test_decode_sizes_dense(qg, m, k, n, dtype):
 
 
 @pytest.mark.parametrize("m", [16, 40, 64, 200, 1000])
-def test_repeated_launches_stay_consistent(cuda, m):
+def test_repeated_launches_stay_consistent(cuda, gemm_form, m):
     """Forty back-to-back launches per token tile (16 .. 256 rows): every
     output equal to the first up to split-K reassociation, and no bounded wait
     ran out.  Guards the ring
@@ -313,3 +324,39 @@ def test_repeated_launches_stay_consistent(cuda, m):
         # split-K adds partial sums with float32 atomics in any order: a few
         # ulp of reassociation; stale operands would be off by O(1)
         np.testing.assert_allclose(o.cpu().numpy(), first, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("m,dtype", [(512, "bf16"), (1000, "f32"), (4096, "bf16")])
+def test_pairs_match_single_sms(cuda, m, dtype):
+    """The same dense GEMM on single SMs and on SM pairs: both within the
+    GEMM tolerance of the float64 oracle and within float32 reassociation of
+    each other."""
+    import torch
+    from aethermoe_b200 import _lib
+    rng = np.random.default_rng(m + len(dtype))
+    K, N = 2048, 1408  # 11 channel blocks: the last pair holds one real block
+    q = rng.integers(-127, 128, size=(K, N), dtype=np.int8)
+    s = (rng.random(size=(1, N)) * 1e-3 + 1e-4).astype(np.float32)
+    w = _lib.QWeight(q, s, 0)
+    x = rng.normal(size=(m, K)).astype(np.float32)
+    if dtype == "bf16":
+        x = O.bf16_round(x)
+        xt = torch.from_numpy((x.view(np.uint32) >> 16).astype(np.uint16).view(np.int16))
+        xt, code = xt.to(cuda).view(torch.bfloat16), _lib.BF16
+    else:
+        xt, code = torch.from_numpy(x).to(cuda), _lib.F32
+    stream = torch.cuda.current_stream().cuda_stream
+    res = {}
+    for mode in (0, 1):
+        _lib.check(_lib.lib().aem_set_gemm_pairs(mode))
+        o = torch.empty((m, N), dtype=torch.float32, device=cuda)
+        _lib.check(_lib.lib().aem_qgemm(w.handle, 0, xt.data_ptr(), code, m, o.data_ptr(),
+                                        stream), "aem_qgemm")
+        torch.cuda.synchronize()
+        res[mode] = o.cpu().numpy()
+    _lib.check(_lib.lib().aem_set_gemm_pairs(-1))
+    _lib.check(_lib.lib().aem_device_status(None), "aem_device_status")
+    ref = x.astype(np.float64) @ (q.astype(np.float64) * s.astype(np.float64))
+    _close(res[0], ref)
+    _close(res[1], ref)
+    np.testing.assert_allclose(res[1], res[0], rtol=1e-5, atol=1e-5)
