@@ -1111,7 +1111,7 @@ int64_t tiles_estimate(int64_t M, int G, int bt, int64_t nch, int ks) {
 }  // namespace
 
 namespace {
-std::atomic<int> g_pair_mode{-1};
+std::atomic<int> g_pair_mode{0};
 }  // namespace
 
 int gemm_pair_mode() { return g_pair_mode.load(std::memory_order_relaxed); }
