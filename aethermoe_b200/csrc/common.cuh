@@ -271,11 +271,23 @@ __device__ __forceinline__ uint32_t mapa_u32(const void* local, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
     return r;
 }
-// One arrival on an mbarrier of another CTA of the cluster (release, cluster scope).
+// One arrival on the mbarrier at `local_twin`'s offset in CTA `rank` of the
+// cluster (the default release semantics, as for a local arrival).
 __device__ __forceinline__ void mbar_arrive_remote(const uint64_t* local_twin, uint32_t rank) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
-                     mapa_u32(local_twin, rank))
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(mapa_u32(local_twin, rank))
                  : "memory");
+}
+// TMA 2-D tile load into this CTA's shared memory whose completion (bytes)
+// is counted on the mbarrier at `bar_local_twin`'s offset in CTA `bar_rank`
+// of this CTA's tcgen05 pair (no multicast).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* map,
+                                                 const uint64_t* bar_local_twin,
+                                                 uint32_t bar_rank, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(mapa_u32(bar_local_twin, bar_rank)), "r"(x), "r"(y)
+        : "memory");
 }
 __device__ __forceinline__ void st_remote_u32(const void* local_twin, uint32_t rank, uint32_t v) {
     asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(mapa_u32(local_twin, rank)), "r"(v)

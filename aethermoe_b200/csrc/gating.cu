@@ -373,17 +373,48 @@ __device__ __forceinline__ void st_cluster_f32(const float* local, uint32_t rank
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
 }
 
+// Raw activations of 4 consecutive d as loaded from shared memory (float32:
+// 16 bytes; bf16: 8 bytes in .x/.y), widened to float32 only when used, so
+// that a block of loads can be issued ahead of the add chain.
 template <typename XT>
-__device__ __forceinline__ float4 load_x4(const unsigned char* p);
+__device__ __forceinline__ uint4 load_x4_raw(const unsigned char* p);
 template <>
-__device__ __forceinline__ float4 load_x4<float>(const unsigned char* p) {
-    return *reinterpret_cast<const float4*>(p);
+__device__ __forceinline__ uint4 load_x4_raw<float>(const unsigned char* p) {
+    return *reinterpret_cast<const uint4*>(p);
 }
 template <>
-__device__ __forceinline__ float4 load_x4<__nv_bfloat16>(const unsigned char* p) {
+__device__ __forceinline__ uint4 load_x4_raw<__nv_bfloat16>(const unsigned char* p) {
     const uint2 u = *reinterpret_cast<const uint2*>(p);
-    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
-                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+    return make_uint4(u.x, u.y, 0u, 0u);
+}
+template <typename XT>
+__device__ __forceinline__ float4 widen_x4(uint4 r);
+template <>
+__device__ __forceinline__ float4 widen_x4<float>(uint4 r) {
+    return make_float4(__uint_as_float(r.x), __uint_as_float(r.y), __uint_as_float(r.z),
+                       __uint_as_float(r.w));
+}
+template <>
+__device__ __forceinline__ float4 widen_x4<__nv_bfloat16>(uint4 r) {
+    return make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u),
+                       __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xFFFF0000u));
+}
+
+// One chain step over 4 consecutive d: float32 product, float32 add, in order.
+template <bool EXACT>
+__device__ __forceinline__ float chain4(float acc, float4 x, float4 w) {
+    if constexpr (EXACT) {
+        acc = __fadd_rn(acc, __fmul_rn(x.x, w.x));
+        acc = __fadd_rn(acc, __fmul_rn(x.y, w.y));
+        acc = __fadd_rn(acc, __fmul_rn(x.z, w.z));
+        acc = __fadd_rn(acc, __fmul_rn(x.w, w.w));
+    } else {
+        acc = fmaf(x.x, w.x, acc);
+        acc = fmaf(x.y, w.y, acc);
+        acc = fmaf(x.z, w.z, acc);
+        acc = fmaf(x.w, w.w, acc);
+    }
+    return acc;
 }
 
 template <int EPAD, typename XT, bool EXACT>
@@ -452,21 +483,42 @@ __global__ void __launch_bounds__(kSmallThreads)
             const int n4 = min(kSmallDK, D - c * kSmallDK) >> 2;
             const float4* ws = reinterpret_cast<const float4*>(wring + st * C::WST) + el;
             const unsigned char* xs = xring + st * C::XST + tl * C::XROW;
-#pragma unroll 8
-            for (int q = 0; q < n4; ++q) {
-                const float4 wv = ws[q * EB];
-                const float4 xv = load_x4<XT>(xs + q * 4 * C::XB);
-                if constexpr (EXACT) {
-                    acc = __fadd_rn(acc, __fmul_rn(xv.x, wv.x));
-                    acc = __fadd_rn(acc, __fmul_rn(xv.y, wv.y));
-                    acc = __fadd_rn(acc, __fmul_rn(xv.z, wv.z));
-                    acc = __fadd_rn(acc, __fmul_rn(xv.w, wv.w));
-                } else {
-                    acc = fmaf(xv.x, wv.x, acc);
-                    acc = fmaf(xv.y, wv.y, acc);
-                    acc = fmaf(xv.z, wv.z, acc);
-                    acc = fmaf(xv.w, wv.w, acc);
+            if (n4 == kSmallDK / 4) {
+                // A whole chunk: operands of the next 32 d are loaded into
+                // registers while the chain runs over the current 32 (one warp
+                // per scheduler, so the loads must be issued well ahead).
+                constexpr int QB = 8;
+                float4 wa[QB], wb[QB];
+                uint4 xa[QB], xb[QB];
+#pragma unroll
+                for (int i = 0; i < QB; ++i) {
+                    wa[i] = ws[i * EB];
+                    xa[i] = load_x4_raw<XT>(xs + i * 4 * C::XB);
                 }
+#pragma unroll
+                for (int b = 0; b < kSmallDK / 4 / QB; b += 2) {
+#pragma unroll
+                    for (int i = 0; i < QB; ++i) {
+                        wb[i] = ws[((b + 1) * QB + i) * EB];
+                        xb[i] = load_x4_raw<XT>(xs + ((b + 1) * QB + i) * 4 * C::XB);
+                    }
+#pragma unroll
+                    for (int i = 0; i < QB; ++i) acc = chain4<EXACT>(acc, widen_x4<XT>(xa[i]), wa[i]);
+                    if (b + 2 < kSmallDK / 4 / QB) {
+#pragma unroll
+                        for (int i = 0; i < QB; ++i) {
+                            wa[i] = ws[((b + 2) * QB + i) * EB];
+                            xa[i] = load_x4_raw<XT>(xs + ((b + 2) * QB + i) * 4 * C::XB);
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < QB; ++i) acc = chain4<EXACT>(acc, widen_x4<XT>(xb[i]), wb[i]);
+                }
+            } else {
+#pragma unroll 4
+                for (int q = 0; q < n4; ++q)
+                    acc = chain4<EXACT>(acc, widen_x4<XT>(load_x4_raw<XT>(xs + q * 4 * C::XB)),
+                                        ws[q * EB]);
             }
             __syncwarp();
             if (lane == 0) dev::mbar_arrive(&empty[st]);

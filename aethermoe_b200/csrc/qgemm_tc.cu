@@ -558,18 +558,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 // columns.  Per SM and K step this moves 8 + 16 + BT/2*128 bytes into shared
 // memory instead of 8 + 16 + BT*128 (and reads as much back), and one thread
 // issues the MMAs of two SMs.
-// Synchronisation (same barrier offsets in both CTAs):
-//   st_full[s]   local: the stage's activation bytes + one arrival per converter warp;
-//   peer_full[s] even CTA only: the odd CTA's relay thread arrives (remote,
-//                release.cluster) once the odd CTA's st_full[s] completed;
+// Synchronisation (same barrier offsets in both CTAs; every wait and arrival
+// uses the default CTA-scope semantics, as the tcgen05 pipelines of CUTLASS do):
+//   st_full[s]   even CTA: both CTAs' activation TMA bytes (the odd CTA's
+//                loads complete on the even CTA's barrier, .cta_group::2),
+//                its producer's expect-tx arrival and one arrival per
+//                converter warp of BOTH CTAs (the odd CTA's arrive remotely);
 //   st_empty[s]  both: one tcgen05.commit multicast to the pair frees both stages;
 //   accf[b]      both: the commit of a tile's last K step (multicast);
 //   acce[b]      even CTA: 8 local + 8 remote epilogue-warp arrivals.
 // Every wait is bounded; a timeout sets the abort flag in both CTAs.  The pair
 // meets at a cluster barrier after set-up and before teardown, so no CTA
 // exits while its peer may still touch its shared memory.
-constexpr int kPairWarpRelay = kMmaWarp;  // odd CTA: warp 17 relays stage readiness
-
 template <int BT, int SPLIT>
 struct Cfg2 {
     static constexpr int HB = BT / 2;              // token rows per CTA (MMA N / 2)
@@ -585,7 +585,7 @@ struct Cfg2 {
     static constexpr int CG = CG_RAW < AEM_QGEMM_MAX_CONV_GROUPS ? CG_RAW : AEM_QGEMM_MAX_CONV_GROUPS;
     static constexpr int S8 = ((S8_RAW > 12 ? 12 : S8_RAW) / CG) * CG;
     static constexpr int TMEM_COLS = 2 * BT < 32 ? 32 : 2 * BT;
-    static constexpr int BAR_BYTES = (3 * DS + 2 * S8 + 4) * 8 + 16;
+    static constexpr int BAR_BYTES = (2 * DS + 2 * S8 + 4) * 8 + 16;
     static constexpr int TAB_BYTES = 2 * (kMaxGroups + 1) * 4;
     static constexpr int SMEM = 1024 + DS * (W16 + XS) + S8 * W8 + BAR_BYTES + TAB_BYTES;
     static constexpr int CG_WARPS = kConvWarps / CG;
@@ -630,14 +630,11 @@ __device__ __forceinline__ TileInfo decode_tile_pair(int t, const int* s_rows, c
 
 // Bounded wait that, on giving up, raises the abort flag of both CTAs.
 __device__ __forceinline__ bool pair_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          uint32_t peer, int* err, bool cluster_scope) {
-    auto probe = [&]() {
-        return cluster_scope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
-    };
-    if (probe()) return true;
+                                          uint32_t peer, int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
-        if (probe()) return true;
+        if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
         if (globaltimer_ns() - t0 > 2000000000ull) {
             *abort_flag = 1;
@@ -661,8 +658,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t* w8_ring = x_ring + C::DS * C::XS;
     uint64_t* st_full = reinterpret_cast<uint64_t*>(w8_ring + C::S8 * C::W8);
     uint64_t* st_empty = st_full + C::DS;
-    uint64_t* peer_full = st_empty + C::DS;
-    uint64_t* w8_full = peer_full + C::DS;
+    uint64_t* w8_full = st_empty + C::DS;
     uint64_t* w8_empty = w8_full + C::S8;
     uint64_t* accf_bar = w8_empty + C::S8;  // [2]
     uint64_t* acce_bar = accf_bar + 2;      // [2]
@@ -681,9 +677,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
     if (tid == 0) {
         for (int s = 0; s < C::DS; ++s) {
-            mbar_init(&st_full[s], C::CG_WARPS + 1);
+            mbar_init(&st_full[s], 2 * C::CG_WARPS + 1);  // used in the even CTA
             mbar_init(&st_empty[s], 1);
-            mbar_init(&peer_full[s], 1);
         }
         for (int s = 0; s < C::S8; ++s) {
             mbar_init(&w8_full[s], 1);
@@ -747,7 +742,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const int8_t* wsrc =
                     p.wq + ((static_cast<int64_t>(ti.wg) * p.NT + nb) * p.KT) * (kCh * kKT);
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                    if (!pair_wait(&w8_empty[s8], ph8 ^ 1, abort_flag, peer, p.err, false)) {
+                    if (!pair_wait(&w8_empty[s8], ph8 ^ 1, abort_flag, peer, p.err)) {
                         ok = false;
                         break;
                     }
@@ -772,14 +767,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const int n_eff = min(BT, (ti.nrows + 31) & ~31);  // MMA N: halves of >= 16 rows
                 const int row = static_cast<int>(ti.row0) + static_cast<int>(cta) * (n_eff / 2);
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                    if (!pair_wait(&st_empty[sx], phx ^ 1, abort_flag, peer, p.err, true)) {
+                    if (!pair_wait(&st_empty[sx], phx ^ 1, abort_flag, peer, p.err)) {
                         ok = false;
                         break;
                     }
                     uint8_t* st = x_ring + sx * C::XS;
-                    mbar_arrive_expect_tx(&st_full[sx], C::XS);
-                    tma_load_2d(st, &tm_xh, &st_full[sx], kt * kKT, row);
-                    if (SPLIT == 2) tma_load_2d(st + C::XB, &tm_xl, &st_full[sx], kt * kKT, row);
+                    // both halves' bytes complete on the even CTA's barrier
+                    if (cta == 0) mbar_arrive_expect_tx(&st_full[sx], 2 * C::XS);
+                    tma_load_2d_pair(st, &tm_xh, &st_full[sx], 0, kt * kKT, row);
+                    if (SPLIT == 2)
+                        tma_load_2d_pair(st + C::XB, &tm_xl, &st_full[sx], 0, kt * kKT, row);
                     if (++sx == C::DS) {
                         sx = 0;
                         phx ^= 1;
@@ -799,14 +796,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const int b = it & 1;
                 const uint32_t aph = (it >> 1) & 1;
                 // both CTAs' epilogues have drained accumulator b
-                if (!pair_wait(&acce_bar[b], aph ^ 1, abort_flag, peer, p.err, true)) break;
+                if (!pair_wait(&acce_bar[b], aph ^ 1, abort_flag, peer, p.err)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BT);
                 const int n_eff = min(BT, (ti.nrows + 31) & ~31);
                 const uint32_t idesc = idesc_bf16_f32(2 * kCh, static_cast<uint32_t>(n_eff));
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                    if (!pair_wait(&st_full[ss], phs, abort_flag, peer, p.err, false) ||
-                        !pair_wait(&peer_full[ss], phs, abort_flag, peer, p.err, true)) {
+                    // both CTAs' activation halves and converted weights are in
+                    if (!pair_wait(&st_full[ss], phs, abort_flag, peer, p.err)) {
                         ok = false;
                         break;
                     }
@@ -830,25 +827,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (!ok) break;
                 tc_commit_pair(&accf_bar[b], 0x3);
             }
-        } else if (cta == 1 && lane == 0) {
-            // ================= relay: this CTA's stage is in -> the even CTA's peer_full
-            int ss = 0;
-            uint32_t phs = 0;
-            bool ok = true;
-            for (int t = pair; t < total && ok && !*abort_flag; t += npairs) {
-                const TileInfo ti = decode_tile_pair<BT>(t, s_rows, s_tiles, p, npair, nkt, kper);
-                for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                    if (!pair_wait(&st_full[ss], phs, abort_flag, peer, p.err, false)) {
-                        ok = false;
-                        break;
-                    }
-                    mbar_arrive_remote(&peer_full[ss], 0);
-                    if (++ss == C::DS) {
-                        ss = 0;
-                        phs ^= 1;
-                    }
-                }
-            }
         }
     } else if (warp < kConvWarps) {
         // ================= converters (this CTA's channel block)
@@ -864,8 +842,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const uint32_t ph16 = (kc / C::DS) & 1;
                 const int s8 = static_cast<int>(kc % C::S8);
                 const uint32_t ph8 = (kc / C::S8) & 1;
-                if (!pair_wait(&w8_full[s8], ph8, abort_flag, peer, p.err, false) ||
-                    !pair_wait(&st_empty[s16], ph16 ^ 1, abort_flag, peer, p.err, true)) {
+                if (!pair_wait(&w8_full[s8], ph8, abort_flag, peer, p.err) ||
+                    !pair_wait(&st_empty[s16], ph16 ^ 1, abort_flag, peer, p.err)) {
                     ok = false;
                     break;
                 }
@@ -891,7 +869,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(&st_full[s16]);
+                    if (cta == 0)
+                        mbar_arrive(&st_full[s16]);
+                    else
+                        mbar_arrive_remote(&st_full[s16], 0);
                     mbar_arrive(&w8_empty[s8]);
                 }
             }
@@ -908,7 +889,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int b = it & 1;
             const uint32_t aph = (it >> 1) & 1;
             if (!__all_sync(0xFFFFFFFFu,
-                            pair_wait(&accf_bar[b], aph, abort_flag, peer, p.err, true)))
+                            pair_wait(&accf_bar[b], aph, abort_flag, peer, p.err)))
                 break;
             tc_fence_after();
             const int n0 = ti.n0 + static_cast<int>(cta) * kCh;

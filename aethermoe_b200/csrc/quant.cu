@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(kDecodeThreads)
             xs[mm][xpad(kk)] = v;
         }
         __syncthreads();
-#pragma unroll 2
+#pragma unroll 4
         for (int kb = 0; kb < nkb; ++kb) {
             const int8_t* src = wtile + static_cast<int64_t>(kc + kb) * kWTileBytes;
             uint4 wv[4];
@@ -274,9 +274,25 @@ aem_status launch_qgemm_decode(const GemmArgs& a, cudaStream_t s) {
     // without ReLU, and either an accumulating caller or a plain store into
     // rows that are zeroed first (no row map)
     const bool can_split = !a.out_bf16 && !a.relu && (a.atomic_add || a.rowmap == nullptr);
+    // one wave: at most as many CTAs as can be resident at once (a second,
+    // partial wave of a few CTAs would double the time)
+    int per_sm = 8;
+    {
+        int n = 0;
+        auto k1 = qgemm_decode_kernel<1>;
+        auto k4 = qgemm_decode_kernel<4>;
+        if ((a.M <= 1 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k1, kDecodeThreads, 0)
+                      : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k4, kDecodeThreads, 0)) ==
+                cudaSuccess &&
+            n > 0)
+            per_sm = n;
+        else
+            cudaGetLastError();
+    }
+    const int64_t slots = static_cast<int64_t>(per_sm) * sms;
     int64_t ks = 1;
     if (can_split) {
-        ks = std::max<int64_t>(1, (8 * static_cast<int64_t>(sms) + busy - 1) / busy);
+        ks = std::max<int64_t>(1, slots / busy);
         ks = std::min<int64_t>(ks, w.KT);
     }
     const int kper = static_cast<int>((w.KT + ks - 1) / ks);
