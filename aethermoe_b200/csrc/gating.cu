@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(WARPS * 32)
 // thread-block cluster (EB experts each) and the tokens over clusters (TT per
 // CTA); every consumer thread owns ONE (token, expert) logit and walks d in
 // increasing order (EXACT: float32 product, float32 add).  A producer warp
-// streams 128-wide chunks of d -- the CTA's expert block of the weights (one
+// streams chunks of d (up to 512 wide) -- the CTA's expert block of the weights (one
 // contiguous bulk copy in the expert-block layout) and its tokens' activation
 // rows (one bulk copy per row) -- through a ring of mbarrier-tracked stages,
 // so no CTA-wide barrier interrupts the chains.  At the end every thread
@@ -335,8 +335,7 @@ __global__ void __launch_bounds__(WARPS * 32)
 // the same selection as the large-batch kernel.  Every mbarrier wait is
 // bounded (globaltimer); a timeout sets an error bit and the roles run out,
 // so the cluster barrier is always reached by every thread.
-constexpr int kSmallDK = 128;     // d per stage
-constexpr int kSmallStages = 6;
+constexpr int kSmallStages = 4;
 constexpr int kSmallCons = 128;   // consumer threads (warps 0-3); warp 4 produces
 constexpr int kSmallThreads = kSmallCons + 32;
 
@@ -345,14 +344,19 @@ struct SmallCfg {
     static constexpr int EB = EPAD / 8 > 8 ? EPAD / 8 : 8;  // experts per CTA
     static constexpr int CL = EPAD / EB;                   // CTAs per cluster (<= 8)
     static constexpr int TT = kSmallCons / EB;             // tokens per CTA
+    // d per stage: 16 KB of weights per stage (512 d for up to 64 experts),
+    // so four stages keep about 4 us of the add chain's operands in flight
+    // with few, large bulk copies
+    static constexpr int DK = 4096 / EB > 512 ? 512 : 4096 / EB;
     static constexpr int XB = static_cast<int>(sizeof(XT));
-    static constexpr int XROW = kSmallDK * XB + 16;        // padded activation row, bytes
-    static constexpr int WST = kSmallDK / 4 * EB * 16;     // weight stage, bytes
+    static constexpr int XROW = DK * XB + 16;              // padded activation row, bytes
+    static constexpr int WST = DK / 4 * EB * 16;           // weight stage, bytes
     static constexpr int XST = TT * XROW;                  // activation stage, bytes
     static constexpr int LG = TT * EPAD * 4;               // gathered logits, bytes
     static constexpr int SMEM = kSmallStages * (WST + XST) + LG + 2 * kSmallStages * 8 + 16;
     static_assert(CL >= 1 && CL <= 8 && EB * CL == EPAD && TT * EB == kSmallCons, "shape");
-    static_assert((kSmallDK * XB) % 16 == 0 && XROW % 16 == 0 && WST % 16 == 0, "16-byte copies");
+    static_assert((DK * XB) % 16 == 0 && XROW % 16 == 0 && WST % 16 == 0, "16-byte copies");
+    static_assert(DK % 64 == 0 && SMEM <= 227 * 1024, "chunk and shared memory");
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -400,6 +404,14 @@ __device__ __forceinline__ float4 widen_x4<__nv_bfloat16>(uint4 r) {
                        __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xFFFF0000u));
 }
 
+// Marks a prefetched operand block as needed at this point of the program:
+// the block's loads must be issued before it, so they overlap the add chain
+// placed in front of it instead of sitting next to their uses.
+__device__ __forceinline__ void pin4(const float4& w, const uint4& x) {
+    asm volatile("" ::"f"(w.x), "f"(w.y), "f"(w.z), "f"(w.w), "r"(x.x), "r"(x.y), "r"(x.z),
+                 "r"(x.w));
+}
+
 // One chain step over 4 consecutive d: float32 product, float32 add, in order.
 template <bool EXACT>
 __device__ __forceinline__ float chain4(float acc, float4 x, float4 w) {
@@ -418,7 +430,7 @@ __device__ __forceinline__ float chain4(float acc, float4 x, float4 w) {
 }
 
 template <int EPAD, typename XT, bool EXACT>
-__global__ void __launch_bounds__(kSmallThreads)
+__global__ void __launch_bounds__(kSmallThreads, 1)
     gating_small_kernel(const XT* __restrict__ x, const float4* __restrict__ wblk,
                         const float* __restrict__ bias, int64_t N, int D, int64_t Dpad, int E,
                         int k, int ksel, int32_t* __restrict__ idx_out,
@@ -440,7 +452,7 @@ __global__ void __launch_bounds__(kSmallThreads)
     const int cb = blockIdx.y;  // expert block = rank in the (1, CL, 1) cluster
     const int64_t tok0 = static_cast<int64_t>(blockIdx.x) * TT;
     const int rows = static_cast<int>(min(static_cast<int64_t>(TT), N - tok0));
-    const int nch = (D + kSmallDK - 1) / kSmallDK;
+    const int nch = (D + C::DK - 1) / C::DK;
     if (tid == 0) {
         for (int st = 0; st < kSmallStages; ++st) {
             dev::mbar_init(&full[st], 1);
@@ -463,14 +475,14 @@ __global__ void __launch_bounds__(kSmallThreads)
                 const uint32_t ph = (c / kSmallStages) & 1;
                 if (!dev::mbar_wait_bounded(&empty[st], ph ^ 1, abort_flag, err, ERR_GEMM_TIMEOUT))
                     break;
-                const int dd = min(kSmallDK, D - c * kSmallDK);
+                const int dd = min(C::DK, D - c * C::DK);
                 const uint32_t xb = static_cast<uint32_t>(dd * C::XB);
                 dev::mbar_arrive_expect_tx(&full[st], C::WST + rows * xb);
-                dev::bulk_load(wring + st * C::WST, wsrc + static_cast<int64_t>(c) * (kSmallDK / 4) * EB,
+                dev::bulk_load(wring + st * C::WST, wsrc + static_cast<int64_t>(c) * (C::DK / 4) * EB,
                                C::WST, &full[st]);
                 for (int r = 0; r < rows; ++r)
                     dev::bulk_load(xring + st * C::XST + r * C::XROW,
-                                   x + (tok0 + r) * static_cast<int64_t>(D) + c * kSmallDK, xb,
+                                   x + (tok0 + r) * static_cast<int64_t>(D) + c * C::DK, xb,
                                    &full[st]);
             }
         }
@@ -480,10 +492,10 @@ __global__ void __launch_bounds__(kSmallThreads)
             const int st = c % kSmallStages;
             const uint32_t ph = (c / kSmallStages) & 1;
             if (!dev::mbar_wait_bounded(&full[st], ph, abort_flag, err, ERR_GEMM_TIMEOUT)) break;
-            const int n4 = min(kSmallDK, D - c * kSmallDK) >> 2;
+            const int n4 = min(C::DK, D - c * C::DK) >> 2;
             const float4* ws = reinterpret_cast<const float4*>(wring + st * C::WST) + el;
             const unsigned char* xs = xring + st * C::XST + tl * C::XROW;
-            if (n4 == kSmallDK / 4) {
+            if (n4 == C::DK / 4) {
                 // A whole chunk: operands of the next 32 d are loaded into
                 // registers while the chain runs over the current 32 (one warp
                 // per scheduler, so the loads must be issued well ahead).
@@ -496,7 +508,7 @@ __global__ void __launch_bounds__(kSmallThreads)
                     xa[i] = load_x4_raw<XT>(xs + i * 4 * C::XB);
                 }
 #pragma unroll
-                for (int b = 0; b < kSmallDK / 4 / QB; b += 2) {
+                for (int b = 0; b < C::DK / 4 / QB; b += 2) {
 #pragma unroll
                     for (int i = 0; i < QB; ++i) {
                         wb[i] = ws[((b + 1) * QB + i) * EB];
@@ -504,7 +516,9 @@ __global__ void __launch_bounds__(kSmallThreads)
                     }
 #pragma unroll
                     for (int i = 0; i < QB; ++i) acc = chain4<EXACT>(acc, widen_x4<XT>(xa[i]), wa[i]);
-                    if (b + 2 < kSmallDK / 4 / QB) {
+#pragma unroll
+                    for (int i = 0; i < QB; ++i) pin4(wb[i], xb[i]);
+                    if (b + 2 < C::DK / 4 / QB) {
 #pragma unroll
                         for (int i = 0; i < QB; ++i) {
                             wa[i] = ws[((b + 2) * QB + i) * EB];
@@ -513,6 +527,10 @@ __global__ void __launch_bounds__(kSmallThreads)
                     }
 #pragma unroll
                     for (int i = 0; i < QB; ++i) acc = chain4<EXACT>(acc, widen_x4<XT>(xb[i]), wb[i]);
+                    if (b + 2 < C::DK / 4 / QB) {
+#pragma unroll
+                        for (int i = 0; i < QB; ++i) pin4(wa[i], xa[i]);
+                    }
                 }
             } else {
 #pragma unroll 4

@@ -96,6 +96,7 @@ struct TcParams {
     int relu;
     int atomic_add;
     int red_v4;             // atomic_add with N, ldo multiples of 4: 16-byte reductions
+    int stream_k;           // split the (tile, K step) space evenly over the CTAs (atomic_add)
     const int* rowmap;
     const float* rowscale;
     int* err;
@@ -176,6 +177,44 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const int* s_rows, const 
     ti.kt1 = min(nkt, ti.kt0 + kper);
     (void)nch;
     return ti;
+}
+
+// The work of one CTA, item by item: whole tiles round-robin (tile t =
+// blockIdx.x + i * gridDim.x, each over its K range), or, with stream-K, an
+// equal contiguous share of the flattened (tile, K step) space -- a share may
+// start or end inside a tile, whose partial sums the epilogue then adds into
+// the zeroed output -- so every CTA streams the same number of weight tiles.
+struct WorkCursor {
+    int t;
+    int64_t w, w1;
+};
+__device__ __forceinline__ WorkCursor work_begin(const TcParams& p, int total, int nkt) {
+    WorkCursor c;
+    c.t = blockIdx.x;
+    const int64_t units = static_cast<int64_t>(total) * nkt;
+    c.w = p.stream_k ? units * blockIdx.x / gridDim.x : 0;
+    c.w1 = p.stream_k ? units * (blockIdx.x + 1) / gridDim.x : 0;
+    return c;
+}
+template <int BT>
+__device__ __forceinline__ bool work_next(WorkCursor& c, TileInfo& ti, const int* s_rows,
+                                          const int* s_tiles, const TcParams& p, int total,
+                                          int nch, int nkt, int kper) {
+    if (!p.stream_k) {
+        if (c.t >= total) return false;
+        ti = decode_tile<BT>(c.t, s_rows, s_tiles, p, nch, nkt, kper);
+        c.t += gridDim.x;
+        return true;
+    }
+    if (c.w >= c.w1) return false;
+    const int t = static_cast<int>(c.w / nkt);
+    const int k0 = static_cast<int>(c.w % nkt);
+    const int k1 = static_cast<int>(min(static_cast<int64_t>(nkt), k0 + (c.w1 - c.w)));
+    ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, nkt);  // ksplit is 1 here
+    ti.kt0 = k0;
+    ti.kt1 = k1;
+    c.w += k1 - k0;
+    return true;
 }
 
 // 4 signed bytes -> 2 words of bf16x2 (exact).  Each byte b becomes the float
@@ -281,8 +320,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             int s8 = 0;
             uint32_t ph8 = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < total && ok && !*abort_flag; t += gridDim.x) {
-                const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
+            TileInfo ti;
+            for (WorkCursor wc = work_begin(p, total, nkt);
+                 ok && !*abort_flag && work_next<BT>(wc, ti, s_rows, s_tiles, p, total, nch, nkt, kper);) {
                 // the tile's 8 KB blocks along K are consecutive in the tiled layout
                 const int8_t* wsrc =
                     p.wq + ((static_cast<int64_t>(ti.wg) * p.NT + ti.n0 / kCh) * p.KT) * (kCh * kKT);
@@ -308,8 +348,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             int sx = 0;
             uint32_t phx = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < total && ok && !*abort_flag; t += gridDim.x) {
-                const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
+            TileInfo ti;
+            for (WorkCursor wc = work_begin(p, total, nkt);
+                 ok && !*abort_flag && work_next<BT>(wc, ti, s_rows, s_tiles, p, total, nch, nkt, kper);) {
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
                     if (!mbar_wait_bounded(&st_empty[sx], phx ^ 1, abort_flag, p.err,
                                            ERR_GEMM_TIMEOUT)) {
@@ -336,8 +377,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phs = 0;
             int it = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < total && ok && !*abort_flag; t += gridDim.x, ++it) {
-                const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
+            TileInfo ti;
+            for (WorkCursor wc = work_begin(p, total, nkt);
+                 ok && !*abort_flag && work_next<BT>(wc, ti, s_rows, s_tiles, p, total, nch, nkt, kper);
+                 ++it) {
                 const int b = it & 1;
                 const uint32_t aph = (it >> 1) & 1;
                 if (!mbar_wait_bounded(&acce_bar[b], aph ^ 1, abort_flag, p.err, ERR_GEMM_TIMEOUT))
@@ -383,8 +426,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int gtid = tid % C::CG_THREADS;
         uint32_t kc = 0;  // K steps so far, in the order every role walks them
         bool ok = true;
-        for (int t = blockIdx.x; t < total && ok && !*abort_flag; t += gridDim.x) {
-            const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
+        TileInfo ti;
+        for (WorkCursor wc = work_begin(p, total, nkt);
+             ok && !*abort_flag && work_next<BT>(wc, ti, s_rows, s_tiles, p, total, nch, nkt, kper);) {
             for (int kt = ti.kt0; kt < ti.kt1; ++kt, ++kc) {
                 if (static_cast<int>(kc % C::CG) != group) continue;
                 const int s16 = static_cast<int>(kc % C::DS);
@@ -405,7 +449,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int item = gtid + C::CG_THREADS * i;  // 128 rows x 4 chunks
                     const int r = item >> 2;
                     const int ch = item & 3;
-                    const uint4 v = *reinterpret_cast<const uint4*>(w8 + r * 64 + ch * 16);
+                    const uint4 v =
+                        *reinterpret_cast<const uint4*>(w8 + r * 64 + wtile_chunk(r, ch) * 16);
                     const uint2 a0 = i8x4_to_bf16x4(v.x);
                     const uint2 a1 = i8x4_to_bf16x4(v.y);
                     const uint2 a2 = i8x4_to_bf16x4(v.z);
@@ -435,9 +480,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int h = ei >> 2;
         int it = 0;
         // loop exits are warp-uniform: the TMEM loads below are warp-collective
-        for (int t = blockIdx.x; t < total && !__any_sync(0xFFFFFFFFu, *abort_flag != 0);
-             t += gridDim.x, ++it) {
-            const TileInfo ti = decode_tile<BT>(t, s_rows, s_tiles, p, nch, nkt, kper);
+        TileInfo ti;
+        for (WorkCursor wc = work_begin(p, total, nkt);
+             !__any_sync(0xFFFFFFFFu, *abort_flag != 0) &&
+             work_next<BT>(wc, ti, s_rows, s_tiles, p, total, nch, nkt, kper);
+             ++it) {
             const int b = it & 1;
             const uint32_t aph = (it >> 1) & 1;
             if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&accf_bar[b], aph, abort_flag, p.err,
@@ -577,8 +624,12 @@ struct Cfg2 {
     static constexpr int W16 = kCh * kKT * 2;
     static constexpr int XB = HB * kKT * 2;        // bf16 activation half-tile, per part
     static constexpr int XS = SPLIT * XB;
+    // The activation tile's TMA, issued when a stage frees, takes 1000-2000
+    // cycles to land (measured), so the operand ring gets the depth: the
+    // int8 ring, whose tiles are re-read from L2 by every token tile, keeps
+    // four stages.
     static constexpr int BUDGET = 216 * 1024;
-    static constexpr int DS_RAW = (BUDGET - 8 * W8) / (W16 + XS);
+    static constexpr int DS_RAW = (BUDGET - 4 * W8) / (W16 + XS);
     static constexpr int DS = DS_RAW > 8 ? 8 : (DS_RAW < 2 ? 2 : DS_RAW);
     static constexpr int S8_RAW = (BUDGET - DS * (W16 + XS)) / W8;
     static constexpr int CG_RAW = DS >= 4 ? 4 : (DS >= 2 ? 2 : 1);
@@ -854,7 +905,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     const int item = gtid + C::CG_THREADS * i;
                     const int r = item >> 2;
                     const int ch = item & 3;
-                    const uint4 v = *reinterpret_cast<const uint4*>(w8 + r * 64 + ch * 16);
+                    const uint4 v =
+                        *reinterpret_cast<const uint4*>(w8 + r * 64 + wtile_chunk(r, ch) * 16);
                     const uint2 a0 = i8x4_to_bf16x4(v.x);
                     const uint2 a1 = i8x4_to_bf16x4(v.y);
                     const uint2 a2 = i8x4_to_bf16x4(v.z);
@@ -1092,7 +1144,7 @@ int64_t tiles_estimate(int64_t M, int G, int bt, int64_t nch, int ks) {
 }  // namespace
 
 namespace {
-std::atomic<int> g_pair_mode{0};
+std::atomic<int> g_pair_mode{-1};
 }  // namespace
 
 int gemm_pair_mode() { return g_pair_mode.load(std::memory_order_relaxed); }
@@ -1154,6 +1206,11 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
     p.rowmap = a.rowmap;
     p.rowscale = a.rowscale;
     p.err = err;
+    p.stream_k = (a.stream_k && a.atomic_add && !a.relu && !a.out_bf16) ? 1 : 0;
+    if (p.stream_k) {
+        ks = 1;
+        p.ksplit = 1;
+    }
     AEM_REQUIRE(!(ks > 1 && (a.relu || a.out_bf16)), "qgemm: split-K is float32 without ReLU only");
 
     // Upper bound of the tiles of all groups: sum_g ceil(rows_g / bt) <= ceil(M / bt) + (#non-empty groups).
@@ -1161,8 +1218,12 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
     const int64_t tiles_ub = ((rows + bt - 1) / bt + std::min<int64_t>(a.G, rows)) * nch * ks;
     // SM pairs (cta_group::2) for large token tiles: half the activation bytes
     // per SM and half the MMA issue per FLOP
+    // automatic: 128/256-row tiles over an even number of 128-channel blocks
+    // (an odd count leaves the last pair's second block idle: 1/12 of the
+    // MMAs at 11 blocks, which measured slower than single SMs)
     const int mode = gemm_pair_mode();
-    if (bt >= 64 && (mode == 1 || (mode < 0 && bt >= 128))) {
+    if (!p.stream_k && bt >= 64 &&
+        (mode == 1 || (mode < 0 && bt >= 128 && (nch % 2 == 0 || nch >= 15)))) {
         const int64_t ptiles = ((rows + bt - 1) / bt + std::min<int64_t>(a.G, rows)) *
                                ((nch + 1) / 2) * ks;
         const int pairs =
@@ -1170,7 +1231,8 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
         if (a.x_lo) return launch_pair_bt<2>(bt, a, p, pairs, s);
         return launch_pair_bt<1>(bt, a, p, pairs, s);
     }
-    const int grid = static_cast<int>(std::min<int64_t>(sms, std::max<int64_t>(1, tiles_ub)));
+    const int grid = p.stream_k ? sms
+                                : static_cast<int>(std::min<int64_t>(sms, std::max<int64_t>(1, tiles_ub)));
     if (a.x_lo) return launch_bt<2>(bt, a, p, grid, s);
     return launch_bt<1>(bt, a, p, grid, s);
 }

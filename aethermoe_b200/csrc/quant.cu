@@ -118,9 +118,9 @@ __global__ void qgemm_simt_kernel(const __nv_bfloat16* __restrict__ xh,
 // group).  At these sizes the tensor-core kernel's per-K-step issue loop, not
 // the weight stream, sets the time; here every SM streams weights at memory
 // speed.  One CTA of 128 threads per (row group, 128-channel block, K range).
-// Thread t owns 16-byte chunk c = t % 4 (16 consecutive K) of channel rows
-// t/4 + 32j (j < 4) of every 8 KB weight tile, so each warp load reads 512
-// contiguous bytes and the chunk's 16 activations serve four rows.  int8 ->
+// Thread t owns the 16-byte chunk at position t % 4 (16 consecutive K) of
+// channel rows t/4 + 32j (j < 4) of every 8 KB weight tile, so each warp load
+// reads 512 contiguous bytes and the chunk's 16 activations serve four rows.  int8 ->
 // float is exact (2^23 + 128 + b as a float bit pattern, minus 2^23 + 128);
 // products are summed by packed float32 FMAs (even and odd K in two lanes);
 // the four owners of a row combine by shuffles.  Split-K partial sums (KS > 1)
@@ -162,7 +162,9 @@ __global__ void __launch_bounds__(kDecodeThreads)
     if (m <= 0 || kt0 >= kt1) return;  // uniform over the CTA
     const int64_t wg = group_base + (wmod ? g % wmod : g);
     const int t = threadIdx.x;
-    const int c = t & 3;
+    // this thread streams chunk position t & 3 of rows t/4 + 32j: the K
+    // offsets (logical chunk) stored there, the same for every j
+    const int c = wtile_chunk(t >> 2, t & 3);
     const int8_t* wtile = q + ((wg * NT + nb) * KT) * kWTileBytes + t * 16;  // + j * 2048
     float2 acc[4][MAXM];
 #pragma unroll

@@ -89,8 +89,11 @@ int gate_small_eb(int64_t Epad);  // experts per CTA of the small-batch kernel
 
 // Packed INT8 weight (device), pre-tiled for the GEMM's weight stream:
 // [G][NT][KT][128][64] int8 with NT = ceil(N/128), KT = ceil(K/64): every
-// 128-output-channel x 64-K tile is one contiguous 8 KB block (rows of 64
-// K-consecutive bytes), zero padded.  scale [G][N] float32.
+// 128-output-channel x 64-K tile is one contiguous 8 KB block of 64-byte
+// channel rows, zero padded.  Inside a row, the 16-byte chunk c (K offsets
+// 16c .. 16c+15) sits at chunk position c ^ ((row >> 1) & 3), so 32 threads
+// reading the same chunk of 32 consecutive rows from shared memory touch
+// every bank group evenly (4 wavefronts per 512 bytes).  scale [G][N] float32.
 constexpr int64_t kWTileN = 128, kWTileK = 64, kWTileBytes = kWTileN * kWTileK;
 struct QWeight {
     int device = 0;
@@ -98,11 +101,14 @@ struct QWeight {
     int8_t* q = nullptr;
     float* scale = nullptr;
 };
+// Chunk position of the 16-byte chunk c of channel row r inside a tile.
+__host__ __device__ inline int wtile_chunk(int r, int c) { return c ^ ((r >> 1) & 3); }
 // Byte offset of element (g, n, k) in the tiled layout.
 __host__ __device__ inline int64_t wtile_offset(int64_t g, int64_t n, int64_t k, int64_t NT,
                                                 int64_t KT) {
-    return ((g * NT + n / kWTileN) * KT + k / kWTileK) * kWTileBytes + (n % kWTileN) * kWTileK +
-           (k % kWTileK);
+    const int r = static_cast<int>(n % kWTileN), kk = static_cast<int>(k % kWTileK);
+    return ((g * NT + n / kWTileN) * KT + k / kWTileK) * kWTileBytes + r * kWTileK +
+           wtile_chunk(r, kk >> 4) * 16 + (kk & 15);
 }
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -136,6 +142,9 @@ struct GemmArgs {
     bool relu = false;
     bool atomic_add = false;   // float32 out only: red.add partial sums (split-K)
     int ksplit = 1;
+    // atomic_add only: every CTA takes an equal share of the (tile, K step)
+    // space (partial tiles add into the output, which must start at zero)
+    bool stream_k = false;
     const int* rowmap = nullptr;    // output row of activation row r (nullable)
     const float* rowscale = nullptr;  // per-activation-row multiplier (nullable)
     int token_tile = 0;        // 0 = choose from average rows per group

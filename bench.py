@@ -447,6 +447,8 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     if aem.device_count() < 1:
         raise SystemExit("no sm_100 device visible to libaethermoe")
+    if args.gemm_pairs != "default":
+        _lib.check(aem.lib().aem_set_gemm_pairs({"auto": -1, "off": 0, "on": 1}[args.gemm_pairs]))
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=dev)
@@ -558,6 +560,7 @@ def run_ours(args):
                        "global_batch": tokens, "parallelism": f"ep{world}",
                        "expert_placement": "round-robin (expert e on rank e % R)",
                        "ep_pipeline": (args.ep_pipeline if world > 1 else None),
+                       "gemm_pairs": args.gemm_pairs,
                        "l2": (f"inputs rotate over {N_INPUT_BUFFERS} buffers "
                               f"({N_INPUT_BUFFERS * tokens * D_MODEL * 2 >> 20} MiB > 126 MiB L2); "
                               "per-step working set > 1 GiB")},
@@ -806,6 +809,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-sample-tokens", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemm-pairs", choices=["default", "auto", "off", "on"], default="default",
+                    help="INT8 GEMM on SM pairs (aem_set_gemm_pairs): auto = from 128-row tiles")
     ap.add_argument("--exchange-compare", action="store_true",
                     help="N>1: also time the step's token exchange through NCCL all-to-all")
     ap.add_argument("--no-parity", action="store_true",

@@ -170,7 +170,7 @@ def gemm_form(cuda, request):
     from aethermoe_b200 import _lib
     _lib.check(_lib.lib().aem_set_gemm_pairs(0 if request.param == "single" else 1))
     yield request.param
-    _lib.check(_lib.lib().aem_set_gemm_pairs(0))
+    _lib.check(_lib.lib().aem_set_gemm_pairs(-1))
 
 
 @pytest.mark.parametrize("tile", [256, 128, 64])
@@ -354,7 +354,7 @@ def test_pairs_match_single_sms(cuda, m, dtype):
                                         stream), "aem_qgemm")
         torch.cuda.synchronize()
         res[mode] = o.cpu().numpy()
-    _lib.check(_lib.lib().aem_set_gemm_pairs(0))
+    _lib.check(_lib.lib().aem_set_gemm_pairs(-1))
     _lib.check(_lib.lib().aem_device_status(None), "aem_device_status")
     ref = x.astype(np.float64) @ (q.astype(np.float64) * s.astype(np.float64))
     _close(res[0], ref)
