@@ -131,6 +131,11 @@ _SIGS = {
     "aem_ep_free": (_int, [_vp]),
     "aem_ep_forward": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp]),
     "aem_ep_forward_host": (_int, [_vp, _vp, _vp, _int, _i64, _vp, _int]),
+    "aem_ep_submit_host": (_int, [_vp, _vp, _vp, _int, _i64, _vp, _int,
+                                  ctypes.POINTER(ctypes.c_uint64)]),
+    "aem_moe_submit_host": (_int, [_vp, _vp, _vp, _int, _i64, _vp, _int,
+                                   ctypes.POINTER(ctypes.c_uint64)]),
+    "aem_context_wait": (_int, [_vp, ctypes.c_uint64]),
     "aem_ep_last_routing": (_int, [_vp, _vp, _vp, _vp, _vp]),
     "aem_capacity_route_static": (_int, [_vp, _vp, _vp, _i64, _int, _u64, _vp, _vp]),
     "aem_kernel_launches": (ctypes.c_uint64, []),

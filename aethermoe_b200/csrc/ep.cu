@@ -1710,6 +1710,27 @@ aem_status aem_ep_forward_host(aem_context_t ctx, aem_ep_t h, const void* x, aem
     return aem::check_device_errors(c->stream, "aem_ep_forward_host");
 }
 
+aem_status aem_ep_submit_host(aem_context_t ctx, aem_ep_t h, const void* x, aem_dtype x_dtype,
+                              int64_t T_local, void* out, aem_dtype out_dtype, uint64_t* ticket) {
+    AEM_REQUIRE(ctx != nullptr && h != nullptr && ticket != nullptr,
+                "aem_ep_submit_host: NULL argument");
+    AEM_REQUIRE(T_local >= 1 && T_local < (1ll << 28), "aem_ep_submit_host: T out of range");
+    AEM_REQUIRE(x && out, "aem_ep_submit_host: NULL buffer");
+    AEM_REQUIRE(x_dtype == AEM_F32 || x_dtype == AEM_BF16, "aem_ep_submit_host: bad x dtype");
+    AEM_REQUIRE(out_dtype == AEM_F32 || out_dtype == AEM_BF16, "aem_ep_submit_host: bad out dtype");
+    auto* c = reinterpret_cast<aem::Context*>(ctx);
+    auto* ep = reinterpret_cast<aem::Ep*>(h);
+    const int64_t d = ep->cfg.d_model;
+    const size_t xb = static_cast<size_t>(T_local) * d * (x_dtype == AEM_F32 ? 4 : 2);
+    const size_t ob = static_cast<size_t>(T_local) * d * (out_dtype == AEM_F32 ? 4 : 2);
+    return aem::pipe_submit(
+        c, x, xb, out, ob,
+        [&](const void* din, void* dout, cudaStream_t s) {
+            return ep_forward_checked(h, din, x_dtype, T_local, dout, out_dtype, nullptr, false, s);
+        },
+        ticket);
+}
+
 aem_status aem_ep_mark_unhealthy(aem_ep_t h, int rank) {
     AEM_REQUIRE(h != nullptr, "aem_ep_mark_unhealthy: NULL layer");
     auto* ep = reinterpret_cast<aem::Ep*>(h);

@@ -311,6 +311,7 @@ aem_status aem_context_destroy(aem_context_t ctx) {
     if (!ctx) return AEM_OK;
     auto* c = reinterpret_cast<aem::Context*>(ctx);
     cudaSetDevice(c->device);
+    aem::pipe_free(c);
     cudaStreamSynchronize(c->stream);
     if (c->dev) cudaFree(c->dev);
     if (c->host) cudaFreeHost(c->host);

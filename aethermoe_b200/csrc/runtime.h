@@ -7,6 +7,7 @@
 
 #include "aem.h"
 
+#include <functional>
 #include <utility>
 #include <vector>
 
@@ -53,11 +54,14 @@ struct PhaseProfiler {
     ~PhaseProfiler();
 };
 
+struct HostPipe;  // asynchronous host-buffer steps (pipeline.cu)
+
 // Host-staging context behind aem_context_t: one stream plus grow-only
 // device and pinned-host buffers for the *_host entry points.
 struct Context {
     int device = 0;
     cudaStream_t stream = nullptr;
+    HostPipe* pipe = nullptr;  // created by the first asynchronous submit
     void* dev = nullptr;
     size_t dev_bytes = 0;
     void* host = nullptr;
@@ -65,6 +69,16 @@ struct Context {
     aem_status reserve_device(size_t bytes);
     aem_status reserve_host(size_t bytes);
 };
+
+// Asynchronous host-buffer steps on a context (pipeline.cu): copies x
+// (xb bytes) in on an upload stream, runs compute(device in, device out,
+// context stream), copies ob bytes out on a download stream; two steps in
+// flight per context.  pipe_wait reports the step's in-kernel errors.
+aem_status pipe_submit(Context* c, const void* x, size_t xb, void* out, size_t ob,
+                       const std::function<aem_status(const void*, void*, cudaStream_t)>& compute,
+                       uint64_t* ticket);
+aem_status pipe_wait(Context* c, uint64_t ticket);
+void pipe_free(Context* c);
 
 // Packed gating weight (device).  The [D, E] weight is stored as
 // [Dpad/4][Epad][4] float32: for every group of 4 consecutive d, the 4

@@ -614,7 +614,14 @@ def ctypes_stream(stream):
 
 
 def e2e_run(args, layer, world, rank, tl, dev, stream, barrier):
-    """Same step through the public API with pinned HOST buffers each step."""
+    """The step through the public API on pinned HOST buffers: every step
+    copies its tokens in and its outputs out.  The steps go through the
+    asynchronous host API (aem_moe_submit_host / aem_ep_submit_host +
+    aem_context_wait), so step i+1's upload and step i-1's download overlap
+    step i's compute, as a serving loop would run them; two input and two
+    output buffers alternate, and a step's output is read back (its wait
+    returns) before its buffer is written again.  Timed with CUDA events on
+    the context's compute stream, max over ranks."""
     import ctypes
     import torch
     import aethermoe_b200 as aem
@@ -623,43 +630,31 @@ def e2e_run(args, layer, world, rank, tl, dev, stream, barrier):
     xh = [torch.empty((tl, D_MODEL), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     for i, x in enumerate(xh):
         x.copy_(torch.randn((tl, D_MODEL), generator=torch.Generator().manual_seed(50 + i)))
-    oh = torch.empty((tl, D_MODEL), dtype=torch.bfloat16).pin_memory()
-    if world == 1:
-        ctx = _lib.context(dev.index)
-        cstream = torch.cuda.ExternalStream(aem.lib().aem_context_stream(ctx))
+    oh = [torch.empty((tl, D_MODEL), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    ctx = _lib.context(dev.index)
+    cstream = torch.cuda.ExternalStream(aem.lib().aem_context_stream(ctx))
+    submit = aem.lib().aem_moe_submit_host if world == 1 else aem.lib().aem_ep_submit_host
 
-        def step(i):
-            _lib.check(aem.lib().aem_moe_forward_host(ctx, layer.handle, xh[i % 2].data_ptr(),
-                                                      _lib.BF16, tl, oh.data_ptr(), _lib.BF16))
-        for i in range(2):
-            step(i)
-        torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(cstream)
-        for i in range(steps):
-            step(i)
-        e1.record(cstream)
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1)
-    else:
-        ctx = _lib.context(dev.index)
-        cstream = torch.cuda.ExternalStream(aem.lib().aem_context_stream(ctx))
-
-        def step(i):
-            _lib.check(aem.lib().aem_ep_forward_host(ctx, layer.handle, xh[i % 2].data_ptr(),
-                                                     _lib.BF16, tl, oh.data_ptr(), _lib.BF16))
-        for i in range(2):
-            step(i)
-        barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(cstream)
-        for i in range(steps):
-            step(i)
-        e1.record(cstream)
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1)
+    def run(n):
+        tickets = []
+        for i in range(n):
+            t = ctypes.c_uint64()
+            _lib.check(submit(ctx, layer.handle, xh[i % 2].data_ptr(), _lib.BF16, tl,
+                              oh[i % 2].data_ptr(), _lib.BF16, ctypes.byref(t)), "submit")
+            tickets.append(t.value)
+            if i >= 1:
+                _lib.check(aem.lib().aem_context_wait(ctx, tickets[i - 1]), "aem_context_wait")
+        _lib.check(aem.lib().aem_context_wait(ctx, tickets[-1]), "aem_context_wait")
+    run(2)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(cstream)
+    run(steps)
+    e1.record(cstream)  # the last step's output is on the host: this marks the end
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
         import torch.distributed as dist
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -667,8 +662,10 @@ def e2e_run(args, layer, world, rank, tl, dev, stream, barrier):
     tokens = tl * world
     return {"value": tokens * steps / (ms * 1e-3), "unit": UNIT,
             "h2d_bytes_per_step": tokens * D_MODEL * 2, "d2h_bytes_per_step": tokens * D_MODEL * 2,
-            "steps": steps, "api": "aem_moe_forward_host" if world == 1 else
-            "aem_ep_forward_host (every rank)"}
+            "steps": steps,
+            "api": ("aem_moe_submit_host + aem_context_wait" if world == 1 else
+                    "aem_ep_submit_host + aem_context_wait (every rank)"),
+            "overlap": "two steps in flight: uploads and downloads on their own streams"}
 
 
 # ------------------------------------------------------------------ other configs

@@ -290,6 +290,20 @@ aem_status aem_moe_set_hidden_dtype(aem_moe_t moe, int hidden_dtype);
 /* HOST-buffer form of aem_moe_forward (synchronous). */
 aem_status aem_moe_forward_host(aem_context_t ctx, aem_moe_t moe, const void* x, aem_dtype x_dtype,
                                 int64_t T, void* out, aem_dtype out_dtype);
+/* Asynchronous form of aem_moe_forward_host for a stream of steps: copies x
+ * in on the context's upload stream, computes on the context's stream once
+ * the copy landed, copies the output out on its download stream -- so with
+ * page-locked host buffers the next step's upload and the previous step's
+ * download overlap the current step's compute.  Returns at once with a
+ * ticket; at most two steps are in flight per context (a third submit waits
+ * on the host for the oldest to finish).  x and out must stay valid and
+ * untouched until aem_context_wait(ctx, ticket) returns, which also reports
+ * the step's in-kernel errors.  Steps run in submission order. */
+aem_status aem_moe_submit_host(aem_context_t ctx, aem_moe_t moe, const void* x, aem_dtype x_dtype,
+                               int64_t T, void* out, aem_dtype out_dtype, uint64_t* ticket);
+/* Waits for the step of `ticket` (from a *_submit_host call on ctx): its
+ * output is in the host buffer when this returns AEM_OK. */
+aem_status aem_context_wait(aem_context_t ctx, uint64_t ticket);
 /* Per-phase profiling with CUDA events recorded on the step's stream.
  * enable != 0 starts (and clears) accumulation; aem_moe_profile_read
  * synchronises, then writes the summed milliseconds of each phase
@@ -427,6 +441,10 @@ aem_status aem_ep_forward_tolerant(aem_ep_t ep, const void* x, aem_dtype x_dtype
  * aem_ep_forward.  A peer failure is returned as AEM_ETIMEOUT / AEM_EDEVICE. */
 aem_status aem_ep_forward_host(aem_context_t ctx, aem_ep_t ep, const void* x, aem_dtype x_dtype,
                                int64_t T_local, void* out, aem_dtype out_dtype);
+/* Asynchronous form of aem_ep_forward_host (see aem_moe_submit_host):
+ * collective -- every rank submits the same sequence of steps. */
+aem_status aem_ep_submit_host(aem_context_t ctx, aem_ep_t ep, const void* x, aem_dtype x_dtype,
+                              int64_t T_local, void* out, aem_dtype out_dtype, uint64_t* ticket);
 /* The host learned that `rank` is gone (a store, a heartbeat, a process
  * exit): later steps leave it out and never touch its memory again.  A rank
  * that exited must be marked here before the next step; the in-step deadline

@@ -75,6 +75,21 @@ def _worker(rank, world, port, outdir, placement, pipeline=-1):
     torch.cuda.synchronize()
     from aethermoe_b200 import _lib
     _lib.check(_lib.lib().aem_device_status(None), "aem_device_status")
+    # the same step three times through the asynchronous host API
+    import ctypes
+    ctx = _lib.context(rank)
+    xh = xt.cpu().pin_memory()
+    oh = [torch.empty((tl, d), dtype=torch.float32).pin_memory() for _ in range(3)]
+    tickets = []
+    for o in oh:
+        t = ctypes.c_uint64()
+        _lib.check(_lib.lib().aem_ep_submit_host(ctx, layer.handle, xh.data_ptr(), _lib.BF16, tl,
+                                                 o.data_ptr(), _lib.F32, ctypes.byref(t)))
+        tickets.append(t.value)
+    for t in tickets:
+        _lib.check(_lib.lib().aem_context_wait(ctx, t))
+    for o in oh:
+        np.testing.assert_allclose(o.numpy(), outs[-1].cpu().numpy(), rtol=0, atol=1e-5)
     np.savez(os.path.join(outdir, f"rank{rank}.npz"), out=outs[-1].cpu().numpy(),
              out0=outs[0].cpu().numpy(), idx=idx.cpu().numpy(), val=val.cpu().numpy(),
              eff=eff.cpu().numpy(), outb=ob.float().cpu().numpy())
