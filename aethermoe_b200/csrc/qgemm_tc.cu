@@ -44,6 +44,8 @@ namespace aem {
 
 aem_status launch_qgemm_simt(const GemmArgs& a, cudaStream_t s);
 aem_status launch_qgemm_decode(const GemmArgs& a, cudaStream_t s);
+aem_status launch_qgemm_gemv(const GemmArgs& a, cudaStream_t s);
+int gemv_max_rows();
 
 namespace {
 
@@ -1157,8 +1159,8 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
                 "qgemm: weight group out of range");
     AEM_REQUIRE(!(a.atomic_add && a.out_bf16), "qgemm: split-K needs float32 output");
     if (a.M == 0) return AEM_OK;
-    // decode sizes (at most 4 rows, so at most 4 per group): CUDA cores
-    if (a.M <= 4 && a.token_tile == 0) return launch_qgemm_decode(a, s);
+    // few rows (so few per group): the bandwidth-bound weight stream
+    if (a.M <= gemv_max_rows() && a.token_tile == 0) return launch_qgemm_gemv(a, s);
     if (w.K % 8 != 0) return launch_qgemm_simt(a, s);
     AEM_REQUIRE(a.M < (1ll << 31) && w.G * w.N < (1ll << 31), "qgemm: too many rows");
     const int dev = current_device();

@@ -360,3 +360,78 @@ def test_pairs_match_single_sms(cuda, m, dtype):
     _close(res[0], ref)
     _close(res[1], ref)
     np.testing.assert_allclose(res[1], res[0], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("sizes,K,N", [([0, 1, 7, 9, 0, 15], 448, 300), ([32], 200, 130),
+                                        ([3, 0, 5], 4096, 1536), ([16, 16], 40, 257)])
+@pytest.mark.parametrize("mode", ["relu_bf16", "scaled_add", "f32_store"])
+def test_weight_stream_path(cuda, sizes, K, N, mode):
+    """At most 32 rows: the bandwidth-bound weight stream (warp MMAs on
+    registers loaded straight from the int8 tiles).  Groups of 0-32 rows, K
+    and N that are not multiples of the 64 x 128 tile, float32 activations as
+    hi + lo (f32_store; the layer tests cover the hi + lo hidden output)."""
+    import torch
+    from aethermoe_b200 import _lib
+    rng = np.random.default_rng(sum(sizes) + K + N + len(mode))
+    G = len(sizes)
+    q = rng.integers(-127, 128, size=(G, K, N), dtype=np.int8)
+    s = (rng.random(size=(G, N)) * 1e-3 + 1e-4).astype(np.float32)
+    w = _lib.QWeight(q, s, 0)
+    rows = np.r_[0, np.cumsum(sizes)].astype(np.int32)
+    M = int(rows[-1])
+    x = rng.normal(size=(M, K)).astype(np.float32)
+    ref = np.zeros((M, N))
+    for g in range(G):
+        a, b = rows[g], rows[g + 1]
+        ref[a:b] = x[a:b].astype(np.float64) @ (q[g].astype(np.float64) * s[g].astype(np.float64))
+    hi = O.bf16_round(x)
+    tobf = lambda a: torch.from_numpy((a.view(np.uint32) >> 16).astype(np.uint16).view(np.int16)).to(cuda).view(torch.bfloat16)  # noqa: E731
+    rt = torch.from_numpy(rows).to(cuda)
+    stream = torch.cuda.current_stream().cuda_stream
+    L = _lib.lib()
+    if mode == "f32_store":
+        # dense call on each group's rows through aem_qgemm (float32 x split hi + lo)
+        for g in range(G):
+            a, b = rows[g], rows[g + 1]
+            if b == a:
+                continue
+            xt = torch.from_numpy(x[a:b].copy()).to(cuda)
+            out = torch.empty((b - a, N), dtype=torch.float32, device=cuda)
+            _lib.check(L.aem_qgemm(w.handle, g, xt.data_ptr(), _lib.F32, b - a, out.data_ptr(),
+                                   stream), "aem_qgemm")
+            torch.cuda.synchronize()
+            _close(out.cpu().numpy(), ref[a:b])
+        return
+    if mode == "relu_bf16":
+        # the MoE layer's up projection: grouped, ReLU, bf16 output
+        xt = tobf(hi)
+        out = torch.zeros((M, N), dtype=torch.bfloat16, device=cuda)
+        _lib.check(L.aem_grouped_qgemm(w.handle, rt.data_ptr(), G, xt.data_ptr(), M,
+                                       out.data_ptr(), _lib.BF16, N, 1, 0, None, None, 0, 1,
+                                       stream), "aem_grouped_qgemm")
+        torch.cuda.synchronize()
+        refh = np.zeros((M, N))
+        for g in range(G):
+            a, b = rows[g], rows[g + 1]
+            refh[a:b] = hi[a:b].astype(np.float64) @ (q[g].astype(np.float64) * s[g].astype(np.float64))
+        _close(out.float().cpu().numpy(), np.maximum(refh, 0.0), rtol=2 ** -8 + 1e-3, atol=1e-3)
+    else:
+        rmap = rng.permutation(M).astype(np.int32)
+        rscale = (rng.random(M) + 0.5).astype(np.float32)
+        base = rng.normal(size=(M, N)).astype(np.float32)
+        out = torch.from_numpy(base.copy()).to(cuda)
+        mt = torch.from_numpy(rmap).to(cuda)
+        st = torch.from_numpy(rscale).to(cuda)
+        xt = tobf(hi)
+        _lib.check(L.aem_grouped_qgemm(w.handle, rt.data_ptr(), G, xt.data_ptr(), M,
+                                       out.data_ptr(), _lib.F32, N, 0, 1, mt.data_ptr(),
+                                       st.data_ptr(), 0, 1, stream), "aem_grouped_qgemm")
+        torch.cuda.synchronize()
+        refh = np.zeros((M, N))
+        for g in range(G):
+            a, b = rows[g], rows[g + 1]
+            refh[a:b] = hi[a:b].astype(np.float64) @ (q[g].astype(np.float64) * s[g].astype(np.float64))
+        want = base.astype(np.float64).copy()
+        want[rmap] += refh * rscale[:, None].astype(np.float64)
+        _close(out.cpu().numpy(), want)
+    _lib.check(L.aem_device_status(None), "aem_device_status")
