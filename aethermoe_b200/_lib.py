@@ -142,6 +142,7 @@ _SIGS = {
     "aem_moe_profile": (_int, [_vp, _int]),
     "aem_moe_set_hidden_dtype": (_int, [_vp, _int]),
     "aem_set_gemm_pairs": (_int, [_int]),
+    "aem_set_gemm_tmem_a": (_int, [_int]),
     "aem_moe_profile_read": (_int, [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64)]),
     "aem_ep_profile": (_int, [_vp, _int]),
     "aem_ep_profile_read": (_int, [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64)]),

@@ -76,6 +76,7 @@ constexpr int kW8Warp = 16;   // int8 weight producer
 constexpr int kMmaWarp = 17;  // MMA issuer + TMEM allocation
 constexpr int kXWarp = 18;    // activation producer
 constexpr int kThreads = 19 * 32;
+constexpr int kMmaWarpX = 19;  // further MMA issuers (TMEM weights, small token tiles)
 static_assert(kEpiWarp0 % 4 == 0, "epilogue warps must start at a warpgroup boundary");
 constexpr int kMaxGroups = 256;
 
@@ -104,10 +105,22 @@ struct TcParams {
     int* err;
 };
 
-template <int BT, int SPLIT>
+constexpr int pow2_cols(int c) { return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512; }
+
+// TSA: the converted bf16 weights go to TMEM (the MMA's A operand read from
+// tensor memory) instead of shared memory; the operand ring's stage then holds
+// only the activation tile in shared memory, and its weights occupy a 32-column
+// slot of TMEM beside the two accumulators.
+template <int BT, int SPLIT, bool TSA = false, int NI = 1>
 struct Cfg {
+    // NI MMA-issuing warps, each with its own accumulators, take the K steps
+    // round-robin: one thread issues a tcgen05.mma only every ~100 cycles
+    // whatever N is, so small token tiles need several issuers to keep the
+    // tensor pipe (and the weight stream) busy; the epilogue adds the NI
+    // partial accumulators.
+    static constexpr int THREADS = (kMmaWarpX + NI - 1) * 32;
     static constexpr int W8 = kCh * kKT;           // int8 weight tile, bytes
-    static constexpr int W16 = kCh * kKT * 2;      // bf16 weight tile (MMA A)
+    static constexpr int W16 = TSA ? 0 : kCh * kKT * 2;  // bf16 weight tile in smem (MMA A)
     static constexpr int XB = BT * kKT * 2;        // bf16 activation tile (MMA B), per part
     static constexpr int XS = SPLIT * XB;          // one activation stage
     // Two rings.  A stage of the operand ring holds one K step's activation
@@ -120,9 +133,16 @@ struct Cfg {
     // leaves of the budget.
     static constexpr int BUDGET = 216 * 1024;
     static constexpr int DS_RAW = (BUDGET - 8 * W8) / (W16 + XS);  // 8 int8 stages first
-    static constexpr int DS = DS_RAW > 8 ? 8 : (DS_RAW < 2 ? 2 : DS_RAW);
+    static constexpr int DS_TMEM = TSA ? (512 - 2 * NI * BT) / 32 : 8;  // TMEM weight slots
+    static constexpr int DS_CAP = DS_TMEM < 8 ? DS_TMEM : 8;
+    static constexpr int DS_FIT = DS_RAW > DS_CAP ? DS_CAP : (DS_RAW < 2 ? 2 : DS_RAW);
+    // a multiple of NI: issuer i then owns the stages s = i mod NI, and its
+    // wait for K step kc follows its own wait for kc - DS (no parity aliasing)
+    static constexpr int DS = (DS_FIT / NI) * NI;
     static constexpr int S8_RAW = (BUDGET - DS * (W16 + XS)) / W8;
-    static constexpr int CG_RAW = DS >= 4 ? 4 : (DS >= 2 ? 2 : 1);
+    // converter groups: with TMEM weights a group is one warpgroup (its four
+    // warps reach the four TMEM lane quarters)
+    static constexpr int CG_RAW = TSA ? 2 : (DS >= 4 ? 4 : (DS >= 2 ? 2 : 1));
     static constexpr int CG = CG_RAW < AEM_QGEMM_MAX_CONV_GROUPS ? CG_RAW : AEM_QGEMM_MAX_CONV_GROUPS;
     // The int8 ring's depth is a multiple of the group count: then the
     // previous fill of the slot a group waits on (K step kc - S8) was that same
@@ -130,7 +150,8 @@ struct Cfg {
     // slot's older phase for kc's (bulk copies may land out of order, so a
     // fill owned by another group would give no such guarantee).
     static constexpr int S8 = ((S8_RAW > 12 ? 12 : S8_RAW) / CG) * CG;
-    static constexpr int TMEM_COLS = 2 * BT < 32 ? 32 : 2 * BT;
+    static constexpr int A_COL0 = 2 * NI * BT;     // first TMEM weight slot (TSA)
+    static constexpr int TMEM_COLS = pow2_cols(2 * NI * BT + (TSA ? 32 * DS : 0));
     static constexpr int BAR_BYTES = (2 * DS + 2 * S8 + 4) * 8 + 16;
     static constexpr int TAB_BYTES = 2 * (kMaxGroups + 1) * 4;
     static constexpr int SMEM = 1024 + DS * (W16 + XS) + S8 * W8 + BAR_BYTES + TAB_BYTES;
@@ -142,6 +163,8 @@ struct Cfg {
     static_assert(S8 >= 2 && DS >= 2, "pipeline needs two stages per ring");
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
     static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N for M=128");
+    static_assert(!TSA || (CG_WARPS == 4 && 2 * NI * BT + 32 * DS <= 512), "TMEM weight slots");
+    static_assert(NI == 1 || (TSA && DS % NI == 0 && DS >= NI), "several issuers need TMEM weights");
 };
 
 struct TileInfo {
@@ -237,11 +260,11 @@ __device__ __forceinline__ uint2 i8x4_to_bf16x4(uint32_t v) {
     return o;
 }
 
-template <int BT, int SPLIT>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BT, int SPLIT, bool TSA, int NI>
+__global__ void __launch_bounds__(Cfg<BT, SPLIT, TSA, NI>::THREADS, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tm_xh,
                     const __grid_constant__ CUtensorMap tm_xl, const TcParams p) {
-    using C = Cfg<BT, SPLIT>;
+    using C = Cfg<BT, SPLIT, TSA, NI>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -275,13 +298,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&w8_empty[s], C::CG_WARPS);
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&accf_bar[b], 1);
+            mbar_init(&accf_bar[b], NI);  // one commit per issuer
             mbar_init(&acce_bar[b], kEpiWarps);
         }
         *abort_flag = 0;
         fence_barrier_init();
     }
-    for (int i = tid; i <= p.G; i += kThreads)
+    for (int i = tid; i <= p.G; i += C::THREADS)
         s_rows[i] = p.group_rows ? p.group_rows[i] : (i == 0 ? 0 : static_cast<int>(p.M));
     if (warp == kMmaWarp) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -372,11 +395,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-    } else if (warp == kMmaWarp) {
-        // ================= MMA issuer
+    } else if (warp == kMmaWarp || (warp >= kMmaWarpX && warp < kMmaWarpX + NI - 1)) {
+        // ================= MMA issuer ii of NI: K steps kc = ii mod NI, into
+        // accumulator (b, ii) at TMEM columns (b * NI + ii) * BT
         if (lane == 0) {
-            int ss = 0;  // operand-ring stage
-            uint32_t phs = 0;
+            const int ii = warp == kMmaWarp ? 0 : warp - kMmaWarpX + 1;
+            uint32_t kc = 0;  // K steps so far, in the order every role walks them
             int it = 0;
             bool ok = true;
             TileInfo ti;
@@ -385,38 +409,55 @@ __global__ void __launch_bounds__(kThreads, 1)
                  ++it) {
                 const int b = it & 1;
                 const uint32_t aph = (it >> 1) & 1;
+                // every issuer waits, even one without K steps in this tile:
+                // its commit below then cannot count toward the buffer's
+                // previous tile
                 if (!mbar_wait_bounded(&acce_bar[b], aph ^ 1, abort_flag, p.err, ERR_GEMM_TIMEOUT))
                     break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BT);
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((b * NI + ii) * BT);
                 // a group's last tile may hold fewer rows: the MMA's N covers
                 // only those (a multiple of 16), the rest of the slot is unused
                 const int n_eff = min(BT, (ti.nrows + 15) & ~15);
                 const uint32_t idesc = idesc_bf16_f32(kCh, static_cast<uint32_t>(n_eff));
-                for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
+                bool first = true;
+                for (int kt = ti.kt0; kt < ti.kt1; ++kt, ++kc) {
+                    if (NI > 1 && static_cast<int>(kc % NI) != ii) continue;
+                    const int ss = static_cast<int>(kc % C::DS);
+                    const uint32_t phs = (kc / C::DS) & 1;
                     // activations and converted weights of this K step are in
                     if (!mbar_wait_bounded(&st_full[ss], phs, abort_flag, p.err, ERR_GEMM_TIMEOUT)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t adesc = smem_desc_sw128(smem_u32(w16_ring + ss * C::W16));
                     const uint64_t bdesc = smem_desc_sw128(smem_u32(x_ring + ss * C::XS));
                     const uint64_t ldesc = smem_desc_sw128(smem_u32(x_ring + ss * C::XS + C::XB));
+                    if constexpr (TSA) {
+                        // weights in TMEM slot ss: 8 columns per UMMA_K=16 step
+                        const uint32_t a_tmem =
+                            tmem_base + static_cast<uint32_t>(C::A_COL0 + 32 * ss);
 #pragma unroll
-                    for (int kk = 0; kk < kKT / 16; ++kk) {
-                        // +32 bytes along K per UMMA_K=16 step (start address field, >>4)
-                        tc_mma_f16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc,
-                                   (kt > ti.kt0 || kk > 0) ? 1u : 0u);
-                        if (SPLIT == 2)
-                            tc_mma_f16(d_tmem, adesc + 2 * kk, ldesc + 2 * kk, idesc, 1u);
+                        for (int kk = 0; kk < kKT / 16; ++kk) {
+                            tc_mma_f16_ts(d_tmem, a_tmem + 8 * kk, bdesc + 2 * kk, idesc,
+                                          (!first || kk > 0) ? 1u : 0u);
+                            if (SPLIT == 2)
+                                tc_mma_f16_ts(d_tmem, a_tmem + 8 * kk, ldesc + 2 * kk, idesc, 1u);
+                        }
+                    } else {
+                        const uint64_t adesc = smem_desc_sw128(smem_u32(w16_ring + ss * C::W16));
+#pragma unroll
+                        for (int kk = 0; kk < kKT / 16; ++kk) {
+                            // +32 bytes along K per UMMA_K=16 step (start address field, >>4)
+                            tc_mma_f16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc,
+                                       (!first || kk > 0) ? 1u : 0u);
+                            if (SPLIT == 2)
+                                tc_mma_f16(d_tmem, adesc + 2 * kk, ldesc + 2 * kk, idesc, 1u);
+                        }
                     }
                     // the stage is free once these MMAs retire
                     tc_commit(&st_empty[ss]);
-                    if (++ss == C::DS) {
-                        ss = 0;
-                        phs ^= 1;
-                    }
+                    first = false;
                 }
                 if (!ok) break;
                 tc_commit(&accf_bar[b]);
@@ -444,8 +485,39 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                uint8_t* st = w16_ring + s16 * C::W16;
                 const uint8_t* w8 = w8_ring + s8 * C::W8;
+                if constexpr (TSA) {
+                    // thread = one channel row = its TMEM lane: the row's 64 int8
+                    // (4 chunks, logical K order) -> 32 bf16x2 columns of slot s16
+                    tc_fence_after();  // after the MMAs that last read the slot
+                    const int r = 32 * (warp & 3) + lane;
+                    uint4 v[4];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        v[c] = *reinterpret_cast<const uint4*>(w8 + r * 64 + wtile_chunk(r, c) * 16);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&w8_empty[s8]);
+                    uint32_t a[32];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const uint32_t wv[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const uint2 o = i8x4_to_bf16x4(wv[e]);
+                            a[8 * c + 2 * e] = o.x;
+                            a[8 * c + 2 * e + 1] = o.y;
+                        }
+                    }
+                    tc_st_32x32b_x32(tmem_base + (static_cast<uint32_t>(32 * (warp & 3)) << 16) +
+                                         static_cast<uint32_t>(C::A_COL0 + 32 * s16),
+                                     a);
+                    tc_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&st_full[s16]);
+                    continue;
+                }
+                uint8_t* st = w16_ring + s16 * C::W16;
 #pragma unroll
                 for (int i = 0; i < 512 / C::CG_THREADS; ++i) {
                     const int item = gtid + C::CG_THREADS * i;  // 128 rows x 4 chunks
@@ -481,12 +553,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = ei & 3;
         const int h = ei >> 2;
         int it = 0;
+        uint32_t kc = 0;  // K steps so far (which issuers took part in a tile)
         // loop exits are warp-uniform: the TMEM loads below are warp-collective
         TileInfo ti;
         for (WorkCursor wc = work_begin(p, total, nkt);
              !__any_sync(0xFFFFFFFFu, *abort_flag != 0) &&
              work_next<BT>(wc, ti, s_rows, s_tiles, p, total, nch, nkt, kper);
              ++it) {
+            // issuer i accumulated into this tile iff one of its K steps
+            // (kc = i mod NI) falls in [kc0, kc0 + steps)
+            const uint32_t kc0 = kc;
+            const int steps = ti.kt1 - ti.kt0;
+            kc += static_cast<uint32_t>(steps);
             const int b = it & 1;
             const uint32_t aph = (it >> 1) & 1;
             if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&accf_bar[b], aph, abort_flag, p.err,
@@ -498,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float sc =
                 nvalid ? __ldg(p.scale + static_cast<int64_t>(ti.wg) * p.N + n) : 0.0f;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                                   static_cast<uint32_t>(b * BT);
+                                   static_cast<uint32_t>(b * NI * BT);
             const int cbeg = h * C::EPI_COLS;
             const int cend = min(cbeg + C::EPI_COLS, ti.nrows);
 #pragma unroll 1
@@ -513,8 +591,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (p.rowscale) my_rs = __ldg(p.rowscale + my_row);
                 }
                 uint32_t r[16];
-                tc_ld_32x32b_x16(tbase + c0, r);
-                tc_wait_ld();
+                if constexpr (NI == 1) {
+                    tc_ld_32x32b_x16(tbase + c0, r);
+                    tc_wait_ld();
+                } else {
+                    // the sum of the issuers' partial accumulators
+                    float sum[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) sum[j] = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < NI; ++i) {
+                        if ((i - static_cast<int>(kc0 % NI) + NI) % NI >= steps) continue;
+                        uint32_t t[16];
+                        tc_ld_32x32b_x16(tbase + static_cast<uint32_t>(i * BT + c0), t);
+                        tc_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) sum[j] += __uint_as_float(t[j]);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(sum[j]);
+                }
                 if (p.red_v4) {
                     // 16-byte reductions: a 4x4 transpose inside each lane quad
                     // gives lane 4m+i the four channels of quad m at column i,
@@ -1050,9 +1146,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (warp == kMmaWarp) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
 }
 
-template <int BT, int SPLIT>
+template <int BT, int SPLIT, bool TSA, int NI = 1>
 aem_status launch_tc(const GemmArgs& a, const TcParams& p, int grid, cudaStream_t s) {
-    using C = Cfg<BT, SPLIT>;
+    using C = Cfg<BT, SPLIT, TSA, NI>;
     const QWeight& w = *a.w;
     CUtensorMap th, tl;
     AEM_TRY(make_tmap_2d(&th, a.x_hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
@@ -1064,9 +1160,9 @@ aem_status launch_tc(const GemmArgs& a, const TcParams& p, int grid, cudaStream_
                              CU_TENSOR_MAP_SWIZZLE_128B));
     else
         tl = th;
-    auto kern = qgemm_tc_kernel<BT, SPLIT>;
+    auto kern = qgemm_tc_kernel<BT, SPLIT, TSA, NI>;
     AEM_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    kern<<<grid, kThreads, C::SMEM, s>>>(th, tl, p);
+    kern<<<grid, C::THREADS, C::SMEM, s>>>(th, tl, p);
     AEM_CHECK_LAUNCH();
     count_launches(1);
     return AEM_OK;
@@ -1127,13 +1223,25 @@ int max_pairs(int dev) {
 }
 
 template <int SPLIT>
-aem_status launch_bt(int bt, const GemmArgs& a, const TcParams& p, int grid, cudaStream_t s) {
+aem_status launch_bt(int bt, bool tsa, const GemmArgs& a, const TcParams& p, int grid,
+                     cudaStream_t s) {
+    if (tsa) {
+        // issuers: as many as TMEM holds accumulators for (4 up to 32-row
+        // tiles, 2 at 64 rows, 1 above)
+        switch (bt) {
+            case 16: return launch_tc<16, SPLIT, true, 4>(a, p, grid, s);
+            case 32: return launch_tc<32, SPLIT, true, 4>(a, p, grid, s);
+            case 64: return launch_tc<64, SPLIT, true, 2>(a, p, grid, s);
+            case 128: return launch_tc<128, SPLIT, true>(a, p, grid, s);
+            default: return launch_tc<192, SPLIT, true>(a, p, grid, s);
+        }
+    }
     switch (bt) {
-        case 16: return launch_tc<16, SPLIT>(a, p, grid, s);
-        case 32: return launch_tc<32, SPLIT>(a, p, grid, s);
-        case 64: return launch_tc<64, SPLIT>(a, p, grid, s);
-        case 128: return launch_tc<128, SPLIT>(a, p, grid, s);
-        default: return launch_tc<256, SPLIT>(a, p, grid, s);
+        case 16: return launch_tc<16, SPLIT, false>(a, p, grid, s);
+        case 32: return launch_tc<32, SPLIT, false>(a, p, grid, s);
+        case 64: return launch_tc<64, SPLIT, false>(a, p, grid, s);
+        case 128: return launch_tc<128, SPLIT, false>(a, p, grid, s);
+        default: return launch_tc<256, SPLIT, false>(a, p, grid, s);
     }
 }
 
@@ -1147,9 +1255,11 @@ int64_t tiles_estimate(int64_t M, int G, int bt, int64_t nch, int ks) {
 
 namespace {
 std::atomic<int> g_pair_mode{-1};
+std::atomic<int> g_tmem_a_mode{-1};
 }  // namespace
 
 int gemm_pair_mode() { return g_pair_mode.load(std::memory_order_relaxed); }
+int gemm_tmem_a_mode() { return g_tmem_a_mode.load(std::memory_order_relaxed); }
 
 aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
     AEM_REQUIRE(a.w != nullptr, "qgemm: weight handle is NULL");
@@ -1159,8 +1269,9 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
                 "qgemm: weight group out of range");
     AEM_REQUIRE(!(a.atomic_add && a.out_bf16), "qgemm: split-K needs float32 output");
     if (a.M == 0) return AEM_OK;
+    const int tmode = gemm_tmem_a_mode();
     // few rows (so few per group): the bandwidth-bound weight stream
-    if (a.M <= gemv_max_rows() && a.token_tile == 0) return launch_qgemm_gemv(a, s);
+    if (a.M <= gemv_max_rows() && a.token_tile == 0 && tmode != 1) return launch_qgemm_gemv(a, s);
     if (w.K % 8 != 0) return launch_qgemm_simt(a, s);
     AEM_REQUIRE(a.M < (1ll << 31) && w.G * w.N < (1ll << 31), "qgemm: too many rows");
     const int dev = current_device();
@@ -1175,6 +1286,9 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
         bt = avg <= 16 ? 16 : avg <= 32 ? 32 : avg <= 64 ? 64 : avg <= 128 ? 128 : 256;
         while (bt > 64 && tiles_estimate(m, a.G, bt, nch, 1) < 2 * sms) bt >>= 1;
     }
+    // converted weights in TMEM (A from tensor memory): token tiles up to 192
+    const bool tsa = tmode == 1 || (tmode < 0 && bt <= 64);
+    if (tsa && bt > 192) bt = 192;
     int ks = a.ksplit < 1 ? 1 : a.ksplit;
     if (ks > nkt) ks = static_cast<int>(nkt);
     const int kper = static_cast<int>((nkt + ks - 1) / ks);
@@ -1224,7 +1338,7 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
     // (an odd count leaves the last pair's second block idle: 1/12 of the
     // MMAs at 11 blocks, which measured slower than single SMs)
     const int mode = gemm_pair_mode();
-    if (!p.stream_k && bt >= 64 &&
+    if (!tsa && !p.stream_k && bt >= 64 &&
         (mode == 1 || (mode < 0 && bt >= 128 && (nch % 2 == 0 || nch >= 15)))) {
         const int64_t ptiles = ((rows + bt - 1) / bt + std::min<int64_t>(a.G, rows)) *
                                ((nch + 1) / 2) * ks;
@@ -1235,11 +1349,18 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
     }
     const int grid = p.stream_k ? sms
                                 : static_cast<int>(std::min<int64_t>(sms, std::max<int64_t>(1, tiles_ub)));
-    if (a.x_lo) return launch_bt<2>(bt, a, p, grid, s);
-    return launch_bt<1>(bt, a, p, grid, s);
+    if (a.x_lo) return launch_bt<2>(bt, tsa, a, p, grid, s);
+    return launch_bt<1>(bt, tsa, a, p, grid, s);
 }
 
 }  // namespace aem
+
+extern "C" aem_status aem_set_gemm_tmem_a(int mode) {
+    AEM_REQUIRE(mode == -1 || mode == 0 || mode == 1,
+                "aem_set_gemm_tmem_a: mode %d is not -1, 0 or 1", mode);
+    aem::g_tmem_a_mode.store(mode, std::memory_order_relaxed);
+    return AEM_OK;
+}
 
 extern "C" aem_status aem_set_gemm_pairs(int mode) {
     AEM_REQUIRE(mode == -1 || mode == 0 || mode == 1,

@@ -1,14 +1,21 @@
 // Bandwidth-bound INT8 GEMM for few activation rows (GEMV-style), on the
 // tensor cores' warp-level MMA.
 //
-// With at most 32 rows per weight group the work per weight byte is a few
+// With at most 16 rows per weight group the work per weight byte is a few
 // multiply-adds, so the kernel is a weight stream: every warp loads its int8
 // rows straight from global memory into registers (16-byte non-caching loads,
 // the next tile's while the current one is multiplied), converts them exactly
 // to bf16 in registers and multiplies them with mma.sync.m16n8k16 (bf16 in,
 // float32 accumulate).  No shared memory holds weights and no barrier paces
 // the stream; shared memory holds the CTA's activation rows, restaged every
-// 512 or 1024 K of its range.
+// 1024 K of its range.  Many small CTAs (four warps) per SM: converting int8
+// costs about two instructions per weight byte, so the kernel needs issue
+// slots and warps to hide latency as much as bytes in flight.  Measured on
+// B200 against this form, a bulk-copy shared-memory ring, a per-thread
+// cp.async pipeline, an fp16 conversion with four tiles in flight and the
+// tcgen05 kernel were all slower at 1-16 rows (fewer warps per SM, more
+// instructions, or the tcgen05 issue chain); the tcgen05 kernel wins from
+// 17 rows on.
 //
 // K permutation: a dot product does not depend on the order of K, so the MMA
 // fragment's K positions are mapped to memory such that thread (g, t) of a warp
@@ -35,7 +42,7 @@ namespace {
 
 constexpr int kGvWarps = 4;
 constexpr int kGvThreads = kGvWarps * 32;
-constexpr int kGvMaxRows = 32;
+constexpr int kGvMaxRows = 16;  // above: the tensor-core kernel (measured faster from 17 rows)
 
 // 4 signed bytes (one 32-bit word, bytes b0 b1 b2 b3) -> two bf16x2 words
 // (b0, b1) and (b2, b3), exact: each byte becomes the float 2^23 + (b + 128)
@@ -134,7 +141,7 @@ __global__ void __launch_bounds__(kGvThreads)
 #pragma unroll
             for (int c = 0; c < 4; ++c) acc[a][n][c] = 0.0f;
 
-    constexpr int SUB = NT8 <= 2 ? 16 : 8;  // 64-wide K tiles of activations staged at once
+    constexpr int SUB = 16;  // 64-wide K tiles of activations staged at once
     constexpr int XS = SUB * 64 * 2 + 16;   // padded activation row, bytes
     unsigned char* xs = gsm;                 // [NT8*8][XS] bf16 (hi)
     unsigned char* xls = gsm + NT8 * 8 * XS; // [NT8*8][XS] bf16 (lo), float32 activations only
@@ -269,7 +276,7 @@ __global__ void __launch_bounds__(kGvThreads)
 
 template <int NT8>
 aem_status launch_gv(const GvParams& p, int64_t groups, cudaStream_t s) {
-    constexpr int SUB = NT8 <= 2 ? 16 : 8;
+    constexpr int SUB = 16;
     const size_t smem = static_cast<size_t>((p.xl ? 2 : 1) * NT8 * 8) * (SUB * 64 * 2 + 16);
     auto kern = qgemv_kernel<NT8>;
     if (smem > 48 * 1024)
@@ -298,7 +305,7 @@ aem_status launch_qgemm_gemv(const GemmArgs& a, cudaStream_t s) {
     AEM_REQUIRE(err != nullptr, "qgemv: no device error word");
     // rows of the largest group: at most M (the group sizes live on the device)
     const int64_t mrows = std::min<int64_t>(a.M, kGvMaxRows);
-    const int nt8 = mrows <= 8 ? 1 : mrows <= 16 ? 2 : 4;
+    const int nt8 = mrows <= 8 ? 1 : 2;
     const int64_t groups = a.group_rows ? a.G : 1;
     const int64_t busy = std::min<int64_t>(groups, a.M) * w.NT;  // CTAs with rows per K range
     // K ranges: enough CTAs for ~4 per SM, ranges of at most 1024 K (shared
@@ -339,11 +346,8 @@ aem_status launch_qgemm_gemv(const GemmArgs& a, cudaStream_t s) {
     p.rowmap = a.rowmap;
     p.rowscale = a.rowscale;
     p.err = err;
-    switch (nt8) {
-        case 1: return launch_gv<1>(p, groups, s);
-        case 2: return launch_gv<2>(p, groups, s);
-        default: return launch_gv<4>(p, groups, s);
-    }
+    if (nt8 == 1) return launch_gv<1>(p, groups, s);
+    return launch_gv<2>(p, groups, s);
 }
 
 }  // namespace aem

@@ -195,6 +195,15 @@ aem_status aem_grouped_qgemm(aem_qweight_t w, const int32_t* group_rows, int G, 
  * pairs from 64-row tiles on.  Results agree within float32 summation
  * order.  No counterpart in the reference. */
 aem_status aem_set_gemm_pairs(int mode);
+/* Where the tensor-core GEMM keeps the converted bf16 weights (process-wide):
+ * -1 (default) automatic -- tensor memory (the MMA reads A from TMEM, so
+ * shared memory carries only the int8 stream and the activations) for token
+ * tiles up to 64 rows, shared memory above; 0 shared memory only; 1 tensor
+ * memory for every tile (token tiles capped at 192 rows, no SM pairs, and
+ * also for the few-row calls that otherwise take the weight-stream kernel).
+ * Results agree within float32 summation order.  No counterpart in the
+ * reference. */
+aem_status aem_set_gemm_tmem_a(int mode);
 /* HOST-buffer form of aem_qgemm (synchronous). */
 aem_status aem_qgemm_host(aem_context_t ctx, aem_qweight_t w, int64_t group, const void* x,
                           aem_dtype x_dtype, int64_t M, float* out);

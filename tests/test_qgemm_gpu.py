@@ -163,14 +163,46 @@ def test_groups_select_their_weights(cuda):
         _close(out.cpu().numpy(), O.qgemm(x, q[grp], s[grp:grp + 1]))
 
 
-@pytest.fixture(params=["single", "pairs"])
-def gemm_form(cuda, request):
-    """Runs a test with the single-SM GEMM only (aem_set_gemm_pairs(0)) and
-    with SM pairs from 64-row token tiles on (aem_set_gemm_pairs(1))."""
+def _set_form(form):
+    """single: single SMs, converted weights in shared memory; pairs: SM
+    pairs from 64-row token tiles on; tmem_a: single SMs with the converted
+    weights in tensor memory for every tile (the MMA reads A from TMEM; token
+    tiles capped at 192 rows; also taken by calls of at most 32 rows);
+    auto: the library's own choice."""
     from aethermoe_b200 import _lib
-    _lib.check(_lib.lib().aem_set_gemm_pairs(0 if request.param == "single" else 1))
+    L = _lib.lib()
+    pairs, tmem_a = {"single": (0, 0), "pairs": (1, 0), "tmem_a": (0, 1), "auto": (-1, -1)}[form]
+    _lib.check(L.aem_set_gemm_pairs(pairs))
+    _lib.check(L.aem_set_gemm_tmem_a(tmem_a))
+
+
+@pytest.fixture(params=["single", "pairs", "tmem_a"])
+def gemm_form(cuda, request):
+    """Runs a test with each form of the tensor-core GEMM (see _set_form)."""
+    _set_form(request.param)
     yield request.param
-    _lib.check(_lib.lib().aem_set_gemm_pairs(-1))
+    _set_form("auto")
+
+
+@pytest.fixture(params=["stream", "tmem_a"])
+def small_form(cuda, request):
+    """Few-row calls: the weight-stream kernel (default) and the tensor-core
+    kernel with weights in TMEM."""
+    _set_form("auto" if request.param == "stream" else "tmem_a")
+    yield request.param
+    _set_form("auto")
+
+
+@pytest.mark.parametrize("m", [1, 8, 64, 512])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_sweep_tmem_a(qg, sweep_weight, m, dtype):
+    """The sweep shape (K=4096, N=14336) with the converted weights in TMEM
+    for every tile, float32 (hi + lo) and bf16 activations."""
+    _set_form("tmem_a")
+    try:
+        test_sweep(qg, sweep_weight, m, dtype)
+    finally:
+        _set_form("auto")
 
 
 @pytest.mark.parametrize("tile", [256, 128, 64])
@@ -229,7 +261,7 @@ def test_grouped_ragged_tiles(cuda, gemm_form, tile, mode):
 
 
 @pytest.mark.parametrize("mode", ["relu_bf16", "scaled_add"])
-def test_grouped_decode_sizes(cuda, mode):
+def test_grouped_decode_sizes(cuda, small_form, mode):
     """At most 4 rows (decode sizes) take the CUDA-core path: groups of 0-2
     rows, a partial output-channel block, K not a multiple of 64."""
     import torch
@@ -362,12 +394,12 @@ def test_pairs_match_single_sms(cuda, m, dtype):
     np.testing.assert_allclose(res[1], res[0], rtol=1e-5, atol=1e-5)
 
 
-@pytest.mark.parametrize("sizes,K,N", [([0, 1, 7, 9, 0, 15], 448, 300), ([32], 200, 130),
-                                        ([3, 0, 5], 4096, 1536), ([16, 16], 40, 257)])
+@pytest.mark.parametrize("sizes,K,N", [([0, 1, 6, 0, 9], 448, 300), ([16], 200, 130),
+                                        ([3, 0, 5], 4096, 1536), ([8, 8], 40, 257)])
 @pytest.mark.parametrize("mode", ["relu_bf16", "scaled_add", "f32_store"])
-def test_weight_stream_path(cuda, sizes, K, N, mode):
-    """At most 32 rows: the bandwidth-bound weight stream (warp MMAs on
-    registers loaded straight from the int8 tiles).  Groups of 0-32 rows, K
+def test_weight_stream_path(cuda, small_form, sizes, K, N, mode):
+    """At most 16 rows: the bandwidth-bound weight stream (warp MMAs on
+    registers loaded straight from the int8 tiles).  Groups of 0-16 rows, K
     and N that are not multiples of the 64 x 128 tile, float32 activations as
     hi + lo (f32_store; the layer tests cover the hi + lo hidden output)."""
     import torch
