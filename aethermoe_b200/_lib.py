@@ -16,7 +16,7 @@ LIB_PATH = os.path.join(HERE, "libaethermoe.so")
 
 AEM_OK, AEM_EINVAL, AEM_ECUDA, AEM_ENCCL, AEM_ETIMEOUT, AEM_ENOMEM, AEM_EUNSUPPORTED, AEM_EDEVICE = range(8)
 F32, BF16 = 0, 1
-GATING_EXACT, GATING_FAST = 0, 1
+GATING_EXACT, GATING_FAST, GATING_CERTIFIED = 0, 1, 2
 CAPACITY_UNLIMITED = (1 << 64) - 1
 MAX_EXPERTS = 256
 MAX_TOPK = 64
@@ -93,6 +93,7 @@ _SIGS = {
     "aem_context_stream": (_vp, [_vp]),
     "aem_gate_pack": (_int, [_vp, _vp, _i64, _i64, _int, ctypes.POINTER(_vp)]),
     "aem_gate_free": (_int, [_vp]),
+    "aem_gate_fallback_rows": (_int, [_vp, ctypes.POINTER(_i64)]),
     "aem_gating": (_int, [_vp, _vp, _int, _i64, _int, _int, _int, _vp, _vp, _vp]),
     "aem_gating_host": (_int, [_vp, _vp, _vp, _int, _i64, _int, _int, _int, _vp, _vp]),
     "aem_quantize_int8": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
@@ -237,6 +238,12 @@ class Gate:
                                   device, ctypes.byref(h)), "aem_gate_pack")
         self.handle = h.value
         self.D, self.E, self.device = d, e, device
+
+    def fallback_rows(self):
+        """Rows of CERTIFIED-mode calls recomputed with the EXACT arithmetic so far."""
+        n = _i64()
+        check(lib().aem_gate_fallback_rows(self.handle, ctypes.byref(n)), "aem_gate_fallback_rows")
+        return n.value
 
     def close(self):
         if getattr(self, "handle", None):

@@ -19,6 +19,7 @@
 // of the CTA.  The top-k is a register/shuffle argmax inside the lane group.
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cfloat>
 
 #include "common.cuh"
@@ -152,11 +153,105 @@ __device__ __forceinline__ void topk_select(float (&v)[NSLOT], int le, unsigned 
     __syncwarp(gmask);
 }
 
-template <int GROUP, int NSLOT, int kTPG, int WARPS, typename XT, bool EXACT, int DKO = 0>
+// ---------------------------------------------------------------------------
+// CERTIFIED mode.  Fast logits F (fused multiply-adds, any order of d split
+// into 64-wide blocks) come with a bound B such that the EXACT logit (float32
+// products summed in increasing d order, then + bias) lies in [F - B, F + B].
+// With P_i the partial sums and a_j >= sum over block j of |x_d w_d|:
+//   * the EXACT sum's rounding is at most u * (sum_i |P_i| + sum |p_i|),
+//   * a chain of fused multiply-adds' rounding is at most u * sum_i |acc_i|,
+//   * inside a block every partial sum is within a_j of the block's end, so
+//     sum_i |P_i| over the block <= 64 * (|P at the block end| + a_j),
+//   * parts of d summed separately and then added carry their start offsets
+//     (sum over a part of |P_i| <= part length * |P at the part start| + the
+//     part's own bound) and one rounding per addition,
+// so with Q = sum over blocks of (64 |P_end| + 65 a_j) (plus the parts'
+// offsets) and Qc = sum over parts of (|P_start| + |S_part|),
+//   |F - EXACT| <= u (2 Q + Qc + 2|F| + 2|b|) (1 + O(D u)),
+// and B = 4 u (Q + Qc + |F| + |b|) leaves a margin for the second-order terms
+// and the float32 rounding of the bound itself.  a_j is the Cauchy-Schwarz
+// bound |x_block| |w_block| (norms precomputed for the weights, per token and
+// block for the activations).  u = 2^-24.
+constexpr float kCertU4 = 4.0f * 5.9604645e-8f;
+
+// Certification of one token's selection from fast logits F and bounds B
+// held by a group of GROUP lanes (lane le owns experts le + GROUP*s): true
+// when every logit is finite, the top ksel (by F, ties to the lowest id) have
+// pairwise ordered intervals (each one's lower end above the next one's upper
+// end) and the last one's lower end is above every unselected expert's upper
+// end -- then the EXACT logits select the same experts in the same order.
+template <int GROUP, int NSLOT>
+__device__ __forceinline__ bool certify_row(const float (&F)[NSLOT], const float (&B)[NSLOT],
+                                            int le, unsigned gmask, int E, int ksel) {
+    bool fin = true;
+#pragma unroll
+    for (int s = 0; s < NSLOT; ++s) {
+        const int e = le + GROUP * s;
+        if (e < E && !(isfinite(F[s]) && isfinite(B[s]))) fin = false;
+    }
+    if (!__all_sync(gmask, fin)) return false;
+    bool sel[NSLOT];
+#pragma unroll
+    for (int s = 0; s < NSLOT; ++s) sel[s] = false;
+    bool ok = true;
+    float prev_lo = 0.0f;
+    for (int kk = 0; kk < ksel; ++kk) {
+        uint64_t bkey = 0;
+        float bf = 0.0f, bb = 0.0f;
+#pragma unroll
+        for (int s = 0; s < NSLOT; ++s) {
+            const int e = le + GROUP * s;
+            const uint64_t key = select_key(F[s], e);
+            if (e < E && !sel[s] && key > bkey) {
+                bkey = key;
+                bf = F[s];
+                bb = B[s];
+            }
+        }
+#pragma unroll
+        for (int off = GROUP / 2; off >= 1; off >>= 1) {
+            const uint64_t ok2 = __shfl_xor_sync(gmask, bkey, off, GROUP);
+            const float of = __shfl_xor_sync(gmask, bf, off, GROUP);
+            const float ob = __shfl_xor_sync(gmask, bb, off, GROUP);
+            if (ok2 > bkey) {
+                bkey = ok2;
+                bf = of;
+                bb = ob;
+            }
+        }
+        const int beste = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(bkey));
+#pragma unroll
+        for (int s = 0; s < NSLOT; ++s)
+            if (le + GROUP * s == beste) sel[s] = true;
+        if (kk > 0 && !(prev_lo > bf + bb)) ok = false;
+        prev_lo = bf - bb;
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int s = 0; s < NSLOT; ++s) {
+        const int e = le + GROUP * s;
+        if (e < E && !sel[s]) mx = fmaxf(mx, F[s] + B[s]);
+    }
+#pragma unroll
+    for (int off = GROUP / 2; off >= 1; off >>= 1)
+        mx = fmaxf(mx, __shfl_xor_sync(gmask, mx, off, GROUP));
+    if (ksel < E && !(prev_lo > mx)) ok = false;
+    return ok;
+}
+
+// Appends row tg to the uncertified list (rows[0] = count).
+__device__ __forceinline__ void cert_defer(int* rows, int64_t tg) {
+    const int i = atomicAdd(rows, 1);
+    rows[1 + i] = static_cast<int>(tg);
+}
+
+template <int GROUP, int NSLOT, int kTPG, int WARPS, typename XT, bool EXACT, int DKO = 0,
+          bool CERT = false>
 __global__ void __launch_bounds__(WARPS * 32)
     gating_kernel(const XT* __restrict__ x, const float4* __restrict__ wpk,
                   const float* __restrict__ bias, int64_t N, int D, int E, int k, int ksel,
-                  int32_t* __restrict__ idx_out, float* __restrict__ val_out) {
+                  int32_t* __restrict__ idx_out, float* __restrict__ val_out,
+                  const float* __restrict__ wsq16, int* __restrict__ cert_rows) {
     using C = GatingCfg<GROUP, NSLOT, kTPG, WARPS, XT, DKO>;
     constexpr int kThreads = C::kThreads;
     constexpr int GPW = C::GPW;
@@ -178,6 +273,7 @@ __global__ void __launch_bounds__(WARPS * 32)
     float4* wring = reinterpret_cast<float4*>(gsm);
     uint4* xring = reinterpret_cast<uint4*>(gsm + sizeof(float4) * kStages * WST);
     float* xs = reinterpret_cast<float*>(xring + kStages * XST);
+    float* xn = xs + (TOK / 2) * XS;  // CERTIFIED: |x| of the chunk, per token
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -188,10 +284,14 @@ __global__ void __launch_bounds__(WARPS * 32)
     const int tbase = (warp * GPW + grp) * kTPG;  // first local token of this lane group
 
     float2 acc[kTPG / 2][NSLOT];  // (token 2p, token 2p+1) of this lane group
+    float2 qb[kTPG / 2][NSLOT];   // CERTIFIED: the bound's sum Q (see certify_row)
 #pragma unroll
     for (int i = 0; i < kTPG / 2; ++i)
 #pragma unroll
-        for (int s = 0; s < NSLOT; ++s) acc[i][s] = make_float2(0.0f, 0.0f);
+        for (int s = 0; s < NSLOT; ++s) {
+            acc[i][s] = make_float2(0.0f, 0.0f);
+            qb[i][s] = make_float2(0.0f, 0.0f);
+        }
 
     // activation rows can be copied in 16-byte pieces when every row start is aligned
     const bool xvec = (static_cast<int64_t>(D) * XB) % 16 == 0 &&
@@ -289,7 +389,42 @@ __global__ void __launch_bounds__(WARPS * 32)
                 }
             }
         }
+        if constexpr (CERT) {
+            // |x| over this chunk, per token (warps over tokens, lanes over d)
+            for (int t = warp; t < TOK; t += WARPS) {
+                float ss = 0.0f;
+                for (int dd = lane; dd < DK; dd += 32) {
+                    const float v = xs[(t >> 1) * XS + (dd >> 2) * 8 + (dd & 3) * 2 + (t & 1)];
+                    ss = fmaf(v, v, ss);
+                }
+#pragma unroll
+                for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
+                if (lane == 0) xn[t] = sqrtf(ss);
+            }
+        }
         __syncthreads();  // the stage and xs are rewritten next
+        if constexpr (CERT) {
+            // Q += DK |P at the chunk's end| + (DK + 1) |x_chunk| |w_chunk|
+            float wn[NSLOT];
+#pragma unroll
+            for (int s = 0; s < NSLOT; ++s) {
+                const int e = le + GROUP * s;
+                float sq = 0.0f;
+                for (int b = 0; b < DK / 16; ++b) sq += __ldg(wsq16 + (c * (DK / 16) + b) * EPAD + e);
+                wn[s] = sqrtf(sq);
+            }
+#pragma unroll
+            for (int p = 0; p < kTPG / 2; ++p) {
+                const float x0 = xn[tbase + 2 * p], x1 = xn[tbase + 2 * p + 1];
+#pragma unroll
+                for (int s = 0; s < NSLOT; ++s) {
+                    qb[p][s].x += static_cast<float>(DK) * fabsf(acc[p][s].x) +
+                                  static_cast<float>(DK + 1) * x0 * wn[s];
+                    qb[p][s].y += static_cast<float>(DK) * fabsf(acc[p][s].y) +
+                                  static_cast<float>(DK + 1) * x1 * wn[s];
+                }
+            }
+        }
     }
     cp_async_wait<0>();
 
@@ -312,6 +447,18 @@ __global__ void __launch_bounds__(WARPS * 32)
             const int e = le + GROUP * s;
             const float lg = (i & 1) ? acc[i >> 1][s].y : acc[i >> 1][s].x;
             v[s] = e < E ? __fadd_rn(lg, bv[s]) : -FLT_MAX;
+        }
+        if constexpr (CERT) {
+            float bnd[NSLOT];
+#pragma unroll
+            for (int s = 0; s < NSLOT; ++s) {
+                const float q = (i & 1) ? qb[i >> 1][s].y : qb[i >> 1][s].x;
+                bnd[s] = kCertU4 * (q + fabsf(v[s]) + fabsf(bv[s]));
+            }
+            if (!certify_row<GROUP, NSLOT>(v, bnd, le, gmask, E, ksel)) {
+                if (le == 0 && tg < N) cert_defer(cert_rows, tg);
+                continue;
+            }
         }
         topk_select<GROUP, NSLOT>(v, le, gmask, tg, N, E, k, ksel, idx_out, val_out);
     }
@@ -608,6 +755,208 @@ cudaError_t launch_small(const Gate& g, const void* x, int64_t N, int k, int kse
     }
 }
 
+// CERTIFIED mode for few tokens: d split over threads.  A CTA takes kCertTT
+// tokens and all experts; thread (e, p) of the 256 sums expert e's products
+// over part p of d (P = 256 / EPAD contiguous parts, whole 64-wide blocks)
+// with fused multiply-adds for the CTA's tokens, keeping per block the
+// bound's sum Q (64 |P_end| + 65 |x_block| |w_block|); one thread per
+// (token, expert) then adds the parts in order, carrying their start offsets
+// into Q (part length * |P_start|) and the additions' own rounding into Qc,
+// and a warp per token certifies and selects.  The activation rows and
+// their per-block norms live in shared memory; the weights are read from the
+// packed [Dpad/4][Epad][4] layout (L2-resident, shared by the CTA's tokens).
+constexpr int kCertTT = 4;
+constexpr int kCertThreads = 256;
+
+__host__ __device__ constexpr size_t cert_small_smem(int64_t Dpad, int EPAD) {
+    return sizeof(float) * (static_cast<size_t>(kCertTT) * Dpad +      // activations
+                            static_cast<size_t>(kCertTT) * (Dpad / 64) +  // block norms
+                            2 * static_cast<size_t>(kCertTT) * kCertThreads +  // part sums, Q
+                            2 * static_cast<size_t>(kCertTT) * EPAD);      // logits, bounds
+}
+
+template <int EPAD, typename XT>
+__global__ void __launch_bounds__(kCertThreads)
+    gating_cert_small_kernel(const XT* __restrict__ x, const float4* __restrict__ wpk,
+                             const float* __restrict__ bias, const float* __restrict__ wsq16,
+                             int64_t N, int D, int64_t Dpad, int E, int k, int ksel,
+                             int32_t* __restrict__ idx_out, float* __restrict__ val_out,
+                             int* __restrict__ cert_rows) {
+    constexpr int P = kCertThreads / EPAD;  // parts of d
+    constexpr int TT = kCertTT;
+    extern __shared__ __align__(16) float csm[];
+    float* xs = csm;                                   // [TT][Dpad]
+    float* xnb = xs + TT * Dpad;                       // [TT][Dpad/64]
+    float* ps = xnb + TT * (Dpad / 64);                // [TT][P][EPAD] part sums
+    float* pq = ps + TT * kCertThreads;                // [TT][P][EPAD] part Q
+    float* fl = pq + TT * kCertThreads;                // [TT][EPAD] fast logits
+    float* fb = fl + TT * EPAD;                        // [TT][EPAD] bounds
+    const int tid = threadIdx.x;
+    const int64_t tok0 = static_cast<int64_t>(blockIdx.x) * TT;
+    const int nblk = static_cast<int>(Dpad / 64);
+    // activation rows as float32, zero past D and past N
+    for (int64_t i = tid; i < TT * Dpad; i += kCertThreads) {
+        const int t = static_cast<int>(i / Dpad);
+        const int64_t d = i - static_cast<int64_t>(t) * Dpad;
+        xs[i] = (tok0 + t < N && d < D) ? load_x<XT>(x + (tok0 + t) * static_cast<int64_t>(D) + d)
+                                        : 0.0f;
+    }
+    __syncthreads();
+    for (int i = tid; i < TT * nblk; i += kCertThreads) {
+        const float* v = xs + static_cast<int64_t>(i / nblk) * Dpad + static_cast<int64_t>(i % nblk) * 64;
+        float ss = 0.0f;
+#pragma unroll 8
+        for (int j = 0; j < 64; ++j) ss = fmaf(v[j], v[j], ss);
+        xnb[i] = sqrtf(ss);
+    }
+    __syncthreads();
+    // ---- part p of d for expert e, all TT tokens
+    const int e = tid % EPAD;
+    const int p = tid / EPAD;
+    const int bpp = (nblk + P - 1) / P;  // blocks per part
+    const int b0 = p * bpp, b1 = min(nblk, b0 + bpp);
+    float acc[TT], q[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+        acc[t] = 0.0f;
+        q[t] = 0.0f;
+    }
+    for (int b = b0; b < b1; ++b) {
+#pragma unroll 4
+        for (int d4 = b * 16; d4 < b * 16 + 16; ++d4) {
+            const float4 w = __ldg(wpk + static_cast<int64_t>(d4) * EPAD + e);
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+                const float4 xv = *reinterpret_cast<const float4*>(xs + t * Dpad + 4 * d4);
+                acc[t] = fmaf(xv.x, w.x, acc[t]);
+                acc[t] = fmaf(xv.y, w.y, acc[t]);
+                acc[t] = fmaf(xv.z, w.z, acc[t]);
+                acc[t] = fmaf(xv.w, w.w, acc[t]);
+            }
+        }
+        const float* ws = wsq16 + static_cast<int64_t>(b) * 4 * EPAD + e;
+        const float wn = sqrtf(__ldg(ws) + __ldg(ws + EPAD) + __ldg(ws + 2 * EPAD) + __ldg(ws + 3 * EPAD));
+#pragma unroll
+        for (int t = 0; t < TT; ++t)
+            q[t] += 64.0f * fabsf(acc[t]) + 65.0f * xnb[t * nblk + b] * wn;
+    }
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+        ps[t * kCertThreads + tid] = acc[t];
+        pq[t * kCertThreads + tid] = q[t];
+    }
+    __syncthreads();
+    // ---- parts in order: logit, Q with the parts' offsets, Qc
+    for (int i = tid; i < TT * EPAD; i += kCertThreads) {
+        const int t = i / EPAD, ee = i % EPAD;
+        float run = 0.0f, Q = 0.0f, Qc = 0.0f;
+        for (int pp = 0; pp < P; ++pp) {
+            const float sp = ps[t * kCertThreads + pp * EPAD + ee];
+            Q += pq[t * kCertThreads + pp * EPAD + ee] + 64.0f * bpp * fabsf(run);
+            Qc += fabsf(run) + fabsf(sp);
+            run += sp;
+        }
+        const float b = ee < E ? __ldg(bias + ee) : 0.0f;
+        const float f = ee < E ? __fadd_rn(run, b) : -FLT_MAX;
+        fl[i] = f;
+        fb[i] = kCertU4 * (Q + Qc + fabsf(f) + fabsf(b));
+    }
+    __syncthreads();
+    // ---- a warp per token: certify, then select from the fast logits or defer
+    constexpr int GROUP = EPAD < 32 ? EPAD : 32;
+    constexpr int NSLOT = EPAD / GROUP;
+    const int warp = tid >> 5, lane = tid & 31;
+    if (warp < TT && lane < GROUP) {
+        const int t = warp;
+        const int64_t tg = tok0 + t;
+        const unsigned gmask = GROUP == 32 ? 0xFFFFFFFFu : ((1u << GROUP) - 1u);
+        float v[NSLOT], bnd[NSLOT];
+#pragma unroll
+        for (int s2 = 0; s2 < NSLOT; ++s2) {
+            v[s2] = fl[t * EPAD + lane + GROUP * s2];
+            bnd[s2] = fb[t * EPAD + lane + GROUP * s2];
+        }
+        if (tg < N) {
+            if (certify_row<GROUP, NSLOT>(v, bnd, lane, gmask, E, ksel))
+                topk_select<GROUP, NSLOT>(v, lane, gmask, tg, N, E, k, ksel, idx_out, val_out);
+            else if (lane == 0)
+                cert_defer(cert_rows, tg);
+        }
+    }
+}
+
+// EXACT recomputation of the rows a certified launch deferred (rows[0] of
+// them at rows[1..]): float32 products summed in increasing d order, bias
+// last, the same selection -- what the EXACT kernels write for those rows.
+// Persistent CTAs over the list; a thread per expert walks all of d (a
+// sequential chain: these are rare rows), the weights from the packed
+// layout, the activation row from shared memory.
+template <int EPAD, typename XT>
+__global__ void __launch_bounds__(EPAD < 32 ? 32 : EPAD)
+    gating_exact_rows_kernel(const XT* __restrict__ x, const float4* __restrict__ wpk,
+                             const float* __restrict__ bias, int64_t N, int D, int64_t Dpad, int E,
+                             int k, int ksel, int32_t* __restrict__ idx_out,
+                             float* __restrict__ val_out, const int* __restrict__ rows,
+                             unsigned long long* __restrict__ total) {
+    constexpr int NT = EPAD < 32 ? 32 : EPAD;
+    constexpr int GROUP = EPAD < 32 ? EPAD : 32;
+    constexpr int NSLOT = EPAD / GROUP;
+    extern __shared__ __align__(16) float esm[];
+    float* xr = esm;          // [Dpad]
+    float* lg = esm + Dpad;   // [EPAD]
+    const int count = rows[0];
+    if (blockIdx.x == 0 && threadIdx.x == 0 && count > 0)
+        atomicAdd(total, static_cast<unsigned long long>(count));
+    const int tid = threadIdx.x;
+    for (int r = blockIdx.x; r < count; r += gridDim.x) {
+        const int64_t tg = rows[1 + r];
+        __syncthreads();  // the previous row's shared data is consumed
+        for (int64_t d = tid; d < Dpad; d += NT)
+            xr[d] = (tg < N && d < D) ? load_x<XT>(x + tg * static_cast<int64_t>(D) + d) : 0.0f;
+        __syncthreads();
+        if (tid < EPAD) {
+            float a = 0.0f;
+            for (int d4 = 0; d4 < (D + 3) / 4; ++d4) {
+                const float4 w = __ldg(wpk + static_cast<int64_t>(d4) * EPAD + tid);
+                const float4 xv = *reinterpret_cast<const float4*>(xr + 4 * d4);
+                a = __fadd_rn(a, __fmul_rn(xv.x, w.x));
+                a = __fadd_rn(a, __fmul_rn(xv.y, w.y));
+                a = __fadd_rn(a, __fmul_rn(xv.z, w.z));
+                a = __fadd_rn(a, __fmul_rn(xv.w, w.w));
+            }
+            lg[tid] = tid < E ? __fadd_rn(a, __ldg(bias + tid)) : -FLT_MAX;
+        }
+        __syncthreads();
+        if (tid < GROUP) {
+            const unsigned gmask = GROUP == 32 ? 0xFFFFFFFFu : ((1u << GROUP) - 1u);
+            float v[NSLOT];
+#pragma unroll
+            for (int s2 = 0; s2 < NSLOT; ++s2) v[s2] = lg[tid + GROUP * s2];
+            topk_select<GROUP, NSLOT>(v, tid, gmask, tg, N, E, k, ksel, idx_out, val_out);
+        }
+    }
+}
+
+// Squared norms of the packed weights per 16-wide block of d: out[b][e] =
+// sum over d in [16b, 16b+16) of w[d][e]^2, [Dpad/16][Epad].
+__global__ void gate_norms_kernel(const float4* __restrict__ wpk, int64_t Dpad, int64_t Epad,
+                                  float* __restrict__ out) {
+    const int64_t total = (Dpad / 16) * Epad;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t b = i / Epad, e = i % Epad;
+        float ss = 0.0f;
+        for (int j = 0; j < 4; ++j) {
+            const float4 w = wpk[(b * 4 + j) * Epad + e];
+            ss = fmaf(w.x, w.x, ss);
+            ss = fmaf(w.y, w.y, ss);
+            ss = fmaf(w.z, w.z, ss);
+            ss = fmaf(w.w, w.w, ss);
+        }
+        out[i] = ss;
+    }
+}
+
 // [Dpad/4][Epad][4] -> [Epad/eb][Dpad/4][eb][4]
 __global__ void block_gate_kernel(const float4* __restrict__ wt, int64_t D4, int64_t Epad, int eb,
                                   float4* __restrict__ out) {
@@ -621,24 +970,26 @@ __global__ void block_gate_kernel(const float4* __restrict__ wt, int64_t D4, int
     }
 }
 
-template <int GROUP, int NSLOT, int TPG, typename XT, bool EXACT, int WARPS = kWarps, int DKO = 0>
+template <int GROUP, int NSLOT, int TPG, typename XT, bool EXACT, int WARPS = kWarps, int DKO = 0,
+          bool CERT = false>
 cudaError_t launch_one(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
                        float* val, cudaStream_t s) {
     using C = GatingCfg<GROUP, NSLOT, TPG, WARPS, XT, DKO>;
     const int64_t blocks = (N + C::TOK - 1) / C::TOK;
-    auto kern = gating_kernel<GROUP, NSLOT, TPG, WARPS, XT, EXACT, DKO>;
-    if (C::SMEM > 48 * 1024) {
+    auto kern = gating_kernel<GROUP, NSLOT, TPG, WARPS, XT, EXACT, DKO, CERT>;
+    const size_t smem = C::SMEM + (CERT ? 4 * C::TOK : 0);
+    if (smem > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(
-            kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM));
+            kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
     }
-    kern<<<static_cast<unsigned>(blocks), WARPS * 32, C::SMEM, s>>>(
+    kern<<<static_cast<unsigned>(blocks), WARPS * 32, smem, s>>>(
         static_cast<const XT*>(x), reinterpret_cast<const float4*>(g.wt), g.bias, N,
-        static_cast<int>(g.D), static_cast<int>(g.E), k, ksel, idx, val);
+        static_cast<int>(g.D), static_cast<int>(g.E), k, ksel, idx, val, g.wsq16, g.cert_rows);
     return cudaGetLastError();
 }
 
-template <typename XT, bool EXACT>
+template <typename XT, bool EXACT, bool CERT = false>
 cudaError_t dispatch_e(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
                        float* val, cudaStream_t s) {
     // Few tokens through a narrow gate: few CTAs, each walking all of D, so
@@ -648,8 +999,8 @@ cudaError_t dispatch_e(const Gate& g, const void* x, int64_t N, int k, int ksel,
     // than the barriers it saves (78 -> 94 us at E=64).
     if (N <= 1024) {
         switch (g.Epad) {
-            case 8: return launch_one<8, 1, 2, XT, EXACT, 4, 256>(g, x, N, k, ksel, idx, val, s);
-            case 16: return launch_one<16, 1, 2, XT, EXACT, 4, 256>(g, x, N, k, ksel, idx, val, s);
+            case 8: return launch_one<8, 1, 2, XT, EXACT, 4, 256, CERT>(g, x, N, k, ksel, idx, val, s);
+            case 16: return launch_one<16, 1, 2, XT, EXACT, 4, 256, CERT>(g, x, N, k, ksel, idx, val, s);
             default: break;
         }
     }
@@ -659,10 +1010,10 @@ cudaError_t dispatch_e(const Gate& g, const void* x, int64_t N, int k, int ksel,
         // 7 warps: 56 tokens per CTA, so 16384 tokens make 293 CTAs -- two
         // per SM on all 148 SMs instead of two on 108 and one on 40
         switch (g.Epad) {
-            case 8: return launch_one<8, 1, 8, XT, EXACT, 7>(g, x, N, k, ksel, idx, val, s);
-            case 16: return launch_one<16, 1, 8, XT, EXACT, 7>(g, x, N, k, ksel, idx, val, s);
-            case 32: return launch_one<32, 1, 8, XT, EXACT, 7>(g, x, N, k, ksel, idx, val, s);
-            case 64: return launch_one<32, 2, 8, XT, EXACT, 7>(g, x, N, k, ksel, idx, val, s);
+            case 8: return launch_one<8, 1, 8, XT, EXACT, 7, 0, CERT>(g, x, N, k, ksel, idx, val, s);
+            case 16: return launch_one<16, 1, 8, XT, EXACT, 7, 0, CERT>(g, x, N, k, ksel, idx, val, s);
+            case 32: return launch_one<32, 1, 8, XT, EXACT, 7, 0, CERT>(g, x, N, k, ksel, idx, val, s);
+            case 64: return launch_one<32, 2, 8, XT, EXACT, 7, 0, CERT>(g, x, N, k, ksel, idx, val, s);
             default: break;
         }
     }
@@ -671,20 +1022,20 @@ cudaError_t dispatch_e(const Gate& g, const void* x, int64_t N, int k, int ksel,
         // even T = 2048 spreads over 256 CTAs; the weights' chunks then come
         // from L2 once per 8 tokens.
         switch (g.Epad) {
-            case 32: return launch_one<32, 1, 2, XT, EXACT, 4>(g, x, N, k, ksel, idx, val, s);
-            case 64: return launch_one<32, 2, 2, XT, EXACT, 4>(g, x, N, k, ksel, idx, val, s);
-            case 128: return launch_one<32, 4, 2, XT, EXACT, 4>(g, x, N, k, ksel, idx, val, s);
-            case 256: return launch_one<32, 8, 2, XT, EXACT, 4>(g, x, N, k, ksel, idx, val, s);
+            case 32: return launch_one<32, 1, 2, XT, EXACT, 4, 0, CERT>(g, x, N, k, ksel, idx, val, s);
+            case 64: return launch_one<32, 2, 2, XT, EXACT, 4, 0, CERT>(g, x, N, k, ksel, idx, val, s);
+            case 128: return launch_one<32, 4, 2, XT, EXACT, 4, 0, CERT>(g, x, N, k, ksel, idx, val, s);
+            case 256: return launch_one<32, 8, 2, XT, EXACT, 4, 0, CERT>(g, x, N, k, ksel, idx, val, s);
             default: break;
         }
     }
     switch (g.Epad) {
-        case 8: return launch_one<8, 1, 4, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
-        case 16: return launch_one<16, 1, 4, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
-        case 32: return launch_one<32, 1, 4, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
-        case 64: return launch_one<32, 2, 4, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
-        case 128: return launch_one<32, 4, 4, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
-        default: return launch_one<32, 8, 4, XT, EXACT>(g, x, N, k, ksel, idx, val, s);
+        case 8: return launch_one<8, 1, 4, XT, EXACT, kWarps, 0, CERT>(g, x, N, k, ksel, idx, val, s);
+        case 16: return launch_one<16, 1, 4, XT, EXACT, kWarps, 0, CERT>(g, x, N, k, ksel, idx, val, s);
+        case 32: return launch_one<32, 1, 4, XT, EXACT, kWarps, 0, CERT>(g, x, N, k, ksel, idx, val, s);
+        case 64: return launch_one<32, 2, 4, XT, EXACT, kWarps, 0, CERT>(g, x, N, k, ksel, idx, val, s);
+        case 128: return launch_one<32, 4, 4, XT, EXACT, kWarps, 0, CERT>(g, x, N, k, ksel, idx, val, s);
+        default: return launch_one<32, 8, 4, XT, EXACT, kWarps, 0, CERT>(g, x, N, k, ksel, idx, val, s);
     }
 }
 
@@ -706,12 +1057,63 @@ __global__ void pack_gate_kernel(const float* __restrict__ w, const float* __res
         bout[e] = (e < E && b) ? b[e] : 0.0f;
 }
 
+template <int EPAD, typename XT>
+cudaError_t launch_cert_e(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
+                          float* val, bool small, cudaStream_t s) {
+    if (small) {
+        const size_t smem = cert_small_smem(g.Dpad, EPAD);
+        auto kern = gating_cert_small_kernel<EPAD, XT>;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        kern<<<static_cast<unsigned>((N + kCertTT - 1) / kCertTT), kCertThreads, smem, s>>>(
+            static_cast<const XT*>(x), reinterpret_cast<const float4*>(g.wt), g.bias, g.wsq16, N,
+            static_cast<int>(g.D), g.Dpad, static_cast<int>(g.E), k, ksel, idx, val, g.cert_rows);
+    } else {
+        const cudaError_t e = dispatch_e<XT, false, true>(g, x, N, k, ksel, idx, val, s);
+        if (e != cudaSuccess) return e;
+    }
+    const cudaError_t e1 = cudaGetLastError();
+    if (e1 != cudaSuccess) return e1;
+    // the rows the first pass could not certify, with the EXACT arithmetic
+    const size_t esmem = sizeof(float) * (g.Dpad + EPAD);
+    auto ek = gating_exact_rows_kernel<EPAD, XT>;
+    if (esmem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(ek, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(esmem));
+        if (e != cudaSuccess) return e;
+    }
+    const int64_t grid = std::min<int64_t>(N, 2 * static_cast<int64_t>(sm_count(g.device)));
+    ek<<<static_cast<unsigned>(std::max<int64_t>(1, grid)), EPAD < 32 ? 32 : EPAD, esmem, s>>>(
+        static_cast<const XT*>(x), reinterpret_cast<const float4*>(g.wt), g.bias, N,
+        static_cast<int>(g.D), g.Dpad, static_cast<int>(g.E), k, ksel, idx, val, g.cert_rows,
+        g.cert_total);
+    return cudaGetLastError();
+}
+
+template <typename XT>
+cudaError_t launch_cert(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
+                        float* val, bool small, cudaStream_t s) {
+    switch (g.Epad) {
+        case 8: return launch_cert_e<8, XT>(g, x, N, k, ksel, idx, val, small, s);
+        case 16: return launch_cert_e<16, XT>(g, x, N, k, ksel, idx, val, small, s);
+        case 32: return launch_cert_e<32, XT>(g, x, N, k, ksel, idx, val, small, s);
+        case 64: return launch_cert_e<64, XT>(g, x, N, k, ksel, idx, val, small, s);
+        case 128: return launch_cert_e<128, XT>(g, x, N, k, ksel, idx, val, small, s);
+        default: return launch_cert_e<256, XT>(g, x, N, k, ksel, idx, val, small, s);
+    }
+}
+
 }  // namespace
 
 int gate_small_eb(int64_t Epad) { return Epad / 8 > 8 ? static_cast<int>(Epad / 8) : 8; }
 
 // Up to this many tokens the small-batch kernel runs (measured crossover).
 constexpr int64_t kSmallBatchMax = 512;
+// Certified mode: the d-split kernel up to this many tokens and this much
+// shared memory (activation rows of 4 tokens: d up to about 12K).
+constexpr int64_t kCertSmallMax = 512;
+constexpr int64_t kCertSmallSmemMax = 200 * 1024;
 
 int gate_epad(int64_t E) {
     if (E <= 8) return 8;
@@ -726,6 +1128,31 @@ aem_status launch_gating(const Gate& g, const void* x, aem_dtype xd, int64_t N, 
                          aem_gating_mode mode, int32_t* idx, float* val, cudaStream_t s) {
     if (N == 0) return AEM_OK;
     cudaError_t e;
+    if (mode == AEM_GATING_CERTIFIED) {
+        // the uncertified-row list: room for every row, emptied per call
+        if (g.cert_cap < N) {
+            if (g.cert_rows) {
+                cudaDeviceSynchronize();
+                cudaFree(g.cert_rows);
+                g.cert_rows = nullptr;
+                g.cert_cap = 0;
+            }
+            AEM_TRY_CUDA(cudaMalloc(&g.cert_rows, sizeof(int) * (N + 1)));
+            g.cert_cap = N;
+        }
+        AEM_TRY_CUDA(cudaMemsetAsync(g.cert_rows, 0, sizeof(int), s));
+        // few tokens: d split over threads (activation rows in shared memory)
+        const bool small = N <= kCertSmallMax && cert_small_smem(g.Dpad, static_cast<int>(g.Epad)) <=
+                                                     static_cast<size_t>(kCertSmallSmemMax);
+        e = xd == AEM_F32 ? launch_cert<float>(g, x, N, k, ksel, idx, val, small, s)
+                          : launch_cert<__nv_bfloat16>(g, x, N, k, ksel, idx, val, small, s);
+        if (e != cudaSuccess) {
+            set_error("certified gating launch failed: %s", cudaGetErrorString(e));
+            return AEM_ECUDA;
+        }
+        count_launches(2);
+        return AEM_OK;
+    }
     const bool exact = mode == AEM_GATING_EXACT;
     const int xbytes = xd == AEM_F32 ? 4 : 2;
     // the small-batch kernel copies whole 16-byte pieces of activation rows
@@ -833,6 +1260,15 @@ aem_status aem_gate_pack(const float* gate_weight, const float* gate_bias, int64
         }
         aem::block_gate_kernel<<<256, 256>>>(reinterpret_cast<const float4*>(g->wt), g->Dpad / 4,
                                               g->Epad, g->eb, reinterpret_cast<float4*>(g->wblk));
+        if (cudaMalloc(&g->wsq16, sizeof(float) * (g->Dpad / 16) * g->Epad) != cudaSuccess ||
+            cudaMalloc(&g->cert_total, sizeof(unsigned long long)) != cudaSuccess ||
+            cudaMemset(g->cert_total, 0, sizeof(unsigned long long)) != cudaSuccess) {
+            set_error("aem_gate_pack: device allocation failed");
+            st = AEM_ENOMEM;
+            break;
+        }
+        aem::gate_norms_kernel<<<256, 256>>>(reinterpret_cast<const float4*>(g->wt), g->Dpad,
+                                              g->Epad, g->wsq16);
         if (cudaDeviceSynchronize() != cudaSuccess) {
             set_error("aem_gate_pack: pack kernel failed: %s",
                       cudaGetErrorString(cudaGetLastError()));
@@ -846,6 +1282,8 @@ aem_status aem_gate_pack(const float* gate_weight, const float* gate_bias, int64
         cudaFree(g->wt);
         cudaFree(g->bias);
         cudaFree(g->wblk);
+        cudaFree(g->wsq16);
+        cudaFree(g->cert_total);
         delete g;
         return st;
     }
@@ -860,7 +1298,21 @@ aem_status aem_gate_free(aem_gate_t gate) {
     cudaFree(g->wt);
     cudaFree(g->bias);
     cudaFree(g->wblk);
+    cudaFree(g->wsq16);
+    cudaFree(g->cert_rows);
+    cudaFree(g->cert_total);
     delete g;
+    return AEM_OK;
+}
+
+aem_status aem_gate_fallback_rows(aem_gate_t gate, int64_t* rows) {
+    AEM_REQUIRE(gate != nullptr && rows != nullptr, "aem_gate_fallback_rows: NULL argument");
+    auto* g = reinterpret_cast<aem::Gate*>(gate);
+    AEM_TRY_CUDA(cudaSetDevice(g->device));
+    AEM_TRY_CUDA(cudaDeviceSynchronize());
+    unsigned long long v = 0;
+    AEM_TRY_CUDA(cudaMemcpy(&v, g->cert_total, sizeof(v), cudaMemcpyDeviceToHost));
+    *rows = static_cast<int64_t>(v);
     return AEM_OK;
 }
 

@@ -287,6 +287,12 @@ aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaSt
                            bool split_x, bool split_h) {
     const int k = cfg.top_k, E = cfg.num_experts;
     const int64_t d = cfg.d_model, f = cfg.d_ffn;
+    // Decode steps (few units): the up projection splits K over the SMs, which
+    // its ReLU / bf16 epilogue would forbid, by summing float32 partial
+    // products into h32; the down projection's weight-stream kernel applies
+    // ReLU and the bf16 rounding (pair) of H as it stages those rows.
+    const bool decode = U <= gemv_max_rows();
+    if (decode && !h32) AEM_TRY_CUDA(cudaMalloc(&h32, sizeof(float) * gemv_max_rows() * f));
     GemmArgs up_a;
     up_a.w = up;
     up_a.group_base = 0;
@@ -301,7 +307,15 @@ aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaSt
     up_a.out_bf16 = true;
     up_a.ldo = f;
     up_a.relu = true;
+    if (decode) {
+        up_a.out = h32;
+        up_a.out_lo = nullptr;
+        up_a.out_bf16 = false;
+        up_a.relu = false;
+        up_a.atomic_add = true;
+    }
     prof.begin(AEM_PHASE_UP, s);
+    if (decode) AEM_TRY_CUDA(cudaMemsetAsync(h32, 0, sizeof(float) * U * f, s));
     AEM_TRY(launch_qgemm(up_a, s));
     prof.end(AEM_PHASE_UP, s);
 
@@ -322,6 +336,12 @@ aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaSt
     dn.rowmap = src_token;
     dn.rowscale = rowscale;
     dn.atomic_add = true;
+    if (decode) {
+        dn.x_hi = nullptr;
+        dn.x_lo = nullptr;
+        dn.x_f32_relu = h32;
+        dn.x_f32_lo = split_h;
+    }
     // Few tiles per SM (decode sizes): stream-K, every SM streams the same
     // number of weight tiles (the output rows start at zero and take red.add).
     const int64_t groups_used = std::min<int64_t>(E, U);
@@ -367,7 +387,8 @@ aem_status aem_moe_create(const aem_moe_config* cfg, aem_gate_t gate, aem_qweigh
                 "aem_moe_create: up weight shape mismatch");
     AEM_REQUIRE(dn->G == cfg->num_experts && dn->K == cfg->d_ffn && dn->N == cfg->d_model,
                 "aem_moe_create: down weight shape mismatch");
-    AEM_REQUIRE(cfg->gating_mode == AEM_GATING_EXACT || cfg->gating_mode == AEM_GATING_FAST,
+    AEM_REQUIRE(cfg->gating_mode == AEM_GATING_EXACT || cfg->gating_mode == AEM_GATING_FAST ||
+                    cfg->gating_mode == AEM_GATING_CERTIFIED,
                 "aem_moe_create: bad gating mode");
     auto* m = new aem::Moe();
     m->cfg = *cfg;
@@ -385,6 +406,7 @@ aem_status aem_moe_free(aem_moe_t moe) {
     cudaDeviceSynchronize();
     cudaFree(m->buf);
     cudaFree(m->split_buf);
+    cudaFree(m->h32);
     aem::seam_free(m);
     delete m;
     return AEM_OK;

@@ -41,6 +41,9 @@ struct Moe {
     int64_t split_cap = 0;
     void* xperm_lo = nullptr;  // bf16 [U, d]
     void* h_lo = nullptr;      // bf16 [U, ffn]
+    // decode steps (at most gemv_max_rows() units): the up projection's
+    // float32 pre-activations [U, ffn], summed over K ranges
+    float* h32 = nullptr;
     PhaseProfiler prof;
     // scheduler seam (seam.cu): staged rows of one iteration and its slice table
     struct SeamStage* seam = nullptr;

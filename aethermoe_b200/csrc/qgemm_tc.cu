@@ -45,7 +45,6 @@ namespace aem {
 aem_status launch_qgemm_simt(const GemmArgs& a, cudaStream_t s);
 aem_status launch_qgemm_decode(const GemmArgs& a, cudaStream_t s);
 aem_status launch_qgemm_gemv(const GemmArgs& a, cudaStream_t s);
-int gemv_max_rows();
 
 namespace {
 
@@ -1269,8 +1268,15 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
                 "qgemm: weight group out of range");
     AEM_REQUIRE(!(a.atomic_add && a.out_bf16), "qgemm: split-K needs float32 output");
     if (a.M == 0) return AEM_OK;
+    if (a.x_f32_relu) {
+        AEM_REQUIRE(a.M <= gemv_max_rows(), "qgemm: float32 pre-activation input takes at most %d rows",
+                    gemv_max_rows());
+        return launch_qgemm_gemv(a, s);
+    }
     const int tmode = gemm_tmem_a_mode();
-    // few rows (so few per group): the bandwidth-bound weight stream
+    // one row: the CUDA-core decode kernel (measured 5% ahead of the weight
+    // stream there); few rows (so few per group): the weight stream on warp MMAs
+    if (a.M == 1 && a.token_tile == 0 && tmode != 1) return launch_qgemm_decode(a, s);
     if (a.M <= gemv_max_rows() && a.token_tile == 0 && tmode != 1) return launch_qgemm_gemv(a, s);
     if (w.K % 8 != 0) return launch_qgemm_simt(a, s);
     AEM_REQUIRE(a.M < (1ll << 31) && w.G * w.N < (1ll << 31), "qgemm: too many rows");

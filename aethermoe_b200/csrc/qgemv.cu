@@ -83,6 +83,8 @@ __device__ __forceinline__ uint4 ld_stream16(const int8_t* p) {
 struct GvParams {
     const __nv_bfloat16* xh;  // [M][K]
     const __nv_bfloat16* xl;  // [M][K] or nullptr (float32 activations split hi + lo)
+    const float* xf;          // [M][K] float32 pre-activations (instead of xh / xl) or nullptr
+    int has_lo;               // a lo plane: xl given, or xf staged as a pair
     const int8_t* wq;         // tiled int8 weights
     const float* scale;
     int64_t M, K, N, NT, KT;
@@ -162,9 +164,29 @@ __global__ void __launch_bounds__(kGvThreads)
             const int64_t k = kbase + c8 * 8;
             if (row < m) {
                 const int64_t o = static_cast<int64_t>(r0 + row) * p.K + k;
-                const bool vec = k + 8 <= p.K && (reinterpret_cast<uintptr_t>(p.xh + o) & 15) == 0 &&
-                                 (!p.xl || (reinterpret_cast<uintptr_t>(p.xl + o) & 15) == 0);
-                if (vec) {
+                if (p.xf) {
+                    // float32 pre-activation: ReLU, then bf16 (and the pair's low half)
+                    __nv_bfloat16 h[8], l[8];
+                    const bool fv = k + 8 <= p.K && (reinterpret_cast<uintptr_t>(p.xf + o) & 15) == 0;
+                    float f[8];
+                    if (fv) {
+                        const float4 f0 = *reinterpret_cast<const float4*>(p.xf + o);
+                        const float4 f1 = *reinterpret_cast<const float4*>(p.xf + o + 4);
+                        f[0] = f0.x; f[1] = f0.y; f[2] = f0.z; f[3] = f0.w;
+                        f[4] = f1.x; f[5] = f1.y; f[6] = f1.z; f[7] = f1.w;
+                    } else {
+                        for (int e = 0; e < 8; ++e) f[e] = k + e < p.K ? p.xf[o + e] : 0.0f;
+                    }
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float v = fmaxf(f[e], 0.0f);
+                        h[e] = __float2bfloat16_rn(v);
+                        l[e] = __float2bfloat16_rn(v - __bfloat162float(h[e]));
+                    }
+                    hv = *reinterpret_cast<uint4*>(h);
+                    lv = *reinterpret_cast<uint4*>(l);
+                } else if (k + 8 <= p.K && (reinterpret_cast<uintptr_t>(p.xh + o) & 15) == 0 &&
+                           (!p.xl || (reinterpret_cast<uintptr_t>(p.xl + o) & 15) == 0)) {
                     hv = *reinterpret_cast<const uint4*>(p.xh + o);
                     if (p.xl) lv = *reinterpret_cast<const uint4*>(p.xl + o);
                 } else {
@@ -179,7 +201,7 @@ __global__ void __launch_bounds__(kGvThreads)
                 }
             }
             *reinterpret_cast<uint4*>(xs + row * XS + c8 * 16) = hv;
-            if (p.xl) *reinterpret_cast<uint4*>(xls + row * XS + c8 * 16) = lv;
+            if (p.has_lo) *reinterpret_cast<uint4*>(xls + row * XS + c8 * 16) = lv;
         }
         __syncthreads();
 
@@ -216,7 +238,7 @@ __global__ void __launch_bounds__(kGvThreads)
                     mma_bf16_16816(acc[1][n], a[2][j].x, a[3][j].x, a[2][j].y, a[3][j].y,
                                    bw[2 * j], bw[2 * j + 1]);
                 }
-                if (p.xl) {
+                if (p.has_lo) {
                     const unsigned char* xq = xls + (n * 8 + gq) * XS + kk * 2;
                     const uint4 l01 = *reinterpret_cast<const uint4*>(xq);
                     const uint4 l23 = *reinterpret_cast<const uint4*>(xq + 16);
@@ -277,7 +299,7 @@ __global__ void __launch_bounds__(kGvThreads)
 template <int NT8>
 aem_status launch_gv(const GvParams& p, int64_t groups, cudaStream_t s) {
     constexpr int SUB = 16;
-    const size_t smem = static_cast<size_t>((p.xl ? 2 : 1) * NT8 * 8) * (SUB * 64 * 2 + 16);
+    const size_t smem = static_cast<size_t>((p.has_lo ? 2 : 1) * NT8 * 8) * (SUB * 64 * 2 + 16);
     auto kern = qgemv_kernel<NT8>;
     if (smem > 48 * 1024)
         AEM_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -324,7 +346,9 @@ aem_status launch_qgemm_gemv(const GemmArgs& a, cudaStream_t s) {
                                        static_cast<size_t>(w.N) * 4, static_cast<size_t>(a.M), s));
     GvParams p;
     p.xh = static_cast<const __nv_bfloat16*>(a.x_hi);
-    p.xl = static_cast<const __nv_bfloat16*>(a.x_lo);
+    p.xl = a.x_f32_relu ? nullptr : static_cast<const __nv_bfloat16*>(a.x_lo);
+    p.xf = a.x_f32_relu;
+    p.has_lo = (a.x_f32_relu ? a.x_f32_lo : a.x_lo != nullptr) ? 1 : 0;
     p.wq = w.q;
     p.scale = w.scale;
     p.M = a.M;

@@ -115,9 +115,8 @@ __global__ void qgemm_simt_kernel(const __nv_bfloat16* __restrict__ xh,
 }
 
 // Decode-size INT8 GEMM on the CUDA cores (at most MAXM <= 4 rows per weight
-// group).  At these sizes the tensor-core kernel's per-K-step issue loop, not
-// the weight stream, sets the time; here every SM streams weights at memory
-// speed.  One CTA of 128 threads per (row group, 128-channel block, K range).
+// group; dispatched for single-row calls, where it measured ahead of the
+// warp-MMA weight stream).  One CTA of 128 threads per (row group, 128-channel block, K range).
 // Thread t owns the 16-byte chunk at position t % 4 (16 consecutive K) of
 // channel rows t/4 + 32j (j < 4) of every 8 KB weight tile, so each warp load
 // reads 512 contiguous bytes and the chunk's 16 activations serve four rows.  int8 ->

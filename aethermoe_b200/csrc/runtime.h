@@ -97,6 +97,14 @@ struct Gate {
     // [b*eb, (b+1)*eb), and one chunk of d of one block is contiguous.
     float* wblk = nullptr;
     int eb = 0;
+    // Certified mode: squared norms of the weights per 16-wide block of d,
+    // [Dpad/16][Epad] (the error bound of the fast logits), and the rows of a
+    // call whose selection was not certified (cert_rows[0] = count, then the
+    // row ids; room for cert_cap rows) with the running total of such rows.
+    float* wsq16 = nullptr;
+    mutable int* cert_rows = nullptr;
+    mutable int64_t cert_cap = 0;
+    unsigned long long* cert_total = nullptr;
 };
 int gate_epad(int64_t E);
 int gate_small_eb(int64_t Epad);  // experts per CTA of the small-batch kernel
@@ -145,6 +153,11 @@ struct GemmArgs {
     int64_t max_rows = 0;      // upper bound of sum_g ceil(rows_g / BT) * BT (grid sizing)
     const void* x_hi = nullptr;  // bf16 [M, K]
     const void* x_lo = nullptr;  // bf16 [M, K] or nullptr (split float32 activations)
+    // weight-stream kernel only (at most gemv_max_rows() rows): float32 [M, K]
+    // pre-activations instead of x_hi / x_lo, taken as bf16(relu(v)) -- and
+    // with x_f32_lo the pair hi + lo, lo = bf16(relu(v) - hi) -- as they are staged
+    const float* x_f32_relu = nullptr;
+    bool x_f32_lo = false;
     void* out = nullptr;
     bool out_bf16 = false;
     // bf16 output only: when set, the output is written as a bf16 pair,
@@ -166,6 +179,7 @@ struct GemmArgs {
                                // device (0 = use M); only picks the token tile
 };
 aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s);
+int gemv_max_rows();  // rows up to which launch_qgemm takes the weight-stream kernel
 int gemm_pair_mode();  // aem_set_gemm_pairs: -1 automatic, 0 never, 1 from 64-row tiles
 
 // float32 [M, K] -> bf16 hi [M, K] + bf16 lo [M, K] (lo may be nullptr), or

@@ -161,8 +161,10 @@ def exchange_compare(layer, x_local, world, rank, tl, dev, stream, place, phases
 
 
 def ep_parity(layer, x_local, world, rank, tokens, dev, stream, gw, gb, cap):
-    """Checks one expert-parallel step against the single-GPU layer run on
-    the GLOBAL batch (before the timed region).
+    """Checks one step of the timed layer -- expert parallel for N>1, the
+    single-GPU layer in the bench's gating mode for N=1 -- against the
+    single-GPU layer with EXACT gating run on the GLOBAL batch (before the
+    timed region).
 
     Every rank runs one step on its slice of input buffer 0; the routing
     (gating ids and the effective expert of every (token, slot) unit) and
@@ -182,12 +184,15 @@ def ep_parity(layer, x_local, world, rank, tokens, dev, stream, gw, gb, cap):
     layer.forward(x_local, out=out, stream=stream)
     idx, _, eff = layer.last_routing(tl, stream=stream)
     torch.cuda.synchronize()
-    g_idx = torch.empty((world,) + tuple(idx.shape), dtype=idx.dtype, device=dev)
-    g_eff = torch.empty((world,) + tuple(eff.shape), dtype=eff.dtype, device=dev)
-    g_out = torch.empty((world, tl, D_MODEL), dtype=torch.float32, device=dev)
-    dist.all_gather_into_tensor(g_idx, idx.contiguous())
-    dist.all_gather_into_tensor(g_eff, eff.contiguous())
-    dist.all_gather_into_tensor(g_out, out)
+    if world == 1:
+        g_idx, g_eff, g_out = idx[None].clone(), eff[None].clone(), out[None].clone()
+    else:
+        g_idx = torch.empty((world,) + tuple(idx.shape), dtype=idx.dtype, device=dev)
+        g_eff = torch.empty((world,) + tuple(eff.shape), dtype=eff.dtype, device=dev)
+        g_out = torch.empty((world, tl, D_MODEL), dtype=torch.float32, device=dev)
+        dist.all_gather_into_tensor(g_idx, idx.contiguous())
+        dist.all_gather_into_tensor(g_eff, eff.contiguous())
+        dist.all_gather_into_tensor(g_out, out)
     torch.cuda.synchronize()
     res = None
     if rank == 0:
@@ -211,12 +216,13 @@ def ep_parity(layer, x_local, world, rank, tokens, dev, stream, gw, gb, cap):
                "rows_checked": tokens, "max_abs_diff": float((got - r).abs().max().item()),
                "max_excess_over_tol": float(excess), "rows_within_tol": bool(excess <= 0),
                "tolerance": "1e-3 + 1e-3*|ref|",
-               "reference": (f"single-GPU layer (aem_moe_forward, all {E} experts) on the "
-                             f"global batch of {tokens} tokens, input buffer 0")}
+               "reference": (f"single-GPU layer (aem_moe_forward, all {E} experts, EXACT gating) "
+                             f"on the global batch of {tokens} tokens, input buffer 0")}
         one.close()
         del up, down, x, ref
         torch.cuda.empty_cache()
-    dist.barrier()
+    if world > 1:
+        dist.barrier()
     return res
 
 
@@ -461,15 +467,17 @@ def run_ours(args):
     # the hot low-id experts spreads over all ranks
     up, down, qlists = expert_weights(range(rank, E, world), dev)
     torch.cuda.synchronize()
+    gmode = _lib.GATING_CERTIFIED if args.gating == "certified" else _lib.GATING_EXACT
     if world == 1:
-        layer = MoELayer(gw, gb, up, None, down, None, K_TOP, capacity=cap, device=local)
+        layer = MoELayer(gw, gb, up, None, down, None, K_TOP, capacity=cap, device=local,
+                         gating_mode=gmode)
     else:
         uid = torch.zeros(128, dtype=torch.uint8, device=dev)
         if rank == 0:
             uid.copy_(torch.frombuffer(bytearray(ep_unique_id()), dtype=torch.uint8))
         dist.broadcast(uid, 0)
         layer = EPLayer(bytes(uid.cpu().numpy()), rank, world, gw, gb, up, None, down, None,
-                        K_TOP, capacity=cap, device=local, max_tokens=tl,
+                        K_TOP, capacity=cap, gating_mode=gmode, device=local, max_tokens=tl,
                         expert_to_rank=[e % world for e in range(E)])
         if args.ep_pipeline != "auto":
             layer.set_pipeline(1 if args.ep_pipeline == "on" else 0)
@@ -477,7 +485,7 @@ def run_ours(args):
     outs = [torch.empty((tl, D_MODEL), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     stream = torch.cuda.current_stream()
     parity = None
-    if world > 1 and not args.no_parity:
+    if not args.no_parity:
         parity = ep_parity(layer, xs[0], world, rank, tokens, dev, stream, gw, gb, cap)
 
     def barrier():
@@ -561,6 +569,10 @@ def run_ours(args):
                        "expert_placement": "round-robin (expert e on rank e % R)",
                        "ep_pipeline": (args.ep_pipeline if world > 1 else None),
                        "gemm_pairs": args.gemm_pairs,
+                       "gating": (("certified: fast logits with a rigorous error bound, rows it "
+                                   "cannot order recomputed in exact sequential float32; indices "
+                                   "bit-identical to exact") if args.gating == "certified"
+                                  else "exact: sequential float32, bit-identical logits"),
                        "l2": (f"inputs rotate over {N_INPUT_BUFFERS} buffers "
                               f"({N_INPUT_BUFFERS * tokens * D_MODEL * 2 >> 20} MiB > 126 MiB L2); "
                               "per-step working set > 1 GiB")},
@@ -682,7 +694,9 @@ def run_suite(args):
     Mixtral-shaped MoE layer: d=4096, ffn=14336, E=8, top-2, no capacity
     limit, T in {1,32,512,4096}, x bf16.  Every call is timed alone with CUDA
     events on its stream after a 256 MiB write that flushes L2; the median of
-    the timed calls is reported.  Roofline: bytes and flops are the
+    the timed calls is reported.  The decode GEMMs (M in {1,8,16,64}, bf16)
+    are also timed back to back: 40 calls over 8 weight copies (470 MB > L2)
+    replayed from one CUDA graph, time per call.  Roofline: bytes and flops are the
     algorithmic figures (unique bytes, 2*M*N*K flops); peaks are the measured
     HBM copy bandwidth and burst bf16 GEMM rate, and for exact gating the
     nominal float32 CUDA-core rate (148 SMs x 128 lanes x 1.965 GHz).
@@ -769,6 +783,46 @@ def run_suite(args):
                  "hbm" if m <= 64 else "tensor")
             del xs, out
     del wq
+    # ---- C2 back to back: 40 calls over 8 weight copies (470 MB > L2) in one
+    # CUDA graph, so every call streams cold weights but no host launch gap
+    # separates them (the decode-serving pattern: consecutive layers)
+    wqs = []
+    for i in range(8):
+        q = torch.randint(-127, 128, (1, K, N), dtype=torch.int8, device=dev)
+        wqs.append(_lib.DeviceQWeight(q, torch.full((1, N), 2.5e-4, device=dev)))
+        del q
+    gs = torch.cuda.Stream()
+    for m in (1, 8, 16, 64):
+        x = torch.randn(m, K, device=dev).to(torch.bfloat16)
+        out = torch.empty((m, N), dtype=torch.float32, device=dev)
+
+        def call(i):
+            _lib.check(L.aem_qgemm(wqs[i % 8].handle, 0, x.data_ptr(), _lib.BF16, m,
+                                   out.data_ptr(), gs.cuda_stream), "aem_qgemm")
+        with torch.cuda.stream(gs):
+            for i in range(8):
+                call(i)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=gs):
+            for i in range(40):
+                call(i)
+        per = []
+        for r in range(4):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(gs):
+                a.record()
+                graph.replay()
+                b.record()
+            torch.cuda.synchronize()
+            per.append(a.elapsed_time(b) * 1e-3 / 40)
+        _lib.check(L.aem_device_status(None), "aem_device_status")
+        sec = min(per[1:])
+        emit("C2 int8 gemm back-to-back", {"M": m, "K": K, "N": N, "x": "bfloat16",
+                                           "calls": "40 in one CUDA graph over 8 weight copies"},
+             sec, K * N + 4 * N + m * K * 2 + 4 * m * N, 2 * m * N * K, "hbm")
+        del graph, x, out
+    del wqs
     # ---- C3: Mixtral-shaped single-GPU MoE layer
     d, f, e, k = 4096, 14336, 8, 2
     qu = torch.randint(-127, 128, (e, d, f), dtype=torch.int8, device=dev)
@@ -811,7 +865,11 @@ def main():
     ap.add_argument("--exchange-compare", action="store_true",
                     help="N>1: also time the step's token exchange through NCCL all-to-all")
     ap.add_argument("--no-parity", action="store_true",
-                    help="N>1: skip the check of one step against the single-GPU layer")
+                    help="skip the check of one step against the single-GPU EXACT-gating layer")
+    ap.add_argument("--gating", choices=["certified", "exact"], default="certified",
+                    help="gating arithmetic of the timed layer: certified (fast logits with a "
+                         "rigorous bound, uncertain rows recomputed exactly: indices "
+                         "bit-identical to exact) or exact (sequential float32)")
     ap.add_argument("--ep-pipeline", choices=["auto", "on", "off"], default="auto",
                     help="expert-parallel two-half pipeline (auto: off)")
     ap.add_argument("--suite", action="store_true",

@@ -48,8 +48,23 @@ typedef enum { AEM_F32 = 0, AEM_BF16 = 1 } aem_dtype;
  *   indices match it bit-exactly on every row.
  * FAST: fused multiply-adds (one rounding per term) in the same order;
  *   indices match on every row whose k-th/(k+1)-th logit gap exceeds
- *   float32 rounding. */
-typedef enum { AEM_GATING_EXACT = 0, AEM_GATING_FAST = 1 } aem_gating_mode;
+ *   float32 rounding.
+ * CERTIFIED: indices bit-identical to EXACT on every row, at FAST speed or
+ *   better: logits are computed with fused multiply-adds (for small batches
+ *   with d split over threads) beside a rigorous bound on their distance
+ *   from the EXACT logits (per 64-wide block of d: the partial sums'
+ *   magnitudes and Cauchy-Schwarz bounds of sum |x w|); a row whose selected
+ *   experts' bound intervals are ordered and clear of every other expert's
+ *   is certified and written from the fast logits (values within float32
+ *   rounding of EXACT's); every other row -- near ties, NaN, +-inf -- is
+ *   recomputed with the EXACT arithmetic (written exactly as EXACT writes it)
+ *   on the device, without a host round trip.  aem_gate_fallback_rows counts
+ *   the recomputed rows. */
+typedef enum {
+    AEM_GATING_EXACT = 0,
+    AEM_GATING_FAST = 1,
+    AEM_GATING_CERTIFIED = 2
+} aem_gating_mode;
 
 #define AEM_MAX_EXPERTS 256 /* fused_gating_metal.py:230 MAX_EXPERTS */
 #define AEM_MAX_TOPK 64     /* fused_gating_metal.py:231 MAX_TOPK */
@@ -107,6 +122,10 @@ typedef struct aem_gate_s* aem_gate_t;
 aem_status aem_gate_pack(const float* gate_weight, const float* gate_bias, int64_t D, int64_t E,
                          int device, aem_gate_t* out);
 aem_status aem_gate_free(aem_gate_t gate);
+/* Rows of this gate's CERTIFIED-mode calls that were recomputed with the
+ * EXACT arithmetic (not certified), since the gate was packed; synchronises
+ * the gate's device.  No counterpart in the reference. */
+aem_status aem_gate_fallback_rows(aem_gate_t gate, int64_t* rows);
 
 /* Fused gating: logits = hidden @ gate_weight + gate_bias, top-k by repeated
  * strict-greater max extraction (ties -> lowest expert id), softmax over the
