@@ -251,7 +251,8 @@ __global__ void __launch_bounds__(WARPS * 32)
     gating_kernel(const XT* __restrict__ x, const float4* __restrict__ wpk,
                   const float* __restrict__ bias, int64_t N, int D, int E, int k, int ksel,
                   int32_t* __restrict__ idx_out, float* __restrict__ val_out,
-                  const float* __restrict__ wsq16, int* __restrict__ cert_rows) {
+                  const float* __restrict__ wsq16, int* __restrict__ cert_rows,
+                  const int* __restrict__ rowlist, unsigned long long* __restrict__ rows_total) {
     using C = GatingCfg<GROUP, NSLOT, kTPG, WARPS, XT, DKO>;
     constexpr int kThreads = C::kThreads;
     constexpr int GPW = C::GPW;
@@ -282,6 +283,20 @@ __global__ void __launch_bounds__(WARPS * 32)
     const int le = lane % GROUP;
     const int64_t tok0 = static_cast<int64_t>(blockIdx.x) * TOK;
     const int tbase = (warp * GPW + grp) * kTPG;  // first local token of this lane group
+    // With a row list (rowlist[0] = count, then row ids: the rows a certified
+    // launch deferred) token tl of the grid is row rowlist[1 + tl]; the grid
+    // is sized for every row and the CTAs past the count leave at once.
+    __shared__ int64_t s_row[TOK];
+    if (rowlist) {
+        const int64_t n_eff = min(N, static_cast<int64_t>(rowlist[0]));
+        if (blockIdx.x == 0 && tid == 0 && rows_total && n_eff > 0)
+            atomicAdd(rows_total, static_cast<unsigned long long>(n_eff));
+        if (tok0 >= n_eff) return;  // uniform over the CTA
+        for (int i = tid; i < TOK; i += kThreads)
+            s_row[i] = tok0 + i < n_eff ? static_cast<int64_t>(rowlist[1 + tok0 + i]) : N;
+        __syncthreads();
+    }
+    auto row_of = [&](int tl) -> int64_t { return rowlist ? s_row[tl] : tok0 + tl; };
 
     float2 acc[kTPG / 2][NSLOT];  // (token 2p, token 2p+1) of this lane group
     float2 qb[kTPG / 2][NSLOT];   // CERTIFIED: the bound's sum Q (see certify_row)
@@ -311,7 +326,7 @@ __global__ void __launch_bounds__(WARPS * 32)
                 for (int i = tid; i < XST; i += kThreads) {
                     const int t = i / XCH;
                     const int d = d0 + (i % XCH) * XPC;
-                    const int64_t tg = tok0 + t;
+                    const int64_t tg = row_of(t);
                     const bool in = tg < N && d < D;
                     const XT* src = in ? x + tg * static_cast<int64_t>(D) + d : x;
                     cp_async_16(xdst + i, src, in ? min(16, (D - d) * XB) : 0);
@@ -338,7 +353,7 @@ __global__ void __launch_bounds__(WARPS * 32)
         } else {
             const int d0 = c * DK;
             for (int i = tid; i < TOK * DK; i += kThreads) {
-                const int64_t tg = tok0 + i / DK;
+                const int64_t tg = row_of(i / DK);
                 const int d = d0 + i % DK;
                 xs[xpos(i)] =
                     (tg < N && d < D) ? load_x<XT>(x + tg * static_cast<int64_t>(D) + d) : 0.0f;
@@ -440,7 +455,7 @@ __global__ void __launch_bounds__(WARPS * 32)
 #pragma unroll
     for (int i = 0; i < kTPG; ++i) {
         const int tl = tbase + i;
-        const int64_t tg = tok0 + tl;
+        const int64_t tg = row_of(tl);
         float v[NSLOT];
 #pragma unroll
         for (int s = 0; s < NSLOT; ++s) {
@@ -778,7 +793,7 @@ __host__ __device__ constexpr size_t cert_small_smem(int64_t Dpad, int EPAD) {
 template <int EPAD, typename XT>
 __global__ void __launch_bounds__(kCertThreads)
     gating_cert_small_kernel(const XT* __restrict__ x, const float4* __restrict__ wpk,
-                             const float* __restrict__ bias, const float* __restrict__ wsq16,
+                             const float* __restrict__ bias, const float* __restrict__ wn64,
                              int64_t N, int D, int64_t Dpad, int E, int k, int ksel,
                              int32_t* __restrict__ idx_out, float* __restrict__ val_out,
                              int* __restrict__ cert_rows) {
@@ -794,20 +809,57 @@ __global__ void __launch_bounds__(kCertThreads)
     const int tid = threadIdx.x;
     const int64_t tok0 = static_cast<int64_t>(blockIdx.x) * TT;
     const int nblk = static_cast<int>(Dpad / 64);
-    // activation rows as float32, zero past D and past N
-    for (int64_t i = tid; i < TT * Dpad; i += kCertThreads) {
-        const int t = static_cast<int>(i / Dpad);
-        const int64_t d = i - static_cast<int64_t>(t) * Dpad;
-        xs[i] = (tok0 + t < N && d < D) ? load_x<XT>(x + (tok0 + t) * static_cast<int64_t>(D) + d)
-                                        : 0.0f;
+    // activation rows as float32, zero past D and past N (16-byte loads when
+    // the rows allow them)
+    constexpr int VEC = 16 / static_cast<int>(sizeof(XT));
+    const bool vec = (static_cast<int64_t>(D) * static_cast<int>(sizeof(XT))) % 16 == 0 &&
+                     (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    const int dp = static_cast<int>(Dpad);
+#pragma unroll 1
+    for (int t = 0; t < TT; ++t) {
+        float* dst = xs + t * dp;
+        if (tok0 + t >= N) {
+            for (int d = tid; d < dp; d += kCertThreads) dst[d] = 0.0f;
+            continue;
+        }
+        const XT* row = x + (tok0 + t) * static_cast<int64_t>(D);
+        const int d0 = vec ? D / VEC * VEC : 0;
+        for (int d = d0 + tid; d < dp; d += kCertThreads)
+            dst[d] = d < D ? load_x<XT>(row + d) : 0.0f;
+    }
+    if (vec) {
+        // the 16-byte pieces of all the CTA's rows in flight together
+        for (int j = tid; j < D / VEC; j += kCertThreads) {
+            uint4 v[TT];
+#pragma unroll
+            for (int t = 0; t < TT; ++t)
+                v[t] = tok0 + t < N ? *reinterpret_cast<const uint4*>(
+                                          x + (tok0 + t) * static_cast<int64_t>(D) + j * VEC)
+                                    : make_uint4(0, 0, 0, 0);
+            asm volatile("" ::: "memory");
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+                const XT* e8 = reinterpret_cast<const XT*>(&v[t]);
+#pragma unroll
+                for (int q = 0; q < VEC; q += 4)
+                    *reinterpret_cast<float4*>(xs + t * dp + j * VEC + q) =
+                        make_float4(load_x<XT>(e8 + q), load_x<XT>(e8 + q + 1),
+                                    load_x<XT>(e8 + q + 2), load_x<XT>(e8 + q + 3));
+            }
+        }
     }
     __syncthreads();
-    for (int i = tid; i < TT * nblk; i += kCertThreads) {
-        const float* v = xs + static_cast<int64_t>(i / nblk) * Dpad + static_cast<int64_t>(i % nblk) * 64;
-        float ss = 0.0f;
-#pragma unroll 8
-        for (int j = 0; j < 64; ++j) ss = fmaf(v[j], v[j], ss);
-        xnb[i] = sqrtf(ss);
+    {
+        // a warp per block: two elements per lane, then a shuffle sum
+        const int w = tid >> 5, ln = tid & 31;
+        for (int i = w; i < TT * nblk; i += kCertThreads / 32) {
+            const float* v = xs + (i / nblk) * dp + (i % nblk) * 64;
+            float ss = v[ln] * v[ln];
+            ss = fmaf(v[ln + 32], v[ln + 32], ss);
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
+            if (ln == 0) xnb[i] = sqrtf(ss);
+        }
     }
     __syncthreads();
     // ---- part p of d for expert e, all TT tokens
@@ -821,24 +873,40 @@ __global__ void __launch_bounds__(kCertThreads)
         acc[t] = 0.0f;
         q[t] = 0.0f;
     }
-    for (int b = b0; b < b1; ++b) {
-#pragma unroll 4
-        for (int d4 = b * 16; d4 < b * 16 + 16; ++d4) {
-            const float4 w = __ldg(wpk + static_cast<int64_t>(d4) * EPAD + e);
+    // two blocks per round: their 32 weight vectors and 2 norms in flight
+    // together (the barrier keeps the compiler from moving loads to their uses)
+    for (int b = b0; b < b1; b += 2) {
+        const bool two = b + 1 < b1;
+        float4 wv[32];
 #pragma unroll
-            for (int t = 0; t < TT; ++t) {
-                const float4 xv = *reinterpret_cast<const float4*>(xs + t * Dpad + 4 * d4);
-                acc[t] = fmaf(xv.x, w.x, acc[t]);
-                acc[t] = fmaf(xv.y, w.y, acc[t]);
-                acc[t] = fmaf(xv.z, w.z, acc[t]);
-                acc[t] = fmaf(xv.w, w.w, acc[t]);
+        for (int j = 0; j < 16; ++j) wv[j] = __ldg(wpk + static_cast<int64_t>(b * 16 + j) * EPAD + e);
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            wv[16 + j] = two ? __ldg(wpk + static_cast<int64_t>((b + 1) * 16 + j) * EPAD + e)
+                             : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const float wn0 = __ldg(wn64 + static_cast<int64_t>(b) * EPAD + e);
+        const float wn1 = two ? __ldg(wn64 + static_cast<int64_t>(b + 1) * EPAD + e) : 0.0f;
+        asm volatile("" ::: "memory");
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            if (h == 1 && !two) break;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int d4 = (b + h) * 16 + j;
+#pragma unroll
+                for (int t = 0; t < TT; ++t) {
+                    const float4 xv = *reinterpret_cast<const float4*>(xs + t * dp + 4 * d4);
+                    acc[t] = fmaf(xv.x, wv[16 * h + j].x, acc[t]);
+                    acc[t] = fmaf(xv.y, wv[16 * h + j].y, acc[t]);
+                    acc[t] = fmaf(xv.z, wv[16 * h + j].z, acc[t]);
+                    acc[t] = fmaf(xv.w, wv[16 * h + j].w, acc[t]);
+                }
             }
-        }
-        const float* ws = wsq16 + static_cast<int64_t>(b) * 4 * EPAD + e;
-        const float wn = sqrtf(__ldg(ws) + __ldg(ws + EPAD) + __ldg(ws + 2 * EPAD) + __ldg(ws + 3 * EPAD));
+            const float wn = h ? wn1 : wn0;
 #pragma unroll
-        for (int t = 0; t < TT; ++t)
-            q[t] += 64.0f * fabsf(acc[t]) + 65.0f * xnb[t * nblk + b] * wn;
+            for (int t = 0; t < TT; ++t)
+                q[t] += 64.0f * fabsf(acc[t]) + 65.0f * xnb[t * nblk + b + h] * wn;
+        }
     }
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
@@ -885,62 +953,10 @@ __global__ void __launch_bounds__(kCertThreads)
     }
 }
 
-// EXACT recomputation of the rows a certified launch deferred (rows[0] of
-// them at rows[1..]): float32 products summed in increasing d order, bias
-// last, the same selection -- what the EXACT kernels write for those rows.
-// Persistent CTAs over the list; a thread per expert walks all of d (a
-// sequential chain: these are rare rows), the weights from the packed
-// layout, the activation row from shared memory.
-template <int EPAD, typename XT>
-__global__ void __launch_bounds__(EPAD < 32 ? 32 : EPAD)
-    gating_exact_rows_kernel(const XT* __restrict__ x, const float4* __restrict__ wpk,
-                             const float* __restrict__ bias, int64_t N, int D, int64_t Dpad, int E,
-                             int k, int ksel, int32_t* __restrict__ idx_out,
-                             float* __restrict__ val_out, const int* __restrict__ rows,
-                             unsigned long long* __restrict__ total) {
-    constexpr int NT = EPAD < 32 ? 32 : EPAD;
-    constexpr int GROUP = EPAD < 32 ? EPAD : 32;
-    constexpr int NSLOT = EPAD / GROUP;
-    extern __shared__ __align__(16) float esm[];
-    float* xr = esm;          // [Dpad]
-    float* lg = esm + Dpad;   // [EPAD]
-    const int count = rows[0];
-    if (blockIdx.x == 0 && threadIdx.x == 0 && count > 0)
-        atomicAdd(total, static_cast<unsigned long long>(count));
-    const int tid = threadIdx.x;
-    for (int r = blockIdx.x; r < count; r += gridDim.x) {
-        const int64_t tg = rows[1 + r];
-        __syncthreads();  // the previous row's shared data is consumed
-        for (int64_t d = tid; d < Dpad; d += NT)
-            xr[d] = (tg < N && d < D) ? load_x<XT>(x + tg * static_cast<int64_t>(D) + d) : 0.0f;
-        __syncthreads();
-        if (tid < EPAD) {
-            float a = 0.0f;
-            for (int d4 = 0; d4 < (D + 3) / 4; ++d4) {
-                const float4 w = __ldg(wpk + static_cast<int64_t>(d4) * EPAD + tid);
-                const float4 xv = *reinterpret_cast<const float4*>(xr + 4 * d4);
-                a = __fadd_rn(a, __fmul_rn(xv.x, w.x));
-                a = __fadd_rn(a, __fmul_rn(xv.y, w.y));
-                a = __fadd_rn(a, __fmul_rn(xv.z, w.z));
-                a = __fadd_rn(a, __fmul_rn(xv.w, w.w));
-            }
-            lg[tid] = tid < E ? __fadd_rn(a, __ldg(bias + tid)) : -FLT_MAX;
-        }
-        __syncthreads();
-        if (tid < GROUP) {
-            const unsigned gmask = GROUP == 32 ? 0xFFFFFFFFu : ((1u << GROUP) - 1u);
-            float v[NSLOT];
-#pragma unroll
-            for (int s2 = 0; s2 < NSLOT; ++s2) v[s2] = lg[tid + GROUP * s2];
-            topk_select<GROUP, NSLOT>(v, tid, gmask, tg, N, E, k, ksel, idx_out, val_out);
-        }
-    }
-}
-
 // Squared norms of the packed weights per 16-wide block of d: out[b][e] =
 // sum over d in [16b, 16b+16) of w[d][e]^2, [Dpad/16][Epad].
 __global__ void gate_norms_kernel(const float4* __restrict__ wpk, int64_t Dpad, int64_t Epad,
-                                  float* __restrict__ out) {
+                                  float* __restrict__ out, float* __restrict__ out64) {
     const int64_t total = (Dpad / 16) * Epad;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -954,6 +970,21 @@ __global__ void gate_norms_kernel(const float4* __restrict__ wpk, int64_t Dpad, 
             ss = fmaf(w.w, w.w, ss);
         }
         out[i] = ss;
+    }
+    // norms per 64-wide block: out64[c][e] = sqrt(sum of the four 16-blocks)
+    const int64_t total64 = (Dpad / 64) * Epad;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total64;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t c = i / Epad, e = i % Epad;
+        float ss = 0.0f;
+        for (int j = 0; j < 16; ++j) {
+            const float4 w = wpk[(c * 16 + j) * Epad + e];
+            ss = fmaf(w.x, w.x, ss);
+            ss = fmaf(w.y, w.y, ss);
+            ss = fmaf(w.z, w.z, ss);
+            ss = fmaf(w.w, w.w, ss);
+        }
+        out64[i] = sqrtf(ss);
     }
 }
 
@@ -973,7 +1004,8 @@ __global__ void block_gate_kernel(const float4* __restrict__ wt, int64_t D4, int
 template <int GROUP, int NSLOT, int TPG, typename XT, bool EXACT, int WARPS = kWarps, int DKO = 0,
           bool CERT = false>
 cudaError_t launch_one(const Gate& g, const void* x, int64_t N, int k, int ksel, int32_t* idx,
-                       float* val, cudaStream_t s) {
+                       float* val, cudaStream_t s, const int* rowlist = nullptr,
+                       unsigned long long* rows_total = nullptr) {
     using C = GatingCfg<GROUP, NSLOT, TPG, WARPS, XT, DKO>;
     const int64_t blocks = (N + C::TOK - 1) / C::TOK;
     auto kern = gating_kernel<GROUP, NSLOT, TPG, WARPS, XT, EXACT, DKO, CERT>;
@@ -985,7 +1017,8 @@ cudaError_t launch_one(const Gate& g, const void* x, int64_t N, int k, int ksel,
     }
     kern<<<static_cast<unsigned>(blocks), WARPS * 32, smem, s>>>(
         static_cast<const XT*>(x), reinterpret_cast<const float4*>(g.wt), g.bias, N,
-        static_cast<int>(g.D), static_cast<int>(g.E), k, ksel, idx, val, g.wsq16, g.cert_rows);
+        static_cast<int>(g.D), static_cast<int>(g.E), k, ksel, idx, val, g.wsq16, g.cert_rows,
+        rowlist, rows_total);
     return cudaGetLastError();
 }
 
@@ -1063,11 +1096,16 @@ cudaError_t launch_cert_e(const Gate& g, const void* x, int64_t N, int k, int ks
     if (small) {
         const size_t smem = cert_small_smem(g.Dpad, EPAD);
         auto kern = gating_cert_small_kernel<EPAD, XT>;
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
-        if (e != cudaSuccess) return e;
+        // the largest shared-memory size this instantiation was opened to, per device
+        static size_t opened[64] = {};
+        if (g.device < 0 || g.device >= 64 || opened[g.device] < smem) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(smem));
+            if (e != cudaSuccess) return e;
+            if (g.device >= 0 && g.device < 64) opened[g.device] = smem;
+        }
         kern<<<static_cast<unsigned>((N + kCertTT - 1) / kCertTT), kCertThreads, smem, s>>>(
-            static_cast<const XT*>(x), reinterpret_cast<const float4*>(g.wt), g.bias, g.wsq16, N,
+            static_cast<const XT*>(x), reinterpret_cast<const float4*>(g.wt), g.bias, g.wn64, N,
             static_cast<int>(g.D), g.Dpad, static_cast<int>(g.E), k, ksel, idx, val, g.cert_rows);
     } else {
         const cudaError_t e = dispatch_e<XT, false, true>(g, x, N, k, ksel, idx, val, s);
@@ -1075,20 +1113,12 @@ cudaError_t launch_cert_e(const Gate& g, const void* x, int64_t N, int k, int ks
     }
     const cudaError_t e1 = cudaGetLastError();
     if (e1 != cudaSuccess) return e1;
-    // the rows the first pass could not certify, with the EXACT arithmetic
-    const size_t esmem = sizeof(float) * (g.Dpad + EPAD);
-    auto ek = gating_exact_rows_kernel<EPAD, XT>;
-    if (esmem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(ek, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(esmem));
-        if (e != cudaSuccess) return e;
-    }
-    const int64_t grid = std::min<int64_t>(N, 2 * static_cast<int64_t>(sm_count(g.device)));
-    ek<<<static_cast<unsigned>(std::max<int64_t>(1, grid)), EPAD < 32 ? 32 : EPAD, esmem, s>>>(
-        static_cast<const XT*>(x), reinterpret_cast<const float4*>(g.wt), g.bias, N,
-        static_cast<int>(g.D), g.Dpad, static_cast<int>(g.E), k, ksel, idx, val, g.cert_rows,
-        g.cert_total);
-    return cudaGetLastError();
+    // The rows the first pass could not certify, with the EXACT arithmetic:
+    // the EXACT kernel in a few-tokens-per-CTA form over the row list, so
+    // the (few) deferred rows spread over many CTAs.
+    constexpr int GR = EPAD < 32 ? EPAD : 32;
+    return launch_one<GR, EPAD / GR, 2, XT, true, 4, 0, false>(g, x, N, k, ksel, idx, val, s,
+                                                              g.cert_rows, g.cert_total);
 }
 
 template <typename XT>
@@ -1261,6 +1291,7 @@ aem_status aem_gate_pack(const float* gate_weight, const float* gate_bias, int64
         aem::block_gate_kernel<<<256, 256>>>(reinterpret_cast<const float4*>(g->wt), g->Dpad / 4,
                                               g->Epad, g->eb, reinterpret_cast<float4*>(g->wblk));
         if (cudaMalloc(&g->wsq16, sizeof(float) * (g->Dpad / 16) * g->Epad) != cudaSuccess ||
+            cudaMalloc(&g->wn64, sizeof(float) * (g->Dpad / 64) * g->Epad) != cudaSuccess ||
             cudaMalloc(&g->cert_total, sizeof(unsigned long long)) != cudaSuccess ||
             cudaMemset(g->cert_total, 0, sizeof(unsigned long long)) != cudaSuccess) {
             set_error("aem_gate_pack: device allocation failed");
@@ -1268,7 +1299,7 @@ aem_status aem_gate_pack(const float* gate_weight, const float* gate_bias, int64
             break;
         }
         aem::gate_norms_kernel<<<256, 256>>>(reinterpret_cast<const float4*>(g->wt), g->Dpad,
-                                              g->Epad, g->wsq16);
+                                              g->Epad, g->wsq16, g->wn64);
         if (cudaDeviceSynchronize() != cudaSuccess) {
             set_error("aem_gate_pack: pack kernel failed: %s",
                       cudaGetErrorString(cudaGetLastError()));
@@ -1283,6 +1314,7 @@ aem_status aem_gate_pack(const float* gate_weight, const float* gate_bias, int64
         cudaFree(g->bias);
         cudaFree(g->wblk);
         cudaFree(g->wsq16);
+        cudaFree(g->wn64);
         cudaFree(g->cert_total);
         delete g;
         return st;
@@ -1299,6 +1331,7 @@ aem_status aem_gate_free(aem_gate_t gate) {
     cudaFree(g->bias);
     cudaFree(g->wblk);
     cudaFree(g->wsq16);
+    cudaFree(g->wn64);
     cudaFree(g->cert_rows);
     cudaFree(g->cert_total);
     delete g;

@@ -102,6 +102,7 @@ struct Gate {
     // call whose selection was not certified (cert_rows[0] = count, then the
     // row ids; room for cert_cap rows) with the running total of such rows.
     float* wsq16 = nullptr;
+    float* wn64 = nullptr;  // norms of the weights per 64-wide block of d, [Dpad/64][Epad]
     mutable int* cert_rows = nullptr;
     mutable int64_t cert_cap = 0;
     unsigned long long* cert_total = nullptr;

@@ -687,9 +687,9 @@ FP32_OPS_NOMINAL = 148 * 128 * 1.965e9  # float32 lane-ops/s of the CUDA cores a
 def run_suite(args):
     """The path's other configurations, one JSON line each (1 GPU).
 
-    C1 gating sweep (EXACT mode: a float32 multiply and add per term):
-    T in {1,16,128,1024,8192}, D=4096, E=8 (top-2) and E=64 (top-6), x bf16
-    and float32.  C2 INT8 GEMM sweep: M in {1,8,64,512,4096}, K=4096,
+    C1 gating sweep, EXACT mode (a float32 multiply and add per term) and
+    CERTIFIED mode (same indices): T in {1,16,128,1024,8192}, D=4096, E=8
+    (top-2) and E=64 (top-6), x bf16 and float32.  C2 INT8 GEMM sweep: M in {1,8,64,512,4096}, K=4096,
     N=14336, x bf16 and float32 (float32 = two bf16 MMAs, hi + lo).  C3
     Mixtral-shaped MoE layer: d=4096, ffn=14336, E=8, top-2, no capacity
     limit, T in {1,32,512,4096}, x bf16.  Every call is timed alone with CUDA
@@ -756,14 +756,16 @@ def run_suite(args):
                 xs = [torch.randn(t, D, device=dev).to(xdt) for _ in range(2)]
                 idx = torch.empty((t, k), dtype=torch.int32, device=dev)
                 val = torch.empty((t, k), dtype=torch.float32, device=dev)
-                sec = timed(lambda i: _lib.check(L.aem_gating(
-                    gate.handle, xs[i % 2].data_ptr(), code, t, k, 0, _lib.GATING_EXACT,
-                    idx.data_ptr(), val.data_ptr(), sp), "aem_gating"))
-                bytes_ = t * D * sx + e * D * 4 + 4 * e + 8 * k * t
-                flops = 2 * t * D * e
-                emit("C1 gating", {"T": t, "D": D, "E": e, "k": k, "x": str(xdt).split(".")[-1],
-                                   "mode": "exact"}, sec, bytes_, flops,
-                     "fp32" if e == 64 else "hbm")
+                for mname, mode in (("exact", _lib.GATING_EXACT),
+                                    ("certified", _lib.GATING_CERTIFIED)):
+                    sec = timed(lambda i: _lib.check(L.aem_gating(
+                        gate.handle, xs[i % 2].data_ptr(), code, t, k, 0, mode,
+                        idx.data_ptr(), val.data_ptr(), sp), "aem_gating"))
+                    bytes_ = t * D * sx + e * D * 4 + 4 * e + 8 * k * t
+                    flops = 2 * t * D * e
+                    emit("C1 gating", {"T": t, "D": D, "E": e, "k": k,
+                                       "x": str(xdt).split(".")[-1], "mode": mname}, sec, bytes_,
+                         flops, "fp32" if e == 64 else "hbm")
                 del xs
         del gate
     # ---- C2: INT8 GEMM sweep
@@ -866,10 +868,10 @@ def main():
                     help="N>1: also time the step's token exchange through NCCL all-to-all")
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the check of one step against the single-GPU EXACT-gating layer")
-    ap.add_argument("--gating", choices=["certified", "exact"], default="certified",
-                    help="gating arithmetic of the timed layer: certified (fast logits with a "
-                         "rigorous bound, uncertain rows recomputed exactly: indices "
-                         "bit-identical to exact) or exact (sequential float32)")
+    ap.add_argument("--gating", choices=["exact", "certified"], default="exact",
+                    help="gating arithmetic of the timed layer: exact (sequential float32, the "
+                         "faster at this shape) or certified (fast logits with a rigorous bound, "
+                         "uncertain rows recomputed exactly: indices bit-identical to exact)")
     ap.add_argument("--ep-pipeline", choices=["auto", "on", "off"], default="auto",
                     help="expert-parallel two-half pipeline (auto: off)")
     ap.add_argument("--suite", action="store_true",
