@@ -238,6 +238,101 @@ __global__ void __launch_bounds__(kThreads)
     }, T, half_T, k);
 }
 
+// Few units (decode steps, single GPU): the whole MoE routing in one CTA --
+// units, capacity ranks, effective experts, expert starts and the grouped
+// permutation -- with the same stable counting sorts as the kernels above
+// (ranks over units in unit order, rounds of kFusedThreads units, warp match
+// masks and a cross-warp prefix), so every output is identical; one launch
+// instead of seven.
+constexpr int kFusedThreads = 512;
+constexpr int kFusedWarps = kFusedThreads / 32;
+constexpr int64_t kFusedMaxUnits = 2048;
+
+__global__ void __launch_bounds__(kFusedThreads)
+    route_fused_kernel(const int32_t* __restrict__ idx, int64_t T, int ldi, int k, int E,
+                       uint64_t capacity, const float* __restrict__ val,
+                       uint32_t* __restrict__ eff_out, int* __restrict__ starts_out,
+                       int32_t* __restrict__ src_token, int32_t* __restrict__ rowmap,
+                       float* __restrict__ rowscale, int32_t* __restrict__ dest_of, int* err) {
+    __shared__ uint32_t s_prim[kFusedMaxUnits], s_sec[kFusedMaxUnits], s_eff[kFusedMaxUnits];
+    __shared__ int run[AEM_MAX_EXPERTS];
+    __shared__ int hw[kFusedWarps][AEM_MAX_EXPERTS];
+    __shared__ int st[AEM_MAX_EXPERTS + 1];
+    const int n = static_cast<int>(T * k);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const unsigned lt = (1u << lane) - 1u;
+    for (int u = tid; u < n; u += kFusedThreads) {
+        const int64_t j = u / T, t = u % T;
+        const int32_t p = idx[t * ldi + j];
+        const int32_t q = ldi > k ? idx[t * ldi + k] : p;
+        if (p < 0 || p >= E || q < 0 || q >= E) atomicOr(err, ERR_ROUTE_EXPERT);
+        s_prim[u] = static_cast<uint32_t>(p);
+        s_sec[u] = static_cast<uint32_t>(q);
+        s_eff[u] = 0xFFFFFFFFu;  // stays so for a unit with an invalid primary
+    }
+    for (int e = tid; e < E; e += kFusedThreads) run[e] = 0;
+    __syncthreads();
+    // stable ranks of keys[u] over u in order, handed to emit(u, e, rank)
+    auto ranks = [&](const uint32_t* keys, auto emit) {
+        for (int r0 = 0; r0 < n; r0 += kFusedThreads) {
+            for (int i = tid; i < kFusedWarps * E; i += kFusedThreads) hw[i / E][i % E] = 0;
+            __syncthreads();
+            const int u = r0 + tid;
+            uint32_t e = u < n ? keys[u] : 0xFFFFFFFFu;
+            if (e >= static_cast<uint32_t>(E)) e = 0xFFFFFFFFu;
+            const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
+            const int in_warp = __popc(peers & lt);
+            if (e != 0xFFFFFFFFu && in_warp == 0) hw[warp][e] = __popc(peers);
+            __syncthreads();
+            for (int x = tid; x < E; x += kFusedThreads) {
+                int acc = run[x];
+                for (int w = 0; w < kFusedWarps; ++w) {
+                    const int v = hw[w][x];
+                    hw[w][x] = acc;
+                    acc += v;
+                }
+                run[x] = acc;
+            }
+            __syncthreads();
+            if (e != 0xFFFFFFFFu) emit(u, e, hw[warp][e] + in_warp);
+            __syncthreads();
+        }
+    };
+    // pass 1: the capacity rule over primaries
+    ranks(s_prim, [&](int u, uint32_t e, int rank) {
+        s_eff[u] = static_cast<uint64_t>(rank) < capacity ? e : s_sec[u];
+    });
+    // expert totals of the effective experts -> starts
+    for (int e = tid; e < E; e += kFusedThreads) run[e] = 0;
+    __syncthreads();
+    for (int u = tid; u < n; u += kFusedThreads)
+        if (s_eff[u] < static_cast<uint32_t>(E)) atomicAdd(&run[s_eff[u]], 1);
+    __syncthreads();
+    if (tid == 0) {
+        int acc = 0;
+        for (int e = 0; e < E; ++e) {
+            st[e] = acc;
+            acc += run[e];
+        }
+        st[E] = acc;
+    }
+    __syncthreads();
+    for (int e = tid; e <= E; e += kFusedThreads) starts_out[e] = st[e];
+    for (int e = tid; e < E; e += kFusedThreads) run[e] = 0;
+    for (int u = tid; u < n; u += kFusedThreads)
+        if (eff_out) eff_out[u] = s_eff[u];
+    __syncthreads();
+    // pass 2: the expert-grouped permutation
+    ranks(s_eff, [&](int u, uint32_t e, int rank) {
+        const int dest = st[e] + rank;
+        const int64_t j = u / T, t = u % T;
+        src_token[dest] = static_cast<int32_t>(t);
+        rowmap[dest] = static_cast<int32_t>(t * k + j);
+        rowscale[dest] = val[t * k + j];
+        if (dest_of) dest_of[u] = dest;
+    });
+}
+
 }  // namespace
 
 int64_t route_chunks(int64_t n) { return (n + kChunk - 1) / kChunk; }
@@ -256,6 +351,16 @@ size_t moe_route_workspace(int64_t T, int k, int E) {
 aem_status route_moe(const MoeRouteArgs& a, cudaStream_t s) {
     const int64_t n = a.T * a.k;
     if (n == 0) return AEM_OK;
+    if (n <= kFusedMaxUnits && a.corr == nullptr && a.half_T == 0 && a.starts_out) {
+        int* err = device_error_word(current_device());
+        AEM_REQUIRE(err != nullptr, "route: no device error word");
+        route_fused_kernel<<<1, kFusedThreads, 0, s>>>(a.idx, a.T, a.ldi, a.k, a.E, a.capacity,
+                                                       a.val, a.eff_out, a.starts_out, a.src_token,
+                                                       a.rowmap, a.rowscale, a.dest_of, err);
+        AEM_CHECK_LAUNCH();
+        count_launches(1);
+        return AEM_OK;
+    }
     const int64_t c = route_chunks_moe(n);
     char* w = static_cast<char*>(a.workspace);
     auto take = [&](size_t bytes) {
