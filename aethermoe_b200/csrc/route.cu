@@ -128,36 +128,54 @@ __global__ void __launch_bounds__(kThreads)
     for (int e = threadIdx.x; e < E; e += kThreads) cnt[static_cast<int64_t>(blockIdx.x) * E + e] = h[e];
 }
 
-// In place: cnt[c][e] -> exclusive prefix over c.  Optionally totals[e] and
-// starts[0..E] (exclusive prefix of totals over e).  One CTA.
-// Exclusive prefix of every expert's per-chunk counts over the chunks (in
-// place), one warp per expert; then the expert starts.
+// In place: cnt[c][e] -> exclusive prefix over c, and starts[0..E]
+// (exclusive prefix of the expert totals over e) when starts is given.  One
+// CTA: thread (group g, expert e) takes a contiguous range of chunks, so a
+// warp's loads are consecutive experts of one chunk (coalesced) and each
+// thread's loads are independent (batched); pass 1 sums the group's range,
+// a prefix over the groups runs in shared memory, pass 2 writes the range's
+// exclusive prefixes.
 __global__ void __launch_bounds__(kScanThreads)
     chunk_scan_kernel(int* __restrict__ cnt, int nchunks, int E, int* __restrict__ starts) {
+    __shared__ int gsum[kScanThreads];  // [group][expert]
     __shared__ int tot[AEM_MAX_EXPERTS];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int e = warp; e < E; e += kScanThreads / 32) {
-        int run = 0;
-        for (int c0 = 0; c0 < nchunks; c0 += 32) {
-            const int c = c0 + lane;
-            const int v = c < nchunks ? cnt[static_cast<int64_t>(c) * E + e] : 0;
-            int inc = v;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int nb = __shfl_up_sync(0xFFFFFFFFu, inc, o);
-                if (lane >= o) inc += nb;
-            }
-            if (c < nchunks) cnt[static_cast<int64_t>(c) * E + e] = run + inc - v;
-            run += __shfl_sync(0xFFFFFFFFu, inc, 31);
-        }
-        if (lane == 0) tot[e] = run;
+    const int ng = kScanThreads / E;    // groups of chunks (E <= 256: at least 4)
+    const int tid = threadIdx.x;
+    const int g = tid / E, e = tid % E;
+    const bool act = g < ng;
+    const int per = (nchunks + ng - 1) / ng;
+    const int c0 = g * per, c1 = min(nchunks, c0 + per);
+    int sum = 0;
+    if (act) {
+#pragma unroll 8
+        for (int c = c0; c < c1; ++c) sum += cnt[static_cast<int64_t>(c) * E + e];
+        gsum[g * E + e] = sum;
     }
     __syncthreads();
-    if (starts && threadIdx.x == 0) {
+    if (tid < E) {
         int run = 0;
-        for (int e = 0; e < E; ++e) {
-            starts[e] = run;
-            run += tot[e];
+        for (int q = 0; q < ng; ++q) {
+            const int v = gsum[q * E + tid];
+            gsum[q * E + tid] = run;
+            run += v;
+        }
+        tot[tid] = run;
+    }
+    __syncthreads();
+    if (act) {
+        int run = gsum[g * E + e];
+        for (int c = c0; c < c1; ++c) {
+            const int64_t i = static_cast<int64_t>(c) * E + e;
+            const int v = cnt[i];
+            cnt[i] = run;
+            run += v;
+        }
+    }
+    if (starts && tid == 0) {
+        int run = 0;
+        for (int x = 0; x < E; ++x) {
+            starts[x] = run;
+            run += tot[x];
         }
         starts[E] = run;
     }
