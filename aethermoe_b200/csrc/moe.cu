@@ -34,7 +34,16 @@ namespace {
 template <typename XT>
 __global__ void gather_rows_kernel(const XT* __restrict__ x, const int32_t* __restrict__ src,
                                    int64_t rows, int64_t d, __nv_bfloat16* __restrict__ out,
-                                   __nv_bfloat16* __restrict__ lo) {
+                                   __nv_bfloat16* __restrict__ lo, float4* __restrict__ z1,
+                                   int64_t n1, float4* __restrict__ z2, int64_t n2) {
+    // zeroing of the step's accumulation buffers rides along (n1, n2 float4s)
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n1 + n2;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        if (i < n1)
+            z1[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        else
+            z2[i - n1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     const int lane = threadIdx.x & 31;
     for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -139,17 +148,25 @@ unsigned grid_for(int64_t work, int per_block) {
 }  // namespace
 
 aem_status gather_rows(const void* x, aem_dtype xd, const int32_t* src, int64_t rows, int64_t d,
-                       void* out, cudaStream_t s, void* out_lo) {
-    if (rows == 0) return AEM_OK;
-    const unsigned g = grid_for(rows, 8);
+                       void* out, cudaStream_t s, void* out_lo, float* zero1, int64_t zero1_n,
+                       float* zero2, int64_t zero2_n) {
+    if (rows == 0 && zero1_n == 0 && zero2_n == 0) return AEM_OK;
+    AEM_REQUIRE(zero1_n % 4 == 0 && zero2_n % 4 == 0 &&
+                    (reinterpret_cast<uintptr_t>(zero1) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(zero2) & 15) == 0,
+                "gather_rows: zeroed ranges must be whole, aligned float4s");
+    const int64_t z4 = (zero1_n + zero2_n) / 4;
+    const unsigned g = std::max(grid_for(rows, 8), grid_for(z4, 256 * 4));
     if (xd == AEM_BF16)
         gather_rows_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(
             static_cast<const __nv_bfloat16*>(x), src, rows, d, static_cast<__nv_bfloat16*>(out),
-            nullptr);
+            nullptr, reinterpret_cast<float4*>(zero1), zero1_n / 4,
+            reinterpret_cast<float4*>(zero2), zero2_n / 4);
     else
-        gather_rows_kernel<float><<<g, 256, 0, s>>>(static_cast<const float*>(x), src, rows, d,
-                                                    static_cast<__nv_bfloat16*>(out),
-                                                    static_cast<__nv_bfloat16*>(out_lo));
+        gather_rows_kernel<float><<<g, 256, 0, s>>>(
+            static_cast<const float*>(x), src, rows, d, static_cast<__nv_bfloat16*>(out),
+            static_cast<__nv_bfloat16*>(out_lo), reinterpret_cast<float4*>(zero1), zero1_n / 4,
+            reinterpret_cast<float4*>(zero2), zero2_n / 4);
     AEM_CHECK_LAUNCH();
     count_launches(1);
     return AEM_OK;
@@ -276,15 +293,24 @@ aem_status Moe::forward(const void* x, aem_dtype xd, int64_t T, void* out, aem_d
     const bool split_x = xd == AEM_F32;
     const bool split_h = hidden_dtype < 0 ? split_x : hidden_dtype == AEM_F32;
     if (split_x || split_h) AEM_TRY(reserve_split(T));
-    AEM_TRY(gather_rows(x, xd, src_token, U, d, xperm, s, split_x ? xperm_lo : nullptr));
+    // the step's accumulation buffers (float32 output rows; at decode sizes
+    // the up projection's pre-activations) are zeroed by the gather's launch
+    const bool decode = U <= gemv_max_rows();
+    if (decode && !h32) AEM_TRY_CUDA(cudaMalloc(&h32, sizeof(float) * gemv_max_rows() * f));
+    float* acc = od == AEM_F32 ? static_cast<float*>(out) : y;
+    const bool z_acc = (T * d) % 4 == 0 && (reinterpret_cast<uintptr_t>(acc) & 15) == 0;
+    const bool z_h = decode && (U * f) % 4 == 0;
+    AEM_TRY(gather_rows(x, xd, src_token, U, d, xperm, s, split_x ? xperm_lo : nullptr,
+                        z_h ? h32 : nullptr, z_h ? U * f : 0, z_acc ? acc : nullptr,
+                        z_acc ? T * d : 0));
     prof.end(AEM_PHASE_ROUTE, s);
-    AEM_TRY(expert_ffn(T, U, out, od, s, split_x, split_h));
+    AEM_TRY(expert_ffn(T, U, out, od, s, split_x, split_h, z_acc, z_h));
     prof.step();
     return AEM_OK;
 }
 
 aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaStream_t s,
-                           bool split_x, bool split_h) {
+                           bool split_x, bool split_h, bool acc_zeroed, bool h32_zeroed) {
     const int k = cfg.top_k, E = cfg.num_experts;
     const int64_t d = cfg.d_model, f = cfg.d_ffn;
     // Decode steps (few units): the up projection splits K over the SMs, which
@@ -315,7 +341,7 @@ aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaSt
         up_a.atomic_add = true;
     }
     prof.begin(AEM_PHASE_UP, s);
-    if (decode) AEM_TRY_CUDA(cudaMemsetAsync(h32, 0, sizeof(float) * U * f, s));
+    if (decode && !h32_zeroed) AEM_TRY_CUDA(cudaMemsetAsync(h32, 0, sizeof(float) * U * f, s));
     AEM_TRY(launch_qgemm(up_a, s));
     prof.end(AEM_PHASE_UP, s);
 
@@ -351,7 +377,7 @@ aem_status Moe::expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaSt
     const int sms = sm_count(gate->device);
     dn.stream_k = tiles < 8 * static_cast<int64_t>(sms);
     prof.begin(AEM_PHASE_DOWN, s);
-    AEM_TRY_CUDA(cudaMemsetAsync(acc, 0, sizeof(float) * T * d, s));
+    if (!acc_zeroed) AEM_TRY_CUDA(cudaMemsetAsync(acc, 0, sizeof(float) * T * d, s));
     AEM_TRY(launch_qgemm(dn, s));
     prof.end(AEM_PHASE_DOWN, s);
     if (od != AEM_F32) {

@@ -10,8 +10,13 @@
 
 namespace aem {
 
+// X[r] = x[src[r]] as bf16 (lo: the float32 pair's low half); also zeroes
+// zero1[0, zero1_n) and zero2[0, zero2_n) (float counts, multiples of 4,
+// 16-byte aligned) in the same launch.
 aem_status gather_rows(const void* x, aem_dtype xd, const int32_t* src, int64_t rows, int64_t d,
-                       void* out, cudaStream_t s, void* out_lo = nullptr);
+                       void* out, cudaStream_t s, void* out_lo = nullptr,
+                       float* zero1 = nullptr, int64_t zero1_n = 0, float* zero2 = nullptr,
+                       int64_t zero2_n = 0);
 aem_status combine_rows(const float* y, int64_t T, int k, int64_t d, void* out, aem_dtype od,
                         cudaStream_t s);
 
@@ -56,8 +61,11 @@ struct Moe {
                        cudaStream_t s);
     // Grouped up GEMM + ReLU, grouped down GEMM (scaled by the gate weight,
     // scattered to row t*k+j), combine -- on xperm/starts/rowmap/rowscale.
+    // acc_zeroed / h32_zeroed: the float32 output rows / decode pre-activations
+    // were zeroed already (by the gather's launch)
     aem_status expert_ffn(int64_t T, int64_t U, void* out, aem_dtype od, cudaStream_t s,
-                          bool split_x = false, bool split_h = false);
+                          bool split_x = false, bool split_h = false, bool acc_zeroed = false,
+                          bool h32_zeroed = false);
 };
 
 void seam_free(Moe* m);  // releases the scheduler seam's buffers (seam.cu)

@@ -43,6 +43,7 @@ namespace {
 constexpr int kGvWarps = 4;
 constexpr int kGvThreads = kGvWarps * 32;
 constexpr int kGvMaxRows = 16;  // above: the tensor-core kernel (measured faster from 17 rows)
+constexpr int kGvMaxGroups = 256;
 
 // 4 signed bytes (one 32-bit word, bytes b0 b1 b2 b3) -> two bf16x2 words
 // (b0, b1) and (b2, b3), exact: each byte becomes the float 2^23 + (b + 128)
@@ -89,6 +90,7 @@ struct GvParams {
     const float* scale;
     int64_t M, K, N, NT, KT;
     const int* group_rows;    // nullptr: one group of M rows
+    int G;                    // groups in group_rows (blockIdx.z picks the z-th with rows)
     int64_t group_base;
     int wmod;
     int ks;                   // K ranges
@@ -109,7 +111,40 @@ __global__ void __launch_bounds__(kGvThreads)
     extern __shared__ __align__(16) unsigned char gsm[];
     const int nb = blockIdx.x;  // 128-channel tile row
     const int ks = blockIdx.y;
-    const int g = blockIdx.z;
+    // grouped: the grid covers min(G, M) group slots; slot z takes the z-th
+    // group that has rows (most groups are empty at decode sizes)
+    int g = 0;
+    if (p.group_rows) {
+        __shared__ int s_rows[kGvMaxGroups + 1];
+        __shared__ int s_pick;
+        for (int i = threadIdx.x; i <= p.G; i += kGvThreads) s_rows[i] = p.group_rows[i];
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            const int lane0 = threadIdx.x;
+            int base = 0, pick = -1;
+            bool bad = false;
+            for (int c0 = 0; c0 < p.G; c0 += 32) {
+                const int gg = c0 + lane0;
+                const int mm = gg < p.G ? s_rows[gg + 1] - s_rows[gg] : 0;
+                if (mm < 0 || mm > NT8 * 8) bad = true;
+                const unsigned bal = __ballot_sync(0xFFFFFFFFu, mm > 0);
+                const int before = base + __popc(bal & ((1u << lane0) - 1u));
+                if (mm > 0 && before == static_cast<int>(blockIdx.z)) pick = gg;
+                base += __popc(bal);
+            }
+            // one lane at most found the slot's group
+            const unsigned has = __ballot_sync(0xFFFFFFFFu, pick >= 0);
+            if (lane0 == 0) s_pick = has ? -2 : -1;
+            __syncwarp();
+            if (pick >= 0) s_pick = pick;
+            if (__any_sync(0xFFFFFFFFu, bad) && lane0 == 0 && blockIdx.x == 0 && blockIdx.y == 0 &&
+                blockIdx.z == 0)
+                atomicOr(p.err, ERR_GEMM_GROUPS);
+        }
+        __syncthreads();
+        g = s_pick;
+        if (g < 0) return;  // fewer groups with rows than slots (uniform over the CTA)
+    }
     const int r0 = p.group_rows ? p.group_rows[g] : 0;
     const int r1 = p.group_rows ? p.group_rows[g + 1] : static_cast<int>(p.M);
     const int m = r1 - r0;
@@ -328,8 +363,10 @@ aem_status launch_qgemm_gemv(const GemmArgs& a, cudaStream_t s) {
     // rows of the largest group: at most M (the group sizes live on the device)
     const int64_t mrows = std::min<int64_t>(a.M, kGvMaxRows);
     const int nt8 = mrows <= 8 ? 1 : 2;
-    const int64_t groups = a.group_rows ? a.G : 1;
-    const int64_t busy = std::min<int64_t>(groups, a.M) * w.NT;  // CTAs with rows per K range
+    AEM_REQUIRE(a.G >= 1 && a.G <= kGvMaxGroups, "qgemv: G=%d outside [1, %d]", a.G, kGvMaxGroups);
+    // group slots: at most min(G, M) groups have rows (each slot finds its group)
+    const int64_t groups = a.group_rows ? std::min<int64_t>(a.G, a.M) : 1;
+    const int64_t busy = groups * w.NT;  // CTAs with rows per K range
     // K ranges: enough CTAs for ~4 per SM, ranges of at most 1024 K (shared
     // memory for the activation rows); split only where partial sums may add
     const bool can_split = !a.out_bf16 && !a.relu && (a.atomic_add || a.rowmap == nullptr);
@@ -357,6 +394,7 @@ aem_status launch_qgemm_gemv(const GemmArgs& a, cudaStream_t s) {
     p.NT = w.NT;
     p.KT = w.KT;
     p.group_rows = a.group_rows;
+    p.G = a.group_rows ? a.G : 1;
     p.group_base = a.group_base;
     p.wmod = a.wmod;
     p.ks = static_cast<int>(ks);
