@@ -4,11 +4,14 @@
 // With at most 16 rows per weight group the work per weight byte is a few
 // multiply-adds, so the kernel is a weight stream: every warp loads its int8
 // rows straight from global memory into registers (16-byte non-caching loads,
-// the next tile's while the current one is multiplied), converts them exactly
+// the next tiles' while the current one is multiplied), converts them exactly
 // to bf16 in registers and multiplies them with mma.sync.m16n8k16 (bf16 in,
 // float32 accumulate).  No shared memory holds weights and no barrier paces
 // the stream; shared memory holds the CTA's activation rows, restaged every
-// 1024 K of its range.  Many small CTAs (four warps) per SM: converting int8
+// 768 K of its range.  Three register buffers keep two tiles in flight
+// while a third is converted and multiplied (the loop is unrolled by three,
+// so no buffer is copied), and the K split makes one wave of CTAs (four per
+// SM at this register use).  Many small CTAs (four warps): converting int8
 // costs about two instructions per weight byte, so the kernel needs issue
 // slots and warps to hide latency as much as bytes in flight.  Measured on
 // B200 against this form, a bulk-copy shared-memory ring, a per-thread
@@ -178,15 +181,62 @@ __global__ void __launch_bounds__(kGvThreads)
 #pragma unroll
             for (int c = 0; c < 4; ++c) acc[a][n][c] = 0.0f;
 
-    constexpr int SUB = 16;  // 64-wide K tiles of activations staged at once
+    constexpr int SUB = 12;  // 64-wide K tiles of activations staged at once (a multiple of 3)
     constexpr int XS = SUB * 64 * 2 + 16;   // padded activation row, bytes
     unsigned char* xs = gsm;                 // [NT8*8][XS] bf16 (hi)
     unsigned char* xls = gsm + NT8 * 8 * XS; // [NT8*8][XS] bf16 (lo), float32 activations only
 
-    uint4 wcur[4], wnext[4];
+    // two weight tiles in flight during each tile's compute: tile kt0 + r lives in
+    // wa, wb or wc by r mod 3
+    uint4 wa[4], wb[4], wc[4];
+    auto fetch = [&](uint4 (&w)[4], int kt) {
+        if (kt < kt1) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-        wcur[i] = ld_stream16(wtile0 + static_cast<int64_t>(kt0) * kWTileBytes + offs[i]);
+            for (int i = 0; i < 4; ++i)
+                w[i] = ld_stream16(wtile0 + static_cast<int64_t>(kt) * kWTileBytes + offs[i]);
+        }
+    };
+    fetch(wa, kt0);
+    fetch(wb, kt0 + 1);
+    auto compute = [&](const uint4 (&w)[4], int kt, int sb) {
+        // A fragments: rows i = 0..3 (m-tile i/2, half i%2), K steps j = 0..3
+        uint2 a[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            a[i][0] = gv_i8x4_to_bf16x4(w[i].x);
+            a[i][1] = gv_i8x4_to_bf16x4(w[i].y);
+            a[i][2] = gv_i8x4_to_bf16x4(w[i].z);
+            a[i][3] = gv_i8x4_to_bf16x4(w[i].w);
+        }
+        const int kk = (kt - sb) * 64 + 16 * t;
+#pragma unroll
+        for (int n = 0; n < NT8; ++n) {
+            const unsigned char* xr = xs + (n * 8 + gq) * XS + kk * 2;
+            const uint4 b01 = *reinterpret_cast<const uint4*>(xr);       // K steps 0, 1
+            const uint4 b23 = *reinterpret_cast<const uint4*>(xr + 16);  // K steps 2, 3
+            const uint32_t bw[8] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                mma_bf16_16816(acc[0][n], a[0][j].x, a[1][j].x, a[0][j].y, a[1][j].y,
+                               bw[2 * j], bw[2 * j + 1]);
+                mma_bf16_16816(acc[1][n], a[2][j].x, a[3][j].x, a[2][j].y, a[3][j].y,
+                               bw[2 * j], bw[2 * j + 1]);
+            }
+            if (p.has_lo) {
+                const unsigned char* xq = xls + (n * 8 + gq) * XS + kk * 2;
+                const uint4 l01 = *reinterpret_cast<const uint4*>(xq);
+                const uint4 l23 = *reinterpret_cast<const uint4*>(xq + 16);
+                const uint32_t lw[8] = {l01.x, l01.y, l01.z, l01.w, l23.x, l23.y, l23.z, l23.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    mma_bf16_16816(acc[0][n], a[0][j].x, a[1][j].x, a[0][j].y, a[1][j].y,
+                                   lw[2 * j], lw[2 * j + 1]);
+                    mma_bf16_16816(acc[1][n], a[2][j].x, a[3][j].x, a[2][j].y, a[3][j].y,
+                                   lw[2 * j], lw[2 * j + 1]);
+                }
+            }
+        }
+    };
     for (int sb = kt0; sb < kt1; sb += SUB) {
         const int se = min(kt1, sb + SUB);
         // ---- the token rows' activations of tiles [sb, se) (rows past m, K past K: zero)
@@ -240,56 +290,17 @@ __global__ void __launch_bounds__(kGvThreads)
         }
         __syncthreads();
 
-        for (int kt = sb; kt < se; ++kt) {
-            if (kt + 1 < kt1) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    wnext[i] =
-                        ld_stream16(wtile0 + static_cast<int64_t>(kt + 1) * kWTileBytes + offs[i]);
+        // sub-ranges start a multiple of 3 tiles after kt0 (SUB is)
+        for (int kt = sb; kt < se; kt += 3) {
+            fetch(wc, kt + 2);
+            compute(wa, kt, sb);
+            if (kt + 1 < se) {
+                fetch(wa, kt + 3);
+                compute(wb, kt + 1, sb);
             }
-            // A fragments: rows i = 0..3 (m-tile i/2, half i%2), K steps j = 0..3
-            uint2 a[4][4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                a[i][0] = gv_i8x4_to_bf16x4(wcur[i].x);
-                a[i][1] = gv_i8x4_to_bf16x4(wcur[i].y);
-                a[i][2] = gv_i8x4_to_bf16x4(wcur[i].z);
-                a[i][3] = gv_i8x4_to_bf16x4(wcur[i].w);
-            }
-            const int kk = (kt - sb) * 64 + 16 * t;
-#pragma unroll
-            for (int n = 0; n < NT8; ++n) {
-                const unsigned char* xr = xs + (n * 8 + gq) * XS + kk * 2;
-                const uint4 b01 = *reinterpret_cast<const uint4*>(xr);       // K steps 0, 1
-                const uint4 b23 = *reinterpret_cast<const uint4*>(xr + 16);  // K steps 2, 3
-                const uint32_t bw[8] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    // A regs: (row g, K pair 0), (row g+8, K pair 0), (row g, K pair 1),
-                    // (row g+8, K pair 1); this thread's rows 0/1 are m-tile 0's g/g+8,
-                    // rows 2/3 m-tile 1's
-                    mma_bf16_16816(acc[0][n], a[0][j].x, a[1][j].x, a[0][j].y, a[1][j].y,
-                                   bw[2 * j], bw[2 * j + 1]);
-                    mma_bf16_16816(acc[1][n], a[2][j].x, a[3][j].x, a[2][j].y, a[3][j].y,
-                                   bw[2 * j], bw[2 * j + 1]);
-                }
-                if (p.has_lo) {
-                    const unsigned char* xq = xls + (n * 8 + gq) * XS + kk * 2;
-                    const uint4 l01 = *reinterpret_cast<const uint4*>(xq);
-                    const uint4 l23 = *reinterpret_cast<const uint4*>(xq + 16);
-                    const uint32_t lw[8] = {l01.x, l01.y, l01.z, l01.w, l23.x, l23.y, l23.z, l23.w};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        mma_bf16_16816(acc[0][n], a[0][j].x, a[1][j].x, a[0][j].y, a[1][j].y,
-                                       lw[2 * j], lw[2 * j + 1]);
-                        mma_bf16_16816(acc[1][n], a[2][j].x, a[3][j].x, a[2][j].y, a[3][j].y,
-                                       lw[2 * j], lw[2 * j + 1]);
-                    }
-                }
-            }
-            if (kt + 1 < kt1) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) wcur[i] = wnext[i];
+            if (kt + 2 < se) {
+                fetch(wb, kt + 4);
+                compute(wc, kt + 2, sb);
             }
         }
     }
@@ -333,7 +344,7 @@ __global__ void __launch_bounds__(kGvThreads)
 
 template <int NT8>
 aem_status launch_gv(const GvParams& p, int64_t groups, cudaStream_t s) {
-    constexpr int SUB = 16;
+    constexpr int SUB = 12;
     const size_t smem = static_cast<size_t>((p.has_lo ? 2 : 1) * NT8 * 8) * (SUB * 64 * 2 + 16);
     auto kern = qgemv_kernel<NT8>;
     if (smem > 48 * 1024)
@@ -372,7 +383,8 @@ aem_status launch_qgemm_gemv(const GemmArgs& a, cudaStream_t s) {
     const bool can_split = !a.out_bf16 && !a.relu && (a.atomic_add || a.rowmap == nullptr);
     int64_t ks = 1;
     if (can_split) {
-        ks = std::max<int64_t>(1, (4 * static_cast<int64_t>(sms) + busy - 1) / busy);
+        // one wave: as many CTAs as fit resident (4 per SM at this register use)
+        ks = std::max<int64_t>(1, (4 * static_cast<int64_t>(sms)) / busy);
         ks = std::min<int64_t>(ks, w.KT);
     }
     const int kper = static_cast<int>((w.KT + ks - 1) / ks);
