@@ -26,7 +26,7 @@ __all__ = [
     "reference_gating", "quantize_int8", "dequantize_int8", "qgemm",
     "capacity_assign", "moe_units", "moe_route", "bf16_round",
     "moe_layer", "moe_layer_rows", "ep_local_counts", "ep_slot_bases",
-    "zipf_bias", "default_capacity",
+    "zipf_bias", "default_capacity", "certified_fast_logits",
 ]
 
 
@@ -154,6 +154,61 @@ def certified_rows(hidden, gate_weight, gate_bias, k):
     bk = np.take_along_axis(bound, order[:, k - 1:k], 1)[:, 0]
     bn = np.take_along_axis(bound, order[:, k:k + 1], 1)[:, 0]
     return (kth - nxt) > 2.0 * (bk + bn)
+
+
+def _fma32(a, b, c):
+    """float32 fused multiply-add a*b + c with one rounding: the float32
+    product is exact in float64 and the float64 sum is rounded once to
+    float32 (a double rounding that differs from a true single rounding only
+    at float64 ties -- far inside the bound's margin)."""
+    return (a.astype(np.float64) * b.astype(np.float64) + c.astype(np.float64)).astype(np.float32)
+
+
+def certified_fast_logits(hidden, gate_weight, gate_bias, parts=1, block=64):
+    """Fast logits and their certified bound, the arithmetic of the CERTIFIED
+    gating kernels (this library's own mode: the reference has only the
+    sequential form of ``prototype/math_proto.py:33-34``).
+
+    d is cut into ``parts`` contiguous parts of whole ``block``-wide blocks;
+    each part is a chain of float32 fused multiply-adds from zero; after each
+    block ``Q += block |P| + (block + 1) |x_block| |w_block|``; the parts are
+    then added in order with ``Q += len(part) |P_start|`` and ``Qc += |P_start|
+    + |S_part|``, the bias added last.  Returns ``(F, B)`` float32 ``[N, E]``
+    with ``B = 4 u (Q + Qc + |F| + |b|)``, ``u = 2**-24``: the bound on the
+    distance from the sequential logits (``gating_logits_seq``).
+    """
+    h = np.ascontiguousarray(hidden, dtype=np.float32)
+    w = np.ascontiguousarray(gate_weight, dtype=np.float32)
+    b = np.asarray(gate_bias, dtype=np.float32).reshape(-1)
+    n, d = h.shape
+    e = w.shape[1]
+    nblk = -(-d // block)
+    dpad = nblk * block
+    hp = np.zeros((n, dpad), np.float32)
+    hp[:, :d] = h
+    wp = np.zeros((dpad, e), np.float32)
+    wp[:d] = w
+    bpp = -(-nblk // parts)
+    xn = np.sqrt(np.square(hp.reshape(n, nblk, block).astype(np.float64)).sum(2)).astype(np.float32)
+    wn = np.sqrt(np.square(wp.reshape(nblk, block, e).astype(np.float64)).sum(1)).astype(np.float32)
+    run = np.zeros((n, e), np.float32)
+    Q = np.zeros((n, e), np.float64)
+    Qc = np.zeros((n, e), np.float64)
+    for p in range(parts):
+        acc = np.zeros((n, e), np.float32)
+        q = np.zeros((n, e), np.float64)
+        for blk in range(p * bpp, min(nblk, (p + 1) * bpp)):
+            for dd in range(blk * block, (blk + 1) * block):
+                acc = _fma32(hp[:, dd][:, None], wp[dd][None, :], acc)
+            q += block * np.abs(acc.astype(np.float64)) + (block + 1) * (
+                xn[:, blk][:, None].astype(np.float64) * wn[blk][None, :])
+        Q += q + block * bpp * np.abs(run.astype(np.float64))
+        Qc += np.abs(run.astype(np.float64)) + np.abs(acc.astype(np.float64))
+        run = (run + acc).astype(np.float32)
+    f = (run + b[None, :]).astype(np.float32)
+    u = 2.0 ** -24
+    bound = (4 * u * (Q + Qc + np.abs(f) + np.abs(b)[None, :])).astype(np.float32)
+    return f, bound
 
 
 # ----------------------------------------------------------------------------
