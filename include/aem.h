@@ -59,7 +59,9 @@ typedef enum { AEM_F32 = 0, AEM_BF16 = 1 } aem_dtype;
  *   rounding of EXACT's); every other row -- near ties, NaN, +-inf -- is
  *   recomputed with the EXACT arithmetic (written exactly as EXACT writes it)
  *   on the device, without a host round trip.  aem_gate_fallback_rows counts
- *   the recomputed rows. */
+ *   the recomputed rows.  CERTIFIED calls on one gate share that gate's
+ *   device list of deferred rows: they must not overlap on the GPU (issue
+ *   them on one stream, or one gate per stream). */
 typedef enum {
     AEM_GATING_EXACT = 0,
     AEM_GATING_FAST = 1,
