@@ -1340,12 +1340,14 @@ aem_status launch_qgemm(const GemmArgs& a, cudaStream_t s) {
     const int64_t tiles_ub = ((rows + bt - 1) / bt + std::min<int64_t>(a.G, rows)) * nch * ks;
     // SM pairs (cta_group::2) for large token tiles: half the activation bytes
     // per SM and half the MMA issue per FLOP
-    // automatic: 128/256-row tiles over an even number of 128-channel blocks
-    // (an odd count leaves the last pair's second block idle: 1/12 of the
-    // MMAs at 11 blocks, which measured slower than single SMs)
+    // automatic: 128/256-row tiles over an even number of 128-channel blocks,
+    // or at least 11 (an odd count leaves the last pair's second block idle:
+    // 1/12 of the MMAs at 11 blocks, which the halved activation traffic
+    // still beats -- measured 5% ahead of single SMs on the 1408-channel up
+    // projection of the layer bench)
     const int mode = gemm_pair_mode();
     if (!tsa && !p.stream_k && bt >= 64 &&
-        (mode == 1 || (mode < 0 && bt >= 128 && (nch % 2 == 0 || nch >= 15)))) {
+        (mode == 1 || (mode < 0 && bt >= 128 && (nch % 2 == 0 || nch >= 11)))) {
         const int64_t ptiles = ((rows + bt - 1) / bt + std::min<int64_t>(a.G, rows)) *
                                ((nch + 1) / 2) * ks;
         const int pairs =

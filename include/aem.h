@@ -210,7 +210,7 @@ aem_status aem_grouped_qgemm(aem_qweight_t w, const int32_t* group_rows, int G, 
                              int token_tile, int ksplit, void* stream);
 /* Which form of the tensor-core GEMM runs (process-wide, every device):
  * -1 (default) automatic -- token tiles of 128 or 256 rows over an even
- * number of 128-channel blocks (or at least 15) run on SM pairs (tcgen05
+ * number of 128-channel blocks (or at least 11) run on SM pairs (tcgen05
  * cta_group::2: two SMs share one 256-channel tile, each holding half of
  * the token rows), everything else on single SMs; 0 single SMs only; 1 SM
  * pairs from 64-row tiles on.  Results agree within float32 summation
