@@ -325,8 +325,10 @@ aem_status aem_moe_forward_host(aem_context_t ctx, aem_moe_t moe, const void* x,
  * the copy landed, copies the output out on its download stream -- so with
  * page-locked host buffers the next step's upload and the previous step's
  * download overlap the current step's compute.  Returns at once with a
- * ticket; at most two steps are in flight per context (a third submit waits
- * on the host for the oldest to finish).  x and out must stay valid and
+ * ticket; at most three steps are in flight per context (a fourth submit
+ * waits on the host for the oldest to finish): a caller that waits for step
+ * i - 2 after submitting step i keeps the compute stream busy while step
+ * i + 1 uploads and step i - 1 downloads.  x and out must stay valid and
  * untouched until aem_context_wait(ctx, ticket) returns, which also reports
  * the step's in-kernel errors.  Steps run in submission order. */
 aem_status aem_moe_submit_host(aem_context_t ctx, aem_moe_t moe, const void* x, aem_dtype x_dtype,
