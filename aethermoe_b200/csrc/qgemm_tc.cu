@@ -66,6 +66,15 @@ constexpr int kConvThreads = kConvWarps * 32;
 // G <= D the slot's previous phase (kc - D) is at most one phase ahead of the
 // barrier and the parity wait cannot alias an older phase.  The int8 ring's
 // depth is a multiple of G, for the same reason (see Cfg::S8).
+#ifndef AEM_PAIR_W16_STAGES
+#define AEM_PAIR_W16_STAGES 4     // SM-pair form: converted-weight slots
+#endif
+#ifndef AEM_PAIR_W8_STAGES
+#define AEM_PAIR_W8_STAGES 8      // SM-pair form: int8 weight slots, at least
+#endif
+#ifndef AEM_PAIR_X_STAGES_MAX
+#define AEM_PAIR_X_STAGES_MAX 8   // SM-pair form: activation slots, at most
+#endif
 #ifndef AEM_QGEMM_MAX_CONV_GROUPS
 #define AEM_QGEMM_MAX_CONV_GROUPS 4
 #endif
@@ -702,13 +711,24 @@ __global__ void __launch_bounds__(Cfg<BT, SPLIT, TSA, NI>::THREADS, 1)
 // columns.  Per SM and K step this moves 8 + 16 + BT/2*128 bytes into shared
 // memory instead of 8 + 16 + BT*128 (and reads as much back), and one thread
 // issues the MMAs of two SMs.
+// The activation tiles and the converted weights sit in two rings of their
+// own depths (DX and DW slots; K step kc uses slots kc % DX and kc % DW),
+// synchronised per K step through NB barrier slots (kc % NB): the activation
+// TMA, issued when its slot frees and landing 1000-2000 cycles later, gets
+// the deep ring, the conversion, which starts once the int8 tile is in, the
+// shallow one.  A producer reuses slot kc % D after the MMAs of K step
+// kc - D completed, i.e. it waits on st_empty[(kc - D) % NB] for phase
+// (kc - D) / NB.  That parity wait is exact because NB >= D (the barrier
+// cannot have completed K step kc - D + NB, which needs this very tile) and
+// the producer already saw K step kc - D - NB complete (its own earlier
+// wait; for converter groups NB is a multiple of the group count).
 // Synchronisation (same barrier offsets in both CTAs; every wait and arrival
 // uses the default CTA-scope semantics, as the tcgen05 pipelines of CUTLASS do):
-//   st_full[s]   even CTA: both CTAs' activation TMA bytes (the odd CTA's
+//   st_full[j]   even CTA: both CTAs' activation TMA bytes (the odd CTA's
 //                loads complete on the even CTA's barrier, .cta_group::2),
 //                its producer's expect-tx arrival and one arrival per
 //                converter warp of BOTH CTAs (the odd CTA's arrive remotely);
-//   st_empty[s]  both: one tcgen05.commit multicast to the pair frees both stages;
+//   st_empty[j]  both: one tcgen05.commit multicast to the pair per K step;
 //   accf[b]      both: the commit of a tile's last K step (multicast);
 //   acce[b]      even CTA: 8 local + 8 remote epilogue-warp arrivals.
 // Every wait is bounded; a timeout sets the abort flag in both CTAs.  The pair
@@ -721,27 +741,32 @@ struct Cfg2 {
     static constexpr int W16 = kCh * kKT * 2;
     static constexpr int XB = HB * kKT * 2;        // bf16 activation half-tile, per part
     static constexpr int XS = SPLIT * XB;
-    // The activation tile's TMA, issued when a stage frees, takes 1000-2000
-    // cycles to land (measured), so the operand ring gets the depth: the
-    // int8 ring, whose tiles are re-read from L2 by every token tile, keeps
-    // four stages.
     static constexpr int BUDGET = 216 * 1024;
-    static constexpr int DS_RAW = (BUDGET - 4 * W8) / (W16 + XS);
-    static constexpr int DS = DS_RAW > 8 ? 8 : (DS_RAW < 2 ? 2 : DS_RAW);
-    static constexpr int S8_RAW = (BUDGET - DS * (W16 + XS)) / W8;
-    static constexpr int CG_RAW = DS >= 4 ? 4 : (DS >= 2 ? 2 : 1);
-    static constexpr int CG = CG_RAW < AEM_QGEMM_MAX_CONV_GROUPS ? CG_RAW : AEM_QGEMM_MAX_CONV_GROUPS;
+    static constexpr int CG = 4 < AEM_QGEMM_MAX_CONV_GROUPS ? 4 : AEM_QGEMM_MAX_CONV_GROUPS;
+    // eight int8 slots measured 1-2% ahead of four at the layer bench's
+    // shapes; with float32 activations (two 16 KB parts per slot) four leave
+    // room for three activation slots
+    static constexpr int S8_WANT = SPLIT == 2 ? 4 : AEM_PAIR_W8_STAGES;
+    static constexpr int S8_MIN = ((S8_WANT + CG - 1) / CG) * CG;
+    static constexpr int DW = AEM_PAIR_W16_STAGES;
+    static constexpr int DX_RAW = (BUDGET - S8_MIN * W8 - DW * W16) / XS;
+    static constexpr int DX = DX_RAW > AEM_PAIR_X_STAGES_MAX ? AEM_PAIR_X_STAGES_MAX : DX_RAW;
+    // the int8 ring, whose tiles are re-read from L2 by every token tile,
+    // takes what is left (a multiple of the converter groups)
+    static constexpr int S8_RAW = (BUDGET - DX * XS - DW * W16) / W8;
     static constexpr int S8 = ((S8_RAW > 12 ? 12 : S8_RAW) / CG) * CG;
+    static constexpr int NB_RAW = DX > DW ? DX : DW;
+    static constexpr int NB = ((NB_RAW + CG - 1) / CG) * CG;
     static constexpr int TMEM_COLS = 2 * BT < 32 ? 32 : 2 * BT;
-    static constexpr int BAR_BYTES = (2 * DS + 2 * S8 + 4) * 8 + 16;
+    static constexpr int BAR_BYTES = (2 * NB + 2 * S8 + 4) * 8 + 16;
     static constexpr int TAB_BYTES = 2 * (kMaxGroups + 1) * 4;
-    static constexpr int SMEM = 1024 + DS * (W16 + XS) + S8 * W8 + BAR_BYTES + TAB_BYTES;
+    static constexpr int SMEM = 1024 + DW * W16 + DX * XS + S8 * W8 + BAR_BYTES + TAB_BYTES;
     static constexpr int CG_WARPS = kConvWarps / CG;
     static constexpr int CG_THREADS = CG_WARPS * 32;
     static constexpr int EPI_COLS = BT >= 32 ? BT / 2 : BT;
-    static_assert(CG <= DS && S8 >= CG && S8 % CG == 0 && kConvWarps % CG == 0,
-                  "converter groups vs rings");
-    static_assert(S8 >= 2 && DS >= 2, "pipeline needs two stages per ring");
+    static_assert(S8 >= CG && S8 % CG == 0 && kConvWarps % CG == 0, "converter groups vs rings");
+    static_assert(NB >= DX && NB >= DW && NB % CG == 0, "barrier slots vs rings");
+    static_assert(S8 >= 2 && DX >= 2 && DW >= 2, "pipeline needs two stages per ring");
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
     static_assert(BT % 32 == 0 && BT >= 32 && BT <= 256, "MMA N for M=256 (N/2 rows per CTA)");
 };
@@ -802,11 +827,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* w16_ring = smem;
-    uint8_t* x_ring = w16_ring + C::DS * C::W16;
-    uint8_t* w8_ring = x_ring + C::DS * C::XS;
+    uint8_t* x_ring = w16_ring + C::DW * C::W16;
+    uint8_t* w8_ring = x_ring + C::DX * C::XS;
     uint64_t* st_full = reinterpret_cast<uint64_t*>(w8_ring + C::S8 * C::W8);
-    uint64_t* st_empty = st_full + C::DS;
-    uint64_t* w8_full = st_empty + C::DS;
+    uint64_t* st_empty = st_full + C::NB;
+    uint64_t* w8_full = st_empty + C::NB;
     uint64_t* w8_empty = w8_full + C::S8;
     uint64_t* accf_bar = w8_empty + C::S8;  // [2]
     uint64_t* acce_bar = accf_bar + 2;      // [2]
@@ -824,7 +849,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int npairs = gridDim.x >> 1;
 
     if (tid == 0) {
-        for (int s = 0; s < C::DS; ++s) {
+        for (int s = 0; s < C::NB; ++s) {
             mbar_init(&st_full[s], 2 * C::CG_WARPS + 1);  // used in the even CTA
             mbar_init(&st_empty[s], 1);
         }
@@ -907,36 +932,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else if (warp == kXWarp) {
         // ================= activation producer: this CTA's half of the token rows
         if (lane == 0) {
-            int sx = 0;
-            uint32_t phx = 0;
+            uint32_t kc = 0;
             bool ok = true;
             for (int t = pair; t < total && ok && !*abort_flag; t += npairs) {
                 const TileInfo ti = decode_tile_pair<BT>(t, s_rows, s_tiles, p, npair, nkt, kper);
                 const int n_eff = min(BT, (ti.nrows + 31) & ~31);  // MMA N: halves of >= 16 rows
                 const int row = static_cast<int>(ti.row0) + static_cast<int>(cta) * (n_eff / 2);
-                for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                    if (!pair_wait(&st_empty[sx], phx ^ 1, abort_flag, peer, p.err)) {
-                        ok = false;
-                        break;
+                for (int kt = ti.kt0; kt < ti.kt1; ++kt, ++kc) {
+                    if (kc >= static_cast<uint32_t>(C::DX)) {  // slot kc % DX: K step kc - DX done
+                        const uint32_t j = kc - C::DX;
+                        if (!pair_wait(&st_empty[j % C::NB], (j / C::NB) & 1, abort_flag, peer,
+                                       p.err)) {
+                            ok = false;
+                            break;
+                        }
                     }
-                    uint8_t* st = x_ring + sx * C::XS;
+                    uint8_t* st = x_ring + (kc % C::DX) * C::XS;
+                    uint64_t* full = &st_full[kc % C::NB];
                     // both halves' bytes complete on the even CTA's barrier
-                    if (cta == 0) mbar_arrive_expect_tx(&st_full[sx], 2 * C::XS);
-                    tma_load_2d_pair(st, &tm_xh, &st_full[sx], 0, kt * kKT, row);
-                    if (SPLIT == 2)
-                        tma_load_2d_pair(st + C::XB, &tm_xl, &st_full[sx], 0, kt * kKT, row);
-                    if (++sx == C::DS) {
-                        sx = 0;
-                        phx ^= 1;
-                    }
+                    if (cta == 0) mbar_arrive_expect_tx(full, 2 * C::XS);
+                    tma_load_2d_pair(st, &tm_xh, full, 0, kt * kKT, row);
+                    if (SPLIT == 2) tma_load_2d_pair(st + C::XB, &tm_xl, full, 0, kt * kKT, row);
                 }
             }
         }
     } else if (warp == kMmaWarp) {
-        if (cta == 0 && lane == 0) {
-            // ================= MMA issuer of the pair
-            int ss = 0;
-            uint32_t phs = 0;
+        if (cta == 0) {
+            // ================= MMA issuer of the pair: the whole warp runs the
+            // loop (warp-uniform values), one elected lane issues -- 4-5%
+            // faster than one lane running it alone (dense 4096 x 4096 x 14336)
+            int sb = 0, sw = 0, sx = 0;  // kc % NB, kc % DW, kc % DX
+            uint32_t phb = 0;            // (kc / NB) & 1
             int it = 0;
             bool ok = true;
             for (int t = pair; t < total && ok && !*abort_flag; t += npairs, ++it) {
@@ -944,36 +970,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const int b = it & 1;
                 const uint32_t aph = (it >> 1) & 1;
                 // both CTAs' epilogues have drained accumulator b
-                if (!pair_wait(&acce_bar[b], aph ^ 1, abort_flag, peer, p.err)) break;
+                if (!__all_sync(0xFFFFFFFFu,
+                                pair_wait(&acce_bar[b], aph ^ 1, abort_flag, peer, p.err)))
+                    break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BT);
                 const int n_eff = min(BT, (ti.nrows + 31) & ~31);
                 const uint32_t idesc = idesc_bf16_f32(2 * kCh, static_cast<uint32_t>(n_eff));
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
                     // both CTAs' activation halves and converted weights are in
-                    if (!pair_wait(&st_full[ss], phs, abort_flag, peer, p.err)) {
+                    if (!__all_sync(0xFFFFFFFFu,
+                                    pair_wait(&st_full[sb], phb, abort_flag, peer, p.err))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t adesc = smem_desc_sw128(smem_u32(w16_ring + ss * C::W16));
-                    const uint64_t bdesc = smem_desc_sw128(smem_u32(x_ring + ss * C::XS));
-                    const uint64_t ldesc = smem_desc_sw128(smem_u32(x_ring + ss * C::XS + C::XB));
+                    const uint64_t adesc = smem_desc_sw128(smem_u32(w16_ring + sw * C::W16));
+                    const uint64_t bdesc = smem_desc_sw128(smem_u32(x_ring + sx * C::XS));
+                    const uint64_t ldesc = smem_desc_sw128(smem_u32(x_ring + sx * C::XS + C::XB));
 #pragma unroll
                     for (int kk = 0; kk < kKT / 16; ++kk) {
-                        tc_mma_f16_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc,
-                                        (kt > ti.kt0 || kk > 0) ? 1u : 0u);
+                        tc_mma_f16_pair_elect(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc,
+                                              (kt > ti.kt0 || kk > 0) ? 1u : 0u);
                         if (SPLIT == 2)
-                            tc_mma_f16_pair(d_tmem, adesc + 2 * kk, ldesc + 2 * kk, idesc, 1u);
+                            tc_mma_f16_pair_elect(d_tmem, adesc + 2 * kk, ldesc + 2 * kk, idesc,
+                                                  1u);
                     }
-                    tc_commit_pair(&st_empty[ss], 0x3);  // frees the stage in both CTAs
-                    if (++ss == C::DS) {
-                        ss = 0;
-                        phs ^= 1;
+                    tc_commit_pair_elect(&st_empty[sb], 0x3);  // frees K step kc's slots in both CTAs
+                    if (++sb == C::NB) {
+                        sb = 0;
+                        phb ^= 1;
                     }
+                    if (++sw == C::DW) sw = 0;
+                    if (++sx == C::DX) sx = 0;
                 }
                 if (!ok) break;
-                tc_commit_pair(&accf_bar[b], 0x3);
+                tc_commit_pair_elect(&accf_bar[b], 0x3);
             }
         }
     } else if (warp < kConvWarps) {
@@ -986,16 +1018,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const TileInfo ti = decode_tile_pair<BT>(t, s_rows, s_tiles, p, npair, nkt, kper);
             for (int kt = ti.kt0; kt < ti.kt1; ++kt, ++kc) {
                 if (static_cast<int>(kc % C::CG) != group) continue;
-                const int s16 = static_cast<int>(kc % C::DS);
-                const uint32_t ph16 = (kc / C::DS) & 1;
                 const int s8 = static_cast<int>(kc % C::S8);
                 const uint32_t ph8 = (kc / C::S8) & 1;
+                // slot kc % DW is free once K step kc - DW's MMAs completed
+                const uint32_t j = kc - C::DW;
                 if (!pair_wait(&w8_full[s8], ph8, abort_flag, peer, p.err) ||
-                    !pair_wait(&st_empty[s16], ph16 ^ 1, abort_flag, peer, p.err)) {
+                    (kc >= static_cast<uint32_t>(C::DW) &&
+                     !pair_wait(&st_empty[j % C::NB], (j / C::NB) & 1, abort_flag, peer, p.err))) {
                     ok = false;
                     break;
                 }
-                uint8_t* st = w16_ring + s16 * C::W16;
+                uint8_t* st = w16_ring + (kc % C::DW) * C::W16;
                 const uint8_t* w8 = w8_ring + s8 * C::W8;
 #pragma unroll
                 for (int i = 0; i < 512 / C::CG_THREADS; ++i) {
@@ -1019,9 +1052,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) {
                     if (cta == 0)
-                        mbar_arrive(&st_full[s16]);
+                        mbar_arrive(&st_full[kc % C::NB]);
                     else
-                        mbar_arrive_remote(&st_full[s16], 0);
+                        mbar_arrive_remote(&st_full[kc % C::NB], 0);
                     mbar_arrive(&w8_empty[s8]);
                 }
             }
