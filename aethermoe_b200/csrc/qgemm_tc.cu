@@ -965,7 +965,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t phb = 0;            // (kc / NB) & 1
             int it = 0;
             bool ok = true;
-            for (int t = pair; t < total && ok && !*abort_flag; t += npairs, ++it) {
+            // (the abort vote keeps the warp's lanes on one path)
+            for (int t = pair; t < total && ok && !__any_sync(0xFFFFFFFFu, *abort_flag != 0);
+                 t += npairs, ++it) {
                 const TileInfo ti = decode_tile_pair<BT>(t, s_rows, s_tiles, p, npair, nkt, kper);
                 const int b = it & 1;
                 const uint32_t aph = (it >> 1) & 1;

@@ -576,7 +576,7 @@ def run_ours(args):
                        "l2": (f"inputs rotate over {N_INPUT_BUFFERS} buffers "
                               f"({N_INPUT_BUFFERS * tokens * D_MODEL * 2 >> 20} MiB > 126 MiB L2); "
                               "per-step working set > 1 GiB")},
-            "roofline": {"kernel": "qgemm_tc_kernel (grouped INT8-weight GEMM, up + down launches)",
+            "roofline": {"kernel": "qgemm_tc_pair_kernel (grouped INT8-weight GEMM on SM pairs, up + down launches)",
                          "bound": "tensor", "achieved": tflops,
                          "peak": peak, "unit": "TFLOP/s",
                          "frac": (tflops / peak) if tflops and peak else None,
