@@ -639,9 +639,14 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
                     break;
                 const int dd = min(C::DK, D - c * C::DK);
                 const uint32_t xb = static_cast<uint32_t>(dd * C::XB);
-                dev::mbar_arrive_expect_tx(&full[st], C::WST + rows * xb);
+                // the packed gate is Dpad wide (a multiple of 256, not of the
+                // chunk): the last chunk's weight copy stops at Dpad
+                const int wd = static_cast<int>(
+                    min(static_cast<int64_t>(C::DK), Dpad - static_cast<int64_t>(c) * C::DK));
+                const uint32_t wb = static_cast<uint32_t>(wd / 4 * EB * 16);
+                dev::mbar_arrive_expect_tx(&full[st], wb + rows * xb);
                 dev::bulk_load(wring + st * C::WST, wsrc + static_cast<int64_t>(c) * (C::DK / 4) * EB,
-                               C::WST, &full[st]);
+                               wb, &full[st]);
                 for (int r = 0; r < rows; ++r)
                     dev::bulk_load(xring + st * C::XST + r * C::XROW,
                                    x + (tok0 + r) * static_cast<int64_t>(D) + c * C::DK, xb,
