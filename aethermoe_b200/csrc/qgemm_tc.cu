@@ -250,6 +250,13 @@ __device__ __forceinline__ bool work_next(WorkCursor& c, TileInfo& ti, const int
     return true;
 }
 
+// Two floats rounded to bf16 (nearest even), packed: `lo` in the low half,
+// the lower address of the pair in memory.
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 // 4 signed bytes -> 2 words of bf16x2 (exact).  Each byte b becomes the float
 // 2^23 + (b + 128) by byte permutation, minus (2^23 + 128); the bf16 is the
 // float's upper half (integers |b| <= 128 have no low mantissa bits).
@@ -1085,15 +1092,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                    static_cast<uint32_t>(b * BT);
             const int cbeg = h * C::EPI_COLS;
             const int cend = min(cbeg + C::EPI_COLS, ti.nrows);
+            // bf16 output without a low half: each lane stores 8 channels of a
+            // row at once (16 bytes) after an 8x8 transpose inside its group
+            // of 8 lanes -- 2 stores per 16-column chunk instead of 16 (the
+            // per-row 2-byte stores queued behind the converters' shared-memory
+            // traffic and made the epilogue as long as a tile's main loop)
+            const bool v8 = !p.red_v4 && p.out_bf16 && !p.out_lo && !p.atomic_add &&
+                            ((p.N | static_cast<int>(p.ldo & 7)) & 7) == 0 &&
+                            (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
+            // output row and row scale of row c0 + lane (lanes < 16; loading
+            // them a chunk ahead measured no faster)
+            auto row_info = [&](int c0, int& orow, float& rs) {
+                orow = 0;
+                rs = 1.0f;
+                const int64_t row = ti.row0 + c0 + (lane & 15);
+                if (lane < 16 && c0 + lane < ti.nrows) {
+                    orow = p.rowmap ? __ldg(p.rowmap + row) : static_cast<int>(row);
+                    if (p.rowscale) rs = __ldg(p.rowscale + row);
+                }
+            };
 #pragma unroll 1
             for (int c0 = cbeg; c0 < cend; c0 += 16) {
-                int my_orow = 0;
-                float my_rs = 1.0f;
-                const int64_t my_row = ti.row0 + c0 + (lane & 15);
-                if (lane < 16 && c0 + lane < ti.nrows) {
-                    my_orow = p.rowmap ? __ldg(p.rowmap + my_row) : static_cast<int>(my_row);
-                    if (p.rowscale) my_rs = __ldg(p.rowscale + my_row);
-                }
+                int my_orow;
+                float my_rs;
+                row_info(c0, my_orow, my_rs);
                 uint32_t r[16];
                 tc_ld_32x32b_x16(tbase + c0, r);
                 tc_wait_ld();
@@ -1138,25 +1160,69 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         if (qvalid && c0 + j4 + qi < ti.nrows)
                             red_add_v4(obase + orow * p.ldo, a[0], a[1], a[2], a[3]);
                     }
-                    continue;
-                }
+                } else if (v8) {
+                    float a[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int64_t orow = __shfl_sync(0xFFFFFFFFu, my_orow, j);
-                    const float rs = __shfl_sync(0xFFFFFFFFu, my_rs, j);
-                    if (nvalid && c0 + j < ti.nrows) {
-                        float v = __uint_as_float(r[j]) * sc * rs;
+                    for (int j = 0; j < 16; ++j) {
+                        float v = __uint_as_float(r[j]) * sc;
+                        if (p.rowscale) v *= __shfl_sync(0xFFFFFFFFu, my_rs, j);
                         if (p.relu) v = fmaxf(v, 0.0f);
-                        if (p.out_bf16) {
-                            const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-                            reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + n] = hi;
-                            if (p.out_lo)
-                                reinterpret_cast<__nv_bfloat16*>(p.out_lo)[orow * p.ldo + n] =
-                                    __float2bfloat16_rn(v - __bfloat162float(hi));
-                        } else if (p.atomic_add) {
-                            atomicAdd(reinterpret_cast<float*>(p.out) + orow * p.ldo + n, v);
-                        } else {
-                            reinterpret_cast<float*>(p.out)[orow * p.ldo + n] = v;
+                        a[j] = v;
+                    }
+                    // lane 8g + i holds channel 8g + i of rows 0..15; after the
+                    // butterfly (distances 4, 2, 1; both 8-row blocks) it holds
+                    // channels 8g..8g+7 of rows i (a[0..7]) and 8 + i (a[8..15])
+                    const int li = lane & 7;
+#pragma unroll
+                    for (int sd = 4; sd >= 1; sd >>= 1) {
+#pragma unroll
+                        for (int blk = 0; blk < 16; blk += 8) {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                if (j & sd) continue;
+                                const float send = (li & sd) ? a[blk + j] : a[blk + j + sd];
+                                const float got = __shfl_xor_sync(0xFFFFFFFFu, send, sd);
+                                if (li & sd)
+                                    a[blk + j] = got;
+                                else
+                                    a[blk + j + sd] = got;
+                            }
+                        }
+                    }
+                    const int nb = n0 + q * 32 + 8 * (lane >> 3);  // this lane's first channel
+#pragma unroll
+                    for (int blk = 0; blk < 16; blk += 8) {
+                        const int rr = blk + li;  // row within the chunk
+                        const int64_t orow = __shfl_sync(0xFFFFFFFFu, my_orow, rr);
+                        if (c0 + rr < ti.nrows && nb < p.N) {
+                            uint4 v;
+                            v.x = bf16x2_bits(a[blk + 0], a[blk + 1]);
+                            v.y = bf16x2_bits(a[blk + 2], a[blk + 3]);
+                            v.z = bf16x2_bits(a[blk + 4], a[blk + 5]);
+                            v.w = bf16x2_bits(a[blk + 6], a[blk + 7]);
+                            *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) +
+                                                      orow * p.ldo + nb) = v;
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int64_t orow = __shfl_sync(0xFFFFFFFFu, my_orow, j);
+                        const float rs = __shfl_sync(0xFFFFFFFFu, my_rs, j);
+                        if (nvalid && c0 + j < ti.nrows) {
+                            float v = __uint_as_float(r[j]) * sc * rs;
+                            if (p.relu) v = fmaxf(v, 0.0f);
+                            if (p.out_bf16) {
+                                const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+                                reinterpret_cast<__nv_bfloat16*>(p.out)[orow * p.ldo + n] = hi;
+                                if (p.out_lo)
+                                    reinterpret_cast<__nv_bfloat16*>(p.out_lo)[orow * p.ldo + n] =
+                                        __float2bfloat16_rn(v - __bfloat162float(hi));
+                            } else if (p.atomic_add) {
+                                atomicAdd(reinterpret_cast<float*>(p.out) + orow * p.ldo + n, v);
+                            } else {
+                                reinterpret_cast<float*>(p.out)[orow * p.ldo + n] = v;
+                            }
                         }
                     }
                 }
