@@ -140,6 +140,20 @@ __global__ void combine4_kernel(const float4* __restrict__ y, int64_t T, int k, 
     }
 }
 
+// k == 1 with bf16 output (the layer's float32 output rows -> bf16): a
+// straight conversion, 8 values per thread and iteration, no row arithmetic.
+__global__ void f32_to_bf16_kernel(const float4* __restrict__ y, int64_t n8,
+                                   uint4* __restrict__ out) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float4 a = y[2 * i];
+        const float4 b = y[2 * i + 1];
+        __nv_bfloat162 h[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
+                               __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
+        out[i] = *reinterpret_cast<const uint4*>(h);
+    }
+}
+
 unsigned grid_for(int64_t work, int per_block) {
     const int64_t b = (work + per_block - 1) / per_block;
     return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(b, 148 * 16)));
@@ -175,7 +189,11 @@ aem_status gather_rows(const void* x, aem_dtype xd, const int32_t* src, int64_t 
 aem_status combine_rows(const float* y, int64_t T, int k, int64_t d, void* out, aem_dtype od,
                         cudaStream_t s) {
     if (T == 0) return AEM_OK;
-    if ((d & 3) == 0) {
+    if (k == 1 && od == AEM_BF16 && (T * d) % 8 == 0 &&
+        ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(out)) & 15) == 0) {
+        f32_to_bf16_kernel<<<grid_for(T * d / 8, 256), 256, 0, s>>>(
+            reinterpret_cast<const float4*>(y), T * d / 8, static_cast<uint4*>(out));
+    } else if ((d & 3) == 0) {
         const unsigned g = grid_for(T * d / 4, 256);
         if (od == AEM_BF16)
             combine4_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(
