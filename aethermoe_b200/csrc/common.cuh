@@ -349,18 +349,8 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
                  : "memory");
 }
 // D[tmem of both CTAs] (+)= A[smem of both] * B[smem, N split over the pair]^T,
-// issued by one thread of the pair's even CTA.
-__device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                                uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// The same, issued by one elected lane of a warp that runs the issue loop
-// together (its operands then stay warp-uniform).
+// issued in the pair's even CTA by one elected lane of a warp that runs the
+// issue loop together (its operands then stay warp-uniform).
 __device__ __forceinline__ void tc_mma_f16_pair_elect(uint32_t d_tmem, uint64_t a_desc,
                                                       uint64_t b_desc, uint32_t idesc,
                                                       uint32_t accumulate) {
@@ -373,16 +363,9 @@ __device__ __forceinline__ void tc_mma_f16_pair_elect(uint32_t d_tmem, uint64_t 
         : "memory");
 }
 // Arrive (once) on the mbarrier at `bar`'s offset in every CTA of `cta_mask`
-// when all previously issued tcgen05 ops of this thread complete.
-__device__ __forceinline__ void tc_commit_pair(uint64_t* bar, uint16_t cta_mask) {
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-        " [%0], %1;" ::"r"(smem_u32(bar)),
-        "h"(cta_mask)
-        : "memory");
-}
-// The same from one elected lane (the lane that issued the MMAs: elect.sync
-// picks the lowest active lane every time).
+// when all tcgen05 ops previously issued by the elected lane complete (the
+// lane that issued the MMAs: elect.sync picks the lowest active lane every
+// time).
 __device__ __forceinline__ void tc_commit_pair_elect(uint64_t* bar, uint16_t cta_mask) {
     asm volatile(
         "{\n\t.reg .pred e;\n\t"
