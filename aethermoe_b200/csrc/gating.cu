@@ -85,6 +85,17 @@ struct GatingCfg {
     static_assert(TPG % 2 == 0, "tokens are processed in pairs");
 };
 
+// Packed fused multiply-add of two float32 lanes, each rounded once.
+__device__ __forceinline__ float2 fma_rn2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
 // Selection key of a logit in np.argmax order: every NaN ranks above every
 // number (np.argmax returns the first NaN), -0.0 ranks equal to +0.0, and
 // otherwise the float order; the low word (0xFFFFFFFF - expert) makes the
@@ -252,8 +263,14 @@ __global__ void __launch_bounds__(WARPS * 32)
                   const float* __restrict__ bias, int64_t N, int D, int E, int k, int ksel,
                   int32_t* __restrict__ idx_out, float* __restrict__ val_out,
                   const float* __restrict__ wsq16, int* __restrict__ cert_rows,
-                  const int* __restrict__ rowlist, unsigned long long* __restrict__ rows_total) {
+                  const int* __restrict__ rowlist, unsigned long long* __restrict__ rows_total,
+                  float one, float neg0) {
     using C = GatingCfg<GROUP, NSLOT, kTPG, WARPS, XT, DKO>;
+    // 1.0 and -0.0 arrive as launch arguments, so the compiler cannot fold
+    // the EXACT mode's fused multiply-adds below back into a plain multiply
+    // and add (which it may then contract into one fused multiply-add)
+    const float2 one2 = make_float2(one, one);
+    const float2 nz2 = make_float2(neg0, neg0);
     constexpr int kThreads = C::kThreads;
     constexpr int GPW = C::GPW;
     constexpr int TOK = C::TOK;
@@ -377,19 +394,23 @@ __global__ void __launch_bounds__(WARPS * 32)
                 for (int p = 0; p < kTPG / 2; ++p) {
                     float2 a = acc[p][s];
                     if constexpr (EXACT) {
-                        // float32 product, then float32 add, d in increasing order.
-                        // Scalar ops: a packed fp32x2 multiply followed by a packed
-                        // add (as intrinsics or as explicit mul.rn/add.rn.f32x2)
-                        // was measured to round like one fused multiply-add,
-                        // which reorders experts whose logits are 1 ulp apart.
-                        a.x = __fadd_rn(a.x, __fmul_rn(xa[p].x, wv.x));
-                        a.y = __fadd_rn(a.y, __fmul_rn(xa[p].y, wv.x));
-                        a.x = __fadd_rn(a.x, __fmul_rn(xa[p].z, wv.y));
-                        a.y = __fadd_rn(a.y, __fmul_rn(xa[p].w, wv.y));
-                        a.x = __fadd_rn(a.x, __fmul_rn(xb[p].x, wv.z));
-                        a.y = __fadd_rn(a.y, __fmul_rn(xb[p].y, wv.z));
-                        a.x = __fadd_rn(a.x, __fmul_rn(xb[p].z, wv.w));
-                        a.y = __fadd_rn(a.y, __fmul_rn(xb[p].w, wv.w));
+                        // float32 product, then float32 add, d in increasing order,
+                        // for the lane group's two tokens at once: the product as
+                        // x*w + (-0.0) and the sum as p*1.0 + acc, packed fp32x2
+                        // fused multiply-adds that each round exactly once like the
+                        // plain multiply and add (x*w + -0 and p*1 are exact; a
+                        // -0 product stays -0).  A packed multiply followed by a
+                        // packed add was measured to round like one fused
+                        // multiply-add, which reorders experts whose logits are
+                        // 1 ulp apart; this form halves the scalar instruction count.
+                        a = fma_rn2(fma_rn2(make_float2(xa[p].x, xa[p].y),
+                                            make_float2(wv.x, wv.x), nz2), one2, a);
+                        a = fma_rn2(fma_rn2(make_float2(xa[p].z, xa[p].w),
+                                            make_float2(wv.y, wv.y), nz2), one2, a);
+                        a = fma_rn2(fma_rn2(make_float2(xb[p].x, xb[p].y),
+                                            make_float2(wv.z, wv.z), nz2), one2, a);
+                        a = fma_rn2(fma_rn2(make_float2(xb[p].z, xb[p].w),
+                                            make_float2(wv.w, wv.w), nz2), one2, a);
                     } else {
                         a.x = fmaf(xa[p].x, wv.x, a.x);
                         a.y = fmaf(xa[p].y, wv.x, a.y);
@@ -1023,7 +1044,7 @@ cudaError_t launch_one(const Gate& g, const void* x, int64_t N, int k, int ksel,
     kern<<<static_cast<unsigned>(blocks), WARPS * 32, smem, s>>>(
         static_cast<const XT*>(x), reinterpret_cast<const float4*>(g.wt), g.bias, N,
         static_cast<int>(g.D), static_cast<int>(g.E), k, ksel, idx, val, g.wsq16, g.cert_rows,
-        rowlist, rows_total);
+        rowlist, rows_total, 1.0f, -0.0f);
     return cudaGetLastError();
 }
 
